@@ -1,0 +1,128 @@
+"""Generate the golden fixtures from the reference implementation itself.
+
+Run from the repository root in a container where the reference package is
+mounted (read-only) at ``/root/reference``::
+
+    python tests/golden/make_golden.py [/root/reference]
+
+It imports the reference (``torchcodec`` is stubbed: the reference only uses it
+for file decode/encode in unblend/api.py:20-21), builds each model exactly as
+the registry does under ``torch.manual_seed(seed)`` (unblend/repo.py:121-143),
+checks that ``unblend_b200.synth.htdemucs_state_dict`` reproduces those weights
+bit for bit, and saves the reference's fp32 CPU outputs on synthetic audio:
+
+* ``htdemucs_small.pt``   reduced-width HTDemucs (0.5 s segment), batch 2,
+  full outputs of ``HTDemucs.forward`` (unblend/htdemucs.py:650).
+* ``htdemucs_full.pt``    registry ``htdemucs`` (4 stems) on a 1 s clip, every
+  5th output sample plus per-stem sums / sums of squares of the full output.
+* ``htdemucs_6s_full.pt`` registry ``htdemucs_6s`` (seed 2), same summaries.
+* ``apply_small.pt``      ``apply_model`` (unblend/apply.py:500) with the
+  reduced model over a 4-segment track, shifts 0 and shifts 1 (offsets drawn
+  after ``random.seed(5)``), every 7th output sample plus full sums.
+
+The fixtures hold only outputs and small inputs; weights are regenerated from
+the seed on the fly, and ``weights_digest`` pins that regeneration.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import os
+import random
+import sys
+import types
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, ROOT)
+
+from unblend_b200.synth import htdemucs_config, htdemucs_state_dict, synth_track  # noqa: E402
+
+SMALL_OVERRIDES = dict(channels=8, bottom_channels=32, t_heads=4, t_layers=3, segment=0.5)
+
+
+def import_reference(path: str):
+    """Import the reference ``unblend`` package with ``torchcodec`` stubbed."""
+    for name in ("torchcodec", "torchcodec.decoders", "torchcodec.encoders"):
+        mod = types.ModuleType(name)
+        mod.AudioDecoder = object
+        mod.AudioEncoder = object
+        sys.modules.setdefault(name, mod)
+    if path not in sys.path:
+        sys.path.insert(0, path)
+    import unblend  # noqa: F401
+    import unblend.apply
+    import unblend.htdemucs
+    return unblend
+
+
+def weights_digest(sd: dict) -> str:
+    """sha256 over every tensor's name and raw float32 bytes, in key order."""
+    h = hashlib.sha256()
+    for k in sorted(sd):
+        h.update(k.encode())
+        h.update(sd[k].detach().float().contiguous().numpy().tobytes())
+    return h.hexdigest()
+
+
+def _summary(y: torch.Tensor) -> dict:
+    """Per-stem sum and sum of squares over a ``[B, S, C, L]`` output (float64)."""
+    yd = y.double()
+    return {"sum": yd.sum(dim=(0, 2, 3)), "sumsq": (yd * yd).sum(dim=(0, 2, 3))}
+
+
+def build_reference(unblend, cfg: dict, seed: int):
+    torch.manual_seed(seed)
+    model = unblend.htdemucs.HTDemucs(**cfg).eval()
+    mine = htdemucs_state_dict(cfg, seed)
+    ref = model.state_dict()
+    assert set(ref) == set(mine), "state_dict keys differ"
+    for k in ref:
+        assert torch.equal(ref[k], mine[k]), f"weight {k} differs"
+    return model, weights_digest(mine)
+
+
+def main(ref_path: str) -> None:
+    unblend = import_reference(ref_path)
+    torch.set_num_threads(os.cpu_count() or 1)
+    with torch.inference_mode():
+        # Reduced model, full outputs.
+        cfg = htdemucs_config("htdemucs", **SMALL_OVERRIDES)
+        model, digest = build_reference(unblend, cfg, 0)
+        mix = torch.stack([synth_track(0.15, 10), synth_track(0.15, 11)])
+        out = model(mix)
+        torch.save({"config": cfg, "seed": 0, "weights_digest": digest, "mix": mix, "out": out.clone()},
+                   os.path.join(HERE, "htdemucs_small.pt"))
+
+        # apply_model over a 4-segment track with the reduced model.
+        track = synth_track(1.3, 1)[None]
+        res = {"config": cfg, "seed": 0, "weights_digest": digest, "mix": track,
+               "overlap": 0.25, "chunk_batch_size": 3, "decimate": 7}
+        y0 = unblend.apply.apply_model(model, track, device="cpu", shifts=0, overlap=0.25,
+                                       chunk_batch_size=3)
+        res["shifts0"] = {"out": y0[..., ::7].clone(), **_summary(y0)}
+        random.seed(5)
+        offsets = [random.randint(0, int(0.5 * cfg["samplerate"]))]
+        random.seed(5)
+        y1 = unblend.apply.apply_model(model, track, device="cpu", shifts=1, overlap=0.25,
+                                       chunk_batch_size=3)
+        res["shifts1"] = {"out": y1[..., ::7].clone(), "offsets": offsets, **_summary(y1)}
+        torch.save(res, os.path.join(HERE, "apply_small.pt"))
+
+        # Registry configurations on a 1 s clip (padded to the 7.8 s segment).
+        for name, seed, fname in (("htdemucs", 0, "htdemucs_full.pt"),
+                                  ("htdemucs_6s", 2, "htdemucs_6s_full.pt")):
+            cfg = htdemucs_config(name)
+            model, digest = build_reference(unblend, cfg, seed)
+            mix = synth_track(1.0, 0)[None]
+            out = model(mix)
+            torch.save({"config": cfg, "seed": seed, "weights_digest": digest, "mix": mix,
+                        "decimate": 5, "out": out[..., ::5].clone(), **_summary(out)},
+                       os.path.join(HERE, fname))
+    print("fixtures written to", HERE)
+
+
+if __name__ == "__main__":
+    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")

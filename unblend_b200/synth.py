@@ -1,0 +1,282 @@
+"""Seeded random-init weights and synthetic audio for the separation path.
+
+Checkpoints and datasets are unavailable offline, so every workload runs on
+random-init weights and synthetic audio:
+
+* ``htdemucs_state_dict(config, seed)`` reproduces ``torch.manual_seed(seed)``
+  followed by ``HTDemucs(**config)`` (unblend/htdemucs.py:58-368) parameter for
+  parameter. It instantiates the same ``torch.nn`` parameter owners in the
+  same construction order, so the torch RNG is consumed identically, then
+  applies the reference's ``rescale_module`` trick (unblend/blocks.py:207-236)
+  and the smoothed frequency embedding (unblend/blocks.py:353-403). The result
+  is keyed exactly like the reference ``state_dict`` (strict-loadable).
+* ``synth_track(seconds, seed)`` generates the stereo 44.1 kHz test signal:
+  8 sinusoids per channel (log-uniform 40-8000 Hz, amplitudes U(0.05, 0.3)),
+  pink noise at -20 dB and a decaying impulse train at 120 BPM, normalised to
+  0.9 peak.
+"""
+
+from __future__ import annotations
+
+import math
+from collections import OrderedDict
+
+import numpy as np
+import torch
+from torch import nn
+
+# Architecture configs of the two HTDemucs registry entries
+# (unblend/metadata.json "htdemucs" and "htdemucs_6s" -> "config").
+_HTDEMUCS_COMMON = dict(
+    audio_channels=2,
+    samplerate=44100,
+    segment=7.8,
+    channels=48,
+    growth=2,
+    nfft=4096,
+    cac=True,
+    depth=4,
+    rewrite=True,
+    freq_emb=0.2,
+    emb_scale=10,
+    emb_smooth=True,
+    kernel_size=8,
+    stride=4,
+    time_stride=2,
+    context=1,
+    context_enc=0,
+    norm_starts=4,
+    norm_groups=4,
+    dconv_mode=3,
+    dconv_depth=2,
+    dconv_comp=8,
+    dconv_init=1e-3,
+    t_layers=5,
+    t_hidden_scale=4.0,
+    t_heads=8,
+    t_layer_scale=True,
+    t_gelu=True,
+    t_emb="sin",
+    t_max_period=10000.0,
+    t_weight_pos_embed=1.0,
+    t_norm_in=True,
+    t_norm_first=True,
+    t_norm_out=True,
+    t_cross_first=False,
+    rescale=0.1,
+)
+
+HTDEMUCS_CONFIGS = {
+    "htdemucs": dict(
+        _HTDEMUCS_COMMON,
+        sources=["drums", "bass", "other", "vocals"],
+        bottom_channels=512,
+    ),
+    "htdemucs_6s": dict(
+        _HTDEMUCS_COMMON,
+        sources=["drums", "bass", "other", "vocals", "guitar", "piano"],
+        bottom_channels=0,
+    ),
+}
+
+
+def htdemucs_config(name: str = "htdemucs", **overrides) -> dict:
+    """Return a copy of a registry HTDemucs config with ``overrides`` applied.
+
+    :param name: ``"htdemucs"`` or ``"htdemucs_6s"``.
+    :param overrides: Fields to replace (e.g. a reduced ``channels`` for tests).
+    :return: Config dict with the reference constructor's field names.
+    """
+    cfg = dict(HTDEMUCS_CONFIGS[name])
+    cfg.update(overrides)
+    cfg["sources"] = list(cfg["sources"])
+    return cfg
+
+
+def _take(prefix: str, module: nn.Module, out: "OrderedDict[str, torch.Tensor]") -> None:
+    """Copy every parameter of ``module`` into ``out`` under ``prefix``."""
+    for name, p in module.named_parameters():
+        out[f"{prefix}.{name}"] = p.detach().clone()
+
+
+def _dconv(prefix: str, channels: int, cfg: dict, out, convs: list) -> None:
+    """DConv parameters (unblend/blocks.py:238-305), construction order."""
+    hidden = int(channels / cfg["dconv_comp"])
+    for d in range(cfg["dconv_depth"]):
+        dil = 2**d
+        c1 = nn.Conv1d(channels, hidden, 3, dilation=dil, padding=dil)
+        g1 = nn.GroupNorm(1, hidden)
+        c2 = nn.Conv1d(hidden, 2 * channels, 1)
+        g2 = nn.GroupNorm(1, 2 * channels)
+        p = f"{prefix}.dconv.layers.{d}"
+        _take(f"{p}.0", c1, out)
+        _take(f"{p}.1", g1, out)
+        _take(f"{p}.3", c2, out)
+        _take(f"{p}.4", g2, out)
+        out[f"{p}.6.scale"] = torch.full((channels,), cfg["dconv_init"])
+        convs += [f"{p}.0", f"{p}.3"]
+
+
+def htdemucs_state_dict(cfg: dict, seed: int) -> "OrderedDict[str, torch.Tensor]":
+    """Random-init HTDemucs weights identical to ``manual_seed(seed); HTDemucs(**cfg)``.
+
+    Follows the layer construction loop of unblend/htdemucs.py:216-321, the
+    rescale pass of unblend/blocks.py:207-236 and the transformer construction
+    of unblend/transformer.py:581-643. Only configurations the registry ships
+    are supported (all-frequency encoder layers, CaC, no MultiWrap, no norms
+    in the encoder/decoder layers, sinusoidal transformer embedding).
+
+    :param cfg: Config from :func:`htdemucs_config`.
+    :param seed: Seed given to ``torch.manual_seed``.
+    :return: State dict keyed like the reference module.
+    """
+    if cfg.get("multi_freqs"):
+        raise ValueError("MultiWrap configs are not supported")
+    if not cfg["cac"] or cfg["norm_starts"] < cfg["depth"] or cfg["t_emb"] != "sin":
+        raise ValueError("only the registry HTDemucs variants are supported")
+    state: "OrderedDict[str, torch.Tensor]" = OrderedDict()
+    conv_keys: list[str] = []
+    rng_state = torch.random.get_rng_state()
+    torch.manual_seed(seed)
+    try:
+        K, S = cfg["kernel_size"], cfg["stride"]
+        chin = cfg["audio_channels"]
+        chin_z = chin * 2
+        chout = chout_z = cfg["channels"]
+        freqs = cfg["nfft"] // 2
+        nsrc = len(cfg["sources"])
+        depth = cfg["depth"]
+        ctx = cfg["context"]
+        for index in range(depth):
+            if freqs <= K:
+                raise ValueError("configs that reach a single frequency are not supported")
+            # Frequency encoder layer: Conv2d (K,1)/(S,1), 1x1 rewrite, DConv.
+            p = f"encoder.{index}"
+            _take(f"{p}.conv", nn.Conv2d(chin_z, chout_z, [K, 1], [S, 1], [K // 4, 0]), state)
+            _take(f"{p}.rewrite", nn.Conv2d(chout_z, 2 * chout_z, 1, 1, 0), state)
+            conv_keys += [f"{p}.conv", f"{p}.rewrite"]
+            _dconv(p, chout_z, cfg, state, conv_keys)
+            # Time encoder layer.
+            p = f"tencoder.{index}"
+            _take(f"{p}.conv", nn.Conv1d(chin, chout, K, S, K // 4), state)
+            _take(f"{p}.rewrite", nn.Conv1d(chout, 2 * chout, 1, 1, 0), state)
+            conv_keys += [f"{p}.conv", f"{p}.rewrite"]
+            _dconv(p, chout, cfg, state, conv_keys)
+            if index == 0:
+                chin = cfg["audio_channels"] * nsrc
+                chin_z = chin * 2
+            # Decoders are inserted at the front, so layer ``index`` lands at
+            # position depth-1-index.
+            p = f"decoder.{depth - 1 - index}"
+            _take(f"{p}.conv_tr", nn.ConvTranspose2d(chout_z, chin_z, [K, 1], [S, 1]), state)
+            _take(f"{p}.rewrite", nn.Conv2d(chout_z, 2 * chout_z, 1 + 2 * ctx, 1, ctx), state)
+            conv_keys += [f"{p}.conv_tr", f"{p}.rewrite"]
+            _dconv(p, chout_z, cfg, state, conv_keys)
+            p = f"tdecoder.{depth - 1 - index}"
+            _take(f"{p}.conv_tr", nn.ConvTranspose1d(chout, chin, K, S), state)
+            _take(f"{p}.rewrite", nn.Conv1d(chout, 2 * chout, 1 + 2 * ctx, 1, ctx), state)
+            conv_keys += [f"{p}.conv_tr", f"{p}.rewrite"]
+            _dconv(p, chout, cfg, state, conv_keys)
+            chin, chin_z = chout, chout_z
+            chout = int(cfg["growth"] * chout)
+            chout_z = int(cfg["growth"] * chout_z)
+            freqs //= S
+            if index == 0 and cfg["freq_emb"]:
+                emb = nn.Embedding(freqs, chin_z)
+                w = emb.weight.data
+                if cfg["emb_smooth"]:
+                    w = torch.cumsum(w, dim=0)
+                    w = w / torch.arange(1, freqs + 1).to(w).sqrt()[:, None]
+                state["freq_emb.embedding.weight"] = (w / cfg["emb_scale"]).clone()
+        if cfg["rescale"]:
+            for key in conv_keys:
+                w = state[f"{key}.weight"]
+                scale = (w.std() / cfg["rescale"]) ** 0.5
+                state[f"{key}.weight"] = w / scale
+                state[f"{key}.bias"] = state[f"{key}.bias"] / scale
+        dim = cfg["channels"] * cfg["growth"] ** (depth - 1)
+        bottom = cfg["bottom_channels"]
+        if bottom:
+            for name, (a, b) in (
+                ("channel_upsampler", (dim, bottom)),
+                ("channel_downsampler", (bottom, dim)),
+                ("channel_upsampler_t", (dim, bottom)),
+                ("channel_downsampler_t", (bottom, dim)),
+            ):
+                _take(name, nn.Conv1d(a, b, 1), state)
+            dim = bottom
+        if cfg["t_layers"] > 0:
+            hidden = int(dim * cfg["t_hidden_scale"])
+            heads = cfg["t_heads"]
+            p = "crosstransformer"
+            _take(f"{p}.norm_in", nn.LayerNorm(dim), state)
+            _take(f"{p}.norm_in_t", nn.LayerNorm(dim), state)
+            parity = 1 if cfg["t_cross_first"] else 0
+            for idx in range(cfg["t_layers"]):
+                for branch in ("layers", "layers_t"):
+                    q = f"{p}.{branch}.{idx}"
+                    if idx % 2 == parity:
+                        layer = nn.TransformerEncoderLayer(
+                            dim, heads, hidden, 0.0, batch_first=True, norm_first=True
+                        )
+                        _take(q, layer, state)
+                        state[f"{q}.norm_out.weight"] = torch.ones(dim)
+                        state[f"{q}.norm_out.bias"] = torch.zeros(dim)
+                    else:
+                        _take(f"{q}.cross_attn", nn.MultiheadAttention(dim, heads, batch_first=True), state)
+                        _take(f"{q}.linear1", nn.Linear(dim, hidden), state)
+                        _take(f"{q}.linear2", nn.Linear(hidden, dim), state)
+                        for n in ("norm1", "norm2", "norm3"):
+                            _take(f"{q}.{n}", nn.LayerNorm(dim), state)
+                        state[f"{q}.norm_out.weight"] = torch.ones(dim)
+                        state[f"{q}.norm_out.bias"] = torch.zeros(dim)
+                    state[f"{q}.gamma_1.scale"] = torch.full((dim,), 1e-4)
+                    state[f"{q}.gamma_2.scale"] = torch.full((dim,), 1e-4)
+    finally:
+        torch.random.set_rng_state(rng_state)
+    return state
+
+
+def synth_track(seconds: float, seed: int, samplerate: int = 44100) -> torch.Tensor:
+    """Synthetic stereo mixture ``[2, round(seconds * samplerate)]`` in fp32.
+
+    Per channel: 8 sinusoids with log-uniform frequencies over 40-8000 Hz and
+    amplitudes U(0.05, 0.3), pink noise at -20 dB relative to the sinusoid RMS,
+    and a decaying impulse train at 120 BPM; the mix is normalised to 0.9 peak.
+
+    :param seconds: Duration in seconds.
+    :param seed: Generator seed.
+    :param samplerate: Sample rate in Hz.
+    :return: ``[2, samples]`` float32 tensor.
+    """
+    rng = np.random.default_rng(seed)
+    n = int(round(seconds * samplerate))
+    t = np.arange(n, dtype=np.float64) / samplerate
+    out = np.zeros((2, n), dtype=np.float64)
+    for ch in range(2):
+        freqs = np.exp(rng.uniform(math.log(40.0), math.log(8000.0), 8))
+        amps = rng.uniform(0.05, 0.3, 8)
+        phases = rng.uniform(0, 2 * math.pi, 8)
+        tone = np.zeros(n)
+        for f, a, ph in zip(freqs, amps, phases):
+            tone += a * np.sin(2 * math.pi * f * t + ph)
+        # Pink noise: white noise shaped by 1/sqrt(f) in the frequency domain.
+        white = rng.standard_normal(n)
+        spec = np.fft.rfft(white)
+        k = np.arange(spec.shape[0], dtype=np.float64)
+        k[0] = 1.0
+        pink = np.fft.irfft(spec / np.sqrt(k), n=n)
+        tone_rms = np.sqrt(np.mean(tone**2)) + 1e-12
+        pink *= (tone_rms * 10 ** (-20 / 20)) / (np.sqrt(np.mean(pink**2)) + 1e-12)
+        # Impulse train: one click per beat at 120 BPM with exponential decay.
+        clicks = np.zeros(n)
+        beat = int(samplerate * 60 / 120)
+        decay = np.exp(-np.arange(min(beat, 4410)) / (0.01 * samplerate))
+        for start in range(0, n, beat):
+            seg = decay[: n - start]
+            clicks[start : start + seg.shape[0]] += 0.5 * seg * rng.uniform(0.5, 1.0)
+        out[ch] = tone + pink + clicks
+    peak = np.abs(out).max()
+    if peak > 0:
+        out *= 0.9 / peak
+    return torch.from_numpy(out.astype(np.float32))
