@@ -1,0 +1,270 @@
+#!/usr/bin/env python
+"""Throughput of the segmented HTDemucs separation forward on B200.
+
+Metric: audio-seconds separated per second (x realtime), HTDemucs 4-stem
+(registry ``htdemucs`` architecture, random init under seed 0), 44.1 kHz
+stereo, overlap 0.25, segments batched 32 per forward, fp32. One step is one
+pass of ``apply_model`` over one 180 s synthetic track (31 segments). With N
+ranks (torchrun) every rank separates its own 180 s track (seed 1 + rank):
+whole tracks per rank, no data-path collective, weak scaling.
+
+* ``value``: track resident in HBM before the timed region; K steps timed with
+  CUDA events between barriers; max over ranks.
+* ``e2e``: the same step through the public API with a pinned host track:
+  host->device copy, separation, device->host copy of the stems, per step.
+* ``roofline``: the dominant kernel's algorithmic FLOPs per launch over its
+  mean launch time (CUDA events around each launch in one extra probed step),
+  against the measured peak in MEASURED_PEAKS.json.
+* ``cpu_baseline``: the CPU oracle (a restatement of the reference's fp32 CPU
+  forward) on a bounded 30 s sample, rank 0 at N=1 only.
+
+``--impl reference`` times that CPU implementation alone (the reference path
+runs only on host cores; there is no reference GPU kernel to run).
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+TRACK_SECONDS = 180.0
+BATCH = 32
+CPU_SAMPLE_SECONDS = 30.0
+METRIC = "audio-sec separated/sec (x realtime), HTDemucs 44.1kHz stereo"
+
+
+def _args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def _dist():
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def _peaks() -> dict:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        d = json.load(open(path))
+        return {"hbm": d["hbm_gbs"], "bf16": d["bf16_tflops"], "src": "measured"}
+    return {"hbm": 6650.0, "bf16": 1590.0, "src": "fallback"}
+
+
+class Clocks:
+    """Samples nvidia-smi clocks / throttle reasons during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = tempfile.mktemp(suffix=".csv")
+
+    def start(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        self.proc.wait()
+        self.f.close()
+        sms, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sms.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sms) if sms else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sms)}
+
+
+def cpu_baseline(seconds: float = CPU_SAMPLE_SECONDS) -> dict:
+    """The oracle (fp32 CPU restatement of the reference forward) over a bounded sample."""
+    import torch
+
+    from oracle.apply_oracle import apply_model as oracle_apply
+    from oracle.htdemucs_oracle import htdemucs_forward, segment_length
+    from unblend_b200.synth import htdemucs_config, htdemucs_state_dict, synth_track
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    cfg = htdemucs_config("htdemucs")
+    sd = htdemucs_state_dict(cfg, 0)
+    mix = synth_track(seconds, 1)[None]
+    fwd = lambda b: htdemucs_forward(sd, b, cfg)  # noqa: E731
+    fwd(mix[..., : segment_length(cfg)])  # warm-up segment
+    t0 = time.perf_counter()
+    oracle_apply(fwd, mix, 4, segment_length(cfg), cfg["samplerate"], overlap=0.25, chunk_batch_size=BATCH)
+    dt = time.perf_counter() - t0
+    return {"value": seconds / dt, "unit": "audio-s/s", "cores": cores, "kind": "port",
+            "sample": f"oracle apply_model over a {seconds:.0f} s synthetic track (seed 1), fp32, overlap 0.25"}
+
+
+def run_reference(args) -> None:
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    vals = []
+    for _ in range(max(1, args.steps)):
+        vals.append(cpu_baseline(CPU_SAMPLE_SECONDS / 2))
+    v = statistics.median(x["value"] for x in vals)
+    base = dict(vals[0])
+    base["value"] = v
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "audio-s/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "dtype": "f32", "data": "synthetic", "vs_baseline": None,
+            "config": {"workload": "HTDemucs 4-stem fp32 apply_model on host cores (bounded sample)",
+                       "overlap": 0.25},
+            "cpu_baseline": base, "e2e": {"value": v, "unit": "audio-s/s", "h2d_bytes_per_step": 0,
+                                          "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    args = _args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    import torch
+    import torch.distributed as dist
+
+    from unblend_b200 import _lib
+    from unblend_b200.apply import apply_model
+    from unblend_b200.htdemucs import HTDemucsCuda
+    from unblend_b200.synth import htdemucs_config, htdemucs_state_dict, synth_track
+
+    world, rank, local = _dist()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    cfg = htdemucs_config("htdemucs")
+    model = HTDemucsCuda(cfg, htdemucs_state_dict(cfg, 0)).to(dev)
+    track = synth_track(TRACK_SECONDS, 1 + rank)
+    track_dev = track.to(dev)
+    step = lambda: apply_model(model, track_dev, chunk_batch_size=BATCH)  # noqa: E731
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    def timed(fn, k):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(k):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ms = s.elapsed_time(e) / k
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    clocks = Clocks(dev.index if world == 1 else local)
+    launches0 = _lib.counters["launches"]
+    clocks.start()
+    ms = timed(step, args.steps)
+    clk = clocks.stop()
+    launches = _lib.counters["launches"] - launches0
+
+    # End to end through the public API with a pinned host track.
+    host = track.pin_memory()
+    e2e_step = lambda: apply_model(model, host, device=dev, chunk_batch_size=BATCH)  # noqa: E731
+    e2e_step()
+    e2e_ms = timed(e2e_step, max(1, args.steps))
+
+    # Roofline of the dominant kernel: one probed step with events around each launch.
+    _lib.probe = []
+    step()
+    torch.cuda.synchronize()
+    agg: dict = {}
+    for name, s, e, work in _lib.probe:
+        a = agg.setdefault(name, {"ms": 0.0, "n": 0, "work": 0.0})
+        a["ms"] += s.elapsed_time(e)
+        a["n"] += 1
+        a["work"] += work or 0.0
+    _lib.probe = None
+    top = max(agg, key=lambda k: agg[k]["ms"])
+    peaks = _peaks()
+    a = agg[top]
+    tflops = a["work"] / (a["ms"] * 1e-3) / 1e12 if a["ms"] > 0 else 0.0
+    roofline = {"kernel": top, "bound": "tensor", "achieved": round(tflops, 3), "peak": peaks["bf16"],
+                "unit": "TFLOP/s", "frac": round(tflops / peaks["bf16"], 5), "traffic": None,
+                "peak_source": f"{peaks['src']} bf16 dense (burst)",
+                "share_of_step": round(a["ms"] / sum(v["ms"] for v in agg.values()), 3),
+                "launches_per_step": a["n"]}
+
+    value = world * TRACK_SECONDS / (ms * 1e-3)
+    e2e_value = world * TRACK_SECONDS / (e2e_ms * 1e-3)
+    L = track.shape[-1]
+    line = {"metric": METRIC, "value": round(value, 3), "unit": "audio-s/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "HTDemucs 4-stem, 180 s stereo track, 31 segments of 7.8 s, overlap 0.25, "
+                                   "32 segments per launch", "track_seconds": TRACK_SECONDS, "segments_per_launch": BATCH,
+                       "parallelism": f"whole tracks per rank x{world}",
+                       "l2": "inputs and activations far larger than L2 (no flush needed)"},
+            "e2e": {"value": round(e2e_value, 3), "unit": "audio-s/s", "h2d_bytes_per_step": 2 * L * 4,
+                    "d2h_bytes_per_step": 4 * 2 * L * 4},
+            "gpu_launches": launches, "roofline": roofline, "clocks": clk,
+            "kernels": {k: {"ms": round(v["ms"], 3), "n": v["n"]} for k, v in sorted(agg.items(), key=lambda kv: -kv[1]["ms"])}}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

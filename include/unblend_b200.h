@@ -1,0 +1,192 @@
+/*
+ * unblend_b200 — C ABI of the B200 (sm_100a) segmented separation forward.
+ *
+ * Every entry point is stream-ordered on the `stream` argument (a
+ * cudaStream_t passed as void*), never synchronises, allocates nothing, and
+ * returns 0 on success or a positive code (a cudaError_t value, or
+ * UNBLEND_ERR_INVALID for bad arguments). The caller owns all memory: inputs,
+ * outputs and workspaces are plain device pointers. Activations are
+ * channels-last float32 unless a field says otherwise.
+ *
+ * The reference (Python/PyTorch) has no FFI for this path; each entry point
+ * replaces the torch operator sequence named beside it, with the reference
+ * file:line it restates.
+ */
+#ifndef UNBLEND_B200_H
+#define UNBLEND_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define UNBLEND_ERR_INVALID 1000
+
+/* Activation applied in a convolution epilogue. */
+enum UnblendAct {
+  UNBLEND_ACT_NONE = 0,
+  UNBLEND_ACT_GELU = 1, /* exact erf GELU, F.gelu */
+  UNBLEND_ACT_GLU = 2   /* F.glu over interleaved (value, gate) column pairs */
+};
+
+/* Transform applied to each input element as it is loaded. */
+enum UnblendPrologue {
+  UNBLEND_PRO_NONE = 0,
+  UNBLEND_PRO_GN_GELU = 1, /* gelu((x - mean[g]) * rstd[g] * gamma[c] + beta[c]) */
+  UNBLEND_PRO_ADD = 2      /* x + x2 (decoder skip connection) */
+};
+
+/*
+ * Implicit-GEMM 2-D convolution over a channels-last tensor:
+ *   y[b,ho,wo,n] = bias[n] + sum_{kh,kw,c} A(b, ho*sh+kh*dh-ph, wo*sw+kw*dw-pw, c) * w[n,kh,kw,c]
+ * with zero padding outside [0,h_in) x [0,w_in). Covers every Conv1d/Conv2d
+ * and Linear of the path (1-D convs use h=1; linears use h=1, kernel 1x1).
+ * Weights are [n_out, kh, kw, c_in] row-major (K contiguous).
+ * Output element (b,ho,wo,n') with n' = n (or n/2 after GLU) is written to
+ *   out + b*out_sb + ho*out_sh + wo*out_sw + (n'/n_group)*out_sg + n'%n_group.
+ * Epilogue order: bias, activation, then `out = res + scale[n'] * y` when
+ * `res` is set (res may alias out), then optional GroupNorm statistics
+ * (sum, sum of squares in double) per group (b) or (b, ho).
+ */
+typedef struct {
+  int batch, h_in, w_in, c_in;
+  long long in_sb, in_sh, in_sw;
+  int h_out, w_out, n_out;
+  int kh, kw, sh, sw, dh, dw, ph, pw;
+  long long out_sb, out_sh, out_sw, out_sg;
+  int n_group;
+  int act;            /* UnblendAct */
+  int prologue;       /* UnblendPrologue */
+  /* prologue GN: float (mean, rstd) per group g = pro_group_per_h ? b*h_in + hi : b */
+  const float* pro_stats;
+  const float* pro_gamma;
+  const float* pro_beta;
+  int pro_group_per_h;
+  const float* pro_x2; /* UNBLEND_PRO_ADD: second input, same strides as the input */
+  /* residual epilogue */
+  const float* res;
+  const float* res_scale; /* [n'] or NULL for scale 1 */
+  /* statistics epilogue: double[2*groups], group = b*(stats_per_h ? h_out : 1) + ... */
+  double* stats;
+  int stats_per_h;
+} UnblendConvParams;
+
+/* Conv1d / Conv2d / Linear (unblend/blocks.py:461,467,695,297,300; torch nn.Linear in
+ * unblend/transformer.py:290-301,402-412) as an implicit GEMM, fp32 SIMT path. */
+int unblend_conv2d_f32(const float* x, const float* w, const float* bias, float* y,
+                       const UnblendConvParams* p, void* stream);
+
+/* Per-group mean / rstd from the double (sum, sumsq) statistics:
+ * mean = s/n, var = (sq - s*mean)/(n - unbiased), rstd = 1/sqrt(var + eps) when
+ * `std_mode` is 0 (GroupNorm / LayerNorm); when 1, writes std = sqrt(var) and
+ * the normaliser 1/(1e-5 + std) (HTDemucs input normalisation,
+ * unblend/htdemucs.py:671-678). out: float[2*groups] = (mean, rstd_or_inv). */
+int unblend_stats_finalize(const double* stats, float* out, int groups, double count,
+                           float eps, int unbiased, int std_mode, void* stream);
+
+/* Zero a double buffer (statistics accumulators). */
+int unblend_zero_f64(double* p, long long n, void* stream);
+
+/* Sum / sum of squares per group of a contiguous [groups, n] fp32 array (double). */
+int unblend_group_sums(const float* x, double* stats, int groups, long long n, void* stream);
+
+/*
+ * Normalise + optionally apply affine + activation elementwise:
+ *   y[r, c] = act((x[r,c] - mean[g]) * rstd[g] * gamma[c] + beta[c])
+ * for rows r of a [rows, c] tensor with group g = r / rows_per_group.
+ * gamma/beta may be NULL (1 and 0). act: UnblendAct (GLU not allowed).
+ */
+int unblend_group_norm_apply(const float* x, float* y, const float* stats2, const float* gamma,
+                             const float* beta, long long rows, int c, long long rows_per_group,
+                             int act, void* stream);
+
+/* DConv tail (unblend/blocks.py:293-317): x += scale * glu(gn(z)) per element.
+ * z is contiguous [groups, rows_per_group, 2c] with interleaved (value, gate)
+ * columns and GroupNorm(1) stats2 = (mean, rstd) per group; x element
+ * (g, r, ch) lives at x + g*x_group_stride + r*c + ch. gamma/beta are in the
+ * interleaved column order of z. */
+int unblend_dconv_tail(float* x, const float* z, const float* stats2, const float* gamma,
+                       const float* beta, const float* scale, long long groups,
+                       long long rows_per_group, int c, long long x_group_stride, void* stream);
+
+/* LayerNorm over the last dim (eps 1e-5) with optional additive table:
+ * y[r,:] = ln(x[r,:]) * gamma + beta + (pos ? pos_scale * pos[r % pos_rows, :] : 0). */
+int unblend_layer_norm(const float* x, float* y, const float* gamma, const float* beta,
+                       const float* pos, float pos_scale, long long pos_rows, long long rows,
+                       int c, void* stream);
+
+/* Multi-head attention core softmax(Q K^T * scale) V for all heads
+ * (torch nn.MultiheadAttention, unblend/transformer.py:290-301, 402-412).
+ * Q rows are [b, lq, q_stride] with head h at columns h*hd; K, V likewise.
+ * Output [b, lq, heads*hd]. */
+int unblend_attention_f32(const float* q, const float* k, const float* v, float* out, int batch,
+                          int heads, int lq, int lk, int hd, long long q_sb, long long q_sr,
+                          long long kv_sb, long long kv_sr, long long o_sb, long long o_sr,
+                          float scale, void* stream);
+
+/* Elementwise y[i] = a[i] + alpha * b[i % b_period] (skip adds, embeddings). */
+int unblend_add(const float* a, const float* b, float* y, long long n, long long b_period,
+                float alpha, void* stream);
+
+/*
+ * HTDemucs STFT front end (unblend/htdemucs.py:370-395, unblend/blocks.py:60-88):
+ * mix [batch, 2, length] (channel-first, as given to forward) ->
+ * spec [batch, nfft/2, frames, 4] channels-last CaC (c0.re, c0.im, c1.re, c1.im),
+ * frames = ceil(length / hop), hop = nfft/4, Hann window (periodic), normalized.
+ * window: float[nfft]. Only nfft = 4096 is supported.
+ */
+int unblend_stft_cac(const float* mix, float* spec, const float* window, int batch, int length,
+                     int nfft, void* stream);
+
+/* y = (x - mean[b]) / (1e-5 + std[b]) over a contiguous [batch, n] array with
+ * stats2 = (mean, std) per batch (unblend/htdemucs.py:671-673). */
+int unblend_standardize(const float* x, float* y, const float* stats2, long long n_per_batch,
+                        int batch, void* stream);
+
+/* Transpose + normalise the time branch input: mix [b, 2, L] -> xt [b, L_pad, 2]
+ * with (x - mean[b]) / (1e-5 + std[b]); rows L..L_pad-1 are zero. stats2 = (mean, std) per b. */
+int unblend_time_input(const float* mix, float* xt, const float* stats2, int batch, int length,
+                       int length_pad, void* stream);
+
+/*
+ * HTDemucs output stage (unblend/htdemucs.py:692-704, _ispec :397-412,
+ * ispectro unblend/blocks.py:165-204):
+ *   out[b,s,c,n] = istft(spec*std+mean)[b,s,c,n] + xt[b, n, s*2+c] * stdt + meant
+ * spec: [batch, nfft/2, frames, S*4] channels-last CaC; xt: [batch, >=length, S*2];
+ * fstats/tstats: float (mean, std) per batch; frames_buf: workspace of
+ * batch*S*2*frames*nfft floats. out: [batch, S, 2, length].
+ */
+int unblend_istft_output(const float* spec, const float* xt, long long xt_sb, const float* fstats,
+                         const float* tstats, const float* window, float* frames_buf, float* out,
+                         int batch, int sources, int length, int nfft, void* stream);
+
+/* Per-batch (mean, std) with torch.var_mean semantics (unbiased) of a contiguous
+ * [batch, n] array; out float[2*batch] = (mean, std). Uses `work` double[2*batch]. */
+int unblend_mean_std(const float* x, double* work, float* out, int batch, long long n,
+                     void* stream);
+
+/* Segment engine (unblend/apply.py:278-311, 406-432, 1219-1238, 1329). */
+/* Gather centred, zero-padded chunks: batch[i, c, :] = track[c, start_i ...] for
+ * i < n, where start_i = offsets[i] - (segment - min(L - offsets[i], segment)) / 2.
+ * offsets is a device array of n int64 values. */
+int unblend_gather_chunks(const float* track, int channels, long long length, const long long* offsets,
+                          int n, int segment, float* batch, void* stream);
+
+/* Weighted overlap-add of model outputs y[i, rows, segment] (rows = S*C) into
+ * acc[rows, L] and sum_w[L] with the triangular weight (transition power 1),
+ * after the centre trim of short chunks. Positions [lo, hi) are visited; they
+ * must cover every position the n chunks touch. */
+int unblend_overlap_add(const float* y, int n, int rows, int segment, const long long* offsets,
+                        long long length, long long lo, long long hi, float* acc, float* sum_w,
+                        void* stream);
+
+/* out = acc / sum_w (broadcast over [S*C, L]). */
+int unblend_divide(const float* acc, const float* sum_w, float* out, int rows, long long length,
+                   void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* UNBLEND_B200_H */

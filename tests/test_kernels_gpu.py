@@ -1,0 +1,260 @@
+"""Per-kernel parity on the GPU: each C-ABI entry point against a plain PyTorch
+fp32 reference of the same operation (small, odd shapes and edge cases, in the
+manner of the reference's tests/test_metal_kernels.py)."""
+
+from __future__ import annotations
+
+import ctypes
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from conftest import rel_err
+from unblend_b200 import _lib
+from unblend_b200._lib import ACT_GELU, ACT_GLU, ACT_NONE, PRO_ADD, PRO_GN_GELU, PRO_NONE, ConvParams
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-5
+
+
+def _ref_conv(x, w, b, kh, kw, sh, sw, dh, dw, ph, pw):
+    """x [B,H,W,C], w [N,KH,KW,C] -> [B,Ho,Wo,N] via F.conv2d."""
+    y = F.conv2d(x.permute(0, 3, 1, 2), w.permute(0, 3, 1, 2), b, (sh, sw), (ph, pw), (dh, dw))
+    return y.permute(0, 2, 3, 1)
+
+
+def _conv(x, w, b, y, *, B, H, W, C, in_s, Ho, Wo, N, out_s, kh=1, kw=1, sh=1, sw=1, dh=1, dw=1, ph=0, pw=0,
+          act=ACT_NONE, prologue=PRO_NONE, pro_stats=None, pro_gamma=None, pro_beta=None, pro_per_h=0,
+          pro_x2=None, res=None, res_scale=None, stats=None, stats_per_h=0, n_group=None, out_sg=0):
+    p = ConvParams()
+    p.batch, p.h_in, p.w_in, p.c_in = B, H, W, C
+    p.in_sb, p.in_sh, p.in_sw = in_s
+    p.h_out, p.w_out, p.n_out = Ho, Wo, N
+    p.kh, p.kw, p.sh, p.sw, p.dh, p.dw, p.ph, p.pw = kh, kw, sh, sw, dh, dw, ph, pw
+    p.out_sb, p.out_sh, p.out_sw = out_s
+    p.out_sg = out_sg
+    p.n_group = n_group or (N // 2 if act == ACT_GLU else N)
+    p.act, p.prologue = act, prologue
+    p.pro_stats, p.pro_gamma, p.pro_beta = _lib.ptr(pro_stats), _lib.ptr(pro_gamma), _lib.ptr(pro_beta)
+    p.pro_group_per_h = pro_per_h
+    p.pro_x2 = _lib.ptr(pro_x2)
+    p.res, p.res_scale = _lib.ptr(res), _lib.ptr(res_scale)
+    p.stats, p.stats_per_h = _lib.ptr(stats), stats_per_h
+    _lib.call("unblend_conv2d_f32", x.data_ptr(), w.data_ptr(), _lib.ptr(b), y.data_ptr(), ctypes.byref(p))
+
+
+def _cl(shape):
+    return torch.randn(*shape, device="cuda")
+
+
+@pytest.mark.parametrize("B,H,W,C,N,kh,sh,ph", [(2, 32, 13, 4, 12, 8, 4, 2), (1, 16, 70, 9, 130, 8, 4, 2)])
+def test_conv_freq_encoder_gelu(B, H, W, C, N, kh, sh, ph):
+    x, w, b = _cl((B, H, W, C)), _cl((N, kh, 1, C)) * 0.2, _cl((N,))
+    Ho = (H + 2 * ph - kh) // sh + 1
+    y = torch.empty(B, Ho, W, N, device="cuda")
+    _conv(x, w, b, y, B=B, H=H, W=W, C=C, in_s=(H * W * C, W * C, C), Ho=Ho, Wo=W, N=N,
+          out_s=(Ho * W * N, W * N, N), kh=kh, sh=sh, ph=ph, act=ACT_GELU)
+    ref = F.gelu(_ref_conv(x, w, b, kh, 1, sh, 1, 1, 1, ph, 0))
+    assert rel_err(y, ref) < TOL
+
+
+def test_conv_time_strided_rows_with_capacity():
+    B, L, cap, C, N = 2, 37, 40, 3, 10
+    xs = _cl((B, cap, C))
+    w, b = _cl((N, 1, 8, C)) * 0.3, _cl((N,))
+    Wo = -(-L // 4)
+    y = torch.full((B, 12, N), float("nan"), device="cuda")
+    _conv(xs, w, b, y, B=B, H=1, W=L, C=C, in_s=(cap * C, cap * C, C), Ho=1, Wo=Wo, N=N,
+          out_s=(12 * N, 12 * N, N), kw=8, sw=4, pw=2)
+    xp = F.pad(xs[:, :L].permute(0, 2, 1), (0, 4 - L % 4))
+    ref = F.conv1d(xp, w[:, 0].permute(0, 2, 1), b, 4, 2).permute(0, 2, 1)
+    assert rel_err(y[:, :Wo], ref) < TOL
+    assert torch.isnan(y[:, Wo:]).all()  # rows past the output length are untouched
+
+
+def test_conv_dilated_with_group_stats():
+    B, H, W, C, N = 2, 5, 41, 16, 2
+    x, w, b = _cl((B, H, W, C)), _cl((N, 1, 3, C)) * 0.2, _cl((N,))
+    y = torch.empty(B, H, W, N, device="cuda")
+    st = torch.zeros(2 * B * H, device="cuda", dtype=torch.float64)
+    _conv(x, w, b, y, B=B, H=H, W=W, C=C, in_s=(H * W * C, W * C, C), Ho=H, Wo=W, N=N,
+          out_s=(H * W * N, W * N, N), kw=3, dw=2, pw=2, stats=st, stats_per_h=1)
+    ref = _ref_conv(x, w, b, 1, 3, 1, 1, 1, 2, 0, 2)
+    assert rel_err(y, ref) < TOL
+    r = ref.double().reshape(B * H, -1)
+    assert torch.allclose(st[0::2], r.sum(1), rtol=1e-6, atol=1e-6)
+    assert torch.allclose(st[1::2], r.pow(2).sum(1), rtol=1e-6)
+
+
+def test_conv_gn_gelu_prologue_and_glu_epilogue():
+    B, H, W, C, N = 2, 3, 50, 6, 20
+    x = _cl((B, H, W, C)) * 3 + 1
+    w, b = _cl((N, 1, 1, C)) * 0.3, _cl((N,))
+    g, be = _cl((C,)), _cl((C,))
+    xg = x.reshape(B * H, -1).double()
+    mean, var = xg.mean(1), xg.var(1, unbiased=False)
+    st = torch.stack([mean, 1.0 / torch.sqrt(var + 1e-5)], 1).float().reshape(-1).contiguous()
+    y = torch.empty(B, H, W, N // 2, device="cuda")
+    _conv(x, w, b, y, B=B, H=H, W=W, C=C, in_s=(H * W * C, W * C, C), Ho=H, Wo=W, N=N,
+          out_s=(H * W * N // 2, W * N // 2, N // 2), act=ACT_GLU, prologue=PRO_GN_GELU, pro_stats=st,
+          pro_gamma=g, pro_beta=be, pro_per_h=1)
+    xn = F.group_norm(x.permute(0, 1, 3, 2).reshape(B * H, C, W), 1, g, be, 1e-5)
+    xn = F.gelu(xn).reshape(B, H, C, W).permute(0, 1, 3, 2)
+    z = _ref_conv(xn, w, b, 1, 1, 1, 1, 1, 1, 0, 0)
+    ref = z[..., 0::2] * torch.sigmoid(z[..., 1::2])
+    assert rel_err(y, ref) < TOL
+
+
+def test_conv_skip_add_3x3_glu():
+    B, H, W, C, N = 1, 9, 17, 12, 24
+    x, s = _cl((B, H, W, C)), _cl((B, H, W, C))
+    w, b = _cl((N, 3, 3, C)) * 0.1, _cl((N,))
+    y = torch.empty(B, H, W, N // 2, device="cuda")
+    _conv(x, w, b, y, B=B, H=H, W=W, C=C, in_s=(H * W * C, W * C, C), Ho=H, Wo=W, N=N,
+          out_s=(H * W * N // 2, W * N // 2, N // 2), kh=3, kw=3, ph=1, pw=1, act=ACT_GLU,
+          prologue=PRO_ADD, pro_x2=s)
+    z = _ref_conv(x + s, w, b, 3, 3, 1, 1, 1, 1, 1, 1)
+    assert rel_err(y, z[..., 0::2] * torch.sigmoid(z[..., 1::2])) < TOL
+
+
+def test_linear_residual_layerscale_with_stats_inplace():
+    B, L, K, N = 3, 77, 64, 48
+    x, w, b = _cl((B, L, K)), _cl((N, 1, 1, K)) * 0.1, _cl((N,))
+    res, sc = _cl((B, L, N)), _cl((N,))
+    out = res.clone()
+    st = torch.zeros(2 * B, device="cuda", dtype=torch.float64)
+    _conv(x, w, b, out, B=B, H=1, W=L, C=K, in_s=(L * K, L * K, K), Ho=1, Wo=L, N=N,
+          out_s=(L * N, L * N, N), res=out, res_scale=sc, stats=st)
+    ref = res + sc * (x @ w[:, 0, 0].t() + b)
+    assert rel_err(out, ref) < TOL
+    assert torch.allclose(st[0::2], ref.double().reshape(B, -1).sum(1), rtol=1e-6, atol=1e-6)
+
+
+@pytest.mark.parametrize("freq", [True, False])
+def test_transposed_conv_phase_split(freq):
+    from unblend_b200.htdemucs import _convtr_phases
+
+    B, P, T, Cin, Cout = 2, 7, 5, 12, 6
+    wt, bias = torch.randn(Cin, Cout, 8) * 0.2, torch.randn(Cout)
+    lo, hi = _convtr_phases(wt)
+    lo, hi, b2 = lo.cuda(), hi.cuda(), bias.repeat(2).cuda()
+    if freq:
+        x = _cl((B, P, T, Cin))
+        out = torch.empty(B, 4 * P, T, Cout, device="cuda")
+        row = T * Cout
+        for wgt, ph, base in ((lo, 1, 0), (hi, 0, 2)):
+            _conv(x, wgt, b2, out.view(-1)[base * row:], B=B, H=P, W=T, C=Cin, in_s=(P * T * Cin, T * Cin, Cin),
+                  Ho=P, Wo=T, N=2 * Cout, out_s=(4 * P * T * Cout, 4 * row, Cout), kh=2, ph=ph, n_group=Cout,
+                  out_sg=row)
+        ref = F.conv_transpose2d(x.permute(0, 3, 1, 2), wt[..., None].cuda(), bias.cuda(), (4, 1))
+        ref = ref[:, :, 2:-2, :].permute(0, 2, 3, 1)
+    else:
+        x = _cl((B, P, Cin))
+        out = torch.empty(B, 4 * P, Cout, device="cuda")
+        for wgt, pw, base in ((lo, 1, 0), (hi, 0, 2)):
+            _conv(x, wgt, b2, out.view(-1)[base * Cout:], B=B, H=1, W=P, C=Cin, in_s=(P * Cin, P * Cin, Cin),
+                  Ho=1, Wo=P, N=2 * Cout, out_s=(4 * P * Cout, 4 * P * Cout, 4 * Cout), kw=2, pw=pw,
+                  n_group=Cout, out_sg=Cout)
+        ref = F.conv_transpose1d(x.permute(0, 2, 1), wt.cuda(), bias.cuda(), 4)[:, :, 2:2 + 4 * P]
+        ref = ref.permute(0, 2, 1)
+    assert rel_err(out, ref) < TOL
+
+
+@pytest.mark.parametrize("lq,lk,heads,hd", [(100, 70, 3, 64), (130, 64, 2, 48), (9, 200, 4, 8)])
+def test_attention(lq, lk, heads, hd):
+    B, D = 2, heads * hd
+    q, k, v = _cl((B, lq, D)), _cl((B, lk, D)), _cl((B, lk, D))
+    o = torch.empty(B, lq, D, device="cuda")
+    _lib.call("unblend_attention_f32", q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), B, heads, lq, lk,
+              hd, lq * D, D, lk * D, D, lq * D, D, 1.0 / math.sqrt(hd))
+    qh = q.view(B, lq, heads, hd).transpose(1, 2)
+    kh = k.view(B, lk, heads, hd).transpose(1, 2)
+    vh = v.view(B, lk, heads, hd).transpose(1, 2)
+    ref = (torch.softmax(qh @ kh.transpose(-1, -2) / math.sqrt(hd), -1) @ vh).transpose(1, 2).reshape(B, lq, D)
+    assert rel_err(o, ref) < TOL
+
+
+def test_layer_norm_with_positional_table():
+    rows, c, prow = 50, 512, 25
+    x, g, b, pos = _cl((rows, c)) * 2 + 3, _cl((c,)), _cl((c,)), _cl((prow, c))
+    y = torch.empty_like(x)
+    _lib.call("unblend_layer_norm", x.data_ptr(), y.data_ptr(), g.data_ptr(), b.data_ptr(), pos.data_ptr(), 1.0,
+              prow, rows, c)
+    ref = F.layer_norm(x, (c,), g, b, 1e-5) + pos.repeat(2, 1)
+    assert rel_err(y, ref) < TOL
+
+
+def test_group_norm_apply_and_mean_std():
+    B, n = 3, 10007
+    x = _cl((B, n)) * 5 + 2
+    work = torch.empty(2 * B, device="cuda", dtype=torch.float64)
+    st = torch.empty(2 * B, device="cuda")
+    _lib.call("unblend_mean_std", x.data_ptr(), work.data_ptr(), st.data_ptr(), B, n)
+    var, mean = torch.var_mean(x.double(), dim=1)
+    assert torch.allclose(st[0::2].double(), mean, rtol=1e-6, atol=1e-6)
+    assert torch.allclose(st[1::2].double(), var.sqrt(), rtol=1e-6)
+    y = torch.empty_like(x)
+    _lib.call("unblend_standardize", x.data_ptr(), y.data_ptr(), st.data_ptr(), n, B)
+    assert rel_err(y, (x - mean[:, None].float()) / (1e-5 + var.sqrt()[:, None].float())) < TOL
+
+
+def test_stft_front_end():
+    from oracle.htdemucs_oracle import _spec
+
+    mix = _cl((2, 2, 30000)) * 0.3
+    frames = -(-30000 // 1024)
+    spec = torch.empty(2, 2048, frames, 4, device="cuda")
+    win = torch.hann_window(4096, device="cuda")
+    _lib.call("unblend_stft_cac", mix.data_ptr(), spec.data_ptr(), win.data_ptr(), 2, 30000, 4096)
+    z = _spec(mix.cpu(), 4096)  # [B, 2, 2048, frames] complex
+    ref = torch.view_as_real(z).permute(0, 2, 3, 1, 4).reshape(2, 2048, frames, 4)
+    assert rel_err(spec, ref) < 1e-5
+
+
+def test_istft_output_stage():
+    from oracle.htdemucs_oracle import _ispec
+
+    B, S, L = 2, 3, 30000
+    frames = -(-L // 1024)
+    spec = _cl((B, 2048, frames, S * 4)) * 0.1
+    xt = _cl((B, L + 3, S * 2)) * 0.1
+    fst = torch.tensor([0.01, 1.5, -0.02, 0.7], device="cuda")
+    tst = torch.tensor([0.03, 0.4, 0.0, 2.0], device="cuda")
+    win = torch.hann_window(4096, device="cuda")
+    fb = torch.empty(B * S * 2 * frames * 4096, device="cuda")
+    out = torch.empty(B, S, 2, L, device="cuda")
+    _lib.call("unblend_istft_output", spec.data_ptr(), xt.data_ptr(), (L + 3) * S * 2, fst.data_ptr(),
+              tst.data_ptr(), win.data_ptr(), fb.data_ptr(), out.data_ptr(), B, S, L, 4096)
+    sc = spec.cpu().view(B, 2048, frames, S, 2, 2)  # (s, c, ri)
+    den = sc * fst.cpu()[1::2].view(B, 1, 1, 1, 1, 1) + fst.cpu()[0::2].view(B, 1, 1, 1, 1, 1)
+    zc = torch.view_as_complex(den.permute(0, 3, 4, 1, 2, 5).contiguous())  # [B, S, 2, F, T]
+    xs = _ispec(zc, L, 4096)
+    xtt = xt.cpu()[:, :L].view(B, L, S, 2).permute(0, 2, 3, 1)
+    ref = xs + xtt * tst.cpu()[1::2].view(B, 1, 1, 1) + tst.cpu()[0::2].view(B, 1, 1, 1)
+    assert rel_err(out, ref) < 1e-5
+
+
+def test_segment_engine_pointwise_model():
+    from oracle.apply_oracle import apply_unshifted
+
+    C, L, seg, stride = 2, 10000, 3000, 2250
+    track = _cl((C, L))
+    offsets = list(range(0, L, stride))
+    acc = torch.zeros(2 * C, L, device="cuda")
+    sw = torch.zeros(L, device="cuda")
+    for i in range(0, len(offsets), 3):
+        grp = offsets[i : i + 3]
+        off_t = torch.tensor(grp, device="cuda", dtype=torch.int64)
+        batch = torch.empty(len(grp), C, seg, device="cuda")
+        _lib.call("unblend_gather_chunks", track.data_ptr(), C, L, off_t.data_ptr(), len(grp), seg, batch.data_ptr())
+        y = torch.stack([batch, 2 * batch], 1).contiguous()  # [n, S=2, C, seg]
+        hi = min(L, grp[-1] + seg)
+        _lib.call("unblend_overlap_add", y.data_ptr(), len(grp), 2 * C, seg, off_t.data_ptr(), L, grp[0], hi,
+                  acc.data_ptr(), sw.data_ptr())
+    out = torch.empty_like(acc)
+    _lib.call("unblend_divide", acc.data_ptr(), sw.data_ptr(), out.data_ptr(), 2 * C, L)
+    ref = apply_unshifted(lambda b: torch.stack([b, 2 * b], 1), track.cpu()[None], 2, seg, 0.25, 3)
+    assert rel_err(out.view(1, 2, C, L), ref) < 1e-6
+    assert torch.allclose(out.view(2, C, L)[0], track, atol=1e-5)

@@ -1,0 +1,157 @@
+"""ctypes binding of the C ABI declared in ``include/unblend_b200.h``.
+
+The shared library is built in-tree (``python -m unblend_b200.build``). There is
+no fallback: if the library is missing or a launcher returns an error, the
+call raises. Launch errors carry the CUDA error text; an out-of-memory code is
+reported with the words "CUDA out of memory" so ``apply_model``'s OOM backoff
+(unblend/apply.py:32-53) still recognises it.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "_lib", "libunblend_b200.so")
+ERR_INVALID = 1000
+
+c_int = ctypes.c_int
+c_ll = ctypes.c_longlong
+c_float = ctypes.c_float
+c_double = ctypes.c_double
+c_void_p = ctypes.c_void_p
+
+ACT_NONE, ACT_GELU, ACT_GLU = 0, 1, 2
+PRO_NONE, PRO_GN_GELU, PRO_ADD = 0, 1, 2
+
+
+class ConvParams(ctypes.Structure):
+    """Mirror of ``UnblendConvParams``."""
+
+    _fields_ = [
+        ("batch", c_int), ("h_in", c_int), ("w_in", c_int), ("c_in", c_int),
+        ("in_sb", c_ll), ("in_sh", c_ll), ("in_sw", c_ll),
+        ("h_out", c_int), ("w_out", c_int), ("n_out", c_int),
+        ("kh", c_int), ("kw", c_int), ("sh", c_int), ("sw", c_int),
+        ("dh", c_int), ("dw", c_int), ("ph", c_int), ("pw", c_int),
+        ("out_sb", c_ll), ("out_sh", c_ll), ("out_sw", c_ll), ("out_sg", c_ll),
+        ("n_group", c_int), ("act", c_int), ("prologue", c_int),
+        ("pro_stats", c_void_p), ("pro_gamma", c_void_p), ("pro_beta", c_void_p),
+        ("pro_group_per_h", c_int), ("pro_x2", c_void_p),
+        ("res", c_void_p), ("res_scale", c_void_p),
+        ("stats", c_void_p), ("stats_per_h", c_int),
+    ]
+
+
+# name -> argtypes (all return int)
+_SIGNATURES = {
+    "unblend_conv2d_f32": [c_void_p, c_void_p, c_void_p, c_void_p, ctypes.POINTER(ConvParams), c_void_p],
+    "unblend_stats_finalize": [c_void_p, c_void_p, c_int, c_double, c_float, c_int, c_int, c_void_p],
+    "unblend_zero_f64": [c_void_p, c_ll, c_void_p],
+    "unblend_group_sums": [c_void_p, c_void_p, c_int, c_ll, c_void_p],
+    "unblend_group_norm_apply": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_ll, c_int, c_ll, c_int,
+                                 c_void_p],
+    "unblend_dconv_tail": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_ll, c_ll, c_int,
+                           c_ll, c_void_p],
+    "unblend_layer_norm": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_ll, c_ll, c_int,
+                           c_void_p],
+    "unblend_attention_f32": [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
+                              c_ll, c_ll, c_ll, c_ll, c_ll, c_ll, c_float, c_void_p],
+    "unblend_add": [c_void_p, c_void_p, c_void_p, c_ll, c_ll, c_float, c_void_p],
+    "unblend_standardize": [c_void_p, c_void_p, c_void_p, c_ll, c_int, c_void_p],
+    "unblend_stft_cac": [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p],
+    "unblend_time_input": [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p],
+    "unblend_istft_output": [c_void_p, c_void_p, c_ll, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                             c_int, c_int, c_int, c_int, c_void_p],
+    "unblend_mean_std": [c_void_p, c_void_p, c_void_p, c_int, c_ll, c_void_p],
+    "unblend_gather_chunks": [c_void_p, c_int, c_ll, c_void_p, c_int, c_int, c_void_p, c_void_p],
+    "unblend_overlap_add": [c_void_p, c_int, c_int, c_int, c_void_p, c_ll, c_ll, c_ll, c_void_p, c_void_p,
+                            c_void_p],
+    "unblend_divide": [c_void_p, c_void_p, c_void_p, c_int, c_ll, c_void_p],
+}
+
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Load the shared library (once) and declare every entry point."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(
+            f"unblend_b200 CUDA library not built ({LIB_PATH}); run `python -m unblend_b200.build`"
+        )
+    lib = ctypes.CDLL(LIB_PATH)
+    for name, args in _SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = c_int
+    _lib = lib
+    return lib
+
+
+def exported_symbols() -> list[str]:
+    """Entry points this binding declares (all must exist in the library)."""
+    return list(_SIGNATURES)
+
+
+def _cuda_error_string(code: int) -> str:
+    try:
+        from cuda.bindings import runtime as rt  # type: ignore
+
+        err, name = rt.cudaGetErrorName(rt.cudaError_t(code))
+        return name.decode() if isinstance(name, bytes) else str(name)
+    except Exception:  # pragma: no cover - best effort text only
+        return f"cudaError {code}"
+
+
+def check(name: str, rc: int) -> None:
+    """Raise ``RuntimeError`` for a non-zero launcher return code."""
+    if rc == 0:
+        return
+    if rc == ERR_INVALID:
+        raise RuntimeError(f"{name}: invalid arguments")
+    text = _cuda_error_string(rc)
+    if rc == 2:  # cudaErrorMemoryAllocation
+        raise RuntimeError(f"CUDA out of memory in {name} ({text})")
+    raise RuntimeError(f"{name} failed: {text} ({rc})")
+
+
+# Kernels launched by one call of each entry point (1 unless listed).
+KERNELS_PER_CALL = {"unblend_mean_std": 3, "unblend_istft_output": 2}
+
+# Launch accounting: total kernels launched through this binding.
+counters = {"launches": 0}
+
+# Optional per-launch timing probe: when a list, each call appends
+# (name, start_event, end_event, work) with CUDA events recorded on the
+# launching stream around the launch; ``work`` is the caller's algorithmic
+# FLOP count for the launch (or None).
+probe: list | None = None
+
+
+def call(name: str, *args, work: float | None = None) -> None:
+    """Invoke ``name`` with ``args`` (the trailing stream is appended) and check it."""
+    lib = load()
+    cur = torch.cuda.current_stream()
+    stream = c_void_p(cur.cuda_stream)
+    if probe is not None:
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(cur)
+        rc = getattr(lib, name)(*args, stream)
+        end.record(cur)
+        probe.append((name, start, end, work))
+    else:
+        rc = getattr(lib, name)(*args, stream)
+    counters["launches"] += KERNELS_PER_CALL.get(name, 1)
+    check(name, rc)
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    """Device pointer of a tensor (None stays None)."""
+    return None if t is None else t.data_ptr()

@@ -1,0 +1,52 @@
+// Shared helpers for the unblend_b200 CUDA kernels (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/unblend_b200.h"
+
+#define UB_CHECK_LAUNCH()                           \
+  do {                                              \
+    cudaError_t _e = cudaGetLastError();            \
+    if (_e != cudaSuccess) return (int)_e;          \
+  } while (0)
+
+#define UB_REQUIRE(cond)                            \
+  do {                                              \
+    if (!(cond)) return UNBLEND_ERR_INVALID;        \
+  } while (0)
+
+namespace ub {
+
+constexpr int kNumSMs = 148;
+
+__device__ __forceinline__ float gelu_erf(float x) {
+  // Exact GELU as torch F.gelu(approximate='none'): 0.5 x (1 + erf(x / sqrt(2))).
+  return 0.5f * x * (1.0f + erff(x * 0.70710678118654752440f));
+}
+
+__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline unsigned grid_1d(long long n, int threads, long long cap = 148LL * 16) {
+  long long g = (n + threads - 1) / threads;
+  if (g > cap) g = cap;
+  if (g < 1) g = 1;
+  return (unsigned)g;
+}
+
+}  // namespace ub

@@ -1,0 +1,215 @@
+// Generic implicit-GEMM convolution, fp32 SIMT (CUDA cores).
+//
+// Every Conv1d / Conv2d / ConvTranspose phase / Linear of the HTDemucs forward
+// (unblend/blocks.py:461-467, 688-695, 297-300; unblend/transformer.py:290-301)
+// can run here: output positions are the GEMM M dimension, output channels N,
+// and (kh, kw, c_in) the K dimension gathered on the fly from a channels-last
+// input with zero padding. Fused prologue (GroupNorm+GELU or a skip add on the
+// loaded input) and epilogue (bias, GELU/GLU, LayerScale residual, GroupNorm
+// statistics). This is the exact-fp32 path; dense layers also have a
+// tensor-core path (tcgen05) built on the same parameter block.
+#include "common.cuh"
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BN = 64;
+constexpr int BK = 16;
+constexpr int NT = 256;
+
+struct ConvArgs {
+  UnblendConvParams p;
+  const float* x;
+  const float* w;
+  const float* bias;
+  float* y;
+  long long M;
+  int K;
+};
+
+__device__ __forceinline__ float load_a(const ConvArgs& a, int b, int hi, int wi, int ci) {
+  const UnblendConvParams& p = a.p;
+  long long off = (long long)b * p.in_sb + (long long)hi * p.in_sh + (long long)wi * p.in_sw + ci;
+  float v = __ldg(a.x + off);
+  if (p.prologue == UNBLEND_PRO_GN_GELU) {
+    int g = p.pro_group_per_h ? b * p.h_in + hi : b;
+    v = (v - __ldg(p.pro_stats + 2 * g)) * __ldg(p.pro_stats + 2 * g + 1);
+    v = ub::gelu_erf(v * __ldg(p.pro_gamma + ci) + __ldg(p.pro_beta + ci));
+  } else if (p.prologue == UNBLEND_PRO_ADD) {
+    v += __ldg(p.pro_x2 + off);
+  }
+  return v;
+}
+
+__global__ void __launch_bounds__(NT) conv_simt_kernel(ConvArgs a) {
+  const UnblendConvParams& p = a.p;
+  __shared__ __align__(16) float As[2][BK][BM + 4];
+  __shared__ __align__(16) float Bs[2][BK][BN + 4];
+
+  const int tid = threadIdx.x;
+  const long long m0 = (long long)blockIdx.x * BM;
+  const int n0 = blockIdx.y * BN;
+
+  // A-load role: one output position, 8 consecutive k.
+  const int am = tid >> 1;
+  const int ak = (tid & 1) * 8;
+  const long long m = m0 + am;
+  const bool mvalid = m < a.M;
+  int wo = 0, ho = 0, b = 0;
+  if (mvalid) {
+    wo = (int)(m % p.w_out);
+    long long t = m / p.w_out;
+    ho = (int)(t % p.h_out);
+    b = (int)(t / p.h_out);
+  }
+  const int hbase = ho * p.sh - p.ph;
+  const int wbase = wo * p.sw - p.pw;
+
+  // B-load role: one output channel, 4 consecutive k.
+  const int bn = tid >> 2;
+  const int bk = (tid & 3) * 4;
+  const int nrow = n0 + bn;
+  const float* wrow = a.w + (long long)nrow * a.K;
+
+  float ra[8], rb[4];
+  auto load_tiles = [&](int k0) {
+    int k = k0 + ak;
+    int tap = k / p.c_in;
+    int ci = k - tap * p.c_in;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float v = 0.f;
+      if (mvalid && k + i < a.K) {
+        int kh = tap / p.kw;
+        int kwi = tap - kh * p.kw;
+        int hi = hbase + kh * p.dh;
+        int wi = wbase + kwi * p.dw;
+        if (hi >= 0 && hi < p.h_in && wi >= 0 && wi < p.w_in) v = load_a(a, b, hi, wi, ci);
+      }
+      ra[i] = v;
+      if (++ci == p.c_in) { ci = 0; ++tap; }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      int kk = k0 + bk + j;
+      rb[j] = (nrow < p.n_out && kk < a.K) ? __ldg(wrow + kk) : 0.f;
+    }
+  };
+  auto store_tiles = [&](int buf) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) As[buf][ak + i][am] = ra[i];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) Bs[buf][bk + j][bn] = rb[j];
+  };
+
+  const int tx = tid & 15;  // N direction: 4 columns each
+  const int ty = tid >> 4;  // M direction: 8 rows each
+  float acc[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+
+  const int ktiles = (a.K + BK - 1) / BK;
+  load_tiles(0);
+  store_tiles(0);
+  __syncthreads();
+  for (int kt = 0; kt < ktiles; ++kt) {
+    const int buf = kt & 1;
+    if (kt + 1 < ktiles) load_tiles((kt + 1) * BK);
+#pragma unroll
+    for (int kk = 0; kk < BK; ++kk) {
+      float4 a0 = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 8]);
+      float4 a1 = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 8 + 4]);
+      float4 b0 = *reinterpret_cast<const float4*>(&Bs[buf][kk][tx * 4]);
+      float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      float bv[4] = {b0.x, b0.y, b0.z, b0.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    if (kt + 1 < ktiles) store_tiles(buf ^ 1);
+    __syncthreads();
+  }
+
+  // Epilogue.
+  const bool glu = p.act == UNBLEND_ACT_GLU;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const long long mm = m0 + ty * 8 + i;
+    const bool rv = mm < a.M;
+    int owo = 0, oho = 0, ob = 0;
+    if (rv) {
+      owo = (int)(mm % p.w_out);
+      long long t = mm / p.w_out;
+      oho = (int)(t % p.h_out);
+      ob = (int)(t / p.h_out);
+    }
+    const long long rowoff = (long long)ob * p.out_sb + (long long)oho * p.out_sh + (long long)owo * p.out_sw;
+    float s1 = 0.f, s2 = 0.f;
+    float vals[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      int n = n0 + tx * 4 + j;
+      float v = acc[i][j];
+      if (n < p.n_out && a.bias) v += __ldg(a.bias + n);
+      if (p.act == UNBLEND_ACT_GELU) v = ub::gelu_erf(v);
+      vals[j] = v;
+    }
+    const int nouts = glu ? 2 : 4;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (j >= nouts) break;
+      int n = glu ? (n0 + tx * 4) / 2 + j : n0 + tx * 4 + j;
+      int ncount = glu ? p.n_out / 2 : p.n_out;
+      float v = glu ? vals[2 * j] * ub::sigmoidf_(vals[2 * j + 1]) : vals[j];
+      if (rv && n < ncount) {
+        long long off = rowoff + (long long)(n / p.n_group) * p.out_sg + (n % p.n_group);
+        if (p.res) v = p.res[off] + (p.res_scale ? __ldg(p.res_scale + n) : 1.f) * v;
+        a.y[off] = v;
+        s1 += v;
+        s2 += v * v;
+      }
+    }
+    if (p.stats) {
+      // Reduce over the 16 threads that share this output row (lanes differing in bits 0-3).
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) {
+        s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+        s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+      }
+      if (tx == 0 && rv) {
+        int g = p.stats_per_h ? ob * p.h_out + oho : ob;
+        atomicAdd(p.stats + 2 * g, (double)s1);
+        atomicAdd(p.stats + 2 * g + 1, (double)s2);
+      }
+    }
+  }
+}
+
+}  // namespace
+
+extern "C" int unblend_conv2d_f32(const float* x, const float* w, const float* bias, float* y,
+                                  const UnblendConvParams* p, void* stream) {
+  UB_REQUIRE(x && w && y && p);
+  UB_REQUIRE(p->batch > 0 && p->h_out > 0 && p->w_out > 0 && p->n_out > 0 && p->c_in > 0);
+  UB_REQUIRE(p->kh > 0 && p->kw > 0 && p->sh > 0 && p->sw > 0 && p->dh > 0 && p->dw > 0);
+  UB_REQUIRE(p->n_group > 0);
+  UB_REQUIRE(p->act != UNBLEND_ACT_GLU || (p->n_out % 2) == 0);
+  UB_REQUIRE(p->prologue != UNBLEND_PRO_GN_GELU || (p->pro_stats && p->pro_gamma && p->pro_beta));
+  UB_REQUIRE(p->prologue != UNBLEND_PRO_ADD || p->pro_x2);
+  ConvArgs a;
+  a.p = *p;
+  a.x = x;
+  a.w = w;
+  a.bias = bias;
+  a.y = y;
+  a.M = (long long)p->batch * p->h_out * p->w_out;
+  a.K = p->kh * p->kw * p->c_in;
+  dim3 grid((unsigned)((a.M + BM - 1) / BM), (unsigned)((p->n_out + BN - 1) / BN));
+  UB_REQUIRE(grid.y < 65536);
+  conv_simt_kernel<<<grid, NT, 0, ub::as_stream(stream)>>>(a);
+  UB_CHECK_LAUNCH();
+  return 0;
+}

@@ -1,0 +1,277 @@
+// Normalisation, statistics and elementwise kernels (HBM-streaming, fp32).
+//
+// GroupNorm(1, C) of the DConv branches (unblend/blocks.py:282-302), the
+// transformer LayerNorms and sequence-global norm_out GroupNorm
+// (unblend/transformer.py:225-236, 310-316), the HTDemucs input
+// normalisation (unblend/htdemucs.py:669-678) and the DConv tail
+// x + LayerScale * GLU(GN(z)) (unblend/blocks.py:293-317).
+// Statistics accumulate in double so that fp32 parity holds for groups of
+// millions of elements.
+#include "common.cuh"
+
+namespace {
+
+__global__ void zero_f64_kernel(double* p, long long n) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x)
+    p[i] = 0.0;
+}
+
+// grid: (blocks_per_group, groups); one partial per block then a double atomic.
+__global__ void group_sums_kernel(const float* __restrict__ x, double* stats, long long n) {
+  const float* xg = x + (long long)blockIdx.y * n;
+  double s1 = 0.0, s2 = 0.0;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    double v = (double)__ldg(xg + i);
+    s1 += v;
+    s2 += v * v;
+  }
+  s1 = ub::warp_sum_d(s1);
+  s2 = ub::warp_sum_d(s2);
+  __shared__ double sh[2][32];
+  int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  if (lane == 0) {
+    sh[0][wid] = s1;
+    sh[1][wid] = s2;
+  }
+  __syncthreads();
+  if (wid == 0) {
+    int nw = blockDim.x >> 5;
+    s1 = lane < nw ? sh[0][lane] : 0.0;
+    s2 = lane < nw ? sh[1][lane] : 0.0;
+    s1 = ub::warp_sum_d(s1);
+    s2 = ub::warp_sum_d(s2);
+    if (lane == 0) {
+      atomicAdd(stats + 2 * blockIdx.y, s1);
+      atomicAdd(stats + 2 * blockIdx.y + 1, s2);
+    }
+  }
+}
+
+__global__ void stats_finalize_kernel(const double* stats, float* out, int groups, double count,
+                                      float eps, int unbiased, int std_mode) {
+  int g = blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= groups) return;
+  double s = stats[2 * g], sq = stats[2 * g + 1];
+  double mean = s / count;
+  double var = (sq - s * mean) / (count - (unbiased ? 1.0 : 0.0));
+  if (var < 0) var = 0;
+  out[2 * g] = (float)mean;
+  if (std_mode)
+    out[2 * g + 1] = (float)sqrt(var);
+  else
+    out[2 * g + 1] = (float)(1.0 / sqrt(var + (double)eps));
+}
+
+__global__ void group_norm_apply_kernel(const float* __restrict__ x, float* __restrict__ y,
+                                        const float* __restrict__ st, const float* __restrict__ gamma,
+                                        const float* __restrict__ beta, long long rows, int c,
+                                        long long rows_per_group, int act) {
+  long long n = rows * c;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    long long r = i / c;
+    int ch = (int)(i - r * c);
+    long long g = r / rows_per_group;
+    float v = (x[i] - st[2 * g]) * st[2 * g + 1];
+    if (gamma) v = v * gamma[ch];
+    if (beta) v = v + beta[ch];
+    if (act == UNBLEND_ACT_GELU) v = ub::gelu_erf(v);
+    y[i] = v;
+  }
+}
+
+__global__ void dconv_tail_kernel(float* __restrict__ x, const float* __restrict__ z,
+                                  const float* __restrict__ st, const float* __restrict__ gamma,
+                                  const float* __restrict__ beta, const float* __restrict__ scale,
+                                  long long groups, long long rows_per_group, int c, long long x_gs) {
+  const long long n = groups * rows_per_group * c;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / c;
+    const int ch = (int)(i - r * c);
+    const long long g = r / rows_per_group;
+    const long long rr = r - g * rows_per_group;
+    const float mean = st[2 * g], rstd = st[2 * g + 1];
+    const float2 zz = *reinterpret_cast<const float2*>(z + r * 2 * c + 2 * ch);
+    const float va = (zz.x - mean) * rstd * gamma[2 * ch] + beta[2 * ch];
+    const float vg = (zz.y - mean) * rstd * gamma[2 * ch + 1] + beta[2 * ch + 1];
+    float* xp = x + g * x_gs + rr * c + ch;
+    *xp = *xp + scale[ch] * (va * ub::sigmoidf_(vg));
+  }
+}
+
+// One warp per row; c <= 1024 and c % 32 == 0 not required.
+__global__ void layer_norm_kernel(const float* __restrict__ x, float* __restrict__ y,
+                                  const float* __restrict__ gamma, const float* __restrict__ beta,
+                                  const float* __restrict__ pos, float pos_scale, long long pos_rows,
+                                  long long rows, int c) {
+  long long row = blockIdx.x * (long long)(blockDim.x >> 5) + (threadIdx.x >> 5);
+  int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float* xr = x + row * c;
+  float vals[32];
+  int nper = (c + 31) / 32;
+  float s = 0.f;
+  for (int j = 0; j < nper; ++j) {
+    int ch = lane + 32 * j;
+    float v = ch < c ? xr[ch] : 0.f;
+    vals[j] = v;
+    s += v;
+  }
+  float mean = ub::warp_sum(s) / c;
+  float s2 = 0.f;
+  for (int j = 0; j < nper; ++j) {
+    int ch = lane + 32 * j;
+    float d = ch < c ? vals[j] - mean : 0.f;
+    s2 += d * d;
+  }
+  float var = ub::warp_sum(s2) / c;
+  float rstd = rsqrtf(var + 1e-5f);
+  float* yr = y + row * c;
+  const float* pr = pos ? pos + (row % pos_rows) * c : nullptr;
+  for (int j = 0; j < nper; ++j) {
+    int ch = lane + 32 * j;
+    if (ch < c) {
+      float v = (vals[j] - mean) * rstd * gamma[ch] + beta[ch];
+      if (pr) v += pos_scale * pr[ch];
+      yr[ch] = v;
+    }
+  }
+}
+
+__global__ void add_kernel(const float* __restrict__ a, const float* __restrict__ b, float* y,
+                           long long n, long long period, float alpha) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x)
+    y[i] = a[i] + alpha * b[i % period];
+}
+
+__global__ void time_input_kernel(const float* __restrict__ mix, float* __restrict__ xt,
+                                  const float* __restrict__ st, int batch, int length, int length_pad) {
+  long long n = (long long)batch * length_pad;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    int b = (int)(i / length_pad);
+    int t = (int)(i - (long long)b * length_pad);
+    float2 o = make_float2(0.f, 0.f);
+    if (t < length) {
+      float mean = st[2 * b], den = 1e-5f + st[2 * b + 1];
+      const float* mb = mix + (long long)b * 2 * length;
+      o.x = (mb[t] - mean) / den;
+      o.y = (mb[length + t] - mean) / den;
+    }
+    *reinterpret_cast<float2*>(xt + 2 * i) = o;
+  }
+}
+
+}  // namespace
+
+extern "C" int unblend_zero_f64(double* p, long long n, void* stream) {
+  UB_REQUIRE(p && n >= 0);
+  if (n == 0) return 0;
+  zero_f64_kernel<<<ub::grid_1d(n, 256), 256, 0, ub::as_stream(stream)>>>(p, n);
+  UB_CHECK_LAUNCH();
+  return 0;
+}
+
+extern "C" int unblend_group_sums(const float* x, double* stats, int groups, long long n, void* stream) {
+  UB_REQUIRE(x && stats && groups > 0 && n > 0 && groups < 65536);
+  long long per = (n + 255) / 256;
+  int bx = (int)(per < 256 ? per : 256);
+  dim3 grid(bx, groups);
+  group_sums_kernel<<<grid, 256, 0, ub::as_stream(stream)>>>(x, stats, n);
+  UB_CHECK_LAUNCH();
+  return 0;
+}
+
+extern "C" int unblend_stats_finalize(const double* stats, float* out, int groups, double count,
+                                      float eps, int unbiased, int std_mode, void* stream) {
+  UB_REQUIRE(stats && out && groups > 0 && count > (unbiased ? 1.0 : 0.0));
+  stats_finalize_kernel<<<(groups + 127) / 128, 128, 0, ub::as_stream(stream)>>>(
+      stats, out, groups, count, eps, unbiased, std_mode);
+  UB_CHECK_LAUNCH();
+  return 0;
+}
+
+extern "C" int unblend_group_norm_apply(const float* x, float* y, const float* stats2, const float* gamma,
+                                        const float* beta, long long rows, int c, long long rows_per_group,
+                                        int act, void* stream) {
+  UB_REQUIRE(x && y && stats2 && rows > 0 && c > 0 && rows_per_group > 0);
+  UB_REQUIRE(act == UNBLEND_ACT_NONE || act == UNBLEND_ACT_GELU);
+  group_norm_apply_kernel<<<ub::grid_1d(rows * c, 256), 256, 0, ub::as_stream(stream)>>>(
+      x, y, stats2, gamma, beta, rows, c, rows_per_group, act);
+  UB_CHECK_LAUNCH();
+  return 0;
+}
+
+extern "C" int unblend_dconv_tail(float* x, const float* z, const float* stats2, const float* gamma,
+                                  const float* beta, const float* scale, long long groups,
+                                  long long rows_per_group, int c, long long x_group_stride, void* stream) {
+  UB_REQUIRE(x && z && stats2 && gamma && beta && scale && groups > 0 && rows_per_group > 0 && c > 0);
+  UB_REQUIRE(x_group_stride >= rows_per_group * c);
+  dconv_tail_kernel<<<ub::grid_1d(groups * rows_per_group * c, 256), 256, 0, ub::as_stream(stream)>>>(
+      x, z, stats2, gamma, beta, scale, groups, rows_per_group, c, x_group_stride);
+  UB_CHECK_LAUNCH();
+  return 0;
+}
+
+extern "C" int unblend_layer_norm(const float* x, float* y, const float* gamma, const float* beta,
+                                  const float* pos, float pos_scale, long long pos_rows, long long rows,
+                                  int c, void* stream) {
+  UB_REQUIRE(x && y && gamma && beta && rows > 0 && c > 0 && c <= 1024);
+  UB_REQUIRE(!pos || pos_rows > 0);
+  unsigned grid = (unsigned)((rows + 7) / 8);
+  layer_norm_kernel<<<grid, 256, 0, ub::as_stream(stream)>>>(x, y, gamma, beta, pos, pos_scale,
+                                                               pos_rows, rows, c);
+  UB_CHECK_LAUNCH();
+  return 0;
+}
+
+extern "C" int unblend_add(const float* a, const float* b, float* y, long long n, long long b_period,
+                           float alpha, void* stream) {
+  UB_REQUIRE(a && b && y && n > 0 && b_period > 0);
+  add_kernel<<<ub::grid_1d(n, 256), 256, 0, ub::as_stream(stream)>>>(a, b, y, n, b_period, alpha);
+  UB_CHECK_LAUNCH();
+  return 0;
+}
+
+extern "C" int unblend_time_input(const float* mix, float* xt, const float* stats2, int batch, int length,
+                                  int length_pad, void* stream) {
+  UB_REQUIRE(mix && xt && stats2 && batch > 0 && length > 0 && length_pad >= length);
+  time_input_kernel<<<ub::grid_1d((long long)batch * length_pad, 256), 256, 0, ub::as_stream(stream)>>>(
+      mix, xt, stats2, batch, length, length_pad);
+  UB_CHECK_LAUNCH();
+  return 0;
+}
+
+extern "C" int unblend_mean_std(const float* x, double* work, float* out, int batch, long long n,
+                                void* stream) {
+  int rc = unblend_zero_f64(work, 2LL * batch, stream);
+  if (rc) return rc;
+  rc = unblend_group_sums(x, work, batch, n, stream);
+  if (rc) return rc;
+  return unblend_stats_finalize(work, out, batch, (double)n, 0.f, 1, 1, stream);
+}
+
+namespace {
+__global__ void standardize_kernel(const float* __restrict__ x, float* __restrict__ y,
+                                   const float* __restrict__ st, long long n_per_batch, int batch) {
+  long long n = n_per_batch * batch;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    long long b = i / n_per_batch;
+    y[i] = (x[i] - st[2 * b]) / (1e-5f + st[2 * b + 1]);
+  }
+}
+}  // namespace
+
+extern "C" int unblend_standardize(const float* x, float* y, const float* stats2, long long n_per_batch,
+                                   int batch, void* stream) {
+  UB_REQUIRE(x && y && stats2 && n_per_batch > 0 && batch > 0);
+  standardize_kernel<<<ub::grid_1d(n_per_batch * batch, 256), 256, 0, ub::as_stream(stream)>>>(
+      x, y, stats2, n_per_batch, batch);
+  UB_CHECK_LAUNCH();
+  return 0;
+}

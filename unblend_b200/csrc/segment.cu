@@ -1,0 +1,100 @@
+// Segment engine kernels: centred zero-padded chunk gather, triangular
+// weighted overlap-add with a weight sum, and the final divide
+// (unblend/apply.py:278-311 TensorChunk.padded, 406-432 _split_weight,
+// 1219-1238 accumulate, 1329 out / sum_weight). HBM-streaming, fp32.
+#include "common.cuh"
+
+namespace {
+
+// Triangular cross-fade weight of unblend/apply.py:426-430 with
+// transition_power 1: rising 1..half, falling (T-half)..1, divided by the max.
+__device__ __forceinline__ float split_weight(int j, int seg) {
+  const int half = seg / 2;
+  const float mx = (float)(half > seg - half ? half : seg - half);
+  const float v = j < half ? (float)(j + 1) : (float)(seg - j);
+  return v / mx;
+}
+
+__global__ void gather_chunks_kernel(const float* __restrict__ track, int channels, long long length,
+                                     const long long* __restrict__ offsets, int n, int seg,
+                                     float* __restrict__ batch) {
+  const long long total = (long long)n * channels * seg;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int j = (int)(i % seg);
+    const long long ic = i / seg;
+    const int c = (int)(ic % channels);
+    const int k = (int)(ic / channels);
+    const long long o = offsets[k];
+    const long long len = length - o < seg ? length - o : seg;
+    const long long start = o - (seg - len) / 2;
+    const long long src = start + j;
+    batch[i] = (src >= 0 && src < length) ? __ldg(track + (long long)c * length + src) : 0.f;
+  }
+}
+
+__global__ void overlap_add_kernel(const float* __restrict__ y, int n, int rows, int seg,
+                                   const long long* __restrict__ offsets, long long length, long long lo,
+                                   long long span, float* __restrict__ acc, float* __restrict__ sum_w) {
+  const long long total = (long long)rows * span;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long p = lo + i % span;
+    const int r = (int)(i / span);
+    if (p >= length) continue;
+    float a = 0.f, ws = 0.f;
+    for (int k = 0; k < n; ++k) {
+      const long long o = offsets[k];
+      const long long len = length - o < seg ? length - o : seg;
+      const long long j = p - o;
+      if (j < 0 || j >= len) continue;
+      const int trim = (int)((seg - len) / 2);
+      const float w = split_weight((int)j, seg);
+      a += y[((long long)k * rows + r) * seg + trim + j] * w;
+      ws += w;
+    }
+    acc[(long long)r * length + p] += a;
+    if (r == 0) sum_w[p] += ws;
+  }
+}
+
+__global__ void divide_kernel(const float* __restrict__ acc, const float* __restrict__ sum_w,
+                              float* __restrict__ out, int rows, long long length) {
+  const long long total = (long long)rows * length;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x)
+    out[i] = acc[i] / sum_w[i % length];
+}
+
+}  // namespace
+
+extern "C" int unblend_gather_chunks(const float* track, int channels, long long length, const long long* offsets,
+                                     int n, int segment, float* batch, void* stream) {
+  UB_REQUIRE(track && offsets && batch && channels > 0 && length > 0 && n > 0 && segment > 0);
+  const long long total = (long long)n * channels * segment;
+  gather_chunks_kernel<<<ub::grid_1d(total, 256), 256, 0, ub::as_stream(stream)>>>(
+      track, channels, length, offsets, n, segment, batch);
+  UB_CHECK_LAUNCH();
+  return 0;
+}
+
+extern "C" int unblend_overlap_add(const float* y, int n, int rows, int segment, const long long* offsets,
+                                   long long length, long long lo, long long hi, float* acc, float* sum_w,
+                                   void* stream) {
+  UB_REQUIRE(y && offsets && acc && sum_w && n > 0 && rows > 0 && segment > 0 && length > 0);
+  UB_REQUIRE(lo >= 0 && hi > lo);
+  const long long span = hi - lo;
+  overlap_add_kernel<<<ub::grid_1d((long long)rows * span, 256), 256, 0, ub::as_stream(stream)>>>(
+      y, n, rows, segment, offsets, length, lo, span, acc, sum_w);
+  UB_CHECK_LAUNCH();
+  return 0;
+}
+
+extern "C" int unblend_divide(const float* acc, const float* sum_w, float* out, int rows, long long length,
+                              void* stream) {
+  UB_REQUIRE(acc && sum_w && out && rows > 0 && length > 0);
+  divide_kernel<<<ub::grid_1d((long long)rows * length, 256), 256, 0, ub::as_stream(stream)>>>(
+      acc, sum_w, out, rows, length);
+  UB_CHECK_LAUNCH();
+  return 0;
+}

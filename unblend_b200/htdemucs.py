@@ -1,0 +1,558 @@
+"""HTDemucs forward on B200: the drop-in model behind ``apply_model``.
+
+``HTDemucsCuda`` keeps the model contract that the reference segment engine
+drives (unblend/backends.py:36-59; unblend/apply.py:1201-1202): ``sources``,
+``samplerate``, ``audio_channels``, ``max_allowed_segment``,
+``_fixed_batch_shape`` and ``forward(mix[B, C, T]) -> [B, S, C, T]``. It is built
+from the reference ``state_dict`` (strict keys, unblend/repo.py:138) and its
+constructor config, repacks the weights once into kernel layouts on the device,
+and runs every step of ``HTDemucs.forward`` (unblend/htdemucs.py:650-704) as
+CUDA kernels of ``libunblend_b200.so`` through its C ABI. There is no CPU
+path: ``forward`` raises unless its input and weights are on a CUDA device.
+
+Activations are channels-last: the frequency branch is ``[B, F, T, C]`` (T = STFT
+frames), the time branch ``[B, rows, C]`` where each level's buffers hold
+``4 * ceil(L / 4)`` rows so that encoder outputs and transposed-conv outputs of
+a level share one batch stride. Transformer tokens of the frequency branch are
+ordered (f, t); the 2-D positional table is laid out to match.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+from torch import nn
+
+from . import _lib
+from ._lib import ACT_GELU, ACT_GLU, ACT_NONE, PRO_ADD, PRO_GN_GELU, PRO_NONE, ConvParams
+from .synth import HTDEMUCS_CONFIGS
+
+
+def _key(name: str) -> str:
+    return name.replace(".", "__")
+
+
+@dataclass
+class Act:
+    """A channels-last activation view: ``t`` holds [B, H, W, C] with strides sb/sh/sw."""
+
+    t: torch.Tensor
+    B: int
+    H: int
+    W: int
+    C: int
+    sb: int
+    sh: int
+    sw: int
+
+    @staticmethod
+    def freq(B: int, F: int, T: int, C: int, device) -> "Act":
+        t = torch.empty(B * F * T * C, device=device, dtype=torch.float32)
+        return Act(t, B, F, T, C, F * T * C, T * C, C)
+
+    @staticmethod
+    def time(B: int, rows: int, cap: int, C: int, device) -> "Act":
+        t = torch.empty(B * cap * C, device=device, dtype=torch.float32)
+        return Act(t, B, 1, rows, C, cap * C, cap * C, C)
+
+    def like(self) -> "Act":
+        return Act(torch.empty_like(self.t), self.B, self.H, self.W, self.C, self.sb, self.sh, self.sw)
+
+
+def sin_embedding(length: int, dim: int, max_period: float = 10000.0) -> torch.Tensor:
+    """1-D sinusoidal table ``[length, dim]`` (cos | sin halves), as unblend/transformer.py:18-48."""
+    pos = torch.arange(length, dtype=torch.float32).view(-1, 1)
+    half = dim // 2
+    adim = torch.arange(half, dtype=torch.float32).view(1, -1)
+    phase = pos / (max_period ** (adim / (half - 1)))
+    return torch.cat([torch.cos(phase), torch.sin(phase)], dim=-1)
+
+
+def sin_embedding_2d(d_model: int, height: int, width: int, max_period: float = 10000.0) -> torch.Tensor:
+    """2-D sinusoidal table ``[d_model, height, width]``, as unblend/transformer.py:51-107."""
+    pe = torch.zeros(d_model, height, width)
+    half = d_model // 2
+    div = torch.exp(torch.arange(0.0, half, 2) * -(math.log(max_period) / half))
+    pos_w = torch.arange(0.0, width).unsqueeze(1)
+    pos_h = torch.arange(0.0, height).unsqueeze(1)
+    pe[0:half:2] = torch.sin(pos_w * div).t().unsqueeze(1).repeat(1, height, 1)
+    pe[1:half:2] = torch.cos(pos_w * div).t().unsqueeze(1).repeat(1, height, 1)
+    pe[half::2] = torch.sin(pos_h * div).t().unsqueeze(2).repeat(1, 1, width)
+    pe[half + 1 :: 2] = torch.cos(pos_h * div).t().unsqueeze(2).repeat(1, 1, width)
+    return pe
+
+
+def _interleave_rows(t: torch.Tensor) -> torch.Tensor:
+    """Reorder the 2C output rows (value half, gate half) to (v0, g0, v1, g1, ...)."""
+    c = t.shape[0] // 2
+    idx = torch.stack([torch.arange(c), torch.arange(c) + c], dim=1).reshape(-1)
+    return t[idx].contiguous()
+
+
+def _conv_w(w: torch.Tensor) -> torch.Tensor:
+    """Conv weight to [Cout, KH, KW, Cin] (Conv1d kernels become KH=1)."""
+    if w.dim() == 3:
+        return w.permute(0, 2, 1).unsqueeze(1).contiguous()
+    return w.permute(0, 2, 3, 1).contiguous()
+
+
+def _convtr_phases(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Split a stride-4, kernel-8 transposed conv into two 2-tap convs.
+
+    ``w`` is [Cin, Cout, 8] (or [Cin, Cout, 8, 1]). After the pad-2 crop, output
+    row 4p+s receives X[p]W[2]+X[p-1]W[6] (s=0), X[p]W[3]+X[p-1]W[7] (s=1),
+    X[p+1]W[0]+X[p]W[4] (s=2), X[p+1]W[1]+X[p]W[5] (s=3). Phases {0,1} read
+    taps (p-1, p) and phases {2,3} read taps (p, p+1). Each returned weight is
+    [2*Cout, 2 taps, Cin] with rows ordered (s, cout).
+    """
+    if w.dim() == 4:
+        w = w[..., 0]
+    wk = w.permute(2, 1, 0)  # [8, Cout, Cin]
+    lo = torch.stack([torch.stack([wk[6], wk[2]], 1), torch.stack([wk[7], wk[3]], 1)], 0)
+    hi = torch.stack([torch.stack([wk[4], wk[0]], 1), torch.stack([wk[5], wk[1]], 1)], 0)
+    # [2 phases, Cout, 2 taps, Cin] -> [2*Cout, 2, Cin]
+    return lo.reshape(-1, 2, w.shape[0]).contiguous(), hi.reshape(-1, 2, w.shape[0]).contiguous()
+
+
+class HTDemucsCuda(nn.Module):
+    """HTDemucs separation forward as sm_100a CUDA kernels (fp32).
+
+    :param config: HTDemucs constructor config (registry ``config`` fields).
+    :param state_dict: Reference-layout weights (strict key set).
+    """
+
+    def __init__(self, config: dict, state_dict: dict) -> None:
+        super().__init__()
+        cfg = dict(HTDEMUCS_CONFIGS["htdemucs"])
+        cfg.update(config)
+        if cfg.get("multi_freqs") or not cfg["cac"] or cfg["norm_starts"] < cfg["depth"]:
+            raise ValueError("unsupported HTDemucs variant")
+        if cfg["nfft"] != 4096 or cfg["kernel_size"] != 8 or cfg["stride"] != 4 or cfg["t_emb"] != "sin":
+            raise ValueError("unsupported HTDemucs geometry")
+        self.config = cfg
+        self.sources = list(cfg["sources"])
+        self.samplerate = cfg["samplerate"]
+        self.audio_channels = cfg["audio_channels"]
+        self.max_allowed_segment = cfg["segment"]
+        self.segment_length = int(round(cfg["segment"] * cfg["samplerate"]))
+        self._fixed_batch_shape = False
+        self.depth = cfg["depth"]
+        self.weights = nn.ParameterDict()
+        self._pack(state_dict)
+
+    @classmethod
+    def from_reference(cls, module: nn.Module) -> "HTDemucsCuda":
+        """Build from a reference ``HTDemucs`` instance (its captured init kwargs + state_dict)."""
+        args, kwargs = getattr(module, "_init_args_kwargs", ((), {}))
+        cfg = dict(kwargs)
+        if args:
+            cfg["sources"] = args[0]
+        return cls(cfg, module.state_dict())
+
+    # ------------------------------------------------------------------ weights
+    def _put(self, name: str, t: torch.Tensor) -> None:
+        self.weights[_key(name)] = nn.Parameter(t.detach().float().contiguous().clone(), requires_grad=False)
+
+    def w(self, name: str) -> torch.Tensor:
+        return self.weights[_key(name)]
+
+    def _pack(self, sd: dict) -> None:
+        sd = {k: v.detach().float().cpu() for k, v in sd.items()}
+        cfg = self.config
+        for idx in range(self.depth):
+            for pre in (f"encoder.{idx}", f"tencoder.{idx}"):
+                self._put(f"{pre}.conv.w", _conv_w(sd[f"{pre}.conv.weight"]))
+                self._put(f"{pre}.conv.b", sd[f"{pre}.conv.bias"])
+                self._put(f"{pre}.rewrite.w", _interleave_rows(_conv_w(sd[f"{pre}.rewrite.weight"])))
+                self._put(f"{pre}.rewrite.b", _interleave_rows(sd[f"{pre}.rewrite.bias"]))
+                self._pack_dconv(sd, pre)
+            for pre in (f"decoder.{idx}", f"tdecoder.{idx}"):
+                self._put(f"{pre}.rewrite.w", _interleave_rows(_conv_w(sd[f"{pre}.rewrite.weight"])))
+                self._put(f"{pre}.rewrite.b", _interleave_rows(sd[f"{pre}.rewrite.bias"]))
+                lo, hi = _convtr_phases(sd[f"{pre}.conv_tr.weight"])
+                self._put(f"{pre}.convtr.lo", lo)
+                self._put(f"{pre}.convtr.hi", hi)
+                self._put(f"{pre}.convtr.b", sd[f"{pre}.conv_tr.bias"].repeat(2))
+                self._pack_dconv(sd, pre)
+        if cfg["freq_emb"]:
+            self._put("freq_emb", sd["freq_emb.embedding.weight"] * cfg["emb_scale"] * cfg["freq_emb"])
+        self.bottom = cfg["bottom_channels"]
+        if self.bottom:
+            for n in ("channel_upsampler", "channel_downsampler", "channel_upsampler_t", "channel_downsampler_t"):
+                self._put(f"{n}.w", sd[f"{n}.weight"][..., 0])
+                self._put(f"{n}.b", sd[f"{n}.bias"])
+        p = "crosstransformer"
+        self.t_layers = cfg["t_layers"]
+        if self.t_layers:
+            for n in ("norm_in", "norm_in_t"):
+                self._put(f"{p}.{n}.weight", sd[f"{p}.{n}.weight"])
+                self._put(f"{p}.{n}.bias", sd[f"{p}.{n}.bias"])
+            parity = 1 if cfg["t_cross_first"] else 0
+            for idx in range(self.t_layers):
+                for br in ("layers", "layers_t"):
+                    q = f"{p}.{br}.{idx}"
+                    attn = "self_attn" if idx % 2 == parity else "cross_attn"
+                    for k in (f"{attn}.in_proj_weight", f"{attn}.in_proj_bias", f"{attn}.out_proj.weight",
+                              f"{attn}.out_proj.bias", "linear1.weight", "linear1.bias", "linear2.weight",
+                              "linear2.bias", "norm1.weight", "norm1.bias", "norm2.weight", "norm2.bias",
+                              "norm_out.weight", "norm_out.bias", "gamma_1.scale", "gamma_2.scale"):
+                        self._put(f"{q}.{k}", sd[f"{q}.{k}"])
+                    if idx % 2 != parity:
+                        self._put(f"{q}.norm3.weight", sd[f"{q}.norm3.weight"])
+                        self._put(f"{q}.norm3.bias", sd[f"{q}.norm3.bias"])
+        self.window = None
+
+    def _pack_dconv(self, sd: dict, pre: str) -> None:
+        for d in range(self.config["dconv_depth"]):
+            q = f"{pre}.dconv.layers.{d}"
+            self._put(f"{q}.c1.w", _conv_w(sd[f"{q}.0.weight"]))
+            self._put(f"{q}.c1.b", sd[f"{q}.0.bias"])
+            self._put(f"{q}.g1.w", sd[f"{q}.1.weight"])
+            self._put(f"{q}.g1.b", sd[f"{q}.1.bias"])
+            self._put(f"{q}.c2.w", _interleave_rows(_conv_w(sd[f"{q}.3.weight"])))
+            self._put(f"{q}.c2.b", _interleave_rows(sd[f"{q}.3.bias"]))
+            self._put(f"{q}.g2.w", _interleave_rows(sd[f"{q}.4.weight"]))
+            self._put(f"{q}.g2.b", _interleave_rows(sd[f"{q}.4.bias"]))
+            self._put(f"{q}.scale", sd[f"{q}.6.scale"])
+
+    def _tables(self, device: torch.device, F: int, T: int, Lt: int) -> dict:
+        """Window, positional and frequency-embedding tables (cached per device and shape)."""
+        key = (str(device), F, T, Lt)
+        cache = self.__dict__.setdefault("_table_cache", {})
+        if key not in cache:
+            cfg = self.config
+            dim = self.bottom or cfg["channels"] * cfg["growth"] ** (self.depth - 1)
+            tabs = {"window": torch.hann_window(cfg["nfft"]).to(device)}
+            if self.t_layers:
+                pe = sin_embedding_2d(dim, F, T, cfg["t_max_period"])  # [C, F, T]
+                pos2 = pe.permute(1, 2, 0).reshape(F * T, dim) * cfg["t_weight_pos_embed"]
+                pos1 = sin_embedding(Lt, dim, cfg["t_max_period"]) * cfg["t_weight_pos_embed"]
+                tabs["pos2"] = pos2.contiguous().to(device)
+                tabs["pos1"] = pos1.contiguous().to(device)
+            for v in tabs.values():
+                assert v.is_contiguous()
+            cache[key] = tabs
+        return cache[key]
+
+    # ------------------------------------------------------------------ launch helpers
+    def _conv(self, x: Act, w: torch.Tensor, b: torch.Tensor | None, out: Act, *, h_out: int, w_out: int,
+              n_out: int, kh: int = 1, kw: int = 1, sh: int = 1, sw: int = 1, dh: int = 1, dw: int = 1,
+              ph: int = 0, pw: int = 0, act: int = ACT_NONE, prologue: int = PRO_NONE,
+              pro_stats: torch.Tensor | None = None, pro_gamma=None, pro_beta=None, pro_per_h: int = 0,
+              pro_x2: Act | None = None, res: torch.Tensor | None = None, res_scale=None,
+              stats: torch.Tensor | None = None, stats_per_h: int = 0, n_group: int | None = None,
+              out_sg: int = 0, out_offset: int = 0, out_sh: int | None = None, out_sw: int | None = None) -> None:
+        p = ConvParams()
+        p.batch, p.h_in, p.w_in, p.c_in = x.B, x.H, x.W, x.C
+        p.in_sb, p.in_sh, p.in_sw = x.sb, x.sh, x.sw
+        p.h_out, p.w_out, p.n_out = h_out, w_out, n_out
+        p.kh, p.kw, p.sh, p.sw, p.dh, p.dw, p.ph, p.pw = kh, kw, sh, sw, dh, dw, ph, pw
+        p.out_sb = out.sb
+        p.out_sh = out.sh if out_sh is None else out_sh
+        p.out_sw = out.sw if out_sw is None else out_sw
+        p.out_sg = out_sg
+        n_final = n_out // 2 if act == ACT_GLU else n_out
+        p.n_group = n_group if n_group is not None else n_final
+        p.act, p.prologue = act, prologue
+        p.pro_stats, p.pro_gamma, p.pro_beta = _lib.ptr(pro_stats), _lib.ptr(pro_gamma), _lib.ptr(pro_beta)
+        p.pro_group_per_h = pro_per_h
+        if pro_x2 is not None:
+            assert (pro_x2.sb, pro_x2.sh, pro_x2.sw) == (x.sb, x.sh, x.sw)
+            p.pro_x2 = pro_x2.t.data_ptr()
+        p.res = _lib.ptr(res)
+        p.res_scale = _lib.ptr(res_scale)
+        p.stats = _lib.ptr(stats)
+        p.stats_per_h = stats_per_h
+        y = out.t.data_ptr() + 4 * out_offset
+        flops = 2.0 * x.B * h_out * w_out * n_out * kh * kw * x.C
+        _lib.call("unblend_conv2d_f32", x.t.data_ptr(), w.data_ptr(), _lib.ptr(b), y, ctypes_byref(p), work=flops)
+
+    def _stats(self, stats: torch.Tensor, groups: int, count: float) -> torch.Tensor:
+        out = torch.empty(2 * groups, device=stats.device, dtype=torch.float32)
+        _lib.call("unblend_stats_finalize", stats.data_ptr(), out.data_ptr(), groups, float(count), 1e-5, 0, 0)
+        return out
+
+    def _dconv(self, x: Act, pre: str) -> None:
+        """DConv residual branch in place (unblend/blocks.py:238-317)."""
+        B, H, W, C = x.B, x.H, x.W, x.C
+        hid = int(C / self.config["dconv_comp"])
+        per_h = 1 if H > 1 else 0
+        groups = B * H
+        dev = x.t.device
+        for d in range(self.config["dconv_depth"]):
+            q = f"{pre}.dconv.layers.{d}"
+            dil = 2**d
+            h = Act.freq(B, H, W, hid, dev)
+            st1 = torch.zeros(2 * groups, device=dev, dtype=torch.float64)
+            self._conv(x, self.w(f"{q}.c1.w"), self.w(f"{q}.c1.b"), h, h_out=H, w_out=W, n_out=hid, kw=3,
+                       dw=dil, pw=dil, stats=st1, stats_per_h=per_h)
+            s1 = self._stats(st1, groups, W * hid)
+            z = Act.freq(B, H, W, 2 * C, dev)
+            st2 = torch.zeros(2 * groups, device=dev, dtype=torch.float64)
+            self._conv(h, self.w(f"{q}.c2.w"), self.w(f"{q}.c2.b"), z, h_out=H, w_out=W, n_out=2 * C,
+                       prologue=PRO_GN_GELU, pro_stats=s1, pro_gamma=self.w(f"{q}.g1.w"),
+                       pro_beta=self.w(f"{q}.g1.b"), pro_per_h=per_h, stats=st2, stats_per_h=per_h)
+            s2 = self._stats(st2, groups, W * 2 * C)
+            _lib.call("unblend_dconv_tail", x.t.data_ptr(), z.t.data_ptr(), s2.data_ptr(),
+                      self.w(f"{q}.g2.w").data_ptr(), self.w(f"{q}.g2.b").data_ptr(),
+                      self.w(f"{q}.scale").data_ptr(), groups, W, C, x.sh if H > 1 else x.sb)
+
+    def _enc(self, x: Act, pre: str, freq: bool) -> Act:
+        """HEncLayer (unblend/blocks.py:474-511): conv -> GELU -> DConv -> 1x1 rewrite -> GLU."""
+        cout = self.w(f"{pre}.conv.b").shape[0]
+        dev = x.t.device
+        if freq:
+            ho, wo = x.H // 4, x.W
+            y = Act.freq(x.B, ho, wo, cout, dev)
+            self._conv(x, self.w(f"{pre}.conv.w"), self.w(f"{pre}.conv.b"), y, h_out=ho, w_out=wo, n_out=cout,
+                       kh=8, sh=4, ph=2, act=ACT_GELU)
+        else:
+            wo = -(-x.W // 4)
+            y = Act.time(x.B, wo, 4 * -(-wo // 4), cout, dev)
+            self._conv(x, self.w(f"{pre}.conv.w"), self.w(f"{pre}.conv.b"), y, h_out=1, w_out=wo, n_out=cout,
+                       kw=8, sw=4, pw=2, act=ACT_GELU)
+        self._dconv(y, pre)
+        out = y.like()
+        self._conv(y, self.w(f"{pre}.rewrite.w"), self.w(f"{pre}.rewrite.b"), out, h_out=y.H, w_out=y.W,
+                   n_out=2 * cout, act=ACT_GLU)
+        return out
+
+    def _dec(self, x: Act, skip: Act, pre: str, freq: bool, last: bool, length: int) -> Act:
+        """HDecLayer (unblend/blocks.py:706-747): +skip -> 3-tap rewrite -> GLU -> DConv -> convT -> crop -> GELU."""
+        C = x.C
+        y = x.like()
+        if freq:
+            self._conv(x, self.w(f"{pre}.rewrite.w"), self.w(f"{pre}.rewrite.b"), y, h_out=x.H, w_out=x.W,
+                       n_out=2 * C, kh=3, kw=3, ph=1, pw=1, act=ACT_GLU, prologue=PRO_ADD, pro_x2=skip)
+        else:
+            self._conv(x, self.w(f"{pre}.rewrite.w"), self.w(f"{pre}.rewrite.b"), y, h_out=1, w_out=x.W,
+                       n_out=2 * C, kw=3, pw=1, act=ACT_GLU, prologue=PRO_ADD, pro_x2=skip)
+        self._dconv(y, pre)
+        cout = self.w(f"{pre}.convtr.b").shape[0] // 2
+        act = ACT_NONE if last else ACT_GELU
+        dev = x.t.device
+        b = self.w(f"{pre}.convtr.b")
+        if freq:
+            out = Act.freq(x.B, 4 * x.H, x.W, cout, dev)
+            row = out.sh  # stride of one output frequency row
+            for tag, ph, base in (("lo", 1, 0), ("hi", 0, 2)):
+                self._conv(y, self.w(f"{pre}.convtr.{tag}"), b, out, h_out=x.H, w_out=x.W, n_out=2 * cout,
+                           kh=2, ph=ph, act=act, n_group=cout, out_sg=row, out_offset=base * row,
+                           out_sh=4 * row)
+        else:
+            cap = 4 * x.W
+            out = Act.time(x.B, length, cap, cout, dev)
+            for tag, pw, base in (("lo", 1, 0), ("hi", 0, 2)):
+                self._conv(y, self.w(f"{pre}.convtr.{tag}"), b, out, h_out=1, w_out=x.W, n_out=2 * cout,
+                           kw=2, pw=pw, act=act, n_group=cout, out_sg=cout, out_offset=base * cout,
+                           out_sw=4 * cout)
+        return out
+
+    def _linear(self, x: torch.Tensor, B: int, L: int, K: int, w: torch.Tensor, b: torch.Tensor | None,
+                out: torch.Tensor, N: int, act: int = ACT_NONE, res: torch.Tensor | None = None,
+                res_scale=None, stats: torch.Tensor | None = None) -> None:
+        xa = Act(x, B, 1, L, K, L * K, L * K, K)
+        oa = Act(out, B, 1, L, N if act != ACT_GLU else N // 2, L * N, L * N, N)
+        self._conv(xa, w, b, oa, h_out=1, w_out=L, n_out=N, act=act, res=res, res_scale=res_scale, stats=stats)
+
+    def _ln(self, x: torch.Tensor, rows: int, c: int, name: str, pos: torch.Tensor | None = None,
+            pos_rows: int = 1) -> torch.Tensor:
+        y = torch.empty_like(x)
+        _lib.call("unblend_layer_norm", x.data_ptr(), y.data_ptr(), self.w(f"{name}.weight").data_ptr(),
+                  self.w(f"{name}.bias").data_ptr(), _lib.ptr(pos), 1.0, pos_rows, rows, c)
+        return y
+
+    def _attn_layer(self, q: str, x: torch.Tensor, kv_src: torch.Tensor | None, B: int, L: int, Lk: int,
+                    D: int, cross: bool) -> torch.Tensor:
+        """One transformer layer with norm_first, LayerScale and norm_out (unblend/transformer.py:328-359, 461-481)."""
+        heads = self.config["t_heads"]
+        hd = D // heads
+        dev = x.device
+        attn = "cross_attn" if cross else "self_attn"
+        win, bin_ = self.w(f"{q}.{attn}.in_proj_weight"), self.w(f"{q}.{attn}.in_proj_bias")
+        h = self._ln(x, B * L, D, f"{q}.norm1")
+        att = torch.empty(B * L * D, device=dev, dtype=torch.float32)
+        if not cross:
+            qkv = torch.empty(B * L * 3 * D, device=dev, dtype=torch.float32)
+            self._linear(h, B, L, D, win, bin_, qkv, 3 * D)
+            base = qkv.data_ptr()
+            _lib.call("unblend_attention_f32", base, base + 4 * D, base + 8 * D, att.data_ptr(), B, heads, L, L,
+                      hd, L * 3 * D, 3 * D, L * 3 * D, 3 * D, L * D, D, 1.0 / math.sqrt(hd),
+                      work=4.0 * B * L * L * D)
+        else:
+            kvn = self._ln(kv_src, B * Lk, D, f"{q}.norm2")
+            qp = torch.empty(B * L * D, device=dev, dtype=torch.float32)
+            self._linear(h, B, L, D, win[:D], bin_[:D], qp, D)
+            kv = torch.empty(B * Lk * 2 * D, device=dev, dtype=torch.float32)
+            self._linear(kvn, B, Lk, D, win[D:].contiguous(), bin_[D:].contiguous(), kv, 2 * D)
+            base = kv.data_ptr()
+            _lib.call("unblend_attention_f32", qp.data_ptr(), base, base + 4 * D, att.data_ptr(), B, heads, L,
+                      Lk, hd, L * D, D, Lk * 2 * D, 2 * D, L * D, D, 1.0 / math.sqrt(hd),
+                      work=4.0 * B * L * Lk * D)
+        x_new = torch.empty_like(x)
+        self._linear(att, B, L, D, self.w(f"{q}.{attn}.out_proj.weight"), self.w(f"{q}.{attn}.out_proj.bias"),
+                     x_new, D, res=x, res_scale=self.w(f"{q}.gamma_1.scale"))
+        h2 = self._ln(x_new, B * L, D, f"{q}.norm3" if cross else f"{q}.norm2")
+        hidden = self.w(f"{q}.linear1.bias").shape[0]
+        f = torch.empty(B * L * hidden, device=dev, dtype=torch.float32)
+        self._linear(h2, B, L, D, self.w(f"{q}.linear1.weight"), self.w(f"{q}.linear1.bias"), f, hidden,
+                     act=ACT_GELU)
+        st = torch.zeros(2 * B, device=dev, dtype=torch.float64)
+        self._linear(f, B, L, hidden, self.w(f"{q}.linear2.weight"), self.w(f"{q}.linear2.bias"), x_new, D,
+                     res=x_new, res_scale=self.w(f"{q}.gamma_2.scale"), stats=st)
+        s = self._stats(st, B, L * D)
+        _lib.call("unblend_group_norm_apply", x_new.data_ptr(), x_new.data_ptr(), s.data_ptr(),
+                  self.w(f"{q}.norm_out.weight").data_ptr(), self.w(f"{q}.norm_out.bias").data_ptr(), B * L, D,
+                  L, ACT_NONE)
+        return x_new
+
+    def _transformer(self, x: Act, xt: Act, tabs: dict) -> tuple[Act, Act]:
+        """Channel up-sampling, CrossTransformerEncoder (unblend/transformer.py:703-742), down-sampling."""
+        B, F, T, C0 = x.B, x.H, x.W, x.C
+        Lx, Lt = F * T, xt.W
+        dev = x.t.device
+        D = self.bottom or C0
+        p = "crosstransformer"
+        # Time rows of this level may sit in a buffer with spare capacity rows.
+        xt_rows = xt.t if xt.sb == Lt * C0 else xt.t.view(B, -1)[:, : Lt * C0].contiguous().view(-1)
+        if self.bottom:
+            xu = torch.empty(B * Lx * D, device=dev, dtype=torch.float32)
+            self._linear(x.t, B, Lx, C0, self.w("channel_upsampler.w"), self.w("channel_upsampler.b"), xu, D)
+            xtu = torch.empty(B * Lt * D, device=dev, dtype=torch.float32)
+            self._linear(xt_rows, B, Lt, C0, self.w("channel_upsampler_t.w"), self.w("channel_upsampler_t.b"), xtu,
+                         D)
+        else:
+            xu, xtu = x.t, xt_rows
+        self._trace_tok("up_x", xu, B, Lx, D)
+        self._trace_tok("up_xt", xtu, B, Lt, D)
+        xs = self._ln(xu, B * Lx, D, f"{p}.norm_in", tabs["pos2"], Lx)
+        xts = self._ln(xtu, B * Lt, D, f"{p}.norm_in_t", tabs["pos1"], Lt)
+        self._trace_tok("in_x", xs, B, Lx, D)
+        self._trace_tok("in_xt", xts, B, Lt, D)
+        parity = 1 if self.config["t_cross_first"] else 0
+        for idx in range(self.t_layers):
+            if idx % 2 == parity:
+                xs = self._attn_layer(f"{p}.layers.{idx}", xs, None, B, Lx, Lx, D, False)
+                xts = self._attn_layer(f"{p}.layers_t.{idx}", xts, None, B, Lt, Lt, D, False)
+            else:
+                old = xs
+                xs = self._attn_layer(f"{p}.layers.{idx}", xs, xts, B, Lx, Lt, D, True)
+                xts = self._attn_layer(f"{p}.layers_t.{idx}", xts, old, B, Lt, Lx, D, True)
+            self._trace_tok(f"l{idx}_x", xs, B, Lx, D)
+            self._trace_tok(f"l{idx}_xt", xts, B, Lt, D)
+        xo = Act.freq(B, F, T, C0, dev)
+        xto = Act.time(B, Lt, xt.sb // C0, C0, dev)
+        if self.bottom:
+            self._linear(xs, B, Lx, D, self.w("channel_downsampler.w"), self.w("channel_downsampler.b"), xo.t, C0)
+            xd = torch.empty(B * Lt * C0, device=dev, dtype=torch.float32)
+            self._linear(xts, B, Lt, D, self.w("channel_downsampler_t.w"), self.w("channel_downsampler_t.b"), xd, C0)
+            xto.t.view(B, -1)[:, : Lt * C0].copy_(xd.view(B, -1))
+        else:
+            xo.t.copy_(xs)
+            xto.t.view(B, -1)[:, : Lt * C0].copy_(xts.view(B, -1))
+        return xo, xto
+
+    # ------------------------------------------------------------------ forward
+    #: When set to a dict, ``forward`` stores a CPU copy of every stage output
+    #: in the reference's channel-first layout (debugging aid, slow).
+    trace: dict | None = None
+
+    def _trace_act(self, name: str, a: Act) -> None:
+        if self.trace is None:
+            return
+        if a.H > 1 or a.sb == a.H * a.W * a.C:
+            v = a.t.view(a.B, a.H, a.W, a.C).permute(0, 3, 1, 2)
+            v = v[:, :, 0] if a.H == 1 else v
+        else:
+            v = a.t.view(a.B, -1, a.C)[:, : a.W].permute(0, 2, 1)
+        self.trace[name] = v.detach().cpu().clone()
+
+    def _trace_tok(self, name: str, t: torch.Tensor, B: int, L: int, D: int) -> None:
+        if self.trace is not None:
+            self.trace[name] = t.view(B, L, D).detach().cpu().clone()
+
+    def forward(self, mix: torch.Tensor) -> torch.Tensor:
+        """Separate ``mix`` [B, C, T<=segment] into ``[B, S, C, T]`` (unblend/htdemucs.py:650-704)."""
+        if mix.device.type != "cuda":
+            raise RuntimeError("HTDemucsCuda runs on CUDA devices only (no CPU path)")
+        wdev = next(iter(self.weights.values())).device
+        if wdev != mix.device:
+            raise RuntimeError(f"weights are on {wdev}, input on {mix.device}; call .to(device) first")
+        T = self.segment_length
+        length = mix.shape[-1]
+        if length > T:
+            raise ValueError(f"Given length {length} is longer than training length {T}")
+        mix = mix.float()
+        if length < T:
+            mix = torch.nn.functional.pad(mix, (0, T - length))
+        mix = mix.contiguous()
+        out = self._forward_full(mix)
+        if length < T:
+            out = out[..., :length]
+        return out
+
+    def _forward_full(self, mix: torch.Tensor) -> torch.Tensor:
+        B, C, T = mix.shape
+        if C != 2:
+            raise ValueError("stereo input expected")
+        dev = mix.device
+        S = len(self.sources)
+        nfft = self.config["nfft"]
+        frames = -(-T // (nfft // 4))
+        Fq = nfft // 2
+        levels = [T]
+        for _ in range(self.depth):
+            levels.append(-(-levels[-1] // 4))
+        tabs = self._tables(dev, Fq // 4**self.depth, frames, levels[-1])
+        # STFT front end and normalisation of both branches.
+        spec = Act.freq(B, Fq, frames, 4, dev)
+        _lib.call("unblend_stft_cac", mix.data_ptr(), spec.t.data_ptr(), tabs["window"].data_ptr(), B, T, nfft)
+        work = torch.empty(4 * B, device=dev, dtype=torch.float64)
+        fstats = torch.empty(2 * B, device=dev, dtype=torch.float32)
+        tstats = torch.empty(2 * B, device=dev, dtype=torch.float32)
+        _lib.call("unblend_mean_std", spec.t.data_ptr(), work.data_ptr(), fstats.data_ptr(), B, Fq * frames * 4)
+        _lib.call("unblend_standardize", spec.t.data_ptr(), spec.t.data_ptr(), fstats.data_ptr(),
+                  Fq * frames * 4, B)
+        _lib.call("unblend_mean_std", mix.data_ptr(), work.data_ptr(), tstats.data_ptr(), B, 2 * T)
+        xt = Act.time(B, T, T, 2, dev)
+        _lib.call("unblend_time_input", mix.data_ptr(), xt.t.data_ptr(), tstats.data_ptr(), B, T, T)
+        x = spec
+        self._trace_act("spec", x)
+        self._trace_act("xt", xt)
+        saved, saved_t = [], []
+        for idx in range(self.depth):
+            xt = self._enc(xt, f"tencoder.{idx}", False)
+            saved_t.append(xt)
+            x = self._enc(x, f"encoder.{idx}", True)
+            if idx == 0 and "freq_emb" in self.weights:
+                emb = self.w("freq_emb")  # [F, C]
+                table = emb[:, None, :].expand(x.H, x.W, x.C).contiguous()
+                _lib.call("unblend_add", x.t.data_ptr(), table.data_ptr(), x.t.data_ptr(), x.t.numel(),
+                          table.numel(), 1.0)
+            saved.append(x)
+            self._trace_act(f"tenc{idx}", xt)
+            self._trace_act(f"enc{idx}", x)
+        if self.t_layers:
+            x, xt = self._transformer(x, xt, tabs)
+            self._trace_act("tr_x", x)
+            self._trace_act("tr_xt", xt)
+        for idx in range(self.depth):
+            last = idx == self.depth - 1
+            x = self._dec(x, saved.pop(-1), f"decoder.{idx}", True, last, 0)
+            xt = self._dec(xt, saved_t.pop(-1), f"tdecoder.{idx}", False, last, levels[self.depth - 1 - idx])
+            self._trace_act(f"dec{idx}", x)
+            self._trace_act(f"tdec{idx}", xt)
+        out = torch.empty(B, S, 2, T, device=dev, dtype=torch.float32)
+        frames_buf = torch.empty(B * S * 2 * frames * nfft, device=dev, dtype=torch.float32)
+        _lib.call("unblend_istft_output", x.t.data_ptr(), xt.t.data_ptr(), xt.sb, fstats.data_ptr(),
+                  tstats.data_ptr(), tabs["window"].data_ptr(), frames_buf.data_ptr(), out.data_ptr(), B, S, T,
+                  nfft)
+        return out
+
+
+def ctypes_byref(p: ConvParams):
+    import ctypes
+
+    return ctypes.byref(p)
