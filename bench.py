@@ -50,6 +50,7 @@ def _args():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--precision", default="fp32", choices=["fp32", "bf16", "fp32-simt"])
     return ap.parse_args()
 
 
@@ -181,7 +182,7 @@ def main() -> None:
     world, rank, local = _dist()
     dev = torch.device("cuda", torch.cuda.current_device())
     cfg = htdemucs_config("htdemucs")
-    model = HTDemucsCuda(cfg, htdemucs_state_dict(cfg, 0)).to(dev)
+    model = HTDemucsCuda(cfg, htdemucs_state_dict(cfg, 0), precision=args.precision).to(dev)
     track = synth_track(TRACK_SECONDS, 1 + rank)
     track_dev = track.to(dev)
     step = lambda: apply_model(model, track_dev, chunk_batch_size=BATCH)  # noqa: E731

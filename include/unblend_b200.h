@@ -77,6 +77,23 @@ typedef struct {
 int unblend_conv2d_f32(const float* x, const float* w, const float* bias, float* y,
                        const UnblendConvParams* p, void* stream);
 
+/* The same convolution on the tcgen05 tensor cores (TMA-fed implicit GEMM,
+ * TMEM accumulator). mode 0: fp32 accuracy by the 3-pass TF32 split, weights
+ * given as w_hi = w with the low 13 mantissa bits cleared and w_lo = w - w_hi
+ * (fp32, [n_out, K]); mode 1: bf16 operands, w_hi is bf16 [n_out, K], w_lo
+ * unused. block_n: 64, 128 or 256 output channels per tile. Requirements:
+ * no prologue, c_in % 8 == 0 and >= 16, unit stride along w (or the stride-4
+ * kernel-8 pad-2 time convolution, whose input rows up to a multiple of 4
+ * past w_in must be zero), n_group and all output strides multiples of 4.
+ * Replaces the same reference operators as unblend_conv2d_f32. */
+int unblend_conv2d_tc(const float* x, const void* w_hi, const void* w_lo, const float* bias, float* y,
+                      const UnblendConvParams* p, int mode, int block_n, void* stream);
+
+/* Read the device flag that the tensor-core kernels set when a bounded
+ * barrier wait gives up (0 = none); clear it when `clear` is non-zero.
+ * Synchronous host call. */
+int unblend_error_flag(int* out_host, int clear);
+
 /* Per-group mean / rstd from the double (sum, sumsq) statistics:
  * mean = s/n, var = (sq - s*mean)/(n - unbiased), rstd = 1/sqrt(var + eps) when
  * `std_mode` is 0 (GroupNorm / LayerNorm); when 1, writes std = sqrt(var) and

@@ -258,3 +258,131 @@ def test_segment_engine_pointwise_model():
     ref = apply_unshifted(lambda b: torch.stack([b, 2 * b], 1), track.cpu()[None], 2, seg, 0.25, 3)
     assert rel_err(out.view(1, 2, C, L), ref) < 1e-6
     assert torch.allclose(out.view(2, C, L)[0], track, atol=1e-5)
+
+
+# ---------------------------------------------------------------- tensor-core (tcgen05) convolution
+
+def _split_tf32(w: torch.Tensor):
+    from unblend_b200.htdemucs import split_tf32
+
+    return split_tf32(w)
+
+
+def _conv_tc(x, w, b, y, mode, block_n, **kw):
+    """Same parameter block as _conv, launched on the tcgen05 kernel."""
+    wf = w.reshape(w.shape[0], -1).contiguous()
+    if mode == _lib.TC_TF32X3:
+        whi, wlo = _split_tf32(wf)
+    else:
+        whi, wlo = wf.to(torch.bfloat16).contiguous(), None
+    p = ConvParams()
+    B, H, W, C = kw["B"], kw["H"], kw["W"], kw["C"]
+    p.batch, p.h_in, p.w_in, p.c_in = B, H, W, C
+    p.in_sb, p.in_sh, p.in_sw = kw["in_s"]
+    p.h_out, p.w_out, p.n_out = kw["Ho"], kw["Wo"], kw["N"]
+    p.kh, p.kw, p.sh, p.sw = kw.get("kh", 1), kw.get("kw", 1), kw.get("sh", 1), kw.get("sw", 1)
+    p.dh, p.dw, p.ph, p.pw = kw.get("dh", 1), kw.get("dw", 1), kw.get("ph", 0), kw.get("pw", 0)
+    p.out_sb, p.out_sh, p.out_sw = kw["out_s"]
+    p.out_sg = kw.get("out_sg", 0)
+    act = kw.get("act", ACT_NONE)
+    p.n_group = kw.get("n_group") or (kw["N"] // 2 if act == ACT_GLU else kw["N"])
+    p.act = act
+    p.res, p.res_scale = _lib.ptr(kw.get("res")), _lib.ptr(kw.get("res_scale"))
+    p.stats, p.stats_per_h = _lib.ptr(kw.get("stats")), kw.get("stats_per_h", 0)
+    _lib.call("unblend_conv2d_tc", x.data_ptr(), whi.data_ptr(), _lib.ptr(wlo), _lib.ptr(b), y.data_ptr(),
+              ctypes.byref(p), mode, block_n)
+    torch.cuda.synchronize()
+    assert _lib.error_flag() == 0
+
+
+# 3-pass TF32 (hi*hi + hi*lo + lo*hi) leaves ~2^-20 relative error per product;
+# over K = 512..864 that is a few 1e-5 of the output RMS.
+TC_TOL = {_lib.TC_TF32X3: 6e-5, _lib.TC_BF16: 3e-2}
+MODES = [_lib.TC_TF32X3, _lib.TC_BF16]
+
+
+@pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("block_n", [64, 128, 256])
+def test_tc_linear_residual_stats(mode, block_n):
+    B, L, K, N = 2, 300, 512, 200
+    x, w, b = _cl((B, L, K)), _cl((N, 1, 1, K)) * 0.05, _cl((N,))
+    res, sc = _cl((B, L, N)), _cl((N,))
+    out = res.clone()
+    st = torch.zeros(2 * B, device="cuda", dtype=torch.float64)
+    _conv_tc(x, w, b, out, mode, block_n, B=B, H=1, W=L, C=K, in_s=(L * K, L * K, K), Ho=1, Wo=L, N=N,
+             out_s=(L * N, L * N, N), res=out, res_scale=sc, stats=st)
+    ref = res + sc * (x @ w[:, 0, 0].t() + b)
+    assert rel_err(out, ref) < TC_TOL[mode]
+    # statistics are those of the values written
+    o = out.double().reshape(B, -1)
+    assert torch.allclose(st[0::2], o.sum(1), rtol=1e-6, atol=1e-4)
+    assert torch.allclose(st[1::2], o.pow(2).sum(1), rtol=1e-6)
+
+
+@pytest.mark.parametrize("mode", MODES)
+def test_tc_freq_encoder_conv_112_row_tiles(mode):
+    B, H, W, C, N = 2, 16, 336, 48, 96
+    x, w, b = _cl((B, H, W, C)), _cl((N, 8, 1, C)) * 0.05, _cl((N,))
+    Ho = H // 4
+    y = torch.empty(B, Ho, W, N, device="cuda")
+    _conv_tc(x, w, b, y, mode, 128, B=B, H=H, W=W, C=C, in_s=(H * W * C, W * C, C), Ho=Ho, Wo=W, N=N,
+             out_s=(Ho * W * N, W * N, N), kh=8, sh=4, ph=2, act=ACT_GELU)
+    ref = F.gelu(_ref_conv(x, w, b, 8, 1, 4, 1, 1, 1, 2, 0))
+    assert rel_err(y, ref) < TC_TOL[mode]
+
+
+@pytest.mark.parametrize("mode", MODES)
+def test_tc_3x3_glu_and_dilated(mode):
+    B, H, W, C, N = 1, 8, 336, 96, 192
+    x, w, b = _cl((B, H, W, C)), _cl((N, 3, 3, C)) * 0.03, _cl((N,))
+    y = torch.empty(B, H, W, N // 2, device="cuda")
+    _conv_tc(x, w, b, y, mode, 128, B=B, H=H, W=W, C=C, in_s=(H * W * C, W * C, C), Ho=H, Wo=W, N=N,
+             out_s=(H * W * N // 2, W * N // 2, N // 2), kh=3, kw=3, ph=1, pw=1, act=ACT_GLU)
+    z = _ref_conv(x, w, b, 3, 3, 1, 1, 1, 1, 1, 1)
+    assert rel_err(y, z[..., 0::2] * torch.sigmoid(z[..., 1::2])) < TC_TOL[mode]
+    # dilated k=3 along w with per-(b, h) statistics
+    w2, b2 = _cl((64, 1, 3, C)) * 0.05, _cl((64,))
+    y2 = torch.empty(B, H, W, 64, device="cuda")
+    st = torch.zeros(2 * B * H, device="cuda", dtype=torch.float64)
+    _conv_tc(x, w2, b2, y2, mode, 64, B=B, H=H, W=W, C=C, in_s=(H * W * C, W * C, C), Ho=H, Wo=W, N=64,
+             out_s=(H * W * 64, W * 64, 64), kw=3, dw=2, pw=2, stats=st, stats_per_h=1)
+    ref2 = _ref_conv(x, w2, b2, 1, 3, 1, 1, 1, 2, 0, 2)
+    assert rel_err(y2, ref2) < TC_TOL[mode]
+    o2 = y2.double().reshape(B * H, -1)
+    assert torch.allclose(st[0::2], o2.sum(1), rtol=1e-6, atol=1e-4)
+
+
+@pytest.mark.parametrize("mode", MODES)
+def test_tc_time_stride4_super_rows(mode):
+    B, L, C, N = 2, 1001, 48, 96
+    cap = 4 * -(-L // 4)
+    xs = torch.zeros(B, cap, C, device="cuda")
+    xs[:, :L] = _cl((B, L, C))
+    w, b = _cl((N, 1, 8, C)) * 0.05, _cl((N,))
+    Wo = -(-L // 4)
+    y = torch.empty(B, Wo, N, device="cuda")
+    _conv_tc(xs, w, b, y, mode, 128, B=B, H=1, W=L, C=C, in_s=(cap * C, cap * C, C), Ho=1, Wo=Wo, N=N,
+             out_s=(Wo * N, Wo * N, N), kw=8, sw=4, pw=2)
+    xp = F.pad(xs[:, :L].permute(0, 2, 1), (0, cap - L))
+    ref = F.conv1d(xp, w[:, 0].permute(0, 2, 1), b, 4, 2).permute(0, 2, 1)
+    assert rel_err(y, ref) < TC_TOL[mode]
+
+
+@pytest.mark.parametrize("mode", MODES)
+def test_tc_transposed_conv_phase_split(mode):
+    from unblend_b200.htdemucs import _convtr_phases
+
+    B, P, T, Cin, Cout = 2, 8, 336, 96, 48
+    wt, bias = torch.randn(Cin, Cout, 8) * 0.05, torch.randn(Cout)
+    lo, hi = _convtr_phases(wt)
+    lo, hi, b2 = lo.cuda(), hi.cuda(), bias.repeat(2).cuda()
+    x = _cl((B, P, T, Cin))
+    out = torch.empty(B, 4 * P, T, Cout, device="cuda")
+    row = T * Cout
+    for wgt, ph, base in ((lo, 1, 0), (hi, 0, 2)):
+        _conv_tc(x, wgt[:, :, None, :], b2, out.view(-1)[base * row:], mode, 128, B=B, H=P, W=T, C=Cin,
+                 in_s=(P * T * Cin, T * Cin, Cin), Ho=P, Wo=T, N=2 * Cout, out_s=(4 * P * T * Cout, 4 * row, Cout),
+                 kh=2, ph=ph, n_group=Cout, out_sg=row, act=ACT_GELU)
+    ref = F.conv_transpose2d(x.permute(0, 3, 1, 2), wt[..., None].cuda(), bias.cuda(), (4, 1))
+    ref = F.gelu(ref[:, :, 2:-2, :].permute(0, 2, 3, 1))
+    assert rel_err(out, ref) < TC_TOL[mode]

@@ -71,7 +71,16 @@ _SIGNATURES = {
     "unblend_overlap_add": [c_void_p, c_int, c_int, c_int, c_void_p, c_ll, c_ll, c_ll, c_void_p, c_void_p,
                             c_void_p],
     "unblend_divide": [c_void_p, c_void_p, c_void_p, c_int, c_ll, c_void_p],
+    "unblend_conv2d_tc": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, ctypes.POINTER(ConvParams), c_int,
+                          c_int, c_void_p],
 }
+
+# Entry points without a stream argument.
+_HOST_SIGNATURES = {
+    "unblend_error_flag": [ctypes.POINTER(c_int), c_int],
+}
+
+TC_TF32X3, TC_BF16 = 0, 1
 
 _lib = None
 
@@ -86,7 +95,7 @@ def load() -> ctypes.CDLL:
             f"unblend_b200 CUDA library not built ({LIB_PATH}); run `python -m unblend_b200.build`"
         )
     lib = ctypes.CDLL(LIB_PATH)
-    for name, args in _SIGNATURES.items():
+    for name, args in {**_SIGNATURES, **_HOST_SIGNATURES}.items():
         fn = getattr(lib, name)
         fn.argtypes = args
         fn.restype = c_int
@@ -96,7 +105,14 @@ def load() -> ctypes.CDLL:
 
 def exported_symbols() -> list[str]:
     """Entry points this binding declares (all must exist in the library)."""
-    return list(_SIGNATURES)
+    return list(_SIGNATURES) + list(_HOST_SIGNATURES)
+
+
+def error_flag(clear: bool = True) -> int:
+    """Read (and by default clear) the device flag that bounded waits set on timeout."""
+    v = c_int(0)
+    check("unblend_error_flag", load().unblend_error_flag(ctypes.byref(v), 1 if clear else 0))
+    return v.value
 
 
 def _cuda_error_string(code: int) -> str:

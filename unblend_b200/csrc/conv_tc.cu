@@ -1,0 +1,484 @@
+// Implicit-GEMM convolution on the 5th-generation tensor cores (tcgen05).
+//
+// Same operation and parameter block as the SIMT path (UnblendConvParams):
+// output positions (b, h, w) are the M dimension, output channels N, and the
+// K dimension is walked tap by tap. Each K chunk of 32 input channels of one
+// tap is a TMA box load of [m_box rows x 32 channels] from a 4-D tensor map of
+// the channels-last input (C, W, H, B) at the tap's shifted coordinates; the
+// hardware's out-of-bounds zero fill implements the convolution padding.
+//
+// Warp roles (192 threads, one 128 x BN output tile per CTA):
+//   warp 0    TMA producer (one elected lane)
+//   warp 1    TMEM allocation + MMA issue (one elected lane)
+//   warps 2-5 operand conversion in shared memory, then the epilogue
+// fp32 mode: each fp32 A tile is split in place into a TF32 "hi" part and a
+// residual "lo" tile; weights come pre-split; D += Ahi*Bhi + Ahi*Blo + Alo*Bhi
+// (3 x kind::tf32) keeps fp32-level accuracy. bf16 mode: the fp32 A tile is
+// converted to bf16 and multiplied with bf16 weights (kind::f16).
+// The accumulator lives in TMEM (128 lanes x BN fp32 columns); the epilogue
+// reads it with tcgen05.ld and applies bias, GELU / GLU, the LayerScale
+// residual and GroupNorm statistics, as the SIMT kernel does.
+#include <cuda_bf16.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "tc_common.cuh"
+
+namespace {
+
+using namespace ub::tc;
+
+constexpr int MAXT = 16;
+constexpr int NT = 192;
+
+struct TcArgs {
+  int B, H, W_out;
+  int m_valid, m_box;
+  int tiles_w, tiles_n;
+  int n_out;
+  int a_sh;
+  int ntaps, nchunks;
+  int tap_dh[MAXT], tap_dw[MAXT], tap_c0[MAXT], tap_clen[MAXT], tap_k0[MAXT];
+  const float* bias;
+  float* y;
+  long long out_sb, out_sh, out_sw, out_sg;
+  int n_group;
+  int act;
+  const float* res;
+  const float* res_scale;
+  double* stats;
+  int stats_per_h;
+};
+
+template <int BN, int MODE>
+struct Layout {
+  static constexpr int A_BYTES = 128 * 128;                          // fp32 staging, 128 rows x 32 K
+  static constexpr int AC_BYTES = MODE == 0 ? 128 * 128 : 128 * 64;   // lo (fp32) or bf16 tile
+  static constexpr int B_BYTES = MODE == 0 ? BN * 128 : BN * 64;      // one weight tile
+  static constexpr int B_TILES = MODE == 0 ? 2 : 1;                   // hi + lo, or bf16
+  static constexpr int STAGE = A_BYTES + AC_BYTES + B_TILES * B_BYTES;
+  static constexpr int STAGES = (200 * 1024) / STAGE > 4 ? 4 : (200 * 1024) / STAGE;
+  static constexpr int SMEM = STAGES * STAGE + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+__device__ __forceinline__ float gelu(float x) { return ub::gelu_erf(x); }
+
+template <int BN, int MODE>
+__global__ void __launch_bounds__(NT, 1)
+    conv_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
+                   const __grid_constant__ CUtensorMap mapB2, const __grid_constant__ TcArgs a) {
+  using L = Layout<BN, MODE>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::STAGES * L::STAGE);
+  uint64_t* conv = full + L::STAGES;
+  uint64_t* empty = conv + L::STAGES;
+  uint64_t* accum = empty + L::STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const long long tile = blockIdx.x;
+  const int n_tile = (int)(tile % a.tiles_n);
+  const long long m_tile = tile / a.tiles_n;
+  const int tw = (int)(m_tile % a.tiles_w);
+  const long long t2 = m_tile / a.tiles_w;
+  const int h = (int)(t2 % a.H);
+  const int b = (int)(t2 / a.H);
+  const int w0 = tw * a.m_valid;
+  const int n0 = n_tile * BN;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < L::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&conv[s], 4);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accum, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, BN);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int nk = a.nchunks;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint32_t bytes = (uint32_t)(a.m_box * 128 + L::B_TILES * L::B_BYTES);
+      int it = 0;
+      bool ok = true;
+      for (int t = 0; t < a.ntaps && ok; ++t) {
+        const int ca = a.tap_c0[t], wa = w0 + a.tap_dw[t], ha = h * a.a_sh + a.tap_dh[t], kb = a.tap_k0[t];
+        for (int cc = 0; cc < a.tap_clen[t] && ok; cc += 32, ++it) {
+          const int s = it % L::STAGES;
+          const int r = it / L::STAGES;
+          if (r > 0 && !mbar_wait(&empty[s], (r - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = smem + s * L::STAGE;
+          mbar_expect_tx(&full[s], bytes);
+          tma_load_4d(st, &mapA, &full[s], ca + cc, wa, ha, b);
+          uint8_t* sb = st + L::A_BYTES + L::AC_BYTES;
+          tma_load_2d(sb, &mapB, &full[s], kb + cc, n0);
+          if (MODE == 0) tma_load_2d(sb + L::B_BYTES, &mapB2, &full[s], kb + cc, n0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = instr_desc(MODE == 0 ? 2u : 1u, (uint32_t)BN);
+      bool ok = true;
+      for (int it = 0; it < nk; ++it) {
+        const int s = it % L::STAGES;
+        const int r = it / L::STAGES;
+        if (!mbar_wait(&conv[s], r & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint8_t* st = smem + s * L::STAGE;
+        const uint32_t sa = smem_u32(st);
+        const uint32_t sac = sa + L::A_BYTES;
+        const uint32_t sb = sac + L::AC_BYTES;
+        if (MODE == 0) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint64_t dah = smem_desc(sa + 32 * j, 128), dal = smem_desc(sac + 32 * j, 128);
+            const uint64_t dbh = smem_desc(sb + 32 * j, 128), dbl = smem_desc(sb + L::B_BYTES + 32 * j, 128);
+            umma_tf32(tmem, dah, dbh, idesc, (it > 0 || j > 0) ? 1u : 0u);
+            umma_tf32(tmem, dah, dbl, idesc, 1u);
+            umma_tf32(tmem, dal, dbh, idesc, 1u);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const uint64_t da = smem_desc(sac + 32 * j, 64), db = smem_desc(sb + 32 * j, 64);
+            umma_bf16(tmem, da, db, idesc, (it > 0 || j > 0) ? 1u : 0u);
+          }
+        }
+        umma_commit(&empty[s]);
+      }
+      if (ok) umma_commit(accum);
+      else atomicExch(&g_error_flag, 2);
+    }
+  } else {
+    // Converter warps: split / pack each landed A tile for the MMA.
+    const int ct = threadIdx.x - 64;  // 0..127
+    bool ok = true;
+    for (int it = 0; it < nk; ++it) {
+      const int s = it % L::STAGES;
+      const int r = it / L::STAGES;
+      if (!mbar_wait(&full[s], r & 1)) {
+        ok = false;
+        break;
+      }
+      uint8_t* st = smem + s * L::STAGE;
+      if (MODE == 0) {
+        float4* hi = reinterpret_cast<float4*>(st);
+        float4* lo = reinterpret_cast<float4*>(st + L::A_BYTES);
+#pragma unroll
+        for (int i = ct; i < 1024; i += 128) {
+          float4 v = hi[i];
+          // hi = v rounded to the nearest TF32 value (ties away from zero),
+          // lo = v - hi exactly.
+          float4 vh, vl;
+          vh.x = __uint_as_float((__float_as_uint(v.x) + 0x1000u) & 0xFFFFE000u);
+          vh.y = __uint_as_float((__float_as_uint(v.y) + 0x1000u) & 0xFFFFE000u);
+          vh.z = __uint_as_float((__float_as_uint(v.z) + 0x1000u) & 0xFFFFE000u);
+          vh.w = __uint_as_float((__float_as_uint(v.w) + 0x1000u) & 0xFFFFE000u);
+          vl.x = v.x - vh.x;
+          vl.y = v.y - vh.y;
+          vl.z = v.z - vh.z;
+          vl.w = v.w - vh.w;
+          hi[i] = vh;
+          lo[i] = vl;
+        }
+      } else {
+        const uint8_t* src = st;
+        uint8_t* dst = st + L::A_BYTES;
+#pragma unroll
+        for (int i = ct; i < 1024; i += 128) {
+          const int row = i >> 3, c = i & 7;
+          const float4 v = *reinterpret_cast<const float4*>(src + row * 128 + ((c ^ (row & 7)) << 4));
+          __nv_bfloat162 p0 = __floats2bfloat162_rn(v.x, v.y);
+          __nv_bfloat162 p1 = __floats2bfloat162_rn(v.z, v.w);
+          uint2 packed;
+          packed.x = *reinterpret_cast<uint32_t*>(&p0);
+          packed.y = *reinterpret_cast<uint32_t*>(&p1);
+          *reinterpret_cast<uint2*>(dst + row * 64 + (((c >> 1) ^ ((row >> 1) & 3)) << 4) + (c & 1) * 8) = packed;
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&conv[s]);
+    }
+    // Epilogue: TMEM -> registers -> fused ops -> global.
+    if (ok) ok = mbar_wait(accum, 0);
+    tc_fence_after();
+    if (ok) {
+      const int q = warp & 3;
+      const int row = q * 32 + lane;
+      const int wpos = w0 + row;
+      const bool rv = row < a.m_valid && wpos < a.W_out;
+      const long long rowoff = (long long)b * a.out_sb + (long long)h * a.out_sh + (long long)wpos * a.out_sw;
+      const bool glu = a.act == UNBLEND_ACT_GLU;
+      const int ncount = glu ? a.n_out / 2 : a.n_out;
+      float s1 = 0.f, s2 = 0.f;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t acc[32];
+        __syncwarp();
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, acc);
+        if (!rv || n0 + c0 >= a.n_out) continue;  // after the warp-wide load
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int n = n0 + c0 + j;
+          float x = __uint_as_float(acc[j]);
+          if (a.bias && n < a.n_out) x += __ldg(a.bias + n);
+          if (a.act == UNBLEND_ACT_GELU) x = gelu(x);
+          v[j] = x;
+        }
+        const int nouts = glu ? 16 : 32;
+        const int nb = glu ? (n0 + c0) / 2 : n0 + c0;
+#pragma unroll
+        for (int j4 = 0; j4 < 8; ++j4) {
+          if (j4 * 4 >= nouts) break;
+          const int n = nb + j4 * 4;
+          if (n >= ncount) break;
+          float o[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int jj = j4 * 4 + e;
+            o[e] = glu ? v[2 * jj] * ub::sigmoidf_(v[2 * jj + 1]) : v[jj];
+          }
+          const long long off = rowoff + (long long)(n / a.n_group) * a.out_sg + (n % a.n_group);
+          if (n + 4 <= ncount) {
+            if (a.res) {
+              const float4 rr = *reinterpret_cast<const float4*>(a.res + off);
+              const float rs[4] = {rr.x, rr.y, rr.z, rr.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) o[e] = rs[e] + (a.res_scale ? __ldg(a.res_scale + n + e) : 1.f) * o[e];
+            }
+            *reinterpret_cast<float4*>(a.y + off) = make_float4(o[0], o[1], o[2], o[3]);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              s1 += o[e];
+              s2 += o[e] * o[e];
+            }
+          } else {
+            for (int e = 0; e < 4 && n + e < ncount; ++e) {
+              float x = o[e];
+              if (a.res) x = a.res[off + e] + (a.res_scale ? __ldg(a.res_scale + n + e) : 1.f) * x;
+              a.y[off + e] = x;
+              s1 += x;
+              s2 += x * x;
+            }
+          }
+        }
+      }
+      if (a.stats) {
+        s1 = ub::warp_sum(s1);
+        s2 = ub::warp_sum(s2);
+        if (lane == 0) {
+          const int g = a.stats_per_h ? b * a.H + h : b;
+          atomicAdd(a.stats + 2 * g, (double)s1);
+          atomicAdd(a.stats + 2 * g + 1, (double)s2);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, BN);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+bool make_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* base, const cuuint64_t* dims,
+              const cuuint64_t* strides_bytes, const cuuint32_t* box, CUtensorMapSwizzle sw) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = fn(m, dt, (cuuint32_t)rank, const_cast<void*>(base), dims, strides_bytes, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int BN, int MODE>
+int launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb2, const TcArgs& args, long long tiles,
+           cudaStream_t st) {
+  using L = Layout<BN, MODE>;
+  auto k = conv_tc_kernel<BN, MODE>;
+  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
+  k<<<(unsigned)tiles, NT, L::SMEM, st>>>(ma, mb, mb2, args);
+  UB_CHECK_LAUNCH();
+  return 0;
+}
+
+}  // namespace
+
+extern "C" int unblend_error_flag(int* out_host, int clear) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, ub::tc::g_error_flag, sizeof(int));
+  if (e != cudaSuccess) return (int)e;
+  if (out_host) *out_host = v;
+  if (clear) {
+    int z = 0;
+    e = cudaMemcpyToSymbol(ub::tc::g_error_flag, &z, sizeof(int));
+    if (e != cudaSuccess) return (int)e;
+  }
+  return 0;
+}
+
+extern "C" int unblend_conv2d_tc(const float* x, const void* w_hi, const void* w_lo, const float* bias, float* y,
+                                 const UnblendConvParams* p, int mode, int block_n, void* stream) {
+  UB_REQUIRE(x && w_hi && y && p && (mode == 0 || mode == 1));
+  UB_REQUIRE(mode == 1 || w_lo);
+  UB_REQUIRE(block_n == 64 || block_n == 128 || block_n == 256);
+  UB_REQUIRE(p->prologue == UNBLEND_PRO_NONE);
+  UB_REQUIRE(p->c_in % 8 == 0 && p->c_in >= 16);
+  UB_REQUIRE(p->n_group % 4 == 0 && p->out_sg % 4 == 0 && p->out_sw % 4 == 0 && p->out_sh % 4 == 0 &&
+             p->out_sb % 4 == 0);
+  UB_REQUIRE(p->act != UNBLEND_ACT_GLU || p->n_out % 2 == 0);
+  UB_REQUIRE(p->in_sw == p->c_in && p->in_sh % 4 == 0 && p->in_sb % 4 == 0);
+  TcArgs a{};
+  a.B = p->batch;
+  a.H = p->h_out;
+  a.W_out = p->w_out;
+  a.n_out = p->n_out;
+  a.bias = bias;
+  a.y = y;
+  a.out_sb = p->out_sb;
+  a.out_sh = p->out_sh;
+  a.out_sw = p->out_sw;
+  a.out_sg = p->out_sg;
+  a.n_group = p->n_group;
+  a.act = p->act;
+  a.res = p->res;
+  a.res_scale = p->res_scale;
+  a.stats = p->stats;
+  a.stats_per_h = p->stats_per_h;
+
+  // A operand tensor map (C, W, H, B) and the tap table.
+  CUtensorMap ma, mb, mb2;
+  cuuint64_t dims[4];
+  cuuint64_t strides[3];
+  int kw_taps = p->kw, kh_taps = p->kh;
+  const long long K = (long long)p->kh * p->kw * p->c_in;
+  int nt = 0;
+  if (p->sw == 1) {
+    dims[0] = (cuuint64_t)p->c_in;
+    dims[1] = (cuuint64_t)p->w_in;
+    dims[2] = (cuuint64_t)p->h_in;
+    dims[3] = (cuuint64_t)p->batch;
+    strides[0] = (cuuint64_t)p->in_sw * 4;
+    strides[1] = (cuuint64_t)p->in_sh * 4;
+    strides[2] = (cuuint64_t)p->in_sb * 4;
+    a.a_sh = p->sh;
+    UB_REQUIRE(kh_taps * kw_taps <= MAXT);
+    for (int i = 0; i < kh_taps; ++i)
+      for (int j = 0; j < kw_taps; ++j) {
+        a.tap_dh[nt] = i * p->dh - p->ph;
+        a.tap_dw[nt] = j * p->dw - p->pw;
+        a.tap_c0[nt] = 0;
+        a.tap_clen[nt] = p->c_in;
+        a.tap_k0[nt] = nt * p->c_in;
+        ++nt;
+      }
+  } else {
+    // Stride-4, kernel-8, pad-2 time convolution read as "super rows" of 4
+    // consecutive input rows: output w needs super rows w-1 (last two input
+    // rows), w (all four) and w+1 (first two). Input rows past the logical
+    // length must be zero up to a multiple of 4.
+    UB_REQUIRE(p->sw == 4 && p->kw == 8 && p->pw == 2 && p->kh == 1 && p->h_in == 1 && p->dw == 1);
+    UB_REQUIRE(p->in_sb % (4 * p->c_in) == 0);
+    const int C = p->c_in;
+    UB_REQUIRE((2 * C) % 32 == 0);
+    dims[0] = (cuuint64_t)(4 * C);
+    dims[1] = (cuuint64_t)((p->w_in + 3) / 4);
+    dims[2] = 1;
+    dims[3] = (cuuint64_t)p->batch;
+    strides[0] = (cuuint64_t)(4 * C) * 4;
+    strides[1] = (cuuint64_t)p->in_sb * 4;
+    strides[2] = (cuuint64_t)p->in_sb * 4;
+    a.a_sh = 0;
+    const int c0s[3] = {2 * C, 0, 0}, clen[3] = {2 * C, 4 * C, 2 * C}, k0s[3] = {0, 2 * C, 6 * C};
+    for (int i = 0; i < 3; ++i) {
+      a.tap_dh[nt] = 0;
+      a.tap_dw[nt] = i - 1;
+      a.tap_c0[nt] = c0s[i];
+      a.tap_clen[nt] = clen[i];
+      a.tap_k0[nt] = k0s[i];
+      ++nt;
+    }
+  }
+  a.ntaps = nt;
+  int nch = 0;
+  for (int i = 0; i < nt; ++i) nch += (a.tap_clen[i] + 31) / 32;
+  a.nchunks = nch;
+  // Rows of one tile: all 128 unless a row of W does not split into 128s
+  // (e.g. 336 STFT frames = 3 x 112).
+  int m_valid = 128;
+  if (p->w_out % 128 != 0 && p->h_out > 1) {
+    for (int mv = 128; mv >= 64; mv -= 8)
+      if (p->w_out % mv == 0) {
+        m_valid = mv;
+        break;
+      }
+  }
+  a.m_valid = m_valid;
+  a.m_box = m_valid;
+  a.tiles_w = (p->w_out + m_valid - 1) / m_valid;
+  a.tiles_n = (p->n_out + block_n - 1) / block_n;
+  cuuint32_t boxA[4] = {32, (cuuint32_t)m_valid, 1, 1};
+  if (!make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, dims, strides, boxA, CU_TENSOR_MAP_SWIZZLE_128B))
+    return UNBLEND_ERR_INVALID;
+  // Weights [N, K] (K contiguous): fp32 hi/lo pair or bf16.
+  cuuint64_t wd[2] = {(cuuint64_t)K, (cuuint64_t)p->n_out};
+  if (mode == 0) {
+    cuuint64_t ws[1] = {(cuuint64_t)K * 4};
+    cuuint32_t boxB[2] = {32, (cuuint32_t)block_n};
+    UB_REQUIRE((K * 4) % 16 == 0);
+    if (!make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, w_hi, wd, ws, boxB, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map(&mb2, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, w_lo, wd, ws, boxB, CU_TENSOR_MAP_SWIZZLE_128B))
+      return UNBLEND_ERR_INVALID;
+  } else {
+    cuuint64_t ws[1] = {(cuuint64_t)K * 2};
+    cuuint32_t boxB[2] = {32, (cuuint32_t)block_n};
+    UB_REQUIRE((K * 2) % 16 == 0);
+    if (!make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w_hi, wd, ws, boxB, CU_TENSOR_MAP_SWIZZLE_64B))
+      return UNBLEND_ERR_INVALID;
+    mb2 = mb;
+  }
+  const long long tiles = (long long)p->batch * p->h_out * a.tiles_w * a.tiles_n;
+  UB_REQUIRE(tiles > 0 && tiles < (1LL << 31));
+  cudaStream_t st = ub::as_stream(stream);
+  if (mode == 0) {
+    if (block_n == 64) return launch<64, 0>(ma, mb, mb2, a, tiles, st);
+    if (block_n == 128) return launch<128, 0>(ma, mb, mb2, a, tiles, st);
+    return launch<256, 0>(ma, mb, mb2, a, tiles, st);
+  }
+  if (block_n == 64) return launch<64, 1>(ma, mb, mb2, a, tiles, st);
+  if (block_n == 128) return launch<128, 1>(ma, mb, mb2, a, tiles, st);
+  return launch<256, 1>(ma, mb, mb2, a, tiles, st);
+}

@@ -116,15 +116,33 @@ def _convtr_phases(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     return lo.reshape(-1, 2, w.shape[0]).contiguous(), hi.reshape(-1, 2, w.shape[0]).contiguous()
 
 
+def split_tf32(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Split fp32 ``w`` into ``hi`` (rounded to TF32, low 13 mantissa bits clear) and ``lo = w - hi``."""
+    w = w.float().contiguous()
+    hi = ((w.view(torch.int32) + 0x1000) & ~0x1FFF).view(torch.float32)
+    return hi.contiguous(), (w - hi).contiguous()
+
+
+PRECISIONS = ("fp32", "bf16", "fp32-simt")
+
+
 class HTDemucsCuda(nn.Module):
-    """HTDemucs separation forward as sm_100a CUDA kernels (fp32).
+    """HTDemucs separation forward as sm_100a CUDA kernels.
 
     :param config: HTDemucs constructor config (registry ``config`` fields).
     :param state_dict: Reference-layout weights (strict key set).
+    :param precision: ``"fp32"`` (dense layers on tcgen05 tensor cores with the
+        3-pass TF32 split, fp32-level accuracy), ``"bf16"`` (bf16 tensor-core
+        operands, fp32 accumulation and fp32 activations) or ``"fp32-simt"``
+        (every layer on CUDA-core fp32 FMA kernels).
     """
 
-    def __init__(self, config: dict, state_dict: dict) -> None:
+    def __init__(self, config: dict, state_dict: dict, precision: str = "fp32") -> None:
         super().__init__()
+        if precision not in PRECISIONS:
+            raise ValueError(f"precision must be one of {PRECISIONS}")
+        self.precision = precision
+        self._tc_cache: dict = {}
         cfg = dict(HTDEMUCS_CONFIGS["htdemucs"])
         cfg.update(config)
         if cfg.get("multi_freqs") or not cfg["cac"] or cfg["norm_starts"] < cfg["depth"]:
@@ -202,6 +220,13 @@ class HTDemucsCuda(nn.Module):
                     if idx % 2 != parity:
                         self._put(f"{q}.norm3.weight", sd[f"{q}.norm3.weight"])
                         self._put(f"{q}.norm3.bias", sd[f"{q}.norm3.bias"])
+                        # Query and key/value projections of the cross attention, split once.
+                        win, bin_ = sd[f"{q}.cross_attn.in_proj_weight"], sd[f"{q}.cross_attn.in_proj_bias"]
+                        d = win.shape[1]
+                        self._put(f"{q}.in_q.w", win[:d])
+                        self._put(f"{q}.in_q.b", bin_[:d])
+                        self._put(f"{q}.in_kv.w", win[d:])
+                        self._put(f"{q}.in_kv.b", bin_[d:])
         self.window = None
 
     def _pack_dconv(self, sd: dict, pre: str) -> None:
@@ -267,7 +292,44 @@ class HTDemucsCuda(nn.Module):
         p.stats_per_h = stats_per_h
         y = out.t.data_ptr() + 4 * out_offset
         flops = 2.0 * x.B * h_out * w_out * n_out * kh * kw * x.C
+        if self._tc_eligible(x, p, prologue, out_offset):
+            if prologue == PRO_ADD:
+                # Fold the decoder skip connection into its input (consumed only here).
+                _lib.call("unblend_add", x.t.data_ptr(), pro_x2.t.data_ptr(), x.t.data_ptr(), x.t.numel(),
+                          x.t.numel(), 1.0)
+                p.prologue, p.pro_x2 = PRO_NONE, None
+            mode = _lib.TC_TF32X3 if self.precision == "fp32" else _lib.TC_BF16
+            whi, wlo = self._tc_weight(w, mode)
+            block_n = 64 if n_out <= 64 else 128
+            if mode == _lib.TC_BF16 and n_out >= 512:
+                block_n = 256
+            _lib.call("unblend_conv2d_tc", x.t.data_ptr(), whi.data_ptr(), _lib.ptr(wlo), _lib.ptr(b), y,
+                      ctypes_byref(p), mode, block_n, work=flops)
+            return
         _lib.call("unblend_conv2d_f32", x.t.data_ptr(), w.data_ptr(), _lib.ptr(b), y, ctypes_byref(p), work=flops)
+
+    def _tc_eligible(self, x: Act, p: ConvParams, prologue: int, out_offset: int) -> bool:
+        """Whether this convolution meets the tensor-core kernel's layout requirements."""
+        if self.precision == "fp32-simt" or prologue not in (PRO_NONE, PRO_ADD):
+            return False
+        if x.C % 8 or x.C < 16 or x.sw != x.C or x.sh % 4 or x.sb % 4:
+            return False
+        if p.sw != 1:
+            cap = x.sb // x.C
+            if not (p.sw == 4 and p.kw == 8 and p.pw == 2 and p.kh == 1 and x.H == 1 and x.sb % (4 * x.C) == 0
+                    and cap >= 4 * -(-x.W // 4) and (2 * x.C) % 32 == 0):
+                return False
+        return all(v % 4 == 0 for v in (p.n_group, p.out_sb, p.out_sh, p.out_sw, p.out_sg, out_offset))
+
+    def _tc_weight(self, w: torch.Tensor, mode: int) -> tuple[torch.Tensor, torch.Tensor | None]:
+        """Tensor-core copy of a packed weight: (hi, lo) TF32 split or (bf16, None), cached."""
+        key = (w.data_ptr(), tuple(w.shape), mode)
+        hit = self._tc_cache.get(key)
+        if hit is None:
+            flat = w.reshape(w.shape[0], -1)
+            hit = split_tf32(flat) if mode == _lib.TC_TF32X3 else (flat.to(torch.bfloat16).contiguous(), None)
+            self._tc_cache[key] = hit
+        return hit
 
     def _stats(self, stats: torch.Tensor, groups: int, count: float) -> torch.Tensor:
         out = torch.empty(2 * groups, device=stats.device, dtype=torch.float32)
@@ -315,6 +377,10 @@ class HTDemucsCuda(nn.Module):
                        kw=8, sw=4, pw=2, act=ACT_GELU)
         self._dconv(y, pre)
         out = y.like()
+        if not freq and out.sb // out.C > out.W:
+            # Rows past the logical length are the zero padding the next
+            # stride-4 convolution reads (the reference pads to a multiple of 4).
+            out.t.view(out.B, -1, out.C)[:, out.W :].zero_()
         self._conv(y, self.w(f"{pre}.rewrite.w"), self.w(f"{pre}.rewrite.b"), out, h_out=y.H, w_out=y.W,
                    n_out=2 * cout, act=ACT_GLU)
         return out
@@ -371,10 +437,10 @@ class HTDemucsCuda(nn.Module):
         hd = D // heads
         dev = x.device
         attn = "cross_attn" if cross else "self_attn"
-        win, bin_ = self.w(f"{q}.{attn}.in_proj_weight"), self.w(f"{q}.{attn}.in_proj_bias")
         h = self._ln(x, B * L, D, f"{q}.norm1")
         att = torch.empty(B * L * D, device=dev, dtype=torch.float32)
         if not cross:
+            win, bin_ = self.w(f"{q}.{attn}.in_proj_weight"), self.w(f"{q}.{attn}.in_proj_bias")
             qkv = torch.empty(B * L * 3 * D, device=dev, dtype=torch.float32)
             self._linear(h, B, L, D, win, bin_, qkv, 3 * D)
             base = qkv.data_ptr()
@@ -384,9 +450,9 @@ class HTDemucsCuda(nn.Module):
         else:
             kvn = self._ln(kv_src, B * Lk, D, f"{q}.norm2")
             qp = torch.empty(B * L * D, device=dev, dtype=torch.float32)
-            self._linear(h, B, L, D, win[:D], bin_[:D], qp, D)
+            self._linear(h, B, L, D, self.w(f"{q}.in_q.w"), self.w(f"{q}.in_q.b"), qp, D)
             kv = torch.empty(B * Lk * 2 * D, device=dev, dtype=torch.float32)
-            self._linear(kvn, B, Lk, D, win[D:].contiguous(), bin_[D:].contiguous(), kv, 2 * D)
+            self._linear(kvn, B, Lk, D, self.w(f"{q}.in_kv.w"), self.w(f"{q}.in_kv.b"), kv, 2 * D)
             base = kv.data_ptr()
             _lib.call("unblend_attention_f32", qp.data_ptr(), base, base + 4 * D, att.data_ptr(), B, heads, L,
                       Lk, hd, L * D, D, Lk * 2 * D, 2 * D, L * D, D, 1.0 / math.sqrt(hd),
