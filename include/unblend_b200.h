@@ -127,6 +127,27 @@ int unblend_dconv_tail(float* x, const float* z, const float* stats2, const floa
                        const float* beta, const float* scale, long long groups,
                        long long rows_per_group, int c, long long x_group_stride, void* stream);
 
+/* Fused DConv layer (unblend/blocks.py:238-317) in three streaming passes.
+ * x element (g, r, c) is at x + g*x_gs + r*c_in + c for groups g (GroupNorm
+ * groups: (batch, frequency) rows or batch items) and rows r along time.
+ * conv1: h[g, r, :] = b1 + sum_t W1[:, t, :] x[g, r + (t-1)*dil, :] (zero
+ *   padded), W1 [hid, 3, c]; accumulates (sum, sumsq) of h per group into
+ *   stats (double, zeroed by the caller). Shared memory must hold
+ *   (128 + 2*dil)*(c+4) + 3*hid*c floats (<= 220 KiB).
+ * z_stats: (sum, sumsq) per group of z = W2 gelu(gn1(h)) + b2 with
+ *   st1 = (mean, rstd) of h; W2 [2c, hid] rows interleaved (value, gate).
+ * apply: x += scale * glu(gn2(z)) with z recomputed, st2 = (mean, rstd) of z,
+ *   GN2 affine interleaved like W2. z is never stored. */
+int unblend_dconv_conv1(const float* x, long long x_gs, int groups, int rows, int c, const float* w1,
+                        const float* b1, int hid, int dil, float* h, double* stats, void* stream);
+int unblend_dconv_z_stats(const float* h, int groups, int rows, int hid, int c, const float* st1,
+                          const float* g1w, const float* g1b, const float* w2, const float* b2,
+                          double* stats2, void* stream);
+int unblend_dconv_apply(float* x, long long x_gs, const float* h, int groups, int rows, int hid, int c,
+                        const float* st1, const float* g1w, const float* g1b, const float* w2,
+                        const float* b2, const float* st2, const float* g2w, const float* g2b,
+                        const float* scale, void* stream);
+
 /* LayerNorm over the last dim (eps 1e-5) with optional additive table:
  * y[r,:] = ln(x[r,:]) * gamma + beta + (pos ? pos_scale * pos[r % pos_rows, :] : 0). */
 int unblend_layer_norm(const float* x, float* y, const float* gamma, const float* beta,

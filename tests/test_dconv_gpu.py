@@ -1,0 +1,54 @@
+"""The fused DConv kernels against the reference DConv arithmetic (oracle, fp32)."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from conftest import rel_err
+from oracle.htdemucs_oracle import _dconv as oracle_dconv
+from unblend_b200.htdemucs import Act, HTDemucsCuda
+from unblend_b200.synth import htdemucs_config, htdemucs_state_dict
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def model_and_sd():
+    cfg = htdemucs_config("htdemucs")
+    sd = htdemucs_state_dict(cfg, 0)
+    # Larger LayerScale so the branch is visible above the residual.
+    for k in list(sd):
+        if k.endswith(".6.scale"):
+            sd[k] = torch.randn_like(sd[k])
+    return HTDemucsCuda(cfg, sd, precision="fp32").cuda(), sd
+
+
+@pytest.mark.parametrize("pre,C", [("encoder.0", 48), ("encoder.1", 96), ("encoder.2", 192), ("encoder.3", 384),
+                                   ("decoder.3", 48)])
+def test_fused_dconv_freq_rows(model_and_sd, pre, C):
+    model, sd = model_and_sd
+    B, F, T = 2, 5, 336
+    x = torch.randn(B, F, T, C, device="cuda")
+    a = Act(x.clone().view(-1), B, F, T, C, F * T * C, T * C, C)
+    model._dconv(a, pre)
+    ref_in = x.permute(0, 1, 3, 2).reshape(B * F, C, T).cpu()
+    sdf = {k: v.float() for k, v in sd.items()}
+    ref = oracle_dconv(sdf, pre, ref_in, 2).reshape(B, F, C, T).permute(0, 1, 3, 2)
+    # C = 384 runs its k=3 convolution on the 3-pass TF32 tensor-core kernel.
+    tol = 6e-5 if C >= 384 else 2e-5
+    assert rel_err(a.t.view(B, F, T, C).cpu(), ref) < tol
+
+
+@pytest.mark.parametrize("pre,C,L", [("tencoder.0", 48, 1001), ("tencoder.2", 192, 333)])
+def test_fused_dconv_time_rows_with_capacity(model_and_sd, pre, C, L):
+    model, sd = model_and_sd
+    B, cap = 2, 4 * -(-L // 4)
+    x = torch.randn(B, cap, C, device="cuda")
+    a = Act(x.clone().view(-1), B, 1, L, C, cap * C, cap * C, C)
+    model._dconv(a, pre)
+    sdf = {k: v.float() for k, v in sd.items()}
+    ref = oracle_dconv(sdf, pre, x[:, :L].permute(0, 2, 1).cpu(), 2).permute(0, 2, 1)
+    got = a.t.view(B, cap, C)
+    assert rel_err(got[:, :L].cpu(), ref) < 2e-5
+    assert torch.equal(got[:, L:], x[:, L:])  # capacity rows untouched

@@ -73,6 +73,12 @@ _SIGNATURES = {
     "unblend_divide": [c_void_p, c_void_p, c_void_p, c_int, c_ll, c_void_p],
     "unblend_conv2d_tc": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, ctypes.POINTER(ConvParams), c_int,
                           c_int, c_void_p],
+    "unblend_dconv_conv1": [c_void_p, c_ll, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_int, c_void_p,
+                            c_void_p, c_void_p],
+    "unblend_dconv_z_stats": [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
+                              c_void_p, c_void_p, c_void_p],
+    "unblend_dconv_apply": [c_void_p, c_ll, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p,
+                            c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p],
 }
 
 # Entry points without a stream argument.

@@ -343,14 +343,35 @@ class HTDemucsCuda(nn.Module):
         per_h = 1 if H > 1 else 0
         groups = B * H
         dev = x.t.device
+        x_gs = x.sh if H > 1 else x.sb
         for d in range(self.config["dconv_depth"]):
             q = f"{pre}.dconv.layers.{d}"
             dil = 2**d
             h = Act.freq(B, H, W, hid, dev)
             st1 = torch.zeros(2 * groups, device=dev, dtype=torch.float64)
-            self._conv(x, self.w(f"{q}.c1.w"), self.w(f"{q}.c1.b"), h, h_out=H, w_out=W, n_out=hid, kw=3,
-                       dw=dil, pw=dil, stats=st1, stats_per_h=per_h)
+            conv1_smem = 4 * ((128 + 2 * dil) * (C + 4) + hid * 3 * C)
+            if self.precision != "fp32-simt" and conv1_smem <= 220 * 1024 and C % 4 == 0:
+                _lib.call("unblend_dconv_conv1", x.t.data_ptr(), x_gs, groups, W, C, self.w(f"{q}.c1.w").data_ptr(),
+                          self.w(f"{q}.c1.b").data_ptr(), hid, dil, h.t.data_ptr(), st1.data_ptr(),
+                          work=6.0 * groups * W * C * hid)
+            else:
+                self._conv(x, self.w(f"{q}.c1.w"), self.w(f"{q}.c1.b"), h, h_out=H, w_out=W, n_out=hid, kw=3,
+                           dw=dil, pw=dil, stats=st1, stats_per_h=per_h)
             s1 = self._stats(st1, groups, W * hid)
+            if self.precision != "fp32-simt" and C % 4 == 0:
+                # z = W2 GELU(GN1(h)) is recomputed instead of stored: once for
+                # the GN2 statistics, once for the in-place residual update.
+                st2 = torch.zeros(2 * groups, device=dev, dtype=torch.float64)
+                args = (self.w(f"{q}.g1.w").data_ptr(), self.w(f"{q}.g1.b").data_ptr(),
+                        self.w(f"{q}.c2.w").data_ptr(), self.w(f"{q}.c2.b").data_ptr())
+                _lib.call("unblend_dconv_z_stats", h.t.data_ptr(), groups, W, hid, C, s1.data_ptr(), *args,
+                          st2.data_ptr(), work=4.0 * groups * W * C * hid)
+                s2 = self._stats(st2, groups, W * 2 * C)
+                _lib.call("unblend_dconv_apply", x.t.data_ptr(), x_gs, h.t.data_ptr(), groups, W, hid, C,
+                          s1.data_ptr(), *args, s2.data_ptr(), self.w(f"{q}.g2.w").data_ptr(),
+                          self.w(f"{q}.g2.b").data_ptr(), self.w(f"{q}.scale").data_ptr(),
+                          work=4.0 * groups * W * C * hid)
+                continue
             z = Act.freq(B, H, W, 2 * C, dev)
             st2 = torch.zeros(2 * groups, device=dev, dtype=torch.float64)
             self._conv(h, self.w(f"{q}.c2.w"), self.w(f"{q}.c2.b"), z, h_out=H, w_out=W, n_out=2 * C,
