@@ -163,6 +163,21 @@ int unblend_attention_f32(const float* q, const float* k, const float* v, float*
                           long long kv_sb, long long kv_sr, long long o_sb, long long o_sr,
                           float scale, void* stream);
 
+/* The same attention on the tcgen05 tensor cores (flash attention: S and O in
+ * TMEM, P written back to TMEM as the A operand of the PV product, V
+ * transposed in shared memory). mode 0: 3-pass TF32 split for fp32 accuracy;
+ * mode 1: single-pass TF32 with round-to-nearest operands. Requires hd <= 64,
+ * hd % 4 == 0, strides that are multiples of 4 elements and 16-byte aligned
+ * base pointers. */
+int unblend_attention_tc(const float* q, const float* k, const float* v, float* out, int batch,
+                         int heads, int lq, int lk, int hd, long long q_sb, long long q_sr,
+                         long long kv_sb, long long kv_sr, long long o_sb, long long o_sr,
+                         float scale, int mode, void* stream);
+
+/* Device flag set when a bounded wait of the attention kernel gives up
+ * (0 = none); cleared when `clear` is non-zero. Synchronous host call. */
+int unblend_attention_error_flag(int* out_host, int clear);
+
 /* Elementwise y[i] = a[i] + alpha * b[i % b_period] (skip adds, embeddings). */
 int unblend_add(const float* a, const float* b, float* y, long long n, long long b_period,
                 float alpha, void* stream);

@@ -73,6 +73,8 @@ _SIGNATURES = {
     "unblend_divide": [c_void_p, c_void_p, c_void_p, c_int, c_ll, c_void_p],
     "unblend_conv2d_tc": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, ctypes.POINTER(ConvParams), c_int,
                           c_int, c_void_p],
+    "unblend_attention_tc": [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_ll, c_ll,
+                             c_ll, c_ll, c_ll, c_ll, c_float, c_int, c_void_p],
     "unblend_dconv_conv1": [c_void_p, c_ll, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_int, c_void_p,
                             c_void_p, c_void_p],
     "unblend_dconv_z_stats": [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
@@ -84,6 +86,7 @@ _SIGNATURES = {
 # Entry points without a stream argument.
 _HOST_SIGNATURES = {
     "unblend_error_flag": [ctypes.POINTER(c_int), c_int],
+    "unblend_attention_error_flag": [ctypes.POINTER(c_int), c_int],
 }
 
 TC_TF32X3, TC_BF16 = 0, 1
@@ -116,9 +119,12 @@ def exported_symbols() -> list[str]:
 
 def error_flag(clear: bool = True) -> int:
     """Read (and by default clear) the device flag that bounded waits set on timeout."""
-    v = c_int(0)
-    check("unblend_error_flag", load().unblend_error_flag(ctypes.byref(v), 1 if clear else 0))
-    return v.value
+    total = 0
+    for name in ("unblend_error_flag", "unblend_attention_error_flag"):
+        v = c_int(0)
+        check(name, getattr(load(), name)(ctypes.byref(v), 1 if clear else 0))
+        total |= v.value
+    return total
 
 
 def _cuda_error_string(code: int) -> str:

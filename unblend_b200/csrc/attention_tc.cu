@@ -1,0 +1,480 @@
+// Flash attention on the tcgen05 tensor cores.
+//
+// softmax(Q K^T * scale) V per (batch, head), as nn.MultiheadAttention
+// computes it in eval mode without masks (unblend/transformer.py:290-301
+// self-attention, 402-412 cross-attention), streaming K/V in tiles of 64 keys
+// with an online softmax. One CTA owns 128 queries of one head (head dim <= 64).
+//
+//   warp 0     TMA producer: Q once, then K/V tiles into a 2-3 stage ring
+//   warp 1     MMA issue: S = Q K^T into TMEM, then O += P V with P read from
+//              TMEM (the A operand) and V^T from shared memory (K-major B)
+//   warps 2-5  softmax: one query row per thread; read S from TMEM, update
+//              the running max / sum, write P back over S in TMEM, rescale the
+//              O row in TMEM only when its max moved; final O / l to global
+//   warps 6-9  operand preparation: TF32 rounding / hi-lo split of Q and K in
+//              place, and V transposed to V^T (keys contiguous) while split
+// MODE 0 (fp32 accuracy): every product is hi*hi + hi*lo + lo*hi in
+// kind::tf32 (3 MMAs). MODE 1: single-pass TF32 with round-to-nearest
+// operands (used by the bf16 precision setting).
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "tc_common.cuh"
+
+namespace {
+
+using namespace ub::tc;
+
+constexpr int BQ = 128;
+constexpr int BK = 64;
+constexpr int NT = 320;
+
+template <int MODE>
+struct AL {
+  static constexpr int Q_BYTES = 2 * BQ * 128;   // 2 boxes of 32 dims x 128 rows (fp32)
+  static constexpr int KV_BYTES = 2 * BK * 128;  // 2 boxes of 32 dims x 64 keys, or V^T (64 dims x 64 keys)
+  static constexpr int Q_TOTAL = MODE == 0 ? 2 * Q_BYTES : Q_BYTES;
+  // Stage: K (hi in place) [, K lo], V staging, V^T hi [, V^T lo].
+  static constexpr int K_OFF = 0;
+  static constexpr int KLO_OFF = KV_BYTES;
+  static constexpr int V_OFF = MODE == 0 ? 2 * KV_BYTES : KV_BYTES;
+  static constexpr int VT_OFF = V_OFF + KV_BYTES;
+  static constexpr int VTLO_OFF = VT_OFF + KV_BYTES;
+  static constexpr int STAGE = MODE == 0 ? VTLO_OFF + KV_BYTES : VT_OFF + KV_BYTES;
+  static constexpr int STAGES = MODE == 0 ? 2 : 3;
+  static constexpr int SMEM = Q_TOTAL + STAGES * STAGE + 1024 + 256;
+  // TMEM columns: S/P double buffer, P lo double buffer (MODE 0), the P V
+  // product of the current tile, and the running output accumulator.
+  static constexpr int S_COL = 0;
+  static constexpr int PLO_COL = 128;
+  static constexpr int O_COL = MODE == 0 ? 256 : 128;
+  static constexpr int OACC_COL = O_COL + 64;
+  static constexpr int TMEM_COLS = MODE == 0 ? 512 : 256;
+};
+
+struct AttnArgs {
+  int heads, lq, lk, hd;
+  int q_tiles;
+  float* o;
+  long long o_sb, o_sr;
+  float c;  // scale * log2(e)
+};
+
+__device__ __forceinline__ void tmem_st32(uint32_t addr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(addr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// D[tmem] (+)= A[tmem] * B[smem], kind::tf32.
+__device__ __forceinline__ void umma_tf32_ts(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                             uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accum)
+      : "memory");
+}
+
+__device__ __forceinline__ float tf32_round(float v) {
+  return __uint_as_float((__float_as_uint(v) + 0x1000u) & 0xFFFFE000u);
+}
+
+// Byte offset of element (row r, column c < 32) of a [rows x 32] fp32 tile
+// stored with 128-byte rows and the 128-byte swizzle.
+__device__ __forceinline__ int sw128(int r, int c) { return r * 128 + ((((c >> 2) ^ (r & 7))) << 4) + (c & 3) * 4; }
+
+// Round `n4` float4s at p to TF32 in place; with MODE 0 also write the residuals at lo.
+template <int MODE>
+__device__ __forceinline__ void split_tile(uint8_t* p, uint8_t* lo, int n4, int t, int nt) {
+  float4* h = reinterpret_cast<float4*>(p);
+  float4* l = reinterpret_cast<float4*>(lo);
+  for (int i = t; i < n4; i += nt) {
+    const float4 v = h[i];
+    float4 vh;
+    vh.x = tf32_round(v.x);
+    vh.y = tf32_round(v.y);
+    vh.z = tf32_round(v.z);
+    vh.w = tf32_round(v.w);
+    h[i] = vh;
+    if (MODE == 0) l[i] = make_float4(v.x - vh.x, v.y - vh.y, v.z - vh.z, v.w - vh.w);
+  }
+}
+
+// V staging [2 boxes of (64 keys x 32 dims)] -> V^T [2 blocks of (64 dims x 32 keys)]
+// (keys contiguous, the K-major B operand of O += P V), rounded to TF32, and
+// with MODE 0 the residuals into a second V^T tile.
+template <int MODE>
+__device__ __forceinline__ void transpose_v(const uint8_t* stage_v, uint8_t* vt, uint8_t* vt_lo, int t) {
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    const int i = t + 128 * u;  // float4 index in the staging buffer (1024 of them)
+    const float4 val = reinterpret_cast<const float4*>(stage_v)[i];
+    const int box = i >> 9, within = i & 511;
+    const int key = within >> 3, pchunk = within & 7;
+    const int d0 = box * 32 + ((pchunk ^ (key & 7)) << 2);
+    const float v4[4] = {val.x, val.y, val.z, val.w};
+    const int kb = key >> 5, kk = key & 31;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int d = d0 + e;
+      const int off = kb * (64 * 128) + sw128(d, kk);
+      const float hi = tf32_round(v4[e]);
+      *reinterpret_cast<float*>(vt + off) = hi;
+      if (MODE == 0) *reinterpret_cast<float*>(vt_lo + off) = v4[e] - hi;
+    }
+  }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(NT, 1)
+    attention_tc_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapK,
+                        const __grid_constant__ CUtensorMap mapV, const __grid_constant__ AttnArgs a) {
+  using L = AL<MODE>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sQlo = smem + L::Q_BYTES;
+  uint8_t* sKV = smem + L::Q_TOTAL;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + L::STAGES * L::STAGE);
+  uint64_t* q_full = bars;
+  uint64_t* q_ready = bars + 1;
+  uint64_t* kv_full = bars + 2;
+  uint64_t* kv_conv = kv_full + L::STAGES;
+  uint64_t* kv_free = kv_conv + L::STAGES;
+  uint64_t* s_full = kv_free + L::STAGES;  // [2]
+  uint64_t* p_ready = s_full + 2;          // [2]
+  uint64_t* o_done = p_ready + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = blockIdx.x % a.q_tiles;
+  const int h = (blockIdx.x / a.q_tiles) % a.heads;
+  const int b = blockIdx.x / (a.q_tiles * a.heads);
+  const int q0 = qt * BQ;
+  const int nkv = (a.lk + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(q_ready, 4);
+    for (int s = 0; s < L::STAGES; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_conv[s], 4);
+      mbar_init(&kv_free[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_ready[i], 4);
+    }
+    mbar_init(o_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, L::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_expect_tx(q_full, L::Q_BYTES);
+      tma_load_4d(sQ, &mapQ, q_full, 0, h, q0, b);
+      tma_load_4d(sQ + BQ * 128, &mapQ, q_full, 32, h, q0, b);
+      for (int j = 0; j < nkv; ++j) {
+        const int s = j % L::STAGES, r = j / L::STAGES;
+        if (r > 0 && !mbar_wait(&kv_free[s], (r - 1) & 1)) break;
+        uint8_t* st = sKV + s * L::STAGE;
+        mbar_expect_tx(&kv_full[s], 2 * L::KV_BYTES);
+        tma_load_4d(st + L::K_OFF, &mapK, &kv_full[s], 0, h, j * BK, b);
+        tma_load_4d(st + L::K_OFF + BK * 128, &mapK, &kv_full[s], 32, h, j * BK, b);
+        tma_load_4d(st + L::V_OFF, &mapV, &kv_full[s], 0, h, j * BK, b);
+        tma_load_4d(st + L::V_OFF + BK * 128, &mapV, &kv_full[s], 32, h, j * BK, b);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t id_s = instr_desc(2u, (uint32_t)BK);  // N = 64 keys
+      constexpr uint32_t id_o = instr_desc(2u, 64u);           // N = 64 dims
+      bool ok = mbar_wait(q_ready, 0);
+      const uint32_t q_hi = smem_u32(sQ), q_lo = smem_u32(sQlo);
+      auto issue_s = [&](int j) {
+        const uint8_t* st = sKV + (j % L::STAGES) * L::STAGE;
+        const uint32_t k_hi = smem_u32(st + L::K_OFF), k_lo = smem_u32(st + L::KLO_OFF);
+        const uint32_t d = tmem + L::S_COL + (j & 1) * BK;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint32_t qa = (i >> 2) * (BQ * 128) + (i & 3) * 32;
+          const uint32_t ka = (i >> 2) * (BK * 128) + (i & 3) * 32;
+          umma_tf32(d, smem_desc(q_hi + qa, 128), smem_desc(k_hi + ka, 128), id_s, i > 0 ? 1u : 0u);
+          if (MODE == 0) {
+            umma_tf32(d, smem_desc(q_hi + qa, 128), smem_desc(k_lo + ka, 128), id_s, 1u);
+            umma_tf32(d, smem_desc(q_lo + qa, 128), smem_desc(k_hi + ka, 128), id_s, 1u);
+          }
+        }
+        umma_commit(&s_full[j & 1]);
+      };
+      if (ok) ok = mbar_wait(&kv_conv[0], 0);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0);
+      }
+      for (int j = 0; j < nkv && ok; ++j) {
+        if (j + 1 < nkv) {
+          if (!mbar_wait(&kv_conv[(j + 1) % L::STAGES], ((j + 1) / L::STAGES) & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_s(j + 1);
+        }
+        if (!mbar_wait(&p_ready[j & 1], (j >> 1) & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const int s = j % L::STAGES;
+        const uint8_t* st = sKV + s * L::STAGE;
+        const uint32_t vt_hi = smem_u32(st + L::VT_OFF), vt_lo = smem_u32(st + L::VTLO_OFF);
+        const uint32_t p_hi = tmem + L::S_COL + (j & 1) * BK;
+        const uint32_t p_lo = tmem + L::PLO_COL + (j & 1) * BK;
+        const uint32_t o = tmem + L::O_COL;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {  // 8 keys per step
+          const uint32_t vb = (i >> 2) * (64 * 128) + (i & 3) * 32;
+          umma_tf32_ts(o, p_hi + 8 * i, smem_desc(vt_hi + vb, 128), id_o, i > 0 ? 1u : 0u);
+          if (MODE == 0) {
+            umma_tf32_ts(o, p_hi + 8 * i, smem_desc(vt_lo + vb, 128), id_o, 1u);
+            umma_tf32_ts(o, p_lo + 8 * i, smem_desc(vt_hi + vb, 128), id_o, 1u);
+          }
+        }
+        umma_commit(o_done);
+        umma_commit(&kv_free[s]);
+      }
+      if (!ok) atomicExch(&g_error_flag, 3);
+    }
+  } else if (warp >= 6) {
+    // Operand preparation for Q (once) and every K/V tile.
+    const int ct = threadIdx.x - 192;
+    bool ok = mbar_wait(q_full, 0);
+    if (ok) {
+      split_tile<MODE>(sQ, sQlo, L::Q_BYTES / 16, ct, 128);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(q_ready);
+    }
+    for (int j = 0; j < nkv && ok; ++j) {
+      const int s = j % L::STAGES, r = j / L::STAGES;
+      if (!mbar_wait(&kv_full[s], r & 1)) break;
+      uint8_t* st = sKV + s * L::STAGE;
+      split_tile<MODE>(st + L::K_OFF, st + L::KLO_OFF, L::KV_BYTES / 16, ct, 128);
+      transpose_v<MODE>(st + L::V_OFF, st + L::VT_OFF, st + (MODE == 0 ? L::VTLO_OFF : L::VT_OFF), ct);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&kv_conv[s]);
+    }
+  } else {
+    // Softmax warps 2-5: thread = query row 32*(warp%4) + lane.
+    const int qw = warp & 3;
+    const int row = qw * 32 + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)(qw * 32) << 16);
+    float m = -INFINITY, l = 0.f, corr_prev = 0.f;
+    bool ok = true;
+    // O_acc = O_acc * corr + O_tile for tile t (the first tile initialises O_acc).
+    auto fold_tile = [&](uint32_t base, int t, float corr) {
+      uint32_t a0[32], a1[32], t0[32], t1[32];
+      tmem_ld32(base + L::O_COL, t0);
+      tmem_ld32(base + L::O_COL + 32, t1);
+      if (t > 0) {
+        tmem_ld32(base + L::OACC_COL, a0);
+        tmem_ld32(base + L::OACC_COL + 32, a1);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          t0[i] = __float_as_uint(fmaf(__uint_as_float(a0[i]), corr, __uint_as_float(t0[i])));
+          t1[i] = __float_as_uint(fmaf(__uint_as_float(a1[i]), corr, __uint_as_float(t1[i])));
+        }
+      }
+      tmem_st32(base + L::OACC_COL, t0);
+      tmem_st32(base + L::OACC_COL + 32, t1);
+      tmem_st_wait();
+    };
+    for (int j = 0; j < nkv && ok; ++j) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[j & 1], (j >> 1) & 1))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t s0[32], s1[32];
+      __syncwarp();
+      tmem_ld32(lane_base + L::S_COL + (j & 1) * BK, s0);
+      tmem_ld32(lane_base + L::S_COL + (j & 1) * BK + 32, s1);
+      const int kbase = j * BK;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float v0 = kbase + i < a.lk ? __uint_as_float(s0[i]) * a.c : -INFINITY;
+        const float v1 = kbase + 32 + i < a.lk ? __uint_as_float(s1[i]) * a.c : -INFINITY;
+        s0[i] = __float_as_uint(v0);
+        s1[i] = __float_as_uint(v1);
+        mx = fmaxf(mx, fmaxf(v0, v1));
+      }
+      const float m_new = fmaxf(m, mx);
+      const float corr = exp2f(m - m_new);
+      float sum = 0.f;
+      uint32_t lo0[32], lo1[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float p0 = exp2f(__uint_as_float(s0[i]) - m_new);
+        const float p1 = exp2f(__uint_as_float(s1[i]) - m_new);
+        sum += p0 + p1;
+        const float h0 = tf32_round(p0), h1 = tf32_round(p1);
+        s0[i] = __float_as_uint(h0);
+        s1[i] = __float_as_uint(h1);
+        lo0[i] = __float_as_uint(p0 - h0);
+        lo1[i] = __float_as_uint(p1 - h1);
+      }
+      l = l * corr + sum;
+      m = m_new;
+      if (j > 0) {
+        // Fold the previous tile's P V into the running accumulator with
+        // CUDA-core fp32 arithmetic (the tensor core only ever sums one tile).
+        if (!__all_sync(0xffffffffu, mbar_wait(o_done, (j - 1) & 1))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        fold_tile(lane_base, j - 1, corr_prev);
+      }
+      corr_prev = corr;
+      tmem_st32(lane_base + L::S_COL + (j & 1) * BK, s0);
+      tmem_st32(lane_base + L::S_COL + (j & 1) * BK + 32, s1);
+      if (MODE == 0) {
+        tmem_st32(lane_base + L::PLO_COL + (j & 1) * BK, lo0);
+        tmem_st32(lane_base + L::PLO_COL + (j & 1) * BK + 32, lo1);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_ready[j & 1]);
+    }
+    if (ok && nkv > 0) ok = __all_sync(0xffffffffu, mbar_wait(o_done, (nkv - 1) & 1));
+    tc_fence_after();
+    if (ok) {
+      __syncwarp();
+      fold_tile(lane_base, nkv - 1, corr_prev);
+      uint32_t o0[32], o1[32];
+      tmem_ld32(lane_base + L::OACC_COL, o0);
+      tmem_ld32(lane_base + L::OACC_COL + 32, o1);
+      const int qrow = q0 + row;
+      if (qrow < a.lq) {
+        const float inv = 1.f / l;
+        float* out = a.o + (long long)b * a.o_sb + (long long)qrow * a.o_sr + (long long)h * a.hd;
+#pragma unroll
+        for (int d = 0; d < 64; d += 4) {
+          if (d < a.hd) {
+            float4 v;
+            if (d < 32)
+              v = make_float4(__uint_as_float(o0[d]), __uint_as_float(o0[d + 1]), __uint_as_float(o0[d + 2]),
+                              __uint_as_float(o0[d + 3]));
+            else
+              v = make_float4(__uint_as_float(o1[d - 32]), __uint_as_float(o1[d - 31]),
+                              __uint_as_float(o1[d - 30]), __uint_as_float(o1[d - 29]));
+            *reinterpret_cast<float4*>(out + d) = make_float4(v.x * inv, v.y * inv, v.z * inv, v.w * inv);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, L::TMEM_COLS);
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 4-D map (head dim, head, row, batch) of one of Q/K/V with boxes of 32 dims x box_rows rows.
+bool head_map(CUtensorMap* m, const float* base, int hd, int heads, int rows, int batch, long long row_stride,
+              long long batch_stride, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[4] = {(cuuint64_t)hd, (cuuint64_t)heads, (cuuint64_t)rows, (cuuint64_t)batch};
+  cuuint64_t strides[3] = {(cuuint64_t)hd * 4, (cuuint64_t)row_stride * 4, (cuuint64_t)batch_stride * 4};
+  cuuint32_t box[4] = {32, 1, (cuuint32_t)box_rows, 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(base), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+extern "C" int unblend_attention_error_flag(int* out_host, int clear) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_error_flag, sizeof(int));
+  if (e != cudaSuccess) return (int)e;
+  if (out_host) *out_host = v;
+  if (clear) {
+    int z = 0;
+    e = cudaMemcpyToSymbol(g_error_flag, &z, sizeof(int));
+    if (e != cudaSuccess) return (int)e;
+  }
+  return 0;
+}
+
+extern "C" int unblend_attention_tc(const float* q, const float* k, const float* v, float* out, int batch, int heads,
+                                    int lq, int lk, int hd, long long q_sb, long long q_sr, long long kv_sb,
+                                    long long kv_sr, long long o_sb, long long o_sr, float scale, int mode,
+                                    void* stream) {
+  UB_REQUIRE(q && k && v && out && batch > 0 && heads > 0 && lq > 0 && lk > 0 && (mode == 0 || mode == 1));
+  UB_REQUIRE(hd > 0 && hd <= 64 && hd % 4 == 0);
+  UB_REQUIRE(q_sr % 4 == 0 && q_sb % 4 == 0 && kv_sr % 4 == 0 && kv_sb % 4 == 0 && o_sr % 4 == 0 && o_sb % 4 == 0);
+  UB_REQUIRE((reinterpret_cast<uintptr_t>(q) & 15) == 0 && (reinterpret_cast<uintptr_t>(k) & 15) == 0 &&
+             (reinterpret_cast<uintptr_t>(v) & 15) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0);
+  CUtensorMap mq, mk, mv;
+  if (!head_map(&mq, q, hd, heads, lq, batch, q_sr, q_sb, BQ) ||
+      !head_map(&mk, k, hd, heads, lk, batch, kv_sr, kv_sb, BK) ||
+      !head_map(&mv, v, hd, heads, lk, batch, kv_sr, kv_sb, BK))
+    return UNBLEND_ERR_INVALID;
+  AttnArgs a{};
+  a.heads = heads;
+  a.lq = lq;
+  a.lk = lk;
+  a.hd = hd;
+  a.q_tiles = (lq + BQ - 1) / BQ;
+  a.o = out;
+  a.o_sb = o_sb;
+  a.o_sr = o_sr;
+  a.c = scale * 1.4426950408889634f;
+  const long long grid = (long long)batch * heads * a.q_tiles;
+  UB_REQUIRE(grid < (1LL << 31));
+  cudaStream_t st = ub::as_stream(stream);
+  if (mode == 0) {
+    cudaFuncSetAttribute(attention_tc_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, AL<0>::SMEM);
+    attention_tc_kernel<0><<<(unsigned)grid, NT, AL<0>::SMEM, st>>>(mq, mk, mv, a);
+  } else {
+    cudaFuncSetAttribute(attention_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, AL<1>::SMEM);
+    attention_tc_kernel<1><<<(unsigned)grid, NT, AL<1>::SMEM, st>>>(mq, mk, mv, a);
+  }
+  UB_CHECK_LAUNCH();
+  return 0;
+}

@@ -216,7 +216,7 @@ __global__ void __launch_bounds__(NT, 1)
       if (lane == 0) mbar_arrive(&conv[s]);
     }
     // Epilogue: TMEM -> registers -> fused ops -> global.
-    if (ok) ok = mbar_wait(accum, 0);
+    ok = __all_sync(0xffffffffu, ok && mbar_wait(accum, 0));
     tc_fence_after();
     if (ok) {
       const int q = warp & 3;

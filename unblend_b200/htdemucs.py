@@ -451,6 +451,19 @@ class HTDemucsCuda(nn.Module):
                   self.w(f"{name}.bias").data_ptr(), _lib.ptr(pos), 1.0, pos_rows, rows, c)
         return y
 
+    def _attention(self, q: int, k: int, v: int, o: int, B: int, heads: int, L: int, Lk: int, hd: int, q_sb: int,
+                   q_sr: int, kv_sb: int, kv_sr: int, o_sb: int, o_sr: int) -> None:
+        """softmax(Q K^T / sqrt(hd)) V for all heads: tensor-core flash attention, or SIMT."""
+        work = 4.0 * B * L * Lk * hd * heads
+        scale = 1.0 / math.sqrt(hd)
+        if self.precision != "fp32-simt" and hd % 4 == 0 and hd <= 64 and all(p % 16 == 0 for p in (q, k, v, o)):
+            mode = 0 if self.precision == "fp32" else 1
+            _lib.call("unblend_attention_tc", q, k, v, o, B, heads, L, Lk, hd, q_sb, q_sr, kv_sb, kv_sr, o_sb, o_sr,
+                      scale, mode, work=work)
+            return
+        _lib.call("unblend_attention_f32", q, k, v, o, B, heads, L, Lk, hd, q_sb, q_sr, kv_sb, kv_sr, o_sb, o_sr,
+                  scale, work=work)
+
     def _attn_layer(self, q: str, x: torch.Tensor, kv_src: torch.Tensor | None, B: int, L: int, Lk: int,
                     D: int, cross: bool) -> torch.Tensor:
         """One transformer layer with norm_first, LayerScale and norm_out (unblend/transformer.py:328-359, 461-481)."""
@@ -465,9 +478,8 @@ class HTDemucsCuda(nn.Module):
             qkv = torch.empty(B * L * 3 * D, device=dev, dtype=torch.float32)
             self._linear(h, B, L, D, win, bin_, qkv, 3 * D)
             base = qkv.data_ptr()
-            _lib.call("unblend_attention_f32", base, base + 4 * D, base + 8 * D, att.data_ptr(), B, heads, L, L,
-                      hd, L * 3 * D, 3 * D, L * 3 * D, 3 * D, L * D, D, 1.0 / math.sqrt(hd),
-                      work=4.0 * B * L * L * D)
+            self._attention(base, base + 4 * D, base + 8 * D, att.data_ptr(), B, heads, L, L, hd, L * 3 * D,
+                            3 * D, L * 3 * D, 3 * D, L * D, D)
         else:
             kvn = self._ln(kv_src, B * Lk, D, f"{q}.norm2")
             qp = torch.empty(B * L * D, device=dev, dtype=torch.float32)
@@ -475,9 +487,8 @@ class HTDemucsCuda(nn.Module):
             kv = torch.empty(B * Lk * 2 * D, device=dev, dtype=torch.float32)
             self._linear(kvn, B, Lk, D, self.w(f"{q}.in_kv.w"), self.w(f"{q}.in_kv.b"), kv, 2 * D)
             base = kv.data_ptr()
-            _lib.call("unblend_attention_f32", qp.data_ptr(), base, base + 4 * D, att.data_ptr(), B, heads, L,
-                      Lk, hd, L * D, D, Lk * 2 * D, 2 * D, L * D, D, 1.0 / math.sqrt(hd),
-                      work=4.0 * B * L * Lk * D)
+            self._attention(qp.data_ptr(), base, base + 4 * D, att.data_ptr(), B, heads, L, Lk, hd, L * D, D,
+                            Lk * 2 * D, 2 * D, L * D, D)
         x_new = torch.empty_like(x)
         self._linear(att, B, L, D, self.w(f"{q}.{attn}.out_proj.weight"), self.w(f"{q}.{attn}.out_proj.bias"),
                      x_new, D, res=x, res_scale=self.w(f"{q}.gamma_1.scale"))
