@@ -161,13 +161,13 @@ class HTDemucsCuda(nn.Module):
         self._pack(state_dict)
 
     @classmethod
-    def from_reference(cls, module: nn.Module) -> "HTDemucsCuda":
+    def from_reference(cls, module: nn.Module, precision: str = "fp32") -> "HTDemucsCuda":
         """Build from a reference ``HTDemucs`` instance (its captured init kwargs + state_dict)."""
         args, kwargs = getattr(module, "_init_args_kwargs", ((), {}))
         cfg = dict(kwargs)
         if args:
             cfg["sources"] = args[0]
-        return cls(cfg, module.state_dict())
+        return cls(cfg, module.state_dict(), precision=precision)
 
     # ------------------------------------------------------------------ weights
     def _put(self, name: str, t: torch.Tensor) -> None:
