@@ -22,6 +22,7 @@ extern "C" {
 #endif
 
 #define UNBLEND_ERR_INVALID 1000
+#define UNBLEND_ERR_TOO_LARGE 1001 /* request exceeds a fixed built-in capacity */
 
 /* Activation applied in a convolution epilogue. */
 enum UnblendAct {
@@ -217,6 +218,22 @@ int unblend_istft_output(const float* spec, const float* xt, long long xt_sb, co
 /* Per-batch (mean, std) with torch.var_mean semantics (unbiased) of a contiguous
  * [batch, n] array; out float[2*batch] = (mean, std). Uses `work` double[2*batch]. */
 int unblend_mean_std(const float* x, double* work, float* out, int batch, long long n,
+                     void* stream);
+
+/* unblend_mean_std without the caller-provided `work` buffer. This entry point
+ * has no counterpart in the reference; it exists for callers that cannot
+ * allocate device memory at call time (a real-time audio thread, where
+ * cudaMalloc may stall on a device-wide synchronisation, or a host whose own
+ * memory manager owns all device allocations). Its accumulator is a static
+ * device array of UNBLEND_NOALLOC_MAX_BATCH batch items (64 KiB, held by every
+ * GPU that loads the library until process exit); larger batches return
+ * UNBLEND_ERR_TOO_LARGE. It calls no allocator. The first call on each device
+ * looks up the array's device address (cudaGetSymbolAddress) with that device
+ * current, so make that first call before any stream capture. All calls share
+ * the one array: each call clears the part it uses, and calls that overlap on
+ * the GPU (e.g. on two streams at once) race with each other. */
+#define UNBLEND_NOALLOC_MAX_BATCH 4096
+int unblend_mean_std_noalloc(const float* x, float* out, int batch, long long n,
                      void* stream);
 
 /* Segment engine (unblend/apply.py:278-311, 406-432, 1219-1238, 1329). */

@@ -17,6 +17,8 @@ import torch
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "_lib", "libunblend_b200.so")
 ERR_INVALID = 1000
+ERR_TOO_LARGE = 1001
+NOALLOC_MAX_BATCH = 4096
 
 c_int = ctypes.c_int
 c_ll = ctypes.c_longlong
@@ -67,6 +69,7 @@ _SIGNATURES = {
     "unblend_istft_output": [c_void_p, c_void_p, c_ll, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                              c_int, c_int, c_int, c_int, c_void_p],
     "unblend_mean_std": [c_void_p, c_void_p, c_void_p, c_int, c_ll, c_void_p],
+    "unblend_mean_std_noalloc": [c_void_p, c_void_p, c_int, c_ll, c_void_p],
     "unblend_gather_chunks": [c_void_p, c_int, c_ll, c_void_p, c_int, c_int, c_void_p, c_void_p],
     "unblend_overlap_add": [c_void_p, c_int, c_int, c_int, c_void_p, c_ll, c_ll, c_ll, c_void_p, c_void_p,
                             c_void_p],
@@ -141,6 +144,8 @@ def check(name: str, rc: int) -> None:
     """Raise ``RuntimeError`` for a non-zero launcher return code."""
     if rc == 0:
         return
+    if rc == ERR_TOO_LARGE:
+        raise RuntimeError(f"{name}: request exceeds the entry point's fixed built-in capacity")
     if rc == ERR_INVALID:
         raise RuntimeError(f"{name}: invalid arguments")
     text = _cuda_error_string(rc)

@@ -275,3 +275,55 @@ extern "C" int unblend_standardize(const float* x, float* y, const float* stats2
   UB_CHECK_LAUNCH();
   return 0;
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of unblend_mean_std.
+//
+// unblend_mean_std needs a double[2 * batch] accumulator from its caller. Some
+// callers cannot provide one: code running on a real-time audio thread, where
+// cudaMalloc can block on a device-wide synchronisation for an unbounded time,
+// and hosts that embed this library under a memory manager that owns every
+// device allocation. For them the accumulator lives in this file-scope device
+// array instead: UNBLEND_NOALLOC_MAX_BATCH batch items at most (64 KiB), held
+// by every GPU that loads the library until the process exits.
+static __device__ __align__(256) double g_mean_std_scratch[2 * UNBLEND_NOALLOC_MAX_BATCH];
+
+#include <mutex>
+
+namespace {
+std::mutex g_scratch_mutex;
+double* g_scratch_addr[64] = {nullptr};  // device address of the array, per device ordinal
+
+// Device address of the scratch array on the current device. In host code the
+// array's name is only a host-side stand-in, so the address is resolved once
+// per device with that device current.
+int scratch_for_current_device(double** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return (int)e;
+  if (dev < 0 || dev >= 64) return UNBLEND_ERR_INVALID;
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (!g_scratch_addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_mean_std_scratch);
+    if (e != cudaSuccess) return (int)e;
+    g_scratch_addr[dev] = static_cast<double*>(p);
+  }
+  *out = g_scratch_addr[dev];
+  return 0;
+}
+}  // namespace
+
+extern "C" int unblend_mean_std_noalloc(const float* x, float* out, int batch, long long n, void* stream) {
+  UB_REQUIRE(x && out && batch > 0 && n > 1);
+  if (batch > UNBLEND_NOALLOC_MAX_BATCH) return UNBLEND_ERR_TOO_LARGE;
+  double* scratch = nullptr;
+  int rc = scratch_for_current_device(&scratch);
+  if (rc) return rc;
+  // The array keeps the previous call's sums: clear the part this call uses.
+  rc = unblend_zero_f64(scratch, 2LL * batch, stream);
+  if (rc) return rc;
+  rc = unblend_group_sums(x, scratch, batch, n, stream);
+  if (rc) return rc;
+  return unblend_stats_finalize(scratch, out, batch, (double)n, 0.f, 1, 1, stream);
+}
