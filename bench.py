@@ -40,7 +40,7 @@ sys.path.insert(0, ROOT)
 TRACK_SECONDS = 180.0
 BATCH = 32
 CPU_SAMPLE_SECONDS = 30.0
-METRIC = "audio-sec separated/sec (x realtime), HTDemucs 44.1kHz stereo"
+METRIC = "audio-sec separated/sec (×realtime), HTDemucs 44.1kHz stereo, 1/2/4/8 B200"
 
 
 def _args():
@@ -51,6 +51,9 @@ def _args():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--precision", default="fp32", choices=["fp32", "bf16", "fp32-simt"])
+    ap.add_argument("--seconds", type=float, default=TRACK_SECONDS,
+                    help="track length per rank (smaller values are for profiling only)")
+    ap.add_argument("--batch", type=int, default=BATCH, help="segments per forward")
     return ap.parse_args()
 
 
@@ -183,9 +186,10 @@ def main() -> None:
     dev = torch.device("cuda", torch.cuda.current_device())
     cfg = htdemucs_config("htdemucs")
     model = HTDemucsCuda(cfg, htdemucs_state_dict(cfg, 0), precision=args.precision).to(dev)
-    track = synth_track(TRACK_SECONDS, 1 + rank)
+    seconds, batch = args.seconds, args.batch
+    track = synth_track(seconds, 1 + rank)
     track_dev = track.to(dev)
-    step = lambda: apply_model(model, track_dev, chunk_batch_size=BATCH)  # noqa: E731
+    step = lambda: apply_model(model, track_dev, chunk_batch_size=batch)  # noqa: E731
 
     for _ in range(args.warmup):
         step()
@@ -219,7 +223,7 @@ def main() -> None:
 
     # End to end through the public API with a pinned host track.
     host = track.pin_memory()
-    e2e_step = lambda: apply_model(model, host, device=dev, chunk_batch_size=BATCH)  # noqa: E731
+    e2e_step = lambda: apply_model(model, host, device=dev, chunk_batch_size=batch)  # noqa: E731
     e2e_step()
     e2e_ms = timed(e2e_step, max(1, args.steps))
 
@@ -244,14 +248,17 @@ def main() -> None:
                 "share_of_step": round(a["ms"] / sum(v["ms"] for v in agg.values()), 3),
                 "launches_per_step": a["n"]}
 
-    value = world * TRACK_SECONDS / (ms * 1e-3)
-    e2e_value = world * TRACK_SECONDS / (e2e_ms * 1e-3)
+    value = world * seconds / (ms * 1e-3)
+    e2e_value = world * seconds / (e2e_ms * 1e-3)
     L = track.shape[-1]
+    n_seg = len(range(0, L, int(0.75 * model.segment_length)))
+    dtype = {"fp32": "f32", "bf16": "bf16", "fp32-simt": "f32"}[args.precision]
     line = {"metric": METRIC, "value": round(value, 3), "unit": "audio-s/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "HTDemucs 4-stem, 180 s stereo track, 31 segments of 7.8 s, overlap 0.25, "
-                                   "32 segments per launch", "track_seconds": TRACK_SECONDS, "segments_per_launch": BATCH,
+            "scaling": "weak", "vs_baseline": None, "dtype": dtype, "data": "synthetic",
+            "config": {"workload": f"HTDemucs 4-stem, {seconds:g} s stereo track, {n_seg} segments of 7.8 s, "
+                                   f"overlap 0.25, {batch} segments per launch, precision {args.precision}",
+                       "track_seconds": seconds, "segments_per_launch": batch, "precision": args.precision,
                        "parallelism": f"whole tracks per rank x{world}",
                        "l2": "inputs and activations far larger than L2 (no flush needed)"},
             "e2e": {"value": round(e2e_value, 3), "unit": "audio-s/s", "h2d_bytes_per_step": 2 * L * 4,

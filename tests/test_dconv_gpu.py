@@ -35,8 +35,8 @@ def test_fused_dconv_freq_rows(model_and_sd, pre, C):
     ref_in = x.permute(0, 1, 3, 2).reshape(B * F, C, T).cpu()
     sdf = {k: v.float() for k, v in sd.items()}
     ref = oracle_dconv(sdf, pre, ref_in, 2).reshape(B, F, C, T).permute(0, 1, 3, 2)
-    # C = 384 runs its k=3 convolution on the 3-pass TF32 tensor-core kernel.
-    tol = 6e-5 if C >= 384 else 2e-5
+    # C >= 192 runs both contractions on the 3-pass TF32 tensor-core kernel.
+    tol = 6e-5 if C >= 192 else 2e-5
     assert rel_err(a.t.view(B, F, T, C).cpu(), ref) < tol
 
 
@@ -50,5 +50,5 @@ def test_fused_dconv_time_rows_with_capacity(model_and_sd, pre, C, L):
     sdf = {k: v.float() for k, v in sd.items()}
     ref = oracle_dconv(sdf, pre, x[:, :L].permute(0, 2, 1).cpu(), 2).permute(0, 2, 1)
     got = a.t.view(B, cap, C)
-    assert rel_err(got[:, :L].cpu(), ref) < 2e-5
+    assert rel_err(got[:, :L].cpu(), ref) < (6e-5 if C >= 192 else 2e-5)
     assert torch.equal(got[:, L:], x[:, L:])  # capacity rows untouched

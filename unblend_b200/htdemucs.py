@@ -350,6 +350,26 @@ class HTDemucsCuda(nn.Module):
             h = Act.freq(B, H, W, hid, dev)
             st1 = torch.zeros(2 * groups, device=dev, dtype=torch.float64)
             conv1_smem = 4 * ((128 + 2 * dil) * (C + 4) + hid * 3 * C)
+            # Deep levels (hidden width >= 16): both contractions on the tensor
+            # cores, z materialised (these levels hold few rows).
+            deep = self.precision != "fp32-simt" and hid % 8 == 0 and hid >= 16
+            if deep:
+                self._conv(x, self.w(f"{q}.c1.w"), self.w(f"{q}.c1.b"), h, h_out=H, w_out=W, n_out=hid, kw=3,
+                           dw=dil, pw=dil, stats=st1, stats_per_h=per_h)
+                s1 = self._stats(st1, groups, W * hid)
+                a = h.like()
+                _lib.call("unblend_group_norm_apply", h.t.data_ptr(), a.t.data_ptr(), s1.data_ptr(),
+                          self.w(f"{q}.g1.w").data_ptr(), self.w(f"{q}.g1.b").data_ptr(), groups * W, hid, W,
+                          ACT_GELU)
+                z = Act.freq(B, H, W, 2 * C, dev)
+                st2 = torch.zeros(2 * groups, device=dev, dtype=torch.float64)
+                self._conv(a, self.w(f"{q}.c2.w"), self.w(f"{q}.c2.b"), z, h_out=H, w_out=W, n_out=2 * C,
+                           stats=st2, stats_per_h=per_h)
+                s2 = self._stats(st2, groups, W * 2 * C)
+                _lib.call("unblend_dconv_tail", x.t.data_ptr(), z.t.data_ptr(), s2.data_ptr(),
+                          self.w(f"{q}.g2.w").data_ptr(), self.w(f"{q}.g2.b").data_ptr(),
+                          self.w(f"{q}.scale").data_ptr(), groups, W, C, x_gs)
+                continue
             if self.precision != "fp32-simt" and conv1_smem <= 220 * 1024 and C % 4 == 0:
                 _lib.call("unblend_dconv_conv1", x.t.data_ptr(), x_gs, groups, W, C, self.w(f"{q}.c1.w").data_ptr(),
                           self.w(f"{q}.c1.b").data_ptr(), hid, dil, h.t.data_ptr(), st1.data_ptr(),
