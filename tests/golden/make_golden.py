@@ -19,6 +19,14 @@ bit for bit, and saves the reference's fp32 CPU outputs on synthetic audio:
 * ``apply_small.pt``      ``apply_model`` (unblend/apply.py:500) with the
   reduced model over a 4-segment track, shifts 0 and shifts 1 (offsets drawn
   after ``random.seed(5)``), every 7th output sample plus full sums.
+* ``bsroformer_small.pt`` reduced BS-RoFormer (dim 64, depth 2, 4 heads of 16,
+  seed 3), batch 2 on 0.5 s, full outputs of ``BSRoformer.forward``
+  (unblend/roformer.py:1312).
+* ``bsroformer_full.pt``  the measured BS-RoFormer (dim 512, depth 12, seed 3)
+  on a 1 s clip, every 5th output sample plus per-stem sums.
+* ``bsroformer_apply.pt`` ``apply_model`` with the reduced BS-RoFormer set up by
+  ``configure_inference`` for 0.5 s segments and a complement stem
+  (sources ["vocals", "other"]), over a 4-segment track.
 
 The fixtures hold only outputs and small inputs; weights are regenerated from
 the seed on the fly, and ``weights_digest`` pins that regeneration.
@@ -38,9 +46,16 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, ROOT)
 
-from unblend_b200.synth import htdemucs_config, htdemucs_state_dict, synth_track  # noqa: E402
+from unblend_b200.synth import (  # noqa: E402
+    bsroformer_config,
+    bsroformer_state_dict,
+    htdemucs_config,
+    htdemucs_state_dict,
+    synth_track,
+)
 
 SMALL_OVERRIDES = dict(channels=8, bottom_channels=32, t_heads=4, t_layers=3, segment=0.5)
+ROFORMER_SMALL = dict(dim=64, depth=2, heads=4, dim_head=16)
 
 
 def import_reference(path: str):
@@ -121,8 +136,51 @@ def main(ref_path: str) -> None:
             torch.save({"config": cfg, "seed": seed, "weights_digest": digest, "mix": mix,
                         "decimate": 5, "out": out[..., ::5].clone(), **_summary(out)},
                        os.path.join(HERE, fname))
+    main_roformer(unblend)
     print("fixtures written to", HERE)
 
 
+def build_roformer(unblend, cfg: dict, seed: int):
+    """``manual_seed(seed); BSRoformer(**cfg)``, checked against ``bsroformer_state_dict``."""
+    import unblend.roformer
+
+    torch.manual_seed(seed)
+    model = unblend.roformer.BSRoformer(**cfg).eval()
+    mine = bsroformer_state_dict(cfg, seed)
+    ref = model.state_dict()
+    assert set(ref) == set(mine), "state_dict keys differ"
+    for k in ref:
+        assert torch.equal(ref[k], mine[k]), f"weight {k} differs"
+    return model, weights_digest(mine)
+
+
+def main_roformer(unblend) -> None:
+    """BS-RoFormer fixtures (reduced model, measured configuration, apply_model)."""
+    with torch.inference_mode():
+        cfg = bsroformer_config(**ROFORMER_SMALL)
+        model, digest = build_roformer(unblend, cfg, 3)
+        mix = torch.stack([synth_track(0.5, 20), synth_track(0.5, 21)])
+        out = model(mix)
+        torch.save({"config": cfg, "seed": 3, "weights_digest": digest, "mix": mix, "out": out.clone()},
+                   os.path.join(HERE, "bsroformer_small.pt"))
+
+        model.configure_inference(sources=["vocals", "other"], samplerate=44100, segment_samples=22050)
+        track = synth_track(1.3, 22)[None]
+        y = unblend.apply.apply_model(model, track, device="cpu", shifts=0, overlap=0.25, chunk_batch_size=3)
+        torch.save({"config": cfg, "seed": 3, "weights_digest": digest, "mix": track, "segment_samples": 22050,
+                    "sources": ["vocals", "other"], "overlap": 0.25, "chunk_batch_size": 3, "decimate": 7,
+                    "out": y[..., ::7].clone(), **_summary(y)}, os.path.join(HERE, "bsroformer_apply.pt"))
+
+        cfg = bsroformer_config()
+        model, digest = build_roformer(unblend, cfg, 3)
+        mix = synth_track(1.0, 23)[None]
+        out = model(mix)
+        torch.save({"config": cfg, "seed": 3, "weights_digest": digest, "mix": mix, "decimate": 5,
+                    "out": out[..., ::5].clone(), **_summary(out)}, os.path.join(HERE, "bsroformer_full.pt"))
+
+
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) > 2 and sys.argv[2] == "roformer":
+        main_roformer(import_reference(sys.argv[1]))
+    else:
+        main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")

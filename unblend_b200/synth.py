@@ -237,6 +237,96 @@ def htdemucs_state_dict(cfg: dict, seed: int) -> "OrderedDict[str, torch.Tensor]
     return state
 
 
+# The standard 62-band split of the 1025 bins of a 2048-point STFT
+# (unblend/roformer.py:32-40): 24x2, 12x4, 8x12, 8x24, 8x48, 128, 129.
+DEFAULT_FREQS_PER_BANDS = (2,) * 24 + (4,) * 12 + (12,) * 8 + (24,) * 8 + (48,) * 8 + (128, 129)
+
+# BS-RoFormer of the configuration measured here: dim 512, depth 12, 8 heads
+# of 64, one time and one frequency transformer per depth, n_fft 2048, hop
+# 441, 62 bands, mask estimator depth 2, one stem, 8 s segments.
+BSROFORMER_CONFIG = dict(
+    dim=512,
+    depth=12,
+    stereo=True,
+    num_stems=1,
+    time_transformer_depth=1,
+    freq_transformer_depth=1,
+    freqs_per_bands=DEFAULT_FREQS_PER_BANDS,
+    dim_head=64,
+    heads=8,
+    stft_n_fft=2048,
+    stft_hop_length=441,
+    stft_win_length=2048,
+    stft_normalized=False,
+    zero_dc=True,
+    mask_estimator_depth=2,
+    mlp_expansion_factor=4,
+    skip_connection=False,
+)
+
+
+def bsroformer_config(**overrides) -> dict:
+    """Copy of the measured BS-RoFormer constructor config with ``overrides`` applied."""
+    cfg = dict(BSROFORMER_CONFIG)
+    cfg.update(overrides)
+    cfg["freqs_per_bands"] = tuple(cfg["freqs_per_bands"])
+    return cfg
+
+
+def bsroformer_state_dict(cfg: dict, seed: int) -> "OrderedDict[str, torch.Tensor]":
+    """Random-init BS-RoFormer weights identical to ``manual_seed(seed); BSRoformer(**cfg)``.
+
+    Follows the construction order of ``_RoformerBase._init_common`` and
+    ``BSRoformer.__init__`` (unblend/roformer.py:896-1066, 1207-1310): per depth
+    a time then a frequency ``Transformer`` of (gated ``Attention``,
+    ``FeedForward``) layers, then ``final_norm``, the per-band ``BandSplit``
+    projections and the per-stem, per-band ``MaskEstimator`` MLPs. RMSNorm gains
+    start at one and the frozen rotary frequencies are deterministic.
+
+    :param cfg: Config from :func:`bsroformer_config`.
+    :param seed: Seed given to ``torch.manual_seed``.
+    :return: State dict keyed like the reference module.
+    """
+    if cfg.get("skip_connection") or cfg.get("linear_transformer_depth", 0):
+        raise ValueError("skip connections and linear attention are not supported")
+    dim, heads, dh = cfg["dim"], cfg["heads"], cfg["dim_head"]
+    inner = heads * dh
+    channels = 2 if cfg["stereo"] else 1
+    state: "OrderedDict[str, torch.Tensor]" = OrderedDict()
+    freqs = 1.0 / (10000.0 ** (torch.arange(0, dh, 2)[: dh // 2].float() / dh))
+    rng_state = torch.random.get_rng_state()
+    torch.manual_seed(seed)
+    try:
+        for i in range(cfg["depth"]):
+            for axis, tdepth in ((0, cfg["time_transformer_depth"]), (1, cfg["freq_transformer_depth"])):
+                for j in range(tdepth):
+                    p = f"layers.{i}.{axis}.layers.{j}"
+                    state[f"{p}.0.norm.gamma"] = torch.ones(dim)
+                    _take(f"{p}.0.to_qkv", nn.Linear(dim, 3 * inner, bias=False), state)
+                    _take(f"{p}.0.to_gates", nn.Linear(dim, heads), state)
+                    _take(f"{p}.0.to_out.0", nn.Linear(inner, dim, bias=False), state)
+                    state[f"{p}.0.rotary_embed.freqs"] = freqs.clone()
+                    state[f"{p}.1.net.0.gamma"] = torch.ones(dim)
+                    # FeedForward width is 4 * dim (Transformer's ff_mult).
+                    _take(f"{p}.1.net.1", nn.Linear(dim, 4 * dim), state)
+                    _take(f"{p}.1.net.4", nn.Linear(4 * dim, dim), state)
+        state["final_norm.gamma"] = torch.ones(dim)
+        dims_in = [2 * f * channels for f in cfg["freqs_per_bands"]]
+        for b, d_in in enumerate(dims_in):
+            state[f"band_split.to_features.{b}.0.gamma"] = torch.ones(d_in)
+            _take(f"band_split.to_features.{b}.1", nn.Linear(d_in, dim), state)
+        hidden = dim * cfg["mlp_expansion_factor"]
+        for s in range(cfg["num_stems"]):
+            for b, d_in in enumerate(dims_in):
+                p = f"mask_estimators.{s}.to_freqs.{b}.0"
+                layer_dims = [dim] + [hidden] * (cfg["mask_estimator_depth"] - 1) + [2 * d_in]
+                for k, (a_in, a_out) in enumerate(zip(layer_dims[:-1], layer_dims[1:])):
+                    _take(f"{p}.{2 * k}", nn.Linear(a_in, a_out), state)
+    finally:
+        torch.random.set_rng_state(rng_state)
+    return state
+
+
 def synth_track(seconds: float, seed: int, samplerate: int = 44100) -> torch.Tensor:
     """Synthetic stereo mixture ``[2, round(seconds * samplerate)]`` in fp32.
 
