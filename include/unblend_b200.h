@@ -28,7 +28,8 @@ extern "C" {
 enum UnblendAct {
   UNBLEND_ACT_NONE = 0,
   UNBLEND_ACT_GELU = 1, /* exact erf GELU, F.gelu */
-  UNBLEND_ACT_GLU = 2   /* F.glu over interleaved (value, gate) column pairs */
+  UNBLEND_ACT_GLU = 2,  /* F.glu over interleaved (value, gate) column pairs */
+  UNBLEND_ACT_TANH = 3  /* torch.tanh (BS-RoFormer mask estimator hidden layers) */
 };
 
 /* Transform applied to each input element as it is loaded. */
@@ -179,6 +180,93 @@ int unblend_attention_tc(const float* q, const float* k, const float* v, float* 
  * (0 = none); cleared when `clear` is non-zero. Synchronous host call. */
 int unblend_attention_error_flag(int* out_host, int clear);
 
+/*
+ * Attention with a two-level batch and BS-RoFormer's fusions (gated rotary
+ * Attention, unblend/roformer.py:478-511; axial sequences of
+ * _run_transformers, unblend/roformer.py:1135-1159). Sequence (o, i) of Q has
+ * row r, head h, dim d at q + o*q_so + i*q_si + r*q_sr + h*hd + d (K and V
+ * share the kv_* strides; the output likewise with o_*). Optional:
+ *   rope  float[rope_len, hd/2, 2] (cos, sin) of position r * freq: Q and K
+ *         rows are rotated (interleaved pairs) before QK^T;
+ *   gate  float, the output row of head h is multiplied by
+ *         gate[o*g_so + i*g_si + r*g_sr + h];
+ *   out_bf16  write the output as bf16 instead of fp32.
+ * mode as in unblend_attention_tc; same alignment rules.
+ */
+typedef struct {
+  int outer, inner, heads, lq, lk, hd;
+  long long q_so, q_si, q_sr;
+  long long kv_so, kv_si, kv_sr;
+  void* out;
+  long long o_so, o_si, o_sr;
+  int out_bf16;
+  const float* gate;
+  long long g_so, g_si, g_sr;
+  const float* rope;
+  int rope_len;
+  float scale;
+} UnblendAttnParams;
+
+int unblend_attention_tc2(const float* q, const float* k, const float* v, const UnblendAttnParams* p, int mode,
+                          void* stream);
+
+/*
+ * Grouped linear layers on the tcgen05 tensor cores (nn.Linear of
+ * BS-RoFormer's Attention / FeedForward, unblend/roformer.py:274-308, 478-511,
+ * and the per-band linears of BandSplit / MaskEstimator, 673-800).
+ * A is [rows, a_cols] with leading dimension lda (elements); W is
+ * [w_rows, w_cols] row-major. Each group g computes, for every row r,
+ *   y[j] = act(sum_{k < K_g} A[r, a_col0 + k] * W[w_row0 + j, k] + bias[w_row0 + j]), j < n,
+ * where K_g is k rounded up to the K chunk (32 fp32 / 64 bf16 elements): the
+ * weights must be zero in columns k..K_g-1 (A columns past a_cols read as 0).
+ * With act = UNBLEND_ACT_GLU weight rows are interleaved (value, gate) pairs
+ * and y has n/2 columns. The result (plus res[r, c] when res is set; res may
+ * alias out) goes to out[r * ldo + out_col0 + c] as fp32 or bf16.
+ * mode 0: A and W fp32 (W as TF32 hi/lo split like unblend_conv2d_tc), 3-pass
+ * TF32; mode 1: A and W bf16. block_n: 64, 128 or 256.
+ * Alignment: A, W 16-byte aligned, lda, w_cols and every a_col0 multiples of
+ * 16 bytes' worth of elements.
+ */
+#define UNBLEND_GEMM_MAX_GROUPS 64
+typedef struct {
+  int a_col0, w_row0, n, k, out_col0;
+} UnblendGemmGroup;
+
+typedef struct {
+  int groups;
+  const UnblendGemmGroup* group; /* host array of `groups` entries */
+  const float* bias;             /* [w_rows] or NULL */
+  int act;                       /* UnblendAct */
+  const float* res;              /* fp32 residual or NULL */
+  long long ldr;
+  void* out;
+  long long ldo;
+  int out_bf16;
+} UnblendGemmParams;
+
+int unblend_gemm_tc(const void* a, long long lda, int rows, int a_cols, const void* w_hi, const void* w_lo,
+                    long long w_rows, int w_cols, const UnblendGemmParams* p, int mode, int block_n,
+                    void* stream);
+
+/* Device flag of the grouped GEMM's bounded waits (0 = none). Synchronous host call. */
+int unblend_gemm_error_flag(int* out_host, int clear);
+
+/* RMSNorm over the last dim (F.rms_norm, eps 1e-12; unblend/roformer.py:60-91) of
+ * contiguous fp32 rows [rows, dim] into y (fp32 or bf16, leading dim ldy); dim
+ * % 4 == 0, dim <= 1024. With gates > 0 (<= 16) also writes the attention gates
+ * gate_out[r, h] = sigmoid(y[r] . gate_w[h] + gate_b[h]) (unblend/roformer.py:478-511)
+ * computed from the fp32 normalised row; gate_w is [gates, dim]. */
+int unblend_rms_norm(const float* x, long long rows, int dim, const float* gamma, void* y, long long ldy,
+                     int y_bf16, const float* gate_w, const float* gate_b, int gates, float* gate_out,
+                     void* stream);
+
+/* Per-band RMSNorm of BandSplit (unblend/roformer.py:673-705): band b is columns
+ * [band_start[b], band_start[b+1]) of each fp32 row of x (leading dim ldx);
+ * band_start is a device int array of bands+1 multiples of 4; gamma holds the
+ * bands' weights back to back in column order. */
+int unblend_band_rms_norm(const float* x, long long rows, long long ldx, const int* band_start, int bands,
+                          const float* gamma, void* y, long long ldy, int y_bf16, void* stream);
+
 /* Elementwise y[i] = a[i] + alpha * b[i % b_period] (skip adds, embeddings). */
 int unblend_add(const float* a, const float* b, float* y, long long n, long long b_period,
                 float alpha, void* stream);
@@ -214,6 +302,28 @@ int unblend_time_input(const float* mix, float* xt, const float* stats2, int bat
 int unblend_istft_output(const float* spec, const float* xt, long long xt_sb, const float* fstats,
                          const float* tstats, const float* window, float* frames_buf, float* out,
                          int batch, int sources, int length, int nfft, void* stream);
+
+/*
+ * BS-RoFormer STFT (unblend/roformer.py:1320-1345): torch.stft with center=True
+ * (reflect padding of nfft/2), Hann window (periodic, length nfft), not
+ * normalised, any hop, of both channels of mix [batch, 2, length] into the
+ * frame-major feature layout out[batch, frames, nfft/2+1, 2 (channel), 2 (re, im)],
+ * frames = 1 + length / hop. nfft: 2048 or 4096; length > nfft/2.
+ */
+int unblend_stft_frames(const float* mix, float* out, const float* window, int batch, int length, int nfft,
+                        int hop, void* stream);
+
+/*
+ * BS-RoFormer output (unblend/roformer.py:1346-1379, 1176-1189): for each stem s,
+ * X = stft * mask_s as complex numbers (both [batch, frames, nfft/2+1, 2, 2];
+ * mask_s at mask + s*mask_ss), DC bin zeroed when zero_dc, then torch.istft
+ * (center, Hann, not normalised, window-square envelope) trimmed to `length`:
+ * out[batch, stems (+1), 2, length]. With `complement` (stems must be 1) a second
+ * stem mix - stem 0 is appended. frames_buf: batch*stems*2*frames*nfft floats.
+ */
+int unblend_istft_masked(const float* stft, const float* mask, long long mask_ss, const float* window,
+                         const float* mix, float* frames_buf, float* out, int batch, int stems, int complement,
+                         int length, int nfft, int hop, int zero_dc, void* stream);
 
 /* Per-batch (mean, std) with torch.var_mean semantics (unbiased) of a contiguous
  * [batch, n] array; out float[2*batch] = (mean, std). Uses `work` double[2*batch]. */

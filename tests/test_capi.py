@@ -48,21 +48,25 @@ def test_binding_covers_header():
 
 
 @pytest.mark.skipif(shutil.which("gcc") is None, reason="gcc not available")
-def test_conv_params_layout_matches_c(tmp_path):
-    fields = [f for f, _ in _lib.ConvParams._fields_]
+@pytest.mark.parametrize("ctype,cname", [(_lib.ConvParams, "UnblendConvParams"),
+                                         (_lib.AttnParams, "UnblendAttnParams"),
+                                         (_lib.GemmGroup, "UnblendGemmGroup"),
+                                         (_lib.GemmParams, "UnblendGemmParams")])
+def test_param_struct_layout_matches_c(tmp_path, ctype, cname):
+    fields = [f for f, _ in ctype._fields_]
     src = tmp_path / "layout.c"
-    body = "\n".join(f'  printf("{f} %zu\\n", offsetof(UnblendConvParams, {f}));' for f in fields)
+    body = "\n".join(f'  printf("{f} %zu\\n", offsetof({cname}, {f}));' for f in fields)
     src.write_text(
         '#include <stdio.h>\n#include <stddef.h>\n#include "unblend_b200.h"\n'
-        f'int main(void) {{\n  printf("size %zu\\n", sizeof(UnblendConvParams));\n{body}\n  return 0;\n}}\n'
+        f'int main(void) {{\n  printf("size %zu\\n", sizeof({cname}));\n{body}\n  return 0;\n}}\n'
     )
     exe = tmp_path / "layout"
     subprocess.run(["gcc", "-I", os.path.dirname(HEADER), str(src), "-o", str(exe)], check=True)
     out = dict(line.split() for line in subprocess.run([str(exe)], capture_output=True, text=True,
                                                         check=True).stdout.splitlines())
-    assert int(out["size"]) == ctypes.sizeof(_lib.ConvParams)
+    assert int(out["size"]) == ctypes.sizeof(ctype)
     for f in fields:
-        assert int(out[f]) == getattr(_lib.ConvParams, f).offset, f
+        assert int(out[f]) == getattr(ctype, f).offset, f
 
 
 def test_error_codes_raise():

@@ -1,0 +1,354 @@
+"""BS-RoFormer on the GPU: each new kernel against a plain PyTorch fp32
+reference of the same op, then the whole forward and the segment engine against
+the reference's own outputs (golden fixtures).
+
+Tolerances (north star): fp32 max-abs error <= 1e-4 x output RMS; bf16 at
+>= 40 dB SNR per stem.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from conftest import golden, rel_err
+from unblend_b200 import _lib
+from unblend_b200.apply import apply_model
+from unblend_b200.roformer import BSRoformerCuda, split_tf32
+from unblend_b200.synth import bsroformer_state_dict
+
+pytestmark = pytest.mark.gpu
+FP32_TOL = 1e-4
+BF16_MIN_SNR_DB = 40.0
+
+
+def snr_db(out: torch.Tensor, ref: torch.Tensor) -> list[float]:
+    o, r = out.double().cpu(), ref.double().cpu()
+    res = []
+    for s in range(r.shape[1]):
+        num = r[:, s].pow(2).sum()
+        den = (o[:, s] - r[:, s]).pow(2).sum()
+        res.append(float(10 * math.log10(num / den)) if den > 0 else float("inf"))
+    return res
+
+
+# ---------------------------------------------------------------- spectral
+
+
+@pytest.mark.parametrize("nfft,hop,length", [(2048, 441, 22050), (2048, 441, 5000), (4096, 1000, 9001)])
+def test_stft_frames_matches_torch(nfft, hop, length):
+    torch.manual_seed(0)
+    mix = torch.randn(3, 2, length, device="cuda")
+    win = torch.hann_window(nfft, device="cuda")
+    T = 1 + length // hop
+    out = torch.empty(3, T, nfft // 2 + 1, 2, 2, device="cuda")
+    _lib.call("unblend_stft_frames", mix.data_ptr(), out.data_ptr(), win.data_ptr(), 3, length, nfft, hop)
+    ref = torch.stft(mix.reshape(6, length).double(), n_fft=nfft, hop_length=hop, window=win.double(),
+                     return_complex=True)
+    ref = torch.view_as_real(ref).view(3, 2, nfft // 2 + 1, T, 2).permute(0, 3, 2, 1, 4)
+    assert rel_err(out, ref) < 2e-6
+
+
+@pytest.mark.parametrize("complement,zero_dc", [(0, 1), (1, 1), (0, 0)])
+def test_istft_masked_matches_torch(complement, zero_dc):
+    torch.manual_seed(1)
+    B, S, L, nfft, hop = 2, 1 if complement else 2, 20000, 2048, 441
+    T, Fb = 1 + L // hop, nfft // 2 + 1
+    mix = torch.randn(B, 2, L, device="cuda")
+    win = torch.hann_window(nfft, device="cuda")
+    stft = torch.randn(B, T, Fb, 2, 2, device="cuda")
+    mask = torch.randn(S, B, T, Fb, 2, 2, device="cuda")
+    out = torch.empty(B, S + complement, 2, L, device="cuda")
+    fbuf = torch.empty(B * S * 2 * T * nfft, device="cuda")
+    _lib.call("unblend_istft_masked", stft.data_ptr(), mask.data_ptr(), B * T * Fb * 4, win.data_ptr(),
+              mix.data_ptr(), fbuf.data_ptr(), out.data_ptr(), B, S, complement, L, nfft, hop, zero_dc)
+    z = torch.view_as_complex(stft.double().contiguous())[None] * torch.view_as_complex(mask.double().contiguous())
+    z = z.permute(1, 0, 4, 3, 2).reshape(B * S * 2, Fb, T)  # [B, S, C, F, T]
+    if zero_dc:
+        z = z.clone()
+        z[:, 0] = 0
+    ref = torch.istft(z, n_fft=nfft, hop_length=hop, window=win.double(), length=L).view(B, S, 2, L)
+    if complement:
+        ref = torch.cat([ref, mix.double()[:, None] - ref], dim=1)
+    assert rel_err(out, ref) < 5e-6
+
+
+# ---------------------------------------------------------------- norms
+
+
+@pytest.mark.parametrize("dim,gates,bf16", [(512, 8, 0), (512, 8, 1), (64, 4, 0), (512, 0, 1)])
+def test_rms_norm_and_gates(dim, gates, bf16):
+    torch.manual_seed(2)
+    rows = 1000
+    x = torch.randn(rows, dim, device="cuda") * 3
+    gamma = torch.rand(dim, device="cuda") + 0.5
+    gw = torch.randn(max(gates, 1), dim, device="cuda") * 0.05
+    gb = torch.randn(max(gates, 1), device="cuda")
+    y = torch.empty(rows, dim, device="cuda", dtype=torch.bfloat16 if bf16 else torch.float32)
+    g = torch.empty(rows, max(gates, 1), device="cuda")
+    _lib.call("unblend_rms_norm", x.data_ptr(), rows, dim, gamma.data_ptr(), y.data_ptr(), dim, bf16,
+              gw.data_ptr() if gates else None, gb.data_ptr() if gates else None, gates,
+              g.data_ptr() if gates else None)
+    ref = F.rms_norm(x, (dim,), gamma, eps=1e-12)
+    assert rel_err(y.float(), ref) < (1e-2 if bf16 else 2e-6)
+    if gates:
+        gref = torch.sigmoid(ref @ gw.t() + gb)
+        assert rel_err(g, gref) < 2e-5
+
+
+@pytest.mark.parametrize("bf16", [0, 1])
+def test_band_rms_norm(bf16):
+    torch.manual_seed(3)
+    widths = [8, 8, 16, 48, 516]
+    starts = [sum(widths[:i]) for i in range(len(widths) + 1)]
+    rows, feats = 300, starts[-1]
+    ld = feats if not bf16 else -(-feats // 8) * 8
+    x = torch.randn(rows, feats, device="cuda")
+    gamma = torch.rand(feats, device="cuda") + 0.5
+    st = torch.tensor(starts, dtype=torch.int32, device="cuda")
+    y = torch.zeros(rows, ld, device="cuda", dtype=torch.bfloat16 if bf16 else torch.float32)
+    _lib.call("unblend_band_rms_norm", x.data_ptr(), rows, feats, st.data_ptr(), len(widths), gamma.data_ptr(),
+              y.data_ptr(), ld, bf16)
+    ref = torch.cat([F.rms_norm(x[:, a:b], (b - a,), gamma[a:b], eps=1e-12) for a, b in zip(starts, starts[1:])], 1)
+    assert rel_err(y[:, :feats].float(), ref) < (1e-2 if bf16 else 2e-6)
+
+
+# ---------------------------------------------------------------- grouped GEMM
+
+
+def _gemm(a, w, groups, *, mode, block_n, bias=None, act=_lib.ACT_NONE, res=None, out, ldo, a_cols=None):
+    if mode == _lib.TC_TF32X3:
+        hi, lo = split_tf32(w)
+        a_in = a
+    else:
+        hi, lo = w.to(torch.bfloat16).contiguous(), None
+        a_in = a.to(torch.bfloat16).contiguous()
+    arr = (_lib.GemmGroup * len(groups))(*[_lib.GemmGroup(*g) for g in groups])
+    p = _lib.GemmParams()
+    p.groups = len(groups)
+    p.group = ctypes.cast(arr, ctypes.POINTER(_lib.GemmGroup))
+    p.bias = _lib.ptr(bias)
+    p.act = act
+    p.res = _lib.ptr(res)
+    p.ldr = ldo if res is not None else 0
+    p.out = out.data_ptr()
+    p.ldo = ldo
+    p.out_bf16 = 1 if out.dtype == torch.bfloat16 else 0
+    _lib.call("unblend_gemm_tc", a_in.data_ptr(), a_in.shape[1], a_in.shape[0], a_cols or a_in.shape[1],
+              hi.data_ptr(), _lib.ptr(lo), hi.shape[0], hi.shape[1], ctypes.byref(p), mode, block_n)
+
+
+def _gemm_ref(a, w, groups, bias=None, act=_lib.ACT_NONE, res=None, out_cols=None, bf16=False):
+    a = a.double()
+    w = w.double()
+    if bf16:
+        a = a.float().to(torch.bfloat16).double()
+        w = w.float().to(torch.bfloat16).double()
+    out = torch.zeros(a.shape[0], out_cols, dtype=torch.float64, device=a.device) if res is None else res.double()
+    out = out.clone()
+    for a0, r0, n, k, o0 in groups:
+        y = a[:, a0:a0 + k] @ w[r0:r0 + n, :k].t()
+        if bias is not None:
+            y = y + bias.double()[r0:r0 + n]
+        if act == _lib.ACT_GELU:
+            y = F.gelu(y)
+        elif act == _lib.ACT_TANH:
+            y = torch.tanh(y)
+        elif act == _lib.ACT_GLU:
+            y = y[:, 0::2] * torch.sigmoid(y[:, 1::2])
+        out[:, o0:o0 + y.shape[1]] += y
+    return out
+
+
+@pytest.mark.parametrize("mode,tol", [(_lib.TC_TF32X3, 6e-5), (_lib.TC_BF16, 2e-2)])
+@pytest.mark.parametrize("block_n", [64, 128, 256])
+@pytest.mark.parametrize("act", [_lib.ACT_NONE, _lib.ACT_GELU, _lib.ACT_TANH])
+def test_gemm_single_group(mode, tol, block_n, act):
+    torch.manual_seed(4)
+    m, k, n = 1000, 512, 768
+    a = torch.randn(m, k, device="cuda")
+    w = torch.randn(n, k, device="cuda") / math.sqrt(k)
+    b = torch.randn(n, device="cuda")
+    out = torch.empty(m, n, device="cuda")
+    _gemm(a, w, [(0, 0, n, k, 0)], mode=mode, block_n=block_n, bias=b, act=act, out=out, ldo=n)
+    ref = _gemm_ref(a, w, [(0, 0, n, k, 0)], bias=b, act=act, out_cols=n, bf16=mode == _lib.TC_BF16)
+    assert rel_err(out, ref) < tol
+    assert _lib.error_flag() == 0
+
+
+@pytest.mark.parametrize("mode,tol", [(_lib.TC_TF32X3, 6e-5), (_lib.TC_BF16, 2e-2)])
+def test_gemm_residual_in_place_and_bf16_out(mode, tol):
+    torch.manual_seed(5)
+    m, k, n = 777, 2048, 512
+    a = torch.randn(m, k, device="cuda")
+    w = torch.randn(n, k, device="cuda") / math.sqrt(k)
+    b = torch.randn(n, device="cuda")
+    x = torch.randn(m, n, device="cuda")
+    ref = _gemm_ref(a, w, [(0, 0, n, k, 0)], bias=b, res=x, bf16=mode == _lib.TC_BF16)
+    _gemm(a, w, [(0, 0, n, k, 0)], mode=mode, block_n=256, bias=b, res=x, out=x, ldo=n)
+    assert rel_err(x, ref) < tol
+    out16 = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    _gemm(a, w, [(0, 0, n, k, 0)], mode=mode, block_n=128, bias=b, act=_lib.ACT_GELU, out=out16, ldo=n)
+    ref16 = _gemm_ref(a, w, [(0, 0, n, k, 0)], bias=b, act=_lib.ACT_GELU, out_cols=n, bf16=mode == _lib.TC_BF16)
+    assert rel_err(out16.float(), ref16) < 1e-2
+
+
+@pytest.mark.parametrize("mode,tol", [(_lib.TC_TF32X3, 6e-5), (_lib.TC_BF16, 2e-2)])
+def test_gemm_grouped_bands_glu(mode, tol):
+    """Band-split style groups: ragged K slices of A, zero-padded weight blocks, GLU outputs at band offsets."""
+    torch.manual_seed(6)
+    widths = [8, 8, 16, 48, 96, 516]
+    starts = [sum(widths[:i]) for i in range(len(widths) + 1)]
+    m, feats, dim = 600, starts[-1], 128
+    kpad = -(-max(widths) // 64) * 64
+    a = torch.randn(m, feats, device="cuda")
+    ld = -(-feats // 8) * 8
+    a_pad = torch.zeros(m, ld, device="cuda")
+    a_pad[:, :feats] = a
+    # band split: groups (start_b, b*dim, dim, w_b, b*dim)
+    w = torch.zeros(len(widths) * dim, kpad, device="cuda")
+    groups = []
+    for b, wd in enumerate(widths):
+        w[b * dim:(b + 1) * dim, :wd] = torch.randn(dim, wd, device="cuda") / math.sqrt(wd)
+        groups.append((starts[b], b * dim, dim, wd, b * dim))
+    bias = torch.randn(len(widths) * dim, device="cuda")
+    out = torch.empty(m, len(widths) * dim, device="cuda")
+    _gemm(a_pad, w, groups, mode=mode, block_n=256, bias=bias, out=out, ldo=len(widths) * dim, a_cols=feats)
+    # Reference reads only each band's own columns.
+    ref = _gemm_ref(a_pad, w, groups, bias=bias, out_cols=len(widths) * dim, bf16=mode == _lib.TC_BF16)
+    assert rel_err(out, ref) < tol
+    # mask output: groups (b*dim, row, 2*w_b, dim, start_b) with GLU
+    hid = out
+    w2, groups2, row = [], [], 0
+    for b, wd in enumerate(widths):
+        w2.append(torch.randn(2 * wd, dim, device="cuda") / math.sqrt(dim))
+        groups2.append((b * dim, row, 2 * wd, dim, starts[b]))
+        row += 2 * wd
+    w2 = torch.cat(w2)
+    b2 = torch.randn(row, device="cuda")
+    mask = torch.empty(m, feats, device="cuda")
+    _gemm(hid, w2, groups2, mode=mode, block_n=64, bias=b2, act=_lib.ACT_GLU, out=mask, ldo=feats)
+    ref2 = _gemm_ref(hid, w2, groups2, bias=b2, act=_lib.ACT_GLU, out_cols=feats, bf16=mode == _lib.TC_BF16)
+    assert rel_err(mask, ref2) < tol
+    assert _lib.error_flag() == 0
+
+
+# ---------------------------------------------------------------- attention
+
+
+def _rope(seq, hd):
+    freqs = 1.0 / (10000.0 ** (torch.arange(0, hd, 2)[: hd // 2].float() / hd))
+    ang = torch.arange(seq, dtype=torch.float32)[:, None] * freqs
+    return ang.cos(), ang.sin()
+
+
+def _rotate(t, cos, sin):
+    x1, x2 = t.unflatten(-1, (-1, 2)).unbind(dim=-1)
+    return torch.stack((x1 * cos - x2 * sin, x1 * sin + x2 * cos), dim=-1).flatten(-2)
+
+
+@pytest.mark.parametrize("axis", [0, 1])
+@pytest.mark.parametrize("mode,tol", [(0, 2e-5), (1, 1e-2)])
+def test_attention_axial_rope_gate(axis, mode, tol):
+    """Axial gated rotary attention over a [B, T, bands, 3*inner] qkv buffer."""
+    torch.manual_seed(7)
+    B, T, nb, H, hd = 2, 300, 13, 4, 64
+    inner = H * hd
+    qkv = torch.randn(B, T, nb, 3 * inner, device="cuda")
+    gates = torch.rand(B, T, nb, H, device="cuda")
+    seq = T if axis == 0 else nb
+    cos, sin = _rope(seq, hd)
+    rope = torch.stack([cos, sin], -1).contiguous().cuda()
+    o = torch.empty(B, T, nb, inner, device="cuda")
+    a = _lib.AttnParams()
+    a.heads, a.hd = H, hd
+    q3 = 3 * inner
+    if axis == 0:
+        a.outer, a.inner, a.lq, a.lk = B, nb, T, T
+        a.q_so, a.q_si, a.q_sr = T * nb * q3, q3, nb * q3
+        a.o_so, a.o_si, a.o_sr = T * nb * inner, inner, nb * inner
+        a.g_so, a.g_si, a.g_sr = T * nb * H, H, nb * H
+    else:
+        a.outer, a.inner, a.lq, a.lk = B * T, 1, nb, nb
+        a.q_so, a.q_si, a.q_sr = nb * q3, 4, q3
+        a.o_so, a.o_si, a.o_sr = nb * inner, 0, inner
+        a.g_so, a.g_si, a.g_sr = nb * H, 0, H
+    a.kv_so, a.kv_si, a.kv_sr = a.q_so, a.q_si, a.q_sr
+    a.out, a.out_bf16, a.gate, a.rope, a.rope_len, a.scale = o.data_ptr(), 0, gates.data_ptr(), rope.data_ptr(), seq, hd ** -0.5
+    base = qkv.data_ptr()
+    _lib.call("unblend_attention_tc2", base, base + 4 * inner, base + 8 * inner, ctypes.byref(a), mode)
+    # reference
+    x = qkv.double()
+    if axis == 0:
+        x = x.permute(0, 2, 1, 3)  # [B, nb, T, 3I]
+        g = gates.double().permute(0, 2, 1, 3)
+    else:
+        g = gates.double()
+    q, k, v = x.unflatten(-1, (3, H, hd)).unbind(-3)  # [..., seq, H, hd]
+    q, k, v = (t.transpose(-2, -3) for t in (q, k, v))  # [..., H, seq, hd]
+    q, k = _rotate(q, cos.double().cuda(), sin.double().cuda()), _rotate(k, cos.double().cuda(), sin.double().cuda())
+    att = torch.softmax(q @ k.transpose(-1, -2) * hd ** -0.5, -1) @ v  # [..., H, seq, hd]
+    att = att * g.transpose(-1, -2).unsqueeze(-1)
+    ref = att.transpose(-2, -3).flatten(-2)  # [..., seq, inner]
+    if axis == 0:
+        ref = ref.permute(0, 2, 1, 3)
+    assert rel_err(o, ref) < tol
+    assert _lib.error_flag() == 0
+
+
+# ---------------------------------------------------------------- whole model
+
+
+def _model(g, precision):
+    return BSRoformerCuda(g["config"], bsroformer_state_dict(g["config"], g["seed"]), precision=precision).cuda()
+
+
+def test_small_forward_fp32_matches_reference():
+    g = golden("bsroformer_small.pt")
+    out = _model(g, "fp32")(g["mix"].cuda())
+    assert out.shape == g["out"].shape
+    assert rel_err(out, g["out"]) < FP32_TOL
+    assert _lib.error_flag() == 0
+
+
+def test_small_forward_bf16_snr():
+    g = golden("bsroformer_small.pt")
+    out = _model(g, "bf16")(g["mix"].cuda())
+    assert min(snr_db(out, g["out"])) >= BF16_MIN_SNR_DB
+
+
+@pytest.mark.parametrize("precision", ["fp32", "bf16"])
+def test_full_config_matches_reference(precision):
+    g = golden("bsroformer_full.pt")
+    out = _model(g, precision)(g["mix"].cuda()).cpu()
+    d = g["decimate"]
+    if precision == "fp32":
+        assert rel_err(out[..., ::d], g["out"]) < FP32_TOL
+        assert torch.allclose(out.double().pow(2).sum(dim=(0, 2, 3)), g["sumsq"], rtol=1e-4)
+    else:
+        assert min(snr_db(out[..., ::d], g["out"])) >= BF16_MIN_SNR_DB
+    assert _lib.error_flag() == 0
+
+
+def test_apply_model_with_complement_matches_reference():
+    g = golden("bsroformer_apply.pt")
+    m = _model(g, "fp32")
+    m.configure_inference(sources=g["sources"], samplerate=44100, segment_samples=g["segment_samples"])
+    out = apply_model(m, g["mix"], device="cuda", shifts=0, overlap=g["overlap"],
+                      chunk_batch_size=g["chunk_batch_size"])
+    assert out.shape[1] == 2
+    assert rel_err(out[..., :: g["decimate"]], g["out"]) < FP32_TOL
+    assert torch.allclose(out.double().sum(dim=(0, 2, 3)), g["sum"], rtol=1e-4, atol=1e-3)
+
+
+def test_batch_rows_are_independent():
+    g = golden("bsroformer_small.pt")
+    m = _model(g, "fp32")
+    mix = g["mix"].cuda()
+    both = m(mix)
+    one = m(mix[1:2])
+    assert rel_err(both[1:2], one) < 1e-5

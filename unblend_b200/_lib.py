@@ -26,8 +26,9 @@ c_float = ctypes.c_float
 c_double = ctypes.c_double
 c_void_p = ctypes.c_void_p
 
-ACT_NONE, ACT_GELU, ACT_GLU = 0, 1, 2
+ACT_NONE, ACT_GELU, ACT_GLU, ACT_TANH = 0, 1, 2, 3
 PRO_NONE, PRO_GN_GELU, PRO_ADD = 0, 1, 2
+GEMM_MAX_GROUPS = 64
 
 
 class ConvParams(ctypes.Structure):
@@ -45,6 +46,35 @@ class ConvParams(ctypes.Structure):
         ("pro_group_per_h", c_int), ("pro_x2", c_void_p),
         ("res", c_void_p), ("res_scale", c_void_p),
         ("stats", c_void_p), ("stats_per_h", c_int),
+    ]
+
+
+class AttnParams(ctypes.Structure):
+    """Mirror of ``UnblendAttnParams``."""
+
+    _fields_ = [
+        ("outer", c_int), ("inner", c_int), ("heads", c_int), ("lq", c_int), ("lk", c_int), ("hd", c_int),
+        ("q_so", c_ll), ("q_si", c_ll), ("q_sr", c_ll),
+        ("kv_so", c_ll), ("kv_si", c_ll), ("kv_sr", c_ll),
+        ("out", c_void_p), ("o_so", c_ll), ("o_si", c_ll), ("o_sr", c_ll), ("out_bf16", c_int),
+        ("gate", c_void_p), ("g_so", c_ll), ("g_si", c_ll), ("g_sr", c_ll),
+        ("rope", c_void_p), ("rope_len", c_int),
+        ("scale", c_float),
+    ]
+
+
+class GemmGroup(ctypes.Structure):
+    """Mirror of ``UnblendGemmGroup``."""
+
+    _fields_ = [("a_col0", c_int), ("w_row0", c_int), ("n", c_int), ("k", c_int), ("out_col0", c_int)]
+
+
+class GemmParams(ctypes.Structure):
+    """Mirror of ``UnblendGemmParams``."""
+
+    _fields_ = [
+        ("groups", c_int), ("group", ctypes.POINTER(GemmGroup)), ("bias", c_void_p), ("act", c_int),
+        ("res", c_void_p), ("ldr", c_ll), ("out", c_void_p), ("ldo", c_ll), ("out_bf16", c_int),
     ]
 
 
@@ -84,12 +114,22 @@ _SIGNATURES = {
                               c_void_p, c_void_p, c_void_p],
     "unblend_dconv_apply": [c_void_p, c_ll, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p,
                             c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p],
+    "unblend_attention_tc2": [c_void_p, c_void_p, c_void_p, ctypes.POINTER(AttnParams), c_int, c_void_p],
+    "unblend_gemm_tc": [c_void_p, c_ll, c_int, c_int, c_void_p, c_void_p, c_ll, c_int, ctypes.POINTER(GemmParams),
+                        c_int, c_int, c_void_p],
+    "unblend_rms_norm": [c_void_p, c_ll, c_int, c_void_p, c_void_p, c_ll, c_int, c_void_p, c_void_p, c_int,
+                         c_void_p, c_void_p],
+    "unblend_band_rms_norm": [c_void_p, c_ll, c_ll, c_void_p, c_int, c_void_p, c_void_p, c_ll, c_int, c_void_p],
+    "unblend_stft_frames": [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p],
+    "unblend_istft_masked": [c_void_p, c_void_p, c_ll, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
+                             c_int, c_int, c_int, c_int, c_void_p],
 }
 
 # Entry points without a stream argument.
 _HOST_SIGNATURES = {
     "unblend_error_flag": [ctypes.POINTER(c_int), c_int],
     "unblend_attention_error_flag": [ctypes.POINTER(c_int), c_int],
+    "unblend_gemm_error_flag": [ctypes.POINTER(c_int), c_int],
 }
 
 TC_TF32X3, TC_BF16 = 0, 1
@@ -123,7 +163,7 @@ def exported_symbols() -> list[str]:
 def error_flag(clear: bool = True) -> int:
     """Read (and by default clear) the device flag that bounded waits set on timeout."""
     total = 0
-    for name in ("unblend_error_flag", "unblend_attention_error_flag"):
+    for name in ("unblend_error_flag", "unblend_attention_error_flag", "unblend_gemm_error_flag"):
         v = c_int(0)
         check(name, getattr(load(), name)(ctypes.byref(v), 1 if clear else 0))
         total |= v.value
@@ -155,7 +195,7 @@ def check(name: str, rc: int) -> None:
 
 
 # Kernels launched by one call of each entry point (1 unless listed).
-KERNELS_PER_CALL = {"unblend_mean_std": 3, "unblend_istft_output": 2}
+KERNELS_PER_CALL = {"unblend_mean_std": 3, "unblend_istft_output": 2, "unblend_istft_masked": 2}
 
 # Launch accounting: total kernels launched through this binding.
 counters = {"launches": 0}

@@ -16,6 +16,17 @@
 // MODE 0 (fp32 accuracy): every product is hi*hi + hi*lo + lo*hi in
 // kind::tf32 (3 MMAs). MODE 1: single-pass TF32 with round-to-nearest
 // operands (used by the bf16 precision setting).
+//
+// Sequences are indexed by a two-level batch (outer, inner) with independent
+// strides, so BS-RoFormer's axial attention reads its [batch, frames, bands,
+// dim] tokens in place: along frames with (outer, inner) = (batch, band) and
+// along bands with (batch * frame, 1) (unblend/roformer.py:1135-1159).
+// Optional fusions for BS-RoFormer's gated rotary attention
+// (unblend/roformer.py:478-511): the rotary rotation of Q and K at their
+// sequence positions (interleaved pairs, unblend/roformer.py:251-271) is
+// applied by the operand-preparation warps before rounding, and the output is
+// multiplied by a per-(token, head) gate.
+#include <cuda_bf16.h>
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
@@ -54,9 +65,14 @@ struct AL {
 
 struct AttnArgs {
   int heads, lq, lk, hd;
-  int q_tiles;
-  float* o;
-  long long o_sb, o_sr;
+  int q_tiles, inner;
+  void* o;
+  long long o_so, o_si, o_sr;
+  int o_bf16;
+  const float* gate;
+  long long g_so, g_si, g_sr;
+  const float2* rope;  // [rope_len, hd/2] (cos, sin) or null
+  int rope_len;
   float c;  // scale * log2(e)
 };
 
@@ -93,12 +109,29 @@ __device__ __forceinline__ float tf32_round(float v) {
 __device__ __forceinline__ int sw128(int r, int c) { return r * 128 + ((((c >> 2) ^ (r & 7))) << 4) + (c & 3) * 4; }
 
 // Round `n4` float4s at p to TF32 in place; with MODE 0 also write the residuals at lo.
+// The tile is 2 boxes of [box_rows x 32 dims] (128-byte swizzled rows) whose
+// row r holds sequence position pos0 + r; with `rope`, each (even, odd) dim
+// pair is first rotated by the (cos, sin) of that position.
 template <int MODE>
-__device__ __forceinline__ void split_tile(uint8_t* p, uint8_t* lo, int n4, int t, int nt) {
+__device__ __forceinline__ void split_tile(uint8_t* p, uint8_t* lo, int n4, int t, int nt, int box_rows, int pos0,
+                                           const float2* __restrict__ rope, int rope_len, int hd) {
   float4* h = reinterpret_cast<float4*>(p);
   float4* l = reinterpret_cast<float4*>(lo);
   for (int i = t; i < n4; i += nt) {
-    const float4 v = h[i];
+    float4 v = h[i];
+    if (rope) {
+      const int box = i / (box_rows * 8), within = i - box * (box_rows * 8);
+      const int row = within >> 3;
+      const int d0 = box * 32 + (((within & 7) ^ (row & 7)) << 2);
+      if (d0 < hd) {
+        int pos = pos0 + row;
+        pos = pos < rope_len ? pos : rope_len - 1;
+        const float2 cs0 = __ldg(rope + (long long)pos * (hd >> 1) + (d0 >> 1));
+        const float2 cs1 = __ldg(rope + (long long)pos * (hd >> 1) + (d0 >> 1) + 1);
+        v = make_float4(v.x * cs0.x - v.y * cs0.y, v.x * cs0.y + v.y * cs0.x, v.z * cs1.x - v.w * cs1.y,
+                        v.z * cs1.y + v.w * cs1.x);
+      }
+    }
     float4 vh;
     vh.x = tf32_round(v.x);
     vh.y = tf32_round(v.y);
@@ -158,7 +191,8 @@ __global__ void __launch_bounds__(NT, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = blockIdx.x % a.q_tiles;
   const int h = (blockIdx.x / a.q_tiles) % a.heads;
-  const int b = blockIdx.x / (a.q_tiles * a.heads);
+  const int z = blockIdx.x / (a.q_tiles * a.heads);
+  const int bi = z % a.inner, bo = z / a.inner;
   const int q0 = qt * BQ;
   const int nkv = (a.lk + BK - 1) / BK;
 
@@ -186,17 +220,17 @@ __global__ void __launch_bounds__(NT, 1)
   if (warp == 0) {
     if (lane == 0) {
       mbar_expect_tx(q_full, L::Q_BYTES);
-      tma_load_4d(sQ, &mapQ, q_full, 0, h, q0, b);
-      tma_load_4d(sQ + BQ * 128, &mapQ, q_full, 32, h, q0, b);
+      tma_load_5d(sQ, &mapQ, q_full, 0, h, q0, bi, bo);
+      tma_load_5d(sQ + BQ * 128, &mapQ, q_full, 32, h, q0, bi, bo);
       for (int j = 0; j < nkv; ++j) {
         const int s = j % L::STAGES, r = j / L::STAGES;
         if (r > 0 && !mbar_wait(&kv_free[s], (r - 1) & 1)) break;
         uint8_t* st = sKV + s * L::STAGE;
         mbar_expect_tx(&kv_full[s], 2 * L::KV_BYTES);
-        tma_load_4d(st + L::K_OFF, &mapK, &kv_full[s], 0, h, j * BK, b);
-        tma_load_4d(st + L::K_OFF + BK * 128, &mapK, &kv_full[s], 32, h, j * BK, b);
-        tma_load_4d(st + L::V_OFF, &mapV, &kv_full[s], 0, h, j * BK, b);
-        tma_load_4d(st + L::V_OFF + BK * 128, &mapV, &kv_full[s], 32, h, j * BK, b);
+        tma_load_5d(st + L::K_OFF, &mapK, &kv_full[s], 0, h, j * BK, bi, bo);
+        tma_load_5d(st + L::K_OFF + BK * 128, &mapK, &kv_full[s], 32, h, j * BK, bi, bo);
+        tma_load_5d(st + L::V_OFF, &mapV, &kv_full[s], 0, h, j * BK, bi, bo);
+        tma_load_5d(st + L::V_OFF + BK * 128, &mapV, &kv_full[s], 32, h, j * BK, bi, bo);
       }
     }
   } else if (warp == 1) {
@@ -265,7 +299,7 @@ __global__ void __launch_bounds__(NT, 1)
     const int ct = threadIdx.x - 192;
     bool ok = mbar_wait(q_full, 0);
     if (ok) {
-      split_tile<MODE>(sQ, sQlo, L::Q_BYTES / 16, ct, 128);
+      split_tile<MODE>(sQ, sQlo, L::Q_BYTES / 16, ct, 128, BQ, q0, a.rope, a.rope_len, a.hd);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(q_ready);
@@ -274,7 +308,8 @@ __global__ void __launch_bounds__(NT, 1)
       const int s = j % L::STAGES, r = j / L::STAGES;
       if (!mbar_wait(&kv_full[s], r & 1)) break;
       uint8_t* st = sKV + s * L::STAGE;
-      split_tile<MODE>(st + L::K_OFF, st + L::KLO_OFF, L::KV_BYTES / 16, ct, 128);
+      split_tile<MODE>(st + L::K_OFF, st + L::KLO_OFF, L::KV_BYTES / 16, ct, 128, BK, j * BK, a.rope, a.rope_len,
+                       a.hd);
       transpose_v<MODE>(st + L::V_OFF, st + L::VT_OFF, st + (MODE == 0 ? L::VTLO_OFF : L::VT_OFF), ct);
       fence_proxy_async_smem();
       __syncwarp();
@@ -374,8 +409,11 @@ __global__ void __launch_bounds__(NT, 1)
       tmem_ld32(lane_base + L::OACC_COL + 32, o1);
       const int qrow = q0 + row;
       if (qrow < a.lq) {
-        const float inv = 1.f / l;
-        float* out = a.o + (long long)b * a.o_sb + (long long)qrow * a.o_sr + (long long)h * a.hd;
+        float inv = 1.f / l;
+        if (a.gate)
+          inv *= __ldg(a.gate + (long long)bo * a.g_so + (long long)bi * a.g_si + (long long)qrow * a.g_sr + h);
+        const long long off =
+            (long long)bo * a.o_so + (long long)bi * a.o_si + (long long)qrow * a.o_sr + (long long)h * a.hd;
 #pragma unroll
         for (int d = 0; d < 64; d += 4) {
           if (d < a.hd) {
@@ -386,7 +424,17 @@ __global__ void __launch_bounds__(NT, 1)
             else
               v = make_float4(__uint_as_float(o1[d - 32]), __uint_as_float(o1[d - 31]),
                               __uint_as_float(o1[d - 30]), __uint_as_float(o1[d - 29]));
-            *reinterpret_cast<float4*>(out + d) = make_float4(v.x * inv, v.y * inv, v.z * inv, v.w * inv);
+            v = make_float4(v.x * inv, v.y * inv, v.z * inv, v.w * inv);
+            if (a.o_bf16) {
+              __nv_bfloat162 p0 = __floats2bfloat162_rn(v.x, v.y);
+              __nv_bfloat162 p1 = __floats2bfloat162_rn(v.z, v.w);
+              uint2 packed;
+              packed.x = *reinterpret_cast<uint32_t*>(&p0);
+              packed.y = *reinterpret_cast<uint32_t*>(&p1);
+              *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(a.o) + off + d) = packed;
+            } else {
+              *reinterpret_cast<float4*>(reinterpret_cast<float*>(a.o) + off + d) = v;
+            }
           }
         }
       }
@@ -412,18 +460,75 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// 4-D map (head dim, head, row, batch) of one of Q/K/V with boxes of 32 dims x box_rows rows.
-bool head_map(CUtensorMap* m, const float* base, int hd, int heads, int rows, int batch, long long row_stride,
-              long long batch_stride, int box_rows) {
+// 5-D map (head dim, head, row, inner batch, outer batch) of one of Q/K/V
+// with boxes of 32 dims x box_rows rows.
+bool head_map(CUtensorMap* m, const float* base, int hd, int heads, int rows, int inner, int outer,
+              long long row_stride, long long inner_stride, long long outer_stride, int box_rows) {
   auto fn = encode_fn();
   if (!fn) return false;
-  cuuint64_t dims[4] = {(cuuint64_t)hd, (cuuint64_t)heads, (cuuint64_t)rows, (cuuint64_t)batch};
-  cuuint64_t strides[3] = {(cuuint64_t)hd * 4, (cuuint64_t)row_stride * 4, (cuuint64_t)batch_stride * 4};
-  cuuint32_t box[4] = {32, 1, (cuuint32_t)box_rows, 1};
-  cuuint32_t es[4] = {1, 1, 1, 1};
-  return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(base), dims, strides, box, es,
+  cuuint64_t dims[5] = {(cuuint64_t)hd, (cuuint64_t)heads, (cuuint64_t)rows, (cuuint64_t)inner, (cuuint64_t)outer};
+  cuuint64_t strides[4] = {(cuuint64_t)hd * 4, (cuuint64_t)row_stride * 4, (cuuint64_t)inner_stride * 4,
+                           (cuuint64_t)outer_stride * 4};
+  cuuint32_t box[5] = {32, 1, (cuuint32_t)box_rows, 1, 1};
+  cuuint32_t es[5] = {1, 1, 1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5, const_cast<float*>(base), dims, strides, box, es,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// A stride of a dimension of extent 1 is never used; give it a legal value.
+long long legal_stride(long long s, int extent) { return extent == 1 && s <= 0 ? 4 : s; }
+
+int attention_launch(const float* q, const float* k, const float* v, const UnblendAttnParams* p, int mode,
+                     void* stream) {
+  UB_REQUIRE(q && k && v && p && p->out && (mode == 0 || mode == 1));
+  UB_REQUIRE(p->outer > 0 && p->inner > 0 && p->heads > 0 && p->lq > 0 && p->lk > 0);
+  UB_REQUIRE(p->hd > 0 && p->hd <= 64 && p->hd % 4 == 0);
+  const long long q_so = legal_stride(p->q_so, p->outer), q_si = legal_stride(p->q_si, p->inner);
+  const long long kv_so = legal_stride(p->kv_so, p->outer), kv_si = legal_stride(p->kv_si, p->inner);
+  UB_REQUIRE(p->q_sr > 0 && p->kv_sr > 0 && q_so > 0 && q_si > 0 && kv_so > 0 && kv_si > 0);
+  UB_REQUIRE(p->q_sr % 4 == 0 && q_so % 4 == 0 && q_si % 4 == 0 && p->kv_sr % 4 == 0 && kv_so % 4 == 0 &&
+             kv_si % 4 == 0);
+  UB_REQUIRE(p->o_sr % 4 == 0 && p->o_so % 4 == 0 && p->o_si % 4 == 0);
+  UB_REQUIRE((reinterpret_cast<uintptr_t>(q) & 15) == 0 && (reinterpret_cast<uintptr_t>(k) & 15) == 0 &&
+             (reinterpret_cast<uintptr_t>(v) & 15) == 0 && (reinterpret_cast<uintptr_t>(p->out) & 15) == 0);
+  UB_REQUIRE(!p->rope || (p->rope_len > 0 && (reinterpret_cast<uintptr_t>(p->rope) & 7) == 0));
+  CUtensorMap mq, mk, mv;
+  if (!head_map(&mq, q, p->hd, p->heads, p->lq, p->inner, p->outer, p->q_sr, q_si, q_so, BQ) ||
+      !head_map(&mk, k, p->hd, p->heads, p->lk, p->inner, p->outer, p->kv_sr, kv_si, kv_so, BK) ||
+      !head_map(&mv, v, p->hd, p->heads, p->lk, p->inner, p->outer, p->kv_sr, kv_si, kv_so, BK))
+    return UNBLEND_ERR_INVALID;
+  AttnArgs a{};
+  a.heads = p->heads;
+  a.lq = p->lq;
+  a.lk = p->lk;
+  a.hd = p->hd;
+  a.q_tiles = (p->lq + BQ - 1) / BQ;
+  a.inner = p->inner;
+  a.o = p->out;
+  a.o_so = p->o_so;
+  a.o_si = p->o_si;
+  a.o_sr = p->o_sr;
+  a.o_bf16 = p->out_bf16 ? 1 : 0;
+  a.gate = p->gate;
+  a.g_so = p->g_so;
+  a.g_si = p->g_si;
+  a.g_sr = p->g_sr;
+  a.rope = reinterpret_cast<const float2*>(p->rope);
+  a.rope_len = p->rope_len;
+  a.c = p->scale * 1.4426950408889634f;
+  const long long grid = (long long)p->outer * p->inner * p->heads * a.q_tiles;
+  UB_REQUIRE(grid < (1LL << 31));
+  cudaStream_t st = ub::as_stream(stream);
+  if (mode == 0) {
+    cudaFuncSetAttribute(attention_tc_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, AL<0>::SMEM);
+    attention_tc_kernel<0><<<(unsigned)grid, NT, AL<0>::SMEM, st>>>(mq, mk, mv, a);
+  } else {
+    cudaFuncSetAttribute(attention_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, AL<1>::SMEM);
+    attention_tc_kernel<1><<<(unsigned)grid, NT, AL<1>::SMEM, st>>>(mq, mk, mv, a);
+  }
+  UB_CHECK_LAUNCH();
+  return 0;
 }
 
 }  // namespace
@@ -445,36 +550,28 @@ extern "C" int unblend_attention_tc(const float* q, const float* k, const float*
                                     int lq, int lk, int hd, long long q_sb, long long q_sr, long long kv_sb,
                                     long long kv_sr, long long o_sb, long long o_sr, float scale, int mode,
                                     void* stream) {
-  UB_REQUIRE(q && k && v && out && batch > 0 && heads > 0 && lq > 0 && lk > 0 && (mode == 0 || mode == 1));
-  UB_REQUIRE(hd > 0 && hd <= 64 && hd % 4 == 0);
-  UB_REQUIRE(q_sr % 4 == 0 && q_sb % 4 == 0 && kv_sr % 4 == 0 && kv_sb % 4 == 0 && o_sr % 4 == 0 && o_sb % 4 == 0);
-  UB_REQUIRE((reinterpret_cast<uintptr_t>(q) & 15) == 0 && (reinterpret_cast<uintptr_t>(k) & 15) == 0 &&
-             (reinterpret_cast<uintptr_t>(v) & 15) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0);
-  CUtensorMap mq, mk, mv;
-  if (!head_map(&mq, q, hd, heads, lq, batch, q_sr, q_sb, BQ) ||
-      !head_map(&mk, k, hd, heads, lk, batch, kv_sr, kv_sb, BK) ||
-      !head_map(&mv, v, hd, heads, lk, batch, kv_sr, kv_sb, BK))
-    return UNBLEND_ERR_INVALID;
-  AttnArgs a{};
-  a.heads = heads;
-  a.lq = lq;
-  a.lk = lk;
-  a.hd = hd;
-  a.q_tiles = (lq + BQ - 1) / BQ;
-  a.o = out;
-  a.o_sb = o_sb;
-  a.o_sr = o_sr;
-  a.c = scale * 1.4426950408889634f;
-  const long long grid = (long long)batch * heads * a.q_tiles;
-  UB_REQUIRE(grid < (1LL << 31));
-  cudaStream_t st = ub::as_stream(stream);
-  if (mode == 0) {
-    cudaFuncSetAttribute(attention_tc_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, AL<0>::SMEM);
-    attention_tc_kernel<0><<<(unsigned)grid, NT, AL<0>::SMEM, st>>>(mq, mk, mv, a);
-  } else {
-    cudaFuncSetAttribute(attention_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, AL<1>::SMEM);
-    attention_tc_kernel<1><<<(unsigned)grid, NT, AL<1>::SMEM, st>>>(mq, mk, mv, a);
-  }
-  UB_CHECK_LAUNCH();
-  return 0;
+  UnblendAttnParams p{};
+  p.outer = batch;
+  p.inner = 1;
+  p.heads = heads;
+  p.lq = lq;
+  p.lk = lk;
+  p.hd = hd;
+  p.q_so = q_sb;
+  p.q_si = 4;
+  p.q_sr = q_sr;
+  p.kv_so = kv_sb;
+  p.kv_si = 4;
+  p.kv_sr = kv_sr;
+  p.out = out;
+  p.o_so = o_sb;
+  p.o_si = 0;
+  p.o_sr = o_sr;
+  p.scale = scale;
+  return attention_launch(q, k, v, &p, mode, stream);
+}
+
+extern "C" int unblend_attention_tc2(const float* q, const float* k, const float* v, const UnblendAttnParams* p,
+                                     int mode, void* stream) {
+  return attention_launch(q, k, v, p, mode, stream);
 }

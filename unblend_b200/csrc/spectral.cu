@@ -226,6 +226,212 @@ extern "C" int unblend_stft_cac(const float* mix, float* spec, const float* wind
   return 0;
 }
 
+// ---------------------------------------------------------------------------
+// BS-RoFormer STFT / iSTFT (unblend/roformer.py:1312-1379): torch.stft and
+// torch.istft with center=True (reflect pad n/2), not normalized, Hann window
+// of length n, any hop; n = 2048 or 4096.
+namespace {
+
+// Complex FFT of n = 2^k points (n <= 4096) in shared memory: radix-4
+// Stockham stages, then one radix-2 stage when k is odd. tw = exp(-2 pi i m / 4096).
+__device__ float2* fft_pow2(float2* x, float2* y, const float2* __restrict__ tw, int n) {
+  int ns = 1;
+  for (; ns * 4 <= n; ns *= 4) {
+    const int tws = 4096 / (4 * ns);
+    for (int j = threadIdx.x; j < n / 4; j += blockDim.x) {
+      const int k = j % ns;
+      float2 a0 = x[j];
+      float2 a1 = x[j + n / 4];
+      float2 a2 = x[j + n / 2];
+      float2 a3 = x[j + 3 * n / 4];
+      if (ns > 1) {
+        a1 = cmul(a1, __ldg(tw + ((1 * k * tws) & 4095)));
+        a2 = cmul(a2, __ldg(tw + ((2 * k * tws) & 4095)));
+        a3 = cmul(a3, __ldg(tw + ((3 * k * tws) & 4095)));
+      }
+      float2 s02 = make_float2(a0.x + a2.x, a0.y + a2.y);
+      float2 d02 = make_float2(a0.x - a2.x, a0.y - a2.y);
+      float2 s13 = make_float2(a1.x + a3.x, a1.y + a3.y);
+      float2 d13 = make_float2(a1.x - a3.x, a1.y - a3.y);
+      const int idx = (j / ns) * ns * 4 + k;
+      y[idx] = make_float2(s02.x + s13.x, s02.y + s13.y);
+      y[idx + ns] = make_float2(d02.x + d13.y, d02.y - d13.x);
+      y[idx + 2 * ns] = make_float2(s02.x - s13.x, s02.y - s13.y);
+      y[idx + 3 * ns] = make_float2(d02.x - d13.y, d02.y + d13.x);
+    }
+    __syncthreads();
+    float2* t = x;
+    x = y;
+    y = t;
+  }
+  if (ns < n) {
+    const int tws = 4096 / (2 * ns);
+    for (int j = threadIdx.x; j < n / 2; j += blockDim.x) {
+      const int k = j % ns;
+      const float2 a0 = x[j];
+      const float2 a1 = cmul(x[j + n / 2], __ldg(tw + ((k * tws) & 4095)));
+      const int idx = (j / ns) * ns * 2 + k;
+      y[idx] = make_float2(a0.x + a1.x, a0.y + a1.y);
+      y[idx + ns] = make_float2(a0.x - a1.x, a0.y - a1.y);
+    }
+    __syncthreads();
+    float2* t = x;
+    x = y;
+    y = t;
+  }
+  return x;
+}
+
+// One CTA per (frame, batch): out[b, t, k, c, re/im] for k in [0, n/2].
+__global__ void __launch_bounds__(NT) stft_frames_kernel(const float* __restrict__ mix, float* __restrict__ out,
+                                                         const float* __restrict__ window,
+                                                         const float2* __restrict__ tw, int length, int frames,
+                                                         int n, int hop) {
+  extern __shared__ __align__(16) float2 sbuf[];
+  float2* xa = sbuf;
+  float2* xb = sbuf + n;
+  const int t = blockIdx.x, b = blockIdx.y;
+  const float* m0 = mix + (long long)b * 2 * length;
+  const float* m1 = m0 + length;
+  const int base = t * hop - n / 2;
+  for (int q = threadIdx.x; q < n; q += blockDim.x) {
+    const int src = reflect(base + q, length);
+    const float w = __ldg(window + q);
+    xa[q] = make_float2(w * __ldg(m0 + src), w * __ldg(m1 + src));
+  }
+  __syncthreads();
+  float2* Z = fft_pow2(xa, xb, tw, n);
+  const int bins = n / 2 + 1;
+  float* o = out + ((long long)b * frames + t) * bins * 4;
+  for (int k = threadIdx.x; k < bins; k += blockDim.x) {
+    const float2 zk = Z[k & (n - 1)];
+    const float2 zc = Z[(n - k) & (n - 1)];
+    float4 v;
+    v.x = 0.5f * (zk.x + zc.x);
+    v.y = 0.5f * (zk.y - zc.y);
+    v.z = 0.5f * (zk.y + zc.y);
+    v.w = -0.5f * (zk.x - zc.x);
+    *reinterpret_cast<float4*>(o + (long long)k * 4) = v;
+  }
+}
+
+// One CTA per (frame, stem, batch): X_c = stft * mask (complex), DC zeroed,
+// inverse real FFT of both channels, times the window, into
+// frames_buf[b, s, c, t, q].
+__global__ void __launch_bounds__(NT) istft_mask_frames_kernel(const float* __restrict__ stft,
+                                                               const float* __restrict__ mask, long long mask_ss,
+                                                               const float* __restrict__ window,
+                                                               const float2* __restrict__ tw,
+                                                               float* __restrict__ frames_buf, int frames,
+                                                               int stems, int n, int zero_dc) {
+  extern __shared__ __align__(16) float2 sbuf[];
+  float2* xa = sbuf;
+  float2* xb = sbuf + n;
+  const int t = blockIdx.x, s = blockIdx.y, b = blockIdx.z;
+  const int bins = n / 2 + 1;
+  const float* sp = stft + ((long long)b * frames + t) * bins * 4;
+  const float* mp = mask + (long long)s * mask_ss + ((long long)b * frames + t) * bins * 4;
+  for (int k = threadIdx.x; k < bins; k += blockDim.x) {
+    const float4 a = *reinterpret_cast<const float4*>(sp + (long long)k * 4);
+    const float4 m = *reinterpret_cast<const float4*>(mp + (long long)k * 4);
+    float2 x0 = make_float2(a.x * m.x - a.y * m.y, a.x * m.y + a.y * m.x);
+    float2 x1 = make_float2(a.z * m.z - a.w * m.w, a.z * m.w + a.w * m.z);
+    if (k == 0 && zero_dc) x0 = x1 = make_float2(0.f, 0.f);
+    if (k == 0 || k == n / 2) {  // a real inverse transform ignores these imaginary parts
+      x0.y = 0.f;
+      x1.y = 0.f;
+    }
+    const float2 zk = make_float2(x0.x - x1.y, x0.y + x1.x);  // Z[k] = x0 + i x1
+    xa[k] = make_float2(zk.x, -zk.y);
+    if (k > 0 && k < n / 2) {
+      const float2 zn = make_float2(x0.x + x1.y, -x0.y + x1.x);  // Z[n-k] = conj(x0) + i conj(x1)
+      xa[n - k] = make_float2(zn.x, -zn.y);
+    }
+  }
+  __syncthreads();
+  float2* z = fft_pow2(xa, xb, tw, n);
+  const float inv_n = 1.0f / (float)n;
+  float* f0 = frames_buf + (((long long)b * stems + s) * 2 * frames + t) * n;
+  float* f1 = f0 + (long long)frames * n;
+  for (int q = threadIdx.x; q < n; q += blockDim.x) {
+    const float w = __ldg(window + q) * inv_n;
+    const float2 v = z[q];
+    f0[q] = v.x * w;
+    f1[q] = -v.y * w;
+  }
+}
+
+// out[b, s, c, m] = OLA(frames)[m + n/2] / window-square envelope; with
+// `complement`, stem `stems` is mix - stem 0.
+__global__ void istft_ola_kernel_any(const float* __restrict__ frames_buf, const float* __restrict__ window,
+                                     const float* __restrict__ mix, float* __restrict__ out, int batch, int stems,
+                                     int out_stems, int length, int frames, int n, int hop) {
+  const long long total = (long long)batch * stems * 2 * length;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int m = (int)(i % length);
+    const long long rc = i / length;  // (b, s, c)
+    const int c = (int)(rc % 2);
+    const int s = (int)((rc / 2) % stems);
+    const int b = (int)(rc / (2 * stems));
+    const int pos = m + n / 2;
+    int j0 = pos - (n - 1) > 0 ? (pos - (n - 1) + hop - 1) / hop : 0;
+    int j1 = pos / hop;
+    if (j1 > frames - 1) j1 = frames - 1;
+    const float* fb = frames_buf + rc * frames * (long long)n;
+    float acc = 0.f, env = 0.f;
+    for (int j = j0; j <= j1; ++j) {
+      const int p = pos - j * hop;
+      const float w = __ldg(window + p);
+      env += w * w;
+      acc += fb[(long long)j * n + p];
+    }
+    const float v = env > 1e-11f ? acc / env : 0.f;
+    out[(((long long)b * out_stems + s) * 2 + c) * length + m] = v;
+    if (out_stems > stems)
+      out[(((long long)b * out_stems + stems) * 2 + c) * length + m] =
+          __ldg(mix + ((long long)b * 2 + c) * length + m) - v;
+  }
+}
+
+}  // namespace
+
+extern "C" int unblend_stft_frames(const float* mix, float* out, const float* window, int batch, int length,
+                                   int nfft, int hop, void* stream) {
+  UB_REQUIRE(mix && out && window && batch > 0 && batch < 65536 && (nfft == 2048 || nfft == 4096) && hop > 0);
+  UB_REQUIRE(length > nfft / 2);
+  const float2* tw = current_twiddles();
+  UB_REQUIRE(tw);
+  const int frames = 1 + length / hop;
+  const size_t smem = 2 * (size_t)nfft * sizeof(float2);
+  cudaFuncSetAttribute(stft_frames_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  stft_frames_kernel<<<dim3(frames, batch), NT, smem, ub::as_stream(stream)>>>(mix, out, window, tw, length, frames,
+                                                                              nfft, hop);
+  UB_CHECK_LAUNCH();
+  return 0;
+}
+
+extern "C" int unblend_istft_masked(const float* stft, const float* mask, long long mask_ss, const float* window,
+                                    const float* mix, float* frames_buf, float* out, int batch, int stems,
+                                    int complement, int length, int nfft, int hop, int zero_dc, void* stream) {
+  UB_REQUIRE(stft && mask && window && frames_buf && out && batch > 0 && stems > 0 && length > 0 && hop > 0);
+  UB_REQUIRE((nfft == 2048 || nfft == 4096) && batch < 65536 && stems < 65536);
+  UB_REQUIRE(!complement || (stems == 1 && mix));
+  const float2* tw = current_twiddles();
+  UB_REQUIRE(tw);
+  const int frames = 1 + length / hop;
+  const size_t smem = 2 * (size_t)nfft * sizeof(float2);
+  cudaFuncSetAttribute(istft_mask_frames_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  istft_mask_frames_kernel<<<dim3(frames, stems, batch), NT, smem, ub::as_stream(stream)>>>(
+      stft, mask, mask_ss, window, tw, frames_buf, frames, stems, nfft, zero_dc);
+  UB_CHECK_LAUNCH();
+  const long long total = (long long)batch * stems * 2 * length;
+  istft_ola_kernel_any<<<ub::grid_1d(total, 256), 256, 0, ub::as_stream(stream)>>>(
+      frames_buf, window, mix, out, batch, stems, stems + (complement ? 1 : 0), length, frames, nfft, hop);
+  UB_CHECK_LAUNCH();
+  return 0;
+}
+
 extern "C" int unblend_istft_output(const float* spec, const float* xt, long long xt_sb, const float* fstats,
                                     const float* tstats, const float* window, float* frames_buf, float* out,
                                     int batch, int sources, int length, int nfft, void* stream) {
