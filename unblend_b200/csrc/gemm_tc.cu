@@ -15,8 +15,13 @@
 // Warp roles:
 //   warp 0      TMA producer (one elected lane): A box [128 rows x KC], W box [BN rows x KC]
 //   warp 1      TMEM allocation + MMA issue (one elected lane)
-//   warps 2-5   epilogue: TMEM -> registers -> bias / activation / residual -> global
-//   warps 6-9   (MODE 0 only) split each fp32 A tile into TF32 hi + lo in shared memory
+//   warps 2-9   epilogue: warp w reads TMEM lanes 32*(w%4).. (its 32 rows) for one half
+//               of the tile's columns, 32 columns at a time; the 32x32 block is
+//               transposed through a swizzled shared-memory tile so that each
+//               lane then owns 4 consecutive columns of a row: bias loads are one
+//               float4 per lane, and every global store / residual load of the
+//               warp covers 4 whole row segments (coalesced)
+//   warps 10-13 (MODE 0 only) split each fp32 A tile into TF32 hi + lo in shared memory
 // MODE 0: fp32 A and fp32 hi/lo weights, D += Ahi*Whi + Ahi*Wlo + Alo*Whi in
 // kind::tf32 (fp32-level accuracy). MODE 1: bf16 A and bf16 weights straight
 // from TMA into kind::f16 MMAs (no conversion pass).
@@ -47,6 +52,11 @@ struct GemmArgs {
   GroupDesc g[UNBLEND_GEMM_MAX_GROUPS];
 };
 
+constexpr int EPI_WARPS = 8;
+constexpr int EPI_W0 = 2;                // first epilogue warp
+constexpr int CONV_W0 = EPI_W0 + EPI_WARPS;
+constexpr int EPI_TILE = 32 * 32 * 4;    // per-warp transpose tile (32 rows x 32 fp32)
+
 template <int BN, int MODE>
 struct GL {
   static constexpr int KC = MODE == 0 ? 32 : 64;  // K elements per stage (128-byte rows)
@@ -55,11 +65,13 @@ struct GL {
   static constexpr int B_BYTES = BN * 128;
   static constexpr int B_TILES = MODE == 0 ? 2 : 1;
   static constexpr int STAGE = A_BYTES + ALO_BYTES + B_TILES * B_BYTES;
-  static constexpr int STAGES_FIT = (200 * 1024) / STAGE;
+  static constexpr int EPI_BYTES = EPI_WARPS * EPI_TILE;
+  static constexpr int STAGES_FIT = (227 * 1024 - EPI_BYTES - 1024 - 256) / STAGE;
   static constexpr int STAGES = STAGES_FIT > 6 ? 6 : STAGES_FIT;
-  static constexpr int SMEM = STAGES * STAGE + 1024 + 256;
-  static constexpr int NT = MODE == 0 ? 320 : 192;
+  static constexpr int SMEM = STAGES * STAGE + EPI_BYTES + 1024 + 256;
+  static constexpr int NT = 32 * (CONV_W0 + (MODE == 0 ? 4 : 0));
   static constexpr int TMEM_COLS = 2 * BN;
+  static_assert(STAGES >= 2, "pipeline needs two stages");
 };
 
 // Tile t -> (group g, first row m0, n-tile index nt). Tiles are numbered group
@@ -74,64 +86,96 @@ __device__ __forceinline__ void decode_tile(const GemmArgs& a, int t, int& g, in
   nt = local % n_tiles;
 }
 
-__device__ __forceinline__ float act_fn(float x, int act) {
-  if (act == UNBLEND_ACT_GELU) return ub::gelu_erf(x);
-  if (act == UNBLEND_ACT_TANH) return tanhf(x);
+__device__ __forceinline__ float tanh_approx(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Epilogue activation. FAST (the bf16 path, whose outputs are rounded to bf16
+// or feed bf16 operands) uses the hardware tanh.approx instruction: tanh
+// directly, and GELU in its tanh form 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715
+// x^3))) (Hendrycks & Gimpel 2016), whose deviation from the exact erf GELU
+// (< 5e-4 absolute) is below half a bf16 ulp of the result. The fp32 path keeps
+// the exact erf GELU and tanhf.
+template <int ACT, bool FAST>
+__device__ __forceinline__ float act_fn(float x) {
+  if (ACT == UNBLEND_ACT_GELU) {
+    if (FAST) {
+      const float z = 0.7978845608028654f * fmaf(0.044715f * x, x * x, x);
+      return 0.5f * x * (1.0f + tanh_approx(z));
+    }
+    return ub::gelu_erf(x);
+  }
+  if (ACT == UNBLEND_ACT_TANH) return FAST ? tanh_approx(x) : tanhf(x);
   return x;
 }
 
-// Store `cnt` (<= NOUT) values o[0..cnt) at column `col` of row `row`, adding
-// the residual first when present.
-template <int NOUT>
-__device__ __forceinline__ void store_run(const GemmArgs& a, long long row, int col, float (&o)[NOUT], int cnt) {
-  const long long ro = row * a.ldr + col;
-  const long long oo = row * a.ldo + col;
-#pragma unroll
-  for (int j4 = 0; j4 < NOUT / 4; ++j4) {
-    if (4 * j4 >= cnt) break;
-    if (a.vec && 4 * j4 + 4 <= cnt) {
-      float v0 = o[4 * j4], v1 = o[4 * j4 + 1], v2 = o[4 * j4 + 2], v3 = o[4 * j4 + 3];
-      if (a.res) {
-        const float4 r = *reinterpret_cast<const float4*>(a.res + ro + 4 * j4);
-        v0 += r.x;
-        v1 += r.y;
-        v2 += r.z;
-        v3 += r.w;
+template <bool FAST>
+__device__ __forceinline__ float sigmoid_fn(float x) {
+  if (FAST) return 0.5f * tanh_approx(0.5f * x) + 0.5f;
+  return ub::sigmoidf_(x);
+}
+
+// Store NV (4, or 2 after GLU) consecutive values of one row at element
+// offset `off` (cnt of them valid), adding the residual values `r` (already
+// loaded by the caller) when present.
+template <int NV, int OBF>
+__device__ __forceinline__ void store_vals(const GemmArgs& a, long long off, float (&o)[NV], const float4& r,
+                                           int cnt) {
+  if (a.vec && cnt == NV) {
+    if (a.res) {
+      o[0] += r.x;
+      o[1] += r.y;
+      if (NV == 4) {
+        o[2] += r.z;
+        o[3] += r.w;
       }
-      if (a.out_bf16) {
-        __nv_bfloat162 p0 = __floats2bfloat162_rn(v0, v1);
-        __nv_bfloat162 p1 = __floats2bfloat162_rn(v2, v3);
+    }
+    if (OBF) {
+      __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.out) + off;
+      __nv_bfloat162 p0 = __floats2bfloat162_rn(o[0], o[1]);
+      if (NV == 4) {
+        __nv_bfloat162 p1 = __floats2bfloat162_rn(o[2], o[3]);
         uint2 packed;
         packed.x = *reinterpret_cast<uint32_t*>(&p0);
         packed.y = *reinterpret_cast<uint32_t*>(&p1);
-        *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(a.out) + oo + 4 * j4) = packed;
+        *reinterpret_cast<uint2*>(out) = packed;
       } else {
-        *reinterpret_cast<float4*>(reinterpret_cast<float*>(a.out) + oo + 4 * j4) = make_float4(v0, v1, v2, v3);
+        *reinterpret_cast<__nv_bfloat162*>(out) = p0;
       }
     } else {
+      float* out = reinterpret_cast<float*>(a.out) + off;
+      if (NV == 4)
+        *reinterpret_cast<float4*>(out) = make_float4(o[0], o[1], o[2], o[3]);
+      else
+        *reinterpret_cast<float2*>(out) = make_float2(o[0], o[1]);
+    }
+    return;
+  }
+  const float rr[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        if (4 * j4 + e < cnt) {
-          float v = o[4 * j4 + e];
-          if (a.res) v += a.res[ro + 4 * j4 + e];
-          if (a.out_bf16)
-            reinterpret_cast<__nv_bfloat16*>(a.out)[oo + 4 * j4 + e] = __float2bfloat16_rn(v);
-          else
-            reinterpret_cast<float*>(a.out)[oo + 4 * j4 + e] = v;
-        }
-      }
+  for (int e = 0; e < NV; ++e) {
+    if (e < cnt) {
+      float v = o[e];
+      if (a.res) v += rr[e];
+      if (OBF)
+        reinterpret_cast<__nv_bfloat16*>(a.out)[off + e] = __float2bfloat16_rn(v);
+      else
+        reinterpret_cast<float*>(a.out)[off + e] = v;
     }
   }
 }
 
-template <int BN, int MODE>
+template <int BN, int MODE, int ACT, int OBF>
 __global__ void __launch_bounds__(GL<BN, MODE>::NT, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
                    const __grid_constant__ CUtensorMap mapB2, const __grid_constant__ GemmArgs a) {
   using L = GL<BN, MODE>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::STAGES * L::STAGE);
+  uint8_t* epi_smem = smem + L::STAGES * L::STAGE;
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi_smem + L::EPI_BYTES);
   uint64_t* conv = full + L::STAGES;
   uint64_t* empty = conv + L::STAGES;
   uint64_t* acc_full = empty + L::STAGES;  // [2]
@@ -149,7 +193,7 @@ __global__ void __launch_bounds__(GL<BN, MODE>::NT, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 4);
+      mbar_init(&acc_empty[i], EPI_WARPS);
     }
     fence_mbar_init();
   }
@@ -233,9 +277,13 @@ __global__ void __launch_bounds__(GL<BN, MODE>::NT, 1)
       }
       if (!ok) atomicExch(&g_error_flag, 2);
     }
-  } else if (warp < 6) {
-    // Epilogue warps: warp w reads TMEM lanes 32*(w%4) .. 32*(w%4)+31.
-    const int q = warp & 3;
+  } else if (warp < CONV_W0) {
+    // Epilogue warps.
+    const int e = warp - EPI_W0;
+    const int q = warp & 3;           // TMEM lane quarter this warp may read
+    const int c_lo = (e >> 2) * (BN / 2);
+    float4* stage = reinterpret_cast<float4*>(epi_smem + e * EPI_TILE);
+    const int ch = lane & 7;          // this lane's 4-column group after the transpose
     int i = 0;
     for (int t = blockIdx.x; t < a.total_tiles; t += gridDim.x, ++i) {
       int g, m0, nt;
@@ -245,36 +293,73 @@ __global__ void __launch_bounds__(GL<BN, MODE>::NT, 1)
       const int buf = i & 1, u = i >> 1;
       if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[buf], u & 1))) break;
       tc_fence_after();
-      const long long row = (long long)m0 + q * 32 + lane;
-      const bool rv = row < a.m;
+      const long long row0 = (long long)m0 + q * 32;
       const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
-      const bool glu = a.act == UNBLEND_ACT_GLU;
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
+      for (int c0 = c_lo; c0 < c_lo + BN / 2; c0 += 32) {
         if (n0 + c0 >= gd.n) break;  // uniform across the warp
         uint32_t acc[32];
-        __syncwarp();
         tmem_ld32(base + (uint32_t)c0, acc);
-        if (!rv) continue;
-        float v[32];
+        __syncwarp();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int n = n0 + c0 + j;
-          float x = __uint_as_float(acc[j]);
-          if (a.bias && n < gd.n) x += __ldg(a.bias + gd.w_row0 + n);
-          v[j] = act_fn(x, a.act);
+        for (int j = 0; j < 8; ++j)
+          stage[lane * 8 + (j ^ (lane & 7))] =
+              make_float4(__uint_as_float(acc[4 * j]), __uint_as_float(acc[4 * j + 1]),
+                          __uint_as_float(acc[4 * j + 2]), __uint_as_float(acc[4 * j + 3]));
+        __syncwarp();
+        const int ncol = n0 + c0 + ch * 4;  // group-local column of this lane's first value
+        const int nvalid = min(4, gd.n - ncol);
+        float4 bv = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (a.bias && nvalid > 0) {
+          const float* bp = a.bias + gd.w_row0 + ncol;
+          if (nvalid == 4) {
+            bv = __ldg(reinterpret_cast<const float4*>(bp));
+          } else {
+            bv.x = __ldg(bp);
+            if (nvalid > 1) bv.y = __ldg(bp + 1);
+            if (nvalid > 2) bv.z = __ldg(bp + 2);
+          }
         }
-        if (glu) {
-          float o[16];
+        constexpr bool FAST = MODE == 1;
+        const int oc = gd.out_col0 + (ACT == UNBLEND_ACT_GLU ? ncol / 2 : ncol);
+        const int ocnt = ACT == UNBLEND_ACT_GLU ? nvalid / 2 : nvalid;
+        // Residual values of the lane's 8 rows, all loads in flight at once.
+        float4 rv[8];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) o[j] = v[2 * j] * ub::sigmoidf_(v[2 * j + 1]);
-          const int col = (n0 + c0) / 2;
-          const int cnt = min(16, gd.n / 2 - col);
-          store_run<16>(a, row, gd.out_col0 + col, o, cnt);
-        } else {
-          const int col = n0 + c0;
-          const int cnt = min(32, gd.n - col);
-          store_run<32>(a, row, gd.out_col0 + col, v, cnt);
+        for (int k = 0; k < 8; ++k) {
+          rv[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+          const long long row = row0 + k * 4 + (lane >> 3);
+          if (a.res && row < a.m && nvalid > 0) {
+            const float* rp = a.res + row * a.ldr + oc;
+            if (a.vec && ocnt == (ACT == UNBLEND_ACT_GLU ? 2 : 4)) {
+              if (ACT == UNBLEND_ACT_GLU) {
+                const float2 t2 = *reinterpret_cast<const float2*>(rp);
+                rv[k] = make_float4(t2.x, t2.y, 0.f, 0.f);
+              } else {
+                rv[k] = *reinterpret_cast<const float4*>(rp);
+              }
+            } else {
+              rv[k].x = rp[0];
+              if (ocnt > 1) rv[k].y = rp[1];
+              if (ocnt > 2) rv[k].z = rp[2];
+              if (ocnt > 3) rv[k].w = rp[3];
+            }
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int r = k * 4 + (lane >> 3);
+          const long long row = row0 + r;
+          const float4 v = stage[r * 8 + (ch ^ (r & 7))];
+          if (row >= a.m || nvalid <= 0) continue;
+          float x[4] = {act_fn<ACT, FAST>(v.x + bv.x), act_fn<ACT, FAST>(v.y + bv.y),
+                        act_fn<ACT, FAST>(v.z + bv.z), act_fn<ACT, FAST>(v.w + bv.w)};
+          if (ACT == UNBLEND_ACT_GLU) {
+            float o[2] = {x[0] * sigmoid_fn<FAST>(x[1]), x[2] * sigmoid_fn<FAST>(x[3])};
+            store_vals<2, OBF>(a, row * a.ldo + oc, o, rv[k], ocnt);
+          } else {
+            store_vals<4, OBF>(a, row * a.ldo + oc, x, rv[k], ocnt);
+          }
         }
       }
       tc_fence_before();
@@ -282,8 +367,8 @@ __global__ void __launch_bounds__(GL<BN, MODE>::NT, 1)
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
   } else if (MODE == 0) {
-    // Converter warps 6-9: TF32 hi (in place) + lo split of each fp32 A tile.
-    const int ct = threadIdx.x - 192;
+    // Converter warps: TF32 hi (in place) + lo split of each fp32 A tile.
+    const int ct = threadIdx.x - 32 * CONV_W0;
     int it = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < a.total_tiles && ok; t += gridDim.x) {
@@ -362,17 +447,45 @@ int sm_count() {
   return n;
 }
 
-template <int BN, int MODE>
+template <int BN, int MODE, int ACT, int OBF>
 int launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb2, const GemmArgs& args,
            cudaStream_t st) {
   using L = GL<BN, MODE>;
-  auto k = gemm_tc_kernel<BN, MODE>;
+  auto k = gemm_tc_kernel<BN, MODE, ACT, OBF>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
   int grid = sm_count();
   if (grid > args.total_tiles) grid = args.total_tiles;
   k<<<grid, L::NT, L::SMEM, st>>>(ma, mb, mb2, args);
   UB_CHECK_LAUNCH();
   return 0;
+}
+
+template <int BN, int MODE>
+int dispatch_epi(int act, int obf, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb2,
+                 const GemmArgs& g, cudaStream_t st) {
+  switch (act * 2 + obf) {
+    case UNBLEND_ACT_NONE * 2: return launch<BN, MODE, UNBLEND_ACT_NONE, 0>(ma, mb, mb2, g, st);
+    case UNBLEND_ACT_NONE * 2 + 1: return launch<BN, MODE, UNBLEND_ACT_NONE, 1>(ma, mb, mb2, g, st);
+    case UNBLEND_ACT_GELU * 2: return launch<BN, MODE, UNBLEND_ACT_GELU, 0>(ma, mb, mb2, g, st);
+    case UNBLEND_ACT_GELU * 2 + 1: return launch<BN, MODE, UNBLEND_ACT_GELU, 1>(ma, mb, mb2, g, st);
+    case UNBLEND_ACT_GLU * 2: return launch<BN, MODE, UNBLEND_ACT_GLU, 0>(ma, mb, mb2, g, st);
+    case UNBLEND_ACT_GLU * 2 + 1: return launch<BN, MODE, UNBLEND_ACT_GLU, 1>(ma, mb, mb2, g, st);
+    case UNBLEND_ACT_TANH * 2: return launch<BN, MODE, UNBLEND_ACT_TANH, 0>(ma, mb, mb2, g, st);
+    case UNBLEND_ACT_TANH * 2 + 1: return launch<BN, MODE, UNBLEND_ACT_TANH, 1>(ma, mb, mb2, g, st);
+    default: return UNBLEND_ERR_INVALID;
+  }
+}
+
+int dispatch_mode(int mode, int block_n, int act, int obf, const CUtensorMap& ma, const CUtensorMap& mb,
+                  const CUtensorMap& mb2, const GemmArgs& g, cudaStream_t st) {
+  if (mode == 0) {
+    if (block_n == 64) return dispatch_epi<64, 0>(act, obf, ma, mb, mb2, g, st);
+    if (block_n == 128) return dispatch_epi<128, 0>(act, obf, ma, mb, mb2, g, st);
+    return dispatch_epi<256, 0>(act, obf, ma, mb, mb2, g, st);
+  }
+  if (block_n == 64) return dispatch_epi<64, 1>(act, obf, ma, mb, mb2, g, st);
+  if (block_n == 128) return dispatch_epi<128, 1>(act, obf, ma, mb, mb2, g, st);
+  return dispatch_epi<256, 1>(act, obf, ma, mb, mb2, g, st);
 }
 
 }  // namespace
@@ -394,6 +507,7 @@ extern "C" int unblend_gemm_tc(const void* a, long long lda, int rows, int a_col
   UB_REQUIRE(mode == 1 || (reinterpret_cast<uintptr_t>(w_lo) & 15) == 0);
   UB_REQUIRE(lda >= a_cols && lda % align == 0 && w_cols % align == 0);
   UB_REQUIRE(p->ldo > 0 && (!p->res || p->ldr > 0));
+  UB_REQUIRE(!p->bias || (reinterpret_cast<uintptr_t>(p->bias) & 15) == 0);
   GemmArgs g{};
   g.m = rows;
   g.groups = p->groups;
@@ -412,7 +526,8 @@ extern "C" int unblend_gemm_tc(const void* a, long long lda, int rows, int a_col
     const UnblendGemmGroup& s = p->group[i];
     UB_REQUIRE(s.n > 0 && s.k > 0 && s.k <= w_cols && s.a_col0 >= 0 && s.a_col0 % align == 0 && s.a_col0 < a_cols);
     UB_REQUIRE(s.w_row0 >= 0 && s.w_row0 + (long long)s.n <= w_rows && s.out_col0 >= 0);
-    UB_REQUIRE(p->act != UNBLEND_ACT_GLU || s.n % 2 == 0);
+    UB_REQUIRE(p->act != UNBLEND_ACT_GLU || s.n % 4 == 0);
+    UB_REQUIRE(!p->bias || s.w_row0 % 4 == 0);
     if (s.out_col0 % 4 != 0) vec = false;
     GroupDesc& d = g.g[i];
     d.a_col0 = s.a_col0;
@@ -435,15 +550,7 @@ extern "C" int unblend_gemm_tc(const void* a, long long lda, int rows, int a_col
   } else {
     mb2 = mb;
   }
-  cudaStream_t st = ub::as_stream(stream);
-  if (mode == 0) {
-    if (block_n == 64) return launch<64, 0>(ma, mb, mb2, g, st);
-    if (block_n == 128) return launch<128, 0>(ma, mb, mb2, g, st);
-    return launch<256, 0>(ma, mb, mb2, g, st);
-  }
-  if (block_n == 64) return launch<64, 1>(ma, mb, mb2, g, st);
-  if (block_n == 128) return launch<128, 1>(ma, mb, mb2, g, st);
-  return launch<256, 1>(ma, mb, mb2, g, st);
+  return dispatch_mode(mode, block_n, p->act, g.out_bf16, ma, mb, mb2, g, ub::as_stream(stream));
 }
 
 extern "C" int unblend_gemm_error_flag(int* out_host, int clear) {
