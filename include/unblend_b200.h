@@ -210,6 +210,18 @@ typedef struct {
 int unblend_attention_tc2(const float* q, const float* k, const float* v, const UnblendAttnParams* p, int mode,
                           void* stream);
 
+/* The same attention with bf16 Q, K, V (head dim 64) on kind::f16 tensor cores:
+ * a persistent flash-attention kernel over (sequence, head, 128-query) units,
+ * fp32 softmax and accumulation, P rounded to bf16. Strides as in
+ * unblend_attention_tc2 (elements of the bf16 tensors, multiples of 8); rope
+ * must be NULL (apply the rotation when producing Q and K, e.g. in
+ * unblend_gemm_tc); gate and out_bf16 as there. */
+int unblend_attention_bf16(const void* q, const void* k, const void* v, const UnblendAttnParams* p,
+                           void* stream);
+
+/* Device flag of unblend_attention_bf16's bounded waits (0 = none). Synchronous host call. */
+int unblend_attention_bf16_error_flag(int* out_host, int clear);
+
 /*
  * Grouped linear layers on the tcgen05 tensor cores (nn.Linear of
  * BS-RoFormer's Attention / FeedForward, unblend/roformer.py:274-308, 478-511,
@@ -220,8 +232,11 @@ int unblend_attention_tc2(const float* q, const float* k, const float* v, const 
  * where K_g is k rounded up to the K chunk (32 fp32 / 64 bf16 elements): the
  * weights must be zero in columns k..K_g-1 (A columns past a_cols read as 0).
  * With act = UNBLEND_ACT_GLU weight rows are interleaved (value, gate) pairs
- * and y has n/2 columns. The result (plus res[r, c] when res is set; res may
- * alias out) goes to out[r * ldo + out_col0 + c] as fp32 or bf16.
+ * and y has n/2 columns. With rope set, each (even, odd) column pair j < rope_cols
+ * is rotated by rope[pos, (j % rope_hd) / 2] = (cos, sin), pos = (r / rope_div) %
+ * rope_mod (the rotary embedding of Q and K, unblend/roformer.py:251-271; rope is
+ * float[rope_mod, rope_hd/2, 2]). The result (plus res[r, c] when res is set; res
+ * may alias out) goes to out[r * ldo + out_col0 + c] as fp32 or bf16.
  * mode 0: A and W fp32 (W as TF32 hi/lo split like unblend_conv2d_tc), 3-pass
  * TF32; mode 1: A and W bf16. block_n: 64, 128 or 256.
  * Alignment: A, W 16-byte aligned, lda, w_cols and every a_col0 multiples of
@@ -242,6 +257,8 @@ typedef struct {
   void* out;
   long long ldo;
   int out_bf16;
+  const float* rope; /* optional rotary table (act must be NONE) */
+  int rope_cols, rope_hd, rope_div, rope_mod;
 } UnblendGemmParams;
 
 int unblend_gemm_tc(const void* a, long long lda, int rows, int a_cols, const void* w_hi, const void* w_lo,

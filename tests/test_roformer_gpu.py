@@ -353,3 +353,81 @@ def test_batch_rows_are_independent():
     both = m(mix)
     one = m(mix[1:2])
     assert rel_err(both[1:2], one) < 1e-5
+
+
+@pytest.mark.parametrize("axis", [0, 1])
+@pytest.mark.parametrize("out_bf16", [1, 0])
+def test_attention_bf16_axial_gate(axis, out_bf16):
+    """Persistent bf16 attention (no rotary: Q and K arrive rotated) against a float64 reference."""
+    torch.manual_seed(8)
+    B, T, nb, H, hd = 2, 300, 13, 4, 64
+    inner = H * hd
+    qkv = torch.randn(B, T, nb, 3 * inner, device="cuda").to(torch.bfloat16)
+    gates = torch.rand(B, T, nb, H, device="cuda")
+    seq = T if axis == 0 else nb
+    o = torch.empty(B, T, nb, inner, device="cuda", dtype=torch.bfloat16 if out_bf16 else torch.float32)
+    a = _lib.AttnParams()
+    a.heads, a.hd = H, hd
+    q3 = 3 * inner
+    if axis == 0:
+        a.outer, a.inner, a.lq, a.lk = B, nb, T, T
+        a.q_so, a.q_si, a.q_sr = T * nb * q3, q3, nb * q3
+        a.o_so, a.o_si, a.o_sr = T * nb * inner, inner, nb * inner
+        a.g_so, a.g_si, a.g_sr = T * nb * H, H, nb * H
+    else:
+        a.outer, a.inner, a.lq, a.lk = B * T, 1, nb, nb
+        a.q_so, a.q_si, a.q_sr = nb * q3, 8, q3
+        a.o_so, a.o_si, a.o_sr = nb * inner, 0, inner
+        a.g_so, a.g_si, a.g_sr = nb * H, 0, H
+    a.kv_so, a.kv_si, a.kv_sr = a.q_so, a.q_si, a.q_sr
+    a.out, a.out_bf16, a.gate, a.scale = o.data_ptr(), out_bf16, gates.data_ptr(), hd ** -0.5
+    base = qkv.data_ptr()
+    _lib.call("unblend_attention_bf16", base, base + 2 * inner, base + 4 * inner, ctypes.byref(a))
+    x = qkv.double()
+    g = gates.double()
+    if axis == 0:
+        x = x.permute(0, 2, 1, 3)
+        g = g.permute(0, 2, 1, 3)
+    q, k, v = (t.transpose(-2, -3) for t in x.unflatten(-1, (3, H, hd)).unbind(-3))
+    att = torch.softmax(q @ k.transpose(-1, -2) * hd ** -0.5, -1) @ v
+    ref = (att * g.transpose(-1, -2).unsqueeze(-1)).transpose(-2, -3).flatten(-2)
+    if axis == 0:
+        ref = ref.permute(0, 2, 1, 3)
+    # P is rounded to bf16 (2^-9 relative) before the P V product
+    assert rel_err(o.float(), ref) < 2e-2
+    assert _lib.error_flag() == 0
+
+
+@pytest.mark.parametrize("axis", [0, 1])
+def test_gemm_rope_epilogue(axis):
+    """The QKV projection with the rotary rotation of Q and K applied in its epilogue."""
+    torch.manual_seed(9)
+    B, T, nb, H, hd, dim = 2, 40, 7, 2, 64, 128
+    inner = H * hd
+    rows = B * T * nb
+    seq = T if axis == 0 else nb
+    cos, sin = _rope(seq, hd)
+    table = torch.stack([cos, sin], -1).contiguous().cuda()
+    a = torch.randn(rows, dim, device="cuda")
+    w = torch.randn(3 * inner, dim, device="cuda") / math.sqrt(dim)
+    out = torch.empty(rows, 3 * inner, device="cuda")
+    hi, lo = split_tf32(w)
+    arr = (_lib.GemmGroup * 1)(_lib.GemmGroup(0, 0, 3 * inner, dim, 0))
+    p = _lib.GemmParams()
+    p.groups, p.group, p.act = 1, ctypes.cast(arr, ctypes.POINTER(_lib.GemmGroup)), _lib.ACT_NONE
+    p.out, p.ldo, p.out_bf16 = out.data_ptr(), 3 * inner, 0
+    p.rope, p.rope_cols, p.rope_hd = table.data_ptr(), 2 * inner, hd
+    p.rope_div, p.rope_mod = (nb, T) if axis == 0 else (1, nb)
+    _lib.call("unblend_gemm_tc", a.data_ptr(), dim, rows, dim, hi.data_ptr(), lo.data_ptr(), 3 * inner, dim,
+              ctypes.byref(p), _lib.TC_TF32X3, 256)
+    y = (a.double() @ w.double().t()).view(B, T, nb, 3, H, hd)
+    pos = torch.arange(T if axis == 0 else nb)
+    c = cos.double().cuda()[pos]
+    s_ = sin.double().cuda()[pos]
+    if axis == 0:  # [B, T, nb, qk, H, hd/2] broadcast over T
+        c, s_ = c[None, :, None, None, None, :], s_[None, :, None, None, None, :]
+    else:
+        c, s_ = c[None, None, :, None, None, :], s_[None, None, :, None, None, :]
+    qk = _rotate(y[:, :, :, :2], c, s_)
+    ref = torch.cat([qk, y[:, :, :, 2:]], dim=3).reshape(rows, 3 * inner)
+    assert rel_err(out, ref) < 6e-5

@@ -75,6 +75,7 @@ class GemmParams(ctypes.Structure):
     _fields_ = [
         ("groups", c_int), ("group", ctypes.POINTER(GemmGroup)), ("bias", c_void_p), ("act", c_int),
         ("res", c_void_p), ("ldr", c_ll), ("out", c_void_p), ("ldo", c_ll), ("out_bf16", c_int),
+        ("rope", c_void_p), ("rope_cols", c_int), ("rope_hd", c_int), ("rope_div", c_int), ("rope_mod", c_int),
     ]
 
 
@@ -115,6 +116,7 @@ _SIGNATURES = {
     "unblend_dconv_apply": [c_void_p, c_ll, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p,
                             c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p],
     "unblend_attention_tc2": [c_void_p, c_void_p, c_void_p, ctypes.POINTER(AttnParams), c_int, c_void_p],
+    "unblend_attention_bf16": [c_void_p, c_void_p, c_void_p, ctypes.POINTER(AttnParams), c_void_p],
     "unblend_gemm_tc": [c_void_p, c_ll, c_int, c_int, c_void_p, c_void_p, c_ll, c_int, ctypes.POINTER(GemmParams),
                         c_int, c_int, c_void_p],
     "unblend_rms_norm": [c_void_p, c_ll, c_int, c_void_p, c_void_p, c_ll, c_int, c_void_p, c_void_p, c_int,
@@ -130,6 +132,7 @@ _HOST_SIGNATURES = {
     "unblend_error_flag": [ctypes.POINTER(c_int), c_int],
     "unblend_attention_error_flag": [ctypes.POINTER(c_int), c_int],
     "unblend_gemm_error_flag": [ctypes.POINTER(c_int), c_int],
+    "unblend_attention_bf16_error_flag": [ctypes.POINTER(c_int), c_int],
 }
 
 TC_TF32X3, TC_BF16 = 0, 1
@@ -163,7 +166,8 @@ def exported_symbols() -> list[str]:
 def error_flag(clear: bool = True) -> int:
     """Read (and by default clear) the device flag that bounded waits set on timeout."""
     total = 0
-    for name in ("unblend_error_flag", "unblend_attention_error_flag", "unblend_gemm_error_flag"):
+    for name in ("unblend_error_flag", "unblend_attention_error_flag", "unblend_gemm_error_flag",
+                 "unblend_attention_bf16_error_flag"):
         v = c_int(0)
         check(name, getattr(load(), name)(ctypes.byref(v), 1 if clear else 0))
         total |= v.value

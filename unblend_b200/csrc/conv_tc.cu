@@ -58,7 +58,8 @@ struct Layout {
   static constexpr int B_TILES = MODE == 0 ? 2 : 1;                   // hi + lo, or bf16
   static constexpr int STAGE = A_BYTES + AC_BYTES + B_TILES * B_BYTES;
   static constexpr int STAGES = (200 * 1024) / STAGE > 4 ? 4 : (200 * 1024) / STAGE;
-  static constexpr int SMEM = STAGES * STAGE + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int EPI_BYTES = 4 * 32 * 32 * 4;  // one 32 x 32 fp32 transpose tile per epilogue warp
+  static constexpr int SMEM = STAGES * STAGE + EPI_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
 
 __device__ __forceinline__ float gelu(float x) { return ub::gelu_erf(x); }
@@ -70,7 +71,8 @@ __global__ void __launch_bounds__(NT, 1)
   using L = Layout<BN, MODE>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::STAGES * L::STAGE);
+  uint8_t* epi_smem = smem + L::STAGES * L::STAGE;
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi_smem + L::EPI_BYTES);
   uint64_t* conv = full + L::STAGES;
   uint64_t* empty = conv + L::STAGES;
   uint64_t* accum = empty + L::STAGES;
@@ -215,78 +217,129 @@ __global__ void __launch_bounds__(NT, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&conv[s]);
     }
-    // Epilogue: TMEM -> registers -> fused ops -> global.
+    // Epilogue: TMEM -> registers -> shared-memory transpose -> fused ops ->
+    // global. After the transpose each lane owns 4 consecutive output channels
+    // of 8 rows, so bias / scale loads are one float4 per lane and each store
+    // instruction of the warp writes 4 whole row segments.
     ok = __all_sync(0xffffffffu, ok && mbar_wait(accum, 0));
     tc_fence_after();
     if (ok) {
       const int q = warp & 3;
-      const int row = q * 32 + lane;
-      const int wpos = w0 + row;
-      const bool rv = row < a.m_valid && wpos < a.W_out;
-      const long long rowoff = (long long)b * a.out_sb + (long long)h * a.out_sh + (long long)wpos * a.out_sw;
+      float4* stage = reinterpret_cast<float4*>(epi_smem + (warp - 2) * 4096);
+      const int ch = lane & 7;
       const bool glu = a.act == UNBLEND_ACT_GLU;
-      const int ncount = glu ? a.n_out / 2 : a.n_out;
-      float s1 = 0.f, s2 = 0.f;
+      double s1 = 0.0, s2 = 0.0;  // per-lane statistics: fp32 partials of 4 values, summed in double
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
+        if (n0 + c0 >= a.n_out) break;  // uniform across the warp
         uint32_t acc[32];
         __syncwarp();
         tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, acc);
-        if (!rv || n0 + c0 >= a.n_out) continue;  // after the warp-wide load
-        float v[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int n = n0 + c0 + j;
-          float x = __uint_as_float(acc[j]);
-          if (a.bias && n < a.n_out) x += __ldg(a.bias + n);
-          if (a.act == UNBLEND_ACT_GELU) x = gelu(x);
-          v[j] = x;
+        for (int j = 0; j < 8; ++j)
+          stage[lane * 8 + (j ^ (lane & 7))] =
+              make_float4(__uint_as_float(acc[4 * j]), __uint_as_float(acc[4 * j + 1]),
+                          __uint_as_float(acc[4 * j + 2]), __uint_as_float(acc[4 * j + 3]));
+        __syncwarp();
+        const int n = n0 + c0 + ch * 4;  // first of this lane's 4 accumulator columns
+        const int nvalid = min(4, a.n_out - n);
+        float4 bv = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (a.bias && nvalid > 0) {
+          if (nvalid == 4) {
+            bv = __ldg(reinterpret_cast<const float4*>(a.bias + n));
+          } else {
+            bv.x = __ldg(a.bias + n);
+            if (nvalid > 1) bv.y = __ldg(a.bias + n + 1);
+            if (nvalid > 2) bv.z = __ldg(a.bias + n + 2);
+          }
         }
-        const int nouts = glu ? 16 : 32;
-        const int nb = glu ? (n0 + c0) / 2 : n0 + c0;
+        const int nb = glu ? n / 2 : n;  // first output channel
+        const int ocnt = glu ? nvalid / 2 : nvalid;
+        const long long goff = (long long)(nb / a.n_group) * a.out_sg + (nb % a.n_group);
+        float4 sc = make_float4(1.f, 1.f, 1.f, 1.f);
+        if (a.res && a.res_scale && ocnt > 0) {
+          sc.x = __ldg(a.res_scale + nb);
+          if (ocnt > 1) sc.y = __ldg(a.res_scale + nb + 1);
+          if (ocnt > 2) sc.z = __ldg(a.res_scale + nb + 2);
+          if (ocnt > 3) sc.w = __ldg(a.res_scale + nb + 3);
+        }
+        // Residual values of the lane's 8 rows, all loads in flight at once.
+        float4 rv[8];
 #pragma unroll
-        for (int j4 = 0; j4 < 8; ++j4) {
-          if (j4 * 4 >= nouts) break;
-          const int n = nb + j4 * 4;
-          if (n >= ncount) break;
+        for (int k = 0; k < 8; ++k) {
+          rv[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+          const int row = q * 32 + k * 4 + (lane >> 3);
+          const int wpos = w0 + row;
+          if (a.res && ocnt > 0 && row < a.m_valid && wpos < a.W_out) {
+            const float* rp = a.res + (long long)b * a.out_sb + (long long)h * a.out_sh +
+                              (long long)wpos * a.out_sw + goff;
+            if (ocnt == 4) {
+              rv[k] = *reinterpret_cast<const float4*>(rp);
+            } else {
+              rv[k].x = rp[0];
+              if (ocnt > 1) rv[k].y = rp[1];
+              if (ocnt > 2) rv[k].z = rp[2];
+            }
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int r = k * 4 + (lane >> 3);
+          const int row = q * 32 + r;
+          const int wpos = w0 + row;
+          const float4 v = stage[r * 8 + (ch ^ (r & 7))];
+          if (ocnt <= 0 || row >= a.m_valid || wpos >= a.W_out) continue;
+          float x[4] = {v.x + bv.x, v.y + bv.y, v.z + bv.z, v.w + bv.w};
+          if (a.act == UNBLEND_ACT_GELU) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) x[e] = gelu(x[e]);
+          }
           float o[4];
+          if (glu) {
+            o[0] = x[0] * ub::sigmoidf_(x[1]);
+            o[1] = x[2] * ub::sigmoidf_(x[3]);
+            o[2] = o[3] = 0.f;
+          } else {
+            o[0] = x[0];
+            o[1] = x[1];
+            o[2] = x[2];
+            o[3] = x[3];
+          }
+          if (a.res) {
+            o[0] = rv[k].x + sc.x * o[0];
+            o[1] = rv[k].y + sc.y * o[1];
+            o[2] = rv[k].z + sc.z * o[2];
+            o[3] = rv[k].w + sc.w * o[3];
+          }
+          float* yp = a.y + (long long)b * a.out_sb + (long long)h * a.out_sh + (long long)wpos * a.out_sw + goff;
+          if (ocnt == 4) {
+            *reinterpret_cast<float4*>(yp) = make_float4(o[0], o[1], o[2], o[3]);
+          } else if (ocnt == 2 && glu) {
+            *reinterpret_cast<float2*>(yp) = make_float2(o[0], o[1]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              if (e < ocnt) yp[e] = o[e];
+          }
+          float t1 = 0.f, t2 = 0.f;
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const int jj = j4 * 4 + e;
-            o[e] = glu ? v[2 * jj] * ub::sigmoidf_(v[2 * jj + 1]) : v[jj];
-          }
-          const long long off = rowoff + (long long)(n / a.n_group) * a.out_sg + (n % a.n_group);
-          if (n + 4 <= ncount) {
-            if (a.res) {
-              const float4 rr = *reinterpret_cast<const float4*>(a.res + off);
-              const float rs[4] = {rr.x, rr.y, rr.z, rr.w};
-#pragma unroll
-              for (int e = 0; e < 4; ++e) o[e] = rs[e] + (a.res_scale ? __ldg(a.res_scale + n + e) : 1.f) * o[e];
-            }
-            *reinterpret_cast<float4*>(a.y + off) = make_float4(o[0], o[1], o[2], o[3]);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              s1 += o[e];
-              s2 += o[e] * o[e];
-            }
-          } else {
-            for (int e = 0; e < 4 && n + e < ncount; ++e) {
-              float x = o[e];
-              if (a.res) x = a.res[off + e] + (a.res_scale ? __ldg(a.res_scale + n + e) : 1.f) * x;
-              a.y[off + e] = x;
-              s1 += x;
-              s2 += x * x;
+            if (e < ocnt) {
+              t1 += o[e];
+              t2 += o[e] * o[e];
             }
           }
+          s1 += t1;
+          s2 += t2;
         }
       }
       if (a.stats) {
-        s1 = ub::warp_sum(s1);
-        s2 = ub::warp_sum(s2);
+        s1 = ub::warp_sum_d(s1);
+        s2 = ub::warp_sum_d(s2);
         if (lane == 0) {
           const int g = a.stats_per_h ? b * a.H + h : b;
-          atomicAdd(a.stats + 2 * g, (double)s1);
-          atomicAdd(a.stats + 2 * g + 1, (double)s2);
+          atomicAdd(a.stats + 2 * g, s1);
+          atomicAdd(a.stats + 2 * g + 1, s2);
         }
       }
     }
@@ -361,6 +414,9 @@ extern "C" int unblend_conv2d_tc(const float* x, const void* w_hi, const void* w
              p->out_sb % 4 == 0);
   UB_REQUIRE(p->act != UNBLEND_ACT_GLU || p->n_out % 2 == 0);
   UB_REQUIRE(p->in_sw == p->c_in && p->in_sh % 4 == 0 && p->in_sb % 4 == 0);
+  UB_REQUIRE(!bias || (reinterpret_cast<uintptr_t>(bias) & 15) == 0);
+  UB_REQUIRE((reinterpret_cast<uintptr_t>(y) & 15) == 0 && (!p->res || (reinterpret_cast<uintptr_t>(p->res) & 15) == 0));
+  UB_REQUIRE(p->act != UNBLEND_ACT_GLU || p->n_out % 4 == 0);
   TcArgs a{};
   a.B = p->batch;
   a.H = p->h_out;

@@ -49,6 +49,8 @@ struct GemmArgs {
   long long ldo;
   const float* res;
   long long ldr;
+  const float2* rope;
+  int rope_cols, rope_hd, rope_div, rope_mod;
   GroupDesc g[UNBLEND_GEMM_MAX_GROUPS];
 };
 
@@ -354,6 +356,16 @@ __global__ void __launch_bounds__(GL<BN, MODE>::NT, 1)
           if (row >= a.m || nvalid <= 0) continue;
           float x[4] = {act_fn<ACT, FAST>(v.x + bv.x), act_fn<ACT, FAST>(v.y + bv.y),
                         act_fn<ACT, FAST>(v.z + bv.z), act_fn<ACT, FAST>(v.w + bv.w)};
+          if (ACT == UNBLEND_ACT_NONE && a.rope && ncol < a.rope_cols) {
+            const int pos = (int)((row / a.rope_div) % a.rope_mod);
+            const float2* cs = a.rope + (long long)pos * (a.rope_hd >> 1) + ((ncol % a.rope_hd) >> 1);
+            const float2 c0 = __ldg(cs), c1 = __ldg(cs + 1);
+            const float x0 = x[0], x1 = x[1], x2 = x[2], x3 = x[3];
+            x[0] = x0 * c0.x - x1 * c0.y;
+            x[1] = x0 * c0.y + x1 * c0.x;
+            x[2] = x2 * c1.x - x3 * c1.y;
+            x[3] = x2 * c1.y + x3 * c1.x;
+          }
           if (ACT == UNBLEND_ACT_GLU) {
             float o[2] = {x[0] * sigmoid_fn<FAST>(x[1]), x[2] * sigmoid_fn<FAST>(x[3])};
             store_vals<2, OBF>(a, row * a.ldo + oc, o, rv[k], ocnt);
@@ -518,6 +530,15 @@ extern "C" int unblend_gemm_tc(const void* a, long long lda, int rows, int a_col
   g.ldo = p->ldo;
   g.res = p->res;
   g.ldr = p->ldr;
+  if (p->rope) {
+    UB_REQUIRE(p->act == UNBLEND_ACT_NONE && p->rope_hd >= 4 && p->rope_hd % 4 == 0 && p->rope_cols % 4 == 0);
+    UB_REQUIRE(p->rope_div > 0 && p->rope_mod > 0 && (reinterpret_cast<uintptr_t>(p->rope) & 7) == 0);
+    g.rope = reinterpret_cast<const float2*>(p->rope);
+    g.rope_cols = p->rope_cols;
+    g.rope_hd = p->rope_hd;
+    g.rope_div = p->rope_div;
+    g.rope_mod = p->rope_mod;
+  }
   const int m_tiles = (rows + 127) / 128;
   long long tiles = 0;
   bool vec = (reinterpret_cast<uintptr_t>(p->out) & 15) == 0 && p->ldo % 4 == 0;

@@ -319,6 +319,8 @@ class HTDemucsCuda(nn.Module):
             if not (p.sw == 4 and p.kw == 8 and p.pw == 2 and p.kh == 1 and x.H == 1 and x.sb % (4 * x.C) == 0
                     and cap >= 4 * -(-x.W // 4) and (2 * x.C) % 32 == 0):
                 return False
+        if p.act == ACT_GLU and p.n_out % 4:
+            return False
         return all(v % 4 == 0 for v in (p.n_group, p.out_sb, p.out_sh, p.out_sw, p.out_sg, out_offset))
 
     def _tc_weight(self, w: torch.Tensor, mode: int) -> tuple[torch.Tensor, torch.Tensor | None]:

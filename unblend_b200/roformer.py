@@ -256,7 +256,8 @@ class BSRoformerCuda(nn.Module):
 
     # ------------------------------------------------------------------ launch helpers
     def _gemm(self, lin: _Linear, a: torch.Tensor, lda: int, rows: int, a_cols: int, out: torch.Tensor, ldo: int,
-              act: int = ACT_NONE, res: torch.Tensor | None = None, block_n: int = 256) -> None:
+              act: int = ACT_NONE, res: torch.Tensor | None = None, block_n: int = 256,
+              rope: tuple | None = None) -> None:
         mode = _lib.TC_BF16 if self.precision == "bf16" else _lib.TC_TF32X3
         for g0 in range(0, len(lin.groups), _lib.GEMM_MAX_GROUPS):
             chunk = lin.groups[g0:g0 + _lib.GEMM_MAX_GROUPS]
@@ -271,6 +272,9 @@ class BSRoformerCuda(nn.Module):
             p.out = out.data_ptr()
             p.ldo = ldo
             p.out_bf16 = 1 if out.dtype == torch.bfloat16 else 0
+            if rope is not None:
+                table, p.rope_cols, p.rope_hd, p.rope_div, p.rope_mod = rope
+                p.rope = table.data_ptr()
             work = rows * 2.0 * sum(n * k for _, _, n, k, _ in chunk)
             _lib.call("unblend_gemm_tc", a.data_ptr(), lda, rows, a_cols, lin.hi.data_ptr(), _lib.ptr(lin.lo),
                       lin.rows, lin.cols, ctypes.byref(p), mode, block_n, work=work)
@@ -289,8 +293,13 @@ class BSRoformerCuda(nn.Module):
         _lib.call("unblend_rms_norm", x.data_ptr(), rows, dim, self._vec[f"{p}.attn.gamma"].data_ptr(),
                   xn.data_ptr(), dim, 1 if xn.dtype == torch.bfloat16 else 0, self._vec[f"{p}.gates.w"].data_ptr(),
                   self._vec[f"{p}.gates.b"].data_ptr(), H, gates.data_ptr())
-        qkv = torch.empty(rows, 3 * inner, device=dev, dtype=torch.float32)
-        self._gemm(self._lin[f"{p}.qkv"], xn, dim, rows, dim, qkv, 3 * inner)
+        bf16 = self.precision == "bf16" and hd == 64
+        seq = T if axis == 0 else nb
+        rope = tabs[f"rope{axis}"]
+        qkv = torch.empty(rows, 3 * inner, device=dev, dtype=torch.bfloat16 if bf16 else torch.float32)
+        # bf16 path: the rotary rotation of Q and K is applied in the projection's epilogue.
+        self._gemm(self._lin[f"{p}.qkv"], xn, dim, rows, dim, qkv, 3 * inner,
+                   rope=(rope, 2 * inner, hd, nb if axis == 0 else 1, seq) if bf16 else None)
         o = torch.empty(rows, inner, device=dev, dtype=self._act_dtype())
         a = AttnParams()
         a.heads, a.hd = H, hd
@@ -300,25 +309,29 @@ class BSRoformerCuda(nn.Module):
             a.q_so, a.q_si, a.q_sr = T * nb * q3, q3, nb * q3
             a.o_so, a.o_si, a.o_sr = T * nb * inner, inner, nb * inner
             a.g_so, a.g_si, a.g_sr = T * nb * H, H, nb * H
-            seq = T
         else:  # sequences along bands, batch (b, frame)
             a.outer, a.inner, a.lq, a.lk = B * T, 1, nb, nb
             a.q_so, a.q_si, a.q_sr = nb * q3, 4, q3
             a.o_so, a.o_si, a.o_sr = nb * inner, 0, inner
             a.g_so, a.g_si, a.g_sr = nb * H, 0, H
-            seq = nb
+            if bf16:
+                a.q_si = 8
         a.kv_so, a.kv_si, a.kv_sr = a.q_so, a.q_si, a.q_sr
         a.out = o.data_ptr()
         a.out_bf16 = 1 if o.dtype == torch.bfloat16 else 0
         a.gate = gates.data_ptr()
-        rope = tabs[f"rope{axis}"]
-        a.rope = rope.data_ptr()
-        a.rope_len = seq
         a.scale = hd ** -0.5
-        mode = 1 if self.precision == "bf16" else 0
         base = qkv.data_ptr()
-        _lib.call("unblend_attention_tc2", base, base + 4 * inner, base + 8 * inner, ctypes.byref(a), mode,
-                  work=4.0 * a.outer * a.inner * H * seq * seq * hd)
+        work = 4.0 * a.outer * a.inner * H * seq * seq * hd
+        if bf16:
+            a.kv_si = a.q_si
+            _lib.call("unblend_attention_bf16", base, base + 2 * inner, base + 4 * inner, ctypes.byref(a), work=work)
+        else:
+            a.rope = rope.data_ptr()
+            a.rope_len = seq
+            mode = 1 if self.precision == "bf16" else 0
+            _lib.call("unblend_attention_tc2", base, base + 4 * inner, base + 8 * inner, ctypes.byref(a), mode,
+                      work=work)
         self._gemm(self._lin[f"{p}.out"], o, inner, rows, inner, x, dim, res=x)
 
     def _ff_layer(self, x: torch.Tensor, p: str, rows: int) -> None:
