@@ -393,8 +393,13 @@ def test_attention_bf16_axial_gate(axis, out_bf16):
     ref = (att * g.transpose(-1, -2).unsqueeze(-1)).transpose(-2, -3).flatten(-2)
     if axis == 0:
         ref = ref.permute(0, 2, 1, 3)
-    # P is rounded to bf16 (2^-9 relative) before the P V product
-    assert rel_err(o.float(), ref) < 2e-2
+    # P is rounded to bf16 (2^-9 relative) before the P V product. A float64
+    # emulation of exactly that rounding on these shapes gives a worst element of
+    # ~1.2e-2 of the output RMS (3.1e-2 with the bf16 output rounding: the gated
+    # outputs reach 14x their RMS) and ~1.5e-3 in RMS.
+    assert rel_err(o.float(), ref) < (6e-2 if out_bf16 else 4e-2)
+    err = (o.double() - ref).pow(2).mean().sqrt() / ref.pow(2).mean().sqrt()
+    assert err < 4e-3
     assert _lib.error_flag() == 0
 
 

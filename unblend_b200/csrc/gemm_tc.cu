@@ -27,6 +27,7 @@
 // from TMA into kind::f16 MMAs (no conversion pass).
 #include <cuda_bf16.h>
 #include <cudaTypedefs.h>
+#include <string.h>
 
 #include "common.cuh"
 #include "tc_common.cuh"
@@ -51,6 +52,7 @@ struct GemmArgs {
   long long ldr;
   const float2* rope;
   int rope_cols, rope_hd, rope_div, rope_mod;
+  int tma_store;  // 1: whole 32-column chunks leave through TMA bulk stores (no residual)
   GroupDesc g[UNBLEND_GEMM_MAX_GROUPS];
 };
 
@@ -87,6 +89,16 @@ __device__ __forceinline__ void decode_tile(const GemmArgs& a, int t, int& g, in
   m0 = (local / n_tiles) * 128;
   nt = local % n_tiles;
 }
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map), "r"(src),
+               "r"(x), "r"(y)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// Wait until every committed bulk store of this thread has finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 
 __device__ __forceinline__ float tanh_approx(float x) {
   float y;
@@ -172,7 +184,8 @@ __device__ __forceinline__ void store_vals(const GemmArgs& a, long long off, flo
 template <int BN, int MODE, int ACT, int OBF>
 __global__ void __launch_bounds__(GL<BN, MODE>::NT, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
-                   const __grid_constant__ CUtensorMap mapB2, const __grid_constant__ GemmArgs a) {
+                   const __grid_constant__ CUtensorMap mapB2, const __grid_constant__ CUtensorMap mapO,
+                   const __grid_constant__ GemmArgs a) {
   using L = GL<BN, MODE>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -297,11 +310,83 @@ __global__ void __launch_bounds__(GL<BN, MODE>::NT, 1)
       tc_fence_after();
       const long long row0 = (long long)m0 + q * 32;
       const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
+      // Rotary position of this lane's own TMEM row (the TMA-store path keeps lane = row).
+      const int my_row = (int)row0 + lane;
+      const int rope_pos = a.rope ? (my_row / a.rope_div) % a.rope_mod : 0;
 #pragma unroll 1
       for (int c0 = c_lo; c0 < c_lo + BN / 2; c0 += 32) {
         if (n0 + c0 >= gd.n) break;  // uniform across the warp
         uint32_t acc[32];
         tmem_ld32(base + (uint32_t)c0, acc);
+        if (a.tma_store && n0 + c0 + 32 <= gd.n) {
+          // Whole chunk: activation in the lane = row layout, packed into a
+          // swizzled staging tile, stored by one bulk tensor copy.
+          constexpr bool FAST = MODE == 1;
+          constexpr int NV = ACT == UNBLEND_ACT_GLU ? 16 : 32;      // values per row
+          constexpr int RB = NV * (OBF ? 2 : 4);                     // staging row bytes: 32, 64 or 128
+          constexpr int CH = RB / 16;                                // 16-byte chunks per row
+          float v[32];
+          if (a.bias) {
+            const float4* bp = reinterpret_cast<const float4*>(a.bias + gd.w_row0 + n0 + c0);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float4 b4 = __ldg(bp + j);
+              v[4 * j] = __uint_as_float(acc[4 * j]) + b4.x;
+              v[4 * j + 1] = __uint_as_float(acc[4 * j + 1]) + b4.y;
+              v[4 * j + 2] = __uint_as_float(acc[4 * j + 2]) + b4.z;
+              v[4 * j + 3] = __uint_as_float(acc[4 * j + 3]) + b4.w;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(acc[j]);
+          }
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = act_fn<ACT, FAST>(v[j]);
+          if (ACT == UNBLEND_ACT_NONE && a.rope && n0 + c0 < a.rope_cols) {
+            const float4* cs = reinterpret_cast<const float4*>(a.rope + (long long)rope_pos * (a.rope_hd >> 1) +
+                                                                (((n0 + c0) % a.rope_hd) >> 1));
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {  // pairs (4j, 4j+1) and (4j+2, 4j+3)
+              const float4 c2 = __ldg(cs + j);
+              const float x0 = v[4 * j], x1 = v[4 * j + 1], x2 = v[4 * j + 2], x3 = v[4 * j + 3];
+              v[4 * j] = x0 * c2.x - x1 * c2.y;
+              v[4 * j + 1] = x0 * c2.y + x1 * c2.x;
+              v[4 * j + 2] = x2 * c2.z - x3 * c2.w;
+              v[4 * j + 3] = x2 * c2.w + x3 * c2.z;
+            }
+          }
+          uint32_t w[OBF ? NV / 2 : NV];  // the packed row: NV/2 words of bf16 pairs, or NV fp32 words
+#pragma unroll
+          for (int j = 0; j < NV; ++j) {
+            const float o = ACT == UNBLEND_ACT_GLU ? v[2 * j] * sigmoid_fn<FAST>(v[2 * j + 1]) : v[j];
+            if (OBF) {
+              if (j & 1) {
+                __nv_bfloat162 b2 = __floats2bfloat162_rn(__uint_as_float(w[j >> 1]), o);
+                w[j >> 1] = *reinterpret_cast<uint32_t*>(&b2);
+              } else {
+                w[j >> 1] = __float_as_uint(o);
+              }
+            } else {
+              w[j] = __float_as_uint(o);
+            }
+          }
+          uint8_t* stg = epi_smem + e * EPI_TILE;
+          if (lane == 0) bulk_wait_read();  // the previous store has left the staging tile
+          __syncwarp();
+          const int swz = ((lane * RB) >> 7) & (CH - 1);
+#pragma unroll
+          for (int j = 0; j < CH; ++j)
+            *reinterpret_cast<uint4*>(stg + lane * RB + ((j ^ swz) << 4)) =
+                make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            const int x = gd.out_col0 + (ACT == UNBLEND_ACT_GLU ? (n0 + c0) / 2 : n0 + c0);
+            tma_store_2d(&mapO, smem_u32(stg), x, (int)row0);
+          }
+          continue;
+        }
+        if (a.tma_store && lane == 0) bulk_wait_read();
         __syncwarp();
 #pragma unroll
         for (int j = 0; j < 8; ++j)
@@ -357,7 +442,7 @@ __global__ void __launch_bounds__(GL<BN, MODE>::NT, 1)
           float x[4] = {act_fn<ACT, FAST>(v.x + bv.x), act_fn<ACT, FAST>(v.y + bv.y),
                         act_fn<ACT, FAST>(v.z + bv.z), act_fn<ACT, FAST>(v.w + bv.w)};
           if (ACT == UNBLEND_ACT_NONE && a.rope && ncol < a.rope_cols) {
-            const int pos = (int)((row / a.rope_div) % a.rope_mod);
+            const int pos = ((int)row / a.rope_div) % a.rope_mod;  // rows < 2^31 (checked on the host)
             const float2* cs = a.rope + (long long)pos * (a.rope_hd >> 1) + ((ncol % a.rope_hd) >> 1);
             const float2 c0 = __ldg(cs), c1 = __ldg(cs + 1);
             const float x0 = x[0], x1 = x[1], x2 = x[2], x3 = x[3];
@@ -378,6 +463,8 @@ __global__ void __launch_bounds__(GL<BN, MODE>::NT, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
+    if (a.tma_store && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    __syncwarp();
   } else if (MODE == 0) {
     // Converter warps: TF32 hi (in place) + lo split of each fp32 A tile.
     const int ct = threadIdx.x - 32 * CONV_W0;
@@ -460,44 +547,44 @@ int sm_count() {
 }
 
 template <int BN, int MODE, int ACT, int OBF>
-int launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb2, const GemmArgs& args,
-           cudaStream_t st) {
+int launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb2, const CUtensorMap& mo,
+           const GemmArgs& args, cudaStream_t st) {
   using L = GL<BN, MODE>;
   auto k = gemm_tc_kernel<BN, MODE, ACT, OBF>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
   int grid = sm_count();
   if (grid > args.total_tiles) grid = args.total_tiles;
-  k<<<grid, L::NT, L::SMEM, st>>>(ma, mb, mb2, args);
+  k<<<grid, L::NT, L::SMEM, st>>>(ma, mb, mb2, mo, args);
   UB_CHECK_LAUNCH();
   return 0;
 }
 
 template <int BN, int MODE>
 int dispatch_epi(int act, int obf, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb2,
-                 const GemmArgs& g, cudaStream_t st) {
+                 const CUtensorMap& mo, const GemmArgs& g, cudaStream_t st) {
   switch (act * 2 + obf) {
-    case UNBLEND_ACT_NONE * 2: return launch<BN, MODE, UNBLEND_ACT_NONE, 0>(ma, mb, mb2, g, st);
-    case UNBLEND_ACT_NONE * 2 + 1: return launch<BN, MODE, UNBLEND_ACT_NONE, 1>(ma, mb, mb2, g, st);
-    case UNBLEND_ACT_GELU * 2: return launch<BN, MODE, UNBLEND_ACT_GELU, 0>(ma, mb, mb2, g, st);
-    case UNBLEND_ACT_GELU * 2 + 1: return launch<BN, MODE, UNBLEND_ACT_GELU, 1>(ma, mb, mb2, g, st);
-    case UNBLEND_ACT_GLU * 2: return launch<BN, MODE, UNBLEND_ACT_GLU, 0>(ma, mb, mb2, g, st);
-    case UNBLEND_ACT_GLU * 2 + 1: return launch<BN, MODE, UNBLEND_ACT_GLU, 1>(ma, mb, mb2, g, st);
-    case UNBLEND_ACT_TANH * 2: return launch<BN, MODE, UNBLEND_ACT_TANH, 0>(ma, mb, mb2, g, st);
-    case UNBLEND_ACT_TANH * 2 + 1: return launch<BN, MODE, UNBLEND_ACT_TANH, 1>(ma, mb, mb2, g, st);
+    case UNBLEND_ACT_NONE * 2: return launch<BN, MODE, UNBLEND_ACT_NONE, 0>(ma, mb, mb2, mo, g, st);
+    case UNBLEND_ACT_NONE * 2 + 1: return launch<BN, MODE, UNBLEND_ACT_NONE, 1>(ma, mb, mb2, mo, g, st);
+    case UNBLEND_ACT_GELU * 2: return launch<BN, MODE, UNBLEND_ACT_GELU, 0>(ma, mb, mb2, mo, g, st);
+    case UNBLEND_ACT_GELU * 2 + 1: return launch<BN, MODE, UNBLEND_ACT_GELU, 1>(ma, mb, mb2, mo, g, st);
+    case UNBLEND_ACT_GLU * 2: return launch<BN, MODE, UNBLEND_ACT_GLU, 0>(ma, mb, mb2, mo, g, st);
+    case UNBLEND_ACT_GLU * 2 + 1: return launch<BN, MODE, UNBLEND_ACT_GLU, 1>(ma, mb, mb2, mo, g, st);
+    case UNBLEND_ACT_TANH * 2: return launch<BN, MODE, UNBLEND_ACT_TANH, 0>(ma, mb, mb2, mo, g, st);
+    case UNBLEND_ACT_TANH * 2 + 1: return launch<BN, MODE, UNBLEND_ACT_TANH, 1>(ma, mb, mb2, mo, g, st);
     default: return UNBLEND_ERR_INVALID;
   }
 }
 
 int dispatch_mode(int mode, int block_n, int act, int obf, const CUtensorMap& ma, const CUtensorMap& mb,
-                  const CUtensorMap& mb2, const GemmArgs& g, cudaStream_t st) {
+                  const CUtensorMap& mb2, const CUtensorMap& mo, const GemmArgs& g, cudaStream_t st) {
   if (mode == 0) {
-    if (block_n == 64) return dispatch_epi<64, 0>(act, obf, ma, mb, mb2, g, st);
-    if (block_n == 128) return dispatch_epi<128, 0>(act, obf, ma, mb, mb2, g, st);
-    return dispatch_epi<256, 0>(act, obf, ma, mb, mb2, g, st);
+    if (block_n == 64) return dispatch_epi<64, 0>(act, obf, ma, mb, mb2, mo, g, st);
+    if (block_n == 128) return dispatch_epi<128, 0>(act, obf, ma, mb, mb2, mo, g, st);
+    return dispatch_epi<256, 0>(act, obf, ma, mb, mb2, mo, g, st);
   }
-  if (block_n == 64) return dispatch_epi<64, 1>(act, obf, ma, mb, mb2, g, st);
-  if (block_n == 128) return dispatch_epi<128, 1>(act, obf, ma, mb, mb2, g, st);
-  return dispatch_epi<256, 1>(act, obf, ma, mb, mb2, g, st);
+  if (block_n == 64) return dispatch_epi<64, 1>(act, obf, ma, mb, mb2, mo, g, st);
+  if (block_n == 128) return dispatch_epi<128, 1>(act, obf, ma, mb, mb2, mo, g, st);
+  return dispatch_epi<256, 1>(act, obf, ma, mb, mb2, mo, g, st);
 }
 
 }  // namespace
@@ -539,7 +626,7 @@ extern "C" int unblend_gemm_tc(const void* a, long long lda, int rows, int a_col
     g.rope_div = p->rope_div;
     g.rope_mod = p->rope_mod;
   }
-  const int m_tiles = (rows + 127) / 128;
+  const int m_tiles = (rows + 127) / 128;  // rows is an int: row indices fit 32 bits
   long long tiles = 0;
   bool vec = (reinterpret_cast<uintptr_t>(p->out) & 15) == 0 && p->ldo % 4 == 0;
   if (p->res) vec = vec && (reinterpret_cast<uintptr_t>(p->res) & 15) == 0 && p->ldr % 4 == 0;
@@ -571,7 +658,30 @@ extern "C" int unblend_gemm_tc(const void* a, long long lda, int rows, int a_col
   } else {
     mb2 = mb;
   }
-  return dispatch_mode(mode, block_n, p->act, g.out_bf16, ma, mb, mb2, g, ub::as_stream(stream));
+  // Output tensor map for the bulk-store epilogue: [rows, ldo] with a box of one
+  // 32-row chunk (32 columns, 16 after GLU) and the swizzle matching its row bytes.
+  CUtensorMap mo;
+  memset(&mo, 0, sizeof(mo));
+  const int oesz = g.out_bf16 ? 2 : 4;
+  bool tma = !p->res && (reinterpret_cast<uintptr_t>(p->out) & 15) == 0 && (p->ldo * oesz) % 16 == 0;
+  for (int i = 0; i < p->groups && tma; ++i) tma = (p->group[i].out_col0 * oesz) % 16 == 0;
+  if (tma) {
+    const int nv = p->act == UNBLEND_ACT_GLU ? 16 : 32;
+    const int rb = nv * oesz;
+    const CUtensorMapSwizzle sw = rb == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                  : rb == 64  ? CU_TENSOR_MAP_SWIZZLE_64B
+                                              : CU_TENSOR_MAP_SWIZZLE_32B;
+    cuuint64_t dims[2] = {(cuuint64_t)p->ldo, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)p->ldo * oesz};
+    cuuint32_t box[2] = {(cuuint32_t)nv, 32};
+    cuuint32_t es[2] = {1, 1};
+    auto fn = encode_fn();
+    tma = fn && fn(&mo, g.out_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, p->out,
+                   dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  }
+  g.tma_store = tma ? 1 : 0;
+  return dispatch_mode(mode, block_n, p->act, g.out_bf16, ma, mb, mb2, mo, g, ub::as_stream(stream));
 }
 
 extern "C" int unblend_gemm_error_flag(int* out_host, int clear) {

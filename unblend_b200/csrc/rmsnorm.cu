@@ -32,6 +32,43 @@ __device__ __forceinline__ void store4(void* y, long long off, float4 v, int bf1
   }
 }
 
+// Sum each of v[0..15] over the warp; lane l ends up holding the total of
+// v[idx(l)] with idx(l) = 8*b4 + 4*b3 + 2*b2 + b1 (b_k = bit k of l), in 16
+// shuffles instead of 80 (a butterfly reduce-scatter).
+__device__ __forceinline__ float reduce16(float (&v)[16], int lane) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const bool up = lane & 16;
+    const float send = up ? v[i] : v[i + 8];
+    const float keep = up ? v[i + 8] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const bool up = lane & 8;
+    const float send = up ? v[i] : v[i + 4];
+    const float keep = up ? v[i + 4] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const bool up = lane & 4;
+    const float send = up ? v[i] : v[i + 2];
+    const float keep = up ? v[i + 2] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+  }
+  {
+    const bool up = lane & 2;
+    const float send = up ? v[0] : v[1];
+    const float keep = up ? v[1] : v[0];
+    v[0] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+  }
+  return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
+}
+
+// One warp normalises ROWS rows per iteration (independent loads in flight);
+// with gates, each gate weight read from shared memory serves all ROWS rows.
+template <int ROWS>
 __global__ void __launch_bounds__(256) rms_norm_kernel(const float* __restrict__ x, long long rows, int dim,
                                                        const float* __restrict__ gamma, void* __restrict__ y,
                                                        long long ldy, int y_bf16, const float* __restrict__ gw,
@@ -43,43 +80,79 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const float* __restrict__
   const int lane = threadIdx.x & 31;
   const int nv = dim >> 2;
   const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
-  for (long long r = blockIdx.x * (long long)(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
-    const float4* xr = reinterpret_cast<const float4*>(x + r * dim);
-    float4 v[kMaxVec];
-    float ss = 0.f;
+  const long long groups = (rows + ROWS - 1) / ROWS;
+  for (long long gi = blockIdx.x * (long long)(blockDim.x >> 5) + (threadIdx.x >> 5); gi < groups; gi += warps) {
+    const long long r0 = gi * ROWS;
+    float4 v[ROWS][kMaxVec];
+    float inv[ROWS];
 #pragma unroll
-    for (int i = 0; i < kMaxVec; ++i) {
-      const int c = lane + 32 * i;
-      v[i] = c < nv ? __ldg(xr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-      ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+    for (int k = 0; k < ROWS; ++k) {
+      const bool rv = r0 + k < rows;
+      const float4* xr = reinterpret_cast<const float4*>(x + (r0 + k) * dim);
+#pragma unroll
+      for (int i = 0; i < kMaxVec; ++i) {
+        const int c = lane + 32 * i;
+        v[k][i] = rv && c < nv ? __ldg(xr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
     }
-    ss = ub::warp_sum(ss);
-    const float inv = rsqrtf(ss / (float)dim + kEps);
-    float gacc[kMaxGates];
 #pragma unroll
-    for (int h = 0; h < kMaxGates; ++h) gacc[h] = 0.f;
+    for (int k = 0; k < ROWS; ++k) {
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < kMaxVec; ++i)
+        ss += v[k][i].x * v[k][i].x + v[k][i].y * v[k][i].y + v[k][i].z * v[k][i].z + v[k][i].w * v[k][i].w;
+      ss = ub::warp_sum(ss);
+      inv[k] = rsqrtf(ss / (float)dim + kEps);
+    }
 #pragma unroll
     for (int i = 0; i < kMaxVec; ++i) {
       const int c = lane + 32 * i;
       if (c < nv) {
         const float4 g = __ldg(reinterpret_cast<const float4*>(gamma) + c);
-        const float4 o = make_float4(v[i].x * inv * g.x, v[i].y * inv * g.y, v[i].z * inv * g.z, v[i].w * inv * g.w);
-        store4(y, r * ldy + 4 * c, o, y_bf16);
 #pragma unroll
-        for (int h = 0; h < kMaxGates; ++h) {
-          if (h < gates) {
-            const float4 w = *reinterpret_cast<const float4*>(s_gw + h * dim + 4 * c);
-            gacc[h] += o.x * w.x + o.y * w.y + o.z * w.z + o.w * w.w;
-          }
+        for (int k = 0; k < ROWS; ++k) {
+          v[k][i] = make_float4(v[k][i].x * inv[k] * g.x, v[k][i].y * inv[k] * g.y, v[k][i].z * inv[k] * g.z,
+                                v[k][i].w * inv[k] * g.w);
+          if (r0 + k < rows) store4(y, (r0 + k) * ldy + 4 * c, v[k][i], y_bf16);
         }
       }
     }
-    if (gates > 0) {
+    if (gates == 8 && ROWS == 2) {
+      float acc[16];
 #pragma unroll
-      for (int h = 0; h < kMaxGates; ++h) {
-        if (h < gates) {
-          const float s = ub::warp_sum(gacc[h]);
-          if (lane == h) gout[r * gates + h] = ub::sigmoidf_(s + __ldg(gb + h));
+      for (int q = 0; q < 16; ++q) acc[q] = 0.f;
+#pragma unroll
+      for (int i = 0; i < kMaxVec; ++i) {
+        const int c = lane + 32 * i;
+        if (c < nv) {
+#pragma unroll
+          for (int h = 0; h < 8; ++h) {
+            const float4 w = *reinterpret_cast<const float4*>(s_gw + h * dim + 4 * c);
+#pragma unroll
+            for (int k = 0; k < ROWS; ++k)
+              acc[k * 8 + h] += v[k][i].x * w.x + v[k][i].y * w.y + v[k][i].z * w.z + v[k][i].w * w.w;
+          }
+        }
+      }
+      const float tot = reduce16(acc, lane);
+      const int idx = ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
+      const int k = idx >> 3, h = idx & 7;
+      if ((lane & 1) == 0 && r0 + k < rows) gout[(r0 + k) * 8 + h] = ub::sigmoidf_(tot + __ldg(gb + h));
+    } else if (gates > 0) {
+#pragma unroll
+      for (int k = 0; k < ROWS; ++k) {
+        for (int h = 0; h < gates; ++h) {
+          float acc = 0.f;
+#pragma unroll
+          for (int i = 0; i < kMaxVec; ++i) {
+            const int c = lane + 32 * i;
+            if (c < nv) {
+              const float4 w = *reinterpret_cast<const float4*>(s_gw + h * dim + 4 * c);
+              acc += v[k][i].x * w.x + v[k][i].y * w.y + v[k][i].z * w.z + v[k][i].w * w.w;
+            }
+          }
+          acc = ub::warp_sum(acc);
+          if (lane == 0 && r0 + k < rows) gout[(r0 + k) * gates + h] = ub::sigmoidf_(acc + __ldg(gb + h));
         }
       }
     }
@@ -129,11 +202,11 @@ extern "C" int unblend_rms_norm(const float* x, long long rows, int dim, const f
   const size_t smem = (size_t)gates * dim * sizeof(float);
   UB_REQUIRE(smem <= 200 * 1024);
   if (smem > 48 * 1024)
-    cudaFuncSetAttribute(rms_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  const long long blocks_needed = (rows + 7) / 8;
-  const unsigned grid = (unsigned)(blocks_needed < 148LL * 16 ? blocks_needed : 148LL * 16);
-  rms_norm_kernel<<<grid, 256, smem, ub::as_stream(stream)>>>(x, rows, dim, gamma, y, ldy, y_bf16 ? 1 : 0, gate_w,
-                                                              gate_b, gates, gate_out);
+    cudaFuncSetAttribute(rms_norm_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const long long blocks_needed = (rows + 15) / 16;
+  const unsigned grid = (unsigned)(blocks_needed < 148LL * 8 ? blocks_needed : 148LL * 8);
+  rms_norm_kernel<2><<<grid, 256, smem, ub::as_stream(stream)>>>(x, rows, dim, gamma, y, ldy, y_bf16 ? 1 : 0, gate_w,
+                                                                 gate_b, gates, gate_out);
   UB_CHECK_LAUNCH();
   return 0;
 }
