@@ -7,10 +7,14 @@
 // the channels-last input (C, W, H, B) at the tap's shifted coordinates; the
 // hardware's out-of-bounds zero fill implements the convolution padding.
 //
-// Warp roles (192 threads, one 128 x BN output tile per CTA):
+// Persistent: one CTA per SM walks the 128 x BN output tiles in a grid-stride
+// loop, with the accumulator double-buffered in TMEM (2 x BN columns) so the
+// epilogue of one tile overlaps the main loop of the next.
+// Warp roles (320 threads):
 //   warp 0    TMA producer (one elected lane)
 //   warp 1    TMEM allocation + MMA issue (one elected lane)
-//   warps 2-5 operand conversion in shared memory, then the epilogue
+//   warps 2-5 operand conversion in shared memory
+//   warps 6-9 epilogue
 // fp32 mode: each fp32 A tile is split in place into a TF32 "hi" part and a
 // residual "lo" tile; weights come pre-split; D += Ahi*Bhi + Ahi*Blo + Alo*Bhi
 // (3 x kind::tf32) keeps fp32-level accuracy. bf16 mode: the fp32 A tile is
@@ -29,9 +33,10 @@ namespace {
 using namespace ub::tc;
 
 constexpr int MAXT = 16;
-constexpr int NT = 192;
+constexpr int NT = 320;
 
 struct TcArgs {
+  long long tiles;
   int B, H, W_out;
   int m_valid, m_box;
   int tiles_w, tiles_n;
@@ -64,6 +69,24 @@ struct Layout {
 
 __device__ __forceinline__ float gelu(float x) { return ub::gelu_erf(x); }
 
+struct TileCoord {
+  int b, h, w0, n0;
+};
+
+// Tile t -> (batch, output row h, first output position w0, first channel n0);
+// channel tiles fastest so that concurrently running CTAs share the input rows.
+template <int BN>
+__device__ __forceinline__ TileCoord tile_coord(const TcArgs& a, long long t) {
+  TileCoord c;
+  c.n0 = (int)(t % a.tiles_n) * BN;
+  const long long m_tile = t / a.tiles_n;
+  c.w0 = (int)(m_tile % a.tiles_w) * a.m_valid;
+  const long long t2 = m_tile / a.tiles_w;
+  c.h = (int)(t2 % a.H);
+  c.b = (int)(t2 / a.H);
+  return c;
+}
+
 template <int BN, int MODE>
 __global__ void __launch_bounds__(NT, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
@@ -75,20 +98,13 @@ __global__ void __launch_bounds__(NT, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(epi_smem + L::EPI_BYTES);
   uint64_t* conv = full + L::STAGES;
   uint64_t* empty = conv + L::STAGES;
-  uint64_t* accum = empty + L::STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  uint64_t* acc_full = empty + L::STAGES;  // [2]
+  uint64_t* acc_empty = acc_full + 2;      // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const long long tile = blockIdx.x;
-  const int n_tile = (int)(tile % a.tiles_n);
-  const long long m_tile = tile / a.tiles_n;
-  const int tw = (int)(m_tile % a.tiles_w);
-  const long long t2 = m_tile / a.tiles_w;
-  const int h = (int)(t2 % a.H);
-  const int b = (int)(t2 / a.H);
-  const int w0 = tw * a.m_valid;
-  const int n0 = n_tile * BN;
+  const long long tiles = a.tiles;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < L::STAGES; ++s) {
@@ -96,10 +112,13 @@ __global__ void __launch_bounds__(NT, 1)
       mbar_init(&conv[s], 4);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accum, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 4);
+    }
     fence_mbar_init();
   }
-  if (warp == 1) tmem_alloc(tmem_slot, BN);
+  if (warp == 1) tmem_alloc(tmem_slot, 2 * BN);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -111,21 +130,25 @@ __global__ void __launch_bounds__(NT, 1)
       const uint32_t bytes = (uint32_t)(a.m_box * 128 + L::B_TILES * L::B_BYTES);
       int it = 0;
       bool ok = true;
-      for (int t = 0; t < a.ntaps && ok; ++t) {
-        const int ca = a.tap_c0[t], wa = w0 + a.tap_dw[t], ha = h * a.a_sh + a.tap_dh[t], kb = a.tap_k0[t];
-        for (int cc = 0; cc < a.tap_clen[t] && ok; cc += 32, ++it) {
-          const int s = it % L::STAGES;
-          const int r = it / L::STAGES;
-          if (r > 0 && !mbar_wait(&empty[s], (r - 1) & 1)) {
-            ok = false;
-            break;
+      for (long long t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        const TileCoord c = tile_coord<BN>(a, t);
+        for (int tap = 0; tap < a.ntaps && ok; ++tap) {
+          const int ca = a.tap_c0[tap], wa = c.w0 + a.tap_dw[tap], ha = c.h * a.a_sh + a.tap_dh[tap];
+          const int kb = a.tap_k0[tap];
+          for (int cc = 0; cc < a.tap_clen[tap] && ok; cc += 32, ++it) {
+            const int s = it % L::STAGES;
+            const int r = it / L::STAGES;
+            if (r > 0 && !mbar_wait(&empty[s], (r - 1) & 1)) {
+              ok = false;
+              break;
+            }
+            uint8_t* st = smem + s * L::STAGE;
+            mbar_expect_tx(&full[s], bytes);
+            tma_load_4d(st, &mapA, &full[s], ca + cc, wa, ha, c.b);
+            uint8_t* sb = st + L::A_BYTES + L::AC_BYTES;
+            tma_load_2d(sb, &mapB, &full[s], kb + cc, c.n0);
+            if (MODE == 0) tma_load_2d(sb + L::B_BYTES, &mapB2, &full[s], kb + cc, c.n0);
           }
-          uint8_t* st = smem + s * L::STAGE;
-          mbar_expect_tx(&full[s], bytes);
-          tma_load_4d(st, &mapA, &full[s], ca + cc, wa, ha, b);
-          uint8_t* sb = st + L::A_BYTES + L::AC_BYTES;
-          tma_load_2d(sb, &mapB, &full[s], kb + cc, n0);
-          if (MODE == 0) tma_load_2d(sb + L::B_BYTES, &mapB2, &full[s], kb + cc, n0);
         }
       }
     }
@@ -133,108 +156,123 @@ __global__ void __launch_bounds__(NT, 1)
     if (lane == 0) {
       constexpr uint32_t idesc = instr_desc(MODE == 0 ? 2u : 1u, (uint32_t)BN);
       bool ok = true;
-      for (int it = 0; it < nk; ++it) {
-        const int s = it % L::STAGES;
-        const int r = it / L::STAGES;
-        if (!mbar_wait(&conv[s], r & 1)) {
+      int it = 0, i = 0;
+      for (long long t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++i) {
+        const int buf = i & 1, u = i >> 1;
+        if (u > 0 && !mbar_wait(&acc_empty[buf], (u - 1) & 1)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        uint8_t* st = smem + s * L::STAGE;
-        const uint32_t sa = smem_u32(st);
-        const uint32_t sac = sa + L::A_BYTES;
-        const uint32_t sb = sac + L::AC_BYTES;
-        if (MODE == 0) {
+        const uint32_t d = tmem + (uint32_t)(buf * BN);
+        for (int kc = 0; kc < nk; ++kc, ++it) {
+          const int s = it % L::STAGES;
+          const int r = it / L::STAGES;
+          if (!mbar_wait(&conv[s], r & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          uint8_t* st = smem + s * L::STAGE;
+          const uint32_t sa = smem_u32(st);
+          const uint32_t sac = sa + L::A_BYTES;
+          const uint32_t sb = sac + L::AC_BYTES;
+          if (MODE == 0) {
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const uint64_t dah = smem_desc(sa + 32 * j, 128), dal = smem_desc(sac + 32 * j, 128);
-            const uint64_t dbh = smem_desc(sb + 32 * j, 128), dbl = smem_desc(sb + L::B_BYTES + 32 * j, 128);
-            umma_tf32(tmem, dah, dbh, idesc, (it > 0 || j > 0) ? 1u : 0u);
-            umma_tf32(tmem, dah, dbl, idesc, 1u);
-            umma_tf32(tmem, dal, dbh, idesc, 1u);
+            for (int j = 0; j < 4; ++j) {
+              const uint64_t dah = smem_desc(sa + 32 * j, 128), dal = smem_desc(sac + 32 * j, 128);
+              const uint64_t dbh = smem_desc(sb + 32 * j, 128), dbl = smem_desc(sb + L::B_BYTES + 32 * j, 128);
+              umma_tf32(d, dah, dbh, idesc, (kc > 0 || j > 0) ? 1u : 0u);
+              umma_tf32(d, dah, dbl, idesc, 1u);
+              umma_tf32(d, dal, dbh, idesc, 1u);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              const uint64_t da = smem_desc(sac + 32 * j, 64), db = smem_desc(sb + 32 * j, 64);
+              umma_bf16(d, da, db, idesc, (kc > 0 || j > 0) ? 1u : 0u);
+            }
+          }
+          umma_commit(&empty[s]);
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[buf]);
+      }
+      if (!ok) atomicExch(&g_error_flag, 2);
+    }
+  } else if (warp < 6) {
+    // Converter warps 2-5: split / pack each landed A tile for the MMA.
+    const int ct = threadIdx.x - 64;  // 0..127
+    int it = 0;
+    bool ok = true;
+    for (long long t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+      for (int kc = 0; kc < nk; ++kc, ++it) {
+        const int s = it % L::STAGES;
+        const int r = it / L::STAGES;
+        if (!mbar_wait(&full[s], r & 1)) {
+          ok = false;
+          break;
+        }
+        uint8_t* st = smem + s * L::STAGE;
+        if (MODE == 0) {
+          float4* hi = reinterpret_cast<float4*>(st);
+          float4* lo = reinterpret_cast<float4*>(st + L::A_BYTES);
+#pragma unroll
+          for (int k = ct; k < 1024; k += 128) {
+            const float4 v = hi[k];
+            // hi = v rounded to the nearest TF32 value (ties away from zero), lo = v - hi exactly.
+            float4 vh;
+            vh.x = __uint_as_float((__float_as_uint(v.x) + 0x1000u) & 0xFFFFE000u);
+            vh.y = __uint_as_float((__float_as_uint(v.y) + 0x1000u) & 0xFFFFE000u);
+            vh.z = __uint_as_float((__float_as_uint(v.z) + 0x1000u) & 0xFFFFE000u);
+            vh.w = __uint_as_float((__float_as_uint(v.w) + 0x1000u) & 0xFFFFE000u);
+            hi[k] = vh;
+            lo[k] = make_float4(v.x - vh.x, v.y - vh.y, v.z - vh.z, v.w - vh.w);
           }
         } else {
+          const uint8_t* src = st;
+          uint8_t* dst = st + L::A_BYTES;
 #pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            const uint64_t da = smem_desc(sac + 32 * j, 64), db = smem_desc(sb + 32 * j, 64);
-            umma_bf16(tmem, da, db, idesc, (it > 0 || j > 0) ? 1u : 0u);
+          for (int k = ct; k < 1024; k += 128) {
+            const int row = k >> 3, c = k & 7;
+            const float4 v = *reinterpret_cast<const float4*>(src + row * 128 + ((c ^ (row & 7)) << 4));
+            __nv_bfloat162 p0 = __floats2bfloat162_rn(v.x, v.y);
+            __nv_bfloat162 p1 = __floats2bfloat162_rn(v.z, v.w);
+            uint2 packed;
+            packed.x = *reinterpret_cast<uint32_t*>(&p0);
+            packed.y = *reinterpret_cast<uint32_t*>(&p1);
+            *reinterpret_cast<uint2*>(dst + row * 64 + (((c >> 1) ^ ((row >> 1) & 3)) << 4) + (c & 1) * 8) = packed;
           }
         }
-        umma_commit(&empty[s]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&conv[s]);
       }
-      if (ok) umma_commit(accum);
-      else atomicExch(&g_error_flag, 2);
     }
   } else {
-    // Converter warps: split / pack each landed A tile for the MMA.
-    const int ct = threadIdx.x - 64;  // 0..127
-    bool ok = true;
-    for (int it = 0; it < nk; ++it) {
-      const int s = it % L::STAGES;
-      const int r = it / L::STAGES;
-      if (!mbar_wait(&full[s], r & 1)) {
-        ok = false;
-        break;
-      }
-      uint8_t* st = smem + s * L::STAGE;
-      if (MODE == 0) {
-        float4* hi = reinterpret_cast<float4*>(st);
-        float4* lo = reinterpret_cast<float4*>(st + L::A_BYTES);
-#pragma unroll
-        for (int i = ct; i < 1024; i += 128) {
-          float4 v = hi[i];
-          // hi = v rounded to the nearest TF32 value (ties away from zero),
-          // lo = v - hi exactly.
-          float4 vh, vl;
-          vh.x = __uint_as_float((__float_as_uint(v.x) + 0x1000u) & 0xFFFFE000u);
-          vh.y = __uint_as_float((__float_as_uint(v.y) + 0x1000u) & 0xFFFFE000u);
-          vh.z = __uint_as_float((__float_as_uint(v.z) + 0x1000u) & 0xFFFFE000u);
-          vh.w = __uint_as_float((__float_as_uint(v.w) + 0x1000u) & 0xFFFFE000u);
-          vl.x = v.x - vh.x;
-          vl.y = v.y - vh.y;
-          vl.z = v.z - vh.z;
-          vl.w = v.w - vh.w;
-          hi[i] = vh;
-          lo[i] = vl;
-        }
-      } else {
-        const uint8_t* src = st;
-        uint8_t* dst = st + L::A_BYTES;
-#pragma unroll
-        for (int i = ct; i < 1024; i += 128) {
-          const int row = i >> 3, c = i & 7;
-          const float4 v = *reinterpret_cast<const float4*>(src + row * 128 + ((c ^ (row & 7)) << 4));
-          __nv_bfloat162 p0 = __floats2bfloat162_rn(v.x, v.y);
-          __nv_bfloat162 p1 = __floats2bfloat162_rn(v.z, v.w);
-          uint2 packed;
-          packed.x = *reinterpret_cast<uint32_t*>(&p0);
-          packed.y = *reinterpret_cast<uint32_t*>(&p1);
-          *reinterpret_cast<uint2*>(dst + row * 64 + (((c >> 1) ^ ((row >> 1) & 3)) << 4) + (c & 1) * 8) = packed;
-        }
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&conv[s]);
-    }
-    // Epilogue: TMEM -> registers -> shared-memory transpose -> fused ops ->
-    // global. After the transpose each lane owns 4 consecutive output channels
-    // of 8 rows, so bias / scale loads are one float4 per lane and each store
-    // instruction of the warp writes 4 whole row segments.
-    ok = __all_sync(0xffffffffu, ok && mbar_wait(accum, 0));
-    tc_fence_after();
-    if (ok) {
-      const int q = warp & 3;
-      float4* stage = reinterpret_cast<float4*>(epi_smem + (warp - 2) * 4096);
-      const int ch = lane & 7;
-      const bool glu = a.act == UNBLEND_ACT_GLU;
+    // Epilogue warps 6-9: TMEM -> registers -> shared-memory transpose -> fused
+    // ops -> global. After the transpose each lane owns 4 consecutive output
+    // channels of 8 rows, so bias / scale loads are one float4 per lane and
+    // each store instruction of the warp writes 4 whole row segments.
+    const int q = warp & 3;  // TMEM lane quarter this warp may read
+    float4* stage = reinterpret_cast<float4*>(epi_smem + (warp - 6) * 4096);
+    const int ch = lane & 7;
+    const bool glu = a.act == UNBLEND_ACT_GLU;
+    int i = 0;
+    for (long long t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
+      const TileCoord tc = tile_coord<BN>(a, t);
+      const int b = tc.b, h = tc.h, w0 = tc.w0, n0 = tc.n0;
+      const int buf = i & 1, u = i >> 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[buf], u & 1))) break;
+      tc_fence_after();
+      const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
       double s1 = 0.0, s2 = 0.0;  // per-lane statistics: fp32 partials of 4 values, summed in double
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         if (n0 + c0 >= a.n_out) break;  // uniform across the warp
         uint32_t acc[32];
         __syncwarp();
-        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, acc);
+        tmem_ld32(base + (uint32_t)c0, acc);
 #pragma unroll
         for (int j = 0; j < 8; ++j)
           stage[lane * 8 + (j ^ (lane & 7))] =
@@ -256,6 +294,7 @@ __global__ void __launch_bounds__(NT, 1)
         const int nb = glu ? n / 2 : n;  // first output channel
         const int ocnt = glu ? nvalid / 2 : nvalid;
         const long long goff = (long long)(nb / a.n_group) * a.out_sg + (nb % a.n_group);
+        const long long rowbase = (long long)b * a.out_sb + (long long)h * a.out_sh + goff;
         float4 sc = make_float4(1.f, 1.f, 1.f, 1.f);
         if (a.res && a.res_scale && ocnt > 0) {
           sc.x = __ldg(a.res_scale + nb);
@@ -271,8 +310,7 @@ __global__ void __launch_bounds__(NT, 1)
           const int row = q * 32 + k * 4 + (lane >> 3);
           const int wpos = w0 + row;
           if (a.res && ocnt > 0 && row < a.m_valid && wpos < a.W_out) {
-            const float* rp = a.res + (long long)b * a.out_sb + (long long)h * a.out_sh +
-                              (long long)wpos * a.out_sw + goff;
+            const float* rp = a.res + rowbase + (long long)wpos * a.out_sw;
             if (ocnt == 4) {
               rv[k] = *reinterpret_cast<const float4*>(rp);
             } else {
@@ -311,7 +349,7 @@ __global__ void __launch_bounds__(NT, 1)
             o[2] = rv[k].z + sc.z * o[2];
             o[3] = rv[k].w + sc.w * o[3];
           }
-          float* yp = a.y + (long long)b * a.out_sb + (long long)h * a.out_sh + (long long)wpos * a.out_sw + goff;
+          float* yp = a.y + rowbase + (long long)wpos * a.out_sw;
           if (ocnt == 4) {
             *reinterpret_cast<float4*>(yp) = make_float4(o[0], o[1], o[2], o[3]);
           } else if (ocnt == 2 && glu) {
@@ -333,6 +371,10 @@ __global__ void __launch_bounds__(NT, 1)
           s2 += t2;
         }
       }
+      // The accumulator buffer is free once every lane has read its columns.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
       if (a.stats) {
         s1 = ub::warp_sum_d(s1);
         s2 = ub::warp_sum_d(s2);
@@ -348,7 +390,7 @@ __global__ void __launch_bounds__(NT, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, BN);
+    tmem_dealloc(tmem, 2 * BN);
   }
 }
 
@@ -383,7 +425,10 @@ int launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb2,
   using L = Layout<BN, MODE>;
   auto k = conv_tc_kernel<BN, MODE>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
-  k<<<(unsigned)tiles, NT, L::SMEM, st>>>(ma, mb, mb2, args);
+  int dev = 0, sms = ub::kNumSMs;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const unsigned grid = (unsigned)(tiles < sms ? tiles : sms);
+  k<<<grid, NT, L::SMEM, st>>>(ma, mb, mb2, args);
   UB_CHECK_LAUNCH();
   return 0;
 }
@@ -528,6 +573,7 @@ extern "C" int unblend_conv2d_tc(const float* x, const void* w_hi, const void* w
   }
   const long long tiles = (long long)p->batch * p->h_out * a.tiles_w * a.tiles_n;
   UB_REQUIRE(tiles > 0 && tiles < (1LL << 31));
+  a.tiles = tiles;
   cudaStream_t st = ub::as_stream(stream);
   if (mode == 0) {
     if (block_n == 64) return launch<64, 0>(ma, mb, mb2, a, tiles, st);
