@@ -60,6 +60,9 @@ def _args():
     ap.add_argument("--seconds", type=float, default=None,
                     help="track length per rank (smaller values are for profiling only)")
     ap.add_argument("--batch", type=int, default=None, help="segments per forward")
+    ap.add_argument("--split-track", action="store_true",
+                    help="N>1: all ranks separate the same track, its segments sharded across ranks with the "
+                         "overlap-strip exchange (strong scaling); default: one track per rank (weak scaling)")
     args = ap.parse_args()
     rof = args.model == "bsroformer"
     if args.precision is None:
@@ -238,9 +241,15 @@ def main() -> None:
         seg_len = model.segment_length
     n_stems = len(model.sources)
     seconds, batch = args.seconds, args.batch
-    track = synth_track(seconds, 1 + rank)
+    split = args.split_track and world > 1
+    track = synth_track(seconds, 1 if split else 1 + rank)
     track_dev = track.to(dev)
-    step = lambda: apply_model(model, track_dev, chunk_batch_size=batch)  # noqa: E731
+    if split:
+        from unblend_b200.distributed import apply_model_sharded
+
+        step = lambda: apply_model_sharded(model, track_dev, chunk_batch_size=batch, gather=False)  # noqa: E731
+    else:
+        step = lambda: apply_model(model, track_dev, chunk_batch_size=batch)  # noqa: E731
 
     for _ in range(args.warmup):
         step()
@@ -274,7 +283,13 @@ def main() -> None:
 
     # End to end through the public API with a pinned host track.
     host = track.pin_memory()
-    e2e_step = lambda: apply_model(model, host, device=dev, chunk_batch_size=batch)  # noqa: E731
+    if split:
+        def e2e_step():
+            out = apply_model_sharded(model, host.to(dev, non_blocking=True), chunk_batch_size=batch, gather=True)
+            if rank == 0:
+                out.to("cpu")
+    else:
+        e2e_step = lambda: apply_model(model, host, device=dev, chunk_batch_size=batch)  # noqa: E731
     e2e_step()
     e2e_ms = timed(e2e_step, max(1, args.steps))
 
@@ -299,8 +314,9 @@ def main() -> None:
                 "share_of_step": round(a["ms"] / sum(v["ms"] for v in agg.values()), 3),
                 "launches_per_step": a["n"]}
 
-    value = world * seconds / (ms * 1e-3)
-    e2e_value = world * seconds / (e2e_ms * 1e-3)
+    tracks = 1 if split else world
+    value = tracks * seconds / (ms * 1e-3)
+    e2e_value = tracks * seconds / (e2e_ms * 1e-3)
     L = track.shape[-1]
     n_seg = len(range(0, L, int(0.75 * seg_len)))
     dtype = {"fp32": "f32", "bf16": "bf16", "fp32-simt": "f32"}[args.precision]
@@ -312,10 +328,11 @@ def main() -> None:
                 f"overlap 0.25, {batch} segments per launch, precision {args.precision}")
     line = {"metric": METRIC, "value": round(value, 3), "unit": "audio-s/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": dtype, "data": "synthetic",
+            "scaling": "strong" if split else "weak", "vs_baseline": None, "dtype": dtype, "data": "synthetic",
             "config": {"workload": work,
                        "track_seconds": seconds, "segments_per_launch": batch, "precision": args.precision,
-                       "parallelism": f"whole tracks per rank x{world}",
+                       "parallelism": (f"one track, segments sharded over {world} ranks + NCCL strip exchange"
+                                       if split else f"whole tracks per rank x{world}"),
                        "l2": "inputs and activations far larger than L2 (no flush needed)"},
             "e2e": {"value": round(e2e_value, 3), "unit": "audio-s/s", "h2d_bytes_per_step": 2 * L * 4,
                     "d2h_bytes_per_step": n_stems * 2 * L * 4},

@@ -37,21 +37,19 @@ def _segment_plan(model: Any, overlap: float) -> tuple[int, int]:
     return segment, stride
 
 
-def _apply_unshifted(model: Callable, mix: torch.Tensor, n_sources: int, segment: int, stride: int,
-                     chunk_batch_size: int, progress_callback: Callable | None) -> torch.Tensor:
-    """One ``[C, L]`` device track -> ``[S, C, L]`` (unblend/apply.py:1009-1333)."""
+def _accumulate(model: Callable, mix: torch.Tensor, n_sources: int, segment: int, offsets: list[int],
+                off_dev: torch.Tensor, chunk_batch_size: int, acc: torch.Tensor, sum_w: torch.Tensor,
+                progress: Callable[[int], None] | None = None) -> None:
+    """Separate the chunks starting at ``offsets`` and overlap-add them into ``acc``/``sum_w``.
+
+    ``acc`` is ``[S*C, L]`` and ``sum_w`` ``[L]`` over the whole track (only the
+    positions the chunks touch are written); ``off_dev`` holds ``offsets`` as
+    int64 on the device (unblend/apply.py:1155-1238).
+    """
     C, L = mix.shape
     dev = mix.device
-    offsets = list(range(0, L, stride))
-    off_dev = torch.tensor(offsets, device=dev, dtype=torch.int64)
-    acc = torch.zeros(n_sources * C, L, device=dev, dtype=torch.float32)
-    sum_w = torch.zeros(L, device=dev, dtype=torch.float32)
     fixed = bool(getattr(model, "_fixed_batch_shape", False))
     total = len(offsets)
-    if progress_callback:
-        progress_callback("processing_start", {"total_chunks": total, "total_inputs": 1,
-                                               "input_total_chunks": [total]})
-    done = 0
     for i in range(0, total, chunk_batch_size):
         n = min(chunk_batch_size, total - i)
         rows = chunk_batch_size if fixed else n
@@ -68,13 +66,34 @@ def _apply_unshifted(model: Callable, mix: torch.Tensor, n_sources: int, segment
         hi = min(L, offsets[i + n - 1] + segment)
         _lib.call("unblend_overlap_add", y.data_ptr(), n, n_sources * C, segment, offp, L, lo, hi,
                   acc.data_ptr(), sum_w.data_ptr())
-        if progress_callback:
+        if progress is not None:
+            progress(n)
+
+
+def _apply_unshifted(model: Callable, mix: torch.Tensor, n_sources: int, segment: int, stride: int,
+                     chunk_batch_size: int, progress_callback: Callable | None) -> torch.Tensor:
+    """One ``[C, L]`` device track -> ``[S, C, L]`` (unblend/apply.py:1009-1333)."""
+    C, L = mix.shape
+    dev = mix.device
+    offsets = list(range(0, L, stride))
+    off_dev = torch.tensor(offsets, device=dev, dtype=torch.int64)
+    acc = torch.zeros(n_sources * C, L, device=dev, dtype=torch.float32)
+    sum_w = torch.zeros(L, device=dev, dtype=torch.float32)
+    total = len(offsets)
+    progress = None
+    if progress_callback:
+        progress_callback("processing_start", {"total_chunks": total, "total_inputs": 1,
+                                               "input_total_chunks": [total]})
+        done = [0]
+
+        def progress(n: int) -> None:
             torch.cuda.synchronize(dev)
             for _ in range(n):
-                done += 1
-                progress_callback("chunk_complete", {"completed_chunks": done, "total_chunks": total,
-                                                     "input_index": 0, "input_completed_chunks": done,
+                done[0] += 1
+                progress_callback("chunk_complete", {"completed_chunks": done[0], "total_chunks": total,
+                                                     "input_index": 0, "input_completed_chunks": done[0],
                                                      "input_total_chunks": total})
+    _accumulate(model, mix, n_sources, segment, offsets, off_dev, chunk_batch_size, acc, sum_w, progress)
     out = torch.empty_like(acc)
     _lib.call("unblend_divide", acc.data_ptr(), sum_w.data_ptr(), out.data_ptr(), n_sources * C, L)
     if progress_callback:
