@@ -96,3 +96,27 @@ def test_apply_model_matches_reference(key, shifts):
     out = apply_model(m, g["mix"].cuda(), shifts=shifts, overlap=g["overlap"],
                       chunk_batch_size=g["chunk_batch_size"], shift_offsets=g[key].get("offsets"))
     assert rel_err(out.cpu()[..., :: g["decimate"]], g[key]["out"]) < FP32_TOL
+
+
+def test_compiled_core_replays_cuda_graphs():
+    """enable_compiled_core: the captured launch sequence reproduces the eager forward; tails are zero-padded."""
+    from unblend_b200.apply import apply_model
+
+    g = golden("htdemucs_small.pt")
+    m = _model(g)
+    mix = g["mix"].cuda()
+    eager = m(mix)
+    m.enable_compiled_core()
+    assert m._fixed_batch_shape
+    first = m(mix)
+    second = m(mix * 0.5)
+    assert torch.equal(first, eager)
+    assert torch.equal(second, m.__dict__["_graphed"].fn(mix.float().contiguous() * 0.5)[..., : mix.shape[-1]])
+    m.disable_compiled_core()
+    assert not m._fixed_batch_shape and "_graphed" not in m.__dict__
+    ga = golden("apply_small.pt")
+    ma = _model(ga)
+    ma.enable_compiled_core()
+    out = apply_model(ma, ga["mix"].cuda(), overlap=ga["overlap"], chunk_batch_size=ga["chunk_batch_size"])
+    assert rel_err(out.cpu()[..., :: ga["decimate"]], ga["shifts0"]["out"]) < FP32_TOL
+    assert _lib.error_flag() == 0

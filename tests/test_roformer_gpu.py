@@ -436,3 +436,15 @@ def test_gemm_rope_epilogue(axis):
     qk = _rotate(y[:, :, :, :2], c, s_)
     ref = torch.cat([qk, y[:, :, :, 2:]], dim=3).reshape(rows, 3 * inner)
     assert rel_err(out, ref) < 6e-5
+
+
+def test_compiled_core_replays_cuda_graphs():
+    g = golden("bsroformer_small.pt")
+    for precision in ("fp32", "bf16"):
+        m = _model(g, precision)
+        mix = g["mix"].cuda()
+        eager = m(mix)
+        m.enable_compiled_core()
+        assert torch.equal(m(mix), eager) and torch.equal(m(mix), eager)
+        m.disable_compiled_core()
+    assert _lib.error_flag() == 0

@@ -1,0 +1,49 @@
+"""CUDA-graph replay of a model's fixed-shape forward (the ``enable_compiled_core`` hook).
+
+The reference compiles its hot core with ``torch.compile(mode="reduce-overhead")``
+(unblend/htdemucs.py:553-583), i.e. CUDA graphs over a fixed batch shape, and
+sets ``_fixed_batch_shape`` so ``apply_model`` zero-pads tail batches
+(unblend/apply.py:1189-1196). Here the launch sequence of the CUDA forward is
+captured as-is into a ``torch.cuda.CUDAGraph`` per input shape: the first call
+with a shape runs the forward once eagerly (lazy kernel attributes, tables),
+then captures it; later calls copy the input into the captured buffer and
+replay the graph, so a forward costs one graph launch on the host instead of a
+few hundred kernel launches.
+"""
+
+from __future__ import annotations
+
+from typing import Callable
+
+import torch
+
+
+class GraphedForward:
+    """Replays ``fn`` (a ``[B, C, T] -> tensor`` CUDA forward) from CUDA graphs, one per input shape."""
+
+    def __init__(self, fn: Callable[[torch.Tensor], torch.Tensor]) -> None:
+        self.fn = fn
+        self.graphs: dict = {}
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        key = (tuple(x.shape), x.dtype, x.device)
+        entry = self.graphs.get(key)
+        if entry is None:
+            static_in = x.clone()
+            side = torch.cuda.Stream(device=x.device)
+            side.wait_stream(torch.cuda.current_stream(x.device))
+            with torch.cuda.stream(side):
+                self.fn(static_in)  # eager warm-up: lazy attributes and cached tables
+            torch.cuda.current_stream(x.device).wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, capture_error_mode="relaxed"):
+                static_out = self.fn(static_in)
+            entry = self.graphs[key] = (graph, static_in, static_out)
+        graph, static_in, static_out = entry
+        static_in.copy_(x)
+        graph.replay()
+        return static_out.clone()
+
+    def release(self) -> None:
+        """Drop every captured graph and its private memory pool."""
+        self.graphs.clear()

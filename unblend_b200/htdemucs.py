@@ -608,10 +608,39 @@ class HTDemucsCuda(nn.Module):
         if length < T:
             mix = torch.nn.functional.pad(mix, (0, T - length))
         mix = mix.contiguous()
-        out = self._forward_full(mix)
+        graphed = self.__dict__.get("_graphed")
+        out = graphed(mix) if graphed is not None else self._forward_full(mix)
         if length < T:
             out = out[..., :length]
         return out
+
+    # ------------------------------------------------------------------ optional hooks (unblend/backends.py:62-111)
+    def prefill_inference_caches(self) -> None:
+        """Build the window / positional tables of the segment shape before any graph capture."""
+        dev = next(iter(self.weights.values())).device
+        if dev.type != "cuda":
+            return
+        nfft = self.config["nfft"]
+        frames = -(-self.segment_length // (nfft // 4))
+        lt = self.segment_length
+        for _ in range(self.depth):
+            lt = -(-lt // 4)
+        self._tables(dev, nfft // 2 // 4**self.depth, frames, lt)
+
+    def enable_compiled_core(self) -> None:
+        """Replay the forward from CUDA graphs (one per batch shape); tail batches get zero-padded."""
+        from .graphs import GraphedForward
+
+        self.prefill_inference_caches()
+        self.__dict__["_graphed"] = GraphedForward(self._forward_full)
+        self._fixed_batch_shape = True
+
+    def disable_compiled_core(self) -> None:
+        """Back to eager launches; releases the captured graphs."""
+        graphed = self.__dict__.pop("_graphed", None)
+        if graphed is not None:
+            graphed.release()
+        self._fixed_batch_shape = False
 
     def _forward_full(self, mix: torch.Tensor) -> torch.Tensor:
         B, C, T = mix.shape

@@ -363,6 +363,40 @@ class BSRoformerCuda(nn.Module):
             raise ValueError(f"input of {L} samples is too short for a {self.n_fft}-point centred STFT")
         in_dtype = mix.dtype
         mix = mix.float().contiguous()
+        graphed = self.__dict__.get("_graphed")
+        out = graphed(mix) if graphed is not None else self._forward_impl(mix)
+        return out if in_dtype == torch.float32 else out.to(in_dtype)
+
+    # ------------------------------------------------------------------ optional hooks (unblend/backends.py:62-111)
+    #: The RoFormer calibrator sweeps power-of-two batches (unblend/roformer.py:1075-1078).
+    prefers_power_of_two_batch = True
+    #: RoFormer consumes the raw mixture (no track-level normalisation by the caller).
+    external_normalization = False
+
+    def prefill_inference_caches(self) -> None:
+        """Build the window and rotary tables of the configured segment before any graph capture."""
+        if self._device.type == "cuda" and hasattr(self, "samplerate"):
+            seg = int(round(self.max_allowed_segment * self.samplerate))
+            self._tables(1 + seg // self.hop)
+
+    def enable_compiled_core(self) -> None:
+        """Replay the forward from CUDA graphs (one per batch shape); tail batches get zero-padded."""
+        from .graphs import GraphedForward
+
+        self.prefill_inference_caches()
+        self.__dict__["_graphed"] = GraphedForward(self._forward_impl)
+        self._fixed_batch_shape = True
+
+    def disable_compiled_core(self) -> None:
+        """Back to eager launches; releases the captured graphs."""
+        graphed = self.__dict__.pop("_graphed", None)
+        if graphed is not None:
+            graphed.release()
+        self._fixed_batch_shape = False
+
+    def _forward_impl(self, mix: torch.Tensor) -> torch.Tensor:
+        """The forward on a contiguous fp32 ``[B, 2, L]`` CUDA mixture."""
+        B, C, L = mix.shape
         dev = mix.device
         cfg = self.config
         T = 1 + L // self.hop
@@ -418,7 +452,7 @@ class BSRoformerCuda(nn.Module):
         _lib.call("unblend_istft_masked", stft.data_ptr(), mask.data_ptr(), frames * self.features,
                   tabs["window"].data_ptr(), mix.data_ptr(), fbuf.data_ptr(), out.data_ptr(), B, S, comp, L,
                   self.n_fft, self.hop, 1 if cfg["zero_dc"] else 0)
-        return out if in_dtype == torch.float32 else out.to(in_dtype)
+        return out
 
 
 def build_roformer(architecture: str, config: dict, *, sources: list[str], samplerate: int, segment_samples: int,
