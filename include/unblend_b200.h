@@ -150,6 +150,9 @@ int unblend_dconv_apply(float* x, long long x_gs, const float* h, int groups, in
                         const float* b2, const float* st2, const float* g2w, const float* g2b,
                         const float* scale, void* stream);
 
+/* Device flag set when a bounded wait of the DConv apply kernel gives up (0 = none). Synchronous host call. */
+int unblend_dconv_error_flag(int* out_host, int clear);
+
 /* LayerNorm over the last dim (eps 1e-5) with optional additive table:
  * y[r,:] = ln(x[r,:]) * gamma + beta + (pos ? pos_scale * pos[r % pos_rows, :] : 0). */
 int unblend_layer_norm(const float* x, float* y, const float* gamma, const float* beta,

@@ -133,6 +133,7 @@ _HOST_SIGNATURES = {
     "unblend_attention_error_flag": [ctypes.POINTER(c_int), c_int],
     "unblend_gemm_error_flag": [ctypes.POINTER(c_int), c_int],
     "unblend_attention_bf16_error_flag": [ctypes.POINTER(c_int), c_int],
+    "unblend_dconv_error_flag": [ctypes.POINTER(c_int), c_int],
 }
 
 TC_TF32X3, TC_BF16 = 0, 1
@@ -167,7 +168,7 @@ def error_flag(clear: bool = True) -> int:
     """Read (and by default clear) the device flag that bounded waits set on timeout."""
     total = 0
     for name in ("unblend_error_flag", "unblend_attention_error_flag", "unblend_gemm_error_flag",
-                 "unblend_attention_bf16_error_flag"):
+                 "unblend_attention_bf16_error_flag", "unblend_dconv_error_flag"):
         v = c_int(0)
         check(name, getattr(load(), name)(ctypes.byref(v), 1 if clear else 0))
         total |= v.value

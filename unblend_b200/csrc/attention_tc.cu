@@ -131,27 +131,34 @@ __device__ __forceinline__ void split_tile(uint8_t* p, uint8_t* lo, int n4, int 
 
 // V staging [2 boxes of (64 keys x 32 dims)] -> V^T [2 blocks of (64 dims x 32 keys)]
 // (keys contiguous, the K-major B operand of O += P V), rounded to TF32, and
-// with MODE 0 the residuals into a second V^T tile.
+// with MODE 0 the residuals into a second V^T tile. Each warp moves 32
+// consecutive keys of one 4-dim chunk per step, so the 32 scalar stores of a
+// step (one dim, 32 keys) fall in 32 different banks.
 template <int MODE>
 __device__ __forceinline__ void transpose_v(const uint8_t* stage_v, uint8_t* vt, uint8_t* vt_lo, int t) {
+  const int lane = t & 31, w = t >> 5;
 #pragma unroll
   for (int u = 0; u < 8; ++u) {
-    const int i = t + 128 * u;  // float4 index in the staging buffer (1024 of them)
-    const float4 val = reinterpret_cast<const float4*>(stage_v)[i];
-    const int box = i >> 9, within = i & 511;
-    const int key = within >> 3, pchunk = within & 7;
-    const int d0 = box * 32 + ((pchunk ^ (key & 7)) << 2);
+    const int unit = w * 8 + u;          // 32 units: (key half, box, chunk)
+    const int kh = unit >> 4, box = (unit >> 3) & 1, c = unit & 7;
+    const int key = kh * 32 + lane;
+    const float4 val = *reinterpret_cast<const float4*>(stage_v + box * (64 * 128) + key * 128 + ((c ^ (key & 7)) << 4));
     const float v4[4] = {val.x, val.y, val.z, val.w};
-    const int kb = key >> 5, kk = key & 31;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const int d = d0 + e;
-      const int off = kb * (64 * 128) + sw128(d, kk);
+      const int d = box * 32 + c * 4 + e;
+      const int off = kh * (64 * 128) + sw128(d, lane);
       const float hi = tf32_round(v4[e]);
       *reinterpret_cast<float*>(vt + off) = hi;
       if (MODE == 0) *reinterpret_cast<float*>(vt_lo + off) = v4[e] - hi;
     }
   }
+}
+
+__device__ __forceinline__ float ex2f(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 template <int MODE>
@@ -303,29 +310,26 @@ __global__ void __launch_bounds__(NT, 1)
       if (lane == 0) mbar_arrive(&kv_conv[s]);
     }
   } else {
-    // Softmax warps 2-5: thread = query row 32*(warp%4) + lane.
+    // Softmax warps 2-5: thread = query row 32*(warp%4) + lane. The running
+    // output O_acc (64 dims of this row) stays in registers: each tile's P V
+    // product is folded in with CUDA-core FMAs (O_acc = O_acc * corr + O_tile),
+    // which keeps fp32 accuracy over thousands of keys.
     const int qw = warp & 3;
     const int row = qw * 32 + lane;
     const uint32_t lane_base = tmem + ((uint32_t)(qw * 32) << 16);
     float m = -INFINITY, l = 0.f, corr_prev = 0.f;
-    bool ok = true;
-    // O_acc = O_acc * corr + O_tile for tile t (the first tile initialises O_acc).
-    auto fold_tile = [&](uint32_t base, int t, float corr) {
-      uint32_t a0[32], a1[32], t0[32], t1[32];
-      tmem_ld32(base + L::O_COL, t0);
-      tmem_ld32(base + L::O_COL + 32, t1);
-      if (t > 0) {
-        tmem_ld32(base + L::OACC_COL, a0);
-        tmem_ld32(base + L::OACC_COL + 32, a1);
+    float oacc[64];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          t0[i] = __float_as_uint(fmaf(__uint_as_float(a0[i]), corr, __uint_as_float(t0[i])));
-          t1[i] = __float_as_uint(fmaf(__uint_as_float(a1[i]), corr, __uint_as_float(t1[i])));
-        }
+    for (int d = 0; d < 64; ++d) oacc[d] = 0.f;
+    bool ok = true;
+    auto fold_tile = [&](float corr) {
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t t0[32];
+        tmem_ld32(lane_base + L::O_COL + 32 * half, t0);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) oacc[32 * half + i] = fmaf(oacc[32 * half + i], corr, __uint_as_float(t0[i]));
       }
-      tmem_st32(base + L::OACC_COL, t0);
-      tmem_st32(base + L::OACC_COL + 32, t1);
-      tmem_st_wait();
     };
     for (int j = 0; j < nkv && ok; ++j) {
       if (!__all_sync(0xffffffffu, mbar_wait(&s_full[j & 1], (j >> 1) & 1))) {
@@ -348,39 +352,39 @@ __global__ void __launch_bounds__(NT, 1)
         mx = fmaxf(mx, fmaxf(v0, v1));
       }
       const float m_new = fmaxf(m, mx);
-      const float corr = exp2f(m - m_new);
+      const float corr = ex2f(m - m_new);
       float sum = 0.f;
-      uint32_t lo0[32], lo1[32];
+      // P = exp2(s - m_new) rounded to TF32 (hi) plus, in MODE 0, the residual
+      // (lo), written to TMEM one 32-key half at a time.
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float p0 = exp2f(__uint_as_float(s0[i]) - m_new);
-        const float p1 = exp2f(__uint_as_float(s1[i]) - m_new);
-        sum += p0 + p1;
-        const float h0 = tf32_round(p0), h1 = tf32_round(p1);
-        s0[i] = __float_as_uint(h0);
-        s1[i] = __float_as_uint(h1);
-        lo0[i] = __float_as_uint(p0 - h0);
-        lo1[i] = __float_as_uint(p1 - h1);
+      for (int half = 0; half < 2; ++half) {
+        uint32_t (&sh)[32] = half == 0 ? s0 : s1;
+        uint32_t lo[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float p = ex2f(__uint_as_float(sh[i]) - m_new);
+          sum += p;
+          const float hi = tf32_round(p);
+          sh[i] = __float_as_uint(hi);
+          lo[i] = __float_as_uint(p - hi);
+        }
+        tmem_st32(lane_base + L::S_COL + (j & 1) * BK + 32 * half, sh);
+        if (MODE == 0) tmem_st32(lane_base + L::PLO_COL + (j & 1) * BK + 32 * half, lo);
       }
-      l = l * corr + sum;
-      m = m_new;
       if (j > 0) {
-        // Fold the previous tile's P V into the running accumulator with
-        // CUDA-core fp32 arithmetic (the tensor core only ever sums one tile).
+        // Fold the previous tile's P V product (complete once o_done fires)
+        // before P V of this tile may overwrite it. P(j) itself went into the S
+        // tile of P(j-2), whose product was waited for one tile ago.
         if (!__all_sync(0xffffffffu, mbar_wait(o_done, (j - 1) & 1))) {
           ok = false;
           break;
         }
         tc_fence_after();
-        fold_tile(lane_base, j - 1, corr_prev);
+        fold_tile(corr_prev);
       }
+      l = l * corr + sum;
+      m = m_new;
       corr_prev = corr;
-      tmem_st32(lane_base + L::S_COL + (j & 1) * BK, s0);
-      tmem_st32(lane_base + L::S_COL + (j & 1) * BK + 32, s1);
-      if (MODE == 0) {
-        tmem_st32(lane_base + L::PLO_COL + (j & 1) * BK, lo0);
-        tmem_st32(lane_base + L::PLO_COL + (j & 1) * BK + 32, lo1);
-      }
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
@@ -390,10 +394,7 @@ __global__ void __launch_bounds__(NT, 1)
     tc_fence_after();
     if (ok) {
       __syncwarp();
-      fold_tile(lane_base, nkv - 1, corr_prev);
-      uint32_t o0[32], o1[32];
-      tmem_ld32(lane_base + L::OACC_COL, o0);
-      tmem_ld32(lane_base + L::OACC_COL + 32, o1);
+      fold_tile(corr_prev);
       const int qrow = q0 + row;
       if (qrow < a.lq) {
         float inv = 1.f / l;
@@ -404,14 +405,7 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll
         for (int d = 0; d < 64; d += 4) {
           if (d < a.hd) {
-            float4 v;
-            if (d < 32)
-              v = make_float4(__uint_as_float(o0[d]), __uint_as_float(o0[d + 1]), __uint_as_float(o0[d + 2]),
-                              __uint_as_float(o0[d + 3]));
-            else
-              v = make_float4(__uint_as_float(o1[d - 32]), __uint_as_float(o1[d - 31]),
-                              __uint_as_float(o1[d - 30]), __uint_as_float(o1[d - 29]));
-            v = make_float4(v.x * inv, v.y * inv, v.z * inv, v.w * inv);
+            const float4 v = make_float4(oacc[d] * inv, oacc[d + 1] * inv, oacc[d + 2] * inv, oacc[d + 3] * inv);
             if (a.o_bf16) {
               __nv_bfloat162 p0 = __floats2bfloat162_rn(v.x, v.y);
               __nv_bfloat162 p1 = __floats2bfloat162_rn(v.z, v.w);

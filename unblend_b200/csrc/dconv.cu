@@ -210,6 +210,262 @@ __global__ void __launch_bounds__(ROWS) dconv_apply_kernel(float* __restrict__ x
   }
 }
 
+// ---------------------------------------------------------------------------
+// Persistent, channel-blocked z_stats / apply for the thin DConv levels
+// (hidden width <= 16). A CTA walks work items (group, block of IROWS rows) in
+// a grid-stride loop. Thread t keeps the W2 rows of its CPT output channels
+// (value and gate rows) in registers for the whole kernel and walks rows
+// t / CG, t / CG + RPP, ... of each item; GELU(GN1(h)) of the item's rows is
+// staged in shared memory (a broadcast read feeding 2*CPT dot products).
+// apply additionally streams x through shared memory with bulk async copies
+// (cp.async.bulk, double-buffered across items): the load of the next item's
+// rows and the store of the previous one overlap the current update.
+constexpr int CPT = 2;      // output channels per thread
+constexpr int NTH2 = 256;   // threads per CTA (CG * RPP <= NTH2)
+constexpr int IROWS = 64;   // rows per work item
+constexpr int MAXC2 = 384;  // largest C of the persistent apply (x staging: 2 x IROWS x C floats)
+
+__device__ __forceinline__ uint32_t sm_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sm_u32(bar)), "r"(bytes) : "memory");
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   sm_u32(dst)),
+               "l"(src), "r"(bytes), "r"(sm_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_store(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(sm_u32(src)), "r"(bytes)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// Bounded wait (about 2 s of %globaltimer) for the phase `parity` of `bar`; false on timeout.
+__device__ __forceinline__ bool wait_phase(uint64_t* bar, uint32_t parity) {
+  uint64_t t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  while (true) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(sm_u32(bar)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (t - t0 > 2000000000ull) return false;
+  }
+}
+
+template <int MAXH>
+__device__ __forceinline__ void stage_act(const float* __restrict__ h, int g, int r0, int nrows, int rows, int H,
+                                          float m1, float rs1, const float* __restrict__ g1w,
+                                          const float* __restrict__ g1b, float* __restrict__ a_s) {
+  for (int i = threadIdx.x; i < IROWS * MAXH; i += blockDim.x) {
+    const int r = i / MAXH, j = i - (i / MAXH) * MAXH;
+    float v = 0.f;
+    if (j < H && r < nrows)
+      v = ub::gelu_erf((h[((long long)g * rows + r0 + r) * H + j] - m1) * rs1 * __ldg(g1w + j) + __ldg(g1b + j));
+    a_s[i] = v;
+  }
+}
+
+// Dot product of an activation row (16-byte aligned) with the first HW weights;
+// HW is the exact hidden width when it is a multiple of 2 known at compile time.
+template <int MAXH, int HW>
+__device__ __forceinline__ float dot_a(const float* __restrict__ a, const float (&w)[MAXH]) {
+  float z = 0.f;
+#pragma unroll
+  for (int j4 = 0; j4 < HW / 4; ++j4) {
+    const float4 v = *reinterpret_cast<const float4*>(a + 4 * j4);
+    z = fmaf(v.x, w[4 * j4], z);
+    z = fmaf(v.y, w[4 * j4 + 1], z);
+    z = fmaf(v.z, w[4 * j4 + 2], z);
+    z = fmaf(v.w, w[4 * j4 + 3], z);
+  }
+  if (HW % 4 == 2) {
+    const float2 v = *reinterpret_cast<const float2*>(a + HW - 2);
+    z = fmaf(v.x, w[HW - 2], z);
+    z = fmaf(v.y, w[HW - 1], z);
+  }
+  return z;
+}
+
+// 1 / (1 + e^-x) with the hardware exp2 and reciprocal (relative error ~1e-7).
+__device__ __forceinline__ float sigmoid_fast(float x) { return __frcp_rn(1.0f + __expf(-x)); }
+
+template <int MAXH>
+__device__ __forceinline__ void load_w(const float* __restrict__ w2, const float* __restrict__ b2, int H, int cg,
+                                       bool live, float (&w)[2 * CPT][MAXH], float (&bz)[2 * CPT]) {
+#pragma unroll
+  for (int k = 0; k < 2 * CPT; ++k) {
+    const int n = 2 * cg * CPT + k;  // z channel (value/gate interleaved)
+#pragma unroll
+    for (int j = 0; j < MAXH; ++j) w[k][j] = (j < H && live) ? __ldg(w2 + (long long)n * H + j) : 0.f;
+    bz[k] = live ? __ldg(b2 + n) : 0.f;
+  }
+}
+
+template <int MAXH, int HW>
+__global__ void __launch_bounds__(NTH2) dconv_z_stats3_kernel(const float* __restrict__ h, int groups, int rows, int H,
+                                                               int C, const float* __restrict__ st1,
+                                                               const float* __restrict__ g1w,
+                                                               const float* __restrict__ g1b,
+                                                               const float* __restrict__ w2,
+                                                               const float* __restrict__ b2,
+                                                               double* __restrict__ stats2) {
+  __shared__ __align__(16) float a_s[IROWS * MAXH];
+  __shared__ double red[2][NTH2 / 32];
+  const int CG = C / CPT;
+  const int RPP = blockDim.x / CG;
+  const int cg = threadIdx.x % CG, rsub = threadIdx.x / CG;
+  const bool live = rsub < RPP;
+  float w[2 * CPT][MAXH], bz[2 * CPT];
+  load_w<MAXH>(w2, b2, H, cg, live, w, bz);
+  const int nblk = (rows + IROWS - 1) / IROWS;
+  const long long items = (long long)groups * nblk;
+  for (long long it = blockIdx.x; it < items; it += gridDim.x) {
+    const int g = (int)(it / nblk);
+    const int r0 = (int)(it - (long long)g * nblk) * IROWS;
+    const int nrows = min(IROWS, rows - r0);
+    __syncthreads();  // the previous item's readers are done with a_s and red
+    stage_act<MAXH>(h, g, r0, nrows, rows, H, st1[2 * g], st1[2 * g + 1], g1w, g1b, a_s);
+    __syncthreads();
+    float s1 = 0.f, s2 = 0.f;
+    if (live) {
+      for (int r = rsub; r < nrows; r += RPP) {
+        const float* a = a_s + r * MAXH;
+#pragma unroll
+        for (int k = 0; k < 2 * CPT; ++k) {
+          const float z = dot_a<MAXH, HW>(a, w[k]) + bz[k];
+          s1 += z;
+          s2 += z * z;
+        }
+      }
+    }
+    const double d1 = ub::warp_sum_d((double)s1), d2 = ub::warp_sum_d((double)s2);
+    if ((threadIdx.x & 31) == 0) {
+      red[0][threadIdx.x >> 5] = d1;
+      red[1][threadIdx.x >> 5] = d2;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      double a0 = 0, a1 = 0;
+      for (int i = 0; i < (int)(blockDim.x >> 5); ++i) {
+        a0 += red[0][i];
+        a1 += red[1][i];
+      }
+      atomicAdd(stats2 + 2 * g, a0);
+      atomicAdd(stats2 + 2 * g + 1, a1);
+    }
+  }
+}
+
+static __device__ int g_dconv_error = 0;
+
+template <int MAXH, int HW>
+__global__ void __launch_bounds__(NTH2) dconv_apply3_kernel(float* __restrict__ x, long long x_gs, int groups,
+                                                             const float* __restrict__ h, int rows, int H, int C,
+                                                             const float* __restrict__ st1,
+                                                             const float* __restrict__ g1w,
+                                                             const float* __restrict__ g1b,
+                                                             const float* __restrict__ w2,
+                                                             const float* __restrict__ b2,
+                                                             const float* __restrict__ st2,
+                                                             const float* __restrict__ g2w,
+                                                             const float* __restrict__ g2b,
+                                                             const float* __restrict__ scale) {
+  extern __shared__ __align__(128) float dyn[];
+  float* xbuf = dyn;                          // [2][IROWS * C]
+  float* a_s = dyn + 2 * IROWS * C;           // [IROWS * MAXH]
+  __shared__ __align__(8) uint64_t full[2];
+  const int CG = C / CPT;
+  const int RPP = blockDim.x / CG;
+  const int cg = threadIdx.x % CG, rsub = threadIdx.x / CG;
+  const bool live = rsub < RPP;
+  float w[2 * CPT][MAXH], bz[2 * CPT];
+  load_w<MAXH>(w2, b2, H, cg, live, w, bz);
+  float gam[2 * CPT], bet[2 * CPT], sc[CPT];
+#pragma unroll
+  for (int k = 0; k < 2 * CPT; ++k) {
+    gam[k] = live ? __ldg(g2w + 2 * cg * CPT + k) : 0.f;
+    bet[k] = live ? __ldg(g2b + 2 * cg * CPT + k) : 0.f;
+  }
+#pragma unroll
+  for (int e = 0; e < CPT; ++e) sc[e] = live ? __ldg(scale + cg * CPT + e) : 0.f;
+  const int nblk = (rows + IROWS - 1) / IROWS;
+  const long long items = (long long)groups * nblk;
+  if (threadIdx.x == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(sm_u32(&full[0])) : "memory");
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(sm_u32(&full[1])) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  auto item_ptr = [&](long long it, int& g, int& r0, int& nrows) -> float* {
+    g = (int)(it / nblk);
+    r0 = (int)(it - (long long)g * nblk) * IROWS;
+    nrows = min(IROWS, rows - r0);
+    return x + (long long)g * x_gs + (long long)r0 * C;
+  };
+  if (threadIdx.x == 0 && blockIdx.x < items) {
+    int g, r0, nr;
+    float* src = item_ptr(blockIdx.x, g, r0, nr);
+    bulk_load(xbuf, src, (uint32_t)(nr * C * 4), &full[0]);
+  }
+  bool ok = true;
+  int k = 0;
+  for (long long it = blockIdx.x; it < items; it += gridDim.x, ++k) {
+    const int b = k & 1;
+    int g, r0, nrows;
+    float* xg = item_ptr(it, g, r0, nrows);
+    // Prefetch the next item into the other buffer once its previous store has read it.
+    if (threadIdx.x == 0 && it + gridDim.x < items) {
+      asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+      int g2, r2, n2;
+      float* src = item_ptr(it + gridDim.x, g2, r2, n2);
+      bulk_load(xbuf + (b ^ 1) * IROWS * C, src, (uint32_t)(n2 * C * 4), &full[b ^ 1]);
+    }
+    stage_act<MAXH>(h, g, r0, nrows, rows, H, st1[2 * g], st1[2 * g + 1], g1w, g1b, a_s);
+    ok = wait_phase(&full[b], (k >> 1) & 1);
+    if (__syncthreads_or(!ok)) break;
+    const float mean2 = st2[2 * g], rstd2 = st2[2 * g + 1];
+    // GN2 folded per item: (W2 a + b2 - mean2) * rstd2 * gamma + beta = (W2 a) * A + B.
+    float fa[2 * CPT], fb[2 * CPT];
+#pragma unroll
+    for (int q = 0; q < 2 * CPT; ++q) {
+      fa[q] = rstd2 * gam[q];
+      fb[q] = (bz[q] - mean2) * fa[q] + bet[q];
+    }
+    if (live) {
+      float* xs = xbuf + b * IROWS * C + cg * CPT;
+      for (int r = rsub; r < nrows; r += RPP) {
+        const float* a = a_s + r * MAXH;
+        float o[CPT];
+#pragma unroll
+        for (int e = 0; e < CPT; ++e) {
+          const float v = fmaf(dot_a<MAXH, HW>(a, w[2 * e]), fa[2 * e], fb[2 * e]);
+          const float gt = fmaf(dot_a<MAXH, HW>(a, w[2 * e + 1]), fa[2 * e + 1], fb[2 * e + 1]);
+          o[e] = sc[e] * (v * sigmoid_fast(gt));
+        }
+        float2* xp = reinterpret_cast<float2*>(xs + r * C);
+        float2 xv = *xp;
+        xv.x += o[0];
+        xv.y += o[1];
+        *xp = xv;
+      }
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncthreads();  // the item is updated in shared memory; a_s may be restaged
+    if (threadIdx.x == 0) bulk_store(xg, xbuf + b * IROWS * C, (uint32_t)(nrows * C * 4));
+  }
+  if (threadIdx.x == 0) {
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    if (!ok) atomicExch(&g_dconv_error, 1);
+  }
+}
+
 int maxh_for(int H) { return H <= 8 ? 8 : H <= 16 ? 16 : H <= 32 ? 32 : H <= 64 ? 64 : 0; }
 
 }  // namespace
@@ -246,6 +502,20 @@ extern "C" int unblend_dconv_z_stats(const float* h, int groups, int rows, int h
   UB_REQUIRE(smem <= 220 * 1024);
   dim3 grid((rows + ROWS - 1) / ROWS, groups);
   cudaStream_t st = ub::as_stream(stream);
+  if (mh <= 16 && c % CPT == 0 && c / CPT <= NTH2) {
+    const long long items = (long long)groups * ((rows + IROWS - 1) / IROWS);
+    const unsigned g2 = (unsigned)(items < 148LL * 8 ? items : 148LL * 8);
+    if (hid == 6)
+      dconv_z_stats3_kernel<8, 6><<<g2, NTH2, 0, st>>>(h, groups, rows, hid, c, st1, g1w, g1b, w2, b2, stats2);
+    else if (hid == 12)
+      dconv_z_stats3_kernel<16, 12><<<g2, NTH2, 0, st>>>(h, groups, rows, hid, c, st1, g1w, g1b, w2, b2, stats2);
+    else if (mh == 8)
+      dconv_z_stats3_kernel<8, 8><<<g2, NTH2, 0, st>>>(h, groups, rows, hid, c, st1, g1w, g1b, w2, b2, stats2);
+    else
+      dconv_z_stats3_kernel<16, 16><<<g2, NTH2, 0, st>>>(h, groups, rows, hid, c, st1, g1w, g1b, w2, b2, stats2);
+    UB_CHECK_LAUNCH();
+    return 0;
+  }
 #define UB_LAUNCH(MH)                                                                                           \
   {                                                                                                             \
     cudaFuncSetAttribute(dconv_z_stats_kernel<MH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);    \
@@ -270,6 +540,25 @@ extern "C" int unblend_dconv_apply(float* x, long long x_gs, const float* h, int
   UB_REQUIRE(smem <= 220 * 1024);
   dim3 grid((rows + ROWS - 1) / ROWS, groups);
   cudaStream_t st = ub::as_stream(stream);
+  if (mh <= 16 && c % 4 == 0 && c / CPT <= NTH2 && c <= MAXC2 && x_gs % 4 == 0 &&
+      (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    const long long items = (long long)groups * ((rows + IROWS - 1) / IROWS);
+    const size_t smem3 = sizeof(float) * (2 * (size_t)IROWS * c + (size_t)IROWS * mh);
+    const int per_sm = (int)((200 * 1024) / (smem3 + 1024)) < 4 ? (int)((200 * 1024) / (smem3 + 1024)) : 4;
+    const long long cap = 148LL * (per_sm > 0 ? per_sm : 1);
+    const unsigned g3 = (unsigned)(items < cap ? items : cap);
+#define UB_APPLY3(MH, HW)                                                                                    \
+  {                                                                                                          \
+    cudaFuncSetAttribute(dconv_apply3_kernel<MH, HW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem3); \
+    dconv_apply3_kernel<MH, HW><<<g3, NTH2, smem3, st>>>(x, x_gs, groups, h, rows, hid, c, st1, g1w, g1b, w2, b2, \
+                                                         st2, g2w, g2b, scale);                              \
+  }
+    if (hid == 6) UB_APPLY3(8, 6) else if (hid == 12) UB_APPLY3(16, 12) else if (mh == 8) UB_APPLY3(8, 8)
+    else UB_APPLY3(16, 16)
+#undef UB_APPLY3
+    UB_CHECK_LAUNCH();
+    return 0;
+  }
 #define UB_LAUNCH(MH)                                                                                         \
   {                                                                                                           \
     cudaFuncSetAttribute(dconv_apply_kernel<MH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);    \
@@ -279,5 +568,18 @@ extern "C" int unblend_dconv_apply(float* x, long long x_gs, const float* h, int
   if (mh == 8) UB_LAUNCH(8) else if (mh == 16) UB_LAUNCH(16) else if (mh == 32) UB_LAUNCH(32) else UB_LAUNCH(64)
 #undef UB_LAUNCH
   UB_CHECK_LAUNCH();
+  return 0;
+}
+
+extern "C" int unblend_dconv_error_flag(int* out_host, int clear) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_dconv_error, sizeof(int));
+  if (e != cudaSuccess) return (int)e;
+  if (out_host) *out_host = v;
+  if (clear) {
+    int z = 0;
+    e = cudaMemcpyToSymbol(g_dconv_error, &z, sizeof(int));
+    if (e != cudaSuccess) return (int)e;
+  }
   return 0;
 }
