@@ -28,6 +28,7 @@ import argparse
 import datetime
 import json
 import os
+import random
 import statistics
 import subprocess
 import sys
@@ -53,9 +54,13 @@ def _args():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--model", default="htdemucs", choices=["htdemucs", "bsroformer"],
-                    help="htdemucs: the headline workload; bsroformer: BS-RoFormer dim 512 depth 12, 8 s "
-                         "segments, batch 16, bf16, 300 s track")
+    ap.add_argument("--model", default="htdemucs", choices=["htdemucs", "htdemucs_6s", "bsroformer"],
+                    help="htdemucs: the headline workload; htdemucs_6s: 6-source HTDemucs (seed 2), bf16, "
+                         "shifts=1, 240 s track; bsroformer: BS-RoFormer dim 512 depth 12, 8 s segments, batch 16, "
+                         "bf16, 300 s track")
+    ap.add_argument("--shifts", type=int, default=None, help="random-shift rounds per track")
+    ap.add_argument("--tracks", type=int, default=1,
+                    help="tracks per rank and step (e.g. 8 x 240 s bf16 batch 48 per rank for the whole-box sweep)")
     ap.add_argument("--precision", default=None, choices=["fp32", "bf16", "fp32-simt"])
     ap.add_argument("--seconds", type=float, default=None,
                     help="track length per rank (smaller values are for profiling only)")
@@ -65,12 +70,15 @@ def _args():
                          "overlap-strip exchange (strong scaling); default: one track per rank (weak scaling)")
     args = ap.parse_args()
     rof = args.model == "bsroformer"
+    six = args.model == "htdemucs_6s"
     if args.precision is None:
-        args.precision = "bf16" if rof else "fp32"
+        args.precision = "bf16" if rof or six else "fp32"
+    if args.shifts is None:
+        args.shifts = 1 if six else 0
     if rof and args.precision == "fp32-simt":
         ap.error("fp32-simt is an HTDemucs precision")
     if args.seconds is None:
-        args.seconds = ROFORMER_TRACK_SECONDS if rof else TRACK_SECONDS
+        args.seconds = ROFORMER_TRACK_SECONDS if rof else (240.0 if six else TRACK_SECONDS)
     if args.batch is None:
         args.batch = ROFORMER_BATCH if rof else BATCH
     return args
@@ -236,20 +244,31 @@ def main() -> None:
         model.configure_inference(sources=["vocals"], samplerate=44100, segment_samples=ROFORMER_SEGMENT)
         seg_len = ROFORMER_SEGMENT
     else:
-        cfg = htdemucs_config("htdemucs")
-        model = HTDemucsCuda(cfg, htdemucs_state_dict(cfg, 0), precision=args.precision).to(dev)
+        name, seed = ("htdemucs_6s", 2) if args.model == "htdemucs_6s" else ("htdemucs", 0)
+        cfg = htdemucs_config(name)
+        model = HTDemucsCuda(cfg, htdemucs_state_dict(cfg, seed), precision=args.precision).to(dev)
         seg_len = model.segment_length
     n_stems = len(model.sources)
-    seconds, batch = args.seconds, args.batch
+    seconds, batch, shifts = args.seconds, args.batch, args.shifts
     split = args.split_track and world > 1
-    track = synth_track(seconds, 1 if split else 1 + rank)
-    track_dev = track.to(dev)
+    n_tracks = 1 if split else args.tracks
+    random.seed(1234 + rank)
+    if args.tracks > 1:
+        seeds = [100 + rank * args.tracks + i for i in range(args.tracks)]
+    else:
+        seeds = [1 if split else 1 + rank]
+    tracks = [synth_track(seconds, sd) for sd in seeds]
+    track = tracks[0]
+    tracks_dev = [t.to(dev) for t in tracks]
     if split:
         from unblend_b200.distributed import apply_model_sharded
 
-        step = lambda: apply_model_sharded(model, track_dev, chunk_batch_size=batch, gather=False)  # noqa: E731
+        step = lambda: apply_model_sharded(model, tracks_dev[0], chunk_batch_size=batch, shifts=shifts,  # noqa: E731
+                                           gather=False)
     else:
-        step = lambda: apply_model(model, track_dev, chunk_batch_size=batch)  # noqa: E731
+        def step():
+            for td in tracks_dev:
+                apply_model(model, td, chunk_batch_size=batch, shifts=shifts)
 
     for _ in range(args.warmup):
         step()
@@ -282,14 +301,17 @@ def main() -> None:
     launches = _lib.counters["launches"] - launches0
 
     # End to end through the public API with a pinned host track.
-    host = track.pin_memory()
+    hosts = [t.pin_memory() for t in tracks]
     if split:
         def e2e_step():
-            out = apply_model_sharded(model, host.to(dev, non_blocking=True), chunk_batch_size=batch, gather=True)
+            out = apply_model_sharded(model, hosts[0].to(dev, non_blocking=True), chunk_batch_size=batch,
+                                      shifts=shifts, gather=True)
             if rank == 0:
                 out.to("cpu")
     else:
-        e2e_step = lambda: apply_model(model, host, device=dev, chunk_batch_size=batch)  # noqa: E731
+        def e2e_step():
+            for hst in hosts:
+                apply_model(model, hst, device=dev, chunk_batch_size=batch, shifts=shifts)
     e2e_step()
     e2e_ms = timed(e2e_step, max(1, args.steps))
 
@@ -314,9 +336,9 @@ def main() -> None:
                 "share_of_step": round(a["ms"] / sum(v["ms"] for v in agg.values()), 3),
                 "launches_per_step": a["n"]}
 
-    tracks = 1 if split else world
-    value = tracks * seconds / (ms * 1e-3)
-    e2e_value = tracks * seconds / (e2e_ms * 1e-3)
+    job_tracks = 1 if split else world * n_tracks
+    value = job_tracks * seconds / (ms * 1e-3)
+    e2e_value = job_tracks * seconds / (e2e_ms * 1e-3)
     L = track.shape[-1]
     n_seg = len(range(0, L, int(0.75 * seg_len)))
     dtype = {"fp32": "f32", "bf16": "bf16", "fp32-simt": "f32"}[args.precision]
@@ -324,8 +346,13 @@ def main() -> None:
         work = (f"BS-RoFormer dim 512 depth 12 (seed 3), {seconds:g} s stereo track, {n_seg} segments of 8 s, "
                 f"overlap 0.25, {batch} segments per launch, precision {args.precision}")
     else:
-        work = (f"HTDemucs 4-stem, {seconds:g} s stereo track, {n_seg} segments of 7.8 s, "
+        label = "HTDemucs 6-stem (seed 2)" if args.model == "htdemucs_6s" else "HTDemucs 4-stem"
+        work = (f"{label}, {seconds:g} s stereo track, {n_seg} segments of 7.8 s, "
                 f"overlap 0.25, {batch} segments per launch, precision {args.precision}")
+    if shifts:
+        work += f", shifts={shifts}"
+    if n_tracks > 1:
+        work += f", {n_tracks} tracks per rank"
     line = {"metric": METRIC, "value": round(value, 3), "unit": "audio-s/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
             "scaling": "strong" if split else "weak", "vs_baseline": None, "dtype": dtype, "data": "synthetic",
@@ -334,8 +361,8 @@ def main() -> None:
                        "parallelism": (f"one track, segments sharded over {world} ranks + NCCL strip exchange"
                                        if split else f"whole tracks per rank x{world}"),
                        "l2": "inputs and activations far larger than L2 (no flush needed)"},
-            "e2e": {"value": round(e2e_value, 3), "unit": "audio-s/s", "h2d_bytes_per_step": 2 * L * 4,
-                    "d2h_bytes_per_step": n_stems * 2 * L * 4},
+            "e2e": {"value": round(e2e_value, 3), "unit": "audio-s/s", "h2d_bytes_per_step": n_tracks * 2 * L * 4,
+                    "d2h_bytes_per_step": n_tracks * n_stems * 2 * L * 4},
             "gpu_launches": launches, "roofline": roofline, "clocks": clk,
             "kernels": {k: {"ms": round(v["ms"], 3), "n": v["n"]} for k, v in sorted(agg.items(), key=lambda kv: -kv[1]["ms"])}}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

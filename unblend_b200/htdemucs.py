@@ -143,6 +143,8 @@ class HTDemucsCuda(nn.Module):
             raise ValueError(f"precision must be one of {PRECISIONS}")
         self.precision = precision
         self._tc_cache: dict = {}
+        # Output widths from which the 256-column tile is used (per tensor-core mode).
+        self._bn256_min = {_lib.TC_TF32X3: 1 << 30, _lib.TC_BF16: 512}
         cfg = dict(HTDEMUCS_CONFIGS["htdemucs"])
         cfg.update(config)
         if cfg.get("multi_freqs") or not cfg["cac"] or cfg["norm_starts"] < cfg["depth"]:
@@ -301,7 +303,7 @@ class HTDemucsCuda(nn.Module):
             mode = _lib.TC_TF32X3 if self.precision == "fp32" else _lib.TC_BF16
             whi, wlo = self._tc_weight(w, mode)
             block_n = 64 if n_out <= 64 else 128
-            if mode == _lib.TC_BF16 and n_out >= 512:
+            if n_out >= self._bn256_min[mode]:
                 block_n = 256
             _lib.call("unblend_conv2d_tc", x.t.data_ptr(), whi.data_ptr(), _lib.ptr(wlo), _lib.ptr(b), y,
                       ctypes_byref(p), mode, block_n, work=flops)
