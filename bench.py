@@ -107,6 +107,18 @@ def _peaks() -> dict:
     return {"hbm": 6650.0, "bf16": 1590.0, "src": "fallback"}
 
 
+def _traffic(key: str, kernel: str):
+    """DRAM bytes per launch of `kernel` for workload `key` from the committed ncu summary, or None."""
+    path = os.path.join(ROOT, "profiles", "traffic_per_launch.txt")
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        parts = line.split()
+        if len(parts) >= 3 and not line.startswith("#") and parts[0] == key and parts[1] == kernel:
+            return int(parts[2])
+    return None
+
+
 class Clocks:
     """Samples nvidia-smi clocks / throttle reasons during the timed region."""
 
@@ -331,10 +343,16 @@ def main() -> None:
     a = agg[top]
     tflops = a["work"] / (a["ms"] * 1e-3) / 1e12 if a["ms"] > 0 else 0.0
     roofline = {"kernel": top, "bound": "tensor", "achieved": round(tflops, 3), "peak": peaks["bf16"],
-                "unit": "TFLOP/s", "frac": round(tflops / peaks["bf16"], 5), "traffic": None,
+                "unit": "TFLOP/s", "frac": round(tflops / peaks["bf16"], 5),
+                "traffic": _traffic(f"{args.model}:{args.precision}:batch{batch}", top),
+                "traffic_unit": "bytes per launch (ncu capture, see profiles/traffic_per_launch.txt)",
                 "peak_source": f"{peaks['src']} bf16 dense (burst)",
                 "share_of_step": round(a["ms"] / sum(v["ms"] for v in agg.values()), 3),
                 "launches_per_step": a["n"]}
+    if args.precision == "fp32":
+        # fp32 accuracy costs three kind::tf32 MMAs per product, each at half the bf16 rate.
+        roofline["peak_fp32_3xtf32"] = round(peaks["bf16"] / 6, 1)
+        roofline["frac_of_fp32_3xtf32_peak"] = round(tflops / (peaks["bf16"] / 6), 4)
 
     job_tracks = 1 if split else world * n_tracks
     value = job_tracks * seconds / (ms * 1e-3)
