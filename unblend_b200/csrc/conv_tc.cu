@@ -24,6 +24,7 @@
 // residual and GroupNorm statistics, as the SIMT kernel does.
 #include <cuda_bf16.h>
 #include <cudaTypedefs.h>
+#include <string.h>
 
 #include "common.cuh"
 #include "tc_common.cuh"
@@ -53,6 +54,7 @@ struct TcArgs {
   const float* res_scale;
   double* stats;
   int stats_per_h;
+  int tma_store;  // 1: whole 32-column chunks leave through TMA bulk tensor stores (no residual)
 };
 
 template <int BN, int MODE>
@@ -90,7 +92,8 @@ __device__ __forceinline__ TileCoord tile_coord(const TcArgs& a, long long t) {
 template <int BN, int MODE>
 __global__ void __launch_bounds__(NT, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
-                   const __grid_constant__ CUtensorMap mapB2, const __grid_constant__ TcArgs a) {
+                   const __grid_constant__ CUtensorMap mapB2, const __grid_constant__ CUtensorMap mapO,
+                   const __grid_constant__ TcArgs a) {
   using L = Layout<BN, MODE>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -273,6 +276,82 @@ __global__ void __launch_bounds__(NT, 1)
         uint32_t acc[32];
         __syncwarp();
         tmem_ld32(base + (uint32_t)c0, acc);
+        if (a.tma_store && n0 + c0 + 32 <= a.n_out) {
+          // Whole chunk, lane = output position: bias, activation, GLU and the
+          // statistics in registers, one swizzled staging row per lane, then
+          // bulk tensor stores of 16-row halves inside the tile's valid rows.
+          const int row = q * 32 + lane;
+          const bool rv = row < a.m_valid && w0 + row < a.W_out;
+          float v[32];
+          if (a.bias) {
+            const float4* bp = reinterpret_cast<const float4*>(a.bias + n0 + c0);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float4 b4 = __ldg(bp + j);
+              v[4 * j] = __uint_as_float(acc[4 * j]) + b4.x;
+              v[4 * j + 1] = __uint_as_float(acc[4 * j + 1]) + b4.y;
+              v[4 * j + 2] = __uint_as_float(acc[4 * j + 2]) + b4.z;
+              v[4 * j + 3] = __uint_as_float(acc[4 * j + 3]) + b4.w;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(acc[j]);
+          }
+          if (a.act == UNBLEND_ACT_GELU) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = gelu(v[j]);
+          }
+          const int nv = glu ? 16 : 32;
+          if (glu) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = v[2 * j] * ub::sigmoidf_(v[2 * j + 1]);
+          }
+          if (a.stats && rv) {
+            float t1 = 0.f, t2 = 0.f;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (j < nv) {
+                t1 += v[j];
+                t2 += v[j] * v[j];
+              }
+            }
+            s1 += t1;
+            s2 += t2;
+          }
+          uint8_t* stg = reinterpret_cast<uint8_t*>(stage);
+          if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+          __syncwarp();
+          const int rb = nv * 4;                      // staging row bytes: 128 or 64
+          const int swz = ((lane * rb) >> 7) & ((rb >> 4) - 1);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            if (j < (nv >> 2))
+              *reinterpret_cast<float4*>(stg + lane * rb + ((j ^ swz) << 4)) =
+                  make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            const int xcol = glu ? (n0 + c0) / 2 : n0 + c0;
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+              const int r0 = q * 32 + 16 * half;
+              if (r0 < a.m_valid && w0 + r0 < a.W_out) {
+                asm volatile(
+                    "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+                        &mapO),
+                    "r"(smem_u32(stg + half * 16 * rb)), "r"(xcol), "r"(w0 + r0), "r"(h), "r"(b)
+                    : "memory");
+              }
+            }
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+          }
+          continue;
+        }
+        if (a.tma_store) {
+          if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+          __syncwarp();
+        }
 #pragma unroll
         for (int j = 0; j < 8; ++j)
           stage[lane * 8 + (j ^ (lane & 7))] =
@@ -385,6 +464,8 @@ __global__ void __launch_bounds__(NT, 1)
         }
       }
     }
+    if (a.tma_store && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    __syncwarp();
   }
   tc_fence_before();
   __syncthreads();
@@ -420,15 +501,15 @@ bool make_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* base
 }
 
 template <int BN, int MODE>
-int launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb2, const TcArgs& args, long long tiles,
-           cudaStream_t st) {
+int launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb2, const CUtensorMap& mo,
+           const TcArgs& args, long long tiles, cudaStream_t st) {
   using L = Layout<BN, MODE>;
   auto k = conv_tc_kernel<BN, MODE>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
   int dev = 0, sms = ub::kNumSMs;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const unsigned grid = (unsigned)(tiles < sms ? tiles : sms);
-  k<<<grid, NT, L::SMEM, st>>>(ma, mb, mb2, args);
+  k<<<grid, NT, L::SMEM, st>>>(ma, mb, mb2, mo, args);
   UB_CHECK_LAUNCH();
   return 0;
 }
@@ -574,13 +655,30 @@ extern "C" int unblend_conv2d_tc(const float* x, const void* w_hi, const void* w
   const long long tiles = (long long)p->batch * p->h_out * a.tiles_w * a.tiles_n;
   UB_REQUIRE(tiles > 0 && tiles < (1LL << 31));
   a.tiles = tiles;
+  // Output map for the bulk-store epilogue: (channel, w, h, b) with boxes of one
+  // 16-row half of a warp's 32 positions x 32 channels (16 after GLU).
+  CUtensorMap mo;
+  memset(&mo, 0, sizeof(mo));
+  const int n_final = p->act == UNBLEND_ACT_GLU ? p->n_out / 2 : p->n_out;
+  a.tma_store = 0;
+  // Stores go out in 16-row halves, so a tile's valid rows must be whole halves.
+  if (!p->res && p->n_group >= n_final && p->out_sw >= n_final && m_valid % 16 == 0) {
+    const int nv = p->act == UNBLEND_ACT_GLU ? 16 : 32;
+    cuuint64_t od[4] = {(cuuint64_t)n_final, (cuuint64_t)p->w_out, (cuuint64_t)p->h_out, (cuuint64_t)p->batch};
+    cuuint64_t os[3] = {(cuuint64_t)p->out_sw * 4, (cuuint64_t)(p->out_sh > 0 ? p->out_sh : p->out_sw) * 4,
+                        (cuuint64_t)(p->out_sb > 0 ? p->out_sb : p->out_sw) * 4};
+    cuuint32_t ob[4] = {(cuuint32_t)nv, 16, 1, 1};
+    if (make_map(&mo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, y, od, os, ob,
+                 nv == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B))
+      a.tma_store = 1;
+  }
   cudaStream_t st = ub::as_stream(stream);
   if (mode == 0) {
-    if (block_n == 64) return launch<64, 0>(ma, mb, mb2, a, tiles, st);
-    if (block_n == 128) return launch<128, 0>(ma, mb, mb2, a, tiles, st);
-    return launch<256, 0>(ma, mb, mb2, a, tiles, st);
+    if (block_n == 64) return launch<64, 0>(ma, mb, mb2, mo, a, tiles, st);
+    if (block_n == 128) return launch<128, 0>(ma, mb, mb2, mo, a, tiles, st);
+    return launch<256, 0>(ma, mb, mb2, mo, a, tiles, st);
   }
-  if (block_n == 64) return launch<64, 1>(ma, mb, mb2, a, tiles, st);
-  if (block_n == 128) return launch<128, 1>(ma, mb, mb2, a, tiles, st);
-  return launch<256, 1>(ma, mb, mb2, a, tiles, st);
+  if (block_n == 64) return launch<64, 1>(ma, mb, mb2, mo, a, tiles, st);
+  if (block_n == 128) return launch<128, 1>(ma, mb, mb2, mo, a, tiles, st);
+  return launch<256, 1>(ma, mb, mb2, mo, a, tiles, st);
 }
