@@ -71,6 +71,32 @@ struct Layout {
 
 __device__ __forceinline__ float gelu(float x) { return ub::gelu_erf(x); }
 
+__device__ __forceinline__ float tanh_approx(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Activations of the bulk-store epilogue. MODE 1 (bf16 operands, results
+// feeding bf16 GEMMs) uses the tanh form of GELU (Hendrycks & Gimpel 2016,
+// within 5e-4 of the erf form) and sigmoid(x) = (1 + tanh(x/2)) / 2 on the
+// hardware tanh; MODE 0 keeps the exact erf GELU and a sigmoid from the
+// hardware exp2 and reciprocal (relative error ~1e-7).
+template <int MODE>
+__device__ __forceinline__ float epi_gelu(float x) {
+  if (MODE == 1) {
+    const float z = 0.7978845608028654f * fmaf(0.044715f * x, x * x, x);
+    return 0.5f * x * (1.0f + tanh_approx(z));
+  }
+  return ub::gelu_erf(x);
+}
+
+template <int MODE>
+__device__ __forceinline__ float epi_sigmoid(float x) {
+  if (MODE == 1) return fmaf(0.5f, tanh_approx(0.5f * x), 0.5f);
+  return __frcp_rn(1.0f + __expf(-x));
+}
+
 struct TileCoord {
   int b, h, w0, n0;
 };
@@ -299,12 +325,12 @@ __global__ void __launch_bounds__(NT, 1)
           }
           if (a.act == UNBLEND_ACT_GELU) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = gelu(v[j]);
+            for (int j = 0; j < 32; ++j) v[j] = epi_gelu<MODE>(v[j]);
           }
           const int nv = glu ? 16 : 32;
           if (glu) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = v[2 * j] * ub::sigmoidf_(v[2 * j + 1]);
+            for (int j = 0; j < 16; ++j) v[j] = v[2 * j] * epi_sigmoid<MODE>(v[2 * j + 1]);
           }
           if (a.stats && rv) {
             float t1 = 0.f, t2 = 0.f;
