@@ -134,12 +134,12 @@ __device__ __forceinline__ void split_tile(uint8_t* p, uint8_t* lo, int n4, int 
 // with MODE 0 the residuals into a second V^T tile. Each warp moves 32
 // consecutive keys of one 4-dim chunk per step, so the 32 scalar stores of a
 // step (one dim, 32 keys) fall in 32 different banks.
-template <int MODE>
+template <int MODE, int NW>
 __device__ __forceinline__ void transpose_v(const uint8_t* stage_v, uint8_t* vt, uint8_t* vt_lo, int t) {
   const int lane = t & 31, w = t >> 5;
 #pragma unroll
-  for (int u = 0; u < 8; ++u) {
-    const int unit = w * 8 + u;          // 32 units: (key half, box, chunk)
+  for (int u = 0; u < 32 / NW; ++u) {
+    const int unit = w * (32 / NW) + u;  // 32 units: (key half, box, chunk)
     const int kh = unit >> 4, box = (unit >> 3) & 1, c = unit & 7;
     const int key = kh * 32 + lane;
     const float4 val = *reinterpret_cast<const float4*>(stage_v + box * (64 * 128) + key * 128 + ((c ^ (key & 7)) << 4));
@@ -172,12 +172,18 @@ __global__ void __launch_bounds__(NT, 1)
   uint8_t* sQlo = smem + L::Q_BYTES;
   uint8_t* sKV = smem + L::Q_TOTAL;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + L::STAGES * L::STAGE);
+  // K and V travel in separate barrier rings over the same stage slots, so the
+  // next K tile can land (and its QK^T start) while the P V of an older tile
+  // still holds that slot's V.
   uint64_t* q_full = bars;
   uint64_t* q_ready = bars + 1;
-  uint64_t* kv_full = bars + 2;
-  uint64_t* kv_conv = kv_full + L::STAGES;
-  uint64_t* kv_free = kv_conv + L::STAGES;
-  uint64_t* s_full = kv_free + L::STAGES;  // [2]
+  uint64_t* k_full = bars + 2;
+  uint64_t* k_conv = k_full + L::STAGES;
+  uint64_t* k_free = k_conv + L::STAGES;
+  uint64_t* v_full = k_free + L::STAGES;
+  uint64_t* v_conv = v_full + L::STAGES;
+  uint64_t* v_free = v_conv + L::STAGES;
+  uint64_t* s_full = v_free + L::STAGES;  // [2]
   uint64_t* p_ready = s_full + 2;          // [2]
   uint64_t* o_done = p_ready + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 1);
@@ -194,9 +200,12 @@ __global__ void __launch_bounds__(NT, 1)
     mbar_init(q_full, 1);
     mbar_init(q_ready, 4);
     for (int s = 0; s < L::STAGES; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_conv[s], 4);
-      mbar_init(&kv_free[s], 1);
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_conv[s], 2);
+      mbar_init(&k_free[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_conv[s], 2);
+      mbar_init(&v_free[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
@@ -212,19 +221,26 @@ __global__ void __launch_bounds__(NT, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    if (lane == 0) {
+    if (lane == 0) {  // Q, then the K ring
       mbar_expect_tx(q_full, L::Q_BYTES);
       tma_load_5d(sQ, &mapQ, q_full, 0, h, q0, bi, bo);
       tma_load_5d(sQ + BQ * 128, &mapQ, q_full, 32, h, q0, bi, bo);
       for (int j = 0; j < nkv; ++j) {
         const int s = j % L::STAGES, r = j / L::STAGES;
-        if (r > 0 && !mbar_wait(&kv_free[s], (r - 1) & 1)) break;
+        if (r > 0 && !mbar_wait(&k_free[s], (r - 1) & 1)) break;
         uint8_t* st = sKV + s * L::STAGE;
-        mbar_expect_tx(&kv_full[s], 2 * L::KV_BYTES);
-        tma_load_5d(st + L::K_OFF, &mapK, &kv_full[s], 0, h, j * BK, bi, bo);
-        tma_load_5d(st + L::K_OFF + BK * 128, &mapK, &kv_full[s], 32, h, j * BK, bi, bo);
-        tma_load_5d(st + L::V_OFF, &mapV, &kv_full[s], 0, h, j * BK, bi, bo);
-        tma_load_5d(st + L::V_OFF + BK * 128, &mapV, &kv_full[s], 32, h, j * BK, bi, bo);
+        mbar_expect_tx(&k_full[s], L::KV_BYTES);
+        tma_load_5d(st + L::K_OFF, &mapK, &k_full[s], 0, h, j * BK, bi, bo);
+        tma_load_5d(st + L::K_OFF + BK * 128, &mapK, &k_full[s], 32, h, j * BK, bi, bo);
+      }
+    } else if (lane == 1) {  // the V ring
+      for (int j = 0; j < nkv; ++j) {
+        const int s = j % L::STAGES, r = j / L::STAGES;
+        if (r > 0 && !mbar_wait(&v_free[s], (r - 1) & 1)) break;
+        uint8_t* st = sKV + s * L::STAGE;
+        mbar_expect_tx(&v_full[s], L::KV_BYTES);
+        tma_load_5d(st + L::V_OFF, &mapV, &v_full[s], 0, h, j * BK, bi, bo);
+        tma_load_5d(st + L::V_OFF + BK * 128, &mapV, &v_full[s], 32, h, j * BK, bi, bo);
       }
     }
   } else if (warp == 1) {
@@ -248,22 +264,23 @@ __global__ void __launch_bounds__(NT, 1)
           }
         }
         umma_commit(&s_full[j & 1]);
+        umma_commit(&k_free[j % L::STAGES]);
       };
-      if (ok) ok = mbar_wait(&kv_conv[0], 0);
+      if (ok) ok = mbar_wait(&k_conv[0], 0);
       if (ok) {
         tc_fence_after();
         issue_s(0);
       }
       for (int j = 0; j < nkv && ok; ++j) {
         if (j + 1 < nkv) {
-          if (!mbar_wait(&kv_conv[(j + 1) % L::STAGES], ((j + 1) / L::STAGES) & 1)) {
+          if (!mbar_wait(&k_conv[(j + 1) % L::STAGES], ((j + 1) / L::STAGES) & 1)) {
             ok = false;
             break;
           }
           tc_fence_after();
           issue_s(j + 1);
         }
-        if (!mbar_wait(&p_ready[j & 1], (j >> 1) & 1)) {
+        if (!mbar_wait(&p_ready[j & 1], (j >> 1) & 1) || !mbar_wait(&v_conv[j % L::STAGES], (j / L::STAGES) & 1)) {
           ok = false;
           break;
         }
@@ -284,7 +301,7 @@ __global__ void __launch_bounds__(NT, 1)
           }
         }
         umma_commit(o_done);
-        umma_commit(&kv_free[s]);
+        umma_commit(&v_free[s]);
       }
       if (!ok) atomicExch(&g_error_flag, 3);
     }
@@ -298,16 +315,23 @@ __global__ void __launch_bounds__(NT, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(q_ready);
     }
+    // Warps 6-7 prepare K tiles, warps 8-9 V tiles.
+    const bool k_role = warp < 8;
+    const int rt = ct & 63;
     for (int j = 0; j < nkv && ok; ++j) {
       const int s = j % L::STAGES, r = j / L::STAGES;
-      if (!mbar_wait(&kv_full[s], r & 1)) break;
       uint8_t* st = sKV + s * L::STAGE;
-      split_tile<MODE>(st + L::K_OFF, st + L::KLO_OFF, L::KV_BYTES / 16, ct, 128, BK, j * BK, a.rope, a.rope_len,
-                       a.hd);
-      transpose_v<MODE>(st + L::V_OFF, st + L::VT_OFF, st + (MODE == 0 ? L::VTLO_OFF : L::VT_OFF), ct);
+      if (k_role) {
+        if (!mbar_wait(&k_full[s], r & 1)) break;
+        split_tile<MODE>(st + L::K_OFF, st + L::KLO_OFF, L::KV_BYTES / 16, rt, 64, BK, j * BK, a.rope, a.rope_len,
+                         a.hd);
+      } else {
+        if (!mbar_wait(&v_full[s], r & 1)) break;
+        transpose_v<MODE, 2>(st + L::V_OFF, st + L::VT_OFF, st + (MODE == 0 ? L::VTLO_OFF : L::VT_OFF), rt);
+      }
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&kv_conv[s]);
+      if (lane == 0) mbar_arrive(k_role ? &k_conv[s] : &v_conv[s]);
     }
   } else {
     // Softmax warps 2-5: thread = query row 32*(warp%4) + lane. The running
