@@ -464,9 +464,14 @@ extern "C" int unblend_attention_bf16(const void* q, const void* k, const void* 
   a.g_si = p->g_si;
   a.g_sr = p->g_sr;
   a.c = p->scale * 1.4426950408889634f;
-  long long grid = 2LL * sm_count();
-  if (grid > units) grid = units;
   cudaFuncSetAttribute(attention_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+  // Persistent: exactly the CTAs that fit at once (2 per SM by design).
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attention_bf16_kernel, NT, SMEM) != cudaSuccess ||
+      per_sm < 1)
+    per_sm = 1;
+  long long grid = (long long)per_sm * sm_count();
+  if (grid > units) grid = units;
   attention_bf16_kernel<<<(unsigned)grid, NT, SMEM, ub::as_stream(stream)>>>(mq, mk, mv, a);
   UB_CHECK_LAUNCH();
   return 0;

@@ -211,19 +211,19 @@ __global__ void __launch_bounds__(ROWS) dconv_apply_kernel(float* __restrict__ x
 }
 
 // ---------------------------------------------------------------------------
-// Persistent, channel-blocked z_stats / apply for the thin DConv levels
-// (hidden width <= 16). A CTA walks work items (group, block of IROWS rows) in
-// a grid-stride loop. Thread t keeps the W2 rows of its CPT output channels
-// (value and gate rows) in registers for the whole kernel and walks rows
-// t / CG, t / CG + RPP, ... of each item; GELU(GN1(h)) of the item's rows is
-// staged in shared memory (a broadcast read feeding 2*CPT dot products).
-// apply additionally streams x through shared memory with bulk async copies
-// (cp.async.bulk, double-buffered across items): the load of the next item's
-// rows and the store of the previous one overlap the current update.
+// Persistent, channel-blocked z_stats for the thin DConv levels (hidden
+// width <= 16, padded to a multiple of 4 by the caller so h rows are 16-byte
+// aligned). A CTA walks work items (group, block of IROWS rows) in a
+// grid-stride loop with the h rows of the next NBUF-1 items already in flight
+// (bulk async copies into a shared-memory ring). Thread t keeps the W2 rows of
+// its CPT output channels (value and gate rows) in registers for the whole
+// kernel and walks rows t / CG, t / CG + RPP, ... of each item; GELU(GN1(h))
+// of the item's rows is staged in shared memory (a broadcast read feeding
+// 2*CPT dot products).
 constexpr int CPT = 2;      // output channels per thread
 constexpr int NTH2 = 256;   // threads per CTA (CG * RPP <= NTH2)
 constexpr int IROWS = 64;   // rows per work item
-constexpr int MAXC2 = 384;  // largest C of the persistent apply (x staging: 2 x IROWS x C floats)
+constexpr int NBUF = 4;     // items in flight: loads run NBUF-1 items ahead of the compute
 
 __device__ __forceinline__ uint32_t sm_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 
@@ -233,12 +233,6 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                    sm_u32(dst)),
                "l"(src), "r"(bytes), "r"(sm_u32(bar))
                : "memory");
-}
-
-__device__ __forceinline__ void bulk_store(void* dst, const void* src, uint32_t bytes) {
-  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(sm_u32(src)), "r"(bytes)
-               : "memory");
-  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
 
 // Bounded wait (about 2 s of %globaltimer) for the phase `parity` of `bar`; false on timeout.
@@ -259,15 +253,16 @@ __device__ __forceinline__ bool wait_phase(uint64_t* bar, uint32_t parity) {
   }
 }
 
+// GELU(GN1(h)) of an item's rows into a_s [IROWS][MAXH]; hs holds the item's h
+// rows (H floats each) already in shared memory.
 template <int MAXH>
-__device__ __forceinline__ void stage_act(const float* __restrict__ h, int g, int r0, int nrows, int rows, int H,
-                                          float m1, float rs1, const float* __restrict__ g1w,
-                                          const float* __restrict__ g1b, float* __restrict__ a_s) {
+__device__ __forceinline__ void stage_act(const float* __restrict__ hs, int nrows, int H, float m1, float rs1,
+                                          const float* __restrict__ g1w, const float* __restrict__ g1b,
+                                          float* __restrict__ a_s) {
   for (int i = threadIdx.x; i < IROWS * MAXH; i += blockDim.x) {
     const int r = i / MAXH, j = i - (i / MAXH) * MAXH;
     float v = 0.f;
-    if (j < H && r < nrows)
-      v = ub::gelu_erf((h[((long long)g * rows + r0 + r) * H + j] - m1) * rs1 * __ldg(g1w + j) + __ldg(g1b + j));
+    if (j < H && r < nrows) v = ub::gelu_erf((hs[r * H + j] - m1) * rs1 * __ldg(g1w + j) + __ldg(g1b + j));
     a_s[i] = v;
   }
 }
@@ -293,8 +288,6 @@ __device__ __forceinline__ float dot_a(const float* __restrict__ a, const float 
   return z;
 }
 
-// 1 / (1 + e^-x) with the hardware exp2 and reciprocal (relative error ~1e-7).
-__device__ __forceinline__ float sigmoid_fast(float x) { return __frcp_rn(1.0f + __expf(-x)); }
 
 template <int MAXH>
 __device__ __forceinline__ void load_w(const float* __restrict__ w2, const float* __restrict__ b2, int H, int cg,
@@ -308,6 +301,8 @@ __device__ __forceinline__ void load_w(const float* __restrict__ w2, const float
   }
 }
 
+static __device__ int g_dconv_error = 0;
+
 template <int MAXH, int HW>
 __global__ void __launch_bounds__(NTH2) dconv_z_stats3_kernel(const float* __restrict__ h, int groups, int rows, int H,
                                                                int C, const float* __restrict__ st1,
@@ -316,8 +311,10 @@ __global__ void __launch_bounds__(NTH2) dconv_z_stats3_kernel(const float* __res
                                                                const float* __restrict__ w2,
                                                                const float* __restrict__ b2,
                                                                double* __restrict__ stats2) {
+  __shared__ __align__(128) float hbuf[NBUF][IROWS * MAXH];
   __shared__ __align__(16) float a_s[IROWS * MAXH];
   __shared__ double red[2][NTH2 / 32];
+  __shared__ __align__(8) uint64_t full[NBUF];
   const int CG = C / CPT;
   const int RPP = blockDim.x / CG;
   const int cg = threadIdx.x % CG, rsub = threadIdx.x / CG;
@@ -326,20 +323,43 @@ __global__ void __launch_bounds__(NTH2) dconv_z_stats3_kernel(const float* __res
   load_w<MAXH>(w2, b2, H, cg, live, w, bz);
   const int nblk = (rows + IROWS - 1) / IROWS;
   const long long items = (long long)groups * nblk;
-  for (long long it = blockIdx.x; it < items; it += gridDim.x) {
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NBUF; ++i)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(sm_u32(&full[i])) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  auto issue = [&](long long it, int buf) {
+    const int g = (int)(it / nblk);
+    const int r0 = (int)(it - (long long)g * nblk) * IROWS;
+    const int nr = min(IROWS, rows - r0);
+    bulk_load(hbuf[buf], h + ((long long)g * rows + r0) * H, (uint32_t)(nr * H * 4), &full[buf]);
+  };
+  if (threadIdx.x == 0)
+    for (int i = 0; i < NBUF - 1 && blockIdx.x + (long long)i * gridDim.x < items; ++i)
+      issue(blockIdx.x + (long long)i * gridDim.x, i);
+  bool ok = true;
+  int k = 0;
+  for (long long it = blockIdx.x; it < items; it += gridDim.x, ++k) {
+    const int b = k % NBUF;
     const int g = (int)(it / nblk);
     const int r0 = (int)(it - (long long)g * nblk) * IROWS;
     const int nrows = min(IROWS, rows - r0);
-    __syncthreads();  // the previous item's readers are done with a_s and red
-    stage_act<MAXH>(h, g, r0, nrows, rows, H, st1[2 * g], st1[2 * g + 1], g1w, g1b, a_s);
+    // Buffer (k + NBUF - 1) % NBUF was last read by the previous item's
+    // staging, which finished before that item's second barrier.
+    const long long ahead = it + (long long)(NBUF - 1) * gridDim.x;
+    if (threadIdx.x == 0 && ahead < items) issue(ahead, (k + NBUF - 1) % NBUF);
+    ok = wait_phase(&full[b], (k / NBUF) & 1);
+    if (__syncthreads_or(!ok)) break;
+    stage_act<MAXH>(hbuf[b], nrows, H, st1[2 * g], st1[2 * g + 1], g1w, g1b, a_s);
     __syncthreads();
     float s1 = 0.f, s2 = 0.f;
     if (live) {
       for (int r = rsub; r < nrows; r += RPP) {
         const float* a = a_s + r * MAXH;
 #pragma unroll
-        for (int k = 0; k < 2 * CPT; ++k) {
-          const float z = dot_a<MAXH, HW>(a, w[k]) + bz[k];
+        for (int q = 0; q < 2 * CPT; ++q) {
+          const float z = dot_a<MAXH, HW>(a, w[q]) + bz[q];
           s1 += z;
           s2 += z * z;
         }
@@ -361,109 +381,20 @@ __global__ void __launch_bounds__(NTH2) dconv_z_stats3_kernel(const float* __res
       atomicAdd(stats2 + 2 * g + 1, a1);
     }
   }
+  if (threadIdx.x == 0 && !ok) atomicExch(&g_dconv_error, 1);
 }
 
-static __device__ int g_dconv_error = 0;
 
-template <int MAXH, int HW>
-__global__ void __launch_bounds__(NTH2) dconv_apply3_kernel(float* __restrict__ x, long long x_gs, int groups,
-                                                             const float* __restrict__ h, int rows, int H, int C,
-                                                             const float* __restrict__ st1,
-                                                             const float* __restrict__ g1w,
-                                                             const float* __restrict__ g1b,
-                                                             const float* __restrict__ w2,
-                                                             const float* __restrict__ b2,
-                                                             const float* __restrict__ st2,
-                                                             const float* __restrict__ g2w,
-                                                             const float* __restrict__ g2b,
-                                                             const float* __restrict__ scale) {
-  extern __shared__ __align__(128) float dyn[];
-  float* xbuf = dyn;                          // [2][IROWS * C]
-  float* a_s = dyn + 2 * IROWS * C;           // [IROWS * MAXH]
-  __shared__ __align__(8) uint64_t full[2];
-  const int CG = C / CPT;
-  const int RPP = blockDim.x / CG;
-  const int cg = threadIdx.x % CG, rsub = threadIdx.x / CG;
-  const bool live = rsub < RPP;
-  float w[2 * CPT][MAXH], bz[2 * CPT];
-  load_w<MAXH>(w2, b2, H, cg, live, w, bz);
-  float gam[2 * CPT], bet[2 * CPT], sc[CPT];
-#pragma unroll
-  for (int k = 0; k < 2 * CPT; ++k) {
-    gam[k] = live ? __ldg(g2w + 2 * cg * CPT + k) : 0.f;
-    bet[k] = live ? __ldg(g2b + 2 * cg * CPT + k) : 0.f;
-  }
-#pragma unroll
-  for (int e = 0; e < CPT; ++e) sc[e] = live ? __ldg(scale + cg * CPT + e) : 0.f;
-  const int nblk = (rows + IROWS - 1) / IROWS;
-  const long long items = (long long)groups * nblk;
-  if (threadIdx.x == 0) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(sm_u32(&full[0])) : "memory");
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(sm_u32(&full[1])) : "memory");
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  __syncthreads();
-  auto item_ptr = [&](long long it, int& g, int& r0, int& nrows) -> float* {
-    g = (int)(it / nblk);
-    r0 = (int)(it - (long long)g * nblk) * IROWS;
-    nrows = min(IROWS, rows - r0);
-    return x + (long long)g * x_gs + (long long)r0 * C;
-  };
-  if (threadIdx.x == 0 && blockIdx.x < items) {
-    int g, r0, nr;
-    float* src = item_ptr(blockIdx.x, g, r0, nr);
-    bulk_load(xbuf, src, (uint32_t)(nr * C * 4), &full[0]);
-  }
-  bool ok = true;
-  int k = 0;
-  for (long long it = blockIdx.x; it < items; it += gridDim.x, ++k) {
-    const int b = k & 1;
-    int g, r0, nrows;
-    float* xg = item_ptr(it, g, r0, nrows);
-    // Prefetch the next item into the other buffer once its previous store has read it.
-    if (threadIdx.x == 0 && it + gridDim.x < items) {
-      asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-      int g2, r2, n2;
-      float* src = item_ptr(it + gridDim.x, g2, r2, n2);
-      bulk_load(xbuf + (b ^ 1) * IROWS * C, src, (uint32_t)(n2 * C * 4), &full[b ^ 1]);
-    }
-    stage_act<MAXH>(h, g, r0, nrows, rows, H, st1[2 * g], st1[2 * g + 1], g1w, g1b, a_s);
-    ok = wait_phase(&full[b], (k >> 1) & 1);
-    if (__syncthreads_or(!ok)) break;
-    const float mean2 = st2[2 * g], rstd2 = st2[2 * g + 1];
-    // GN2 folded per item: (W2 a + b2 - mean2) * rstd2 * gamma + beta = (W2 a) * A + B.
-    float fa[2 * CPT], fb[2 * CPT];
-#pragma unroll
-    for (int q = 0; q < 2 * CPT; ++q) {
-      fa[q] = rstd2 * gam[q];
-      fb[q] = (bz[q] - mean2) * fa[q] + bet[q];
-    }
-    if (live) {
-      float* xs = xbuf + b * IROWS * C + cg * CPT;
-      for (int r = rsub; r < nrows; r += RPP) {
-        const float* a = a_s + r * MAXH;
-        float o[CPT];
-#pragma unroll
-        for (int e = 0; e < CPT; ++e) {
-          const float v = fmaf(dot_a<MAXH, HW>(a, w[2 * e]), fa[2 * e], fb[2 * e]);
-          const float gt = fmaf(dot_a<MAXH, HW>(a, w[2 * e + 1]), fa[2 * e + 1], fb[2 * e + 1]);
-          o[e] = sc[e] * (v * sigmoid_fast(gt));
-        }
-        float2* xp = reinterpret_cast<float2*>(xs + r * C);
-        float2 xv = *xp;
-        xv.x += o[0];
-        xv.y += o[1];
-        *xp = xv;
-      }
-    }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    __syncthreads();  // the item is updated in shared memory; a_s may be restaged
-    if (threadIdx.x == 0) bulk_store(xg, xbuf + b * IROWS * C, (uint32_t)(nrows * C * 4));
-  }
-  if (threadIdx.x == 0) {
-    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
-    if (!ok) atomicExch(&g_dconv_error, 1);
-  }
+// Grid of a persistent kernel: every CTA resident at once (items are dealt
+// round-robin, so a second wave would double the time of its CTAs' share).
+template <typename K>
+unsigned persistent_grid(K kernel, size_t smem, long long items) {
+  int dev = 0, sms = 148, per_sm = 1;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, NTH2, smem) != cudaSuccess || per_sm < 1)
+    per_sm = 1;
+  const long long cap = (long long)sms * per_sm;
+  return (unsigned)(items < cap ? items : cap);
 }
 
 int maxh_for(int H) { return H <= 8 ? 8 : H <= 16 ? 16 : H <= 32 ? 32 : H <= 64 ? 64 : 0; }
@@ -502,17 +433,16 @@ extern "C" int unblend_dconv_z_stats(const float* h, int groups, int rows, int h
   UB_REQUIRE(smem <= 220 * 1024);
   dim3 grid((rows + ROWS - 1) / ROWS, groups);
   cudaStream_t st = ub::as_stream(stream);
-  if (mh <= 16 && c % CPT == 0 && c / CPT <= NTH2) {
+  if (mh <= 16 && hid % 4 == 0 && c % CPT == 0 && c / CPT <= NTH2 && (reinterpret_cast<uintptr_t>(h) & 15) == 0) {
     const long long items = (long long)groups * ((rows + IROWS - 1) / IROWS);
-    const unsigned g2 = (unsigned)(items < 148LL * 8 ? items : 148LL * 8);
-    if (hid == 6)
-      dconv_z_stats3_kernel<8, 6><<<g2, NTH2, 0, st>>>(h, groups, rows, hid, c, st1, g1w, g1b, w2, b2, stats2);
-    else if (hid == 12)
-      dconv_z_stats3_kernel<16, 12><<<g2, NTH2, 0, st>>>(h, groups, rows, hid, c, st1, g1w, g1b, w2, b2, stats2);
-    else if (mh == 8)
-      dconv_z_stats3_kernel<8, 8><<<g2, NTH2, 0, st>>>(h, groups, rows, hid, c, st1, g1w, g1b, w2, b2, stats2);
-    else
-      dconv_z_stats3_kernel<16, 16><<<g2, NTH2, 0, st>>>(h, groups, rows, hid, c, st1, g1w, g1b, w2, b2, stats2);
+#define UB_ZS3(MH, HW)                                                                                         \
+  {                                                                                                            \
+    const unsigned g2 = persistent_grid(dconv_z_stats3_kernel<MH, HW>, 0, items);                           \
+    dconv_z_stats3_kernel<MH, HW><<<g2, NTH2, 0, st>>>(h, groups, rows, hid, c, st1, g1w, g1b, w2, b2, stats2); \
+  }
+    if (hid == 8) UB_ZS3(8, 8) else if (hid == 12) UB_ZS3(16, 12) else if (mh == 8) UB_ZS3(8, 4)
+    else UB_ZS3(16, 16)
+#undef UB_ZS3
     UB_CHECK_LAUNCH();
     return 0;
   }
@@ -540,25 +470,6 @@ extern "C" int unblend_dconv_apply(float* x, long long x_gs, const float* h, int
   UB_REQUIRE(smem <= 220 * 1024);
   dim3 grid((rows + ROWS - 1) / ROWS, groups);
   cudaStream_t st = ub::as_stream(stream);
-  if (mh <= 16 && c % 4 == 0 && c / CPT <= NTH2 && c <= MAXC2 && x_gs % 4 == 0 &&
-      (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
-    const long long items = (long long)groups * ((rows + IROWS - 1) / IROWS);
-    const size_t smem3 = sizeof(float) * (2 * (size_t)IROWS * c + (size_t)IROWS * mh);
-    const int per_sm = (int)((200 * 1024) / (smem3 + 1024)) < 4 ? (int)((200 * 1024) / (smem3 + 1024)) : 4;
-    const long long cap = 148LL * (per_sm > 0 ? per_sm : 1);
-    const unsigned g3 = (unsigned)(items < cap ? items : cap);
-#define UB_APPLY3(MH, HW)                                                                                    \
-  {                                                                                                          \
-    cudaFuncSetAttribute(dconv_apply3_kernel<MH, HW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem3); \
-    dconv_apply3_kernel<MH, HW><<<g3, NTH2, smem3, st>>>(x, x_gs, groups, h, rows, hid, c, st1, g1w, g1b, w2, b2, \
-                                                         st2, g2w, g2b, scale);                              \
-  }
-    if (hid == 6) UB_APPLY3(8, 6) else if (hid == 12) UB_APPLY3(16, 12) else if (mh == 8) UB_APPLY3(8, 8)
-    else UB_APPLY3(16, 16)
-#undef UB_APPLY3
-    UB_CHECK_LAUNCH();
-    return 0;
-  }
 #define UB_LAUNCH(MH)                                                                                         \
   {                                                                                                           \
     cudaFuncSetAttribute(dconv_apply_kernel<MH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);    \

@@ -316,9 +316,18 @@ __global__ void __launch_bounds__(GL<BN, MODE>::NT, 1)
 #pragma unroll 1
       for (int c0 = c_lo; c0 < c_lo + BN / 2; c0 += 32) {
         if (n0 + c0 >= gd.n) break;  // uniform across the warp
+        const bool bulk = a.tma_store && n0 + c0 + 32 <= gd.n;
+        // Residual row segment of this lane (lane = row on the bulk path), loaded
+        // before the TMEM read so the two latencies overlap.
+        float4 rr[8];
+        if (ACT != UNBLEND_ACT_GLU && bulk && a.res) {
+          const float4* rp = reinterpret_cast<const float4*>(a.res + (long long)my_row * a.ldr + gd.out_col0 + n0 + c0);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) rr[j] = my_row < a.m ? rp[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
         uint32_t acc[32];
         tmem_ld32(base + (uint32_t)c0, acc);
-        if (a.tma_store && n0 + c0 + 32 <= gd.n) {
+        if (bulk) {
           // Whole chunk: activation in the lane = row layout, packed into a
           // swizzled staging tile, stored by one bulk tensor copy.
           constexpr bool FAST = MODE == 1;
@@ -353,6 +362,15 @@ __global__ void __launch_bounds__(GL<BN, MODE>::NT, 1)
               v[4 * j + 1] = x0 * c2.y + x1 * c2.x;
               v[4 * j + 2] = x2 * c2.z - x3 * c2.w;
               v[4 * j + 3] = x2 * c2.w + x3 * c2.z;
+            }
+          }
+          if (ACT != UNBLEND_ACT_GLU && a.res) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              v[4 * j] += rr[j].x;
+              v[4 * j + 1] += rr[j].y;
+              v[4 * j + 2] += rr[j].z;
+              v[4 * j + 3] += rr[j].w;
             }
           }
           uint32_t w[OBF ? NV / 2 : NV];  // the packed row: NV/2 words of bf16 pairs, or NV fp32 words
@@ -663,6 +681,8 @@ extern "C" int unblend_gemm_tc(const void* a, long long lda, int rows, int a_col
   CUtensorMap mo;
   memset(&mo, 0, sizeof(mo));
   const int oesz = g.out_bf16 ? 2 : 4;
+  // Residual epilogues keep the transposed path (prefetched residual rows):
+  // measured faster than per-lane residual reads on the bulk path.
   bool tma = !p->res && (reinterpret_cast<uintptr_t>(p->out) & 15) == 0 && (p->ldo * oesz) % 16 == 0;
   for (int i = 0; i < p->groups && tma; ++i) tma = (p->group[i].out_col0 * oesz) % 16 == 0;
   if (tma) {

@@ -243,6 +243,20 @@ class HTDemucsCuda(nn.Module):
             self._put(f"{q}.g2.w", _interleave_rows(sd[f"{q}.4.weight"]))
             self._put(f"{q}.g2.b", _interleave_rows(sd[f"{q}.4.bias"]))
             self._put(f"{q}.scale", sd[f"{q}.6.scale"])
+            # Hidden width padded to a multiple of 4 with zero channels (16-byte h
+            # rows for the bulk copies of the fused kernels): the padded channels
+            # are exactly 0 before and after GELU(GN1) and meet zero weights in W2.
+            hid = sd[f"{q}.0.weight"].shape[0]
+            hp = -(-hid // 4) * 4
+            if hp != hid:
+                pad = hp - hid
+                c1 = _conv_w(sd[f"{q}.0.weight"])
+                self._put(f"{q}.c1p.w", torch.cat([c1, c1.new_zeros((pad,) + tuple(c1.shape[1:]))]))
+                self._put(f"{q}.c1p.b", torch.cat([sd[f"{q}.0.bias"], sd[f"{q}.0.bias"].new_zeros(pad)]))
+                self._put(f"{q}.g1p.w", torch.cat([sd[f"{q}.1.weight"], sd[f"{q}.1.weight"].new_zeros(pad)]))
+                self._put(f"{q}.g1p.b", torch.cat([sd[f"{q}.1.bias"], sd[f"{q}.1.bias"].new_zeros(pad)]))
+                c2 = _interleave_rows(_conv_w(sd[f"{q}.3.weight"]))
+                self._put(f"{q}.c2p.w", torch.nn.functional.pad(c2, (0, pad)))
 
     def _tables(self, device: torch.device, F: int, T: int, Lt: int) -> dict:
         """Window, positional and frequency-embedding tables (cached per device and shape)."""
@@ -374,24 +388,29 @@ class HTDemucsCuda(nn.Module):
                           self.w(f"{q}.g2.w").data_ptr(), self.w(f"{q}.g2.b").data_ptr(),
                           self.w(f"{q}.scale").data_ptr(), groups, W, C, x_gs)
                 continue
-            if self.precision != "fp32-simt" and conv1_smem <= 220 * 1024 and C % 4 == 0:
-                _lib.call("unblend_dconv_conv1", x.t.data_ptr(), x_gs, groups, W, C, self.w(f"{q}.c1.w").data_ptr(),
-                          self.w(f"{q}.c1.b").data_ptr(), hid, dil, h.t.data_ptr(), st1.data_ptr(),
+            fused = self.precision != "fp32-simt" and conv1_smem <= 220 * 1024 and C % 4 == 0
+            hp = -(-hid // 4) * 4
+            padded = fused and hp != hid
+            pw = (lambda n: self.w(f"{q}.{n[:2]}p.{n[3:]}")) if padded else (lambda n: self.w(f"{q}.{n}"))
+            if fused:
+                h = Act.freq(B, H, W, hp, dev)
+                _lib.call("unblend_dconv_conv1", x.t.data_ptr(), x_gs, groups, W, C, pw("c1.w").data_ptr(),
+                          pw("c1.b").data_ptr(), hp, dil, h.t.data_ptr(), st1.data_ptr(),
                           work=6.0 * groups * W * C * hid)
             else:
                 self._conv(x, self.w(f"{q}.c1.w"), self.w(f"{q}.c1.b"), h, h_out=H, w_out=W, n_out=hid, kw=3,
                            dw=dil, pw=dil, stats=st1, stats_per_h=per_h)
             s1 = self._stats(st1, groups, W * hid)
-            if self.precision != "fp32-simt" and C % 4 == 0:
+            if fused:
                 # z = W2 GELU(GN1(h)) is recomputed instead of stored: once for
                 # the GN2 statistics, once for the in-place residual update.
                 st2 = torch.zeros(2 * groups, device=dev, dtype=torch.float64)
-                args = (self.w(f"{q}.g1.w").data_ptr(), self.w(f"{q}.g1.b").data_ptr(),
-                        self.w(f"{q}.c2.w").data_ptr(), self.w(f"{q}.c2.b").data_ptr())
-                _lib.call("unblend_dconv_z_stats", h.t.data_ptr(), groups, W, hid, C, s1.data_ptr(), *args,
+                args = (pw("g1.w").data_ptr(), pw("g1.b").data_ptr(), pw("c2.w").data_ptr(),
+                        self.w(f"{q}.c2.b").data_ptr())
+                _lib.call("unblend_dconv_z_stats", h.t.data_ptr(), groups, W, hp, C, s1.data_ptr(), *args,
                           st2.data_ptr(), work=4.0 * groups * W * C * hid)
                 s2 = self._stats(st2, groups, W * 2 * C)
-                _lib.call("unblend_dconv_apply", x.t.data_ptr(), x_gs, h.t.data_ptr(), groups, W, hid, C,
+                _lib.call("unblend_dconv_apply", x.t.data_ptr(), x_gs, h.t.data_ptr(), groups, W, hp, C,
                           s1.data_ptr(), *args, s2.data_ptr(), self.w(f"{q}.g2.w").data_ptr(),
                           self.w(f"{q}.g2.b").data_ptr(), self.w(f"{q}.scale").data_ptr(),
                           work=4.0 * groups * W * C * hid)
