@@ -57,6 +57,12 @@ struct TcArgs {
   int tma_store;  // 1: whole 32-column chunks leave through TMA bulk tensor stores (no residual)
 };
 
+// TMEM columns of the double-buffered accumulator: 2 x BN rounded up to a power of two.
+template <int BN>
+struct TmemCols {
+  static constexpr int value = 2 * BN <= 128 ? 128 : 2 * BN <= 256 ? 256 : 512;
+};
+
 template <int BN, int MODE>
 struct Layout {
   static constexpr int A_BYTES = 128 * 128;                          // fp32 staging, 128 rows x 32 K
@@ -147,7 +153,7 @@ __global__ void __launch_bounds__(NT, 1)
     }
     fence_mbar_init();
   }
-  if (warp == 1) tmem_alloc(tmem_slot, 2 * BN);
+  if (warp == 1) tmem_alloc(tmem_slot, TmemCols<BN>::value);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -497,7 +503,7 @@ __global__ void __launch_bounds__(NT, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 2 * BN);
+    tmem_dealloc(tmem, TmemCols<BN>::value);
   }
 }
 
@@ -559,7 +565,7 @@ extern "C" int unblend_conv2d_tc(const float* x, const void* w_hi, const void* w
                                  const UnblendConvParams* p, int mode, int block_n, void* stream) {
   UB_REQUIRE(x && w_hi && y && p && (mode == 0 || mode == 1));
   UB_REQUIRE(mode == 1 || w_lo);
-  UB_REQUIRE(block_n == 64 || block_n == 128 || block_n == 256);
+  UB_REQUIRE(block_n == 64 || block_n == 96 || block_n == 128 || block_n == 192 || block_n == 256);
   UB_REQUIRE(p->prologue == UNBLEND_PRO_NONE);
   UB_REQUIRE(p->c_in % 8 == 0 && p->c_in >= 16);
   UB_REQUIRE(p->n_group % 4 == 0 && p->out_sg % 4 == 0 && p->out_sw % 4 == 0 && p->out_sh % 4 == 0 &&
@@ -701,10 +707,14 @@ extern "C" int unblend_conv2d_tc(const float* x, const void* w_hi, const void* w
   cudaStream_t st = ub::as_stream(stream);
   if (mode == 0) {
     if (block_n == 64) return launch<64, 0>(ma, mb, mb2, mo, a, tiles, st);
+    if (block_n == 96) return launch<96, 0>(ma, mb, mb2, mo, a, tiles, st);
     if (block_n == 128) return launch<128, 0>(ma, mb, mb2, mo, a, tiles, st);
+    if (block_n == 192) return launch<192, 0>(ma, mb, mb2, mo, a, tiles, st);
     return launch<256, 0>(ma, mb, mb2, mo, a, tiles, st);
   }
   if (block_n == 64) return launch<64, 1>(ma, mb, mb2, mo, a, tiles, st);
+  if (block_n == 96) return launch<96, 1>(ma, mb, mb2, mo, a, tiles, st);
   if (block_n == 128) return launch<128, 1>(ma, mb, mb2, mo, a, tiles, st);
+  if (block_n == 192) return launch<192, 1>(ma, mb, mb2, mo, a, tiles, st);
   return launch<256, 1>(ma, mb, mb2, mo, a, tiles, st);
 }

@@ -126,6 +126,23 @@ def split_tf32(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
 PRECISIONS = ("fp32", "bf16", "fp32-simt")
 
 
+def _block_n(n_out: int, bn256_min: int) -> int:
+    """Output-channel tile of the tensor-core convolution: the fewest wasted MMA columns.
+
+    Candidates 64, 96, 128, 192 (and 256 from ``bn256_min`` channels on): the one
+    whose tiles cover ``n_out`` with the least padding, preferring the wider tile
+    on ties (fewer re-reads of the input rows).
+    """
+    cands = [64, 96, 128, 192] + ([256] if n_out >= bn256_min else [])
+    best = None
+    for bn in cands:
+        waste = -(-n_out // bn) * bn - n_out
+        key = (waste, -bn)
+        if best is None or key < best[0]:
+            best = (key, bn)
+    return best[1]
+
+
 class HTDemucsCuda(nn.Module):
     """HTDemucs separation forward as sm_100a CUDA kernels.
 
@@ -316,9 +333,7 @@ class HTDemucsCuda(nn.Module):
                 p.prologue, p.pro_x2 = PRO_NONE, None
             mode = _lib.TC_TF32X3 if self.precision == "fp32" else _lib.TC_BF16
             whi, wlo = self._tc_weight(w, mode)
-            block_n = 64 if n_out <= 64 else 128
-            if n_out >= self._bn256_min[mode]:
-                block_n = 256
+            block_n = _block_n(n_out, self._bn256_min[mode])
             _lib.call("unblend_conv2d_tc", x.t.data_ptr(), whi.data_ptr(), _lib.ptr(wlo), _lib.ptr(b), y,
                       ctypes_byref(p), mode, block_n, work=flops)
             return
