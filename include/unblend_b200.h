@@ -132,12 +132,15 @@ int unblend_dconv_tail(float* x, const float* z, const float* stats2, const floa
 /* Fused DConv layer (unblend/blocks.py:238-317) in three streaming passes.
  * x element (g, r, c) is at x + g*x_gs + r*c_in + c for groups g (GroupNorm
  * groups: (batch, frequency) rows or batch items) and rows r along time.
+ * The hidden width hid is padded to hs = round_up(hid, 4): h rows, W1 rows,
+ * the GN1 affine and W2 rows hold hs values, those past hid zero (so the
+ * padded hidden channels stay exactly 0 and meet zero weights).
  * conv1: h[g, r, :] = b1 + sum_t W1[:, t, :] x[g, r + (t-1)*dil, :] (zero
- *   padded), W1 [hid, 3, c]; accumulates (sum, sumsq) of h per group into
+ *   padded), W1 [hs, 3, c]; accumulates (sum, sumsq) of h per group into
  *   stats (double, zeroed by the caller). Shared memory must hold
- *   (128 + 2*dil)*(c+4) + 3*hid*c floats (<= 220 KiB).
+ *   (128 + 2*dil)*(c+4) + 3*hs*c floats (<= 220 KiB).
  * z_stats: (sum, sumsq) per group of z = W2 gelu(gn1(h)) + b2 with
- *   st1 = (mean, rstd) of h; W2 [2c, hid] rows interleaved (value, gate).
+ *   st1 = (mean, rstd) of h; W2 [2c, hs] rows interleaved (value, gate).
  * apply: x += scale * glu(gn2(z)) with z recomputed, st2 = (mean, rstd) of z,
  *   GN2 affine interleaved like W2. z is never stored. */
 int unblend_dconv_conv1(const float* x, long long x_gs, int groups, int rows, int c, const float* w1,

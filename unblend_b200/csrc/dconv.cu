@@ -253,16 +253,16 @@ __device__ __forceinline__ bool wait_phase(uint64_t* bar, uint32_t parity) {
   }
 }
 
-// GELU(GN1(h)) of an item's rows into a_s [IROWS][MAXH]; hs holds the item's h
-// rows (H floats each) already in shared memory.
+// GELU(GN1(h)) of an item's nrows rows into a_s [nrows][MAXH]; hs holds the
+// item's h rows (H floats each) already in shared memory.
 template <int MAXH>
 __device__ __forceinline__ void stage_act(const float* __restrict__ hs, int nrows, int H, float m1, float rs1,
                                           const float* __restrict__ g1w, const float* __restrict__ g1b,
                                           float* __restrict__ a_s) {
-  for (int i = threadIdx.x; i < IROWS * MAXH; i += blockDim.x) {
+  for (int i = threadIdx.x; i < nrows * MAXH; i += blockDim.x) {
     const int r = i / MAXH, j = i - (i / MAXH) * MAXH;
     float v = 0.f;
-    if (j < H && r < nrows) v = ub::gelu_erf((hs[r * H + j] - m1) * rs1 * __ldg(g1w + j) + __ldg(g1b + j));
+    if (j < H) v = ub::gelu_erf((hs[r * H + j] - m1) * rs1 * __ldg(g1w + j) + __ldg(g1b + j));
     a_s[i] = v;
   }
 }
@@ -385,6 +385,274 @@ __global__ void __launch_bounds__(NTH2) dconv_z_stats3_kernel(const float* __res
 }
 
 
+// ---------------------------------------------------------------------------
+// Register-blocked conv1 for the thin levels (h rows of HP = 4, 8, 12 or 16
+// floats, of which the first HW are computed and the rest written as 0).
+// A CTA owns C1_IR rows of one group; lane l of warp w computes the HW
+// outputs of rows w*32*C1_RT + l + 32*i (i < C1_RT), so one broadcast read of
+// the weights of an input (tap, channel) feeds C1_RT*HW FMAs and the
+// x reads of a warp hit 32 consecutive rows of a tile with an odd row stride
+// (no bank conflicts). Channels are staged C1_CK at a time with their
+// dilation halo, zero outside [0, rows).
+constexpr int C1_NW = 4;
+constexpr int C1_NT = C1_NW * 32;
+constexpr int C1_RT = 3;
+constexpr int C1_IR = C1_NT * C1_RT;  // rows per CTA
+constexpr int C1_CK = 16;              // channels per staged chunk
+constexpr int C1_XS = C1_CK + 1;       // staged row stride (floats)
+
+template <int HP, int HW>
+__global__ void __launch_bounds__(C1_NT) dconv_conv1b_kernel(const float* __restrict__ x, long long x_gs, int rows,
+                                                             int C, const float* __restrict__ w1,
+                                                             const float* __restrict__ b1, int dil,
+                                                             float* __restrict__ h, double* __restrict__ stats) {
+  extern __shared__ __align__(16) float sm[];
+  float* ws = sm;              // [C][3][HP]
+  float* xc = sm + 3 * C * HP; // [C1_IR + 2 * dil][C1_XS]
+  const int g = blockIdx.y;
+  const int r0 = blockIdx.x * C1_IR;
+  const float* xg = x + (long long)g * x_gs;
+  const int tid = threadIdx.x;
+  for (int i = tid; i < HP * 3 * C; i += C1_NT) {
+    const int j = i / (3 * C), rem = i - j * 3 * C;
+    const int t = rem / C, c = rem - t * C;
+    ws[(c * 3 + t) * HP + j] = __ldg(w1 + i);
+  }
+  const int lr0 = (tid >> 5) * 32 * C1_RT + (tid & 31);
+  float acc[C1_RT][HW];
+#pragma unroll
+  for (int j = 0; j < HW; ++j) {
+    const float b = __ldg(b1 + j);
+#pragma unroll
+    for (int i = 0; i < C1_RT; ++i) acc[i][j] = b;
+  }
+  const int last = min(rows, r0 + C1_IR + dil);  // rows past this are never read
+  const int nst = min(C1_IR, rows - r0) + 2 * dil;
+  for (int c0 = 0; c0 < C; c0 += C1_CK) {
+    __syncthreads();  // the previous chunk is consumed (and ws is written)
+    for (int i = tid; i < nst * (C1_CK / 4); i += C1_NT) {
+      const int rr = i / (C1_CK / 4), q = i - rr * (C1_CK / 4);
+      const int r = r0 - dil + rr;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (r >= 0 && r < last) v = __ldg(reinterpret_cast<const float4*>(xg + (long long)r * C + c0 + 4 * q));
+      float* d = xc + rr * C1_XS + 4 * q;
+      d[0] = v.x;
+      d[1] = v.y;
+      d[2] = v.z;
+      d[3] = v.w;
+    }
+    __syncthreads();
+#pragma unroll 2
+    for (int c = 0; c < C1_CK; ++c) {
+#pragma unroll
+      for (int t = 0; t < 3; ++t) {
+        float wv[HP];
+#pragma unroll
+        for (int j4 = 0; j4 < (HW + 3) / 4; ++j4) {
+          const float4 v = *reinterpret_cast<const float4*>(ws + ((c0 + c) * 3 + t) * HP + 4 * j4);
+          wv[4 * j4] = v.x;
+          wv[4 * j4 + 1] = v.y;
+          wv[4 * j4 + 2] = v.z;
+          wv[4 * j4 + 3] = v.w;
+        }
+#pragma unroll
+        for (int i = 0; i < C1_RT; ++i) {
+          // Staged rows beyond nst are stale but only feed rows >= rows, which are dropped.
+          const float xv = xc[(lr0 + 32 * i + t * dil) * C1_XS + c];
+#pragma unroll
+          for (int j = 0; j < HW; ++j) acc[i][j] = fmaf(xv, wv[j], acc[i][j]);
+        }
+      }
+    }
+  }
+  float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+  for (int i = 0; i < C1_RT; ++i) {
+    const int r = r0 + lr0 + 32 * i;
+    if (r < rows && lr0 + 32 * i < C1_IR) {
+      float4* hr = reinterpret_cast<float4*>(h + ((long long)g * rows + r) * HP);
+#pragma unroll
+      for (int j4 = 0; j4 < HP / 4; ++j4) {
+        float v[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v[e] = 4 * j4 + e < HW ? acc[i][4 * j4 + e] : 0.f;
+        hr[j4] = make_float4(v[0], v[1], v[2], v[3]);
+      }
+#pragma unroll
+      for (int j = 0; j < HW; ++j) {
+        s1 += acc[i][j];
+        s2 += acc[i][j] * acc[i][j];
+      }
+    }
+  }
+  const double d1 = ub::warp_sum_d((double)s1), d2 = ub::warp_sum_d((double)s2);
+  __shared__ double red[2][C1_NW];
+  if ((tid & 31) == 0) {
+    red[0][tid >> 5] = d1;
+    red[1][tid >> 5] = d2;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    double a = 0, b = 0;
+    for (int i = 0; i < C1_NW; ++i) {
+      a += red[0][i];
+      b += red[1][i];
+    }
+    atomicAdd(stats + 2 * g, a);
+    atomicAdd(stats + 2 * g + 1, b);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Persistent apply for the thin levels: work items of `ir` rows of one group;
+// the item's x rows and h rows arrive by bulk copy into a ring of A4_NB
+// buffers (loads run A4_AHEAD items ahead), the residual update is computed in
+// place in shared memory and leaves by one bulk store per item. A buffer is
+// reloaded only after the store issued from it two items earlier has finished
+// reading it. Thread (rsub, cg) owns channels [cg*CPT, cg*CPT + CPT) with their
+// W2 value/gate rows in registers and walks rows rsub, rsub + RPP, ...
+constexpr int A4_NB = 4;
+constexpr int A4_AHEAD = 2;
+
+__device__ __forceinline__ void bulk_store(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(sm_u32(src)),
+               "r"(bytes)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+template <int MAXH, int HW>
+__global__ void __launch_bounds__(NTH2) dconv_apply4_kernel(float* __restrict__ x, long long x_gs,
+                                                            const float* __restrict__ h, int groups, int rows, int H,
+                                                            int C, const float* __restrict__ st1,
+                                                            const float* __restrict__ g1w,
+                                                            const float* __restrict__ g1b,
+                                                            const float* __restrict__ w2,
+                                                            const float* __restrict__ b2,
+                                                            const float* __restrict__ st2,
+                                                            const float* __restrict__ g2w,
+                                                            const float* __restrict__ g2b,
+                                                            const float* __restrict__ scale, int ir) {
+  extern __shared__ __align__(128) float dsm[];
+  const int xt = ir * C, ht = ir * H;    // floats per buffer part (multiples of 4)
+  float* a_s = dsm + A4_NB * (xt + ht);  // [ir][MAXH]
+  uint64_t* full = reinterpret_cast<uint64_t*>(a_s + ir * MAXH);
+  const int CG = C / CPT;
+  const int RPP = blockDim.x / CG;
+  const int cg = threadIdx.x % CG, rsub = threadIdx.x / CG;
+  const bool live = rsub < RPP;
+  float w[2 * CPT][MAXH], bz[2 * CPT], gw[2 * CPT], gb[2 * CPT], sc[CPT];
+  load_w<MAXH>(w2, b2, H, cg, live, w, bz);
+#pragma unroll
+  for (int k = 0; k < 2 * CPT; ++k) {
+    gw[k] = live ? __ldg(g2w + 2 * cg * CPT + k) : 0.f;
+    gb[k] = live ? __ldg(g2b + 2 * cg * CPT + k) : 0.f;
+  }
+#pragma unroll
+  for (int e = 0; e < CPT; ++e) sc[e] = live ? __ldg(scale + cg * CPT + e) : 0.f;
+  const int nblk = (rows + ir - 1) / ir;
+  const long long items = (long long)groups * nblk;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < A4_NB; ++i)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(sm_u32(&full[i])) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  auto item_at = [&](long long it) {
+    const int g = (int)(it / nblk);
+    const int r0 = (int)(it - (long long)g * nblk) * ir;
+    return make_int3(g, r0, min(ir, rows - r0));
+  };
+  auto issue = [&](long long it, int buf) {
+    const int3 t = item_at(it);
+    const int g = t.x, r0 = t.y, nr = t.z;
+    float* xb = dsm + buf * (xt + ht);
+    uint64_t* bar = &full[buf];
+    const uint32_t xbytes = (uint32_t)(nr * C * 4), hbytes = (uint32_t)(nr * H * 4);
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sm_u32(bar)), "r"(xbytes + hbytes)
+                 : "memory");
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     sm_u32(xb)),
+                 "l"(x + (long long)g * x_gs + (long long)r0 * C), "r"(xbytes), "r"(sm_u32(bar))
+                 : "memory");
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     sm_u32(xb + xt)),
+                 "l"(h + ((long long)g * rows + r0) * H), "r"(hbytes), "r"(sm_u32(bar))
+                 : "memory");
+  };
+  if (threadIdx.x == 0)
+    for (int i = 0; i < A4_AHEAD && blockIdx.x + (long long)i * gridDim.x < items; ++i)
+      issue(blockIdx.x + (long long)i * gridDim.x, i);
+  bool ok = true;
+  int k = 0;
+  for (long long it = blockIdx.x; it < items; it += gridDim.x, ++k) {
+    const int b = k % A4_NB;
+    const int3 cur = item_at(it);
+    const int g = cur.x, r0 = cur.y, nrows = cur.z;
+    const long long ahead = it + (long long)A4_AHEAD * gridDim.x;
+    if (threadIdx.x == 0 && ahead < items) {
+      // Buffer (k + AHEAD) % NB last held item k + AHEAD - NB = k - 2, whose
+      // store is the older of the (at most) two committed since.
+      asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+      issue(ahead, (k + A4_AHEAD) % A4_NB);
+    }
+    ok = wait_phase(&full[b], (k / A4_NB) & 1);
+    if (__syncthreads_or(!ok)) break;
+    float* xs = dsm + b * (xt + ht);
+    stage_act<MAXH>(xs + xt, nrows, H, st1[2 * g], st1[2 * g + 1], g1w, g1b, a_s);
+    __syncthreads();
+    if (live) {
+      // GN2 of z = W2 a + b2 folded per item: (z - m2) rstd2 gamma + beta = (W2 a) ga + gc.
+      const float m2 = st2[2 * g], rs2 = st2[2 * g + 1];
+      float ga[2 * CPT], gc[2 * CPT];
+#pragma unroll
+      for (int q = 0; q < 2 * CPT; ++q) {
+        ga[q] = rs2 * gw[q];
+        gc[q] = fmaf(bz[q] - m2, ga[q], gb[q]);
+      }
+#pragma unroll 2
+      for (int r = rsub; r < nrows; r += RPP) {
+        const float* a = a_s + r * MAXH;
+        float* xr = xs + r * C + cg * CPT;
+        float o[CPT];
+#pragma unroll
+        for (int e = 0; e < CPT; ++e) {
+          const float v = fmaf(dot_a<MAXH, HW>(a, w[2 * e]), ga[2 * e], gc[2 * e]);
+          const float gt = fmaf(dot_a<MAXH, HW>(a, w[2 * e + 1]), ga[2 * e + 1], gc[2 * e + 1]);
+          o[e] = (sc[e] * v) * ub::sigmoid_approx(gt);
+        }
+        if (CPT == 2) {
+          float2 xv = *reinterpret_cast<float2*>(xr);
+          xv.x += o[0];
+          xv.y += o[CPT - 1];
+          *reinterpret_cast<float2*>(xr) = xv;
+        } else {
+#pragma unroll
+          for (int e = 0; e < CPT; ++e) xr[e] += o[e];
+        }
+      }
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncthreads();
+    if (threadIdx.x == 0)
+      bulk_store(x + (long long)g * x_gs + (long long)r0 * C, xs, (uint32_t)(nrows * C * 4));
+  }
+  if (threadIdx.x == 0) {
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    if (!ok) atomicExch(&g_dconv_error, 1);
+  }
+}
+
+template <typename K>
+unsigned persistent_grid_smem(K kernel, int threads, size_t smem, long long items) {
+  int dev = 0, sms = 148, per_sm = 1;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess || per_sm < 1)
+    per_sm = 1;
+  const long long cap = (long long)sms * per_sm;
+  return (unsigned)(items < cap ? items : cap);
+}
+
 // Grid of a persistent kernel: every CTA resident at once (items are dealt
 // round-robin, so a second wave would double the time of its CTAs' share).
 template <typename K>
@@ -401,20 +669,55 @@ int maxh_for(int H) { return H <= 8 ? 8 : H <= 16 ? 16 : H <= 32 ? 32 : H <= 64 
 
 }  // namespace
 
+// Hidden rows are padded: h rows, W1 rows, GN1 affine and W2 rows hold
+// hs = round_up(hid, 4) values, the ones past hid being zero.
+static inline int padded_hidden(int hid) { return (hid + 3) & ~3; }
+
+// Compute width of the fused kernels: the true width when even (their dot
+// products take float4/float2 steps), else the padded one (zeros).
+static inline int compute_width(int hid) { return hid % 2 == 0 ? hid : padded_hidden(hid); }
+
 extern "C" int unblend_dconv_conv1(const float* x, long long x_gs, int groups, int rows, int c, const float* w1,
                                    const float* b1, int hid, int dil, float* h, double* stats, void* stream) {
   UB_REQUIRE(x && w1 && b1 && h && stats && groups > 0 && rows > 0 && c > 0 && c % 4 == 0);
   UB_REQUIRE(hid > 0 && dil > 0 && dil <= 8 && groups < 65536 && x_gs >= (long long)rows * c);
-  const int mh = maxh_for(hid);
+  const int hs = padded_hidden(hid);
+  const int mh = maxh_for(hs);
   UB_REQUIRE(mh > 0);
-  const size_t smem = sizeof(float) * ((size_t)(ROWS + 2 * dil) * (c + 4) + (size_t)hid * 3 * c);
+  cudaStream_t st = ub::as_stream(stream);
+  if (hs <= 16 && c % C1_CK == 0 && x_gs % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(h) & 15) == 0) {
+    const size_t smem1 = sizeof(float) * ((size_t)3 * c * hs + (size_t)(C1_IR + 2 * dil) * C1_XS);
+    UB_REQUIRE(smem1 <= 200 * 1024);
+    dim3 grid1((rows + C1_IR - 1) / C1_IR, groups);
+    const int hw = compute_width(hid);
+#define UB_C1B(HP, HW)                                                                                          \
+  {                                                                                                             \
+    cudaFuncSetAttribute(dconv_conv1b_kernel<HP, HW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1); \
+    dconv_conv1b_kernel<HP, HW><<<grid1, C1_NT, smem1, st>>>(x, x_gs, rows, c, w1, b1, dil, h, stats);          \
+  }
+    switch (hw) {
+      case 2: UB_C1B(4, 2) break;
+      case 4: UB_C1B(4, 4) break;
+      case 6: UB_C1B(8, 6) break;
+      case 8: UB_C1B(8, 8) break;
+      case 10: UB_C1B(12, 10) break;
+      case 12: UB_C1B(12, 12) break;
+      case 14: UB_C1B(16, 14) break;
+      case 16: UB_C1B(16, 16) break;
+      default: return UNBLEND_ERR_INVALID;
+    }
+#undef UB_C1B
+    UB_CHECK_LAUNCH();
+    return 0;
+  }
+  const size_t smem = sizeof(float) * ((size_t)(ROWS + 2 * dil) * (c + 4) + (size_t)hs * 3 * c);
   UB_REQUIRE(smem <= 220 * 1024);
   dim3 grid((rows + ROWS - 1) / ROWS, groups);
-  cudaStream_t st = ub::as_stream(stream);
 #define UB_LAUNCH(MH)                                                                                         \
   {                                                                                                           \
     cudaFuncSetAttribute(dconv_conv1_kernel<MH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);    \
-    dconv_conv1_kernel<MH><<<grid, ROWS, smem, st>>>(x, x_gs, rows, c, w1, b1, hid, dil, h, stats);           \
+    dconv_conv1_kernel<MH><<<grid, ROWS, smem, st>>>(x, x_gs, rows, c, w1, b1, hs, dil, h, stats);            \
   }
   if (mh == 8) UB_LAUNCH(8) else if (mh == 16) UB_LAUNCH(16) else if (mh == 32) UB_LAUNCH(32) else UB_LAUNCH(64)
 #undef UB_LAUNCH
@@ -427,29 +730,39 @@ extern "C" int unblend_dconv_z_stats(const float* h, int groups, int rows, int h
                                      double* stats2, void* stream) {
   UB_REQUIRE(h && st1 && g1w && g1b && w2 && b2 && stats2 && groups > 0 && rows > 0 && c > 0 && hid > 0);
   UB_REQUIRE(groups < 65536);
-  const int mh = maxh_for(hid);
+  const int hs = padded_hidden(hid);
+  const int mh = maxh_for(hs);
   UB_REQUIRE(mh > 0);
-  const size_t smem = sizeof(float) * ((size_t)2 * c * hid + 2 * c);
-  UB_REQUIRE(smem <= 220 * 1024);
-  dim3 grid((rows + ROWS - 1) / ROWS, groups);
   cudaStream_t st = ub::as_stream(stream);
-  if (mh <= 16 && hid % 4 == 0 && c % CPT == 0 && c / CPT <= NTH2 && (reinterpret_cast<uintptr_t>(h) & 15) == 0) {
+  if (mh <= 16 && c % CPT == 0 && c / CPT <= NTH2 && (reinterpret_cast<uintptr_t>(h) & 15) == 0) {
     const long long items = (long long)groups * ((rows + IROWS - 1) / IROWS);
 #define UB_ZS3(MH, HW)                                                                                         \
   {                                                                                                            \
     const unsigned g2 = persistent_grid(dconv_z_stats3_kernel<MH, HW>, 0, items);                           \
-    dconv_z_stats3_kernel<MH, HW><<<g2, NTH2, 0, st>>>(h, groups, rows, hid, c, st1, g1w, g1b, w2, b2, stats2); \
+    dconv_z_stats3_kernel<MH, HW><<<g2, NTH2, 0, st>>>(h, groups, rows, hs, c, st1, g1w, g1b, w2, b2, stats2); \
   }
-    if (hid == 8) UB_ZS3(8, 8) else if (hid == 12) UB_ZS3(16, 12) else if (mh == 8) UB_ZS3(8, 4)
-    else UB_ZS3(16, 16)
+    switch (compute_width(hid)) {
+      case 2: UB_ZS3(8, 2) break;
+      case 4: UB_ZS3(8, 4) break;
+      case 6: UB_ZS3(8, 6) break;
+      case 8: UB_ZS3(8, 8) break;
+      case 10: UB_ZS3(16, 10) break;
+      case 12: UB_ZS3(16, 12) break;
+      case 14: UB_ZS3(16, 14) break;
+      case 16: UB_ZS3(16, 16) break;
+      default: return UNBLEND_ERR_INVALID;
+    }
 #undef UB_ZS3
     UB_CHECK_LAUNCH();
     return 0;
   }
+  const size_t smem = sizeof(float) * ((size_t)2 * c * hs + 2 * c);
+  UB_REQUIRE(smem <= 220 * 1024);
+  dim3 grid((rows + ROWS - 1) / ROWS, groups);
 #define UB_LAUNCH(MH)                                                                                           \
   {                                                                                                             \
     cudaFuncSetAttribute(dconv_z_stats_kernel<MH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);    \
-    dconv_z_stats_kernel<MH><<<grid, ROWS, smem, st>>>(h, rows, hid, c, st1, g1w, g1b, w2, b2, stats2);         \
+    dconv_z_stats_kernel<MH><<<grid, ROWS, smem, st>>>(h, rows, hs, c, st1, g1w, g1b, w2, b2, stats2);          \
   }
   if (mh == 8) UB_LAUNCH(8) else if (mh == 16) UB_LAUNCH(16) else if (mh == 32) UB_LAUNCH(32) else UB_LAUNCH(64)
 #undef UB_LAUNCH
@@ -464,16 +777,45 @@ extern "C" int unblend_dconv_apply(float* x, long long x_gs, const float* h, int
   UB_REQUIRE(x && h && st1 && g1w && g1b && w2 && b2 && st2 && g2w && g2b && scale);
   UB_REQUIRE(groups > 0 && rows > 0 && c > 0 && c % 4 == 0 && hid > 0 && groups < 65536);
   UB_REQUIRE(x_gs >= (long long)rows * c && x_gs % 4 == 0);
-  const int mh = maxh_for(hid);
+  const int hs = padded_hidden(hid);
+  const int mh = maxh_for(hs);
   UB_REQUIRE(mh > 0);
-  const size_t smem = sizeof(float) * ((size_t)2 * c * hid + 6 * (size_t)c + c);
+  cudaStream_t st = ub::as_stream(stream);
+  if (mh <= 16 && c % CPT == 0 && c / CPT <= NTH2 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(h) & 15) == 0) {
+    const int ir = c <= 48 ? 64 : 32;
+    const size_t smem4 = sizeof(float) * ((size_t)A4_NB * ir * (c + hs) + (size_t)ir * mh) + 8 * A4_NB;
+    UB_REQUIRE(smem4 <= 200 * 1024);
+    const long long items = (long long)groups * ((rows + ir - 1) / ir);
+#define UB_AP4(MH, HW)                                                                                          \
+  {                                                                                                             \
+    cudaFuncSetAttribute(dconv_apply4_kernel<MH, HW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem4); \
+    const unsigned g4 = persistent_grid_smem(dconv_apply4_kernel<MH, HW>, NTH2, smem4, items);                  \
+    dconv_apply4_kernel<MH, HW><<<g4, NTH2, smem4, st>>>(x, x_gs, h, groups, rows, hs, c, st1, g1w, g1b, w2, b2, \
+                                                        st2, g2w, g2b, scale, ir);                              \
+  }
+    switch (compute_width(hid)) {
+      case 2: UB_AP4(8, 2) break;
+      case 4: UB_AP4(8, 4) break;
+      case 6: UB_AP4(8, 6) break;
+      case 8: UB_AP4(8, 8) break;
+      case 10: UB_AP4(16, 10) break;
+      case 12: UB_AP4(16, 12) break;
+      case 14: UB_AP4(16, 14) break;
+      case 16: UB_AP4(16, 16) break;
+      default: return UNBLEND_ERR_INVALID;
+    }
+#undef UB_AP4
+    UB_CHECK_LAUNCH();
+    return 0;
+  }
+  const size_t smem = sizeof(float) * ((size_t)2 * c * hs + 6 * (size_t)c + c);
   UB_REQUIRE(smem <= 220 * 1024);
   dim3 grid((rows + ROWS - 1) / ROWS, groups);
-  cudaStream_t st = ub::as_stream(stream);
 #define UB_LAUNCH(MH)                                                                                         \
   {                                                                                                           \
     cudaFuncSetAttribute(dconv_apply_kernel<MH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);    \
-    dconv_apply_kernel<MH><<<grid, ROWS, smem, st>>>(x, x_gs, h, rows, hid, c, st1, g1w, g1b, w2, b2, st2,    \
+    dconv_apply_kernel<MH><<<grid, ROWS, smem, st>>>(x, x_gs, h, rows, hs, c, st1, g1w, g1b, w2, b2, st2,     \
                                                      g2w, g2b, scale);                                        \
   }
   if (mh == 8) UB_LAUNCH(8) else if (mh == 16) UB_LAUNCH(16) else if (mh == 32) UB_LAUNCH(32) else UB_LAUNCH(64)

@@ -410,7 +410,7 @@ class HTDemucsCuda(nn.Module):
             if fused:
                 h = Act.freq(B, H, W, hp, dev)
                 _lib.call("unblend_dconv_conv1", x.t.data_ptr(), x_gs, groups, W, C, pw("c1.w").data_ptr(),
-                          pw("c1.b").data_ptr(), hp, dil, h.t.data_ptr(), st1.data_ptr(),
+                          pw("c1.b").data_ptr(), hid, dil, h.t.data_ptr(), st1.data_ptr(),
                           work=6.0 * groups * W * C * hid)
             else:
                 self._conv(x, self.w(f"{q}.c1.w"), self.w(f"{q}.c1.b"), h, h_out=H, w_out=W, n_out=hid, kw=3,
@@ -422,10 +422,10 @@ class HTDemucsCuda(nn.Module):
                 st2 = torch.zeros(2 * groups, device=dev, dtype=torch.float64)
                 args = (pw("g1.w").data_ptr(), pw("g1.b").data_ptr(), pw("c2.w").data_ptr(),
                         self.w(f"{q}.c2.b").data_ptr())
-                _lib.call("unblend_dconv_z_stats", h.t.data_ptr(), groups, W, hp, C, s1.data_ptr(), *args,
+                _lib.call("unblend_dconv_z_stats", h.t.data_ptr(), groups, W, hid, C, s1.data_ptr(), *args,
                           st2.data_ptr(), work=4.0 * groups * W * C * hid)
                 s2 = self._stats(st2, groups, W * 2 * C)
-                _lib.call("unblend_dconv_apply", x.t.data_ptr(), x_gs, h.t.data_ptr(), groups, W, hp, C,
+                _lib.call("unblend_dconv_apply", x.t.data_ptr(), x_gs, h.t.data_ptr(), groups, W, hid, C,
                           s1.data_ptr(), *args, s2.data_ptr(), self.w(f"{q}.g2.w").data_ptr(),
                           self.w(f"{q}.g2.b").data_ptr(), self.w(f"{q}.scale").data_ptr(),
                           work=4.0 * groups * W * C * hid)
