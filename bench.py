@@ -59,6 +59,9 @@ def _args():
                          "shifts=1, 240 s track; bsroformer: BS-RoFormer dim 512 depth 12, 8 s segments, batch 16, "
                          "bf16, 300 s track")
     ap.add_argument("--shifts", type=int, default=None, help="random-shift rounds per track")
+    ap.add_argument("--stems", default=None,
+                    help="comma-separated HTDemucs stems to materialise (default: vocals for htdemucs_6s, "
+                         "all stems otherwise)")
     ap.add_argument("--tracks", type=int, default=1,
                     help="tracks per rank and step (e.g. 8 x 240 s bf16 batch 48 per rank for the whole-box sweep)")
     ap.add_argument("--precision", default=None, choices=["fp32", "bf16", "fp32-simt"])
@@ -259,6 +262,9 @@ def main() -> None:
         name, seed = ("htdemucs_6s", 2) if args.model == "htdemucs_6s" else ("htdemucs", 0)
         cfg = htdemucs_config(name)
         model = HTDemucsCuda(cfg, htdemucs_state_dict(cfg, seed), precision=args.precision).to(dev)
+        stems = args.stems or ("vocals" if args.model == "htdemucs_6s" else None)
+        if stems:
+            model.select_sources(stems.split(","))
         seg_len = model.segment_length
     n_stems = len(model.sources)
     seconds, batch, shifts = args.seconds, args.batch, args.shifts
@@ -367,6 +373,8 @@ def main() -> None:
         label = "HTDemucs 6-stem (seed 2)" if args.model == "htdemucs_6s" else "HTDemucs 4-stem"
         work = (f"{label}, {seconds:g} s stereo track, {n_seg} segments of 7.8 s, "
                 f"overlap 0.25, {batch} segments per launch, precision {args.precision}")
+        if len(model.sources) < len(model.config["sources"]):
+            work += f", stems materialised: {','.join(model.sources)}"
     if shifts:
         work += f", shifts={shifts}"
     if n_tracks > 1:

@@ -121,3 +121,28 @@ def test_compiled_core_replays_cuda_graphs():
     out = apply_model(ma, ga["mix"].cuda(), overlap=ga["overlap"], chunk_batch_size=ga["chunk_batch_size"])
     assert rel_err(out.cpu()[..., :: ga["decimate"]], ga["shifts0"]["out"]) < FP32_TOL
     assert _lib.error_flag() == 0
+
+
+@pytest.mark.parametrize("fname,stems", [("htdemucs_6s_full.pt", ["vocals"]), ("htdemucs_small.pt", ["bass", "drums"])])
+def test_selected_stems_match_reference_slices(fname, stems):
+    """select_sources: only the chosen stems are materialised (last ConvTranspose rows and iSTFT), each equal
+    to its slice of the reference output; the selection can be widened again and is validated."""
+    from unblend_b200.apply import ValidationError
+
+    g = golden(fname)
+    m = _model(g)
+    full_sources = list(m.sources)
+    ref = g["out"]
+    d = g.get("decimate", 1)
+    m.select_sources(stems)
+    assert m.sources == stems
+    out = m(g["mix"].cuda()).cpu()
+    assert out.shape[1] == len(stems)
+    idx = [full_sources.index(s) for s in stems]
+    assert rel_err(out[..., ::d], ref[:, idx]) < FP32_TOL
+    m.select_sources(None)
+    assert m.sources == full_sources
+    assert rel_err(m(g["mix"].cuda()).cpu()[..., ::d], ref) < FP32_TOL
+    with pytest.raises(ValidationError):
+        m.select_sources(["kazoo"])
+    assert _lib.error_flag() == 0

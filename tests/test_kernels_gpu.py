@@ -49,7 +49,10 @@ def _cl(shape):
     return torch.randn(*shape, device="cuda")
 
 
-@pytest.mark.parametrize("B,H,W,C,N,kh,sh,ph", [(2, 32, 13, 4, 12, 8, 4, 2), (1, 16, 70, 9, 130, 8, 4, 2)])
+# The first two cases (c_in <= 4, eight taps, n_out a multiple of 16) take the
+# register-gather first-layer kernel; the others the tiled one.
+@pytest.mark.parametrize("B,H,W,C,N,kh,sh,ph", [(2, 36, 13, 4, 48, 8, 4, 2), (1, 20, 7, 1, 16, 8, 4, 2),
+                                                (2, 32, 13, 4, 12, 8, 4, 2), (1, 16, 70, 9, 130, 8, 4, 2)])
 def test_conv_freq_encoder_gelu(B, H, W, C, N, kh, sh, ph):
     x, w, b = _cl((B, H, W, C)), _cl((N, kh, 1, C)) * 0.2, _cl((N,))
     Ho = (H + 2 * ph - kh) // sh + 1
@@ -72,6 +75,22 @@ def test_conv_time_strided_rows_with_capacity():
     ref = F.conv1d(xp, w[:, 0].permute(0, 2, 1), b, 4, 2).permute(0, 2, 1)
     assert rel_err(y[:, :Wo], ref) < TOL
     assert torch.isnan(y[:, Wo:]).all()  # rows past the output length are untouched
+
+
+@pytest.mark.parametrize("C,N", [(2, 48), (4, 64)])
+def test_conv_time_first_layer_thin_path(C, N):
+    """Stereo (or CaC) input, 8 taps stride 4: the register-gather kernel, rows past Wo untouched."""
+    B, L, cap = 3, 1001, 1004
+    xs = _cl((B, cap, C))
+    w, b = _cl((N, 1, 8, C)) * 0.3, _cl((N,))
+    Wo = -(-L // 4)
+    y = torch.full((B, Wo + 3, N), float("nan"), device="cuda")
+    _conv(xs, w, b, y, B=B, H=1, W=L, C=C, in_s=(cap * C, cap * C, C), Ho=1, Wo=Wo, N=N,
+          out_s=((Wo + 3) * N, (Wo + 3) * N, N), kw=8, sw=4, pw=2, act=ACT_GELU)
+    xp = F.pad(xs[:, :L].permute(0, 2, 1), (0, 4 - L % 4))
+    ref = F.gelu(F.conv1d(xp, w[:, 0].permute(0, 2, 1), b, 4, 2)).permute(0, 2, 1)
+    assert rel_err(y[:, :Wo], ref) < TOL
+    assert torch.isnan(y[:, Wo:]).all()
 
 
 def test_conv_dilated_with_group_stats():

@@ -188,6 +188,94 @@ __global__ void __launch_bounds__(NT) conv_simt_kernel(ConvArgs a) {
   }
 }
 
+// First-layer convolutions (c_in <= 4 input channels, up to 8 taps along one
+// axis, n_out a multiple of 16 up to 64, bias + optional GELU, nothing else):
+// K = taps * c_in <= 32 is too short for the tiled kernel above, whose tile
+// loads and index arithmetic then dominate. Here each thread gathers the K
+// inputs of TH_PPT output positions into registers once and sweeps the output
+// channels 16 at a time against the weights held transposed in shared memory
+// (one broadcast float4 read feeds 4 * TH_PPT FMAs).
+constexpr int TH_NT = 128;
+constexpr int TH_PPT = 2;
+
+template <int CIN, int TAPS>
+__global__ void __launch_bounds__(TH_NT) conv_thin_kernel(ConvArgs a) {
+  constexpr int K = CIN * TAPS;
+  const UnblendConvParams& p = a.p;
+  __shared__ __align__(16) float ws[K * 64];  // [k][n]
+  const int N = p.n_out;
+  for (int i = threadIdx.x; i < N * K; i += TH_NT) {
+    const int n = i / K, k = i - n * K;
+    ws[k * N + n] = __ldg(a.w + i);
+  }
+  const bool along_h = p.kw == 1;
+  float xin[TH_PPT][K];
+  long long rowoff[TH_PPT];
+  bool valid[TH_PPT];
+#pragma unroll
+  for (int q = 0; q < TH_PPT; ++q) {
+    const long long m = (long long)blockIdx.x * (TH_NT * TH_PPT) + q * TH_NT + threadIdx.x;
+    valid[q] = m < a.M;
+    int wo = 0, ho = 0, b = 0;
+    if (valid[q]) {
+      wo = (int)(m % p.w_out);
+      const long long t = m / p.w_out;
+      ho = (int)(t % p.h_out);
+      b = (int)(t / p.h_out);
+    }
+    rowoff[q] = (long long)b * p.out_sb + (long long)ho * p.out_sh + (long long)wo * p.out_sw;
+    const int h0 = ho * p.sh - p.ph, w0 = wo * p.sw - p.pw;
+#pragma unroll
+    for (int t = 0; t < TAPS; ++t) {
+      const int hi = along_h ? h0 + t : h0, wi = along_h ? w0 : w0 + t;
+      const bool inb = valid[q] && hi >= 0 && hi < p.h_in && wi >= 0 && wi < p.w_in;
+      const float* src = a.x + (long long)b * p.in_sb + (long long)hi * p.in_sh + (long long)wi * p.in_sw;
+#pragma unroll
+      for (int c = 0; c < CIN; ++c) xin[q][t * CIN + c] = inb ? __ldg(src + c) : 0.f;
+    }
+  }
+  __syncthreads();
+  for (int n0 = 0; n0 < N; n0 += 16) {
+    float acc[TH_PPT][16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float bj = a.bias ? __ldg(a.bias + n0 + j) : 0.f;
+#pragma unroll
+      for (int q = 0; q < TH_PPT; ++q) acc[q][j] = bj;
+    }
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+#pragma unroll
+      for (int j4 = 0; j4 < 4; ++j4) {
+        const float4 w4 = *reinterpret_cast<const float4*>(ws + k * N + n0 + 4 * j4);
+#pragma unroll
+        for (int q = 0; q < TH_PPT; ++q) {
+          acc[q][4 * j4] = fmaf(xin[q][k], w4.x, acc[q][4 * j4]);
+          acc[q][4 * j4 + 1] = fmaf(xin[q][k], w4.y, acc[q][4 * j4 + 1]);
+          acc[q][4 * j4 + 2] = fmaf(xin[q][k], w4.z, acc[q][4 * j4 + 2]);
+          acc[q][4 * j4 + 3] = fmaf(xin[q][k], w4.w, acc[q][4 * j4 + 3]);
+        }
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < TH_PPT; ++q) {
+      if (!valid[q]) continue;
+      float* dst = a.y + rowoff[q] + n0;
+#pragma unroll
+      for (int j4 = 0; j4 < 4; ++j4) {
+        float4 v = make_float4(acc[q][4 * j4], acc[q][4 * j4 + 1], acc[q][4 * j4 + 2], acc[q][4 * j4 + 3]);
+        if (p.act == UNBLEND_ACT_GELU) {
+          v.x = ub::gelu_erf(v.x);
+          v.y = ub::gelu_erf(v.y);
+          v.z = ub::gelu_erf(v.z);
+          v.w = ub::gelu_erf(v.w);
+        }
+        *reinterpret_cast<float4*>(dst + 4 * j4) = v;
+      }
+    }
+  }
+}
+
 }  // namespace
 
 extern "C" int unblend_conv2d_f32(const float* x, const float* w, const float* bias, float* y,
@@ -207,6 +295,21 @@ extern "C" int unblend_conv2d_f32(const float* x, const float* w, const float* b
   a.y = y;
   a.M = (long long)p->batch * p->h_out * p->w_out;
   a.K = p->kh * p->kw * p->c_in;
+  const int taps = p->kh * p->kw;
+  const bool thin = p->c_in <= 4 && (p->kh == 1 || p->kw == 1) && taps == 8 && p->dh == 1 && p->dw == 1 &&
+                    p->prologue == UNBLEND_PRO_NONE && (p->act == UNBLEND_ACT_NONE || p->act == UNBLEND_ACT_GELU) &&
+                    !p->res && !p->stats && p->n_out % 16 == 0 && p->n_out <= 64 && p->n_group >= p->n_out &&
+                    p->out_sb % 4 == 0 && p->out_sh % 4 == 0 && p->out_sw % 4 == 0 &&
+                    (reinterpret_cast<uintptr_t>(y) & 15) == 0 && (p->c_in == 1 || p->c_in == 2 || p->c_in == 4);
+  if (thin) {
+    const long long blocks = (a.M + TH_NT * TH_PPT - 1) / (TH_NT * TH_PPT);
+    UB_REQUIRE(blocks < (1LL << 31));
+    if (p->c_in == 4) conv_thin_kernel<4, 8><<<(unsigned)blocks, TH_NT, 0, ub::as_stream(stream)>>>(a);
+    else if (p->c_in == 2) conv_thin_kernel<2, 8><<<(unsigned)blocks, TH_NT, 0, ub::as_stream(stream)>>>(a);
+    else conv_thin_kernel<1, 8><<<(unsigned)blocks, TH_NT, 0, ub::as_stream(stream)>>>(a);
+    UB_CHECK_LAUNCH();
+    return 0;
+  }
   dim3 grid((unsigned)((a.M + BM - 1) / BM), (unsigned)((p->n_out + BN - 1) / BN));
   UB_REQUIRE(grid.y < 65536);
   conv_simt_kernel<<<grid, NT, 0, ub::as_stream(stream)>>>(a);

@@ -26,6 +26,7 @@ import torch
 from torch import nn
 
 from . import _lib
+from .apply import ValidationError
 from ._lib import ACT_GELU, ACT_GLU, ACT_NONE, PRO_ADD, PRO_GN_GELU, PRO_NONE, ConvParams
 from .synth import HTDEMUCS_CONFIGS
 
@@ -475,22 +476,22 @@ class HTDemucsCuda(nn.Module):
             self._conv(x, self.w(f"{pre}.rewrite.w"), self.w(f"{pre}.rewrite.b"), y, h_out=1, w_out=x.W,
                        n_out=2 * C, kw=3, pw=1, act=ACT_GLU, prologue=PRO_ADD, pro_x2=skip)
         self._dconv(y, pre)
-        cout = self.w(f"{pre}.convtr.b").shape[0] // 2
+        cout = self._wsel(f"{pre}.convtr.b").shape[0] // 2
         act = ACT_NONE if last else ACT_GELU
         dev = x.t.device
-        b = self.w(f"{pre}.convtr.b")
+        b = self._wsel(f"{pre}.convtr.b")
         if freq:
             out = Act.freq(x.B, 4 * x.H, x.W, cout, dev)
             row = out.sh  # stride of one output frequency row
             for tag, ph, base in (("lo", 1, 0), ("hi", 0, 2)):
-                self._conv(y, self.w(f"{pre}.convtr.{tag}"), b, out, h_out=x.H, w_out=x.W, n_out=2 * cout,
+                self._conv(y, self._wsel(f"{pre}.convtr.{tag}"), b, out, h_out=x.H, w_out=x.W, n_out=2 * cout,
                            kh=2, ph=ph, act=act, n_group=cout, out_sg=row, out_offset=base * row,
                            out_sh=4 * row)
         else:
             cap = 4 * x.W
             out = Act.time(x.B, length, cap, cout, dev)
             for tag, pw, base in (("lo", 1, 0), ("hi", 0, 2)):
-                self._conv(y, self.w(f"{pre}.convtr.{tag}"), b, out, h_out=1, w_out=x.W, n_out=2 * cout,
+                self._conv(y, self._wsel(f"{pre}.convtr.{tag}"), b, out, h_out=1, w_out=x.W, n_out=2 * cout,
                            kw=2, pw=pw, act=act, n_group=cout, out_sg=cout, out_offset=base * cout,
                            out_sw=4 * cout)
         return out
@@ -677,6 +678,54 @@ class HTDemucsCuda(nn.Module):
         if graphed is not None:
             graphed.release()
         self._fixed_batch_shape = False
+
+    def select_sources(self, names: list[str] | None) -> "HTDemucsCuda":
+        """Materialise only the named stems (all of them when ``names`` is None).
+
+        The stems of HTDemucs part ways only in the last decoder layers: the
+        final frequency ConvTranspose emits 4 channels per source (2 audio
+        channels x real/imaginary) and the final time ConvTranspose 2 per
+        source; everything before is shared. Selecting stems keeps only their
+        output rows of those two layers and runs the iSTFT for them alone, so
+        ``forward`` returns ``[B, len(names), C, T]`` equal to the matching
+        slices of the full output (``SeparatedSources.isolate_stem`` applied
+        inside the model). ``self.sources`` becomes ``names``, which is what
+        ``apply_model`` reads for the output width.
+        """
+        full = list(self.config["sources"])
+        if names is None:
+            names = full
+        names = list(names)
+        bad = [n for n in names if n not in full]
+        if bad or not names or len(set(names)) != len(names):
+            raise ValidationError(f"Stems {bad or names!r} are not a selection of this model's sources. "
+                                  f"Available stems: {', '.join(full)}")
+        graphed = "_graphed" in self.__dict__
+        if graphed:
+            self.disable_compiled_core()
+        idx = [full.index(n) for n in names]
+        sel = {}
+        if idx != list(range(len(full))):
+            last = self.depth - 1
+            for pre, per in ((f"decoder.{last}", 4), (f"tdecoder.{last}", 2)):
+                b = self.w(f"{pre}.convtr.b")
+                cout = b.shape[0] // 2
+                ch = torch.tensor([s * per + k for s in idx for k in range(per)], device=b.device)
+                rows = torch.cat([ch, ch + cout])  # rows are (phase, channel)
+                for tag in ("lo", "hi"):
+                    sel[f"{pre}.convtr.{tag}"] = self.w(f"{pre}.convtr.{tag}")[rows].contiguous()
+                sel[f"{pre}.convtr.b"] = b[rows].contiguous()
+        self.__dict__["_selected"] = sel
+        self._tc_cache.clear()
+        self.sources = names
+        if graphed:
+            self.enable_compiled_core()
+        return self
+
+    def _wsel(self, name: str) -> torch.Tensor:
+        """Weight ``name``, or its stem-selected rows when a selection is active."""
+        sel = self.__dict__.get("_selected")
+        return sel[name] if sel and name in sel else self.w(name)
 
     def _forward_full(self, mix: torch.Tensor) -> torch.Tensor:
         B, C, T = mix.shape
