@@ -286,9 +286,26 @@ int unblend_rms_norm(const float* x, long long rows, int dim, const float* gamma
 /* Per-band RMSNorm of BandSplit (unblend/roformer.py:673-705): band b is columns
  * [band_start[b], band_start[b+1]) of each fp32 row of x (leading dim ldx);
  * band_start is a device int array of bands+1 multiples of 4; gamma holds the
- * bands' weights back to back in column order. */
+ * bands' weights back to back in column order. Band b is written from column
+ * y_start[b] of y (device array of multiples of 4), or band_start[b] when
+ * y_start is NULL. */
 int unblend_band_rms_norm(const float* x, long long rows, long long ldx, const int* band_start, int bands,
-                          const float* gamma, void* y, long long ldy, int y_bf16, void* stream);
+                          const float* gamma, void* y, long long ldy, int y_bf16, const int* y_start,
+                          void* stream);
+
+/* Mel-Band RoFormer band gather (unblend/roformer.py:1541-1544, index_select):
+ * dst[r, 2j + k] = src[r, 2 idx[j] + k] for k in {0, 1}, j < n; idx is a device
+ * int array of pair indices into the channel-interleaved (bin, channel) axis.
+ * src/dst 8-byte aligned, even leading dims (floats). */
+int unblend_gather_pairs(const float* src, long long src_ld, long long rows, const int* idx, int n, float* dst,
+                         long long dst_ld, void* stream);
+
+/* Mel-Band RoFormer mask scatter-average (unblend/roformer.py:1561-1575,
+ * scatter_add_ then divide by the covering band count):
+ * dst[r, 2c + k] = sum_{q in [offsets[c], offsets[c+1])} src[r, 2 pos[q] + k] / count_c,
+ * summed in ascending q; offsets (n_dst + 1 ints) and pos are device arrays. */
+int unblend_scatter_mean_pairs(const float* src, long long src_ld, long long rows, const int* offsets,
+                               const int* pos, int n_dst, float* dst, long long dst_ld, void* stream);
 
 /* Elementwise y[i] = a[i] + alpha * b[i % b_period] (skip adds, embeddings). */
 int unblend_add(const float* a, const float* b, float* y, long long n, long long b_period,

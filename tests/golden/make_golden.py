@@ -27,6 +27,12 @@ bit for bit, and saves the reference's fp32 CPU outputs on synthetic audio:
 * ``bsroformer_apply.pt`` ``apply_model`` with the reduced BS-RoFormer set up by
   ``configure_inference`` for 0.5 s segments and a complement stem
   (sources ["vocals", "other"]), over a 4-segment track.
+* ``melband_small.pt``   reduced Mel-Band RoFormer (dim 32, depth 2, 12 mel
+  bands, seed 5), batch 2 on 0.5 s, full outputs of ``MelBandRoformer.forward``
+  (unblend/roformer.py:1513), plus the band gather indices.
+* ``melband_kim.pt``      the registry ``melband_roformer_kim`` configuration
+  (dim 384, depth 6, 60 bands, seed 6) set up by ``configure_inference`` with a
+  complement stem, on a 1 s clip: every 5th output sample plus per-stem sums.
 
 The fixtures hold only outputs and small inputs; weights are regenerated from
 the seed on the fly, and ``weights_digest`` pins that regeneration.
@@ -49,6 +55,8 @@ sys.path.insert(0, ROOT)
 from unblend_b200.synth import (  # noqa: E402
     bsroformer_config,
     bsroformer_state_dict,
+    melband_config,
+    melband_state_dict,
     htdemucs_config,
     htdemucs_state_dict,
     synth_track,
@@ -179,8 +187,48 @@ def main_roformer(unblend) -> None:
                     "out": out[..., ::5].clone(), **_summary(out)}, os.path.join(HERE, "bsroformer_full.pt"))
 
 
+MELBAND_SMALL = dict(dim=32, depth=2, num_bands=12, heads=2, dim_head=16, mask_estimator_depth=1)
+
+
+def build_melband(unblend, cfg: dict, seed: int):
+    """``manual_seed(seed); MelBandRoformer(**cfg)``, checked against ``melband_state_dict``."""
+    import unblend.roformer
+
+    torch.manual_seed(seed)
+    model = unblend.roformer.MelBandRoformer(**cfg).eval()
+    mine = melband_state_dict(cfg, seed)
+    ref = model.state_dict()
+    assert set(ref) == set(mine), "state_dict keys differ"
+    for k in ref:
+        assert torch.equal(ref[k], mine[k]), f"weight {k} differs"
+    return model, weights_digest(mine)
+
+
+def main_melband(unblend) -> None:
+    """Mel-Band RoFormer fixtures (reduced model; the kim registry configuration)."""
+    with torch.inference_mode():
+        cfg = melband_config(**MELBAND_SMALL)
+        model, digest = build_melband(unblend, cfg, 5)
+        mix = torch.stack([synth_track(0.5, 30), synth_track(0.5, 31)])
+        out = model(mix)
+        torch.save({"config": cfg, "seed": 5, "weights_digest": digest, "mix": mix, "out": out.clone(),
+                    "freq_indices": model.freq_indices.clone(),
+                    "num_bands_per_freq": model.num_bands_per_freq.clone()},
+                   os.path.join(HERE, "melband_small.pt"))
+        cfg = melband_config()
+        model, digest = build_melband(unblend, cfg, 6)
+        model.configure_inference(sources=["vocals", "other"], samplerate=44100, segment_samples=352800)
+        mix = synth_track(1.0, 32)[None]
+        out = model(mix)
+        torch.save({"config": cfg, "seed": 6, "weights_digest": digest, "mix": mix, "decimate": 5,
+                    "sources": ["vocals", "other"], "out": out[..., ::5].clone(), **_summary(out)},
+                   os.path.join(HERE, "melband_kim.pt"))
+
+
 if __name__ == "__main__":
-    if len(sys.argv) > 2 and sys.argv[2] == "roformer":
+    if len(sys.argv) > 2 and sys.argv[2] == "melband":
+        main_melband(import_reference(sys.argv[1]))
+    elif len(sys.argv) > 2 and sys.argv[2] == "roformer":
         main_roformer(import_reference(sys.argv[1]))
     else:
         main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")

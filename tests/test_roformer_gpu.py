@@ -113,9 +113,17 @@ def test_band_rms_norm(bf16):
     st = torch.tensor(starts, dtype=torch.int32, device="cuda")
     y = torch.zeros(rows, ld, device="cuda", dtype=torch.bfloat16 if bf16 else torch.float32)
     _lib.call("unblend_band_rms_norm", x.data_ptr(), rows, feats, st.data_ptr(), len(widths), gamma.data_ptr(),
-              y.data_ptr(), ld, bf16)
+              y.data_ptr(), ld, bf16, None)
     ref = torch.cat([F.rms_norm(x[:, a:b], (b - a,), gamma[a:b], eps=1e-12) for a, b in zip(starts, starts[1:])], 1)
     assert rel_err(y[:, :feats].float(), ref) < (2.5e-2 if bf16 else 2e-6)
+    # Output bands moved to other columns (gaps untouched).
+    ystart = [0, 16, 32, 56, 112]
+    yo = torch.zeros(rows, 640, device="cuda", dtype=y.dtype)
+    _lib.call("unblend_band_rms_norm", x.data_ptr(), rows, feats, st.data_ptr(), len(widths), gamma.data_ptr(),
+              yo.data_ptr(), 640, bf16, torch.tensor(ystart, dtype=torch.int32, device="cuda").data_ptr())
+    for b, (a, e) in enumerate(zip(starts, starts[1:])):
+        assert rel_err(yo[:, ystart[b]:ystart[b] + e - a].float(), ref[:, a:e]) < (2.5e-2 if bf16 else 2e-6)
+    assert not yo[:, 48:56].float().abs().any()  # gap after band 2 (16 columns from 32)
 
 
 # ---------------------------------------------------------------- grouped GEMM

@@ -67,7 +67,7 @@ def test_inference_contract_and_validation(small):
     with pytest.raises(ValidationError):
         m.configure_inference(sources=["a"], samplerate=True, segment_samples=100)
     with pytest.raises(ValidationError):
-        build_roformer("mel_band_roformer", cfg, sources=["a"], samplerate=44100, segment_samples=100, state=sd)
+        build_roformer("scnet", cfg, sources=["a"], samplerate=44100, segment_samples=100, state=sd)
     with pytest.raises(RuntimeError, match="CUDA devices only"):
         m(torch.zeros(1, 2, 4096))
     with pytest.raises(ValidationError):

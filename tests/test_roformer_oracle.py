@@ -51,3 +51,23 @@ def test_roformer_oracle_apply_with_complement():
     assert rel_err(out[..., :: g["decimate"]], g["out"]) < TOL
     # complement: the two stems sum back to the mixture
     assert torch.allclose(out.sum(dim=1), g["mix"], atol=1e-5)
+
+
+def test_melband_oracle_matches_reference_fixture():
+    """The Mel-Band restatement (band layout, gather, per-transformer norms, scatter-average) equals the
+    reference's own outputs on the reduced model and the kim registry configuration."""
+    from oracle.roformer_oracle import melband_forward, mel_supports
+    from unblend_b200.synth import mel_band_layout, melband_state_dict
+
+    g = golden("melband_small.pt")
+    cfg = g["config"]
+    idx, _, per_bin = mel_band_layout(44100, cfg["stft_n_fft"], cfg["num_bands"], True)
+    assert torch.equal(idx, g["freq_indices"]) and torch.equal(per_bin, g["num_bands_per_freq"])
+    sup = mel_supports(44100, cfg["stft_n_fft"], cfg["num_bands"])
+    assert torch.equal(sup.sum(dim=0), g["num_bands_per_freq"])
+    out = melband_forward(melband_state_dict(cfg, g["seed"]), g["mix"], cfg)
+    assert rel_err(out, g["out"]) < 1e-5
+    k = golden("melband_kim.pt")
+    out = melband_forward(melband_state_dict(k["config"], k["seed"]), k["mix"], k["config"], complement=True,
+                          match_length=True)
+    assert rel_err(out[..., :: k["decimate"]], k["out"]) < 1e-5

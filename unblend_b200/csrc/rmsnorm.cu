@@ -163,7 +163,8 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const float* __restrict__
 __global__ void __launch_bounds__(256) band_rms_norm_kernel(const float* __restrict__ x, long long rows, long long ldx,
                                                             const int* __restrict__ start, int bands,
                                                             const float* __restrict__ gamma, void* __restrict__ y,
-                                                            long long ldy, int y_bf16) {
+                                                            long long ldy, int y_bf16,
+                                                            const int* __restrict__ y_start) {
   const int lane = threadIdx.x & 31;
   const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
   const long long total = rows * bands;
@@ -171,6 +172,7 @@ __global__ void __launch_bounds__(256) band_rms_norm_kernel(const float* __restr
     const long long r = wi / bands;
     const int b = (int)(wi - r * bands);
     const int c0 = __ldg(start + b), c1 = __ldg(start + b + 1);
+    const int o0 = y_start ? __ldg(y_start + b) : c0;
     const int n4 = (c1 - c0) >> 2;
     const float4* xr = reinterpret_cast<const float4*>(x + r * ldx + c0);
     float ss = 0.f;
@@ -183,7 +185,7 @@ __global__ void __launch_bounds__(256) band_rms_norm_kernel(const float* __restr
     for (int i = lane; i < n4; i += 32) {
       const float4 v = __ldg(xr + i);
       const float4 g = __ldg(reinterpret_cast<const float4*>(gamma + c0) + i);
-      store4(y, r * ldy + c0 + 4 * i, make_float4(v.x * inv * g.x, v.y * inv * g.y, v.z * inv * g.z, v.w * inv * g.w),
+      store4(y, r * ldy + o0 + 4 * i, make_float4(v.x * inv * g.x, v.y * inv * g.y, v.z * inv * g.z, v.w * inv * g.w),
              y_bf16);
     }
   }
@@ -212,7 +214,8 @@ extern "C" int unblend_rms_norm(const float* x, long long rows, int dim, const f
 }
 
 extern "C" int unblend_band_rms_norm(const float* x, long long rows, long long ldx, const int* band_start, int bands,
-                                     const float* gamma, void* y, long long ldy, int y_bf16, void* stream) {
+                                     const float* gamma, void* y, long long ldy, int y_bf16, const int* y_start,
+                                     void* stream) {
   UB_REQUIRE(x && band_start && gamma && y && rows > 0 && bands > 0 && ldx % 4 == 0 && ldy % 4 == 0);
   UB_REQUIRE((reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(gamma) & 15) == 0);
   UB_REQUIRE((reinterpret_cast<uintptr_t>(y) & (y_bf16 ? 7 : 15)) == 0);
@@ -220,7 +223,7 @@ extern "C" int unblend_band_rms_norm(const float* x, long long rows, long long l
   const long long blocks_needed = (warps + 7) / 8;
   const unsigned grid = (unsigned)(blocks_needed < 148LL * 16 ? blocks_needed : 148LL * 16);
   band_rms_norm_kernel<<<grid, 256, 0, ub::as_stream(stream)>>>(x, rows, ldx, band_start, bands, gamma, y, ldy,
-                                                               y_bf16 ? 1 : 0);
+                                                               y_bf16 ? 1 : 0, y_start);
   UB_CHECK_LAUNCH();
   return 0;
 }

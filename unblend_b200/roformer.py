@@ -31,7 +31,7 @@ from torch import nn
 from . import _lib
 from ._lib import ACT_GELU, ACT_GLU, ACT_NONE, ACT_TANH, AttnParams, GemmGroup, GemmParams
 from .apply import ValidationError
-from .synth import DEFAULT_FREQS_PER_BANDS
+from .synth import DEFAULT_FREQS_PER_BANDS, MELBAND_DEFAULTS, mel_band_layout
 
 PRECISIONS = ("fp32", "bf16")
 
@@ -87,11 +87,28 @@ class BSRoformerCuda(nn.Module):
     :param precision: ``"bf16"`` or ``"fp32"`` (see the module docstring).
     """
 
+    _defaults = _DEFAULTS
+    #: BS-RoFormer applies one shared ``final_norm``; Mel-Band normalises each transformer's output.
+    _norm_each_transformer = False
+
+    def _band_bins(self, cfg: dict) -> tuple[int, ...]:
+        """Bins per band: the configured contiguous split (unblend/roformer.py:1286-1293)."""
+        fpb = tuple(cfg["freqs_per_bands"])
+        if len(fpb) < 2 or sum(fpb) != self.n_fft // 2 + 1:
+            raise ValidationError(f"freqs_per_bands must sum to {self.n_fft // 2 + 1} for n_fft={self.n_fft}; "
+                                  f"got sum {sum(fpb)} over {len(fpb)} bands.")
+        return fpb
+
+    @staticmethod
+    def _mask_hidden_layers(depth: int) -> int:
+        """Hidden layers of a mask MLP: BS-RoFormer's ``depth`` counts Linears (unblend/roformer.py:1302)."""
+        return depth - 1
+
     def __init__(self, config: dict, state_dict: dict, precision: str = "bf16") -> None:
         super().__init__()
         if precision not in PRECISIONS:
             raise ValueError(f"precision must be one of {PRECISIONS}")
-        cfg = dict(_DEFAULTS)
+        cfg = dict(self._defaults)
         cfg.update(config)
         if cfg["linear_transformer_depth"] != 0:
             raise ValidationError("linear_transformer_depth != 0 is not supported (no shipped checkpoint uses "
@@ -110,16 +127,25 @@ class BSRoformerCuda(nn.Module):
         self.hop = cfg["stft_hop_length"]
         if cfg["stft_win_length"] != self.n_fft or cfg["stft_normalized"] or self.n_fft not in (2048, 4096):
             raise ValueError("the CUDA STFT supports n_fft 2048/4096, win_length == n_fft, not normalised")
-        self.freqs_per_bands = tuple(cfg["freqs_per_bands"])
-        if sum(self.freqs_per_bands) != self.n_fft // 2 + 1:
-            raise ValidationError("freqs_per_bands must cover the STFT bins exactly")
+        self.freqs_per_bands = self._band_bins(cfg)
         self.widths = [2 * f * self.audio_channels for f in self.freqs_per_bands]
         self.starts = [sum(self.widths[:b]) for b in range(len(self.widths) + 1)]
         self.bands = len(self.widths)
         self.features = self.starts[-1]
+        # Band columns of the band-split GEMM operand: each band starts on a
+        # 16-byte boundary of its element type (the TMA row offset), so bands
+        # whose width is not a multiple of 8 bf16 values get a zero gap.
+        align = 8 if precision == "bf16" else 4
+        self.kstarts = [0]
+        for w in self.widths:
+            self.kstarts.append(-(-(self.kstarts[-1] + w) // align) * align)
+        self.kfeatures = self.kstarts[-1]
         # Interface defaults until configure_inference (unblend/roformer.py:1003-1006).
         self.sources = [f"stem_{i}" for i in range(self.num_stems)]
         self.output_complement = False
+        # Mel-Band: iSTFT to the exact input length (else to hop * (frames - 1));
+        # configure_inference turns it on (unblend/roformer.py:1064, 1524).
+        self.match_input_audio_length = bool(cfg.get("match_input_audio_length", False))
         self._fixed_batch_shape = False
         self._pack(state_dict)
         self._device = torch.device("cpu")
@@ -195,7 +221,12 @@ class BSRoformerCuda(nn.Module):
                     self._lin[f"{p}.ff1"] = _Linear(w1, sd[f"{p}.1.net.1.bias"], [(0, 0, w1.shape[0], dim, 0)], bf16)
                     self._lin[f"{p}.ff2"] = _Linear(w2, sd[f"{p}.1.net.4.bias"], [(0, 0, dim, w2.shape[1], 0)],
                                                     bf16)
-        self._vec["final_norm.gamma"] = sd["final_norm.gamma"]
+        if self._norm_each_transformer:
+            for i in range(cfg["depth"]):
+                for axis in (0, 1):
+                    self._vec[f"layers.{i}.{axis}.norm.gamma"] = sd[f"layers.{i}.{axis}.norm.gamma"]
+        else:
+            self._vec["final_norm.gamma"] = sd["final_norm.gamma"]
         # BandSplit: band b's Linear(w_b -> dim) as rows [b*dim, (b+1)*dim) of one
         # zero-padded weight matrix; its RMSNorm gains back to back.
         kpad = -(-max(self.widths) // 64) * 64
@@ -205,20 +236,21 @@ class BSRoformerCuda(nn.Module):
         for b, w in enumerate(self.widths):
             wbs[b * dim:(b + 1) * dim, :w] = sd[f"band_split.to_features.{b}.1.weight"]
             bbs[b * dim:(b + 1) * dim] = sd[f"band_split.to_features.{b}.1.bias"]
-            groups.append((self.starts[b], b * dim, dim, w, b * dim))
+            groups.append((self.kstarts[b], b * dim, dim, w, b * dim))
         self._vec["band.gamma"] = torch.cat([sd[f"band_split.to_features.{b}.0.gamma"] for b in range(self.bands)])
         self._vec["band.starts"] = torch.tensor(self.starts, dtype=torch.int32)
+        self._vec["band.kstarts"] = torch.tensor(self.kstarts, dtype=torch.int32)
         self._lin["band_split"] = _Linear(wbs, bbs, groups, bf16)
         # MaskEstimator per stem: hidden layers (tanh) as grouped GEMMs with
         # one group per band, then the GLU output layer whose band b writes
         # feature columns [start_b, start_b + w_b) of the mask.
-        depth = cfg["mask_estimator_depth"]
+        n_hidden = self._mask_hidden_layers(cfg["mask_estimator_depth"])
         hidden = dim * cfg["mlp_expansion_factor"]
         self.mask_layers: list[list[str]] = []
         for s in range(self.num_stems):
             names = []
             a_in = dim
-            for k in range(depth - 1):
+            for k in range(n_hidden):
                 ws = torch.cat([sd[f"mask_estimators.{s}.to_freqs.{b}.0.{2 * k}.weight"] for b in range(self.bands)])
                 bs = torch.cat([sd[f"mask_estimators.{s}.to_freqs.{b}.0.{2 * k}.bias"] for b in range(self.bands)])
                 groups = [(b * a_in, b * hidden, hidden, a_in, b * hidden) for b in range(self.bands)]
@@ -226,7 +258,7 @@ class BSRoformerCuda(nn.Module):
                 self._lin[name] = _Linear(ws, bs, groups, bf16)
                 names.append(name)
                 a_in = hidden
-            k = depth - 1
+            k = n_hidden
             ws, bs, groups, row = [], [], [], 0
             for b, w in enumerate(self.widths):
                 ws.append(_interleave_glu(sd[f"mask_estimators.{s}.to_freqs.{b}.0.{2 * k}.weight"]))
@@ -408,14 +440,17 @@ class BSRoformerCuda(nn.Module):
                   self.n_fft, self.hop)
         frames = B * T
         # BandSplit: per-band RMSNorm, then the grouped per-band Linear.
-        ldf = self.features if self.precision == "fp32" else -(-self.features // 8) * 8
-        feats = torch.empty(frames, ldf, device=dev, dtype=self._act_dtype())
+        ldf = self.kfeatures if self.precision == "fp32" else -(-self.kfeatures // 8) * 8
+        gaps = self.kstarts != self.starts
+        # The GEMM reads past each band into its neighbour (zero weights there), so gaps must hold zeros.
+        feats = (torch.zeros if gaps else torch.empty)(frames, ldf, device=dev, dtype=self._act_dtype())
         starts = self._vec["band.starts"]
-        _lib.call("unblend_band_rms_norm", stft.data_ptr(), frames, self.features, starts.data_ptr(), nb,
+        band_in = self._band_input(stft, frames)
+        _lib.call("unblend_band_rms_norm", band_in.data_ptr(), frames, band_in.shape[-1], starts.data_ptr(), nb,
                   self._vec["band.gamma"].data_ptr(), feats.data_ptr(), ldf,
-                  1 if feats.dtype == torch.bfloat16 else 0)
+                  1 if feats.dtype == torch.bfloat16 else 0, self._vec["band.kstarts"].data_ptr() if gaps else None)
         x = torch.empty(frames * nb, dim, device=dev, dtype=torch.float32)
-        self._gemm(self._lin["band_split"], feats, ldf, frames, self.features, x, nb * dim)
+        self._gemm(self._lin["band_split"], feats, ldf, frames, self.kfeatures, x, nb * dim)
         # Axial transformers (unblend/roformer.py:1135-1159).
         rows = frames * nb
         store: list[torch.Tensor] = []
@@ -428,10 +463,22 @@ class BSRoformerCuda(nn.Module):
                     p = f"layers.{i}.{axis}.layers.{j}"
                     self._attention_layer(x, p, axis, B, T, tabs)
                     self._ff_layer(x, p, rows)
+                last = i == cfg["depth"] - 1 and axis == 1
+                if self._norm_each_transformer and not last:
+                    # Transformer output RMSNorm (unblend/roformer.py:658, 670), fp32 stream.
+                    xn = torch.empty_like(x)
+                    _lib.call("unblend_rms_norm", x.data_ptr(), rows, dim,
+                              self._vec[f"layers.{i}.{axis}.norm.gamma"].data_ptr(), xn.data_ptr(), dim, 0, None,
+                              None, 0, None)
+                    x = xn
             if cfg["skip_connection"]:
                 store.append(x.clone())
+        # The last normalisation (BS: final_norm; Mel-Band: the last transformer's
+        # output norm) writes the mask estimators' operand directly.
+        last_gamma = (f"layers.{cfg['depth'] - 1}.1.norm.gamma" if self._norm_each_transformer
+                      else "final_norm.gamma")
         xf = torch.empty(rows, dim, device=dev, dtype=self._act_dtype())
-        _lib.call("unblend_rms_norm", x.data_ptr(), rows, dim, self._vec["final_norm.gamma"].data_ptr(),
+        _lib.call("unblend_rms_norm", x.data_ptr(), rows, dim, self._vec[last_gamma].data_ptr(),
                   xf.data_ptr(), dim, 1 if xf.dtype == torch.bfloat16 else 0, None, None, 0, None)
         # Mask estimators: [stems, frames, features] complex masks (fp32).
         S = self.num_stems
@@ -445,21 +492,100 @@ class BSRoformerCuda(nn.Module):
                 self._gemm(lin, h, ld, frames, ld, nxt, width, act=ACT_TANH)
                 h, ld = nxt, width
             self._gemm(self._lin[names[-1]], h, ld, frames, ld, mask[s], self.features, act=ACT_GLU, block_n=64)
+        mask, mask_ld = self._bin_masks(mask, S, frames)
         # Complex masking, DC zeroing, iSTFT, optional complement stem.
         comp = 1 if self.output_complement else 0
-        out = torch.empty(B, S + comp, 2, L, device=dev, dtype=torch.float32)
+        out_len = self._output_length(L)
+        out = torch.empty(B, S + comp, 2, out_len, device=dev, dtype=torch.float32)
         fbuf = torch.empty(B * S * 2 * T * self.n_fft, device=dev, dtype=torch.float32)
-        _lib.call("unblend_istft_masked", stft.data_ptr(), mask.data_ptr(), frames * self.features,
-                  tabs["window"].data_ptr(), mix.data_ptr(), fbuf.data_ptr(), out.data_ptr(), B, S, comp, L,
+        _lib.call("unblend_istft_masked", stft.data_ptr(), mask.data_ptr(), frames * mask_ld,
+                  tabs["window"].data_ptr(), mix.data_ptr(), fbuf.data_ptr(), out.data_ptr(), B, S, comp, out_len,
                   self.n_fft, self.hop, 1 if cfg["zero_dc"] else 0)
         return out
+
+    # ------------------------------------------------------------------ band layout hooks
+    def _band_input(self, stft: torch.Tensor, frames: int) -> torch.Tensor:
+        """BandSplit input rows: the STFT feature rows themselves (contiguous bands)."""
+        return stft.view(frames, -1)
+
+    def _bin_masks(self, mask: torch.Tensor, S: int, frames: int) -> tuple[torch.Tensor, int]:
+        """Per-bin masks for the iSTFT: the band masks already are (contiguous bands)."""
+        return mask, self.features
+
+    def _output_length(self, L: int) -> int:
+        return L
+
+
+class MelBandRoformerCuda(BSRoformerCuda):
+    """Mel-Band RoFormer forward (unblend/roformer.py:1382-1603) on the BS-RoFormer kernels.
+
+    The bands are the supports of a Slaney mel filter bank and overlap, so the
+    band features are gathered from the STFT rows through an index list
+    (``unblend_gather_pairs``) and the per-band masks are summed back onto the
+    bins and divided by each bin's band count (``unblend_scatter_mean_pairs``)
+    before the shared masking iSTFT. Each axial transformer ends with its own
+    RMSNorm (no shared ``final_norm``), and the mask MLPs have
+    ``mask_estimator_depth`` hidden layers.
+    """
+
+    _defaults = MELBAND_DEFAULTS
+    _norm_each_transformer = True
+
+    def _band_bins(self, cfg: dict) -> tuple[int, ...]:
+        try:
+            idx, per_band, per_bin = mel_band_layout(cfg["sample_rate"], self.n_fft, cfg["num_bands"],
+                                                     bool(cfg["stereo"]))
+        except ValueError as e:
+            raise ValidationError("Invalid mel banding: every frequency bin must be covered by at least one "
+                                  "band.") from e
+        # Gather list and its inverse (destination pair -> gathered positions, ascending).
+        self._mel_idx = idx.to(torch.int32)
+        order = torch.argsort(idx, stable=True)
+        counts = torch.bincount(idx, minlength=(self.n_fft // 2 + 1) * self.audio_channels)
+        self._mel_pos = order.to(torch.int32)
+        self._mel_off = torch.cat([torch.zeros(1, dtype=torch.long), counts.cumsum(0)]).to(torch.int32)
+        self.bands_per_bin = per_bin
+        return tuple(int(v) for v in per_band.tolist())
+
+    @staticmethod
+    def _mask_hidden_layers(depth: int) -> int:
+        """Mel-Band's ``depth`` counts hidden layers (``depth + 1`` Linears, unblend/roformer.py:1494-1496)."""
+        return depth
+
+    def to(self, device, *args, **kwargs):
+        super().to(device, *args, **kwargs)
+        for name in ("_mel_idx", "_mel_pos", "_mel_off"):
+            setattr(self, name, getattr(self, name).to(self._device))
+        return self
+
+    def _band_input(self, stft: torch.Tensor, frames: int) -> torch.Tensor:
+        g = torch.empty(frames, self.features, device=stft.device, dtype=torch.float32)
+        fb4 = stft.shape[2] * 4
+        _lib.call("unblend_gather_pairs", stft.data_ptr(), fb4, frames, self._mel_idx.data_ptr(),
+                  self._mel_idx.numel(), g.data_ptr(), self.features)
+        return g
+
+    def _bin_masks(self, mask: torch.Tensor, S: int, frames: int) -> tuple[torch.Tensor, int]:
+        n_bins = (self.n_fft // 2 + 1) * self.audio_channels
+        dense = torch.empty(S, frames, 2 * n_bins, device=mask.device, dtype=torch.float32)
+        _lib.call("unblend_scatter_mean_pairs", mask.data_ptr(), self.features, S * frames,
+                  self._mel_off.data_ptr(), self._mel_pos.data_ptr(), n_bins, dense.data_ptr(), 2 * n_bins)
+        return dense, 2 * n_bins
+
+    def _output_length(self, L: int) -> int:
+        """torch.istft without ``length`` stops at hop * (frames - 1) unless the model matches the input."""
+        return L if self.match_input_audio_length else self.hop * (L // self.hop)
+
+
+_CUDA_ARCHITECTURES = {"bs_roformer": BSRoformerCuda, "mel_band_roformer": MelBandRoformerCuda}
 
 
 def build_roformer(architecture: str, config: dict, *, sources: list[str], samplerate: int, segment_samples: int,
                    state: dict, precision: str = "bf16") -> BSRoformerCuda:
     """Counterpart of ``unblend.roformer.build_roformer`` (unblend/roformer.py:1606-1643) for the CUDA path."""
-    if architecture != "bs_roformer":
-        raise ValidationError(f"architecture {architecture!r} is not built on the CUDA path (bs_roformer only)")
-    model = BSRoformerCuda(config, state, precision=precision)
+    if architecture not in _CUDA_ARCHITECTURES:
+        raise ValidationError(f"architecture {architecture!r} is not built on the CUDA path "
+                              f"({', '.join(_CUDA_ARCHITECTURES)})")
+    model = _CUDA_ARCHITECTURES[architecture](config, state, precision=precision)
     model.configure_inference(sources=sources, samplerate=samplerate, segment_samples=segment_samples)
     return model

@@ -327,6 +327,153 @@ def bsroformer_state_dict(cfg: dict, seed: int) -> "OrderedDict[str, torch.Tenso
     return state
 
 
+# Mel-Band RoFormer of the registry's ``melband_roformer_kim`` entry
+# (unblend/metadata.json): dim 384, depth 6, 60 mel bands, 8 heads of 64,
+# n_fft 2048, hop 441, mask estimator depth 2, one stem, 8 s segments.
+MELBAND_KIM_CONFIG = dict(
+    dim=384,
+    depth=6,
+    stereo=True,
+    num_stems=1,
+    time_transformer_depth=1,
+    freq_transformer_depth=1,
+    num_bands=60,
+    dim_head=64,
+    heads=8,
+    sample_rate=44100,
+    stft_n_fft=2048,
+    stft_hop_length=441,
+    stft_win_length=2048,
+    mask_estimator_depth=2,
+    mlp_expansion_factor=4,
+)
+
+# MelBandRoformer constructor defaults (unblend/roformer.py:1383-1408) for keys the config may omit.
+MELBAND_DEFAULTS = dict(
+    stereo=False, num_stems=1, time_transformer_depth=2, freq_transformer_depth=2, linear_transformer_depth=0,
+    num_bands=60, dim_head=64, heads=8, attn_dropout=0.1, ff_dropout=0.1, sample_rate=44100, stft_n_fft=2048,
+    stft_hop_length=512, stft_win_length=2048, stft_normalized=False, zero_dc=True, mask_estimator_depth=1,
+    mlp_expansion_factor=4, skip_connection=False, match_input_audio_length=False,
+)
+
+
+def melband_config(**overrides) -> dict:
+    """Copy of the ``melband_roformer_kim`` constructor config with ``overrides`` applied."""
+    cfg = dict(MELBAND_KIM_CONFIG)
+    cfg.update(overrides)
+    return cfg
+
+
+def _hz_to_slaney_mel(f: np.ndarray) -> np.ndarray:
+    """Slaney's auditory-toolbox mel scale: 200/3 Hz per mel below 1 kHz, log steps of ln(6.4)/27 above."""
+    f = np.asarray(f, dtype=np.float64)
+    lin = f / (200.0 / 3.0)
+    log_mel0 = 1000.0 / (200.0 / 3.0)
+    with np.errstate(divide="ignore"):
+        logp = log_mel0 + np.log(np.maximum(f, 1000.0) / 1000.0) / (math.log(6.4) / 27.0)
+    return np.where(f >= 1000.0, logp, lin)
+
+
+def _slaney_mel_to_hz(m: np.ndarray) -> np.ndarray:
+    m = np.asarray(m, dtype=np.float64)
+    log_mel0 = 1000.0 / (200.0 / 3.0)
+    return np.where(m >= log_mel0, 1000.0 * np.exp((math.log(6.4) / 27.0) * (m - log_mel0)), m * (200.0 / 3.0))
+
+
+def mel_band_support(sample_rate: int, n_fft: int, num_bands: int) -> np.ndarray:
+    """``[num_bands, n_fft//2 + 1]`` bool: which STFT bins each mel band covers.
+
+    The bands are the triangular filters of a Slaney-normalised mel filter
+    bank spanning 0 Hz to Nyquist (``num_bands + 2`` mel-spaced edges, float64);
+    a bin belongs to a band where the filter weight is positive. As in the
+    reference (unblend/roformer.py:1459-1463), the DC bin is forced into the
+    first band and the Nyquist bin into the last.
+    """
+    n_freqs = n_fft // 2 + 1
+    fft_freqs = np.linspace(0.0, sample_rate / 2, n_freqs)
+    edges = _slaney_mel_to_hz(np.linspace(0.0, float(_hz_to_slaney_mel(sample_rate / 2)), num_bands + 2))
+    widths = np.diff(edges)
+    ramps = edges[:, None] - fft_freqs[None, :]
+    rising = -ramps[:-2] / widths[:-1, None]
+    falling = ramps[2:] / widths[1:, None]
+    weights = np.maximum(0.0, np.minimum(rising, falling)) * (2.0 / (edges[2:] - edges[:-2]))[:, None]
+    support = weights > 0
+    support[0, 0] = True
+    support[-1, -1] = True
+    return support
+
+
+def mel_band_layout(sample_rate: int, n_fft: int, num_bands: int, stereo: bool = True):
+    """Gather indices and coverage counts of the Mel-Band RoFormer band split.
+
+    :return: ``(freq_indices, freqs_per_band, bands_per_freq)``: the bins of
+        band 0, band 1, ... concatenated, as indices into the channel-interleaved
+        frequency axis ``(f, channel)`` when stereo (unblend/roformer.py:1472-1477);
+        the bin count of each band; how many bands cover each bin.
+    """
+    support = mel_band_support(sample_rate, n_fft, num_bands)
+    if not support.any(axis=0).all():
+        raise ValueError("every frequency bin must be covered by at least one mel band")
+    idx = np.concatenate([np.nonzero(row)[0] for row in support]).astype(np.int64)
+    if stereo:
+        idx = (idx[:, None] * 2 + np.arange(2)[None, :]).reshape(-1)
+    return (torch.from_numpy(idx), torch.from_numpy(support.sum(axis=1)).long(),
+            torch.from_numpy(support.sum(axis=0)).long())
+
+
+def melband_state_dict(cfg: dict, seed: int) -> "OrderedDict[str, torch.Tensor]":
+    """Random-init Mel-Band RoFormer weights identical to ``manual_seed(seed); MelBandRoformer(**cfg)``.
+
+    Construction order of ``_RoformerBase._init_common`` and
+    ``MelBandRoformer.__init__`` (unblend/roformer.py:896-1066, 1383-1511): per
+    depth a time then a frequency ``Transformer`` (gated ``Attention`` and
+    ``FeedForward`` layers, then the output RMSNorm), the per-band ``BandSplit``
+    projections over the mel bands, and per stem the per-band ``MaskEstimator``
+    MLPs with ``mask_estimator_depth`` hidden layers.
+    """
+    full = dict(MELBAND_DEFAULTS)
+    full.update(cfg)
+    cfg = full
+    if cfg["skip_connection"] or cfg["linear_transformer_depth"]:
+        raise ValueError("skip connections and linear attention are not supported")
+    dim, heads, dh = cfg["dim"], cfg["heads"], cfg["dim_head"]
+    inner = heads * dh
+    channels = 2 if cfg["stereo"] else 1
+    _, freqs_per_band, _ = mel_band_layout(cfg["sample_rate"], cfg["stft_n_fft"], cfg["num_bands"], cfg["stereo"])
+    state: "OrderedDict[str, torch.Tensor]" = OrderedDict()
+    freqs = 1.0 / (10000.0 ** (torch.arange(0, dh, 2)[: dh // 2].float() / dh))
+    rng_state = torch.random.get_rng_state()
+    torch.manual_seed(seed)
+    try:
+        for i in range(cfg["depth"]):
+            for axis, tdepth in ((0, cfg["time_transformer_depth"]), (1, cfg["freq_transformer_depth"])):
+                for j in range(tdepth):
+                    p = f"layers.{i}.{axis}.layers.{j}"
+                    state[f"{p}.0.norm.gamma"] = torch.ones(dim)
+                    _take(f"{p}.0.to_qkv", nn.Linear(dim, 3 * inner, bias=False), state)
+                    _take(f"{p}.0.to_gates", nn.Linear(dim, heads), state)
+                    _take(f"{p}.0.to_out.0", nn.Linear(inner, dim, bias=False), state)
+                    state[f"{p}.0.rotary_embed.freqs"] = freqs.clone()
+                    state[f"{p}.1.net.0.gamma"] = torch.ones(dim)
+                    _take(f"{p}.1.net.1", nn.Linear(dim, 4 * dim), state)
+                    _take(f"{p}.1.net.4", nn.Linear(4 * dim, dim), state)
+                state[f"layers.{i}.{axis}.norm.gamma"] = torch.ones(dim)
+        dims_in = [2 * int(f) * channels for f in freqs_per_band.tolist()]
+        for b, d_in in enumerate(dims_in):
+            state[f"band_split.to_features.{b}.0.gamma"] = torch.ones(d_in)
+            _take(f"band_split.to_features.{b}.1", nn.Linear(d_in, dim), state)
+        hidden = dim * cfg["mlp_expansion_factor"]
+        for s in range(cfg["num_stems"]):
+            for b, d_in in enumerate(dims_in):
+                p = f"mask_estimators.{s}.to_freqs.{b}.0"
+                layer_dims = [dim] + [hidden] * cfg["mask_estimator_depth"] + [2 * d_in]
+                for k, (a_in, a_out) in enumerate(zip(layer_dims[:-1], layer_dims[1:])):
+                    _take(f"{p}.{2 * k}", nn.Linear(a_in, a_out), state)
+    finally:
+        torch.random.set_rng_state(rng_state)
+    return state
+
+
 def synth_track(seconds: float, seed: int, samplerate: int = 44100) -> torch.Tensor:
     """Synthetic stereo mixture ``[2, round(seconds * samplerate)]`` in fp32.
 
