@@ -54,7 +54,7 @@ def _args():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--model", default="htdemucs", choices=["htdemucs", "htdemucs_6s", "bsroformer"],
+    ap.add_argument("--model", default="htdemucs", choices=["htdemucs", "htdemucs_6s", "bsroformer", "melband"],
                     help="htdemucs: the headline workload; htdemucs_6s: 6-source HTDemucs (seed 2), bf16, "
                          "shifts=1, 240 s track; bsroformer: BS-RoFormer dim 512 depth 12, 8 s segments, batch 16, "
                          "bf16, 300 s track")
@@ -72,7 +72,7 @@ def _args():
                     help="N>1: all ranks separate the same track, its segments sharded across ranks with the "
                          "overlap-strip exchange (strong scaling); default: one track per rank (weak scaling)")
     args = ap.parse_args()
-    rof = args.model == "bsroformer"
+    rof = args.model in ("bsroformer", "melband")
     six = args.model == "htdemucs_6s"
     if args.precision is None:
         args.precision = "bf16" if rof or six else "fp32"
@@ -190,25 +190,32 @@ def cpu_baseline(seconds: float = CPU_SAMPLE_SECONDS) -> dict:
             "sample": f"oracle apply_model over a {seconds:.0f} s synthetic track (seed 1), fp32, overlap 0.25"}
 
 
-def cpu_baseline_roformer(seconds: float = 8.0) -> dict:
-    """The BS-RoFormer oracle (fp32 CPU restatement of the reference forward) over one 8 s segment."""
+def cpu_baseline_roformer(seconds: float = 8.0, mel: bool = False) -> dict:
+    """The BS-RoFormer (or Mel-Band) oracle, fp32 CPU restatements of the reference forward, over one 8 s segment."""
     import torch
 
     from oracle.apply_oracle import apply_unshifted
-    from oracle.roformer_oracle import bsroformer_forward
-    from unblend_b200.synth import bsroformer_config, bsroformer_state_dict, synth_track
+    from oracle.roformer_oracle import bsroformer_forward, melband_forward
+    from unblend_b200.synth import (bsroformer_config, bsroformer_state_dict, melband_config, melband_state_dict,
+                                    synth_track)
 
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
-    cfg = bsroformer_config()
-    sd = bsroformer_state_dict(cfg, 3)
+    if mel:
+        cfg = melband_config()
+        sd = melband_state_dict(cfg, 6)
+        fwd = lambda b: melband_forward(sd, b, cfg, match_length=True)  # noqa: E731
+    else:
+        cfg = bsroformer_config()
+        sd = bsroformer_state_dict(cfg, 3)
+        fwd = lambda b: bsroformer_forward(sd, b, cfg)  # noqa: E731
     mix = synth_track(seconds, 1)[None]
-    fwd = lambda b: bsroformer_forward(sd, b, cfg)  # noqa: E731
     t0 = time.perf_counter()
     apply_unshifted(fwd, mix, 1, ROFORMER_SEGMENT, 0.25, ROFORMER_BATCH)
     dt = time.perf_counter() - t0
+    name = "Mel-Band RoFormer" if mel else "BS-RoFormer"
     return {"value": seconds / dt, "unit": "audio-s/s", "cores": cores, "kind": "port",
-            "sample": f"BS-RoFormer oracle over a {seconds:.0f} s synthetic track (one 8 s segment), fp32"}
+            "sample": f"{name} oracle over a {seconds:.0f} s synthetic track (one 8 s segment), fp32"}
 
 
 def run_reference(args) -> None:
@@ -216,15 +223,16 @@ def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    rof = args.model == "bsroformer"
+    rof = args.model in ("bsroformer", "melband")
+    mel = args.model == "melband"
     vals = []
     for _ in range(max(1, args.steps)):
-        vals.append(cpu_baseline_roformer() if rof else cpu_baseline(CPU_SAMPLE_SECONDS / 2))
+        vals.append(cpu_baseline_roformer(mel=mel) if rof else cpu_baseline(CPU_SAMPLE_SECONDS / 2))
     v = statistics.median(x["value"] for x in vals)
     base = dict(vals[0])
     base["value"] = v
-    work = ("BS-RoFormer dim 512 depth 12 fp32 forward" if rof else "HTDemucs 4-stem fp32 apply_model") + \
-        " on host cores (bounded sample)"
+    work = (("Mel-Band RoFormer dim 384 depth 6 fp32 forward" if mel else "BS-RoFormer dim 512 depth 12 fp32 forward")
+            if rof else "HTDemucs 4-stem fp32 apply_model") + " on host cores (bounded sample)"
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "audio-s/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
             "dtype": "f32", "data": "synthetic", "vs_baseline": None,
@@ -249,8 +257,16 @@ def main() -> None:
 
     world, rank, local = _dist()
     dev = torch.device("cuda", torch.cuda.current_device())
-    rof = args.model == "bsroformer"
-    if rof:
+    rof = args.model in ("bsroformer", "melband")
+    if args.model == "melband":
+        from unblend_b200.roformer import MelBandRoformerCuda
+        from unblend_b200.synth import melband_config, melband_state_dict
+
+        rcfg = melband_config()
+        model = MelBandRoformerCuda(rcfg, melband_state_dict(rcfg, 6), precision=args.precision).to(dev)
+        model.configure_inference(sources=["vocals"], samplerate=44100, segment_samples=ROFORMER_SEGMENT)
+        seg_len = ROFORMER_SEGMENT
+    elif rof:
         from unblend_b200.roformer import BSRoformerCuda
         from unblend_b200.synth import bsroformer_config, bsroformer_state_dict
 
@@ -367,7 +383,9 @@ def main() -> None:
     n_seg = len(range(0, L, int(0.75 * seg_len)))
     dtype = {"fp32": "f32", "bf16": "bf16", "fp32-simt": "f32"}[args.precision]
     if rof:
-        work = (f"BS-RoFormer dim 512 depth 12 (seed 3), {seconds:g} s stereo track, {n_seg} segments of 8 s, "
+        name = ("Mel-Band RoFormer dim 384 depth 6, 60 mel bands (kim config, seed 6)" if args.model == "melband"
+                else "BS-RoFormer dim 512 depth 12 (seed 3)")
+        work = (f"{name}, {seconds:g} s stereo track, {n_seg} segments of 8 s, "
                 f"overlap 0.25, {batch} segments per launch, precision {args.precision}")
     else:
         label = "HTDemucs 6-stem (seed 2)" if args.model == "htdemucs_6s" else "HTDemucs 4-stem"
@@ -392,7 +410,7 @@ def main() -> None:
             "gpu_launches": launches, "roofline": roofline, "clocks": clk,
             "kernels": {k: {"ms": round(v["ms"], 3), "n": v["n"]} for k, v in sorted(agg.items(), key=lambda kv: -kv[1]["ms"])}}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline_roformer() if rof else cpu_baseline()
+        line["cpu_baseline"] = cpu_baseline_roformer(mel=args.model == "melband") if rof else cpu_baseline()
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
