@@ -396,7 +396,8 @@ int unblend_gather_chunks(const float* track, int channels, long long length, co
 /* Weighted overlap-add of model outputs y[i, rows, segment] (rows = S*C) into
  * acc[rows, L] and sum_w[L] with the triangular weight (transition power 1),
  * after the centre trim of short chunks. Positions [lo, hi) are visited; they
- * must cover every position the n chunks touch. */
+ * must cover every position the n chunks touch. offsets ascend (as the
+ * segment plan produces them). */
 int unblend_overlap_add(const float* y, int n, int rows, int segment, const long long* offsets,
                         long long length, long long lo, long long hi, float* acc, float* sum_w,
                         void* stream);

@@ -27,6 +27,10 @@ bit for bit, and saves the reference's fp32 CPU outputs on synthetic audio:
 * ``bsroformer_apply.pt`` ``apply_model`` with the reduced BS-RoFormer set up by
   ``configure_inference`` for 0.5 s segments and a complement stem
   (sources ["vocals", "other"]), over a 4-segment track.
+* ``ensemble_small.pt``  ``apply_model`` on a ``ModelEnsemble`` of two reduced
+  HTDemucs models (seeds 0 and 7): per-source weights with one shift round, and
+  one-hot rows with ``use_only_stem`` ("drums" takes the specialist shortcut,
+  "bass" does not), every 7th output sample plus full sums.
 * ``melband_small.pt``   reduced Mel-Band RoFormer (dim 32, depth 2, 12 mel
   bands, seed 5), batch 2 on 0.5 s, full outputs of ``MelBandRoformer.forward``
   (unblend/roformer.py:1513), plus the band gather indices.
@@ -187,6 +191,32 @@ def main_roformer(unblend) -> None:
                     "out": out[..., ::5].clone(), **_summary(out)}, os.path.join(HERE, "bsroformer_full.pt"))
 
 
+def main_ensemble(unblend) -> None:
+    """ModelEnsemble fixtures: two reduced HTDemucs members (seeds 0 and 7) under apply_model."""
+    torch.set_num_threads(os.cpu_count() or 1)
+    with torch.inference_mode():
+        cfg = htdemucs_config("htdemucs", **SMALL_OVERRIDES)
+        m0, d0 = build_reference(unblend, cfg, 0)
+        m7, d7 = build_reference(unblend, cfg, 7)
+        track = synth_track(1.3, 3)[None]
+        res = {"config": cfg, "seeds": [0, 7], "digests": [d0, d7], "mix": track, "overlap": 0.25,
+               "chunk_batch_size": 3, "decimate": 7}
+        weights = [[1.0, 0.5, 0.0, 2.0], [0.0, 0.5, 1.0, 1.0]]
+        ens = unblend.apply.ModelEnsemble([m0, m7], weights=weights)
+        random.seed(9)
+        offsets = [random.randint(0, int(0.5 * cfg["samplerate"]))]
+        random.seed(9)
+        y = unblend.apply.apply_model(ens, track, device="cpu", shifts=1, overlap=0.25, chunk_batch_size=3)
+        res["weighted"] = {"weights": weights, "offsets": offsets, "out": y[..., ::7].clone(), **_summary(y)}
+        onehot = [[1.0, 0.0, 0.0, 0.0], [0.0, 1.0, 1.0, 1.0]]
+        ens = unblend.apply.ModelEnsemble([m0, m7], weights=onehot)
+        for stem in ("drums", "bass"):
+            y = unblend.apply.apply_model(ens, track, device="cpu", shifts=0, overlap=0.25, chunk_batch_size=3,
+                                          use_only_stem=stem)
+            res[f"only_{stem}"] = {"weights": onehot, "out": y[..., ::7].clone(), **_summary(y)}
+        torch.save(res, os.path.join(HERE, "ensemble_small.pt"))
+
+
 MELBAND_SMALL = dict(dim=32, depth=2, num_bands=12, heads=2, dim_head=16, mask_estimator_depth=1)
 
 
@@ -226,7 +256,9 @@ def main_melband(unblend) -> None:
 
 
 if __name__ == "__main__":
-    if len(sys.argv) > 2 and sys.argv[2] == "melband":
+    if len(sys.argv) > 2 and sys.argv[2] == "ensemble":
+        main_ensemble(import_reference(sys.argv[1]))
+    elif len(sys.argv) > 2 and sys.argv[2] == "melband":
         main_melband(import_reference(sys.argv[1]))
     elif len(sys.argv) > 2 and sys.argv[2] == "roformer":
         main_roformer(import_reference(sys.argv[1]))

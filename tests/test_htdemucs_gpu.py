@@ -146,3 +146,23 @@ def test_selected_stems_match_reference_slices(fname, stems):
     with pytest.raises(ValidationError):
         m.select_sources(["kazoo"])
     assert _lib.error_flag() == 0
+
+
+@pytest.mark.parametrize("case", ["weighted", "only_drums", "only_bass"])
+def test_model_ensemble_matches_reference(case):
+    """ModelEnsemble under apply_model: per-source weights over shared shift offsets, and the one-hot
+    specialist shortcut of use_only_stem, against the reference's own ensemble outputs."""
+    from unblend_b200.apply import ModelEnsemble, apply_model
+
+    g = golden("ensemble_small.pt")
+    members = [HTDemucsCuda(g["config"], htdemucs_state_dict(g["config"], s), precision="fp32").cuda()
+               for s in g["seeds"]]
+    c = g[case]
+    ens = ModelEnsemble(members, weights=c["weights"])
+    kw = dict(overlap=g["overlap"], chunk_batch_size=g["chunk_batch_size"])
+    if case == "weighted":
+        out = apply_model(ens, g["mix"].cuda(), shifts=1, shift_offsets=c["offsets"], **kw)
+    else:
+        out = apply_model(ens, g["mix"].cuda(), use_only_stem=case[5:], **kw)
+    assert rel_err(out.cpu()[..., :: g["decimate"]], c["out"]) < FP32_TOL
+    assert _lib.error_flag() == 0

@@ -42,12 +42,22 @@ __global__ void overlap_add_kernel(const float* __restrict__ y, int n, int rows,
     const long long p = lo + i % span;
     const int r = (int)(i / span);
     if (p >= length) continue;
+    // Offsets ascend, so the chunks holding p start in (p - seg, p]: find the
+    // first with offset > p - seg by bisection (a position lies in at most
+    // ceil(seg / stride) chunks) instead of testing all n.
+    int k0 = 0, k1 = n;
+    while (k0 < k1) {
+      const int mid = (k0 + k1) >> 1;
+      if (__ldg(offsets + mid) > p - seg) k1 = mid;
+      else k0 = mid + 1;
+    }
     float a = 0.f, ws = 0.f;
-    for (int k = 0; k < n; ++k) {
-      const long long o = offsets[k];
+    for (int k = k0; k < n; ++k) {
+      const long long o = __ldg(offsets + k);
+      if (o > p) break;
       const long long len = length - o < seg ? length - o : seg;
       const long long j = p - o;
-      if (j < 0 || j >= len) continue;
+      if (j >= len) continue;
       const int trim = (int)((seg - len) / 2);
       const float w = split_weight((int)j, seg);
       a += y[((long long)k * rows + r) * seg + trim + j] * w;
@@ -78,6 +88,7 @@ extern "C" int unblend_gather_chunks(const float* track, int channels, long long
   return 0;
 }
 
+// offsets: n chunk starts in ascending order.
 extern "C" int unblend_overlap_add(const float* y, int n, int rows, int segment, const long long* offsets,
                                    long long length, long long lo, long long hi, float* acc, float* sum_w,
                                    void* stream) {

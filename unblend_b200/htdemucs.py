@@ -465,35 +465,49 @@ class HTDemucsCuda(nn.Module):
                    n_out=2 * cout, act=ACT_GLU)
         return out
 
-    def _dec(self, x: Act, skip: Act, pre: str, freq: bool, last: bool, length: int) -> Act:
-        """HDecLayer (unblend/blocks.py:706-747): +skip -> 3-tap rewrite -> GLU -> DConv -> convT -> crop -> GELU."""
+    def _dec(self, x: Act, skip: Act, pre: str, freq: bool, last: bool, length: int, skip_in_x: bool = False,
+             next_skip: Act | None = None) -> Act:
+        """HDecLayer (unblend/blocks.py:706-747): +skip -> 3-tap rewrite -> GLU -> DConv -> convT -> crop -> GELU.
+
+        ``skip_in_x``: the skip connection was already added to ``x`` by the previous
+        layer. ``next_skip``: the following decoder layer's skip, added here in the
+        ConvTranspose epilogue (``GELU(convT) + skip``, the same single fp32 addition
+        the next layer would make) instead of by a separate pass over the activation.
+        """
         C = x.C
         y = x.like()
+        pro = dict(prologue=PRO_NONE) if skip_in_x else dict(prologue=PRO_ADD, pro_x2=skip)
         if freq:
             self._conv(x, self.w(f"{pre}.rewrite.w"), self.w(f"{pre}.rewrite.b"), y, h_out=x.H, w_out=x.W,
-                       n_out=2 * C, kh=3, kw=3, ph=1, pw=1, act=ACT_GLU, prologue=PRO_ADD, pro_x2=skip)
+                       n_out=2 * C, kh=3, kw=3, ph=1, pw=1, act=ACT_GLU, **pro)
         else:
             self._conv(x, self.w(f"{pre}.rewrite.w"), self.w(f"{pre}.rewrite.b"), y, h_out=1, w_out=x.W,
-                       n_out=2 * C, kw=3, pw=1, act=ACT_GLU, prologue=PRO_ADD, pro_x2=skip)
+                       n_out=2 * C, kw=3, pw=1, act=ACT_GLU, **pro)
         self._dconv(y, pre)
         cout = self._wsel(f"{pre}.convtr.b").shape[0] // 2
         act = ACT_NONE if last else ACT_GELU
         dev = x.t.device
         b = self._wsel(f"{pre}.convtr.b")
+        if next_skip is not None:
+            want = (4 * x.H * x.W * cout, x.W * cout, cout) if freq else (4 * x.W * cout, 4 * x.W * cout, cout)
+            assert (next_skip.sb, next_skip.sh, next_skip.sw, next_skip.C) == want + (cout,), \
+                "skip layout differs from the decoder output"
         if freq:
             out = Act.freq(x.B, 4 * x.H, x.W, cout, dev)
             row = out.sh  # stride of one output frequency row
             for tag, ph, base in (("lo", 1, 0), ("hi", 0, 2)):
+                res = None if next_skip is None else next_skip.t[base * row:]
                 self._conv(y, self._wsel(f"{pre}.convtr.{tag}"), b, out, h_out=x.H, w_out=x.W, n_out=2 * cout,
                            kh=2, ph=ph, act=act, n_group=cout, out_sg=row, out_offset=base * row,
-                           out_sh=4 * row)
+                           out_sh=4 * row, res=res)
         else:
             cap = 4 * x.W
             out = Act.time(x.B, length, cap, cout, dev)
             for tag, pw, base in (("lo", 1, 0), ("hi", 0, 2)):
+                res = None if next_skip is None else next_skip.t[base * cout:]
                 self._conv(y, self._wsel(f"{pre}.convtr.{tag}"), b, out, h_out=1, w_out=x.W, n_out=2 * cout,
                            kw=2, pw=pw, act=act, n_group=cout, out_sg=cout, out_offset=base * cout,
-                           out_sw=4 * cout)
+                           out_sw=4 * cout, res=res)
         return out
 
     def _linear(self, x: torch.Tensor, B: int, L: int, K: int, w: torch.Tensor, b: torch.Tensor | None,
@@ -774,8 +788,13 @@ class HTDemucsCuda(nn.Module):
             self._trace_act("tr_xt", xt)
         for idx in range(self.depth):
             last = idx == self.depth - 1
-            x = self._dec(x, saved.pop(-1), f"decoder.{idx}", True, last, 0)
-            xt = self._dec(xt, saved_t.pop(-1), f"tdecoder.{idx}", False, last, levels[self.depth - 1 - idx])
+            skip, skip_t = saved.pop(-1), saved_t.pop(-1)
+            # Each ConvTranspose adds the next layer's skip in its epilogue (traced
+            # decoder outputs therefore include it).
+            nxt, nxt_t = (None, None) if last else (saved[-1], saved_t[-1])
+            x = self._dec(x, skip, f"decoder.{idx}", True, last, 0, skip_in_x=idx > 0, next_skip=nxt)
+            xt = self._dec(xt, skip_t, f"tdecoder.{idx}", False, last, levels[self.depth - 1 - idx],
+                           skip_in_x=idx > 0, next_skip=nxt_t)
             self._trace_act(f"dec{idx}", x)
             self._trace_act(f"tdec{idx}", xt)
         out = torch.empty(B, S, 2, T, device=dev, dtype=torch.float32)
