@@ -200,7 +200,17 @@ __global__ void __launch_bounds__(NT, 1)
         }
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(buf * BN);
+        // K steps with real channels in the current chunk: a chunk holds 32 channels
+        // of one tap, and the last chunk of a tap may be partly past c_in (zero fill,
+        // e.g. 16 of 32 for 48-channel layers); the MMAs of all-zero steps are skipped.
+        int tap = 0, cc = 0;
         for (int kc = 0; kc < nk; ++kc, ++it) {
+          const int valid = min(32, a.tap_clen[tap] - cc);
+          cc += 32;
+          if (cc >= a.tap_clen[tap]) {
+            cc = 0;
+            ++tap;
+          }
           const int s = it % L::STAGES;
           const int r = it / L::STAGES;
           if (!mbar_wait(&conv[s], r & 1)) {
@@ -215,6 +225,7 @@ __global__ void __launch_bounds__(NT, 1)
           if (MODE == 0) {
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
+              if (j > 0 && 8 * j >= valid) break;  // 8 channels per kind::tf32 step
               const uint64_t dah = smem_desc(sa + 32 * j, 128), dal = smem_desc(sac + 32 * j, 128);
               const uint64_t dbh = smem_desc(sb + 32 * j, 128), dbl = smem_desc(sb + L::B_BYTES + 32 * j, 128);
               umma_tf32(d, dah, dbh, idesc, (kc > 0 || j > 0) ? 1u : 0u);
@@ -224,6 +235,7 @@ __global__ void __launch_bounds__(NT, 1)
           } else {
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
+              if (j > 0 && 16 * j >= valid) break;  // 16 channels per kind::f16 step
               const uint64_t da = smem_desc(sac + 32 * j, 64), db = smem_desc(sb + 32 * j, 64);
               umma_bf16(d, da, db, idesc, (kc > 0 || j > 0) ? 1u : 0u);
             }
