@@ -307,6 +307,10 @@ int unblend_gather_pairs(const float* src, long long src_ld, long long rows, con
 int unblend_scatter_mean_pairs(const float* src, long long src_ld, long long rows, const int* offsets,
                                const int* pos, int n_dst, float* dst, long long dst_ld, void* stream);
 
+/* y[i] = bf16(x[i]) (round to nearest even); n a multiple of 4, x 16-byte and
+ * y 8-byte aligned. Feeds fp32 projections to the bf16 attention kernel. */
+int unblend_cast_bf16(const float* x, void* y, long long n, void* stream);
+
 /* Elementwise y[i] = a[i] + alpha * b[i % b_period] (skip adds, embeddings). */
 int unblend_add(const float* a, const float* b, float* y, long long n, long long b_period,
                 float alpha, void* stream);

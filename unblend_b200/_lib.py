@@ -124,6 +124,7 @@ _SIGNATURES = {
     "unblend_band_rms_norm": [c_void_p, c_ll, c_ll, c_void_p, c_int, c_void_p, c_void_p, c_ll, c_int, c_void_p,
                               c_void_p],
     "unblend_gather_pairs": [c_void_p, c_ll, c_ll, c_void_p, c_int, c_void_p, c_ll, c_void_p],
+    "unblend_cast_bf16": [c_void_p, c_void_p, c_ll, c_void_p],
     "unblend_scatter_mean_pairs": [c_void_p, c_ll, c_ll, c_void_p, c_void_p, c_int, c_void_p, c_ll, c_void_p],
     "unblend_stft_frames": [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p],
     "unblend_istft_masked": [c_void_p, c_void_p, c_ll, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,

@@ -7,6 +7,8 @@
 // x + LayerScale * GLU(GN(z)) (unblend/blocks.py:293-317).
 // Statistics accumulate in double so that fp32 parity holds for groups of
 // millions of elements.
+#include <cuda_bf16.h>
+
 #include "common.cuh"
 
 namespace {
@@ -166,6 +168,20 @@ __global__ void time_input_kernel(const float* __restrict__ mix, float* __restri
   }
 }
 
+// y[i] = bf16(x[i]) (round to nearest even), four elements per thread.
+__global__ void cast_bf16_kernel(const float4* __restrict__ x, uint2* __restrict__ y, long long n4) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4;
+       i += (long long)gridDim.x * blockDim.x) {
+    const float4 v = __ldg(x + i);
+    __nv_bfloat162 p0 = __floats2bfloat162_rn(v.x, v.y);
+    __nv_bfloat162 p1 = __floats2bfloat162_rn(v.z, v.w);
+    uint2 o;
+    o.x = *reinterpret_cast<uint32_t*>(&p0);
+    o.y = *reinterpret_cast<uint32_t*>(&p1);
+    y[i] = o;
+  }
+}
+
 }  // namespace
 
 extern "C" int unblend_zero_f64(double* p, long long n, void* stream) {
@@ -233,6 +249,15 @@ extern "C" int unblend_add(const float* a, const float* b, float* y, long long n
                            float alpha, void* stream) {
   UB_REQUIRE(a && b && y && n > 0 && b_period > 0);
   add_kernel<<<ub::grid_1d(n, 256), 256, 0, ub::as_stream(stream)>>>(a, b, y, n, b_period, alpha);
+  UB_CHECK_LAUNCH();
+  return 0;
+}
+
+extern "C" int unblend_cast_bf16(const float* x, void* y, long long n, void* stream) {
+  UB_REQUIRE(x && y && n > 0 && n % 4 == 0);
+  UB_REQUIRE((reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(y) & 7) == 0);
+  cast_bf16_kernel<<<ub::grid_1d(n / 4, 256), 256, 0, ub::as_stream(stream)>>>(
+      reinterpret_cast<const float4*>(x), reinterpret_cast<uint2*>(y), n / 4);
   UB_CHECK_LAUNCH();
   return 0;
 }

@@ -27,7 +27,7 @@ from torch import nn
 
 from . import _lib
 from .apply import ValidationError
-from ._lib import ACT_GELU, ACT_GLU, ACT_NONE, PRO_ADD, PRO_GN_GELU, PRO_NONE, ConvParams
+from ._lib import ACT_GELU, ACT_GLU, ACT_NONE, PRO_ADD, PRO_GN_GELU, PRO_NONE, AttnParams, ConvParams
 from .synth import HTDEMUCS_CONFIGS
 
 
@@ -524,11 +524,36 @@ class HTDemucsCuda(nn.Module):
                   self.w(f"{name}.bias").data_ptr(), _lib.ptr(pos), 1.0, pos_rows, rows, c)
         return y
 
-    def _attention(self, q: int, k: int, v: int, o: int, B: int, heads: int, L: int, Lk: int, hd: int, q_sb: int,
-                   q_sr: int, kv_sb: int, kv_sr: int, o_sb: int, o_sr: int) -> None:
-        """softmax(Q K^T / sqrt(hd)) V for all heads: tensor-core flash attention, or SIMT."""
+    def _attention(self, qbuf: torch.Tensor, q_off: int, kvbuf: torch.Tensor, k_off: int, v_off: int, o: int,
+                   B: int, heads: int, L: int, Lk: int, hd: int, q_sb: int, q_sr: int, kv_sb: int, kv_sr: int,
+                   o_sb: int, o_sr: int) -> None:
+        """softmax(Q K^T / sqrt(hd)) V for all heads: tensor-core flash attention, or SIMT.
+
+        Q sits at element ``q_off`` of ``qbuf``, K and V at ``k_off`` / ``v_off`` of
+        ``kvbuf`` (fp32 projections); strides are in elements. In bf16 precision with
+        64-dim heads the projections are rounded to bf16 once and the bf16 kernel runs
+        (kind::f16 MMAs, P in bf16); fp32 keeps the 3-pass TF32 kernel.
+        """
         work = 4.0 * B * L * Lk * hd * heads
         scale = 1.0 / math.sqrt(hd)
+        if (self.precision == "bf16" and hd == 64 and o % 16 == 0
+                and all(v % 8 == 0 for v in (q_off, k_off, v_off, q_sb, q_sr, kv_sb, kv_sr, o_sb, o_sr))):
+            qb = torch.empty(qbuf.numel(), device=qbuf.device, dtype=torch.bfloat16)
+            _lib.call("unblend_cast_bf16", qbuf.data_ptr(), qb.data_ptr(), qbuf.numel())
+            kvb = qb
+            if kvbuf is not qbuf:
+                kvb = torch.empty(kvbuf.numel(), device=kvbuf.device, dtype=torch.bfloat16)
+                _lib.call("unblend_cast_bf16", kvbuf.data_ptr(), kvb.data_ptr(), kvbuf.numel())
+            a = AttnParams()
+            a.outer, a.inner, a.heads, a.lq, a.lk, a.hd = B, 1, heads, L, Lk, hd
+            a.q_so, a.q_si, a.q_sr = q_sb, 8, q_sr
+            a.kv_so, a.kv_si, a.kv_sr = kv_sb, 8, kv_sr
+            a.out, a.o_so, a.o_si, a.o_sr, a.out_bf16 = o, o_sb, 0, o_sr, 0
+            a.scale = scale
+            _lib.call("unblend_attention_bf16", qb.data_ptr() + 2 * q_off, kvb.data_ptr() + 2 * k_off,
+                      kvb.data_ptr() + 2 * v_off, ctypes_byref(a), work=work)
+            return
+        q, k, v = qbuf.data_ptr() + 4 * q_off, kvbuf.data_ptr() + 4 * k_off, kvbuf.data_ptr() + 4 * v_off
         if self.precision != "fp32-simt" and hd % 4 == 0 and hd <= 64 and all(p % 16 == 0 for p in (q, k, v, o)):
             mode = 0 if self.precision == "fp32" else 1
             _lib.call("unblend_attention_tc", q, k, v, o, B, heads, L, Lk, hd, q_sb, q_sr, kv_sb, kv_sr, o_sb, o_sr,
@@ -550,8 +575,7 @@ class HTDemucsCuda(nn.Module):
             win, bin_ = self.w(f"{q}.{attn}.in_proj_weight"), self.w(f"{q}.{attn}.in_proj_bias")
             qkv = torch.empty(B * L * 3 * D, device=dev, dtype=torch.float32)
             self._linear(h, B, L, D, win, bin_, qkv, 3 * D)
-            base = qkv.data_ptr()
-            self._attention(base, base + 4 * D, base + 8 * D, att.data_ptr(), B, heads, L, L, hd, L * 3 * D,
+            self._attention(qkv, 0, qkv, D, 2 * D, att.data_ptr(), B, heads, L, L, hd, L * 3 * D,
                             3 * D, L * 3 * D, 3 * D, L * D, D)
         else:
             kvn = self._ln(kv_src, B * Lk, D, f"{q}.norm2")
@@ -559,8 +583,7 @@ class HTDemucsCuda(nn.Module):
             self._linear(h, B, L, D, self.w(f"{q}.in_q.w"), self.w(f"{q}.in_q.b"), qp, D)
             kv = torch.empty(B * Lk * 2 * D, device=dev, dtype=torch.float32)
             self._linear(kvn, B, Lk, D, self.w(f"{q}.in_kv.w"), self.w(f"{q}.in_kv.b"), kv, 2 * D)
-            base = kv.data_ptr()
-            self._attention(qp.data_ptr(), base, base + 4 * D, att.data_ptr(), B, heads, L, Lk, hd, L * D, D,
+            self._attention(qp, 0, kv, 0, D, att.data_ptr(), B, heads, L, Lk, hd, L * D, D,
                             Lk * 2 * D, 2 * D, L * D, D)
         x_new = torch.empty_like(x)
         self._linear(att, B, L, D, self.w(f"{q}.{attn}.out_proj.weight"), self.w(f"{q}.{attn}.out_proj.bias"),
