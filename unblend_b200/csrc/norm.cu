@@ -113,29 +113,34 @@ __global__ void layer_norm_kernel(const float* __restrict__ x, float* __restrict
   int lane = threadIdx.x & 31;
   if (row >= rows) return;
   const float* xr = x + row * c;
+  // Fixed trip count with a predicate so that vals[] stays in registers
+  // (a runtime-bounded loop indexes it dynamically, i.e. in local memory).
   float vals[32];
-  int nper = (c + 31) / 32;
+  const int nper = (c + 31) / 32;
   float s = 0.f;
-  for (int j = 0; j < nper; ++j) {
-    int ch = lane + 32 * j;
-    float v = ch < c ? xr[ch] : 0.f;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const int ch = lane + 32 * j;
+    const float v = (j < nper && ch < c) ? xr[ch] : 0.f;
     vals[j] = v;
     s += v;
   }
-  float mean = ub::warp_sum(s) / c;
+  const float mean = ub::warp_sum(s) / c;
   float s2 = 0.f;
-  for (int j = 0; j < nper; ++j) {
-    int ch = lane + 32 * j;
-    float d = ch < c ? vals[j] - mean : 0.f;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const int ch = lane + 32 * j;
+    const float d = (j < nper && ch < c) ? vals[j] - mean : 0.f;
     s2 += d * d;
   }
-  float var = ub::warp_sum(s2) / c;
-  float rstd = rsqrtf(var + 1e-5f);
+  const float var = ub::warp_sum(s2) / c;
+  const float rstd = rsqrtf(var + 1e-5f);
   float* yr = y + row * c;
   const float* pr = pos ? pos + (row % pos_rows) * c : nullptr;
-  for (int j = 0; j < nper; ++j) {
-    int ch = lane + 32 * j;
-    if (ch < c) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const int ch = lane + 32 * j;
+    if (j < nper && ch < c) {
       float v = (vals[j] - mean) * rstd * gamma[ch] + beta[ch];
       if (pr) v += pos_scale * pr[ch];
       yr[ch] = v;
@@ -182,6 +187,61 @@ __global__ void cast_bf16_kernel(const float4* __restrict__ x, uint2* __restrict
   }
 }
 
+// Four channels per thread with 32-bit index arithmetic (the launchers use
+// these when c is a multiple of 4 and the element count fits in 31 bits; the
+// per-element 64-bit divisions of the scalar kernels dominated their time).
+__global__ void group_norm_apply4_kernel(const float4* __restrict__ x, float4* __restrict__ y,
+                                         const float* __restrict__ st, const float* __restrict__ gamma,
+                                         const float* __restrict__ beta, int n4, int c4, int rows_per_group,
+                                         int act) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += gridDim.x * blockDim.x) {
+    const int r = i / c4, q = i - r * c4;
+    const int g = r / rows_per_group;
+    const float m = __ldg(st + 2 * g), rs = __ldg(st + 2 * g + 1);
+    const float4 v = x[i];
+    float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float t = (e[k] - m) * rs;
+      if (gamma) t = t * __ldg(gamma + 4 * q + k);
+      if (beta) t = t + __ldg(beta + 4 * q + k);
+      if (act == UNBLEND_ACT_GELU) t = ub::gelu_erf(t);
+      e[k] = t;
+    }
+    y[i] = make_float4(e[0], e[1], e[2], e[3]);
+  }
+}
+
+__global__ void dconv_tail4_kernel(float* __restrict__ x, const float4* __restrict__ z,
+                                   const float* __restrict__ st, const float4* __restrict__ gamma,
+                                   const float4* __restrict__ beta, const float4* __restrict__ scale, int n4,
+                                   int c4, int rows_per_group, long long x_gs) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += gridDim.x * blockDim.x) {
+    const int r = i / c4, q = i - r * c4;
+    const int g = r / rows_per_group, rr = r - g * rows_per_group;
+    const float mean = __ldg(st + 2 * g), rstd = __ldg(st + 2 * g + 1);
+    // z row r: 2c values, (value, gate) interleaved per channel.
+    const float4 z0 = __ldg(z + 2LL * i), z1 = __ldg(z + 2LL * i + 1);
+    const float4 g0 = __ldg(gamma + 2 * q), g1 = __ldg(gamma + 2 * q + 1);
+    const float4 b0 = __ldg(beta + 2 * q), b1 = __ldg(beta + 2 * q + 1);
+    const float4 sc = __ldg(scale + q);
+    const float zv[8] = {z0.x, z0.y, z0.z, z0.w, z1.x, z1.y, z1.z, z1.w};
+    const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+    const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+    const float sv[4] = {sc.x, sc.y, sc.z, sc.w};
+    float4* xp = reinterpret_cast<float4*>(x + (long long)g * x_gs + (long long)rr * (4 * c4)) + q;
+    const float4 xv = *xp;
+    float o[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float va = (zv[2 * k] - mean) * rstd * gv[2 * k] + bv[2 * k];
+      const float vg = (zv[2 * k + 1] - mean) * rstd * gv[2 * k + 1] + bv[2 * k + 1];
+      o[k] = o[k] + sv[k] * (va * ub::sigmoidf_(vg));
+    }
+    *xp = make_float4(o[0], o[1], o[2], o[3]);
+  }
+}
+
 }  // namespace
 
 extern "C" int unblend_zero_f64(double* p, long long n, void* stream) {
@@ -216,6 +276,15 @@ extern "C" int unblend_group_norm_apply(const float* x, float* y, const float* s
                                         int act, void* stream) {
   UB_REQUIRE(x && y && stats2 && rows > 0 && c > 0 && rows_per_group > 0);
   UB_REQUIRE(act == UNBLEND_ACT_NONE || act == UNBLEND_ACT_GELU);
+  if (c % 4 == 0 && rows * c < (1LL << 31) && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(y) & 15) == 0) {
+    const int n4 = (int)(rows * c / 4);
+    group_norm_apply4_kernel<<<ub::grid_1d(n4, 256), 256, 0, ub::as_stream(stream)>>>(
+        reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(y), stats2, gamma, beta, n4, c / 4,
+        (int)rows_per_group, act);
+    UB_CHECK_LAUNCH();
+    return 0;
+  }
   group_norm_apply_kernel<<<ub::grid_1d(rows * c, 256), 256, 0, ub::as_stream(stream)>>>(
       x, y, stats2, gamma, beta, rows, c, rows_per_group, act);
   UB_CHECK_LAUNCH();
@@ -227,6 +296,18 @@ extern "C" int unblend_dconv_tail(float* x, const float* z, const float* stats2,
                                   long long rows_per_group, int c, long long x_group_stride, void* stream) {
   UB_REQUIRE(x && z && stats2 && gamma && beta && scale && groups > 0 && rows_per_group > 0 && c > 0);
   UB_REQUIRE(x_group_stride >= rows_per_group * c);
+  const long long n = groups * rows_per_group * c;
+  if (c % 4 == 0 && n < (1LL << 31) && x_group_stride % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(z) & 15) == 0 && (reinterpret_cast<uintptr_t>(gamma) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(beta) & 15) == 0 && (reinterpret_cast<uintptr_t>(scale) & 15) == 0) {
+    const int n4 = (int)(n / 4);
+    dconv_tail4_kernel<<<ub::grid_1d(n4, 256), 256, 0, ub::as_stream(stream)>>>(
+        x, reinterpret_cast<const float4*>(z), stats2, reinterpret_cast<const float4*>(gamma),
+        reinterpret_cast<const float4*>(beta), reinterpret_cast<const float4*>(scale), n4, c / 4,
+        (int)rows_per_group, x_group_stride);
+    UB_CHECK_LAUNCH();
+    return 0;
+  }
   dconv_tail_kernel<<<ub::grid_1d(groups * rows_per_group * c, 256), 256, 0, ub::as_stream(stream)>>>(
       x, z, stats2, gamma, beta, scale, groups, rows_per_group, c, x_group_stride);
   UB_CHECK_LAUNCH();
