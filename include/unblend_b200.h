@@ -153,6 +153,23 @@ int unblend_dconv_apply(float* x, long long x_gs, const float* h, int groups, in
                         const float* b2, const float* st2, const float* g2w, const float* g2b,
                         const float* scale, void* stream);
 
+/* GN2 statistics of the DConv 1x1 output z = W2 a + b2 (a = GELU(GN1(h))) from
+ * the moments of a, for the thin levels (hid <= 16):
+ * dconv_moments adds, per group g, S1[j] = sum_r a[r, j] and
+ * S2[j, k] = sum_r a[r, j] a[r, k] (j <= k, upper triangle row by row) into
+ * moments[g * K ...], K = hw + hw (hw + 1) / 2, hw the computed hidden width
+ * (hid when even, else hid rounded up to a multiple of 4); moments are double
+ * and zeroed by the caller.
+ * dconv_moment_sums turns them into (sum z, sum z^2) per group for
+ * unblend_stats_finalize, from coef = [W2^T 1 (hw), W2^T b2 (hw), W2^T W2 as
+ * the same packed triangle with off-diagonal entries doubled, sum b2,
+ * sum b2^2] (double, over all 2c rows of W2). Replaces unblend_dconv_z_stats
+ * at hw + hw(hw+1)/2 instead of 2 c hw operations per row. */
+int unblend_dconv_moments(const float* h, int groups, int rows, int hid, const float* st1, const float* g1w,
+                          const float* g1b, double* moments, void* stream);
+int unblend_dconv_moment_sums(const double* moments, const double* coef, int groups, int rows, int hid,
+                              double* sums, void* stream);
+
 /* Device flag set when a bounded wait of the DConv apply kernel gives up (0 = none). Synchronous host call. */
 int unblend_dconv_error_flag(int* out_host, int clear);
 

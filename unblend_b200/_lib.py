@@ -125,6 +125,8 @@ _SIGNATURES = {
                               c_void_p],
     "unblend_gather_pairs": [c_void_p, c_ll, c_ll, c_void_p, c_int, c_void_p, c_ll, c_void_p],
     "unblend_cast_bf16": [c_void_p, c_void_p, c_ll, c_void_p],
+    "unblend_dconv_moments": [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p],
+    "unblend_dconv_moment_sums": [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p],
     "unblend_scatter_mean_pairs": [c_void_p, c_ll, c_ll, c_void_p, c_void_p, c_int, c_void_p, c_ll, c_void_p],
     "unblend_stft_frames": [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p],
     "unblend_istft_masked": [c_void_p, c_void_p, c_ll, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,

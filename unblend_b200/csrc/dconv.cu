@@ -643,6 +643,97 @@ __global__ void __launch_bounds__(NTH2) dconv_apply4_kernel(float* __restrict__ 
   }
 }
 
+// ---------------------------------------------------------------------------
+// GN2 statistics from the moments of the 1x1 conv's input. With a = GELU(GN1(h))
+// (HW values per row) and z = W2 a + b2 (2C values per row), the group sums are
+//   sum z   = wsum . S1 + n sum(b2)
+//   sum z^2 = sum_jk G_jk S2_jk + 2 u . S1 + n sum(b2^2)
+// with S1 = sum_r a, S2 = sum_r a a^T, G = W2^T W2, u = W2^T b2, wsum = W2^T 1:
+// HW + HW(HW+1)/2 accumulations per row instead of the 2C*HW FMAs of z.
+// One warp per item (a group's block of rows), lanes striding its rows; the
+// warp's totals go to the group's moments with double atomics.
+template <int HW>
+__global__ void __launch_bounds__(256) dconv_moments_kernel(const float* __restrict__ h, int groups, int rows,
+                                                            int hs, const float* __restrict__ st1,
+                                                            const float* __restrict__ g1w,
+                                                            const float* __restrict__ g1b,
+                                                            double* __restrict__ mom, int rows_per_item) {
+  constexpr int NP = HW * (HW + 1) / 2;
+  constexpr int K = HW + NP;
+  const int lane = threadIdx.x & 31;
+  const long long nw = (long long)gridDim.x * (blockDim.x >> 5);
+  const int nblk = (rows + rows_per_item - 1) / rows_per_item;
+  const long long items = (long long)groups * nblk;
+  float gw[HW], gb[HW];
+#pragma unroll
+  for (int j = 0; j < HW; ++j) {
+    gw[j] = __ldg(g1w + j);
+    gb[j] = __ldg(g1b + j);
+  }
+  for (long long it = blockIdx.x * (long long)(blockDim.x >> 5) + (threadIdx.x >> 5); it < items; it += nw) {
+    const int g = (int)(it / nblk);
+    const int r0 = (int)(it - (long long)g * nblk) * rows_per_item;
+    const int r1 = min(rows, r0 + rows_per_item);
+    const float m1 = __ldg(st1 + 2 * g), rs1 = __ldg(st1 + 2 * g + 1);
+    float acc[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) acc[k] = 0.f;
+    for (int r = r0 + lane; r < r1; r += 32) {
+      const float* hr = h + ((long long)g * rows + r) * hs;
+      float a[HW];
+#pragma unroll
+      for (int j4 = 0; j4 < HW / 4; ++j4) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(hr) + j4);
+        a[4 * j4] = v.x;
+        a[4 * j4 + 1] = v.y;
+        a[4 * j4 + 2] = v.z;
+        a[4 * j4 + 3] = v.w;
+      }
+      if (HW % 4 == 2) {
+        const float2 v = __ldg(reinterpret_cast<const float2*>(hr + HW - 2));
+        a[HW - 2] = v.x;
+        a[HW - 1] = v.y;
+      }
+#pragma unroll
+      for (int j = 0; j < HW; ++j) a[j] = ub::gelu_erf((a[j] - m1) * rs1 * gw[j] + gb[j]);
+#pragma unroll
+      for (int j = 0; j < HW; ++j) acc[j] += a[j];
+      int q = HW;
+#pragma unroll
+      for (int j = 0; j < HW; ++j)
+#pragma unroll
+        for (int k = j; k < HW; ++k) {
+          acc[q] = fmaf(a[j], a[k], acc[q]);
+          ++q;
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < K; ++k) acc[k] = ub::warp_sum(acc[k]);
+#pragma unroll
+    for (int k = 0; k < K; ++k)
+      if (lane == (k & 31) && r0 < r1) atomicAdd(mom + (long long)g * K + k, (double)acc[k]);
+  }
+}
+
+// (sum, sum of squares) of z per group from its moments; coef holds
+// [wsum (HW), u (HW), G packed as the upper triangle row by row with the
+// off-diagonal entries doubled (NP), sum(b2), sum(b2^2)] in double.
+__global__ void dconv_moment_sums_kernel(const double* __restrict__ mom, const double* __restrict__ coef,
+                                         int groups, int hw, double n, double* __restrict__ sums) {
+  const int K = hw + hw * (hw + 1) / 2;
+  for (int g = blockIdx.x * blockDim.x + threadIdx.x; g < groups; g += gridDim.x * blockDim.x) {
+    const double* m = mom + (long long)g * K;
+    double s = n * coef[2 * hw + K - hw], s2 = n * coef[2 * hw + K - hw + 1];
+    for (int j = 0; j < hw; ++j) {
+      s += coef[j] * m[j];
+      s2 += 2.0 * coef[hw + j] * m[j];
+    }
+    for (int q = 0; q < K - hw; ++q) s2 += coef[2 * hw + q] * m[hw + q];
+    sums[2 * g] = s;
+    sums[2 * g + 1] = s2;
+  }
+}
+
 template <typename K>
 unsigned persistent_grid_smem(K kernel, int threads, size_t smem, long long items) {
   int dev = 0, sms = 148, per_sm = 1;
@@ -820,6 +911,45 @@ extern "C" int unblend_dconv_apply(float* x, long long x_gs, const float* h, int
   }
   if (mh == 8) UB_LAUNCH(8) else if (mh == 16) UB_LAUNCH(16) else if (mh == 32) UB_LAUNCH(32) else UB_LAUNCH(64)
 #undef UB_LAUNCH
+  UB_CHECK_LAUNCH();
+  return 0;
+}
+
+extern "C" int unblend_dconv_moments(const float* h, int groups, int rows, int hid, const float* st1,
+                                     const float* g1w, const float* g1b, double* moments, void* stream) {
+  UB_REQUIRE(h && st1 && g1w && g1b && moments && groups > 0 && rows > 0 && hid > 0 && hid <= 16);
+  UB_REQUIRE((reinterpret_cast<uintptr_t>(h) & 15) == 0);
+  const int hs = padded_hidden(hid);
+  const int rpi = 512;  // rows per warp item: 16 per lane
+  const long long items = (long long)groups * ((rows + rpi - 1) / rpi);
+  const long long warps_needed = items;
+  long long blocks = (warps_needed + 7) / 8;
+  const long long cap = 148LL * 8;
+  if (blocks > cap) blocks = cap;
+  cudaStream_t st = ub::as_stream(stream);
+#define UB_MOM(HW) dconv_moments_kernel<HW><<<(unsigned)blocks, 256, 0, st>>>(h, groups, rows, hs, st1, g1w, g1b, moments, rpi)
+  switch (compute_width(hid)) {
+    case 2: UB_MOM(2); break;
+    case 4: UB_MOM(4); break;
+    case 6: UB_MOM(6); break;
+    case 8: UB_MOM(8); break;
+    case 10: UB_MOM(10); break;
+    case 12: UB_MOM(12); break;
+    case 14: UB_MOM(14); break;
+    case 16: UB_MOM(16); break;
+    default: return UNBLEND_ERR_INVALID;
+  }
+#undef UB_MOM
+  UB_CHECK_LAUNCH();
+  return 0;
+}
+
+extern "C" int unblend_dconv_moment_sums(const double* moments, const double* coef, int groups, int rows, int hid,
+                                         double* sums, void* stream) {
+  UB_REQUIRE(moments && coef && sums && groups > 0 && rows > 0 && hid > 0 && hid <= 16);
+  const int hw = compute_width(hid);
+  dconv_moment_sums_kernel<<<(groups + 127) / 128, 128, 0, ub::as_stream(stream)>>>(moments, coef, groups, hw,
+                                                                                  (double)rows, sums);
   UB_CHECK_LAUNCH();
   return 0;
 }

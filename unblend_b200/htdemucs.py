@@ -35,6 +35,11 @@ def _key(name: str) -> str:
     return name.replace(".", "__")
 
 
+def _moment_width(hid: int) -> int:
+    """Hidden width the fused DConv kernels compute with: the true width when even, else rounded up to 4."""
+    return hid if hid % 2 == 0 else -(-hid // 4) * 4
+
+
 @dataclass
 class Act:
     """A channels-last activation view: ``t`` holds [B, H, W, C] with strides sb/sh/sw."""
@@ -261,6 +266,7 @@ class HTDemucsCuda(nn.Module):
             self._put(f"{q}.g2.w", _interleave_rows(sd[f"{q}.4.weight"]))
             self._put(f"{q}.g2.b", _interleave_rows(sd[f"{q}.4.bias"]))
             self._put(f"{q}.scale", sd[f"{q}.6.scale"])
+            self._put_moment_coef(q, sd[f"{q}.3.weight"], sd[f"{q}.3.bias"])
             # Hidden width padded to a multiple of 4 with zero channels (16-byte h
             # rows for the bulk copies of the fused kernels): the padded channels
             # are exactly 0 before and after GELU(GN1) and meet zero weights in W2.
@@ -275,6 +281,23 @@ class HTDemucsCuda(nn.Module):
                 self._put(f"{q}.g1p.b", torch.cat([sd[f"{q}.1.bias"], sd[f"{q}.1.bias"].new_zeros(pad)]))
                 c2 = _interleave_rows(_conv_w(sd[f"{q}.3.weight"]))
                 self._put(f"{q}.c2p.w", torch.nn.functional.pad(c2, (0, pad)))
+
+    def _put_moment_coef(self, q: str, w2: torch.Tensor, b2: torch.Tensor) -> None:
+        """Coefficients turning the moments of a = GELU(GN1(h)) into the sums of z = W2 a + b2 (float64).
+
+        [W2^T 1, W2^T b2, W2^T W2 upper triangle row by row (off-diagonal doubled), sum b2, sum b2^2]
+        over the computed hidden width (``_moment_width``; extra columns zero).
+        """
+        w = w2.reshape(w2.shape[0], -1).double()
+        b = b2.double()
+        hid = w.shape[1]
+        hw = _moment_width(hid)
+        if hw != hid:
+            w = torch.nn.functional.pad(w, (0, hw - hid))
+        g = w.t() @ w
+        tri = [g[j, k] * (1.0 if j == k else 2.0) for j in range(hw) for k in range(j, hw)]
+        coef = torch.cat([w.sum(0), w.t() @ b, torch.stack(tri), b.sum()[None], (b * b).sum()[None]])
+        self.register_buffer(_key(f"{q}.mom_coef"), coef.contiguous(), persistent=False)
 
     def _tables(self, device: torch.device, F: int, T: int, Lt: int) -> dict:
         """Window, positional and frequency-embedding tables (cached per device and shape)."""
@@ -420,11 +443,17 @@ class HTDemucsCuda(nn.Module):
             if fused:
                 # z = W2 GELU(GN1(h)) is recomputed instead of stored: once for
                 # the GN2 statistics, once for the in-place residual update.
-                st2 = torch.zeros(2 * groups, device=dev, dtype=torch.float64)
                 args = (pw("g1.w").data_ptr(), pw("g1.b").data_ptr(), pw("c2.w").data_ptr(),
                         self.w(f"{q}.c2.b").data_ptr())
-                _lib.call("unblend_dconv_z_stats", h.t.data_ptr(), groups, W, hid, C, s1.data_ptr(), *args,
-                          st2.data_ptr(), work=4.0 * groups * W * C * hid)
+                # GN2 statistics from the moments of GELU(GN1(h)): no z at all.
+                hw = _moment_width(hid)
+                mom = torch.zeros(groups * (hw + hw * (hw + 1) // 2), device=dev, dtype=torch.float64)
+                _lib.call("unblend_dconv_moments", h.t.data_ptr(), groups, W, hid, s1.data_ptr(),
+                          pw("g1.w").data_ptr(), pw("g1.b").data_ptr(), mom.data_ptr(),
+                          work=1.0 * groups * W * hw * (hw + 3))
+                st2 = torch.empty(2 * groups, device=dev, dtype=torch.float64)
+                _lib.call("unblend_dconv_moment_sums", mom.data_ptr(), getattr(self, _key(f"{q}.mom_coef")).data_ptr(),
+                          groups, W, hid, st2.data_ptr())
                 s2 = self._stats(st2, groups, W * 2 * C)
                 _lib.call("unblend_dconv_apply", x.t.data_ptr(), x_gs, h.t.data_ptr(), groups, W, hid, C,
                           s1.data_ptr(), *args, s2.data_ptr(), self.w(f"{q}.g2.w").data_ptr(),
