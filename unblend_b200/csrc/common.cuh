@@ -38,6 +38,18 @@ __device__ __forceinline__ float sigmoid_approx(float x) {
   return r;
 }
 
+// Two fp32 FMAs in one instruction (fma.rn.f32x2, sm_100): c + a * b per lane
+// pair, each rounded once exactly as fmaf. Halves the issue slots of FMA-bound
+// SIMT loops.
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  unsigned long long r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;"
+      : "=l"(r)
+      : "l"(*reinterpret_cast<unsigned long long*>(&a)), "l"(*reinterpret_cast<unsigned long long*>(&b)),
+        "l"(*reinterpret_cast<unsigned long long*>(&c)));
+  return *reinterpret_cast<float2*>(&r);
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

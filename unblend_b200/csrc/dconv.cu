@@ -271,21 +271,19 @@ __device__ __forceinline__ void stage_act(const float* __restrict__ hs, int nrow
 // HW is the exact hidden width when it is a multiple of 2 known at compile time.
 template <int MAXH, int HW>
 __device__ __forceinline__ float dot_a(const float* __restrict__ a, const float (&w)[MAXH]) {
-  float z = 0.f;
+  // Even and odd terms in two packed-FMA partial sums.
+  float2 z = make_float2(0.f, 0.f);
 #pragma unroll
   for (int j4 = 0; j4 < HW / 4; ++j4) {
     const float4 v = *reinterpret_cast<const float4*>(a + 4 * j4);
-    z = fmaf(v.x, w[4 * j4], z);
-    z = fmaf(v.y, w[4 * j4 + 1], z);
-    z = fmaf(v.z, w[4 * j4 + 2], z);
-    z = fmaf(v.w, w[4 * j4 + 3], z);
+    z = ub::fma2(make_float2(v.x, v.y), make_float2(w[4 * j4], w[4 * j4 + 1]), z);
+    z = ub::fma2(make_float2(v.z, v.w), make_float2(w[4 * j4 + 2], w[4 * j4 + 3]), z);
   }
   if (HW % 4 == 2) {
     const float2 v = *reinterpret_cast<const float2*>(a + HW - 2);
-    z = fmaf(v.x, w[HW - 2], z);
-    z = fmaf(v.y, w[HW - 1], z);
+    z = ub::fma2(v, make_float2(w[HW - 2], w[HW - 1]), z);
   }
-  return z;
+  return z.x + z.y;
 }
 
 
@@ -419,12 +417,13 @@ __global__ void __launch_bounds__(C1_NT) dconv_conv1b_kernel(const float* __rest
     ws[(c * 3 + t) * HP + j] = __ldg(w1 + i);
   }
   const int lr0 = (tid >> 5) * 32 * C1_RT + (tid & 31);
-  float acc[C1_RT][HW];
+  static_assert(HW % 2 == 0, "pairs of hidden outputs");
+  float2 acc[C1_RT][HW / 2];  // (output 2p, output 2p+1) of each row, fed by packed FMAs
 #pragma unroll
-  for (int j = 0; j < HW; ++j) {
-    const float b = __ldg(b1 + j);
+  for (int p = 0; p < HW / 2; ++p) {
+    const float2 b = make_float2(__ldg(b1 + 2 * p), __ldg(b1 + 2 * p + 1));
 #pragma unroll
-    for (int i = 0; i < C1_RT; ++i) acc[i][j] = b;
+    for (int i = 0; i < C1_RT; ++i) acc[i][p] = b;
   }
   const int last = min(rows, r0 + C1_IR + dil);  // rows past this are never read
   const int nst = min(C1_IR, rows - r0) + 2 * dil;
@@ -459,8 +458,9 @@ __global__ void __launch_bounds__(C1_NT) dconv_conv1b_kernel(const float* __rest
         for (int i = 0; i < C1_RT; ++i) {
           // Staged rows beyond nst are stale but only feed rows >= rows, which are dropped.
           const float xv = xc[(lr0 + 32 * i + t * dil) * C1_XS + c];
+          const float2 xx = make_float2(xv, xv);
 #pragma unroll
-          for (int j = 0; j < HW; ++j) acc[i][j] = fmaf(xv, wv[j], acc[i][j]);
+          for (int p = 0; p < HW / 2; ++p) acc[i][p] = ub::fma2(xx, make_float2(wv[2 * p], wv[2 * p + 1]), acc[i][p]);
         }
       }
     }
@@ -471,17 +471,23 @@ __global__ void __launch_bounds__(C1_NT) dconv_conv1b_kernel(const float* __rest
     const int r = r0 + lr0 + 32 * i;
     if (r < rows && lr0 + 32 * i < C1_IR) {
       float4* hr = reinterpret_cast<float4*>(h + ((long long)g * rows + r) * HP);
+      float hv[HW];
+#pragma unroll
+      for (int p = 0; p < HW / 2; ++p) {
+        hv[2 * p] = acc[i][p].x;
+        hv[2 * p + 1] = acc[i][p].y;
+      }
 #pragma unroll
       for (int j4 = 0; j4 < HP / 4; ++j4) {
         float v[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) v[e] = 4 * j4 + e < HW ? acc[i][4 * j4 + e] : 0.f;
+        for (int e = 0; e < 4; ++e) v[e] = 4 * j4 + e < HW ? hv[4 * j4 + e] : 0.f;
         hr[j4] = make_float4(v[0], v[1], v[2], v[3]);
       }
 #pragma unroll
       for (int j = 0; j < HW; ++j) {
-        s1 += acc[i][j];
-        s2 += acc[i][j] * acc[i][j];
+        s1 += hv[j];
+        s2 += hv[j] * hv[j];
       }
     }
   }
