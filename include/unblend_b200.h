@@ -328,6 +328,24 @@ int unblend_scatter_mean_pairs(const float* src, long long src_ld, long long row
  * y 8-byte aligned. Feeds fp32 projections to the bf16 attention kernel. */
 int unblend_cast_bf16(const float* x, void* y, long long n, void* stream);
 
+/* Audio I/O edges (unblend/api.py:1080-1112, unblend/audio.py:14-90), fp32 planar [channels, frames]:
+ * pcm16_to_f32: interleaved int16 [frames, cin] -> dst[cout, frames] = x / 32768 with the channel
+ *   conversion of convert_audio_channels (same count: copy; cout 1: mean; cin 1: replicate;
+ *   cin > cout: the first cout); cin, cout <= 8.
+ * convert_channels: the same conversion on fp32 planar input.
+ * resample: y[c, k*lout + p] = sum_{m < taps} x[c, k*lin + m - width] * kern[p, m] (x zero outside
+ *   [0, length)), out_length outputs per channel; kern [lout, taps] is the polyphase filter bank.
+ * max_abs: atomically maxes max|x| (as float bits) into *out_bits (zeroed by the caller).
+ * prevent_clip: mode 1 y = x / max(1.01 max|x|, 1) reading *maxabs_bits; 2 clamp to [-0.99, 0.99];
+ *   3 tanh. */
+int unblend_pcm16_to_f32(const void* src, int cin, long long frames, float* dst, int cout, void* stream);
+int unblend_convert_channels(const float* x, int cin, long long frames, float* y, int cout, void* stream);
+int unblend_resample(const float* x, int channels, long long length, const float* kern, int taps, int lin,
+                     int lout, int width, float* y, long long out_length, void* stream);
+int unblend_max_abs(const float* x, long long n, unsigned* out_bits, void* stream);
+int unblend_prevent_clip(const float* x, float* y, long long n, int mode, const unsigned* maxabs_bits,
+                         void* stream);
+
 /* Elementwise y[i] = a[i] + alpha * b[i % b_period] (skip adds, embeddings). */
 int unblend_add(const float* a, const float* b, float* y, long long n, long long b_period,
                 float alpha, void* stream);

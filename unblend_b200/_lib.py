@@ -125,6 +125,11 @@ _SIGNATURES = {
                               c_void_p],
     "unblend_gather_pairs": [c_void_p, c_ll, c_ll, c_void_p, c_int, c_void_p, c_ll, c_void_p],
     "unblend_cast_bf16": [c_void_p, c_void_p, c_ll, c_void_p],
+    "unblend_pcm16_to_f32": [c_void_p, c_int, c_ll, c_void_p, c_int, c_void_p],
+    "unblend_convert_channels": [c_void_p, c_int, c_ll, c_void_p, c_int, c_void_p],
+    "unblend_resample": [c_void_p, c_int, c_ll, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_ll, c_void_p],
+    "unblend_max_abs": [c_void_p, c_ll, c_void_p, c_void_p],
+    "unblend_prevent_clip": [c_void_p, c_void_p, c_ll, c_int, c_void_p, c_void_p],
     "unblend_dconv_moments": [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p],
     "unblend_dconv_moment_sums": [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p],
     "unblend_scatter_mean_pairs": [c_void_p, c_ll, c_ll, c_void_p, c_void_p, c_int, c_void_p, c_ll, c_void_p],
