@@ -338,10 +338,8 @@ def main() -> None:
     hosts = [t.pin_memory() for t in tracks]
     if split:
         def e2e_step():
-            out = apply_model_sharded(model, hosts[0].to(dev, non_blocking=True), chunk_batch_size=batch,
-                                      shifts=shifts, gather=True)
-            if rank == 0:
-                out.to("cpu")
+            # Host track in, full [S, C, L] result back in page-locked host memory on every rank.
+            apply_model_sharded(model, hosts[0], device=dev, chunk_batch_size=batch, shifts=shifts, gather=True)
     else:
         def e2e_step():
             for hst in hosts:

@@ -48,6 +48,12 @@ def _worker(rank: int, world: int, port: int, key: str, shifts: int, q) -> None:
                                   shift_offsets=g[key].get("offsets"))
         err = rel_err(out[None].cpu()[..., :: g["decimate"]], g[key]["out"])
         lo, hi, own = apply_model_sharded(m, g["mix"][0].cuda(), overlap=g["overlap"], gather=False)
+        # A host track: copied in by the engine, result back in page-locked host memory.
+        host = apply_model_sharded(m, g["mix"][0].clone(), overlap=g["overlap"], chunk_batch_size=1, shifts=shifts,
+                                   shift_offsets=g[key].get("offsets"), device=torch.device("cuda", rank))
+        assert host.device.type == "cpu" and host.is_pinned()
+        # Not bit-equal: the DConv statistics accumulate with float64 atomics, in any order.
+        assert rel_err(host, out.cpu()) < 1e-6
         q.put((rank, err, lo, hi, tuple(own.shape)))
     finally:
         dist.destroy_process_group()

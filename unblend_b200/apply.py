@@ -257,13 +257,18 @@ def apply_model(model: Any, mix: torch.Tensor, device: torch.device | str | None
     if squeeze:
         out = out[0]
     if orig_device.type == "cpu":
-        # Page-locked staging (torch's caching host allocator): the device->host
-        # copy runs at full PCIe/C2C bandwidth instead of through pageable memory.
-        host = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
-        host.copy_(out, non_blocking=True)
-        torch.cuda.current_stream(device).synchronize()
-        return host
+        return _to_host(out)
     return out.to(orig_device)
+
+
+def _to_host(out: torch.Tensor) -> torch.Tensor:
+    """Copy a device result into page-locked host memory (torch's caching host
+    allocator), so the device->host copy runs at full link bandwidth instead of
+    through pageable memory."""
+    host = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    host.copy_(out, non_blocking=True)
+    torch.cuda.current_stream(out.device).synchronize()
+    return host
 
 
 def _shift_plan(shifts: int, rows: int, max_shift: int, shift_offsets: list[int] | None) -> list[list[int]]:

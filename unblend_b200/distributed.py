@@ -27,7 +27,7 @@ from typing import Any
 import torch
 import torch.distributed as dist
 
-from .apply import ValidationError, _accumulate, _segment_plan
+from .apply import ValidationError, _accumulate, _segment_plan, _to_host
 
 
 @dataclass(frozen=True)
@@ -131,12 +131,15 @@ def gather_owned(own: torch.Tensor, plan: list[Shard], rank: int, length: int, g
 
 def apply_model_sharded(model: Any, mix: torch.Tensor, *, overlap: float = 0.25, chunk_batch_size: int = 1,
                         shifts: int = 0, shift_offsets: list[int] | None = None, group: Any = None,
-                        gather: bool = True) -> torch.Tensor | tuple[int, int, torch.Tensor]:
+                        gather: bool = True, device: Any = None) -> torch.Tensor | tuple[int, int, torch.Tensor]:
     """``apply_model`` for one ``[C, L]`` track with its segments sharded across the ranks of ``group``.
 
-    Every rank calls this with the same track (already on its own CUDA device)
-    and arguments. With ``shifts`` the random offsets are drawn on rank 0 and
-    broadcast, so every rank separates the same shifted rounds.
+    Every rank calls this with the same track and arguments. The track is either
+    on this rank's CUDA device, or on the host, in which case it is copied to
+    ``device`` (default: the current CUDA device) and the result comes back in
+    page-locked host memory, as ``apply_model`` does for a host input. With
+    ``shifts`` the random offsets are drawn on rank 0 and broadcast, so every
+    rank separates the same shifted rounds.
 
     :return: the full ``[S, C, L]`` result on every rank when ``gather`` (always
         with ``shifts``), else ``(own_lo, own_hi, out[S, C, own_hi - own_lo])`` for
@@ -144,8 +147,14 @@ def apply_model_sharded(model: Any, mix: torch.Tensor, *, overlap: float = 0.25,
     """
     if not 0.0 <= overlap < 1.0:
         raise ValidationError(f"overlap must be in [0, 1), got {overlap}")
+    host_io = mix.device.type == "cpu"
+    if host_io:
+        dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        if dev.type != "cuda":
+            raise ValidationError("the B200 segment engine runs on CUDA devices only")
+        mix = mix.to(dev, non_blocking=True)
     if mix.dim() != 2 or mix.device.type != "cuda":
-        raise ValidationError("expected one [C, L] track on this rank's CUDA device")
+        raise ValidationError("expected one [C, L] track on the host or on this rank's CUDA device")
     rank = dist.get_rank(group)
     world = dist.get_world_size(group)
     # A collective first: NCCL's batched point-to-point calls need every rank to
@@ -179,12 +188,14 @@ def apply_model_sharded(model: Any, mix: torch.Tensor, *, overlap: float = 0.25,
             _accumulate(model, track, S, segment, list(me.offsets), off_dev, chunk_batch_size, acc, sum_w)
         own = stitch(acc, sum_w, plan, rank, group)
         if not gather and not shifts:
-            return me.own_lo, me.own_hi, own.view(S, C, me.own_hi - me.own_lo)
+            own = own.view(S, C, me.own_hi - me.own_lo)
+            return me.own_lo, me.own_hi, _to_host(own) if host_io else own
         full = gather_owned(own, plan, rank, Lr, group)
         if shifts:
             full = full[:, max_shift - off:][:, :L]
         total = full if total is None else total.add_(full)
-    return (total / len(rounds)).view(S, C, L)
+    out = (total / len(rounds)).view(S, C, L)
+    return _to_host(out) if host_io else out
 
 
 __all__ = ["Shard", "shard_plan", "stitch", "gather_owned", "apply_model_sharded"]
