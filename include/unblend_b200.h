@@ -346,6 +346,13 @@ int unblend_max_abs(const float* x, long long n, unsigned* out_bits, void* strea
 int unblend_prevent_clip(const float* x, float* y, long long n, int mode, const unsigned* maxabs_bits,
                          void* stream);
 
+/* 16-bit PCM export of one stem (unblend/api.py:94-148 export_stem -> prevent_clip, then the
+ * encoder's float -> s16 conversion): x planar fp32 [channels, frames] -> dst interleaved int16
+ * [frames, channels]; the clipping guard of prevent_clip applied first (mode 0 none, 1-3 as above),
+ * then q = saturate_s16(round_half_even(v * 32768)); NaN -> 0. channels <= 8. */
+int unblend_encode_pcm16(const float* x, int channels, long long frames, int mode, const unsigned* maxabs_bits,
+                         void* dst, void* stream);
+
 /* Elementwise y[i] = a[i] + alpha * b[i % b_period] (skip adds, embeddings). */
 int unblend_add(const float* a, const float* b, float* y, long long n, long long b_period,
                 float alpha, void* stream);

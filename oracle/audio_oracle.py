@@ -10,6 +10,13 @@
   audio and the polyphase sums in float64; pinned against torchaudio's own outputs
   (``tests/golden/audio_io.pt``, made by ``tests/golden/make_audio_golden.py``).
 * ``prevent_clip``: unblend/audio.py:70-90.
+* ``encode_pcm16``: unblend/api.py:94-148 (``export_stem``: ``prevent_clip``,
+  then the encoder). The reference hands the clipped float stem to torchcodec's
+  ``AudioEncoder`` (not installed in this image), whose 16-bit PCM WAV path
+  converts samples with FFmpeg libswresample's float -> s16 rule: round
+  ``x * 2**15`` to nearest, ties to even (``lrintf``), saturate to int16.
+  Restated from that published rule; pinned by the round trip through the
+  reference's own decoded fixture (decode -> encode gives the file's bytes back).
 """
 
 from __future__ import annotations
@@ -74,3 +81,11 @@ def prevent_clip(x: np.ndarray, mode: str | None = "rescale") -> np.ndarray:
     if mode == "tanh":
         return np.tanh(x).astype(np.float32)
     return x
+
+
+def encode_pcm16(x: np.ndarray, clip: str | None = "rescale") -> np.ndarray:
+    """Planar float32 ``[C, L]`` -> interleaved int16 ``[L, C]``."""
+    y = prevent_clip(np.asarray(x, dtype=np.float32), clip).astype(np.float32)
+    q = np.rint(y * np.float32(32768.0))
+    q = np.where(np.isnan(q), 0.0, np.clip(q, -32768, 32767))
+    return q.astype(np.int16).T.copy()

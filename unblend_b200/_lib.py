@@ -130,6 +130,7 @@ _SIGNATURES = {
     "unblend_resample": [c_void_p, c_int, c_ll, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_ll, c_void_p],
     "unblend_max_abs": [c_void_p, c_ll, c_void_p, c_void_p],
     "unblend_prevent_clip": [c_void_p, c_void_p, c_ll, c_int, c_void_p, c_void_p],
+    "unblend_encode_pcm16": [c_void_p, c_int, c_ll, c_int, c_void_p, c_void_p, c_void_p],
     "unblend_dconv_moments": [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p],
     "unblend_dconv_moment_sums": [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p],
     "unblend_scatter_mean_pairs": [c_void_p, c_ll, c_ll, c_void_p, c_void_p, c_int, c_void_p, c_ll, c_void_p],

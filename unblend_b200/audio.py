@@ -13,11 +13,15 @@ longer than the separation itself. These keep them on the device:
   (Hann-windowed sinc, 6 zero crossings, roll-off 0.99, rates reduced by their
   gcd) as a polyphase CUDA kernel.
 * :func:`prevent_clip` (unblend/audio.py:70-90): rescale / clamp / tanh.
+* :func:`export_pcm16_wav` (unblend/api.py:94-148 ``export_stem`` for WAV):
+  the clipping guard and the float -> 16-bit PCM conversion in one kernel,
+  then a canonical 44-byte WAV header on the host.
 """
 
 from __future__ import annotations
 
 import math
+import struct
 import wave
 from pathlib import Path
 
@@ -148,5 +152,69 @@ def prevent_clip(audio: torch.Tensor, mode: str | None = "rescale") -> torch.Ten
     return y
 
 
+def _pcm16_wav_header(channels: int, sample_rate: int, frames: int) -> bytes:
+    """Canonical 44-byte RIFF/WAVE header of 16-bit PCM."""
+    data = frames * channels * 2
+    if data > 0xFFFFFFFF - 36:
+        raise ValidationError("stem too long for a RIFF WAV file (4 GiB data limit)")
+    return (b"RIFF" + struct.pack("<I", 36 + data) + b"WAVE"
+            + b"fmt " + struct.pack("<IHHIIHH", 16, 1, channels, sample_rate, sample_rate * channels * 2,
+                                    channels * 2, 16)
+            + b"data" + struct.pack("<I", data))
+
+
+def export_pcm16_wav(audio: torch.Tensor, sample_rate: int, path: Path | str | None = None,
+                     format: str = "wav", clip: str | None = "rescale") -> Path | bytes:
+    """One stem ``[channels, samples]`` to a 16-bit PCM WAV file or bytes (unblend/api.py:94-148 export_stem).
+
+    The clipping guard (``prevent_clip``) and the float -> 16-bit conversion run
+    in one kernel on the device, so only the 2-byte interleaved samples cross to
+    the host. A ``path`` without a suffix gets ``.{format}``; only ``wav`` is
+    encoded here (other containers go through a general-purpose encoder).
+
+    :return: the written path when ``path`` is given, else the file's bytes.
+    """
+    if clip and clip not in CLIP_MODES:
+        raise ValidationError(f"Invalid clip mode '{clip}'. Must be one of: 'rescale', 'clamp', 'tanh', or None")
+    file_path = None
+    if path is not None:
+        file_path = Path(path)
+        if not file_path.suffix:
+            file_path = file_path.with_suffix(f".{format}")
+        fmt = file_path.suffix[1:].lower()
+    else:
+        fmt = format.lower()
+    if fmt != "wav":
+        raise ValidationError(f"only 16-bit PCM WAV is encoded on the device, got '{fmt}'")
+    if audio.dim() != 2:
+        raise ValidationError("expected one stem as [channels, samples]")
+    if sample_rate <= 0:
+        raise ValidationError("sample rate must be positive")
+    channels, frames = audio.shape
+    header = _pcm16_wav_header(channels, sample_rate, frames)
+    dev = audio.device if audio.device.type == "cuda" else torch.device("cuda", torch.cuda.current_device())
+    x = audio.to(dev, dtype=torch.float32, non_blocking=True).contiguous()
+    host = torch.empty(frames * channels, dtype=torch.int16, pin_memory=True)
+    if frames:
+        with torch.cuda.device(dev):
+            bits = None
+            if clip == "rescale":
+                bits = torch.zeros(1, device=dev, dtype=torch.int32)
+                _lib.call("unblend_max_abs", x.data_ptr(), x.numel(), bits.data_ptr())
+            pcm = torch.empty(frames * channels, device=dev, dtype=torch.int16)
+            _lib.call("unblend_encode_pcm16", x.data_ptr(), channels, frames, CLIP_MODES.get(clip, 0) if clip else 0,
+                      _lib.ptr(bits), pcm.data_ptr())
+            host.copy_(pcm, non_blocking=True)
+            torch.cuda.current_stream(dev).synchronize()
+    body = host.numpy().tobytes()
+    if file_path is None:
+        return header + body
+    file_path.parent.mkdir(exist_ok=True, parents=True)
+    with open(file_path, "wb") as f:
+        f.write(header)
+        f.write(body)
+    return file_path
+
+
 __all__ = ["read_pcm16_wav", "convert_audio_channels", "convert_audio", "resample", "sinc_resample_kernel",
-           "prevent_clip"]
+           "prevent_clip", "export_pcm16_wav"]

@@ -2,7 +2,8 @@
 // decode with channel conversion, windowed-sinc resampling, and the clipping
 // guards applied before export (unblend/api.py:1080-1112 _read_pcm16_wav,
 // unblend/audio.py:14-67 convert_audio_channels / convert_audio,
-// unblend/audio.py:70-90 prevent_clip). Decoding on the device moves the
+// unblend/audio.py:70-90 prevent_clip), and the 16-bit PCM export of a stem
+// (unblend/api.py:94-148 export_stem). Decoding and encoding on the device move
 // 2-byte samples over PCIe instead of 4-byte floats.
 #include "common.cuh"
 
@@ -95,7 +96,41 @@ __global__ void prevent_clip_kernel(const float* __restrict__ x, float* __restri
   }
 }
 
+// Export edge: planar fp32 [channels, frames] -> interleaved int16 [frames,
+// channels], the clipping guard above applied first (mode 0 = none), then the
+// float -> signed 16-bit conversion of FFmpeg's libswresample that the
+// reference's encoder runs for a 16-bit PCM WAV stem: round x * 2^15 to the
+// nearest integer (ties to even, as lrintf in the default rounding mode) and
+// saturate to [-32768, 32767]. NaN samples are written as 0.
+__global__ void encode_pcm16_kernel(const float* __restrict__ x, int channels, long long frames, int mode,
+                                    const unsigned* __restrict__ maxabs_bits, short* __restrict__ dst) {
+  const float s = mode == 1 ? fmaxf(1.01f * __uint_as_float(*maxabs_bits), 1.0f) : 1.f;
+  const long long n = frames * channels;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long f = i / channels;
+    const int c = (int)(i - f * channels);
+    float v = __ldg(x + (long long)c * frames + f);
+    if (mode == 1) v = v / s;
+    else if (mode == 2) v = fminf(fmaxf(v, -0.99f), 0.99f);
+    else if (mode == 3) v = tanhf(v);
+    int q = __float2int_rn(v * 32768.f);
+    q = isnan(v) ? 0 : min(max(q, -32768), 32767);
+    dst[i] = (short)q;
+  }
+}
+
 }  // namespace
+
+extern "C" int unblend_encode_pcm16(const float* x, int channels, long long frames, int mode,
+                                    const unsigned* maxabs_bits, void* dst, void* stream) {
+  UB_REQUIRE(x && dst && channels > 0 && channels <= 8 && frames > 0 && mode >= 0 && mode <= 3);
+  UB_REQUIRE(mode != 1 || maxabs_bits);
+  encode_pcm16_kernel<<<ub::grid_1d(frames * channels, 256), 256, 0, ub::as_stream(stream)>>>(
+      x, channels, frames, mode, maxabs_bits, reinterpret_cast<short*>(dst));
+  UB_CHECK_LAUNCH();
+  return 0;
+}
 
 extern "C" int unblend_pcm16_to_f32(const void* src, int cin, long long frames, float* dst, int cout, void* stream) {
   UB_REQUIRE(src && dst && frames > 0 && cin > 0 && cin <= 8 && cout > 0 && cout <= 8);
