@@ -398,6 +398,9 @@ constexpr int C1_RT = 3;
 constexpr int C1_IR = C1_NT * C1_RT;  // rows per CTA
 constexpr int C1_CK = 16;              // channels per staged chunk
 constexpr int C1_XS = C1_CK + 1;       // staged row stride (floats)
+constexpr int C1_MAXDIL = 8;           // largest dilation the launcher accepts
+// float4 staging slots per thread: every (row, 4-channel) slot of a chunk with its halo.
+constexpr int C1_PF = ((C1_IR + 2 * C1_MAXDIL) * (C1_CK / 4) + C1_NT - 1) / C1_NT;
 
 template <int HP, int HW>
 __global__ void __launch_bounds__(C1_NT) dconv_conv1b_kernel(const float* __restrict__ x, long long x_gs, int rows,
@@ -427,20 +430,43 @@ __global__ void __launch_bounds__(C1_NT) dconv_conv1b_kernel(const float* __rest
   }
   const int last = min(rows, r0 + C1_IR + dil);  // rows past this are never read
   const int nst = min(C1_IR, rows - r0) + 2 * dil;
+  // The next chunk's x values are fetched into registers while the current
+  // chunk is computed (all C1_PF loads of a thread in flight at once).
+  // Slot k of thread tid is staged row rq + PF_ROWS * k, channels [4 q, 4 q + 4) of the chunk.
+  constexpr int PF_ROWS = C1_NT / (C1_CK / 4);
+  const int q = tid % (C1_CK / 4), rq = tid / (C1_CK / 4);
+  const float* xs = xg + (long long)(r0 - dil + rq) * C + 4 * q;  // slot 0 of chunk 0
+  float4 pf[C1_PF];
+#pragma unroll
+  for (int k = 0; k < C1_PF; ++k) {
+    const int r = r0 - dil + rq + PF_ROWS * k;
+    pf[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (rq + PF_ROWS * k < nst && r >= 0 && r < last)
+      pf[k] = __ldg(reinterpret_cast<const float4*>(xs + (long long)PF_ROWS * k * C));
+  }
   for (int c0 = 0; c0 < C; c0 += C1_CK) {
     __syncthreads();  // the previous chunk is consumed (and ws is written)
-    for (int i = tid; i < nst * (C1_CK / 4); i += C1_NT) {
-      const int rr = i / (C1_CK / 4), q = i - rr * (C1_CK / 4);
-      const int r = r0 - dil + rr;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (r >= 0 && r < last) v = __ldg(reinterpret_cast<const float4*>(xg + (long long)r * C + c0 + 4 * q));
-      float* d = xc + rr * C1_XS + 4 * q;
-      d[0] = v.x;
-      d[1] = v.y;
-      d[2] = v.z;
-      d[3] = v.w;
+#pragma unroll
+    for (int k = 0; k < C1_PF; ++k) {
+      if (rq + PF_ROWS * k < nst) {
+        float* d = xc + (rq + PF_ROWS * k) * C1_XS + 4 * q;
+        d[0] = pf[k].x;
+        d[1] = pf[k].y;
+        d[2] = pf[k].z;
+        d[3] = pf[k].w;
+      }
     }
     __syncthreads();
+    if (c0 + C1_CK < C) {
+      const float* xn = xs + c0 + C1_CK;
+#pragma unroll
+      for (int k = 0; k < C1_PF; ++k) {
+        const int r = r0 - dil + rq + PF_ROWS * k;
+        pf[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (rq + PF_ROWS * k < nst && r >= 0 && r < last)
+          pf[k] = __ldg(reinterpret_cast<const float4*>(xn + (long long)PF_ROWS * k * C));
+      }
+    }
 #pragma unroll 2
     for (int c = 0; c < C1_CK; ++c) {
 #pragma unroll
@@ -777,7 +803,7 @@ static inline int compute_width(int hid) { return hid % 2 == 0 ? hid : padded_hi
 extern "C" int unblend_dconv_conv1(const float* x, long long x_gs, int groups, int rows, int c, const float* w1,
                                    const float* b1, int hid, int dil, float* h, double* stats, void* stream) {
   UB_REQUIRE(x && w1 && b1 && h && stats && groups > 0 && rows > 0 && c > 0 && c % 4 == 0);
-  UB_REQUIRE(hid > 0 && dil > 0 && dil <= 8 && groups < 65536 && x_gs >= (long long)rows * c);
+  UB_REQUIRE(hid > 0 && dil > 0 && dil <= C1_MAXDIL && groups < 65536 && x_gs >= (long long)rows * c);
   const int hs = padded_hidden(hid);
   const int mh = maxh_for(hs);
   UB_REQUIRE(mh > 0);
