@@ -64,3 +64,22 @@ def test_from_reference_module_matches_direct_construction():
     sa, sb = a.state_dict(), b.state_dict()
     assert sa.keys() == sb.keys()
     assert all(torch.equal(sa[k], sb[k]) for k in sa)
+
+
+@pytest.mark.parametrize("freq", [True, False])
+def test_transposed_conv_as_three_tap_phases(freq):
+    """The packed transposed-conv weight, run as a 3-tap conv whose channel group s is
+    output row 4p + s, reproduces ConvTranspose (stride 4, kernel 8, crop 2)."""
+    import torch.nn.functional as F
+
+    from unblend_b200.htdemucs import _convtr_taps3
+
+    g = torch.Generator().manual_seed(3)
+    B, P, Cin, Cout = 2, 9, 5, 3
+    wt, x = torch.randn(Cin, Cout, 8, generator=g, dtype=torch.float64), torch.randn(B, Cin, P, generator=g,
+                                                                                       dtype=torch.float64)
+    w3 = _convtr_taps3(wt if not freq else wt[..., None])  # [4 Cout, 3, Cin]
+    y = F.conv1d(x, w3.permute(0, 2, 1), padding=1)  # [B, 4 Cout, P]
+    got = y.view(B, 4, Cout, P).permute(0, 2, 3, 1).reshape(B, Cout, 4 * P)
+    ref = F.conv_transpose1d(x, wt, stride=4)[:, :, 2:2 + 4 * P]
+    assert torch.allclose(got, ref, atol=1e-12)

@@ -153,29 +153,24 @@ def test_linear_residual_layerscale_with_stats_inplace():
 
 @pytest.mark.parametrize("freq", [True, False])
 def test_transposed_conv_phase_split(freq):
-    from unblend_b200.htdemucs import _convtr_phases
+    from unblend_b200.htdemucs import _convtr_taps3
 
     B, P, T, Cin, Cout = 2, 7, 5, 12, 6
     wt, bias = torch.randn(Cin, Cout, 8) * 0.2, torch.randn(Cout)
-    lo, hi = _convtr_phases(wt)
-    lo, hi, b2 = lo.cuda(), hi.cuda(), bias.repeat(2).cuda()
+    w3, b4 = _convtr_taps3(wt).cuda(), bias.repeat(4).cuda()
     if freq:
         x = _cl((B, P, T, Cin))
         out = torch.empty(B, 4 * P, T, Cout, device="cuda")
         row = T * Cout
-        for wgt, ph, base in ((lo, 1, 0), (hi, 0, 2)):
-            _conv(x, wgt, b2, out.view(-1)[base * row:], B=B, H=P, W=T, C=Cin, in_s=(P * T * Cin, T * Cin, Cin),
-                  Ho=P, Wo=T, N=2 * Cout, out_s=(4 * P * T * Cout, 4 * row, Cout), kh=2, ph=ph, n_group=Cout,
-                  out_sg=row)
+        _conv(x, w3, b4, out.view(-1), B=B, H=P, W=T, C=Cin, in_s=(P * T * Cin, T * Cin, Cin), Ho=P, Wo=T,
+              N=4 * Cout, out_s=(4 * P * T * Cout, 4 * row, Cout), kh=3, ph=1, n_group=Cout, out_sg=row)
         ref = F.conv_transpose2d(x.permute(0, 3, 1, 2), wt[..., None].cuda(), bias.cuda(), (4, 1))
         ref = ref[:, :, 2:-2, :].permute(0, 2, 3, 1)
     else:
         x = _cl((B, P, Cin))
         out = torch.empty(B, 4 * P, Cout, device="cuda")
-        for wgt, pw, base in ((lo, 1, 0), (hi, 0, 2)):
-            _conv(x, wgt, b2, out.view(-1)[base * Cout:], B=B, H=1, W=P, C=Cin, in_s=(P * Cin, P * Cin, Cin),
-                  Ho=1, Wo=P, N=2 * Cout, out_s=(4 * P * Cout, 4 * P * Cout, 4 * Cout), kw=2, pw=pw,
-                  n_group=Cout, out_sg=Cout)
+        _conv(x, w3, b4, out.view(-1), B=B, H=1, W=P, C=Cin, in_s=(P * Cin, P * Cin, Cin), Ho=1, Wo=P,
+              N=4 * Cout, out_s=(4 * P * Cout, 4 * P * Cout, 4 * Cout), kw=3, pw=1, n_group=Cout, out_sg=Cout)
         ref = F.conv_transpose1d(x.permute(0, 2, 1), wt.cuda(), bias.cuda(), 4)[:, :, 2:2 + 4 * P]
         ref = ref.permute(0, 2, 1)
     assert rel_err(out, ref) < TOL
@@ -389,19 +384,17 @@ def test_tc_time_stride4_super_rows(mode):
 
 @pytest.mark.parametrize("mode", MODES)
 def test_tc_transposed_conv_phase_split(mode):
-    from unblend_b200.htdemucs import _convtr_phases
+    from unblend_b200.htdemucs import _convtr_taps3
 
     B, P, T, Cin, Cout = 2, 8, 336, 96, 48
     wt, bias = torch.randn(Cin, Cout, 8) * 0.05, torch.randn(Cout)
-    lo, hi = _convtr_phases(wt)
-    lo, hi, b2 = lo.cuda(), hi.cuda(), bias.repeat(2).cuda()
+    w3, b4 = _convtr_taps3(wt).cuda(), bias.repeat(4).cuda()
     x = _cl((B, P, T, Cin))
     out = torch.empty(B, 4 * P, T, Cout, device="cuda")
     row = T * Cout
-    for wgt, ph, base in ((lo, 1, 0), (hi, 0, 2)):
-        _conv_tc(x, wgt[:, :, None, :], b2, out.view(-1)[base * row:], mode, 128, B=B, H=P, W=T, C=Cin,
-                 in_s=(P * T * Cin, T * Cin, Cin), Ho=P, Wo=T, N=2 * Cout, out_s=(4 * P * T * Cout, 4 * row, Cout),
-                 kh=2, ph=ph, n_group=Cout, out_sg=row, act=ACT_GELU)
+    _conv_tc(x, w3[:, :, None, :], b4, out.view(-1), mode, 192, B=B, H=P, W=T, C=Cin,
+             in_s=(P * T * Cin, T * Cin, Cin), Ho=P, Wo=T, N=4 * Cout, out_s=(4 * P * T * Cout, 4 * row, Cout),
+             kh=3, ph=1, n_group=Cout, out_sg=row, act=ACT_GELU)
     ref = F.conv_transpose2d(x.permute(0, 3, 1, 2), wt[..., None].cuda(), bias.cuda(), (4, 1))
     ref = F.gelu(ref[:, :, 2:-2, :].permute(0, 2, 3, 1))
     assert rel_err(out, ref) < TC_TOL[mode]

@@ -104,22 +104,22 @@ def _conv_w(w: torch.Tensor) -> torch.Tensor:
     return w.permute(0, 2, 3, 1).contiguous()
 
 
-def _convtr_phases(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-    """Split a stride-4, kernel-8 transposed conv into two 2-tap convs.
+def _convtr_taps3(w: torch.Tensor) -> torch.Tensor:
+    """A stride-4, kernel-8 transposed conv as one 3-tap conv with 4 output phases.
 
     ``w`` is [Cin, Cout, 8] (or [Cin, Cout, 8, 1]). After the pad-2 crop, output
-    row 4p+s receives X[p]W[2]+X[p-1]W[6] (s=0), X[p]W[3]+X[p-1]W[7] (s=1),
-    X[p+1]W[0]+X[p]W[4] (s=2), X[p+1]W[1]+X[p]W[5] (s=3). Phases {0,1} read
-    taps (p-1, p) and phases {2,3} read taps (p, p+1). Each returned weight is
-    [2*Cout, 2 taps, Cin] with rows ordered (s, cout).
+    row 4p+s receives X[p-1]W[6] + X[p]W[2] (s=0), X[p-1]W[7] + X[p]W[3] (s=1),
+    X[p]W[4] + X[p+1]W[0] (s=2), X[p]W[5] + X[p+1]W[1] (s=3). The returned weight
+    is [4*Cout, 3 taps (p-1, p, p+1), Cin] with rows ordered (s, cout) and the
+    unused tap of each phase zero, so one launch reads every input row once and
+    writes all four output rows (channel group s at output row offset s).
     """
     if w.dim() == 4:
         w = w[..., 0]
     wk = w.permute(2, 1, 0)  # [8, Cout, Cin]
-    lo = torch.stack([torch.stack([wk[6], wk[2]], 1), torch.stack([wk[7], wk[3]], 1)], 0)
-    hi = torch.stack([torch.stack([wk[4], wk[0]], 1), torch.stack([wk[5], wk[1]], 1)], 0)
-    # [2 phases, Cout, 2 taps, Cin] -> [2*Cout, 2, Cin]
-    return lo.reshape(-1, 2, w.shape[0]).contiguous(), hi.reshape(-1, 2, w.shape[0]).contiguous()
+    z = torch.zeros_like(wk[0])
+    phases = [(wk[6], wk[2], z), (wk[7], wk[3], z), (z, wk[4], wk[0]), (z, wk[5], wk[1])]
+    return torch.stack([torch.stack(t, 1) for t in phases], 0).reshape(-1, 3, w.shape[0]).contiguous()
 
 
 def split_tf32(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
@@ -214,10 +214,8 @@ class HTDemucsCuda(nn.Module):
             for pre in (f"decoder.{idx}", f"tdecoder.{idx}"):
                 self._put(f"{pre}.rewrite.w", _interleave_rows(_conv_w(sd[f"{pre}.rewrite.weight"])))
                 self._put(f"{pre}.rewrite.b", _interleave_rows(sd[f"{pre}.rewrite.bias"]))
-                lo, hi = _convtr_phases(sd[f"{pre}.conv_tr.weight"])
-                self._put(f"{pre}.convtr.lo", lo)
-                self._put(f"{pre}.convtr.hi", hi)
-                self._put(f"{pre}.convtr.b", sd[f"{pre}.conv_tr.bias"].repeat(2))
+                self._put(f"{pre}.convtr.w", _convtr_taps3(sd[f"{pre}.conv_tr.weight"]))
+                self._put(f"{pre}.convtr.b", sd[f"{pre}.conv_tr.bias"].repeat(4))
                 self._pack_dconv(sd, pre)
         if cfg["freq_emb"]:
             self._put("freq_emb", sd["freq_emb.embedding.weight"] * cfg["emb_scale"] * cfg["freq_emb"])
@@ -513,7 +511,7 @@ class HTDemucsCuda(nn.Module):
             self._conv(x, self.w(f"{pre}.rewrite.w"), self.w(f"{pre}.rewrite.b"), y, h_out=1, w_out=x.W,
                        n_out=2 * C, kw=3, pw=1, act=ACT_GLU, **pro)
         self._dconv(y, pre)
-        cout = self._wsel(f"{pre}.convtr.b").shape[0] // 2
+        cout = self._wsel(f"{pre}.convtr.b").shape[0] // 4
         act = ACT_NONE if last else ACT_GELU
         dev = x.t.device
         b = self._wsel(f"{pre}.convtr.b")
@@ -521,22 +519,19 @@ class HTDemucsCuda(nn.Module):
             want = (4 * x.H * x.W * cout, x.W * cout, cout) if freq else (4 * x.W * cout, 4 * x.W * cout, cout)
             assert (next_skip.sb, next_skip.sh, next_skip.sw, next_skip.C) == want + (cout,), \
                 "skip layout differs from the decoder output"
+        w = self._wsel(f"{pre}.convtr.w")
+        res = None if next_skip is None else next_skip.t
+        # One 3-tap launch for the four output phases: channel group s lands at output row 4p + s.
         if freq:
             out = Act.freq(x.B, 4 * x.H, x.W, cout, dev)
             row = out.sh  # stride of one output frequency row
-            for tag, ph, base in (("lo", 1, 0), ("hi", 0, 2)):
-                res = None if next_skip is None else next_skip.t[base * row:]
-                self._conv(y, self._wsel(f"{pre}.convtr.{tag}"), b, out, h_out=x.H, w_out=x.W, n_out=2 * cout,
-                           kh=2, ph=ph, act=act, n_group=cout, out_sg=row, out_offset=base * row,
-                           out_sh=4 * row, res=res)
+            self._conv(y, w, b, out, h_out=x.H, w_out=x.W, n_out=4 * cout, kh=3, ph=1, act=act, n_group=cout,
+                       out_sg=row, out_sh=4 * row, res=res)
         else:
             cap = 4 * x.W
             out = Act.time(x.B, length, cap, cout, dev)
-            for tag, pw, base in (("lo", 1, 0), ("hi", 0, 2)):
-                res = None if next_skip is None else next_skip.t[base * cout:]
-                self._conv(y, self._wsel(f"{pre}.convtr.{tag}"), b, out, h_out=1, w_out=x.W, n_out=2 * cout,
-                           kw=2, pw=pw, act=act, n_group=cout, out_sg=cout, out_offset=base * cout,
-                           out_sw=4 * cout, res=res)
+            self._conv(y, w, b, out, h_out=1, w_out=x.W, n_out=4 * cout, kw=3, pw=1, act=act, n_group=cout,
+                       out_sg=cout, out_sw=4 * cout, res=res)
         return out
 
     def _linear(self, x: torch.Tensor, B: int, L: int, K: int, w: torch.Tensor, b: torch.Tensor | None,
@@ -775,11 +770,10 @@ class HTDemucsCuda(nn.Module):
             last = self.depth - 1
             for pre, per in ((f"decoder.{last}", 4), (f"tdecoder.{last}", 2)):
                 b = self.w(f"{pre}.convtr.b")
-                cout = b.shape[0] // 2
+                cout = b.shape[0] // 4
                 ch = torch.tensor([s * per + k for s in idx for k in range(per)], device=b.device)
-                rows = torch.cat([ch, ch + cout])  # rows are (phase, channel)
-                for tag in ("lo", "hi"):
-                    sel[f"{pre}.convtr.{tag}"] = self.w(f"{pre}.convtr.{tag}")[rows].contiguous()
+                rows = torch.cat([ch + ph * cout for ph in range(4)])  # rows are (phase, channel)
+                sel[f"{pre}.convtr.w"] = self.w(f"{pre}.convtr.w")[rows].contiguous()
                 sel[f"{pre}.convtr.b"] = b[rows].contiguous()
         self.__dict__["_selected"] = sel
         self._tc_cache.clear()
