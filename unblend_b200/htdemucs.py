@@ -167,7 +167,7 @@ class HTDemucsCuda(nn.Module):
         self.precision = precision
         self._tc_cache: dict = {}
         # Output widths from which the 256-column tile is used (per tensor-core mode).
-        self._bn256_min = {_lib.TC_TF32X3: 1 << 30, _lib.TC_BF16: 512}
+        self._bn256_min = {_lib.TC_TF32X3: 512, _lib.TC_BF16: 512}
         cfg = dict(HTDEMUCS_CONFIGS["htdemucs"])
         cfg.update(config)
         if cfg.get("multi_freqs") or not cfg["cac"] or cfg["norm_starts"] < cfg["depth"]:
