@@ -76,17 +76,6 @@ struct AttnArgs {
   float c;  // scale * log2(e)
 };
 
-// D[tmem] (+)= A[tmem] * B[smem], kind::tf32.
-__device__ __forceinline__ void umma_tf32_ts(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc,
-                                             uint32_t accum) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
-      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accum)
-      : "memory");
-}
-
 __device__ __forceinline__ float tf32_round(float v) {
   return __uint_as_float((__float_as_uint(v) + 0x1000u) & 0xFFFFE000u);
 }

@@ -57,20 +57,45 @@ struct TcArgs {
   int tma_store;  // 1: whole 32-column chunks leave through TMA bulk tensor stores (no residual)
 };
 
-// TMEM columns of the double-buffered accumulator: 2 x BN rounded up to a power of two.
-template <int BN>
+// 3-pass TF32 tiles of up to 128 columns keep the A operand in TMEM: the
+// converter warps write the TF32 hi / lo parts of each landed tile there
+// (tcgen05.st) and the MMAs read A from TMEM, which issue faster than MMAs
+// with both operands in shared memory when N <= 128.
+template <int BN, int MODE>
+struct ATmem {
+  static constexpr bool value = MODE == 0 && BN <= 128;
+};
+
+// TMEM columns: the double-buffered accumulator (2 x BN), plus 64 columns
+// (A hi, A lo) per pipeline stage with A in TMEM; rounded up to a power of two.
+template <int BN, int MODE>
 struct TmemCols {
-  static constexpr int value = 2 * BN <= 128 ? 128 : 2 * BN <= 256 ? 256 : 512;
+  static constexpr int used = 2 * BN + (ATmem<BN, MODE>::value ? 4 * 64 : 0);
+  static constexpr int value = used <= 128 ? 128 : used <= 256 ? 256 : 512;
+  static_assert(used <= 512, "TMEM overflow");
+};
+
+// Channels per K chunk: 32 (128-byte fp32 rows, 128-byte swizzle), or 16 for the
+// 3-pass TF32 mode with 256-column tiles, whose 96 KB stages would leave room for
+// only two (64-byte rows, 64-byte swizzle, four stages).
+template <int BN, int MODE>
+struct ChunkK {
+  static constexpr int value = (MODE == 0 && BN == 256) ? 16 : 32;
 };
 
 template <int BN, int MODE>
 struct Layout {
-  static constexpr int A_BYTES = 128 * 128;                          // fp32 staging, 128 rows x 32 K
-  static constexpr int AC_BYTES = MODE == 0 ? 128 * 128 : 128 * 64;   // lo (fp32) or bf16 tile
-  static constexpr int B_BYTES = MODE == 0 ? BN * 128 : BN * 64;      // one weight tile
+  static constexpr int KC = ChunkK<BN, MODE>::value;
+  static constexpr int ROWB = KC * 4;                                 // fp32 bytes per staged row
+  static constexpr int A_BYTES = 128 * ROWB;  // fp32 staging, 128 rows x KC
+  // lo (fp32) or bf16 tile in shared memory; none with A in TMEM
+  static constexpr int AC_BYTES = ATmem<BN, MODE>::value ? 0 : MODE == 0 ? 128 * ROWB : 128 * 64;
+  static constexpr int B_BYTES = MODE == 0 ? BN * ROWB : BN * 64;     // one weight tile
   static constexpr int B_TILES = MODE == 0 ? 2 : 1;                   // hi + lo, or bf16
   static constexpr int STAGE = A_BYTES + AC_BYTES + B_TILES * B_BYTES;
   static constexpr int STAGES = (200 * 1024) / STAGE > 4 ? 4 : (200 * 1024) / STAGE;
+  static constexpr int A_COL = 2 * BN;  // first TMEM column of the A stages (A in TMEM)
+  static_assert(!ATmem<BN, MODE>::value || STAGES == 4, "four A stages in TMEM");
   static constexpr int EPI_BYTES = 4 * 32 * 32 * 4;  // one 32 x 32 fp32 transpose tile per epilogue warp
   static constexpr int SMEM = STAGES * STAGE + EPI_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
@@ -153,7 +178,7 @@ __global__ void __launch_bounds__(NT, 1)
     }
     fence_mbar_init();
   }
-  if (warp == 1) tmem_alloc(tmem_slot, TmemCols<BN>::value);
+  if (warp == 1) tmem_alloc(tmem_slot, TmemCols<BN, MODE>::value);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -162,7 +187,7 @@ __global__ void __launch_bounds__(NT, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      const uint32_t bytes = (uint32_t)(a.m_box * 128 + L::B_TILES * L::B_BYTES);
+      const uint32_t bytes = (uint32_t)(a.m_box * L::ROWB + L::B_TILES * L::B_BYTES);
       int it = 0;
       bool ok = true;
       for (long long t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
@@ -170,7 +195,7 @@ __global__ void __launch_bounds__(NT, 1)
         for (int tap = 0; tap < a.ntaps && ok; ++tap) {
           const int ca = a.tap_c0[tap], wa = c.w0 + a.tap_dw[tap], ha = c.h * a.a_sh + a.tap_dh[tap];
           const int kb = a.tap_k0[tap];
-          for (int cc = 0; cc < a.tap_clen[tap] && ok; cc += 32, ++it) {
+          for (int cc = 0; cc < a.tap_clen[tap] && ok; cc += L::KC, ++it) {
             const int s = it % L::STAGES;
             const int r = it / L::STAGES;
             if (r > 0 && !mbar_wait(&empty[s], (r - 1) & 1)) {
@@ -200,13 +225,13 @@ __global__ void __launch_bounds__(NT, 1)
         }
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(buf * BN);
-        // K steps with real channels in the current chunk: a chunk holds 32 channels
+        // K steps with real channels in the current chunk: a chunk holds KC channels
         // of one tap, and the last chunk of a tap may be partly past c_in (zero fill,
         // e.g. 16 of 32 for 48-channel layers); the MMAs of all-zero steps are skipped.
         int tap = 0, cc = 0;
         for (int kc = 0; kc < nk; ++kc, ++it) {
-          const int valid = min(32, a.tap_clen[tap] - cc);
-          cc += 32;
+          const int valid = min(L::KC, a.tap_clen[tap] - cc);
+          cc += L::KC;
           if (cc >= a.tap_clen[tap]) {
             cc = 0;
             ++tap;
@@ -222,12 +247,24 @@ __global__ void __launch_bounds__(NT, 1)
           const uint32_t sa = smem_u32(st);
           const uint32_t sac = sa + L::A_BYTES;
           const uint32_t sb = sac + L::AC_BYTES;
-          if (MODE == 0) {
+          if (ATmem<BN, MODE>::value) {
+            // A hi / lo of this stage sit in TMEM columns [A_COL + 64 s, + 64).
+            const uint32_t at = tmem + (uint32_t)(L::A_COL + 64 * s);
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              if (j > 0 && 8 * j >= valid) break;  // 8 channels per kind::tf32 step
-              const uint64_t dah = smem_desc(sa + 32 * j, 128), dal = smem_desc(sac + 32 * j, 128);
+              if (j > 0 && 8 * j >= valid) break;
               const uint64_t dbh = smem_desc(sb + 32 * j, 128), dbl = smem_desc(sb + L::B_BYTES + 32 * j, 128);
+              umma_tf32_ts(d, at + 8 * j, dbh, idesc, (kc > 0 || j > 0) ? 1u : 0u);
+              umma_tf32_ts(d, at + 8 * j, dbl, idesc, 1u);
+              umma_tf32_ts(d, at + 32 + 8 * j, dbh, idesc, 1u);
+            }
+          } else if (MODE == 0) {
+#pragma unroll
+            for (int j = 0; j < L::KC / 8; ++j) {
+              if (j > 0 && 8 * j >= valid) break;  // 8 channels per kind::tf32 step
+              const uint64_t dah = smem_desc(sa + 32 * j, L::ROWB), dal = smem_desc(sac + 32 * j, L::ROWB);
+              const uint64_t dbh = smem_desc(sb + 32 * j, L::ROWB);
+              const uint64_t dbl = smem_desc(sb + L::B_BYTES + 32 * j, L::ROWB);
               umma_tf32(d, dah, dbh, idesc, (kc > 0 || j > 0) ? 1u : 0u);
               umma_tf32(d, dah, dbl, idesc, 1u);
               umma_tf32(d, dal, dbh, idesc, 1u);
@@ -261,11 +298,41 @@ __global__ void __launch_bounds__(NT, 1)
           break;
         }
         uint8_t* st = smem + s * L::STAGE;
+        if (ATmem<BN, MODE>::value) {
+          // Thread = tile row (its warp's TMEM lane quarter): the row's 32 fp32
+          // values from the 128-byte swizzled tile, split, stored as 32 hi and
+          // 32 lo columns. The TMA wrote this stage only after the MMAs that read
+          // the stage's previous A columns completed (empty barrier), so the
+          // columns are free.
+          const int quarter = warp & 3;
+          const int row = quarter * 32 + lane;
+          const uint8_t* src = st + row * 128;
+          uint32_t hv[32], lv[32];
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const float4 v = *reinterpret_cast<const float4*>(src + ((c ^ (row & 7)) << 4));
+            const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float h = __uint_as_float((__float_as_uint(e[k]) + 0x1000u) & 0xFFFFE000u);
+              hv[4 * c + k] = __float_as_uint(h);
+              lv[4 * c + k] = __float_as_uint(e[k] - h);
+            }
+          }
+          const uint32_t ta = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(L::A_COL + 64 * s);
+          tmem_st32(ta, hv);
+          tmem_st32(ta + 32, lv);
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&conv[s]);
+          continue;
+        }
         if (MODE == 0) {
           float4* hi = reinterpret_cast<float4*>(st);
           float4* lo = reinterpret_cast<float4*>(st + L::A_BYTES);
 #pragma unroll
-          for (int k = ct; k < 1024; k += 128) {
+          for (int k = ct; k < 128 * L::KC / 4; k += 128) {
             const float4 v = hi[k];
             // hi = v rounded to the nearest TF32 value (ties away from zero), lo = v - hi exactly.
             float4 vh;
@@ -515,7 +582,7 @@ __global__ void __launch_bounds__(NT, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, TmemCols<BN>::value);
+    tmem_dealloc(tmem, TmemCols<BN, MODE>::value);
   }
 }
 
@@ -659,8 +726,10 @@ extern "C" int unblend_conv2d_tc(const float* x, const void* w_hi, const void* w
     }
   }
   a.ntaps = nt;
+  const int kc = (mode == 0 && block_n == 256) ? ChunkK<256, 0>::value : 32;
+  const CUtensorMapSwizzle kc_swizzle = kc == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
   int nch = 0;
-  for (int i = 0; i < nt; ++i) nch += (a.tap_clen[i] + 31) / 32;
+  for (int i = 0; i < nt; ++i) nch += (a.tap_clen[i] + kc - 1) / kc;
   a.nchunks = nch;
   // Rows of one tile: all 128 unless a row of W does not split into 128s
   // (e.g. 336 STFT frames = 3 x 112).
@@ -676,17 +745,17 @@ extern "C" int unblend_conv2d_tc(const float* x, const void* w_hi, const void* w
   a.m_box = m_valid;
   a.tiles_w = (p->w_out + m_valid - 1) / m_valid;
   a.tiles_n = (p->n_out + block_n - 1) / block_n;
-  cuuint32_t boxA[4] = {32, (cuuint32_t)m_valid, 1, 1};
-  if (!make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, dims, strides, boxA, CU_TENSOR_MAP_SWIZZLE_128B))
+  cuuint32_t boxA[4] = {(cuuint32_t)kc, (cuuint32_t)m_valid, 1, 1};
+  if (!make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, dims, strides, boxA, kc_swizzle))
     return UNBLEND_ERR_INVALID;
   // Weights [N, K] (K contiguous): fp32 hi/lo pair or bf16.
   cuuint64_t wd[2] = {(cuuint64_t)K, (cuuint64_t)p->n_out};
   if (mode == 0) {
     cuuint64_t ws[1] = {(cuuint64_t)K * 4};
-    cuuint32_t boxB[2] = {32, (cuuint32_t)block_n};
+    cuuint32_t boxB[2] = {(cuuint32_t)kc, (cuuint32_t)block_n};
     UB_REQUIRE((K * 4) % 16 == 0);
-    if (!make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, w_hi, wd, ws, boxB, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !make_map(&mb2, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, w_lo, wd, ws, boxB, CU_TENSOR_MAP_SWIZZLE_128B))
+    if (!make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, w_hi, wd, ws, boxB, kc_swizzle) ||
+        !make_map(&mb2, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, w_lo, wd, ws, boxB, kc_swizzle))
       return UNBLEND_ERR_INVALID;
   } else {
     cuuint64_t ws[1] = {(cuuint64_t)K * 2};

@@ -123,6 +123,17 @@ __device__ __forceinline__ void umma_tf32(uint32_t d, uint64_t a, uint64_t b, ui
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem], kind::tf32 (A: 128 lanes x K consecutive columns).
+__device__ __forceinline__ void umma_tf32_ts(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                             uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accum)
+      : "memory");
+}
+
 __device__ __forceinline__ void umma_bf16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
