@@ -45,6 +45,11 @@ struct TcArgs {
   int a_sh;
   int ntaps, nchunks;
   int tap_dh[MAXT], tap_dw[MAXT], tap_c0[MAXT], tap_clen[MAXT], tap_k0[MAXT];
+  // Taps that read the same input rows shifted along w share one A load:
+  // sub-tap 1 / 2 of load t use weight K offsets tap_k1/k2 and read the A tile
+  // from row tap_s1/s2 on (sub-tap 0: row 0, offset tap_k0).
+  int tap_n[MAXT], tap_k1[MAXT], tap_k2[MAXT], tap_s1[MAXT], tap_s2[MAXT];
+  int a_rows;  // rows of each A load: m_box plus the largest sub-tap shift
   const float* bias;
   float* y;
   long long out_sb, out_sh, out_sw, out_sg;
@@ -83,16 +88,28 @@ struct ChunkK {
   static constexpr int value = (MODE == 0 && BN == 256) ? 16 : 32;
 };
 
+// Sub-taps per A load: the bf16 mode with tiles of up to 192 columns groups up
+// to three taps along w (a 3-wide kernel row) onto one A load of 128 + 8 rows,
+// each sub-tap's MMAs starting at its shifted row; the input tile then crosses
+// from L2 once per kernel row instead of once per tap.
+template <int BN, int MODE>
+struct SubTaps {
+  static constexpr int value = (MODE == 1 && BN <= 192) ? 3 : 1;
+};
+
 template <int BN, int MODE>
 struct Layout {
   static constexpr int KC = ChunkK<BN, MODE>::value;
+  static constexpr int NSUB = SubTaps<BN, MODE>::value;
+  static constexpr int A_ROWS = NSUB > 1 ? 136 : 128;                 // 128 rows + shift headroom
   static constexpr int ROWB = KC * 4;                                 // fp32 bytes per staged row
-  static constexpr int A_BYTES = 128 * ROWB;  // fp32 staging, 128 rows x KC
-  // lo (fp32) or bf16 tile in shared memory; none with A in TMEM
-  static constexpr int AC_BYTES = ATmem<BN, MODE>::value ? 0 : MODE == 0 ? 128 * ROWB : 128 * 64;
+  static constexpr int A_BYTES = A_ROWS * ROWB;                       // fp32 staging, A_ROWS x KC
+  // lo (fp32) or bf16 tile in shared memory (1 KB aligned); none with A in TMEM
+  static constexpr int AC_BYTES =
+      ATmem<BN, MODE>::value ? 0 : MODE == 0 ? A_ROWS * ROWB : (A_ROWS * 64 + 1023) / 1024 * 1024;
   static constexpr int B_BYTES = MODE == 0 ? BN * ROWB : BN * 64;     // one weight tile
   static constexpr int B_TILES = MODE == 0 ? 2 : 1;                   // hi + lo, or bf16
-  static constexpr int STAGE = A_BYTES + AC_BYTES + B_TILES * B_BYTES;
+  static constexpr int STAGE = A_BYTES + AC_BYTES + NSUB * B_TILES * B_BYTES;
   static constexpr int STAGES = (200 * 1024) / STAGE > 4 ? 4 : (200 * 1024) / STAGE;
   static constexpr int A_COL = 2 * BN;  // first TMEM column of the A stages (A in TMEM)
   static_assert(!ATmem<BN, MODE>::value || STAGES == 4, "four A stages in TMEM");
@@ -187,14 +204,15 @@ __global__ void __launch_bounds__(NT, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      const uint32_t bytes = (uint32_t)(a.m_box * L::ROWB + L::B_TILES * L::B_BYTES);
+      const uint32_t bytes_a = (uint32_t)(a.a_rows * L::ROWB);
       int it = 0;
       bool ok = true;
       for (long long t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
         const TileCoord c = tile_coord<BN>(a, t);
         for (int tap = 0; tap < a.ntaps && ok; ++tap) {
           const int ca = a.tap_c0[tap], wa = c.w0 + a.tap_dw[tap], ha = c.h * a.a_sh + a.tap_dh[tap];
-          const int kb = a.tap_k0[tap];
+          const int kb = a.tap_k0[tap], ns = a.tap_n[tap];
+          const uint32_t bytes = bytes_a + (uint32_t)(ns * L::B_TILES * L::B_BYTES);
           for (int cc = 0; cc < a.tap_clen[tap] && ok; cc += L::KC, ++it) {
             const int s = it % L::STAGES;
             const int r = it / L::STAGES;
@@ -208,6 +226,8 @@ __global__ void __launch_bounds__(NT, 1)
             uint8_t* sb = st + L::A_BYTES + L::AC_BYTES;
             tma_load_2d(sb, &mapB, &full[s], kb + cc, c.n0);
             if (MODE == 0) tma_load_2d(sb + L::B_BYTES, &mapB2, &full[s], kb + cc, c.n0);
+            if (L::NSUB > 1 && ns > 1) tma_load_2d(sb + L::B_BYTES, &mapB, &full[s], a.tap_k1[tap] + cc, c.n0);
+            if (L::NSUB > 2 && ns > 2) tma_load_2d(sb + 2 * L::B_BYTES, &mapB, &full[s], a.tap_k2[tap] + cc, c.n0);
           }
         }
       }
@@ -231,6 +251,7 @@ __global__ void __launch_bounds__(NT, 1)
         int tap = 0, cc = 0;
         for (int kc = 0; kc < nk; ++kc, ++it) {
           const int valid = min(L::KC, a.tap_clen[tap] - cc);
+          const int ctap = tap;
           cc += L::KC;
           if (cc >= a.tap_clen[tap]) {
             cc = 0;
@@ -270,11 +291,19 @@ __global__ void __launch_bounds__(NT, 1)
               umma_tf32(d, dal, dbh, idesc, 1u);
             }
           } else {
+            // Sub-tap u reads the bf16 A tile from row shift_u on (64-byte rows).
+            const int ns = L::NSUB > 1 ? a.tap_n[ctap] : 1;
 #pragma unroll
-            for (int j = 0; j < 2; ++j) {
-              if (j > 0 && 16 * j >= valid) break;  // 16 channels per kind::f16 step
-              const uint64_t da = smem_desc(sac + 32 * j, 64), db = smem_desc(sb + 32 * j, 64);
-              umma_bf16(d, da, db, idesc, (kc > 0 || j > 0) ? 1u : 0u);
+            for (int u = 0; u < L::NSUB; ++u) {
+              if (u >= ns) break;
+              const int shift = u == 0 ? 0 : u == 1 ? a.tap_s1[ctap] : a.tap_s2[ctap];
+              const uint32_t au = sac + (uint32_t)(64 * shift), bu = sb + (uint32_t)(u * L::B_BYTES);
+#pragma unroll
+              for (int j = 0; j < 2; ++j) {
+                if (j > 0 && 16 * j >= valid) break;  // 16 channels per kind::f16 step
+                const uint64_t da = smem_desc(au + 32 * j, 64), db = smem_desc(bu + 32 * j, 64);
+                umma_bf16(d, da, db, idesc, (kc > 0 || j > 0 || u > 0) ? 1u : 0u);
+              }
             }
           }
           umma_commit(&empty[s]);
@@ -347,7 +376,7 @@ __global__ void __launch_bounds__(NT, 1)
           const uint8_t* src = st;
           uint8_t* dst = st + L::A_BYTES;
 #pragma unroll
-          for (int k = ct; k < 1024; k += 128) {
+          for (int k = ct; k < L::A_ROWS * 8; k += 128) {
             const int row = k >> 3, c = k & 7;
             const float4 v = *reinterpret_cast<const float4*>(src + row * 128 + ((c ^ (row & 7)) << 4));
             __nv_bfloat162 p0 = __floats2bfloat162_rn(v.x, v.y);
@@ -677,6 +706,7 @@ extern "C" int unblend_conv2d_tc(const float* x, const void* w_hi, const void* w
   cuuint64_t dims[4];
   cuuint64_t strides[3];
   int kw_taps = p->kw, kh_taps = p->kh;
+  int max_shift = 0;  // largest sub-tap row shift (rows of each A load past the tile's)
   const long long K = (long long)p->kh * p->kw * p->c_in;
   int nt = 0;
   if (p->sw == 1) {
@@ -689,13 +719,26 @@ extern "C" int unblend_conv2d_tc(const float* x, const void* w_hi, const void* w
     strides[2] = (cuuint64_t)p->in_sb * 4;
     a.a_sh = p->sh;
     UB_REQUIRE(kh_taps * kw_taps <= MAXT);
+    // Up to three consecutive taps of a kernel row share one A load when the
+    // kernel groups sub-taps (bf16 mode, tiles up to 192 columns) and their
+    // shifts stay within the 8 rows of headroom.
+    const int nsub = (mode == 1 && block_n <= 192) ? 3 : 1;
     for (int i = 0; i < kh_taps; ++i)
-      for (int j = 0; j < kw_taps; ++j) {
+      for (int j = 0; j < kw_taps;) {
+        int n = kw_taps - j < nsub ? kw_taps - j : nsub;
+        while (n > 1 && (n - 1) * p->dw > 8) --n;
         a.tap_dh[nt] = i * p->dh - p->ph;
         a.tap_dw[nt] = j * p->dw - p->pw;
         a.tap_c0[nt] = 0;
         a.tap_clen[nt] = p->c_in;
-        a.tap_k0[nt] = nt * p->c_in;
+        a.tap_k0[nt] = (i * kw_taps + j) * p->c_in;
+        a.tap_n[nt] = n;
+        a.tap_k1[nt] = (i * kw_taps + j + 1) * p->c_in;
+        a.tap_k2[nt] = (i * kw_taps + j + 2) * p->c_in;
+        a.tap_s1[nt] = p->dw;
+        a.tap_s2[nt] = 2 * p->dw;
+        if ((n - 1) * p->dw > max_shift) max_shift = (n - 1) * p->dw;
+        j += n;
         ++nt;
       }
   } else {
@@ -722,6 +765,7 @@ extern "C" int unblend_conv2d_tc(const float* x, const void* w_hi, const void* w
       a.tap_c0[nt] = c0s[i];
       a.tap_clen[nt] = clen[i];
       a.tap_k0[nt] = k0s[i];
+      a.tap_n[nt] = 1;
       ++nt;
     }
   }
@@ -743,9 +787,11 @@ extern "C" int unblend_conv2d_tc(const float* x, const void* w_hi, const void* w
   }
   a.m_valid = m_valid;
   a.m_box = m_valid;
+  a.a_rows = m_valid + max_shift;
+  UB_REQUIRE(max_shift <= 8);
   a.tiles_w = (p->w_out + m_valid - 1) / m_valid;
   a.tiles_n = (p->n_out + block_n - 1) / block_n;
-  cuuint32_t boxA[4] = {(cuuint32_t)kc, (cuuint32_t)m_valid, 1, 1};
+  cuuint32_t boxA[4] = {(cuuint32_t)kc, (cuuint32_t)a.a_rows, 1, 1};
   if (!make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, dims, strides, boxA, kc_swizzle))
     return UNBLEND_ERR_INVALID;
   // Weights [N, K] (K contiguous): fp32 hi/lo pair or bf16.
