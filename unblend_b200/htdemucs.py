@@ -323,7 +323,8 @@ class HTDemucsCuda(nn.Module):
               pro_stats: torch.Tensor | None = None, pro_gamma=None, pro_beta=None, pro_per_h: int = 0,
               pro_x2: Act | None = None, res: torch.Tensor | None = None, res_scale=None,
               stats: torch.Tensor | None = None, stats_per_h: int = 0, n_group: int | None = None,
-              out_sg: int = 0, out_offset: int = 0, out_sh: int | None = None, out_sw: int | None = None) -> None:
+              out_sg: int = 0, out_offset: int = 0, out_sh: int | None = None, out_sw: int | None = None,
+              useful: float = 1.0) -> None:
         p = ConvParams()
         p.batch, p.h_in, p.w_in, p.c_in = x.B, x.H, x.W, x.C
         p.in_sb, p.in_sh, p.in_sw = x.sb, x.sh, x.sw
@@ -346,7 +347,8 @@ class HTDemucsCuda(nn.Module):
         p.stats = _lib.ptr(stats)
         p.stats_per_h = stats_per_h
         y = out.t.data_ptr() + 4 * out_offset
-        flops = 2.0 * x.B * h_out * w_out * n_out * kh * kw * x.C
+        # Algorithmic FLOPs (``useful``: the fraction of the kernel's taps that are not structural zeros).
+        flops = 2.0 * x.B * h_out * w_out * n_out * kh * kw * x.C * useful
         if self._tc_eligible(x, p, prologue, out_offset):
             if prologue == PRO_ADD:
                 # Fold the decoder skip connection into its input (consumed only here).
@@ -526,12 +528,12 @@ class HTDemucsCuda(nn.Module):
             out = Act.freq(x.B, 4 * x.H, x.W, cout, dev)
             row = out.sh  # stride of one output frequency row
             self._conv(y, w, b, out, h_out=x.H, w_out=x.W, n_out=4 * cout, kh=3, ph=1, act=act, n_group=cout,
-                       out_sg=row, out_sh=4 * row, res=res)
+                       out_sg=row, out_sh=4 * row, res=res, useful=2.0 / 3.0)
         else:
             cap = 4 * x.W
             out = Act.time(x.B, length, cap, cout, dev)
             self._conv(y, w, b, out, h_out=1, w_out=x.W, n_out=4 * cout, kw=3, pw=1, act=act, n_group=cout,
-                       out_sg=cout, out_sw=4 * cout, res=res)
+                       out_sg=cout, out_sw=4 * cout, res=res, useful=2.0 / 3.0)
         return out
 
     def _linear(self, x: torch.Tensor, B: int, L: int, K: int, w: torch.Tensor, b: torch.Tensor | None,
