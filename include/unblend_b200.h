@@ -142,7 +142,9 @@ int unblend_dconv_tail(float* x, const float* z, const float* stats2, const floa
  * z_stats: (sum, sumsq) per group of z = W2 gelu(gn1(h)) + b2 with
  *   st1 = (mean, rstd) of h; W2 [2c, hs] rows interleaved (value, gate).
  * apply: x += scale * glu(gn2(z)) with z recomputed, st2 = (mean, rstd) of z,
- *   GN2 affine interleaved like W2. z is never stored. */
+ *   GN2 affine interleaved like W2. z is never stored. With h_is_act != 0, h
+ *   already holds a = gelu(gn1(h)) rows (written by dconv_moments' a_out;
+ *   st1, g1w, g1b unused and may be null; hid <= 16). */
 int unblend_dconv_conv1(const float* x, long long x_gs, int groups, int rows, int c, const float* w1,
                         const float* b1, int hid, int dil, float* h, double* stats, void* stream);
 int unblend_dconv_z_stats(const float* h, int groups, int rows, int hid, int c, const float* st1,
@@ -151,7 +153,7 @@ int unblend_dconv_z_stats(const float* h, int groups, int rows, int hid, int c, 
 int unblend_dconv_apply(float* x, long long x_gs, const float* h, int groups, int rows, int hid, int c,
                         const float* st1, const float* g1w, const float* g1b, const float* w2,
                         const float* b2, const float* st2, const float* g2w, const float* g2b,
-                        const float* scale, void* stream);
+                        const float* scale, int h_is_act, void* stream);
 
 /* GN2 statistics of the DConv 1x1 output z = W2 a + b2 (a = GELU(GN1(h))) from
  * the moments of a, for the thin levels (hid <= 16):
@@ -164,9 +166,11 @@ int unblend_dconv_apply(float* x, long long x_gs, const float* h, int groups, in
  * unblend_stats_finalize, from coef = [W2^T 1 (hw), W2^T b2 (hw), W2^T W2 as
  * the same packed triangle with off-diagonal entries doubled, sum b2,
  * sum b2^2] (double, over all 2c rows of W2). Replaces unblend_dconv_z_stats
- * at hw + hw(hw+1)/2 instead of 2 c hw operations per row. */
+ * at hw + hw(hw+1)/2 instead of 2 c hw operations per row. a_out (nullable,
+ * 16-byte aligned, may be h itself) receives the rows of a (hs floats each,
+ * zero past hw) for dconv_apply with h_is_act. */
 int unblend_dconv_moments(const float* h, int groups, int rows, int hid, const float* st1, const float* g1w,
-                          const float* g1b, double* moments, void* stream);
+                          const float* g1b, double* moments, float* a_out, void* stream);
 int unblend_dconv_moment_sums(const double* moments, const double* coef, int groups, int rows, int hid,
                               double* sums, void* stream);
 

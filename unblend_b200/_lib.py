@@ -114,7 +114,7 @@ _SIGNATURES = {
     "unblend_dconv_z_stats": [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
                               c_void_p, c_void_p, c_void_p],
     "unblend_dconv_apply": [c_void_p, c_ll, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p,
-                            c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p],
+                            c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p],
     "unblend_attention_tc2": [c_void_p, c_void_p, c_void_p, ctypes.POINTER(AttnParams), c_int, c_void_p],
     "unblend_attention_bf16": [c_void_p, c_void_p, c_void_p, ctypes.POINTER(AttnParams), c_void_p],
     "unblend_gemm_tc": [c_void_p, c_ll, c_int, c_int, c_void_p, c_void_p, c_ll, c_int, ctypes.POINTER(GemmParams),
@@ -131,7 +131,8 @@ _SIGNATURES = {
     "unblend_max_abs": [c_void_p, c_ll, c_void_p, c_void_p],
     "unblend_prevent_clip": [c_void_p, c_void_p, c_ll, c_int, c_void_p, c_void_p],
     "unblend_encode_pcm16": [c_void_p, c_int, c_ll, c_int, c_void_p, c_void_p, c_void_p],
-    "unblend_dconv_moments": [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p],
+    "unblend_dconv_moments": [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                              c_void_p],
     "unblend_dconv_moment_sums": [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p],
     "unblend_scatter_mean_pairs": [c_void_p, c_ll, c_ll, c_void_p, c_void_p, c_int, c_void_p, c_ll, c_void_p],
     "unblend_stft_frames": [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p],
@@ -153,6 +154,21 @@ TC_TF32X3, TC_BF16 = 0, 1
 _lib = None
 
 
+def _check_fresh() -> None:
+    """Refuse a library built from other sources than the ones beside it: its
+    entry points could take other arguments than the signatures declared here."""
+    from .build import DIGEST_NAME, source_digest
+
+    stamp = os.path.join(os.path.dirname(LIB_PATH), DIGEST_NAME)
+    want = source_digest()
+    have = open(stamp).read().strip() if os.path.exists(stamp) else None
+    if have != want:
+        raise RuntimeError(
+            f"unblend_b200 CUDA library {LIB_PATH} was not built from the current sources; "
+            "run `python -m unblend_b200.build`"
+        )
+
+
 def load() -> ctypes.CDLL:
     """Load the shared library (once) and declare every entry point."""
     global _lib
@@ -162,6 +178,7 @@ def load() -> ctypes.CDLL:
         raise RuntimeError(
             f"unblend_b200 CUDA library not built ({LIB_PATH}); run `python -m unblend_b200.build`"
         )
+    _check_fresh()
     lib = ctypes.CDLL(LIB_PATH)
     for name, args in {**_SIGNATURES, **_HOST_SIGNATURES}.items():
         fn = getattr(lib, name)

@@ -553,7 +553,7 @@ __device__ __forceinline__ void bulk_store(void* dst, const void* src, uint32_t 
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
 
-template <int MAXH, int HW>
+template <int MAXH, int HW, bool PRE>
 __global__ void __launch_bounds__(NTH2) dconv_apply4_kernel(float* __restrict__ x, long long x_gs,
                                                             const float* __restrict__ h, int groups, int rows, int H,
                                                             int C, const float* __restrict__ st1,
@@ -631,8 +631,13 @@ __global__ void __launch_bounds__(NTH2) dconv_apply4_kernel(float* __restrict__ 
     ok = wait_phase(&full[b], (k / A4_NB) & 1);
     if (__syncthreads_or(!ok)) break;
     float* xs = dsm + b * (xt + ht);
-    stage_act<MAXH>(xs + xt, nrows, H, st1[2 * g], st1[2 * g + 1], g1w, g1b, a_s);
-    __syncthreads();
+    // PRE: the h rows already hold GELU(GN1(h)) (written by the moments kernel).
+    const float* arow = PRE ? xs + xt : a_s;
+    const int astride = PRE ? H : MAXH;
+    if (!PRE) {
+      stage_act<MAXH>(xs + xt, nrows, H, st1[2 * g], st1[2 * g + 1], g1w, g1b, a_s);
+      __syncthreads();
+    }
     if (live) {
       // GN2 of z = W2 a + b2 folded per item: (z - m2) rstd2 gamma + beta = (W2 a) ga + gc.
       const float m2 = st2[2 * g], rs2 = st2[2 * g + 1];
@@ -644,7 +649,7 @@ __global__ void __launch_bounds__(NTH2) dconv_apply4_kernel(float* __restrict__ 
       }
 #pragma unroll 2
       for (int r = rsub; r < nrows; r += RPP) {
-        const float* a = a_s + r * MAXH;
+        const float* a = arow + r * astride;
         float* xr = xs + r * C + cg * CPT;
         float o[CPT];
 #pragma unroll
@@ -685,11 +690,12 @@ __global__ void __launch_bounds__(NTH2) dconv_apply4_kernel(float* __restrict__ 
 // One warp per item (a group's block of rows), lanes striding its rows; the
 // warp's totals go to the group's moments with double atomics.
 template <int HW>
-__global__ void __launch_bounds__(256) dconv_moments_kernel(const float* __restrict__ h, int groups, int rows,
+__global__ void __launch_bounds__(256) dconv_moments_kernel(const float* h, int groups, int rows,
                                                             int hs, const float* __restrict__ st1,
                                                             const float* __restrict__ g1w,
                                                             const float* __restrict__ g1b,
-                                                            double* __restrict__ mom, int rows_per_item) {
+                                                            double* __restrict__ mom, int rows_per_item,
+                                                            float* a_out) {
   constexpr int NP = HW * (HW + 1) / 2;
   constexpr int K = HW + NP;
   const int lane = threadIdx.x & 31;
@@ -713,21 +719,34 @@ __global__ void __launch_bounds__(256) dconv_moments_kernel(const float* __restr
     for (int r = r0 + lane; r < r1; r += 32) {
       const float* hr = h + ((long long)g * rows + r) * hs;
       float a[HW];
+      // Plain loads: a_out may be h itself (each row is read, then rewritten, by one lane).
 #pragma unroll
       for (int j4 = 0; j4 < HW / 4; ++j4) {
-        const float4 v = __ldg(reinterpret_cast<const float4*>(hr) + j4);
+        const float4 v = reinterpret_cast<const float4*>(hr)[j4];
         a[4 * j4] = v.x;
         a[4 * j4 + 1] = v.y;
         a[4 * j4 + 2] = v.z;
         a[4 * j4 + 3] = v.w;
       }
       if (HW % 4 == 2) {
-        const float2 v = __ldg(reinterpret_cast<const float2*>(hr + HW - 2));
+        const float2 v = *reinterpret_cast<const float2*>(hr + HW - 2);
         a[HW - 2] = v.x;
         a[HW - 1] = v.y;
       }
 #pragma unroll
       for (int j = 0; j < HW; ++j) a[j] = ub::gelu_erf((a[j] - m1) * rs1 * gw[j] + gb[j]);
+      if (a_out) {
+        // The row of activations for the apply kernel, zero past the computed width.
+        float4* ar = reinterpret_cast<float4*>(a_out + ((long long)g * rows + r) * hs);
+#pragma unroll
+        for (int j4 = 0; j4 < (HW + 3) / 4; ++j4) {
+          float v[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) v[e] = 4 * j4 + e < HW ? a[4 * j4 + e] : 0.f;
+          ar[j4] = make_float4(v[0], v[1], v[2], v[3]);
+        }
+        for (int j = 4 * ((HW + 3) / 4); j < hs; ++j) a_out[((long long)g * rows + r) * hs + j] = 0.f;
+      }
 #pragma unroll
       for (int j = 0; j < HW; ++j) acc[j] += a[j];
       int q = HW;
@@ -896,8 +915,8 @@ extern "C" int unblend_dconv_z_stats(const float* h, int groups, int rows, int h
 extern "C" int unblend_dconv_apply(float* x, long long x_gs, const float* h, int groups, int rows, int hid, int c,
                                    const float* st1, const float* g1w, const float* g1b, const float* w2,
                                    const float* b2, const float* st2, const float* g2w, const float* g2b,
-                                   const float* scale, void* stream) {
-  UB_REQUIRE(x && h && st1 && g1w && g1b && w2 && b2 && st2 && g2w && g2b && scale);
+                                   const float* scale, int h_is_act, void* stream) {
+  UB_REQUIRE(x && h && w2 && b2 && st2 && g2w && g2b && scale && (h_is_act || (st1 && g1w && g1b)));
   UB_REQUIRE(groups > 0 && rows > 0 && c > 0 && c % 4 == 0 && hid > 0 && groups < 65536);
   UB_REQUIRE(x_gs >= (long long)rows * c && x_gs % 4 == 0);
   const int hs = padded_hidden(hid);
@@ -910,12 +929,19 @@ extern "C" int unblend_dconv_apply(float* x, long long x_gs, const float* h, int
     const size_t smem4 = sizeof(float) * ((size_t)A4_NB * ir * (c + hs) + (size_t)ir * mh) + 8 * A4_NB;
     UB_REQUIRE(smem4 <= 200 * 1024);
     const long long items = (long long)groups * ((rows + ir - 1) / ir);
-#define UB_AP4(MH, HW)                                                                                          \
+#define UB_AP4K(MH, HW, PRE)                                                                                   \
   {                                                                                                             \
-    cudaFuncSetAttribute(dconv_apply4_kernel<MH, HW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem4); \
-    const unsigned g4 = persistent_grid_smem(dconv_apply4_kernel<MH, HW>, NTH2, smem4, items);                  \
-    dconv_apply4_kernel<MH, HW><<<g4, NTH2, smem4, st>>>(x, x_gs, h, groups, rows, hs, c, st1, g1w, g1b, w2, b2, \
-                                                        st2, g2w, g2b, scale, ir);                              \
+    auto k4 = dconv_apply4_kernel<MH, HW, PRE>;                                                                 \
+    cudaFuncSetAttribute(k4, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem4);                          \
+    const unsigned g4 = persistent_grid_smem(k4, NTH2, smem4, items);                                           \
+    k4<<<g4, NTH2, smem4, st>>>(x, x_gs, h, groups, rows, hs, c, st1, g1w, g1b, w2, b2, st2, g2w, g2b, scale,   \
+                                ir);                                                                            \
+  }
+#define UB_AP4(MH, HW)      \
+  if (h_is_act) {           \
+    UB_AP4K(MH, HW, true)   \
+  } else {                  \
+    UB_AP4K(MH, HW, false)  \
   }
     switch (compute_width(hid)) {
       case 2: UB_AP4(8, 2) break;
@@ -929,9 +955,11 @@ extern "C" int unblend_dconv_apply(float* x, long long x_gs, const float* h, int
       default: return UNBLEND_ERR_INVALID;
     }
 #undef UB_AP4
+#undef UB_AP4K
     UB_CHECK_LAUNCH();
     return 0;
   }
+  UB_REQUIRE(!h_is_act);  // the general kernel recomputes GELU(GN1(h)) itself
   const size_t smem = sizeof(float) * ((size_t)2 * c * hs + 6 * (size_t)c + c);
   UB_REQUIRE(smem <= 220 * 1024);
   dim3 grid((rows + ROWS - 1) / ROWS, groups);
@@ -948,9 +976,10 @@ extern "C" int unblend_dconv_apply(float* x, long long x_gs, const float* h, int
 }
 
 extern "C" int unblend_dconv_moments(const float* h, int groups, int rows, int hid, const float* st1,
-                                     const float* g1w, const float* g1b, double* moments, void* stream) {
+                                     const float* g1w, const float* g1b, double* moments, float* a_out,
+                                     void* stream) {
   UB_REQUIRE(h && st1 && g1w && g1b && moments && groups > 0 && rows > 0 && hid > 0 && hid <= 16);
-  UB_REQUIRE((reinterpret_cast<uintptr_t>(h) & 15) == 0);
+  UB_REQUIRE((reinterpret_cast<uintptr_t>(h) & 15) == 0 && (reinterpret_cast<uintptr_t>(a_out) & 15) == 0);
   const int hs = padded_hidden(hid);
   const int rpi = 512;  // rows per warp item: 16 per lane
   const long long items = (long long)groups * ((rows + rpi - 1) / rpi);
@@ -959,7 +988,7 @@ extern "C" int unblend_dconv_moments(const float* h, int groups, int rows, int h
   const long long cap = 148LL * 8;
   if (blocks > cap) blocks = cap;
   cudaStream_t st = ub::as_stream(stream);
-#define UB_MOM(HW) dconv_moments_kernel<HW><<<(unsigned)blocks, 256, 0, st>>>(h, groups, rows, hs, st1, g1w, g1b, moments, rpi)
+#define UB_MOM(HW) dconv_moments_kernel<HW><<<(unsigned)blocks, 256, 0, st>>>(h, groups, rows, hs, st1, g1w, g1b, moments, rpi, a_out)
   switch (compute_width(hid)) {
     case 2: UB_MOM(2); break;
     case 4: UB_MOM(4); break;

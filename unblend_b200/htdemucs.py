@@ -448,8 +448,9 @@ class HTDemucsCuda(nn.Module):
                 # GN2 statistics from the moments of GELU(GN1(h)): no z at all.
                 hw = _moment_width(hid)
                 mom = torch.zeros(groups * (hw + hw * (hw + 1) // 2), device=dev, dtype=torch.float64)
+                # The moments pass also rewrites h in place as a = GELU(GN1(h)) for the apply pass.
                 _lib.call("unblend_dconv_moments", h.t.data_ptr(), groups, W, hid, s1.data_ptr(),
-                          pw("g1.w").data_ptr(), pw("g1.b").data_ptr(), mom.data_ptr(),
+                          pw("g1.w").data_ptr(), pw("g1.b").data_ptr(), mom.data_ptr(), h.t.data_ptr(),
                           work=1.0 * groups * W * hw * (hw + 3))
                 st2 = torch.empty(2 * groups, device=dev, dtype=torch.float64)
                 _lib.call("unblend_dconv_moment_sums", mom.data_ptr(), getattr(self, _key(f"{q}.mom_coef")).data_ptr(),
@@ -457,7 +458,7 @@ class HTDemucsCuda(nn.Module):
                 s2 = self._stats(st2, groups, W * 2 * C)
                 _lib.call("unblend_dconv_apply", x.t.data_ptr(), x_gs, h.t.data_ptr(), groups, W, hid, C,
                           s1.data_ptr(), *args, s2.data_ptr(), self.w(f"{q}.g2.w").data_ptr(),
-                          self.w(f"{q}.g2.b").data_ptr(), self.w(f"{q}.scale").data_ptr(),
+                          self.w(f"{q}.g2.b").data_ptr(), self.w(f"{q}.scale").data_ptr(), 1,
                           work=4.0 * groups * W * C * hid)
                 continue
             z = Act.freq(B, H, W, 2 * C, dev)
