@@ -348,7 +348,7 @@ def test_tc_freq_encoder_conv_112_row_tiles(mode, block_n):
 
 
 @pytest.mark.parametrize("mode", MODES)
-@pytest.mark.parametrize("block_n", [128, 256])
+@pytest.mark.parametrize("block_n", [128, 192, 256])
 def test_tc_3x3_glu_and_dilated(mode, block_n):
     B, H, W, C, N = 1, 8, 336, 96, 192
     x, w, b = _cl((B, H, W, C)), _cl((N, 3, 3, C)) * 0.03, _cl((N,))

@@ -82,7 +82,8 @@ struct TmemCols {
 
 // Channels per K chunk: 32 (128-byte fp32 rows, 128-byte swizzle), or 16 for the
 // 3-pass TF32 mode with 256-column tiles, whose 96 KB stages would leave room for
-// only two (64-byte rows, 64-byte swizzle, four stages).
+// only two (64-byte rows, 64-byte swizzle, four stages). (192-column tiles keep
+// 32-channel chunks and two stages: 16-channel chunks measured slower there.)
 template <int BN, int MODE>
 struct ChunkK {
   static constexpr int value = (MODE == 0 && BN == 256) ? 16 : 32;
