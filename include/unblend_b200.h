@@ -72,6 +72,11 @@ typedef struct {
   /* statistics epilogue: double[2*groups], group = b*(stats_per_h ? h_out : 1) + ... */
   double* stats;
   int stats_per_h;
+  /* post-activation add (tensor-core kernel only; NULL elsewhere): output channel n'
+   * of output row h gains post[h * post_sh + n'] after the activation / GLU (a
+   * per-(row, channel) table such as HTDemucs' frequency embedding). */
+  const float* post;
+  long long post_sh;
 } UnblendConvParams;
 
 /* Conv1d / Conv2d / Linear (unblend/blocks.py:461,467,695,297,300; torch nn.Linear in

@@ -304,6 +304,8 @@ def _conv_tc(x, w, b, y, mode, block_n, **kw):
     p.act = act
     p.res, p.res_scale = _lib.ptr(kw.get("res")), _lib.ptr(kw.get("res_scale"))
     p.stats, p.stats_per_h = _lib.ptr(kw.get("stats")), kw.get("stats_per_h", 0)
+    if kw.get("post") is not None:
+        p.post, p.post_sh = kw["post"].data_ptr(), kw["post"].shape[1]
     _lib.call("unblend_conv2d_tc", x.data_ptr(), whi.data_ptr(), _lib.ptr(wlo), _lib.ptr(b), y.data_ptr(),
               ctypes.byref(p), mode, block_n)
     torch.cuda.synchronize()
@@ -402,3 +404,22 @@ def test_tc_transposed_conv_phase_split(mode):
     ref = F.conv_transpose2d(x.permute(0, 3, 1, 2), wt[..., None].cuda(), bias.cuda(), (4, 1))
     ref = F.gelu(ref[:, :, 2:-2, :].permute(0, 2, 3, 1))
     assert rel_err(out, ref) < TC_TOL[mode]
+
+
+@pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("with_res", [False, True])
+def test_tc_post_activation_add(mode, with_res):
+    """GLU(conv) + post[h, c] per output row (the frequency-embedding fold), through the
+    bulk-store epilogue (no residual) and the per-lane residual epilogue."""
+    B, H, W, C, N = 2, 6, 336, 48, 96
+    x, w, b = _cl((B, H, W, C)), _cl((N, 1, 1, C)) * 0.1, _cl((N,))
+    post = _cl((H, N // 2))
+    res = _cl((B, H, W, N // 2)) if with_res else None
+    y = res.clone() if with_res else torch.empty(B, H, W, N // 2, device="cuda")
+    _conv_tc(x, w, b, y, mode, 128, B=B, H=H, W=W, C=C, in_s=(H * W * C, W * C, C), Ho=H, Wo=W, N=N,
+             out_s=(H * W * N // 2, W * N // 2, N // 2), act=ACT_GLU, post=post, res=y if with_res else None)
+    z = _ref_conv(x, w, b, 1, 1, 1, 1, 1, 1, 0, 0)
+    ref = z[..., 0::2] * torch.sigmoid(z[..., 1::2]) + post[None, :, None, :]
+    if with_res:
+        ref = ref + res
+    assert rel_err(y, ref) < TC_TOL[mode]

@@ -46,6 +46,7 @@ class ConvParams(ctypes.Structure):
         ("pro_group_per_h", c_int), ("pro_x2", c_void_p),
         ("res", c_void_p), ("res_scale", c_void_p),
         ("stats", c_void_p), ("stats_per_h", c_int),
+        ("post", c_void_p), ("post_sh", c_ll),
     ]
 
 

@@ -60,6 +60,8 @@ struct TcArgs {
   double* stats;
   int stats_per_h;
   int tma_store;  // 1: whole 32-column chunks leave through TMA bulk tensor stores (no residual)
+  const float* post;  // post-activation add: post[h * post_sh + output channel], or null
+  long long post_sh;
 };
 
 // 3-pass TF32 tiles of up to 128 columns keep the A operand in TMEM: the
@@ -447,6 +449,12 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll
             for (int j = 0; j < 16; ++j) v[j] = v[2 * j] * epi_sigmoid<MODE>(v[2 * j + 1]);
           }
+          if (a.post) {
+            const float* pp = a.post + (long long)h * a.post_sh + (glu ? (n0 + c0) / 2 : n0 + c0);
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < nv) v[j] += __ldg(pp + j);
+          }
           if (a.stats && rv) {
             float t1 = 0.f, t2 = 0.f;
 #pragma unroll
@@ -562,6 +570,12 @@ __global__ void __launch_bounds__(NT, 1)
             o[1] = x[1];
             o[2] = x[2];
             o[3] = x[3];
+          }
+          if (a.post) {
+            const float* pp = a.post + (long long)h * a.post_sh + nb;
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              if (e < ocnt) o[e] += __ldg(pp + e);
           }
           if (a.res) {
             o[0] = rv[k].x + sc.x * o[0];
@@ -701,6 +715,8 @@ extern "C" int unblend_conv2d_tc(const float* x, const void* w_hi, const void* w
   a.res_scale = p->res_scale;
   a.stats = p->stats;
   a.stats_per_h = p->stats_per_h;
+  a.post = p->post;
+  a.post_sh = p->post_sh;
 
   // A operand tensor map (C, W, H, B) and the tap table.
   CUtensorMap ma, mb, mb2;

@@ -324,7 +324,7 @@ class HTDemucsCuda(nn.Module):
               pro_x2: Act | None = None, res: torch.Tensor | None = None, res_scale=None,
               stats: torch.Tensor | None = None, stats_per_h: int = 0, n_group: int | None = None,
               out_sg: int = 0, out_offset: int = 0, out_sh: int | None = None, out_sw: int | None = None,
-              useful: float = 1.0) -> None:
+              useful: float = 1.0, post: torch.Tensor | None = None) -> None:
         p = ConvParams()
         p.batch, p.h_in, p.w_in, p.c_in = x.B, x.H, x.W, x.C
         p.in_sb, p.in_sh, p.in_sw = x.sb, x.sh, x.sw
@@ -356,12 +356,20 @@ class HTDemucsCuda(nn.Module):
                           x.t.numel(), 1.0)
                 p.prologue, p.pro_x2 = PRO_NONE, None
             mode = _lib.TC_TF32X3 if self.precision == "fp32" else _lib.TC_BF16
+            if post is not None:
+                # post [h_out, n_final]: added per (output row, channel) after the activation.
+                p.post, p.post_sh = post.data_ptr(), post.shape[1]
             whi, wlo = self._tc_weight(w, mode)
             block_n = _block_n(n_out, self._bn256_min[mode])
             _lib.call("unblend_conv2d_tc", x.t.data_ptr(), whi.data_ptr(), _lib.ptr(wlo), _lib.ptr(b), y,
                       ctypes_byref(p), mode, block_n, work=flops)
             return
         _lib.call("unblend_conv2d_f32", x.t.data_ptr(), w.data_ptr(), _lib.ptr(b), y, ctypes_byref(p), work=flops)
+        if post is not None:
+            # CUDA-core path: the same add as a separate pass over the dense output.
+            assert out_offset == 0 and out.sb == h_out * w_out * n_final and out.sw == n_final
+            table = post[:, None, :].expand(h_out, w_out, n_final).contiguous()
+            _lib.call("unblend_add", y, table.data_ptr(), y, out.B * table.numel(), table.numel(), 1.0)
 
     def _tc_eligible(self, x: Act, p: ConvParams, prologue: int, out_offset: int) -> bool:
         """Whether this convolution meets the tensor-core kernel's layout requirements."""
@@ -491,8 +499,10 @@ class HTDemucsCuda(nn.Module):
             # Rows past the logical length are the zero padding the next
             # stride-4 convolution reads (the reference pads to a multiple of 4).
             out.t.view(out.B, -1, out.C)[:, out.W :].zero_()
+        # The frequency embedding (added to the first frequency layer's output) rides in the rewrite epilogue.
+        post = self.w("freq_emb") if freq and pre == "encoder.0" and "freq_emb" in self.weights else None
         self._conv(y, self.w(f"{pre}.rewrite.w"), self.w(f"{pre}.rewrite.b"), out, h_out=y.H, w_out=y.W,
-                   n_out=2 * cout, act=ACT_GLU)
+                   n_out=2 * cout, act=ACT_GLU, post=post)
         return out
 
     def _dec(self, x: Act, skip: Act, pre: str, freq: bool, last: bool, length: int, skip_in_x: bool = False,
@@ -822,12 +832,7 @@ class HTDemucsCuda(nn.Module):
         for idx in range(self.depth):
             xt = self._enc(xt, f"tencoder.{idx}", False)
             saved_t.append(xt)
-            x = self._enc(x, f"encoder.{idx}", True)
-            if idx == 0 and "freq_emb" in self.weights:
-                emb = self.w("freq_emb")  # [F, C]
-                table = emb[:, None, :].expand(x.H, x.W, x.C).contiguous()
-                _lib.call("unblend_add", x.t.data_ptr(), table.data_ptr(), x.t.data_ptr(), x.t.numel(),
-                          table.numel(), 1.0)
+            x = self._enc(x, f"encoder.{idx}", True)  # encoder.0 adds the frequency embedding
             saved.append(x)
             self._trace_act(f"tenc{idx}", xt)
             self._trace_act(f"enc{idx}", x)
