@@ -77,6 +77,10 @@ typedef struct {
    * per-(row, channel) table such as HTDemucs' frequency embedding). */
   const float* post;
   long long post_sh;
+  /* 1: y is bf16 (round to nearest even), tensor-core kernel only, for outputs that
+   * feed bf16 consumers directly: no GLU, residual or output groups, n_out a multiple
+   * of 32, whole 16-row tiles (the TMA bulk-store epilogue). */
+  int y_bf16;
 } UnblendConvParams;
 
 /* Conv1d / Conv2d / Linear (unblend/blocks.py:461,467,695,297,300; torch nn.Linear in

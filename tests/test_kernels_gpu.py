@@ -306,6 +306,7 @@ def _conv_tc(x, w, b, y, mode, block_n, **kw):
     p.stats, p.stats_per_h = _lib.ptr(kw.get("stats")), kw.get("stats_per_h", 0)
     if kw.get("post") is not None:
         p.post, p.post_sh = kw["post"].data_ptr(), kw["post"].shape[1]
+    p.y_bf16 = 1 if y.dtype == torch.bfloat16 else 0
     _lib.call("unblend_conv2d_tc", x.data_ptr(), whi.data_ptr(), _lib.ptr(wlo), _lib.ptr(b), y.data_ptr(),
               ctypes.byref(p), mode, block_n)
     torch.cuda.synchronize()
@@ -423,3 +424,16 @@ def test_tc_post_activation_add(mode, with_res):
     if with_res:
         ref = ref + res
     assert rel_err(y, ref) < TC_TOL[mode]
+
+
+@pytest.mark.parametrize("block_n", [128, 256])
+def test_tc_bf16_output(block_n):
+    """Linear layer whose output leaves the bulk-store epilogue as bf16 (round to nearest
+    even of the fp32 result), rows not a multiple of 128."""
+    B, L, K, N = 2, 300, 512, 1536
+    x, w, b = _cl((B, L, K)), _cl((N, 1, 1, K)) * 0.05, _cl((N,))
+    y = torch.empty(B, L, N, device="cuda", dtype=torch.bfloat16)
+    _conv_tc(x, w, b, y, _lib.TC_BF16, block_n, B=B, H=1, W=L, C=K, in_s=(L * K, L * K, K), Ho=1, Wo=L, N=N,
+             out_s=(L * N, L * N, N))
+    ref = x @ w[:, 0, 0].t() + b
+    assert rel_err(y.float(), ref) < TC_TOL[_lib.TC_BF16]

@@ -47,6 +47,7 @@ class ConvParams(ctypes.Structure):
         ("res", c_void_p), ("res_scale", c_void_p),
         ("stats", c_void_p), ("stats_per_h", c_int),
         ("post", c_void_p), ("post_sh", c_ll),
+        ("y_bf16", c_int),
     ]
 
 

@@ -281,7 +281,7 @@ __global__ void __launch_bounds__(TH_NT) conv_thin_kernel(ConvArgs a) {
 extern "C" int unblend_conv2d_f32(const float* x, const float* w, const float* bias, float* y,
                                   const UnblendConvParams* p, void* stream) {
   UB_REQUIRE(x && w && y && p);
-  UB_REQUIRE(!p->post);  // the post-activation add is a tensor-core epilogue feature
+  UB_REQUIRE(!p->post && !p->y_bf16);  // tensor-core epilogue features
   UB_REQUIRE(p->batch > 0 && p->h_out > 0 && p->w_out > 0 && p->n_out > 0 && p->c_in > 0);
   UB_REQUIRE(p->kh > 0 && p->kw > 0 && p->sh > 0 && p->sw > 0 && p->dh > 0 && p->dw > 0);
   UB_REQUIRE(p->n_group > 0);

@@ -62,6 +62,7 @@ struct TcArgs {
   int tma_store;  // 1: whole 32-column chunks leave through TMA bulk tensor stores (no residual)
   const float* post;  // post-activation add: post[h * post_sh + output channel], or null
   long long post_sh;
+  int y_bf16;  // 1: bf16 output through the bulk-store epilogue
 };
 
 // 3-pass TF32 tiles of up to 128 columns keep the A operand in TMEM: the
@@ -470,13 +471,27 @@ __global__ void __launch_bounds__(NT, 1)
           uint8_t* stg = reinterpret_cast<uint8_t*>(stage);
           if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
           __syncwarp();
-          const int rb = nv * 4;                      // staging row bytes: 128 or 64
+          const int rb = a.y_bf16 ? 64 : nv * 4;     // staging row bytes: 128 or 64
           const int swz = ((lane * rb) >> 7) & ((rb >> 4) - 1);
+          if (a.y_bf16) {
+            // 32 values -> 16 bf16 pairs, four 16-byte units of a 64-byte row.
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            if (j < (nv >> 2))
-              *reinterpret_cast<float4*>(stg + lane * rb + ((j ^ swz) << 4)) =
-                  make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            for (int j = 0; j < 4; ++j) {
+              uint32_t u[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                __nv_bfloat162 pr = __floats2bfloat162_rn(v[8 * j + 2 * e], v[8 * j + 2 * e + 1]);
+                u[e] = *reinterpret_cast<uint32_t*>(&pr);
+              }
+              *reinterpret_cast<uint4*>(stg + lane * rb + ((j ^ swz) << 4)) = make_uint4(u[0], u[1], u[2], u[3]);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              if (j < (nv >> 2))
+                *reinterpret_cast<float4*>(stg + lane * rb + ((j ^ swz) << 4)) =
+                    make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            }
           }
           fence_proxy_async_smem();
           __syncwarp();
@@ -717,6 +732,9 @@ extern "C" int unblend_conv2d_tc(const float* x, const void* w_hi, const void* w
   a.stats_per_h = p->stats_per_h;
   a.post = p->post;
   a.post_sh = p->post_sh;
+  a.y_bf16 = p->y_bf16 ? 1 : 0;
+  UB_REQUIRE(!a.y_bf16 || (p->act != UNBLEND_ACT_GLU && !p->res && p->n_out % 32 == 0 && p->n_group >= p->n_out &&
+                           p->out_sw % 8 == 0 && p->out_sh % 8 == 0 && p->out_sb % 8 == 0));
 
   // A operand tensor map (C, W, H, B) and the tap table.
   CUtensorMap ma, mb, mb2;
@@ -840,14 +858,16 @@ extern "C" int unblend_conv2d_tc(const float* x, const void* w_hi, const void* w
   // Stores go out in 16-row halves, so a tile's valid rows must be whole halves.
   if (!p->res && p->n_group >= n_final && p->out_sw >= n_final && m_valid % 16 == 0) {
     const int nv = p->act == UNBLEND_ACT_GLU ? 16 : 32;
+    const int es = a.y_bf16 ? 2 : 4;  // output element bytes
     cuuint64_t od[4] = {(cuuint64_t)n_final, (cuuint64_t)p->w_out, (cuuint64_t)p->h_out, (cuuint64_t)p->batch};
-    cuuint64_t os[3] = {(cuuint64_t)p->out_sw * 4, (cuuint64_t)(p->out_sh > 0 ? p->out_sh : p->out_sw) * 4,
-                        (cuuint64_t)(p->out_sb > 0 ? p->out_sb : p->out_sw) * 4};
+    cuuint64_t os[3] = {(cuuint64_t)p->out_sw * es, (cuuint64_t)(p->out_sh > 0 ? p->out_sh : p->out_sw) * es,
+                        (cuuint64_t)(p->out_sb > 0 ? p->out_sb : p->out_sw) * es};
     cuuint32_t ob[4] = {(cuuint32_t)nv, 16, 1, 1};
-    if (make_map(&mo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, y, od, os, ob,
-                 nv == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B))
+    if (make_map(&mo, a.y_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, y, od, os,
+                 ob, nv * es == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B))
       a.tma_store = 1;
   }
+  UB_REQUIRE(!a.y_bf16 || a.tma_store);  // bf16 output only leaves through the bulk stores
   cudaStream_t st = ub::as_stream(stream);
   if (mode == 0) {
     if (block_n == 64) return launch<64, 0>(ma, mb, mb2, mo, a, tiles, st);

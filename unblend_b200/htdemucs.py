@@ -324,7 +324,7 @@ class HTDemucsCuda(nn.Module):
               pro_x2: Act | None = None, res: torch.Tensor | None = None, res_scale=None,
               stats: torch.Tensor | None = None, stats_per_h: int = 0, n_group: int | None = None,
               out_sg: int = 0, out_offset: int = 0, out_sh: int | None = None, out_sw: int | None = None,
-              useful: float = 1.0, post: torch.Tensor | None = None) -> None:
+              useful: float = 1.0, post: torch.Tensor | None = None, y_bf16: bool = False) -> None:
         p = ConvParams()
         p.batch, p.h_in, p.w_in, p.c_in = x.B, x.H, x.W, x.C
         p.in_sb, p.in_sh, p.in_sw = x.sb, x.sh, x.sw
@@ -359,11 +359,13 @@ class HTDemucsCuda(nn.Module):
             if post is not None:
                 # post [h_out, n_final]: added per (output row, channel) after the activation.
                 p.post, p.post_sh = post.data_ptr(), post.shape[1]
+            p.y_bf16 = 1 if y_bf16 else 0
             whi, wlo = self._tc_weight(w, mode)
             block_n = _block_n(n_out, self._bn256_min[mode])
             _lib.call("unblend_conv2d_tc", x.t.data_ptr(), whi.data_ptr(), _lib.ptr(wlo), _lib.ptr(b), y,
                       ctypes_byref(p), mode, block_n, work=flops)
             return
+        assert not y_bf16, "bf16 output needs the tensor-core path"
         _lib.call("unblend_conv2d_f32", x.t.data_ptr(), w.data_ptr(), _lib.ptr(b), y, ctypes_byref(p), work=flops)
         if post is not None:
             # CUDA-core path: the same add as a separate pass over the dense output.
@@ -552,7 +554,8 @@ class HTDemucsCuda(nn.Module):
                 res_scale=None, stats: torch.Tensor | None = None) -> None:
         xa = Act(x, B, 1, L, K, L * K, L * K, K)
         oa = Act(out, B, 1, L, N if act != ACT_GLU else N // 2, L * N, L * N, N)
-        self._conv(xa, w, b, oa, h_out=1, w_out=L, n_out=N, act=act, res=res, res_scale=res_scale, stats=stats)
+        self._conv(xa, w, b, oa, h_out=1, w_out=L, n_out=N, act=act, res=res, res_scale=res_scale, stats=stats,
+                   y_bf16=out.dtype == torch.bfloat16)
 
     def _ln(self, x: torch.Tensor, rows: int, c: int, name: str, pos: torch.Tensor | None = None,
             pos_rows: int = 1) -> torch.Tensor:
@@ -560,6 +563,10 @@ class HTDemucsCuda(nn.Module):
         _lib.call("unblend_layer_norm", x.data_ptr(), y.data_ptr(), self.w(f"{name}.weight").data_ptr(),
                   self.w(f"{name}.bias").data_ptr(), _lib.ptr(pos), 1.0, pos_rows, rows, c)
         return y
+
+    def _attn_bf16(self, hd: int, D: int) -> bool:
+        """Whether a transformer layer's projections go straight to the bf16 attention kernel."""
+        return self.precision == "bf16" and hd == 64 and D % 32 == 0
 
     def _attention(self, qbuf: torch.Tensor, q_off: int, kvbuf: torch.Tensor, k_off: int, v_off: int, o: int,
                    B: int, heads: int, L: int, Lk: int, hd: int, q_sb: int, q_sr: int, kv_sb: int, kv_sr: int,
@@ -573,14 +580,18 @@ class HTDemucsCuda(nn.Module):
         """
         work = 4.0 * B * L * Lk * hd * heads
         scale = 1.0 / math.sqrt(hd)
-        if (self.precision == "bf16" and hd == 64 and o % 16 == 0
-                and all(v % 8 == 0 for v in (q_off, k_off, v_off, q_sb, q_sr, kv_sb, kv_sr, o_sb, o_sr))):
-            qb = torch.empty(qbuf.numel(), device=qbuf.device, dtype=torch.bfloat16)
-            _lib.call("unblend_cast_bf16", qbuf.data_ptr(), qb.data_ptr(), qbuf.numel())
-            kvb = qb
-            if kvbuf is not qbuf:
-                kvb = torch.empty(kvbuf.numel(), device=kvbuf.device, dtype=torch.bfloat16)
-                _lib.call("unblend_cast_bf16", kvbuf.data_ptr(), kvb.data_ptr(), kvbuf.numel())
+        if qbuf.dtype == torch.bfloat16 or (self.precision == "bf16" and hd == 64 and o % 16 == 0 and
+                                            all(v % 8 == 0 for v in (q_off, k_off, v_off, q_sb, q_sr, kv_sb,
+                                                                     kv_sr, o_sb, o_sr))):
+            if qbuf.dtype == torch.bfloat16:  # projections already rounded by their epilogue
+                qb, kvb = qbuf, kvbuf
+            else:
+                qb = torch.empty(qbuf.numel(), device=qbuf.device, dtype=torch.bfloat16)
+                _lib.call("unblend_cast_bf16", qbuf.data_ptr(), qb.data_ptr(), qbuf.numel())
+                kvb = qb
+                if kvbuf is not qbuf:
+                    kvb = torch.empty(kvbuf.numel(), device=kvbuf.device, dtype=torch.bfloat16)
+                    _lib.call("unblend_cast_bf16", kvbuf.data_ptr(), kvb.data_ptr(), kvbuf.numel())
             a = AttnParams()
             a.outer, a.inner, a.heads, a.lq, a.lk, a.hd = B, 1, heads, L, Lk, hd
             a.q_so, a.q_si, a.q_sr = q_sb, 8, q_sr
@@ -608,17 +619,20 @@ class HTDemucsCuda(nn.Module):
         attn = "cross_attn" if cross else "self_attn"
         h = self._ln(x, B * L, D, f"{q}.norm1")
         att = torch.empty(B * L * D, device=dev, dtype=torch.float32)
+        # bf16 precision with 64-dim heads: the projections leave the tensor cores as bf16
+        # for the bf16 attention kernel (no separate rounding pass).
+        pdt = torch.bfloat16 if self._attn_bf16(hd, D) else torch.float32
         if not cross:
             win, bin_ = self.w(f"{q}.{attn}.in_proj_weight"), self.w(f"{q}.{attn}.in_proj_bias")
-            qkv = torch.empty(B * L * 3 * D, device=dev, dtype=torch.float32)
+            qkv = torch.empty(B * L * 3 * D, device=dev, dtype=pdt)
             self._linear(h, B, L, D, win, bin_, qkv, 3 * D)
             self._attention(qkv, 0, qkv, D, 2 * D, att.data_ptr(), B, heads, L, L, hd, L * 3 * D,
                             3 * D, L * 3 * D, 3 * D, L * D, D)
         else:
             kvn = self._ln(kv_src, B * Lk, D, f"{q}.norm2")
-            qp = torch.empty(B * L * D, device=dev, dtype=torch.float32)
+            qp = torch.empty(B * L * D, device=dev, dtype=pdt)
             self._linear(h, B, L, D, self.w(f"{q}.in_q.w"), self.w(f"{q}.in_q.b"), qp, D)
-            kv = torch.empty(B * Lk * 2 * D, device=dev, dtype=torch.float32)
+            kv = torch.empty(B * Lk * 2 * D, device=dev, dtype=pdt)
             self._linear(kvn, B, Lk, D, self.w(f"{q}.in_kv.w"), self.w(f"{q}.in_kv.b"), kv, 2 * D)
             self._attention(qp, 0, kv, 0, D, att.data_ptr(), B, heads, L, Lk, hd, L * D, D,
                             Lk * 2 * D, 2 * D, L * D, D)
