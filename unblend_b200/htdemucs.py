@@ -361,7 +361,11 @@ class HTDemucsCuda(nn.Module):
                 p.post, p.post_sh = post.data_ptr(), post.shape[1]
             p.y_bf16 = 1 if y_bf16 else 0
             whi, wlo = self._tc_weight(w, mode)
-            block_n = _block_n(n_out, self._bn256_min[mode])
+            bn256 = self._bn256_min[mode]
+            if mode == _lib.TC_BF16 and kw == 3 and sw == 1 and dw * 2 <= 8:
+                # 3-wide kernel rows: tiles of <= 192 columns share one A load across the three taps.
+                bn256 = 1 << 30
+            block_n = _block_n(n_out, bn256)
             _lib.call("unblend_conv2d_tc", x.t.data_ptr(), whi.data_ptr(), _lib.ptr(wlo), _lib.ptr(b), y,
                       ctypes_byref(p), mode, block_n, work=flops)
             return
