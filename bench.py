@@ -5,8 +5,13 @@ Metric: audio-seconds separated per second (x realtime), HTDemucs 4-stem
 (registry ``htdemucs`` architecture, random init under seed 0), 44.1 kHz
 stereo, overlap 0.25, segments batched 32 per forward, fp32. One step is one
 pass of ``apply_model`` over one 180 s synthetic track (31 segments). With N
-ranks (torchrun) every rank separates its own 180 s track (seed 1 + rank):
-whole tracks per rank, no data-path collective, weak scaling.
+ranks (torchrun) the one track's segments are sharded across the ranks
+(contiguous count-balanced runs, at most 32 per forward, so ceil(31 / N) per
+rank) and the overlap strips are exchanged with NCCL point-to-point: strong
+scaling on the same 180 s of audio. ``--whole-tracks`` instead gives every rank
+its own tracks (weak scaling, no data-path collective; with ``--tracks 8
+--batch 48 --seconds 240 --precision bf16`` the whole-box sweep's per-rank
+share, tails pooled across the rank's tracks).
 
 * ``value``: track resident in HBM before the timed region; K steps timed with
   CUDA events between barriers; max over ranks.
@@ -17,9 +22,16 @@ whole tracks per rank, no data-path collective, weak scaling.
   against the measured peak in MEASURED_PEAKS.json.
 * ``cpu_baseline``: the CPU oracle (a restatement of the reference's fp32 CPU
   forward) on a bounded 30 s sample, rank 0 at N=1 only.
+* ``split``: (sharded mode) the slowest rank's separation, strip exchange and
+  gather times from one extra step with CUDA events around each phase.
 
-``--impl reference`` times that CPU implementation alone (the reference path
-runs only on host cores; there is no reference GPU kernel to run).
+The forward is replayed from CUDA graphs (``enable_compiled_core``, the
+reference's compiled-core hook) unless ``--no-graphs``; the roofline probe step
+runs the same kernels eagerly so each launch can be timed.
+
+``--impl reference`` times that CPU implementation alone on the same 30 s
+sample (the reference path runs only on host cores; there is no reference GPU
+kernel to run).
 """
 
 from __future__ import annotations
@@ -68,9 +80,11 @@ def _args():
     ap.add_argument("--seconds", type=float, default=None,
                     help="track length per rank (smaller values are for profiling only)")
     ap.add_argument("--batch", type=int, default=None, help="segments per forward")
-    ap.add_argument("--split-track", action="store_true",
-                    help="N>1: all ranks separate the same track, its segments sharded across ranks with the "
-                         "overlap-strip exchange (strong scaling); default: one track per rank (weak scaling)")
+    ap.add_argument("--whole-tracks", action="store_true",
+                    help="N>1: every rank separates its own track(s), no data-path collective (weak scaling); "
+                         "default: one track's segments sharded across the ranks with the overlap-strip exchange "
+                         "(strong scaling)")
+    ap.add_argument("--no-graphs", action="store_true", help="eager launches instead of CUDA-graph replay")
     args = ap.parse_args()
     rof = args.model in ("bsroformer", "melband")
     six = args.model == "htdemucs_6s"
@@ -106,8 +120,10 @@ def _peaks() -> dict:
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
         d = json.load(open(path))
-        return {"hbm": d["hbm_gbs"], "bf16": d["bf16_tflops"], "src": "measured"}
-    return {"hbm": 6650.0, "bf16": 1590.0, "src": "fallback"}
+        return {"hbm": d["hbm_gbs"], "bf16": d.get("bf16_tflops_sustained") or d["bf16_tflops"],
+                "bf16_burst": d["bf16_tflops"], "src": "measured",
+                "kind": "sustained" if d.get("bf16_tflops_sustained") else "burst"}
+    return {"hbm": 6650.0, "bf16": 1400.0, "bf16_burst": 1590.0, "src": "fallback", "kind": "sustained"}
 
 
 def _traffic(key: str, kernel: str):
@@ -226,8 +242,9 @@ def run_reference(args) -> None:
     rof = args.model in ("bsroformer", "melband")
     mel = args.model == "melband"
     vals = []
+    # Each step is one bounded sample, the same one cpu_baseline times in the B200 arm.
     for _ in range(max(1, args.steps)):
-        vals.append(cpu_baseline_roformer(mel=mel) if rof else cpu_baseline(CPU_SAMPLE_SECONDS / 2))
+        vals.append(cpu_baseline_roformer(mel=mel) if rof else cpu_baseline(CPU_SAMPLE_SECONDS))
     v = statistics.median(x["value"] for x in vals)
     base = dict(vals[0])
     base["value"] = v
@@ -284,25 +301,31 @@ def main() -> None:
         seg_len = model.segment_length
     n_stems = len(model.sources)
     seconds, batch, shifts = args.seconds, args.batch, args.shifts
-    split = args.split_track and world > 1
+    split = world > 1 and not args.whole_tracks
     n_tracks = 1 if split else args.tracks
     random.seed(1234 + rank)
-    if args.tracks > 1:
+    if args.tracks > 1 and not split:
         seeds = [100 + rank * args.tracks + i for i in range(args.tracks)]
     else:
         seeds = [1 if split else 1 + rank]
     tracks = [synth_track(seconds, sd) for sd in seeds]
     track = tracks[0]
     tracks_dev = [t.to(dev) for t in tracks]
+    n_seg_track = len(range(0, track.shape[-1], int(0.75 * seg_len)))
+    if split:
+        # A rank's run of the track is at most ceil(n / N) segments: one forward of that many rows.
+        batch = min(batch, -(-n_seg_track // world))
+    if not args.no_graphs:
+        model.enable_compiled_core()
     if split:
         from unblend_b200.distributed import apply_model_sharded
 
         step = lambda: apply_model_sharded(model, tracks_dev[0], chunk_batch_size=batch, shifts=shifts,  # noqa: E731
                                            gather=False)
     else:
-        def step():
-            for td in tracks_dev:
-                apply_model(model, td, chunk_batch_size=batch, shifts=shifts)
+        from unblend_b200.apply import apply_model_multi
+
+        step = lambda: apply_model_multi(model, tracks_dev, chunk_batch_size=batch, shifts=shifts)  # noqa: E731
 
     for _ in range(args.warmup):
         step()
@@ -334,7 +357,7 @@ def main() -> None:
     clk = clocks.stop()
     launches = _lib.counters["launches"] - launches0
 
-    # End to end through the public API with a pinned host track.
+    # End to end through the public API with pinned host tracks.
     hosts = [t.pin_memory() for t in tracks]
     if split:
         def e2e_step():
@@ -342,11 +365,30 @@ def main() -> None:
             apply_model_sharded(model, hosts[0], device=dev, chunk_batch_size=batch, shifts=shifts, gather=True)
     else:
         def e2e_step():
-            for hst in hosts:
-                apply_model(model, hst, device=dev, chunk_batch_size=batch, shifts=shifts)
+            apply_model_multi(model, hosts, device=dev, chunk_batch_size=batch, shifts=shifts)
     e2e_step()
     e2e_ms = timed(e2e_step, max(1, args.steps))
 
+    phases = None
+    if split:
+        # One more step with CUDA events around the separation, strip exchange and gather.
+        marks: list = []
+        apply_model_sharded(model, tracks_dev[0], chunk_batch_size=batch, shifts=shifts, gather=True,
+                            timings=marks)
+        torch.cuda.synchronize()
+        ev = marks[0]
+        ph = torch.tensor([ev["start"].elapsed_time(ev["separated"]), ev["separated"].elapsed_time(ev["exchanged"]),
+                           ev["exchanged"].elapsed_time(ev["gathered"])], device=dev)
+        dist.all_reduce(ph, op=dist.ReduceOp.MAX)
+        from unblend_b200.distributed import shard_plan
+
+        plan = shard_plan(track.shape[-1], seg_len, int(0.75 * seg_len), world)
+        phases = {"segments_per_rank": [len(p.offsets) for p in plan], "forward_rows": batch,
+                  "separate_ms_max": round(float(ph[0]), 3), "strip_exchange_ms_max": round(float(ph[1]), 3),
+                  "gather_ms_max": round(float(ph[2]), 3)}
+
+    if not args.no_graphs:
+        model.disable_compiled_core()
     # Roofline of the dominant kernel: one probed step with events around each launch.
     _lib.probe = []
     step()
@@ -366,7 +408,9 @@ def main() -> None:
                 "unit": "TFLOP/s", "frac": round(tflops / peaks["bf16"], 5),
                 "traffic": _traffic(f"{args.model}:{args.precision}:batch{batch}", top),
                 "traffic_unit": "bytes per launch (ncu capture, see profiles/traffic_per_launch.txt)",
-                "peak_source": f"{peaks['src']} bf16 dense (burst)",
+                "peak_source": f"{peaks['src']} bf16 dense ({peaks['kind']}: the kernel is timed inside a "
+                               "seconds-long run)",
+                "frac_of_burst_peak": round(tflops / peaks["bf16_burst"], 5),
                 "share_of_step": round(a["ms"] / sum(v["ms"] for v in agg.values()), 3),
                 "launches_per_step": a["n"]}
     if args.precision == "fp32":
@@ -402,10 +446,11 @@ def main() -> None:
                        "track_seconds": seconds, "segments_per_launch": batch, "precision": args.precision,
                        "parallelism": (f"one track, segments sharded over {world} ranks + NCCL strip exchange"
                                        if split else f"whole tracks per rank x{world}"),
+                       "launch": "eager" if args.no_graphs else "CUDA-graph replay of the forward",
                        "l2": "inputs and activations far larger than L2 (no flush needed)"},
             "e2e": {"value": round(e2e_value, 3), "unit": "audio-s/s", "h2d_bytes_per_step": n_tracks * 2 * L * 4,
                     "d2h_bytes_per_step": n_tracks * n_stems * 2 * L * 4},
-            "gpu_launches": launches, "roofline": roofline, "clocks": clk,
+            "gpu_launches": launches, "roofline": roofline, "clocks": clk, "split": phases,
             "kernels": {k: {"ms": round(v["ms"], 3), "n": v["n"]} for k, v in sorted(agg.items(), key=lambda kv: -kv[1]["ms"])}}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_roformer(mel=args.model == "melband") if rof else cpu_baseline()

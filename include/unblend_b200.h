@@ -116,6 +116,11 @@ int unblend_stats_finalize(const double* stats, float* out, int groups, double c
 /* Zero a double buffer (statistics accumulators). */
 int unblend_zero_f64(double* p, long long n, void* stream);
 
+/* Zero `count` blocks of n floats starting `stride` floats apart (count 1: one
+ * contiguous run, e.g. overlap-add accumulators; count > 1: padding rows of a
+ * batch of activations, stride >= n). p 4-byte aligned. */
+int unblend_zero_f32(float* p, long long n, int count, long long stride, void* stream);
+
 /* Sum / sum of squares per group of a contiguous [groups, n] fp32 array (double). */
 int unblend_group_sums(const float* x, double* stats, int groups, long long n, void* stream);
 
@@ -138,7 +143,9 @@ int unblend_dconv_tail(float* x, const float* z, const float* stats2, const floa
                        const float* beta, const float* scale, long long groups,
                        long long rows_per_group, int c, long long x_group_stride, void* stream);
 
-/* Fused DConv layer (unblend/blocks.py:238-317) in three streaming passes.
+/* Fused DConv layer (unblend/blocks.py:238-317) in streaming passes: conv1,
+ * then the GN2 statistics from moments (dconv_moments / dconv_moment_sums,
+ * below), then apply.
  * x element (g, r, c) is at x + g*x_gs + r*c_in + c for groups g (GroupNorm
  * groups: (batch, frequency) rows or batch items) and rows r along time.
  * The hidden width hid is padded to hs = round_up(hid, 4): h rows, W1 rows,
@@ -148,17 +155,14 @@ int unblend_dconv_tail(float* x, const float* z, const float* stats2, const floa
  *   padded), W1 [hs, 3, c]; accumulates (sum, sumsq) of h per group into
  *   stats (double, zeroed by the caller). Shared memory must hold
  *   (128 + 2*dil)*(c+4) + 3*hs*c floats (<= 220 KiB).
- * z_stats: (sum, sumsq) per group of z = W2 gelu(gn1(h)) + b2 with
- *   st1 = (mean, rstd) of h; W2 [2c, hs] rows interleaved (value, gate).
- * apply: x += scale * glu(gn2(z)) with z recomputed, st2 = (mean, rstd) of z,
+ * apply: x += scale * glu(gn2(z)) with z = W2 gelu(gn1(h)) + b2 recomputed,
+ *   st1 = (mean, rstd) of h, W2 [2c, hs] rows interleaved (value, gate),
+ *   st2 = (mean, rstd) of z,
  *   GN2 affine interleaved like W2. z is never stored. With h_is_act != 0, h
  *   already holds a = gelu(gn1(h)) rows (written by dconv_moments' a_out;
  *   st1, g1w, g1b unused and may be null; hid <= 16). */
 int unblend_dconv_conv1(const float* x, long long x_gs, int groups, int rows, int c, const float* w1,
                         const float* b1, int hid, int dil, float* h, double* stats, void* stream);
-int unblend_dconv_z_stats(const float* h, int groups, int rows, int hid, int c, const float* st1,
-                          const float* g1w, const float* g1b, const float* w2, const float* b2,
-                          double* stats2, void* stream);
 int unblend_dconv_apply(float* x, long long x_gs, const float* h, int groups, int rows, int hid, int c,
                         const float* st1, const float* g1w, const float* g1b, const float* w2,
                         const float* b2, const float* st2, const float* g2w, const float* g2b,
@@ -174,8 +178,8 @@ int unblend_dconv_apply(float* x, long long x_gs, const float* h, int groups, in
  * dconv_moment_sums turns them into (sum z, sum z^2) per group for
  * unblend_stats_finalize, from coef = [W2^T 1 (hw), W2^T b2 (hw), W2^T W2 as
  * the same packed triangle with off-diagonal entries doubled, sum b2,
- * sum b2^2] (double, over all 2c rows of W2). Replaces unblend_dconv_z_stats
- * at hw + hw(hw+1)/2 instead of 2 c hw operations per row. a_out (nullable,
+ * sum b2^2] (double, over all 2c rows of W2): hw + hw(hw+1)/2 operations per
+ * row instead of the 2 c hw of evaluating z. a_out (nullable,
  * 16-byte aligned, may be h itself) receives the rows of a (hs floats each,
  * zero past hw) for dconv_apply with h_is_act. */
 int unblend_dconv_moments(const float* h, int groups, int rows, int hid, const float* st1, const float* g1w,
@@ -429,6 +433,10 @@ int unblend_istft_masked(const float* stft, const float* mask, long long mask_ss
 int unblend_mean_std(const float* x, double* work, float* out, int batch, long long n,
                      void* stream);
 
+/* Largest batch unblend_mean_std_noalloc takes (its static accumulator holds
+ * 2 doubles per batch item: 64 KiB). */
+#define UNBLEND_NOALLOC_MAX_BATCH 4096
+
 /* unblend_mean_std without the caller-provided `work` buffer. This entry point
  * has no counterpart in the reference; it exists for callers that cannot
  * allocate device memory at call time (a real-time audio thread, where
@@ -438,12 +446,12 @@ int unblend_mean_std(const float* x, double* work, float* out, int batch, long l
  * GPU that loads the library until process exit); larger batches return
  * UNBLEND_ERR_TOO_LARGE. It calls no allocator. The first call on each device
  * looks up the array's device address (cudaGetSymbolAddress) with that device
- * current, so make that first call before any stream capture. All calls share
- * the one array: each call clears the part it uses, and calls that overlap on
- * the GPU (e.g. on two streams at once) race with each other. */
-#define UNBLEND_NOALLOC_MAX_BATCH 4096
-int unblend_mean_std_noalloc(const float* x, float* out, int batch, long long n,
-                     void* stream);
+ * current, so make that first call before any stream capture; the address is
+ * looked up again when the device's current CUDA context changes (after
+ * cudaDeviceReset, or under a context the host created itself). All calls
+ * share the one array: each call clears the part it uses, and calls that
+ * overlap on the GPU (e.g. on two streams at once) race with each other. */
+int unblend_mean_std_noalloc(const float* x, float* out, int batch, long long n, void* stream);
 
 /* Segment engine (unblend/apply.py:278-311, 406-432, 1219-1238, 1329). */
 /* Gather centred, zero-padded chunks: batch[i, c, :] = track[c, start_i ...] for
@@ -453,13 +461,21 @@ int unblend_gather_chunks(const float* track, int channels, long long length, co
                           int n, int segment, float* batch, void* stream);
 
 /* Weighted overlap-add of model outputs y[i, rows, segment] (rows = S*C) into
- * acc[rows, L] and sum_w[L] with the triangular weight (transition power 1),
- * after the centre trim of short chunks. Positions [lo, hi) are visited; they
- * must cover every position the n chunks touch. offsets ascend (as the
- * segment plan produces them). */
+ * acc[rows, L] and sum_w[L] with the triangular weight raised to `power` (the
+ * reference's transition_power, > 0), after the centre trim of short chunks.
+ * Positions [lo, hi) are visited; they must cover every position the n chunks
+ * touch. offsets ascend (as the segment plan produces them). */
 int unblend_overlap_add(const float* y, int n, int rows, int segment, const long long* offsets,
-                        long long length, long long lo, long long hi, float* acc, float* sum_w,
+                        long long length, long long lo, long long hi, float power, float* acc, float* sum_w,
                         void* stream);
+
+/* In place: y[i, r, trim_i + j] *= weight(j)^power for j < len_i, where len_i =
+ * min(L - offsets[i], segment) and trim_i = (segment - len_i) / 2 (the centre
+ * trim). The weighted contributions of a batch for accumulation on the host
+ * when the track's accumulators do not fit the device
+ * (unblend/apply.py:1058-1085, 1211-1238). */
+int unblend_weight_chunks(float* y, int n, int rows, int segment, const long long* offsets, long long length,
+                          float power, void* stream);
 
 /* out = acc / sum_w (broadcast over [S*C, L]). */
 int unblend_divide(const float* acc, const float* sum_w, float* out, int rows, long long length,

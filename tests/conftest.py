@@ -19,6 +19,17 @@ torch.backends.cudnn.allow_tf32 = False
 torch.backends.cuda.matmul.allow_tf32 = False
 
 
+def reference_path() -> str | None:
+    """Checkout of the reference ``unblend`` project for the tests that import it.
+
+    ``UNBLEND_REFERENCE`` names it; without the variable, a ``reference``
+    directory beside this repository is used when present. ``None`` when
+    neither exists (those tests skip).
+    """
+    path = os.environ.get("UNBLEND_REFERENCE") or os.path.join(os.path.dirname(ROOT), "reference")
+    return path if os.path.isdir(os.path.join(path, "unblend")) else None
+
+
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a)")
 

@@ -28,7 +28,7 @@ sys.path.insert(0, os.path.dirname(HERE))
 sys.path.insert(0, HERE)
 sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
 
-from make_golden import import_reference  # noqa: E402
+from make_golden import import_reference, reference_path  # noqa: E402
 from unblend_b200.synth import synth_track  # noqa: E402
 
 
@@ -71,4 +71,4 @@ def main(ref_path: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    main(sys.argv[1] if len(sys.argv) > 1 else reference_path())

@@ -1,9 +1,10 @@
 """Generate the golden fixtures from the reference implementation itself.
 
-Run from the repository root in a container where the reference package is
-mounted (read-only) at ``/root/reference``::
+Run from the repository root with a checkout of the reference project (the
+path argument, else ``$UNBLEND_REFERENCE``, else ``reference`` beside this
+repository)::
 
-    python tests/golden/make_golden.py [/root/reference]
+    python tests/golden/make_golden.py [<reference checkout> [configs|roformer|ensemble|melband]]
 
 It imports the reference (``torchcodec`` is stubbed: the reference only uses it
 for file decode/encode in unblend/api.py:20-21), builds each model exactly as
@@ -38,6 +39,19 @@ bit for bit, and saves the reference's fp32 CPU outputs on synthetic audio:
   (dim 384, depth 6, 60 bands, seed 6) set up by ``configure_inference`` with a
   complement stem, on a 1 s clip: every 5th output sample plus per-stem sums.
 
+``python tests/golden/make_golden.py <reference> configs`` writes the fixtures
+of two measured configurations (their inputs are regenerated from the seed by
+``synth_track``; ``mix_digest`` pins that):
+
+* ``htdemucs_cfg0.pt``    the registry ``htdemucs`` (seed 0) through
+  ``apply_model`` on a 10 s clip (seed 0), batch 1, shifts 0, overlap 0.25:
+  every 16th output sample, full-resolution windows at the start, around both
+  edges of the first chunk overlap and at the end, plus per-stem sums.
+* ``htdemucs_6s_cfg2.pt`` the registry ``htdemucs_6s`` (seed 2) through
+  ``apply_model`` with one shift round (offset drawn after ``random.seed(2)``)
+  on a 16 s clip (seed 4), batch 4: the vocals stem (every 16th sample and the
+  same windows) plus per-stem sums of all six stems.
+
 The fixtures hold only outputs and small inputs; weights are regenerated from
 the seed on the fly, and ``weights_digest`` pins that regeneration.
 """
@@ -68,6 +82,15 @@ from unblend_b200.synth import (  # noqa: E402
 
 SMALL_OVERRIDES = dict(channels=8, bottom_channels=32, t_heads=4, t_layers=3, segment=0.5)
 ROFORMER_SMALL = dict(dim=64, depth=2, heads=4, dim_head=16)
+
+
+def reference_path() -> str:
+    """The reference checkout: ``$UNBLEND_REFERENCE``, else ``reference`` beside this repository."""
+    repo = os.path.dirname(os.path.dirname(HERE))
+    path = os.environ.get("UNBLEND_REFERENCE") or os.path.join(os.path.dirname(repo), "reference")
+    if not os.path.isdir(os.path.join(path, "unblend")):
+        raise SystemExit(f"reference checkout not found at {path}; set UNBLEND_REFERENCE")
+    return path
 
 
 def import_reference(path: str):
@@ -150,6 +173,57 @@ def main(ref_path: str) -> None:
                        os.path.join(HERE, fname))
     main_roformer(unblend)
     print("fixtures written to", HERE)
+
+
+CFG_DECIMATE = 16
+CFG_WINDOW = 2048
+
+
+def config_windows(length: int, segment: int, stride: int) -> list[int]:
+    """Starts of the full-resolution windows: the track start, both edges of the
+    first chunk overlap, and the end."""
+    return [0, stride - CFG_WINDOW // 2, segment - CFG_WINDOW // 2, length - CFG_WINDOW]
+
+
+def _config_record(y: torch.Tensor, windows: list[int]) -> dict:
+    """Decimated output, full-resolution windows and per-stem sums of ``y`` [1, S, C, L]."""
+    return {"decimate": CFG_DECIMATE, "out": y[..., ::CFG_DECIMATE].clone(), "windows": windows,
+            "window": CFG_WINDOW, "win_out": torch.stack([y[..., w:w + CFG_WINDOW] for w in windows]).clone(),
+            **_summary(y)}
+
+
+def mix_digest(x: torch.Tensor) -> str:
+    return hashlib.sha256(x.contiguous().numpy().tobytes()).hexdigest()
+
+
+def main_configs(unblend) -> None:
+    """Fixtures of the 10 s registry clip (configs 0) and the 6-source vocals run with one shift round."""
+    torch.set_num_threads(os.cpu_count() or 1)
+    with torch.inference_mode():
+        cfg = htdemucs_config("htdemucs")
+        model, digest = build_reference(unblend, cfg, 0)
+        mix = synth_track(10.0, 0)[None]
+        y = unblend.apply.apply_model(model, mix, device="cpu", shifts=0, overlap=0.25, chunk_batch_size=1)
+        seg = int(round(cfg["samplerate"] * cfg["segment"]))
+        win = config_windows(mix.shape[-1], seg, int(0.75 * seg))
+        torch.save({"config": cfg, "seed": 0, "weights_digest": digest, "mix_seconds": 10.0, "mix_seed": 0,
+                    "mix_digest": mix_digest(mix), "overlap": 0.25, "chunk_batch_size": 1, "shifts": 0,
+                    **_config_record(y, win)}, os.path.join(HERE, "htdemucs_cfg0.pt"))
+
+        cfg = htdemucs_config("htdemucs_6s")
+        model, digest = build_reference(unblend, cfg, 2)
+        mix = synth_track(16.0, 4)[None]
+        random.seed(2)
+        offsets = [random.randint(0, int(0.5 * cfg["samplerate"]))]
+        random.seed(2)
+        y = unblend.apply.apply_model(model, mix, device="cpu", shifts=1, overlap=0.25, chunk_batch_size=4)
+        v = cfg["sources"].index("vocals")
+        rec = _config_record(y[:, v:v + 1], win)
+        rec["stem_sum"], rec["stem_sumsq"] = _summary(y)["sum"], _summary(y)["sumsq"]
+        torch.save({"config": cfg, "seed": 2, "weights_digest": digest, "mix_seconds": 16.0, "mix_seed": 4,
+                    "mix_digest": mix_digest(mix), "overlap": 0.25, "chunk_batch_size": 4, "shifts": 1,
+                    "offsets": offsets, "stem": "vocals", **rec}, os.path.join(HERE, "htdemucs_6s_cfg2.pt"))
+    print("config fixtures written to", HERE)
 
 
 def build_roformer(unblend, cfg: dict, seed: int):
@@ -256,11 +330,13 @@ def main_melband(unblend) -> None:
 
 
 if __name__ == "__main__":
-    if len(sys.argv) > 2 and sys.argv[2] == "ensemble":
+    if len(sys.argv) > 2 and sys.argv[2] == "configs":
+        main_configs(import_reference(sys.argv[1]))
+    elif len(sys.argv) > 2 and sys.argv[2] == "ensemble":
         main_ensemble(import_reference(sys.argv[1]))
     elif len(sys.argv) > 2 and sys.argv[2] == "melband":
         main_melband(import_reference(sys.argv[1]))
     elif len(sys.argv) > 2 and sys.argv[2] == "roformer":
         main_roformer(import_reference(sys.argv[1]))
     else:
-        main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+        main(sys.argv[1] if len(sys.argv) > 1 else reference_path())

@@ -3,19 +3,18 @@ module, rejected configurations and argument validation of the segment engine.""
 
 from __future__ import annotations
 
-import os
 import sys
 
 import pytest
 import torch
 
-from conftest import GOLDEN
+from conftest import GOLDEN, reference_path
 from unblend_b200.apply import ValidationError, apply_model
 from unblend_b200.htdemucs import HTDemucsCuda, split_tf32
 from unblend_b200.synth import htdemucs_config, htdemucs_state_dict
 
 SMALL = dict(channels=8, bottom_channels=32, t_heads=4, t_layers=3, segment=0.5)
-REF = "/root/reference"
+REF = reference_path()
 
 
 def test_packed_weights_cover_contract_and_split_is_exact():
@@ -45,12 +44,12 @@ def test_segment_engine_validates_arguments():
     with pytest.raises(ValidationError):
         apply_model(m, torch.zeros(2, 100), overlap=1.0)
     with pytest.raises(ValidationError):
-        apply_model(m, torch.zeros(2, 100), transition_power=2.0)
+        apply_model(m, torch.zeros(2, 100), transition_power=0.5)
     with pytest.raises(ValidationError):
         apply_model(m, torch.zeros(2, 100), chunk_batch_size=0)
 
 
-@pytest.mark.skipif(not os.path.isdir(REF), reason="reference package not mounted")
+@pytest.mark.skipif(REF is None, reason="reference checkout not found (set UNBLEND_REFERENCE)")
 def test_from_reference_module_matches_direct_construction():
     sys.path.insert(0, GOLDEN)
     from make_golden import import_reference

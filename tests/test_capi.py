@@ -74,3 +74,9 @@ def test_error_codes_raise():
         _lib.check("unblend_x", _lib.ERR_INVALID)
     with pytest.raises(RuntimeError, match="CUDA out of memory"):
         _lib.check("unblend_x", 2)
+
+
+def test_noalloc_capacity_matches_header():
+    text = open(HEADER).read()
+    m = re.search(r"^#define\s+UNBLEND_NOALLOC_MAX_BATCH\s+(\d+)", text, flags=re.M)
+    assert m and int(m.group(1)) == _lib.NOALLOC_MAX_BATCH

@@ -267,7 +267,7 @@ def test_segment_engine_pointwise_model():
         y = torch.stack([batch, 2 * batch], 1).contiguous()  # [n, S=2, C, seg]
         hi = min(L, grp[-1] + seg)
         _lib.call("unblend_overlap_add", y.data_ptr(), len(grp), 2 * C, seg, off_t.data_ptr(), L, grp[0], hi,
-                  acc.data_ptr(), sw.data_ptr())
+                  1.0, acc.data_ptr(), sw.data_ptr())
     out = torch.empty_like(acc)
     _lib.call("unblend_divide", acc.data_ptr(), sw.data_ptr(), out.data_ptr(), 2 * C, L)
     ref = apply_unshifted(lambda b: torch.stack([b, 2 * b], 1), track.cpu()[None], 2, seg, 0.25, 3)

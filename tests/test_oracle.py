@@ -101,3 +101,43 @@ def test_oracle_rejects_too_long():
     cfg = htdemucs_config("htdemucs", channels=8, bottom_channels=32, t_heads=4, t_layers=1, segment=0.5)
     with pytest.raises(ValueError):
         htdemucs_forward(htdemucs_state_dict(cfg, 0), torch.zeros(1, 2, 22051), cfg)
+
+
+def _config_fixture(fname: str):
+    """A measured-configuration fixture, its regenerated input (digest-checked) and weights."""
+    g = golden(fname)
+    mix = synth_track(g["mix_seconds"], g["mix_seed"])[None]
+    assert hashlib.sha256(mix.contiguous().numpy().tobytes()).hexdigest() == g["mix_digest"]
+    sd = htdemucs_state_dict(g["config"], g["seed"])
+    assert _digest(sd) == g["weights_digest"]
+    return g, mix, sd
+
+
+def check_config_record(out: torch.Tensor, g: dict, tol: float) -> None:
+    """``out`` [1, S, C, L] against a fixture's decimated samples, full windows and per-stem sums."""
+    w = g["window"]
+    assert rel_err(out[..., :: g["decimate"]], g["out"]) < tol
+    wins = torch.stack([out[..., s:s + w] for s in g["windows"]])
+    assert rel_err(wins, g["win_out"]) < tol
+    assert torch.allclose(out.double().sum(dim=(0, 2, 3)), g["sum"], rtol=1e-4, atol=1e-2)
+    assert torch.allclose(out.double().pow(2).sum(dim=(0, 2, 3)), g["sumsq"], rtol=1e-4)
+
+
+def test_oracle_config0_ten_second_clip():
+    """The registry htdemucs on the 10 s seed-0 clip through apply_model, batch 1 (configs 0)."""
+    g, mix, sd = _config_fixture("htdemucs_cfg0.pt")
+    cfg = g["config"]
+    out = apply_model(lambda b: htdemucs_forward(sd, b, cfg), mix, 4, segment_length(cfg), cfg["samplerate"],
+                      overlap=g["overlap"], chunk_batch_size=g["chunk_batch_size"])
+    check_config_record(out, g, TOL)
+
+
+def test_oracle_config2_six_source_vocals_one_shift():
+    """htdemucs_6s (seed 2) with one shift round drawn after random.seed(2); the vocals stem."""
+    g, mix, sd = _config_fixture("htdemucs_6s_cfg2.pt")
+    cfg = g["config"]
+    out = apply_model(lambda b: htdemucs_forward(sd, b, cfg), mix, 6, segment_length(cfg), cfg["samplerate"],
+                      shifts=1, overlap=g["overlap"], chunk_batch_size=g["chunk_batch_size"], offsets=g["offsets"])
+    v = cfg["sources"].index(g["stem"])
+    check_config_record(out[:, v:v + 1], g, TOL)
+    assert torch.allclose(out.double().pow(2).sum(dim=(0, 2, 3)), g["stem_sumsq"], rtol=1e-4)

@@ -24,15 +24,15 @@ pytestmark = pytest.mark.gpu
 
 def _with_buffer(x: torch.Tensor) -> torch.Tensor:
     batch, n = x.shape
-    work = torch.empty(2 * batch, device="cuda", dtype=torch.float64)
-    out = torch.empty(2 * batch, device="cuda")
+    work = torch.empty(2 * batch, device=x.device, dtype=torch.float64)
+    out = torch.empty(2 * batch, device=x.device)
     _lib.call("unblend_mean_std", x.data_ptr(), work.data_ptr(), out.data_ptr(), batch, n)
     return out
 
 
 def _no_alloc(x: torch.Tensor) -> torch.Tensor:
     batch, n = x.shape
-    out = torch.empty(2 * batch, device="cuda")
+    out = torch.empty(2 * batch, device=x.device)
     _lib.call("unblend_mean_std_noalloc", x.data_ptr(), out.data_ptr(), batch, n)
     return out
 
@@ -57,3 +57,16 @@ def test_no_alloc_rejects_batches_beyond_capacity():
     out = torch.empty(2 * x.shape[0], device="cuda")
     with pytest.raises(RuntimeError, match="fixed built-in capacity"):
         _lib.call("unblend_mean_std_noalloc", x.data_ptr(), out.data_ptr(), x.shape[0], 2)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_no_alloc_on_a_second_device():
+    # The array's address is resolved per device: device 1 after device 0, one stream each.
+    for dev in (0, 1):
+        with torch.cuda.device(dev):
+            g = torch.Generator(device=f"cuda:{dev}").manual_seed(5 + dev)
+            x = torch.randn(5, 40_001, device=f"cuda:{dev}", generator=g) + dev
+            got = _no_alloc(x)
+            want = _with_buffer(x)
+            torch.cuda.synchronize(dev)
+            assert torch.allclose(got, want, rtol=1e-6, atol=1e-7), (dev, got, want)

@@ -86,6 +86,7 @@ _SIGNATURES = {
     "unblend_conv2d_f32": [c_void_p, c_void_p, c_void_p, c_void_p, ctypes.POINTER(ConvParams), c_void_p],
     "unblend_stats_finalize": [c_void_p, c_void_p, c_int, c_double, c_float, c_int, c_int, c_void_p],
     "unblend_zero_f64": [c_void_p, c_ll, c_void_p],
+    "unblend_zero_f32": [c_void_p, c_ll, c_int, c_ll, c_void_p],
     "unblend_group_sums": [c_void_p, c_void_p, c_int, c_ll, c_void_p],
     "unblend_group_norm_apply": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_ll, c_int, c_ll, c_int,
                                  c_void_p],
@@ -104,8 +105,9 @@ _SIGNATURES = {
     "unblend_mean_std": [c_void_p, c_void_p, c_void_p, c_int, c_ll, c_void_p],
     "unblend_mean_std_noalloc": [c_void_p, c_void_p, c_int, c_ll, c_void_p],
     "unblend_gather_chunks": [c_void_p, c_int, c_ll, c_void_p, c_int, c_int, c_void_p, c_void_p],
-    "unblend_overlap_add": [c_void_p, c_int, c_int, c_int, c_void_p, c_ll, c_ll, c_ll, c_void_p, c_void_p,
-                            c_void_p],
+    "unblend_overlap_add": [c_void_p, c_int, c_int, c_int, c_void_p, c_ll, c_ll, c_ll, c_float, c_void_p,
+                            c_void_p, c_void_p],
+    "unblend_weight_chunks": [c_void_p, c_int, c_int, c_int, c_void_p, c_ll, c_float, c_void_p],
     "unblend_divide": [c_void_p, c_void_p, c_void_p, c_int, c_ll, c_void_p],
     "unblend_conv2d_tc": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, ctypes.POINTER(ConvParams), c_int,
                           c_int, c_void_p],
@@ -113,8 +115,6 @@ _SIGNATURES = {
                              c_ll, c_ll, c_ll, c_ll, c_float, c_int, c_void_p],
     "unblend_dconv_conv1": [c_void_p, c_ll, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_int, c_void_p,
                             c_void_p, c_void_p],
-    "unblend_dconv_z_stats": [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
-                              c_void_p, c_void_p, c_void_p],
     "unblend_dconv_apply": [c_void_p, c_ll, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p,
                             c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p],
     "unblend_attention_tc2": [c_void_p, c_void_p, c_void_p, ctypes.POINTER(AttnParams), c_int, c_void_p],

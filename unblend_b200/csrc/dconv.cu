@@ -4,10 +4,14 @@
 // with GroupNorm(1) statistics per group (a (batch, frequency) row of the
 // frequency branch, or a batch item of the time branch). The hidden width is
 // C/8, so both contractions are far too thin for tensor cores to pay; the
-// cost is moving x. Three kernels:
-//   dconv_conv1   h = conv_k3_dil(x) with GN1 sums (x tile + weights in smem)
-//   dconv_z_stats GN2 sums of z = W2 * GELU(GN1(h)) + b2, z never stored
-//   dconv_apply   recompute z, x += scale * GLU(GN2(z)) in place
+// cost is moving x. The kernels:
+//   dconv_conv1        h = conv_k3_dil(x) with GN1 sums (x rows + weights in smem;
+//                      conv1b: register-blocked, every hidden output of 3 rows per lane)
+//   dconv_moments      a = GELU(GN1(h)) written over h, with the sums of a and of
+//                      a a^T per group
+//   dconv_moment_sums  GN2 statistics of z = W2 a + b2 from those moments and the
+//                      float64 coefficients W2^T 1, W2^T b2, W2^T W2 (z never exists)
+//   dconv_apply        recompute z from a, x += scale * GLU(GN2(z)) in place
 // x element (g, r, c) is at x + g * x_gs + r * C + c; h is contiguous
 // [groups, rows, H]. W1 is [H, 3, C]; W2 is [2C, H] with rows interleaved as
 // (value 0, gate 0, value 1, gate 1, ...), GN2 affine in the same order.
@@ -113,51 +117,6 @@ __device__ __forceinline__ float dot_row(const float* __restrict__ wrow, const f
 }
 
 template <int MAXH>
-__global__ void __launch_bounds__(ROWS) dconv_z_stats_kernel(const float* __restrict__ h, int rows, int H, int C,
-                                                             const float* __restrict__ st1,
-                                                             const float* __restrict__ g1w,
-                                                             const float* __restrict__ g1b,
-                                                             const float* __restrict__ w2,
-                                                             const float* __restrict__ b2,
-                                                             double* __restrict__ stats2) {
-  extern __shared__ __align__(16) float sm[];
-  float* ws = sm;  // [2C][H]
-  float* bs = sm + 2 * C * H;
-  for (int i = threadIdx.x; i < 2 * C * H; i += ROWS) ws[i] = w2[i];
-  for (int i = threadIdx.x; i < 2 * C; i += ROWS) bs[i] = b2[i];
-  __syncthreads();
-  const int g = blockIdx.y;
-  const int r = blockIdx.x * ROWS + threadIdx.x;
-  float s1 = 0.f, s2 = 0.f;
-  if (r < rows) {
-    float a[MAXH];
-    load_act<MAXH>(h + ((long long)g * rows + r) * H, H, st1[2 * g], st1[2 * g + 1], g1w, g1b, a);
-    for (int n = 0; n < 2 * C; ++n) {
-      const float z = dot_row<MAXH>(ws + n * H, a, H, bs[n]);
-      s1 += z;
-      s2 += z * z;
-    }
-  }
-  s1 = ub::warp_sum(s1);
-  s2 = ub::warp_sum(s2);
-  __shared__ float red[2][ROWS / 32];
-  if ((threadIdx.x & 31) == 0) {
-    red[0][threadIdx.x >> 5] = s1;
-    red[1][threadIdx.x >> 5] = s2;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    double a0 = 0, a1 = 0;
-    for (int i = 0; i < ROWS / 32; ++i) {
-      a0 += red[0][i];
-      a1 += red[1][i];
-    }
-    atomicAdd(stats2 + 2 * g, a0);
-    atomicAdd(stats2 + 2 * g + 1, a1);
-  }
-}
-
-template <int MAXH>
 __global__ void __launch_bounds__(ROWS) dconv_apply_kernel(float* __restrict__ x, long long x_gs,
                                                            const float* __restrict__ h, int rows, int H, int C,
                                                            const float* __restrict__ st1,
@@ -211,14 +170,14 @@ __global__ void __launch_bounds__(ROWS) dconv_apply_kernel(float* __restrict__ x
 }
 
 // ---------------------------------------------------------------------------
-// Persistent, channel-blocked z_stats for the thin DConv levels (hidden
-// width <= 16, padded to a multiple of 4 by the caller so h rows are 16-byte
+// Persistent, channel-blocked passes over the thin DConv levels (hidden width
+// <= 16, padded to a multiple of 4 by the caller so h rows are 16-byte
 // aligned). A CTA walks work items (group, block of IROWS rows) in a
-// grid-stride loop with the h rows of the next NBUF-1 items already in flight
+// grid-stride loop with the rows of the next NBUF-1 items already in flight
 // (bulk async copies into a shared-memory ring). Thread t keeps the W2 rows of
 // its CPT output channels (value and gate rows) in registers for the whole
-// kernel and walks rows t / CG, t / CG + RPP, ... of each item; GELU(GN1(h))
-// of the item's rows is staged in shared memory (a broadcast read feeding
+// kernel and walks rows t / CG, t / CG + RPP, ... of each item; the item's
+// activations a = GELU(GN1(h)) sit in shared memory (a broadcast read feeding
 // 2*CPT dot products).
 constexpr int CPT = 2;      // output channels per thread
 constexpr int NTH2 = 256;   // threads per CTA (CG * RPP <= NTH2)
@@ -301,86 +260,6 @@ __device__ __forceinline__ void load_w(const float* __restrict__ w2, const float
 
 static __device__ int g_dconv_error = 0;
 
-template <int MAXH, int HW>
-__global__ void __launch_bounds__(NTH2) dconv_z_stats3_kernel(const float* __restrict__ h, int groups, int rows, int H,
-                                                               int C, const float* __restrict__ st1,
-                                                               const float* __restrict__ g1w,
-                                                               const float* __restrict__ g1b,
-                                                               const float* __restrict__ w2,
-                                                               const float* __restrict__ b2,
-                                                               double* __restrict__ stats2) {
-  __shared__ __align__(128) float hbuf[NBUF][IROWS * MAXH];
-  __shared__ __align__(16) float a_s[IROWS * MAXH];
-  __shared__ double red[2][NTH2 / 32];
-  __shared__ __align__(8) uint64_t full[NBUF];
-  const int CG = C / CPT;
-  const int RPP = blockDim.x / CG;
-  const int cg = threadIdx.x % CG, rsub = threadIdx.x / CG;
-  const bool live = rsub < RPP;
-  float w[2 * CPT][MAXH], bz[2 * CPT];
-  load_w<MAXH>(w2, b2, H, cg, live, w, bz);
-  const int nblk = (rows + IROWS - 1) / IROWS;
-  const long long items = (long long)groups * nblk;
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < NBUF; ++i)
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(sm_u32(&full[i])) : "memory");
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  __syncthreads();
-  auto issue = [&](long long it, int buf) {
-    const int g = (int)(it / nblk);
-    const int r0 = (int)(it - (long long)g * nblk) * IROWS;
-    const int nr = min(IROWS, rows - r0);
-    bulk_load(hbuf[buf], h + ((long long)g * rows + r0) * H, (uint32_t)(nr * H * 4), &full[buf]);
-  };
-  if (threadIdx.x == 0)
-    for (int i = 0; i < NBUF - 1 && blockIdx.x + (long long)i * gridDim.x < items; ++i)
-      issue(blockIdx.x + (long long)i * gridDim.x, i);
-  bool ok = true;
-  int k = 0;
-  for (long long it = blockIdx.x; it < items; it += gridDim.x, ++k) {
-    const int b = k % NBUF;
-    const int g = (int)(it / nblk);
-    const int r0 = (int)(it - (long long)g * nblk) * IROWS;
-    const int nrows = min(IROWS, rows - r0);
-    // Buffer (k + NBUF - 1) % NBUF was last read by the previous item's
-    // staging, which finished before that item's second barrier.
-    const long long ahead = it + (long long)(NBUF - 1) * gridDim.x;
-    if (threadIdx.x == 0 && ahead < items) issue(ahead, (k + NBUF - 1) % NBUF);
-    ok = wait_phase(&full[b], (k / NBUF) & 1);
-    if (__syncthreads_or(!ok)) break;
-    stage_act<MAXH>(hbuf[b], nrows, H, st1[2 * g], st1[2 * g + 1], g1w, g1b, a_s);
-    __syncthreads();
-    float s1 = 0.f, s2 = 0.f;
-    if (live) {
-      for (int r = rsub; r < nrows; r += RPP) {
-        const float* a = a_s + r * MAXH;
-#pragma unroll
-        for (int q = 0; q < 2 * CPT; ++q) {
-          const float z = dot_a<MAXH, HW>(a, w[q]) + bz[q];
-          s1 += z;
-          s2 += z * z;
-        }
-      }
-    }
-    const double d1 = ub::warp_sum_d((double)s1), d2 = ub::warp_sum_d((double)s2);
-    if ((threadIdx.x & 31) == 0) {
-      red[0][threadIdx.x >> 5] = d1;
-      red[1][threadIdx.x >> 5] = d2;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      double a0 = 0, a1 = 0;
-      for (int i = 0; i < (int)(blockDim.x >> 5); ++i) {
-        a0 += red[0][i];
-        a1 += red[1][i];
-      }
-      atomicAdd(stats2 + 2 * g, a0);
-      atomicAdd(stats2 + 2 * g + 1, a1);
-    }
-  }
-  if (threadIdx.x == 0 && !ok) atomicExch(&g_dconv_error, 1);
-}
 
 
 // ---------------------------------------------------------------------------
@@ -860,51 +739,6 @@ extern "C" int unblend_dconv_conv1(const float* x, long long x_gs, int groups, i
   {                                                                                                           \
     cudaFuncSetAttribute(dconv_conv1_kernel<MH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);    \
     dconv_conv1_kernel<MH><<<grid, ROWS, smem, st>>>(x, x_gs, rows, c, w1, b1, hs, dil, h, stats);            \
-  }
-  if (mh == 8) UB_LAUNCH(8) else if (mh == 16) UB_LAUNCH(16) else if (mh == 32) UB_LAUNCH(32) else UB_LAUNCH(64)
-#undef UB_LAUNCH
-  UB_CHECK_LAUNCH();
-  return 0;
-}
-
-extern "C" int unblend_dconv_z_stats(const float* h, int groups, int rows, int hid, int c, const float* st1,
-                                     const float* g1w, const float* g1b, const float* w2, const float* b2,
-                                     double* stats2, void* stream) {
-  UB_REQUIRE(h && st1 && g1w && g1b && w2 && b2 && stats2 && groups > 0 && rows > 0 && c > 0 && hid > 0);
-  UB_REQUIRE(groups < 65536);
-  const int hs = padded_hidden(hid);
-  const int mh = maxh_for(hs);
-  UB_REQUIRE(mh > 0);
-  cudaStream_t st = ub::as_stream(stream);
-  if (mh <= 16 && c % CPT == 0 && c / CPT <= NTH2 && (reinterpret_cast<uintptr_t>(h) & 15) == 0) {
-    const long long items = (long long)groups * ((rows + IROWS - 1) / IROWS);
-#define UB_ZS3(MH, HW)                                                                                         \
-  {                                                                                                            \
-    const unsigned g2 = persistent_grid(dconv_z_stats3_kernel<MH, HW>, 0, items);                           \
-    dconv_z_stats3_kernel<MH, HW><<<g2, NTH2, 0, st>>>(h, groups, rows, hs, c, st1, g1w, g1b, w2, b2, stats2); \
-  }
-    switch (compute_width(hid)) {
-      case 2: UB_ZS3(8, 2) break;
-      case 4: UB_ZS3(8, 4) break;
-      case 6: UB_ZS3(8, 6) break;
-      case 8: UB_ZS3(8, 8) break;
-      case 10: UB_ZS3(16, 10) break;
-      case 12: UB_ZS3(16, 12) break;
-      case 14: UB_ZS3(16, 14) break;
-      case 16: UB_ZS3(16, 16) break;
-      default: return UNBLEND_ERR_INVALID;
-    }
-#undef UB_ZS3
-    UB_CHECK_LAUNCH();
-    return 0;
-  }
-  const size_t smem = sizeof(float) * ((size_t)2 * c * hs + 2 * c);
-  UB_REQUIRE(smem <= 220 * 1024);
-  dim3 grid((rows + ROWS - 1) / ROWS, groups);
-#define UB_LAUNCH(MH)                                                                                           \
-  {                                                                                                             \
-    cudaFuncSetAttribute(dconv_z_stats_kernel<MH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);    \
-    dconv_z_stats_kernel<MH><<<grid, ROWS, smem, st>>>(h, rows, hs, c, st1, g1w, g1b, w2, b2, stats2);          \
   }
   if (mh == 8) UB_LAUNCH(8) else if (mh == 16) UB_LAUNCH(16) else if (mh == 32) UB_LAUNCH(32) else UB_LAUNCH(64)
 #undef UB_LAUNCH

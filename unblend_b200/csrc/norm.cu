@@ -19,6 +19,27 @@ __global__ void zero_f64_kernel(double* p, long long n) {
     p[i] = 0.0;
 }
 
+// n floats from p, 16 bytes per store after a scalar head up to the first 16-byte boundary.
+__global__ void zero_f32_kernel(float* p, long long n) {
+  const long long head = (long long)((16 - ((uintptr_t)p & 15)) & 15) / 4;
+  const long long h = head < n ? head : n;
+  const long long t0 = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  const long long step = (long long)gridDim.x * blockDim.x;
+  if (t0 < h) p[t0] = 0.f;
+  float4* q = reinterpret_cast<float4*>(p + h);
+  const long long n4 = (n - h) / 4;
+  for (long long i = t0; i < n4; i += step) q[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (long long i = h + 4 * n4 + t0; i < n; i += step) p[i] = 0.f;
+}
+
+// count blocks of n floats at p + i * stride (small strided regions: padding rows).
+__global__ void zero_f32_blocks_kernel(float* p, int count, long long stride, long long n) {
+  const long long total = (long long)count * n;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x)
+    p[(i / n) * stride + i % n] = 0.f;
+}
+
 // grid: (blocks_per_group, groups); one partial per block then a double atomic.
 __global__ void group_sums_kernel(const float* __restrict__ x, double* stats, long long n) {
   const float* xg = x + (long long)blockIdx.y * n;
@@ -252,6 +273,18 @@ extern "C" int unblend_zero_f64(double* p, long long n, void* stream) {
   return 0;
 }
 
+extern "C" int unblend_zero_f32(float* p, long long n, int count, long long stride, void* stream) {
+  UB_REQUIRE(p && n >= 0 && count >= 1 && ((uintptr_t)p & 3) == 0 && (count == 1 || stride >= n));
+  if (n == 0) return 0;
+  if (count == 1)
+    zero_f32_kernel<<<ub::grid_1d(n / 4 + 1, 256), 256, 0, ub::as_stream(stream)>>>(p, n);
+  else
+    zero_f32_blocks_kernel<<<ub::grid_1d((long long)count * n, 256), 256, 0, ub::as_stream(stream)>>>(
+        p, count, stride, n);
+  UB_CHECK_LAUNCH();
+  return 0;
+}
+
 extern "C" int unblend_group_sums(const float* x, double* stats, int groups, long long n, void* stream) {
   UB_REQUIRE(x && stats && groups > 0 && n > 0 && groups < 65536);
   long long per = (n + 255) / 256;
@@ -394,28 +427,64 @@ extern "C" int unblend_standardize(const float* x, float* y, const float* stats2
 // by every GPU that loads the library until the process exits.
 static __device__ __align__(256) double g_mean_std_scratch[2 * UNBLEND_NOALLOC_MAX_BATCH];
 
+#include <cuda.h>
+
 #include <mutex>
 
 namespace {
 std::mutex g_scratch_mutex;
-double* g_scratch_addr[64] = {nullptr};  // device address of the array, per device ordinal
 
-// Device address of the scratch array on the current device. In host code the
-// array's name is only a host-side stand-in, so the address is resolved once
-// per device with that device current.
+// The array's device address is cached per device together with the CUDA
+// context it was resolved in. A host that resets the device
+// (cudaDeviceReset) or drives it through a context of its own gets a new
+// context, where the array can sit at another address: the address is looked
+// up again whenever the current context differs from the cached one.
+struct ScratchSlot {
+  CUcontext ctx;
+  double* addr;
+};
+ScratchSlot g_scratch[64] = {};
+
+using CtxGetCurrent = CUresult (*)(CUcontext*);
+
+// cuCtxGetCurrent through the runtime's driver entry-point query (no link
+// dependency on the driver library); null if the driver does not provide it.
+CtxGetCurrent ctx_get_current() {
+  static CtxGetCurrent fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<CtxGetCurrent>(p);
+  }();
+  return fn;
+}
+
+// Device address of the scratch array in the current context. In host code the
+// array's name is only a host-side stand-in, so the address is resolved with
+// the device current: on the first call per device, and again after the
+// device's context changed.
 int scratch_for_current_device(double** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return (int)e;
   if (dev < 0 || dev >= 64) return UNBLEND_ERR_INVALID;
+  CtxGetCurrent get = ctx_get_current();
+  CUcontext ctx = nullptr;
+  if (get && get(&ctx) != CUDA_SUCCESS) ctx = nullptr;
   std::lock_guard<std::mutex> lock(g_scratch_mutex);
-  if (!g_scratch_addr[dev]) {
+  ScratchSlot& slot = g_scratch[dev];
+  if (!slot.addr || !ctx || slot.ctx != ctx) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_mean_std_scratch);
     if (e != cudaSuccess) return (int)e;
-    g_scratch_addr[dev] = static_cast<double*>(p);
+    // The lookup makes the device's primary context current if none was.
+    if (get && get(&ctx) != CUDA_SUCCESS) ctx = nullptr;
+    slot.ctx = ctx;
+    slot.addr = static_cast<double*>(p);
   }
-  *out = g_scratch_addr[dev];
+  *out = slot.addr;
   return 0;
 }
 }  // namespace

@@ -1,18 +1,21 @@
 // Segment engine kernels: centred zero-padded chunk gather, triangular
-// weighted overlap-add with a weight sum, and the final divide
+// weighted overlap-add with a weight sum, in-place weighting of trimmed chunk
+// outputs (for accumulation on the host), and the final divide
 // (unblend/apply.py:278-311 TensorChunk.padded, 406-432 _split_weight,
 // 1219-1238 accumulate, 1329 out / sum_weight). HBM-streaming, fp32.
 #include "common.cuh"
 
 namespace {
 
-// Triangular cross-fade weight of unblend/apply.py:426-430 with
-// transition_power 1: rising 1..half, falling (T-half)..1, divided by the max.
-__device__ __forceinline__ float split_weight(int j, int seg) {
+// Triangular cross-fade weight of unblend/apply.py:426-430: rising 1..half,
+// falling (T-half)..1, divided by the max, raised to the transition power
+// (the fp32 quotient first, then powf, as the reference's fp32 tensor ops).
+__device__ __forceinline__ float split_weight(int j, int seg, float power) {
   const int half = seg / 2;
   const float mx = (float)(half > seg - half ? half : seg - half);
   const float v = j < half ? (float)(j + 1) : (float)(seg - j);
-  return v / mx;
+  const float w = v / mx;
+  return power == 1.f ? w : powf(w, power);
 }
 
 __global__ void gather_chunks_kernel(const float* __restrict__ track, int channels, long long length,
@@ -35,7 +38,8 @@ __global__ void gather_chunks_kernel(const float* __restrict__ track, int channe
 
 __global__ void overlap_add_kernel(const float* __restrict__ y, int n, int rows, int seg,
                                    const long long* __restrict__ offsets, long long length, long long lo,
-                                   long long span, float* __restrict__ acc, float* __restrict__ sum_w) {
+                                   long long span, float power, float* __restrict__ acc,
+                                   float* __restrict__ sum_w) {
   const long long total = (long long)rows * span;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
@@ -59,12 +63,29 @@ __global__ void overlap_add_kernel(const float* __restrict__ y, int n, int rows,
       const long long j = p - o;
       if (j >= len) continue;
       const int trim = (int)((seg - len) / 2);
-      const float w = split_weight((int)j, seg);
+      const float w = split_weight((int)j, seg, power);
       a += y[((long long)k * rows + r) * seg + trim + j] * w;
       ws += w;
     }
     acc[(long long)r * length + p] += a;
     if (r == 0) sum_w[p] += ws;
+  }
+}
+
+// y[k, r, trim_k + j] *= w(j) for j < len_k (the chunk's valid length): the
+// contribution of chunk k before it is added on the host.
+__global__ void weight_chunks_kernel(float* __restrict__ y, int n, int rows, int seg,
+                                     const long long* __restrict__ offsets, long long length, float power) {
+  const long long total = (long long)n * rows * seg;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int t = (int)(i % seg);
+    const int k = (int)(i / ((long long)rows * seg));
+    const long long o = __ldg(offsets + k);
+    const int len = (int)(length - o < seg ? length - o : seg);
+    const int trim = (seg - len) / 2;
+    const int j = t - trim;
+    if (j >= 0 && j < len) y[i] *= split_weight(j, seg, power);
   }
 }
 
@@ -90,13 +111,23 @@ extern "C" int unblend_gather_chunks(const float* track, int channels, long long
 
 // offsets: n chunk starts in ascending order.
 extern "C" int unblend_overlap_add(const float* y, int n, int rows, int segment, const long long* offsets,
-                                   long long length, long long lo, long long hi, float* acc, float* sum_w,
-                                   void* stream) {
+                                   long long length, long long lo, long long hi, float power, float* acc,
+                                   float* sum_w, void* stream) {
   UB_REQUIRE(y && offsets && acc && sum_w && n > 0 && rows > 0 && segment > 0 && length > 0);
-  UB_REQUIRE(lo >= 0 && hi > lo);
+  UB_REQUIRE(lo >= 0 && hi > lo && power > 0.f);
   const long long span = hi - lo;
   overlap_add_kernel<<<ub::grid_1d((long long)rows * span, 256), 256, 0, ub::as_stream(stream)>>>(
-      y, n, rows, segment, offsets, length, lo, span, acc, sum_w);
+      y, n, rows, segment, offsets, length, lo, span, power, acc, sum_w);
+  UB_CHECK_LAUNCH();
+  return 0;
+}
+
+extern "C" int unblend_weight_chunks(float* y, int n, int rows, int segment, const long long* offsets,
+                                     long long length, float power, void* stream) {
+  UB_REQUIRE(y && offsets && n > 0 && rows > 0 && segment > 0 && length > 0 && power > 0.f);
+  const long long total = (long long)n * rows * segment;
+  weight_chunks_kernel<<<ub::grid_1d(total, 256), 256, 0, ub::as_stream(stream)>>>(
+      y, n, rows, segment, offsets, length, power);
   UB_CHECK_LAUNCH();
   return 0;
 }

@@ -27,6 +27,7 @@ from typing import Any
 import torch
 import torch.distributed as dist
 
+from . import _lib
 from .apply import ValidationError, _accumulate, _segment_plan, _to_host
 
 
@@ -131,7 +132,8 @@ def gather_owned(own: torch.Tensor, plan: list[Shard], rank: int, length: int, g
 
 def apply_model_sharded(model: Any, mix: torch.Tensor, *, overlap: float = 0.25, chunk_batch_size: int = 1,
                         shifts: int = 0, shift_offsets: list[int] | None = None, group: Any = None,
-                        gather: bool = True, device: Any = None) -> torch.Tensor | tuple[int, int, torch.Tensor]:
+                        gather: bool = True, device: Any = None,
+                        timings: list | None = None) -> torch.Tensor | tuple[int, int, torch.Tensor]:
     """``apply_model`` for one ``[C, L]`` track with its segments sharded across the ranks of ``group``.
 
     Every rank calls this with the same track and arguments. The track is either
@@ -141,6 +143,10 @@ def apply_model_sharded(model: Any, mix: torch.Tensor, *, overlap: float = 0.25,
     ``shifts`` the random offsets are drawn on rank 0 and broadcast, so every
     rank separates the same shifted rounds.
 
+    :param timings: When a list, one dict of CUDA events per round is appended
+        (``start``, ``separated``, ``exchanged``, ``gathered``), recorded on the
+        current stream around this rank's separation, the strip exchange and the
+        gather, for phase timing.
     :return: the full ``[S, C, L]`` result on every rank when ``gather`` (always
         with ``shifts``), else ``(own_lo, own_hi, out[S, C, own_hi - own_lo])`` for
         this rank. Ranks are those of the default process group when ``group`` is None.
@@ -177,20 +183,35 @@ def apply_model_sharded(model: Any, mix: torch.Tensor, *, overlap: float = 0.25,
         padded = torch.nn.functional.pad(mix, (max_shift, max_shift))
         rounds = [(off, padded[:, off:L + max_shift].contiguous()) for off in shift_offsets]
     total = None
+
+    def mark(ev: dict | None, name: str) -> None:
+        if ev is not None:
+            ev[name] = torch.cuda.Event(enable_timing=True)
+            ev[name].record()
+
     for off, track in rounds:
+        ev = {} if timings is not None else None
+        mark(ev, "start")
         Lr = track.shape[-1]
         plan = shard_plan(Lr, segment, stride, world)
         me = plan[rank]
-        acc = torch.zeros(S * C, Lr, device=mix.device, dtype=torch.float32)
-        sum_w = torch.zeros(Lr, device=mix.device, dtype=torch.float32)
+        acc = torch.empty(S * C, Lr, device=mix.device, dtype=torch.float32)
+        sum_w = torch.empty(Lr, device=mix.device, dtype=torch.float32)
+        _lib.call("unblend_zero_f32", acc.data_ptr(), acc.numel(), 1, 0)
+        _lib.call("unblend_zero_f32", sum_w.data_ptr(), sum_w.numel(), 1, 0)
         if me.offsets:
             off_dev = torch.tensor(me.offsets, device=mix.device, dtype=torch.int64)
             _accumulate(model, track, S, segment, list(me.offsets), off_dev, chunk_batch_size, acc, sum_w)
+        mark(ev, "separated")
         own = stitch(acc, sum_w, plan, rank, group)
+        mark(ev, "exchanged")
+        if ev is not None:
+            timings.append(ev)
         if not gather and not shifts:
             own = own.view(S, C, me.own_hi - me.own_lo)
             return me.own_lo, me.own_hi, _to_host(own) if host_io else own
         full = gather_owned(own, plan, rank, Lr, group)
+        mark(ev, "gathered")
         if shifts:
             full = full[:, max_shift - off:][:, :L]
         total = full if total is None else total.add_(full)

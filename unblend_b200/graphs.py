@@ -17,6 +17,8 @@ from typing import Callable
 
 import torch
 
+from . import _lib
+
 
 class GraphedForward:
     """Replays ``fn`` (a ``[B, C, T] -> tensor`` CUDA forward) from CUDA graphs, one per input shape."""
@@ -36,12 +38,17 @@ class GraphedForward:
                 self.fn(static_in)  # eager warm-up: lazy attributes and cached tables
             torch.cuda.current_stream(x.device).wait_stream(side)
             graph = torch.cuda.CUDAGraph()
+            before = _lib.counters["launches"]
             with torch.cuda.graph(graph, capture_error_mode="relaxed"):
                 static_out = self.fn(static_in)
-            entry = self.graphs[key] = (graph, static_in, static_out)
-        graph, static_in, static_out = entry
+            # Kernels of this library inside the graph: counted again on every replay.
+            kernels = _lib.counters["launches"] - before
+            _lib.counters["launches"] = before
+            entry = self.graphs[key] = (graph, static_in, static_out, kernels)
+        graph, static_in, static_out, kernels = entry
         static_in.copy_(x)
         graph.replay()
+        _lib.counters["launches"] += kernels
         return static_out.clone()
 
     def release(self) -> None:

@@ -67,6 +67,52 @@ class Act:
         return Act(torch.empty_like(self.t), self.B, self.H, self.W, self.C, self.sb, self.sh, self.sw)
 
 
+class StatsArena:
+    """The float64 GroupNorm / DConv statistics sums of one forward, zeroed by one launch.
+
+    Every statistics buffer of a forward is a slice of one device buffer per
+    (device, batch) key, zeroed by a single ``unblend_zero_f64`` at the start of
+    the forward instead of one fill per buffer. The first forward of a key
+    learns the size it needs (its slices are separate zeroed buffers); later
+    forwards of that key take slices of the arena. Arenas are never freed while
+    the model lives, so captured CUDA graphs can keep referring to them.
+    """
+
+    def __init__(self) -> None:
+        self.bufs: dict = {}
+        self.retired: list = []
+        self.key = None
+        self.cur: torch.Tensor | None = None
+        self.pos = 0
+
+    def begin(self, device: torch.device, batch: int) -> None:
+        self.key = (str(device), batch)
+        self.device = device
+        self.cur = self.bufs.get(self.key)
+        self.pos = 0
+        if self.cur is not None:
+            _lib.call("unblend_zero_f64", self.cur.data_ptr(), self.cur.numel())
+
+    def take(self, n: int) -> torch.Tensor:
+        """``n`` zeroed doubles (16-byte aligned slices)."""
+        size = n + (n & 1)
+        if self.cur is not None and self.pos + size <= self.cur.numel():
+            t = self.cur[self.pos:self.pos + n]
+        else:
+            t = torch.empty(size, device=self.device, dtype=torch.float64)
+            _lib.call("unblend_zero_f64", t.data_ptr(), size)
+            t = t[:n]
+        self.pos += size
+        return t
+
+    def end(self) -> None:
+        if self.cur is None or self.cur.numel() < self.pos:
+            if self.cur is not None:
+                self.retired.append(self.cur)
+            self.bufs[self.key] = torch.empty(max(self.pos, 2), device=self.device, dtype=torch.float64)
+        self.cur = None
+
+
 def sin_embedding(length: int, dim: int, max_period: float = 10000.0) -> torch.Tensor:
     """1-D sinusoidal table ``[length, dim]`` (cos | sin halves), as unblend/transformer.py:18-48."""
     pos = torch.arange(length, dtype=torch.float32).view(-1, 1)
@@ -160,6 +206,10 @@ class HTDemucsCuda(nn.Module):
         (every layer on CUDA-core fp32 FMA kernels).
     """
 
+    #: The Separator normalises the track before ``apply_model`` and restores it after
+    #: (unblend/api.py:1644, 1706); the RoFormers set this False.
+    external_normalization = True
+
     def __init__(self, config: dict, state_dict: dict, precision: str = "fp32") -> None:
         super().__init__()
         if precision not in PRECISIONS:
@@ -183,6 +233,7 @@ class HTDemucsCuda(nn.Module):
         self._fixed_batch_shape = False
         self.depth = cfg["depth"]
         self.weights = nn.ParameterDict()
+        self._arena = StatsArena()
         self._pack(state_dict)
 
     @classmethod
@@ -419,7 +470,7 @@ class HTDemucsCuda(nn.Module):
             q = f"{pre}.dconv.layers.{d}"
             dil = 2**d
             h = Act.freq(B, H, W, hid, dev)
-            st1 = torch.zeros(2 * groups, device=dev, dtype=torch.float64)
+            st1 = self._arena.take(2 * groups)
             conv1_smem = 4 * ((128 + 2 * dil) * (C + 4) + hid * 3 * C)
             # Deep levels (hidden width >= 16): both contractions on the tensor
             # cores, z materialised (these levels hold few rows).
@@ -433,7 +484,7 @@ class HTDemucsCuda(nn.Module):
                           self.w(f"{q}.g1.w").data_ptr(), self.w(f"{q}.g1.b").data_ptr(), groups * W, hid, W,
                           ACT_GELU)
                 z = Act.freq(B, H, W, 2 * C, dev)
-                st2 = torch.zeros(2 * groups, device=dev, dtype=torch.float64)
+                st2 = self._arena.take(2 * groups)
                 self._conv(a, self.w(f"{q}.c2.w"), self.w(f"{q}.c2.b"), z, h_out=H, w_out=W, n_out=2 * C,
                            stats=st2, stats_per_h=per_h)
                 s2 = self._stats(st2, groups, W * 2 * C)
@@ -461,7 +512,7 @@ class HTDemucsCuda(nn.Module):
                         self.w(f"{q}.c2.b").data_ptr())
                 # GN2 statistics from the moments of GELU(GN1(h)): no z at all.
                 hw = _moment_width(hid)
-                mom = torch.zeros(groups * (hw + hw * (hw + 1) // 2), device=dev, dtype=torch.float64)
+                mom = self._arena.take(groups * (hw + hw * (hw + 1) // 2))
                 # The moments pass also rewrites h in place as a = GELU(GN1(h)) for the apply pass.
                 _lib.call("unblend_dconv_moments", h.t.data_ptr(), groups, W, hid, s1.data_ptr(),
                           pw("g1.w").data_ptr(), pw("g1.b").data_ptr(), mom.data_ptr(), h.t.data_ptr(),
@@ -476,7 +527,7 @@ class HTDemucsCuda(nn.Module):
                           work=4.0 * groups * W * C * hid)
                 continue
             z = Act.freq(B, H, W, 2 * C, dev)
-            st2 = torch.zeros(2 * groups, device=dev, dtype=torch.float64)
+            st2 = self._arena.take(2 * groups)
             self._conv(h, self.w(f"{q}.c2.w"), self.w(f"{q}.c2.b"), z, h_out=H, w_out=W, n_out=2 * C,
                        prologue=PRO_GN_GELU, pro_stats=s1, pro_gamma=self.w(f"{q}.g1.w"),
                        pro_beta=self.w(f"{q}.g1.b"), pro_per_h=per_h, stats=st2, stats_per_h=per_h)
@@ -504,7 +555,8 @@ class HTDemucsCuda(nn.Module):
         if not freq and out.sb // out.C > out.W:
             # Rows past the logical length are the zero padding the next
             # stride-4 convolution reads (the reference pads to a multiple of 4).
-            out.t.view(out.B, -1, out.C)[:, out.W :].zero_()
+            cap = out.sb // out.C
+            _lib.call("unblend_zero_f32", out.t.data_ptr() + 4 * out.W * out.C, (cap - out.W) * out.C, out.B, out.sb)
         # The frequency embedding (added to the first frequency layer's output) rides in the rewrite epilogue.
         post = self.w("freq_emb") if freq and pre == "encoder.0" and "freq_emb" in self.weights else None
         self._conv(y, self.w(f"{pre}.rewrite.w"), self.w(f"{pre}.rewrite.b"), out, h_out=y.H, w_out=y.W,
@@ -648,7 +700,7 @@ class HTDemucsCuda(nn.Module):
         f = torch.empty(B * L * hidden, device=dev, dtype=torch.float32)
         self._linear(h2, B, L, D, self.w(f"{q}.linear1.weight"), self.w(f"{q}.linear1.bias"), f, hidden,
                      act=ACT_GELU)
-        st = torch.zeros(2 * B, device=dev, dtype=torch.float64)
+        st = self._arena.take(2 * B)
         self._linear(f, B, L, hidden, self.w(f"{q}.linear2.weight"), self.w(f"{q}.linear2.bias"), x_new, D,
                      res=x_new, res_scale=self.w(f"{q}.gamma_2.scale"), stats=st)
         s = self._stats(st, B, L * D)
@@ -738,7 +790,7 @@ class HTDemucsCuda(nn.Module):
             mix = torch.nn.functional.pad(mix, (0, T - length))
         mix = mix.contiguous()
         graphed = self.__dict__.get("_graphed")
-        out = graphed(mix) if graphed is not None else self._forward_full(mix)
+        out = graphed(mix) if graphed is not None else self._forward_arena(mix)
         if length < T:
             out = out[..., :length]
         return out
@@ -761,7 +813,7 @@ class HTDemucsCuda(nn.Module):
         from .graphs import GraphedForward
 
         self.prefill_inference_caches()
-        self.__dict__["_graphed"] = GraphedForward(self._forward_full)
+        self.__dict__["_graphed"] = GraphedForward(self._forward_arena)
         self._fixed_batch_shape = True
 
     def disable_compiled_core(self) -> None:
@@ -817,6 +869,13 @@ class HTDemucsCuda(nn.Module):
         """Weight ``name``, or its stem-selected rows when a selection is active."""
         sel = self.__dict__.get("_selected")
         return sel[name] if sel and name in sel else self.w(name)
+
+    def _forward_arena(self, mix: torch.Tensor) -> torch.Tensor:
+        self._arena.begin(mix.device, mix.shape[0])
+        try:
+            return self._forward_full(mix)
+        finally:
+            self._arena.end()
 
     def _forward_full(self, mix: torch.Tensor) -> torch.Tensor:
         B, C, T = mix.shape
