@@ -372,6 +372,27 @@ def test_tc_3x3_glu_and_dilated(mode, block_n):
     assert torch.allclose(st[0::2], o2.sum(1), rtol=1e-6, atol=1e-4)
 
 
+@pytest.mark.parametrize("mode", MODES, ids=["tf32x3", "bf16"])
+@pytest.mark.parametrize("B", [8, 32])
+def test_tc_decoder3_rewrite_headline_shape(mode, B):
+    """The largest 3x3 rewrite of the headline forward: HTDemucs decoder.3 (512 frequency rows x 336
+    frames per segment, 48 -> 96 channels, GLU) at the bench's 32 segments per launch and at 8, with
+    the tile width the model picks (96), checked over every output against torch's fp32 convolution."""
+    H, W, C, N = 512, 336, 48, 96
+    g = torch.Generator(device="cuda").manual_seed(B)
+    x = torch.randn(B, H, W, C, device="cuda", generator=g)
+    w = torch.randn(N, 3, 3, C, device="cuda", generator=g) * 0.05
+    b = torch.randn(N, device="cuda", generator=g)
+    y = torch.empty(B, H, W, N // 2, device="cuda")
+    _conv_tc(x, w, b, y, mode, 96, B=B, H=H, W=W, C=C, in_s=(H * W * C, W * C, C), Ho=H, Wo=W, N=N,
+             out_s=(H * W * N // 2, W * N // 2, N // 2), kh=3, kw=3, ph=1, pw=1, act=ACT_GLU)
+    err = 0.0
+    for i in range(0, B, 4):  # the fp32 reference in slices of 4 segments (bounded memory)
+        z = _ref_conv(x[i:i + 4], w, b, 3, 3, 1, 1, 1, 1, 1, 1)
+        err = max(err, rel_err(y[i:i + 4], z[..., 0::2] * torch.sigmoid(z[..., 1::2])))
+    assert err < TC_TOL[mode]
+
+
 @pytest.mark.parametrize("mode", MODES)
 @pytest.mark.parametrize("block_n", [128, 256])
 def test_tc_time_stride4_super_rows(mode, block_n):

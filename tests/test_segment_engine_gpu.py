@@ -43,6 +43,17 @@ class _Positional(torch.nn.Module):
         return torch.stack([x, 2 * x, 1e-2 * x.cumsum(-1)], 1)
 
 
+class _Pointwise(_Positional):
+    """x, 2x and x*x: per-sample, so any batch size gives bit-identical chunk outputs."""
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.fits is not None and x.shape[0] > self.fits:
+            self.ooms += 1
+            raise RuntimeError("CUDA out of memory (stand-in model, for the backoff test)")
+        self.batches.append(x.shape[0])
+        return torch.stack([x, 2 * x, x * x], 1)
+
+
 def _oracle(model, track: torch.Tensor, power: float = 1.0, overlap: float = 0.25) -> torch.Tensor:
     seg = int(round(model.samplerate * model.max_allowed_segment))
     fwd = lambda b: torch.stack([b, 2 * b, 1e-2 * b.cumsum(-1)], 1)  # noqa: E731
@@ -81,23 +92,24 @@ def test_host_accumulation_matches_device_accumulation(monkeypatch):
     host = eng.apply_model_multi(m, tracks, chunk_batch_size=4, transition_power=2.0)
     for a, b, t in zip(host, resident, tracks):
         assert a.device.type == "cpu" and b.device.type == "cpu"
-        assert rel_err(a, b) < 1e-6
-        assert rel_err(a, _oracle(m, t, 2.0)) < 1e-6
+        # Host accumulation adds chunk by chunk, the device kernel position by position: fp32 rounding only.
+        assert rel_err(a, b) < 1e-5
+        assert rel_err(a, _oracle(m, t, 2.0)) < 1e-5
     # A track on the device, shifted rounds, host accumulators.
     t = tracks[0].cuda()
     host_s = eng.apply_model(m, t, chunk_batch_size=4, shifts=2, shift_offsets=[13, 400])
     monkeypatch.undo()
     res_s = eng.apply_model(m, t, chunk_batch_size=4, shifts=2, shift_offsets=[13, 400])
-    assert rel_err(host_s, res_s) < 1e-6
+    assert rel_err(host_s, res_s) < 1e-5
 
 
 def test_oom_backoff_halves_and_output_is_exact():
-    clean = eng.apply_model(_Positional(), _tracks()[3], chunk_batch_size=8)
-    m = _Positional(fits=2)
+    clean = eng.apply_model(_Pointwise(), _tracks()[3], chunk_batch_size=8)
+    m = _Pointwise(fits=2)
     state = {"chunk_batch_size": 8}
     out = eng.apply_model(m, _tracks()[3], chunk_batch_size=8, oom_backoff_state=state)
     assert state["chunk_batch_size"] == 2 and m.ooms == 2
-    assert rel_err(out, clean) < 1e-7
+    assert torch.equal(out, clean)
     with pytest.raises(RuntimeError, match="out of memory"):
         eng.apply_model(_Positional(fits=1), _tracks()[3], chunk_batch_size=4)
 

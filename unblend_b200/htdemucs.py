@@ -87,30 +87,31 @@ class StatsArena:
 
     def begin(self, device: torch.device, batch: int) -> None:
         self.key = (str(device), batch)
-        self.device = device
         self.cur = self.bufs.get(self.key)
         self.pos = 0
         if self.cur is not None:
             _lib.call("unblend_zero_f64", self.cur.data_ptr(), self.cur.numel())
 
-    def take(self, n: int) -> torch.Tensor:
-        """``n`` zeroed doubles (16-byte aligned slices)."""
+    def take(self, n: int, device: torch.device) -> torch.Tensor:
+        """``n`` zeroed doubles on ``device`` (16-byte aligned slices of the arena inside a forward)."""
         size = n + (n & 1)
-        if self.cur is not None and self.pos + size <= self.cur.numel():
+        if self.cur is not None and self.cur.device == device and self.pos + size <= self.cur.numel():
             t = self.cur[self.pos:self.pos + n]
         else:
-            t = torch.empty(size, device=self.device, dtype=torch.float64)
+            t = torch.empty(size, device=device, dtype=torch.float64)
             _lib.call("unblend_zero_f64", t.data_ptr(), size)
             t = t[:n]
-        self.pos += size
+        if self.key is not None:
+            self.pos += size
         return t
 
-    def end(self) -> None:
+    def end(self, device: torch.device) -> None:
         if self.cur is None or self.cur.numel() < self.pos:
             if self.cur is not None:
                 self.retired.append(self.cur)
-            self.bufs[self.key] = torch.empty(max(self.pos, 2), device=self.device, dtype=torch.float64)
+            self.bufs[self.key] = torch.empty(max(self.pos, 2), device=device, dtype=torch.float64)
         self.cur = None
+        self.key = None
 
 
 def sin_embedding(length: int, dim: int, max_period: float = 10000.0) -> torch.Tensor:
@@ -470,7 +471,7 @@ class HTDemucsCuda(nn.Module):
             q = f"{pre}.dconv.layers.{d}"
             dil = 2**d
             h = Act.freq(B, H, W, hid, dev)
-            st1 = self._arena.take(2 * groups)
+            st1 = self._arena.take(2 * groups, dev)
             conv1_smem = 4 * ((128 + 2 * dil) * (C + 4) + hid * 3 * C)
             # Deep levels (hidden width >= 16): both contractions on the tensor
             # cores, z materialised (these levels hold few rows).
@@ -484,7 +485,7 @@ class HTDemucsCuda(nn.Module):
                           self.w(f"{q}.g1.w").data_ptr(), self.w(f"{q}.g1.b").data_ptr(), groups * W, hid, W,
                           ACT_GELU)
                 z = Act.freq(B, H, W, 2 * C, dev)
-                st2 = self._arena.take(2 * groups)
+                st2 = self._arena.take(2 * groups, dev)
                 self._conv(a, self.w(f"{q}.c2.w"), self.w(f"{q}.c2.b"), z, h_out=H, w_out=W, n_out=2 * C,
                            stats=st2, stats_per_h=per_h)
                 s2 = self._stats(st2, groups, W * 2 * C)
@@ -512,7 +513,7 @@ class HTDemucsCuda(nn.Module):
                         self.w(f"{q}.c2.b").data_ptr())
                 # GN2 statistics from the moments of GELU(GN1(h)): no z at all.
                 hw = _moment_width(hid)
-                mom = self._arena.take(groups * (hw + hw * (hw + 1) // 2))
+                mom = self._arena.take(groups * (hw + hw * (hw + 1) // 2), dev)
                 # The moments pass also rewrites h in place as a = GELU(GN1(h)) for the apply pass.
                 _lib.call("unblend_dconv_moments", h.t.data_ptr(), groups, W, hid, s1.data_ptr(),
                           pw("g1.w").data_ptr(), pw("g1.b").data_ptr(), mom.data_ptr(), h.t.data_ptr(),
@@ -527,7 +528,7 @@ class HTDemucsCuda(nn.Module):
                           work=4.0 * groups * W * C * hid)
                 continue
             z = Act.freq(B, H, W, 2 * C, dev)
-            st2 = self._arena.take(2 * groups)
+            st2 = self._arena.take(2 * groups, dev)
             self._conv(h, self.w(f"{q}.c2.w"), self.w(f"{q}.c2.b"), z, h_out=H, w_out=W, n_out=2 * C,
                        prologue=PRO_GN_GELU, pro_stats=s1, pro_gamma=self.w(f"{q}.g1.w"),
                        pro_beta=self.w(f"{q}.g1.b"), pro_per_h=per_h, stats=st2, stats_per_h=per_h)
@@ -700,7 +701,7 @@ class HTDemucsCuda(nn.Module):
         f = torch.empty(B * L * hidden, device=dev, dtype=torch.float32)
         self._linear(h2, B, L, D, self.w(f"{q}.linear1.weight"), self.w(f"{q}.linear1.bias"), f, hidden,
                      act=ACT_GELU)
-        st = self._arena.take(2 * B)
+        st = self._arena.take(2 * B, dev)
         self._linear(f, B, L, hidden, self.w(f"{q}.linear2.weight"), self.w(f"{q}.linear2.bias"), x_new, D,
                      res=x_new, res_scale=self.w(f"{q}.gamma_2.scale"), stats=st)
         s = self._stats(st, B, L * D)
@@ -875,7 +876,7 @@ class HTDemucsCuda(nn.Module):
         try:
             return self._forward_full(mix)
         finally:
-            self._arena.end()
+            self._arena.end(mix.device)
 
     def _forward_full(self, mix: torch.Tensor) -> torch.Tensor:
         B, C, T = mix.shape
