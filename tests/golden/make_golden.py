@@ -4,7 +4,7 @@ Run from the repository root with a checkout of the reference project (the
 path argument, else ``$UNBLEND_REFERENCE``, else ``reference`` beside this
 repository)::
 
-    python tests/golden/make_golden.py [<reference checkout> [configs|roformer|ensemble|melband]]
+    python tests/golden/make_golden.py [<reference checkout> [configs|roformer|ensemble|melband|scnet]]
 
 It imports the reference (``torchcodec`` is stubbed: the reference only uses it
 for file decode/encode in unblend/api.py:20-21), builds each model exactly as
@@ -52,6 +52,18 @@ of two measured configurations (their inputs are regenerated from the seed by
   on a 16 s clip (seed 4), batch 4: the vocals stem (every 16th sample and the
   same windows) plus per-stem sums of all six stems.
 
+``... scnet`` writes the SCNet fixtures (unblend/scnet.py):
+
+* ``scnet_small_reduced.pt`` the masked architecture with reduced widths (dims
+  4/16/32/32, two dual-path layers, seed 7), batch 2 on 0.5 s, full outputs.
+* ``scnet_plain_reduced.pt`` the plain architecture with the xl band layout and
+  reduced widths (seed 8), batch 2 on 0.5 s, full outputs.
+* ``scnet_small_full.pt`` / ``scnet_xl_full.pt`` the registry ``scnet_small``
+  (seed 9) and ``scnet_xl_wide_v5`` (seed 10) on a 1 s clip: every 5th output
+  sample plus per-stem sums.
+* ``scnet_apply.pt`` ``apply_model`` with the registry ``scnet_small`` over a
+  16 s track (two 11 s segments), batch 2: every 16th sample, windows, sums.
+
 The fixtures hold only outputs and small inputs; weights are regenerated from
 the seed on the fly, and ``weights_digest`` pins that regeneration.
 """
@@ -76,6 +88,8 @@ from unblend_b200.synth import (  # noqa: E402
     melband_config,
     melband_state_dict,
     htdemucs_config,
+    scnet_config,
+    scnet_state_dict,
     htdemucs_state_dict,
     synth_track,
 )
@@ -226,6 +240,54 @@ def main_configs(unblend) -> None:
     print("config fixtures written to", HERE)
 
 
+def build_scnet(unblend, cfg: dict, seed: int):
+    """``manual_seed(seed); build_scnet(...)``, checked against ``scnet_state_dict``."""
+    import unblend.scnet
+
+    torch.manual_seed(seed)
+    kw = {k: v for k, v in cfg.items() if k not in ("architecture", "sources", "samplerate", "segment_samples")}
+    model = unblend.scnet.build_scnet(cfg["architecture"], kw, sources=cfg["sources"], samplerate=cfg["samplerate"],
+                                      segment_samples=cfg["segment_samples"])
+    mine = scnet_state_dict(cfg, seed)
+    ref = model.state_dict()
+    assert set(ref) == set(mine), "state_dict keys differ"
+    for k in ref:
+        assert torch.equal(ref[k], mine[k]), f"weight {k} differs"
+    return model, weights_digest(mine)
+
+
+def main_scnet(unblend) -> None:
+    """SCNet fixtures (reduced masked and plain models, registry configurations, apply_model)."""
+    torch.set_num_threads(os.cpu_count() or 1)
+    reduced = dict(dims=[4, 16, 32, 32], num_dplayer=2, conv_depths=[1, 1, 1])
+    with torch.inference_mode():
+        for name, seed, fname, over in (("scnet_small", 7, "scnet_small_reduced.pt", reduced),
+                                        ("scnet_xl_wide_v5", 8, "scnet_plain_reduced.pt",
+                                         dict(reduced, conv_depths=[2, 1, 1]))):
+            cfg = scnet_config(name, **over)
+            model, digest = build_scnet(unblend, cfg, seed)
+            mix = torch.stack([synth_track(0.5, 40), synth_track(0.5, 41)])
+            torch.save({"config": cfg, "seed": seed, "weights_digest": digest, "mix": mix,
+                        "out": model(mix).clone()}, os.path.join(HERE, fname))
+        for name, seed, fname in (("scnet_small", 9, "scnet_small_full.pt"), ("scnet_xl_wide_v5", 10, "scnet_xl_full.pt")):
+            cfg = scnet_config(name)
+            model, digest = build_scnet(unblend, cfg, seed)
+            mix = synth_track(1.0, 42)[None]
+            out = model(mix)
+            torch.save({"config": cfg, "seed": seed, "weights_digest": digest, "mix": mix,
+                        "decimate": 5, "out": out[..., ::5].clone(), **_summary(out)}, os.path.join(HERE, fname))
+        cfg = scnet_config("scnet_small")
+        model, digest = build_scnet(unblend, cfg, 9)
+        mix = synth_track(16.0, 43)[None]
+        y = unblend.apply.apply_model(model, mix, device="cpu", shifts=0, overlap=0.25, chunk_batch_size=2)
+        seg = cfg["segment_samples"]
+        win = config_windows(mix.shape[-1], seg, int(0.75 * seg))
+        torch.save({"config": cfg, "seed": 9, "weights_digest": digest, "mix_seconds": 16.0, "mix_seed": 43,
+                    "mix_digest": mix_digest(mix), "overlap": 0.25, "chunk_batch_size": 2, "shifts": 0,
+                    **_config_record(y, win)}, os.path.join(HERE, "scnet_apply.pt"))
+    print("SCNet fixtures written to", HERE)
+
+
 def build_roformer(unblend, cfg: dict, seed: int):
     """``manual_seed(seed); BSRoformer(**cfg)``, checked against ``bsroformer_state_dict``."""
     import unblend.roformer
@@ -330,7 +392,9 @@ def main_melband(unblend) -> None:
 
 
 if __name__ == "__main__":
-    if len(sys.argv) > 2 and sys.argv[2] == "configs":
+    if len(sys.argv) > 2 and sys.argv[2] == "scnet":
+        main_scnet(import_reference(sys.argv[1]))
+    elif len(sys.argv) > 2 and sys.argv[2] == "configs":
         main_configs(import_reference(sys.argv[1]))
     elif len(sys.argv) > 2 and sys.argv[2] == "ensemble":
         main_ensemble(import_reference(sys.argv[1]))

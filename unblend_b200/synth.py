@@ -474,6 +474,88 @@ def melband_state_dict(cfg: dict, seed: int) -> "OrderedDict[str, torch.Tensor]"
     return state
 
 
+# SCNet registry entries (unblend/metadata.json "scnet_small" and "scnet_xl_wide_v5"):
+# architecture, sources, samplerate, segment_samples and the constructor config.
+SCNET_CONFIGS = {
+    "scnet_small": dict(
+        architecture="scnet_masked", sources=["drums", "bass", "other", "vocals"], samplerate=44100,
+        segment_samples=485100, audio_channels=2, dims=[4, 32, 64, 128], nfft=4096, hop_size=1024, win_size=4096,
+        normalized=True, band_SR=[0.175, 0.392, 0.433], band_stride=[1, 4, 16], band_kernel=[3, 4, 16],
+        conv_depths=[3, 2, 1], compress=4, conv_kernel=3, num_dplayer=6, expand=1),
+    "scnet_xl_wide_v5": dict(
+        architecture="scnet", sources=["drums", "bass", "other", "vocals"], samplerate=44100,
+        segment_samples=485100, audio_channels=2, dims=[4, 64, 128, 256], nfft=4096, hop_size=1024, win_size=4096,
+        normalized=True, band_SR=[0.23, 0.37, 0.4], band_stride=[1, 4, 4], band_kernel=[3, 4, 4],
+        conv_depths=[3, 3, 3], compress=4, conv_kernel=3, num_dplayer=8, expand=1),
+}
+
+
+def scnet_config(name: str = "scnet_small", **overrides) -> dict:
+    """SCNet registry config (plus ``architecture``, ``sources``, ``samplerate``, ``segment_samples``)."""
+    cfg = {k: (list(v) if isinstance(v, list) else v) for k, v in SCNET_CONFIGS[name].items()}
+    cfg.update(overrides)
+    return cfg
+
+
+def scnet_state_dict(cfg: dict, seed: int) -> "OrderedDict[str, torch.Tensor]":
+    """Random-init SCNet weights identical to ``manual_seed(seed); SCNet(**cfg)`` (or ``SCNetMasked``).
+
+    Follows the construction order of unblend/scnet.py:616-700: for each stage
+    the encoder ``SDblock`` (three band convolutions, the per-band
+    ``ConvolutionModule`` stacks, the global 3x3 convolution), then that
+    stage's decoder (``FusionLayer`` and ``SUlayer``), which the reference
+    inserts at the front of its decoder list; then the dual-path trunk (two
+    bidirectional LSTMs, two linears and two GroupNorms per layer); for the
+    masked architecture (unblend/scnet.py:800-835) the truncated-normal
+    frequency embedding and the mask head.
+    """
+    torch.manual_seed(seed)
+    out: "OrderedDict[str, torch.Tensor]" = OrderedDict()
+    dims, S = cfg["dims"], len(cfg["sources"])
+    kern, stride = cfg["band_kernel"], cfg["band_stride"]
+    stages = len(dims) - 1
+    for i in range(stages):
+        cin, cout = dims[i], dims[i + 1]
+        p = f"encoder.{i}"
+        for j in range(3):
+            _take(f"{p}.SDlayer.convs.{j}", nn.Conv2d(cin, cout, (kern[j], 1), (stride[j], 1), (0, 0)), out)
+        hidden = int(cout / cfg["compress"])
+        k = cfg["conv_kernel"]
+        for j, depth in enumerate(cfg["conv_depths"]):
+            for d in range(abs(depth)):
+                q = f"{p}.conv_modules.{j}.layers.{d}"
+                _take(f"{q}.0", nn.GroupNorm(1, cout), out)
+                _take(f"{q}.1", nn.Conv1d(cout, hidden * 2, k, padding=k // 2), out)
+                _take(f"{q}.3", nn.Conv1d(hidden, hidden, k, padding=k // 2, groups=hidden), out)
+                _take(f"{q}.4", nn.GroupNorm(1, hidden), out)
+                _take(f"{q}.6", nn.Conv1d(hidden, cout, 1), out)
+        _take(f"{p}.globalconv", nn.Conv2d(cout, cout, 3, 1, 1), out)
+        d_idx = stages - 1 - i  # the reference inserts each stage's decoder at the front
+        _take(f"decoder.{d_idx}.0.conv", nn.Conv2d(cout * 2, cout * 2, 3, stride=1, padding=1), out)
+        dec_out = cin if i != 0 else cin * S
+        for j in range(3):
+            _take(f"decoder.{d_idx}.1.convtrs.{j}", nn.ConvTranspose2d(cout, dec_out, [kern[j], 1], [stride[j], 1]),
+                  out)
+    c = dims[-1]
+    for i in range(cfg["num_dplayer"]):
+        d_model = c * (2 if i % 2 == 1 else 1)
+        hid = d_model * cfg["expand"]
+        q = f"separation_net.dp_modules.{i}"
+        for j in range(2):
+            _take(f"{q}.lstm_layers.{j}", nn.LSTM(d_model, hid, num_layers=1, bidirectional=True), out)
+        for j in range(2):
+            _take(f"{q}.linear_layers.{j}", nn.Linear(hid * 2, d_model), out)
+        for j in range(2):
+            _take(f"{q}.norm_layers.{j}", nn.GroupNorm(1, d_model), out)
+    if cfg.get("architecture") == "scnet_masked":
+        pos = torch.zeros(1, dims[0], cfg["nfft"] // 2 + 1, 1)
+        nn.init.trunc_normal_(pos, std=0.02)
+        out["pos_embed_f"] = pos
+        _take("mask_layer.0", nn.Conv2d(4 * S, 64, kernel_size=3, padding="same"), out)
+        _take("mask_layer.2", nn.Conv2d(64, 4 * S, kernel_size=1, padding="same"), out)
+    return out
+
+
 def synth_track(seconds: float, seed: int, samplerate: int = 44100) -> torch.Tensor:
     """Synthetic stereo mixture ``[2, round(seconds * samplerate)]`` in fp32.
 
