@@ -29,7 +29,8 @@ enum UnblendAct {
   UNBLEND_ACT_NONE = 0,
   UNBLEND_ACT_GELU = 1, /* exact erf GELU, F.gelu */
   UNBLEND_ACT_GLU = 2,  /* F.glu over interleaved (value, gate) column pairs */
-  UNBLEND_ACT_TANH = 3  /* torch.tanh (BS-RoFormer mask estimator hidden layers) */
+  UNBLEND_ACT_TANH = 3, /* torch.tanh (BS-RoFormer mask estimator hidden layers) */
+  UNBLEND_ACT_SWISH = 4 /* x * sigmoid(x) (SCNet ConvolutionModule, unblend/scnet.py:37-47) */
 };
 
 /* Transform applied to each input element as it is loaded. */
@@ -423,6 +424,8 @@ int unblend_stft_frames(const float* mix, float* out, const float* window, int b
  * (center, Hann, not normalised, window-square envelope) trimmed to `length`:
  * out[batch, stems (+1), 2, length]. With `complement` (stems must be 1) a second
  * stem mix - stem 0 is appended. frames_buf: batch*stems*2*frames*nfft floats.
+ * A null stft stands for a unit spectrum: the masks themselves are inverted
+ * (SCNet's decoder output, unblend/scnet.py:775-782).
  */
 int unblend_istft_masked(const float* stft, const float* mask, long long mask_ss, const float* window,
                          const float* mix, float* frames_buf, float* out, int batch, int stems, int complement,
@@ -480,6 +483,53 @@ int unblend_weight_chunks(float* y, int n, int rows, int segment, const long lon
 /* out = acc / sum_w (broadcast over [S*C, L]). */
 int unblend_divide(const float* acc, const float* sum_w, float* out, int rows, long long length,
                    void* stream);
+
+/* SCNet (unblend/scnet.py). Activations are channels-last [B, F, T, C]. */
+
+/* y[r, i] = i < n_in ? x[r, i] : 0 for i < n_out: the segment's trailing zeros
+ * before the STFT (stft_padding, unblend/scnet.py:543-572). */
+int unblend_pad_tail(const float* x, float* y, int rows, long long n_in, long long n_out, void* stream);
+
+/* x [batch, n1, n2, groups*4] -> y [groups, batch, n2, n1, 4] (elements of 4
+ * floats; 16-byte aligned buffers), plus add[c * n2 + j] on channel c of
+ * element (., j) when `add` is given (groups must then be 1). Turns the
+ * frame-major STFT [B, T, F, 4] into [B, F, T, 4] (with SCNetMasked's
+ * frequency embedding, unblend/scnet.py:868-874) and the decoder output
+ * [B, F, T, 4S] into per-stem iSTFT input [S, B, T, F, 4]. */
+int unblend_swap_axes(const float* x, float* y, const float* add, int batch, int n1, int n2, int groups,
+                      void* stream);
+
+/* ConvolutionModule depthwise Conv1d (kernel 3, padding 1, groups = channels;
+ * unblend/scnet.py:78-86) along T of z [rows, T, c]: u = b + sum_k w[c, k]
+ * z[t + k - 1]; stats[2r], stats[2r + 1] = sum and sum of squares of row r of u
+ * (double, written, not accumulated) for the GroupNorm(1) that follows. */
+int unblend_depthwise3(const float* z, const float* w, const float* bias, float* u, double* stats, int rows,
+                       int t_len, int c, void* stream);
+
+/* y[k * y_stride + j] = act(x[k * x_stride + j]) for k < count, j < n; act one
+ * of NONE, GELU, TANH, SWISH; in place when x == y with equal strides. */
+int unblend_act_copy(const float* x, long long x_stride, float* y, long long y_stride, int count, long long n,
+                     int act, void* stream);
+
+/* FeatureConversion (unblend/scnet.py:333-437): orthonormal real DFT along T
+ * of x [rows, T, c] (T even) into y [rows, T/2 + 1, 2c] (real parts on the first
+ * c channels, imaginary parts on the next c), and its inverse from
+ * [rows, K, 2c] to [rows, 2 (K - 1), c] (imaginary parts of the first and last
+ * bins ignored, as torch.fft.irfft). */
+int unblend_rfft_time(const float* x, float* y, int rows, int t_len, int c, void* stream);
+int unblend_irfft_time(const float* y, float* x, int rows, int n_bins, int c, void* stream);
+
+/* Bidirectional single-layer LSTM recurrence (torch.nn.LSTM; DualPathRNN,
+ * unblend/scnet.py:440-500). xp rows hold the gate pre-activations
+ * W_ih x + b_ih + b_hh as [forward (i, f, g, o) x hid | reverse ...] (8 hid
+ * floats); whh_t is [2][hid][4 hid] (W_hh transposed, forward then reverse);
+ * h_out rows receive [forward h | reverse h] (2 hid floats). Sequence s step t
+ * is row (s / inner) * outer_stride + (s % inner) * inner_stride +
+ * t * step_stride of both; the reverse direction runs t from steps - 1 down.
+ * hid: 32, 64, 128, 256 or 512. */
+int unblend_lstm_recurrence(const float* xp, const float* whh_t, float* h_out, int n_seq, int steps, int hid,
+                            int inner, long long outer_stride, long long inner_stride, long long step_stride,
+                            void* stream);
 
 #ifdef __cplusplus
 }

@@ -26,7 +26,7 @@ c_float = ctypes.c_float
 c_double = ctypes.c_double
 c_void_p = ctypes.c_void_p
 
-ACT_NONE, ACT_GELU, ACT_GLU, ACT_TANH = 0, 1, 2, 3
+ACT_NONE, ACT_GELU, ACT_GLU, ACT_TANH, ACT_SWISH = 0, 1, 2, 3, 4
 PRO_NONE, PRO_GN_GELU, PRO_ADD = 0, 1, 2
 GEMM_MAX_GROUPS = 64
 
@@ -138,6 +138,13 @@ _SIGNATURES = {
     "unblend_dconv_moment_sums": [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p],
     "unblend_scatter_mean_pairs": [c_void_p, c_ll, c_ll, c_void_p, c_void_p, c_int, c_void_p, c_ll, c_void_p],
     "unblend_stft_frames": [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p],
+    "unblend_pad_tail": [c_void_p, c_void_p, c_int, c_ll, c_ll, c_void_p],
+    "unblend_swap_axes": [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p],
+    "unblend_depthwise3": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p],
+    "unblend_act_copy": [c_void_p, c_ll, c_void_p, c_ll, c_int, c_ll, c_int, c_void_p],
+    "unblend_rfft_time": [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p],
+    "unblend_irfft_time": [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p],
+    "unblend_lstm_recurrence": [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_ll, c_ll, c_ll, c_void_p],
     "unblend_istft_masked": [c_void_p, c_void_p, c_ll, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
                              c_int, c_int, c_int, c_int, c_void_p],
 }

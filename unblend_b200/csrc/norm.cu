@@ -101,6 +101,7 @@ __global__ void group_norm_apply_kernel(const float* __restrict__ x, float* __re
     if (gamma) v = v * gamma[ch];
     if (beta) v = v + beta[ch];
     if (act == UNBLEND_ACT_GELU) v = ub::gelu_erf(v);
+    if (act == UNBLEND_ACT_SWISH) v = v / (1.0f + expf(-v));
     y[i] = v;
   }
 }
@@ -227,6 +228,7 @@ __global__ void group_norm_apply4_kernel(const float4* __restrict__ x, float4* _
       if (gamma) t = t * __ldg(gamma + 4 * q + k);
       if (beta) t = t + __ldg(beta + 4 * q + k);
       if (act == UNBLEND_ACT_GELU) t = ub::gelu_erf(t);
+      if (act == UNBLEND_ACT_SWISH) t = t / (1.0f + expf(-t));
       e[k] = t;
     }
     y[i] = make_float4(e[0], e[1], e[2], e[3]);
@@ -308,7 +310,7 @@ extern "C" int unblend_group_norm_apply(const float* x, float* y, const float* s
                                         const float* beta, long long rows, int c, long long rows_per_group,
                                         int act, void* stream) {
   UB_REQUIRE(x && y && stats2 && rows > 0 && c > 0 && rows_per_group > 0);
-  UB_REQUIRE(act == UNBLEND_ACT_NONE || act == UNBLEND_ACT_GELU);
+  UB_REQUIRE(act == UNBLEND_ACT_NONE || act == UNBLEND_ACT_GELU || act == UNBLEND_ACT_SWISH);
   if (c % 4 == 0 && rows * c < (1LL << 31) && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
       (reinterpret_cast<uintptr_t>(y) & 15) == 0) {
     const int n4 = (int)(rows * c / 4);

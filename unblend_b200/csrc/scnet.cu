@@ -1,0 +1,409 @@
+// SCNet kernels (unblend/scnet.py): what the sparse-compression network needs
+// beyond the convolution, GroupNorm and STFT kernels it shares with the other
+// models. Activations are channels-last [B, F, T, C] (frequency rows, frames,
+// channels), fp32.
+//
+//   pad_tail        zero padding of the segment to the STFT length (stft_padding)
+//   swap_axes       [B, n1, n2, G*4] -> [G, B, n2, n1, 4]: frame-major STFT output to
+//                   frequency-major activations (plus the masked variant's frequency
+//                   embedding), and the decoder output to per-stem iSTFT input
+//   depthwise3      ConvolutionModule's depthwise conv (k = 3 along frames) with the
+//                   GroupNorm(1) sums of each (batch, frequency) row
+//   act_copy        strided copy with GELU / tanh / Swish (band outputs into the full
+//                   band, transposed-conv trims, the mask head's tanh)
+//   rfft_time / irfft_time   FeatureConversion: orthonormal real DFT along frames
+//   lstm_recurrence the bidirectional LSTM recurrence of DualPathRNN (input
+//                   projections precomputed by a GEMM)
+#include <math.h>
+
+#include "common.cuh"
+
+namespace {
+
+__global__ void pad_tail_kernel(const float* __restrict__ x, float* __restrict__ y, int rows, long long n_in,
+                                long long n_out) {
+  const long long total = (long long)rows * n_out;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / n_out, j = i - r * n_out;
+    y[i] = j < n_in ? __ldg(x + r * n_in + j) : 0.f;
+  }
+}
+
+// Block (32, 8): a 32 x 32 tile of float4 elements of one (batch, group).
+__global__ void swap_axes_kernel(const float4* __restrict__ x, float4* __restrict__ y, const float* __restrict__ add,
+                                 int batch, int n1, int n2, int groups) {
+  __shared__ float4 tile[32][33];
+  const int j0 = blockIdx.x * 32, i0 = blockIdx.y * 32;
+  const int b = blockIdx.z % batch, g = blockIdx.z / batch;
+  for (int di = threadIdx.y; di < 32; di += 8) {
+    const int i = i0 + di, j = j0 + threadIdx.x;
+    if (i < n1 && j < n2) tile[di][threadIdx.x] = x[(((long long)b * n1 + i) * n2 + j) * groups + g];
+  }
+  __syncthreads();
+  for (int dj = threadIdx.y; dj < 32; dj += 8) {
+    const int j = j0 + dj, i = i0 + threadIdx.x;
+    if (i < n1 && j < n2) {
+      float4 v = tile[threadIdx.x][dj];
+      if (add) {
+        const float* a = add + (long long)(4 * g) * n2 + j;
+        v.x += __ldg(a);
+        v.y += __ldg(a + n2);
+        v.z += __ldg(a + 2LL * n2);
+        v.w += __ldg(a + 3LL * n2);
+      }
+      y[(((long long)g * batch + b) * n2 + j) * n1 + i] = v;
+    }
+  }
+}
+
+// One block per row r: u[r, t, c] = b[c] + sum_k w[c, k] z[r, t + k - 1, c] (zero outside
+// [0, T)); stats[2r], stats[2r+1] = sum u, sum u^2 over the row (double).
+__global__ void depthwise3_kernel(const float* __restrict__ z, const float* __restrict__ w,
+                                  const float* __restrict__ bias, float* __restrict__ u, double* __restrict__ stats,
+                                  int t_len, int c) {
+  const long long r = blockIdx.x;
+  const float* zr = z + r * t_len * (long long)c;
+  float* ur = u + r * t_len * (long long)c;
+  const int n = t_len * c;
+  double s1 = 0.0, s2 = 0.0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int t = i / c, ch = i - t * c;
+    float v = __ldg(bias + ch);
+    v = fmaf(__ldg(w + 3 * ch + 1), zr[i], v);
+    if (t > 0) v = fmaf(__ldg(w + 3 * ch), zr[i - c], v);
+    if (t + 1 < t_len) v = fmaf(__ldg(w + 3 * ch + 2), zr[i + c], v);
+    ur[i] = v;
+    s1 += v;
+    s2 += (double)v * v;
+  }
+  __shared__ double red[2][32];
+  s1 = ub::warp_sum_d(s1);
+  s2 = ub::warp_sum_d(s2);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    red[0][warp] = s1;
+    red[1][warp] = s2;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double a = 0.0, bq = 0.0;
+    for (int k = 0; k < (int)(blockDim.x >> 5); ++k) {
+      a += red[0][k];
+      bq += red[1][k];
+    }
+    stats[2 * r] = a;
+    stats[2 * r + 1] = bq;
+  }
+}
+
+__device__ __forceinline__ float apply_act(float v, int act) {
+  if (act == UNBLEND_ACT_GELU) return ub::gelu_erf(v);
+  if (act == UNBLEND_ACT_TANH) return tanhf(v);
+  if (act == UNBLEND_ACT_SWISH) return v / (1.0f + expf(-v));
+  return v;
+}
+
+__global__ void act_copy_kernel(const float* __restrict__ x, long long xs, float* __restrict__ y, long long ys,
+                                int count, long long n, int act) {
+  const long long total = (long long)count * n;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long k = i / n, j = i - k * n;
+    y[k * ys + j] = apply_act(x[k * xs + j], act);
+  }
+}
+
+// cos / sin of 2 pi j / T for j < T, from double precision, in shared memory.
+__device__ __forceinline__ void twiddle_table(float2* tab, int t_len) {
+  for (int j = threadIdx.x; j < t_len; j += blockDim.x) {
+    double s, c;
+    sincospi(2.0 * (double)j / (double)t_len, &s, &c);
+    tab[j] = make_float2((float)c, (float)s);
+  }
+}
+
+// Grid (rows, ceil(C / 32)), 256 threads. x [rows, T, C] -> y [rows, K, 2C], K = T/2 + 1:
+// y[., k, c] = sum_t x[t, c] cos(2 pi k t / T) / sqrt(T), y[., k, C + c] = -sum_t x sin(...) / sqrt(T).
+// Lane = channel of the 32-channel slice; warp w computes bins w, w + 8, ... four at a time.
+__global__ void __launch_bounds__(256) rfft_time_kernel(const float* __restrict__ x, float* __restrict__ y, int t_len,
+                                                        int c) {
+  extern __shared__ __align__(16) float sm[];
+  float2* tab = reinterpret_cast<float2*>(sm);
+  float* xs = sm + 2 * t_len;  // [T][32]
+  const long long r = blockIdx.x;
+  const int c0 = blockIdx.y * 32, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nk = t_len / 2 + 1;
+  twiddle_table(tab, t_len);
+  for (int i = threadIdx.x; i < t_len * 32; i += blockDim.x) {
+    const int t = i >> 5, ch = c0 + (i & 31);
+    xs[i] = ch < c ? __ldg(x + (r * t_len + t) * c + ch) : 0.f;
+  }
+  __syncthreads();
+  const float scale = rsqrtf((float)t_len);
+  const int ch = c0 + lane;
+  for (int kb = warp; kb < nk; kb += 32) {
+    float re[4] = {0.f, 0.f, 0.f, 0.f}, im[4] = {0.f, 0.f, 0.f, 0.f};
+    int idx[4] = {0, 0, 0, 0}, kk[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) kk[q] = kb + 8 * q < nk ? kb + 8 * q : 0;
+    for (int t = 0; t < t_len; ++t) {
+      const float v = xs[t * 32 + lane];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 w = tab[idx[q]];
+        re[q] = fmaf(v, w.x, re[q]);
+        im[q] = fmaf(-v, w.y, im[q]);
+        idx[q] += kk[q];
+        if (idx[q] >= t_len) idx[q] -= t_len;
+      }
+    }
+    if (ch < c) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int k = kb + 8 * q;
+        if (k < nk) {
+          float* o = y + (r * nk + k) * 2LL * c;
+          o[ch] = re[q] * scale;
+          o[c + ch] = im[q] * scale;
+        }
+      }
+    }
+  }
+}
+
+// Grid (rows, ceil(C / 32)), 256 threads. y [rows, K, 2C] -> x [rows, T, C], T = 2 (K - 1):
+// x[t, c] = (Re y_0 + (-1)^t Re y_{K-1} + 2 sum_{0<k<K-1} (Re y_k cos - Im y_k sin)(2 pi k t / T)) / sqrt(T)
+// (the imaginary parts of the first and last bins do not enter a real inverse transform).
+__global__ void __launch_bounds__(256) irfft_time_kernel(const float* __restrict__ y, float* __restrict__ x, int nk,
+                                                         int c) {
+  extern __shared__ __align__(16) float sm[];
+  const int t_len = 2 * (nk - 1);
+  float2* tab = reinterpret_cast<float2*>(sm);
+  float* re_s = sm + 2 * t_len;   // [K][32]
+  float* im_s = re_s + nk * 32;   // [K][32]
+  const long long r = blockIdx.x;
+  const int c0 = blockIdx.y * 32, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  twiddle_table(tab, t_len);
+  for (int i = threadIdx.x; i < nk * 32; i += blockDim.x) {
+    const int k = i >> 5, ch = c0 + (i & 31);
+    const float* src = y + (r * nk + k) * 2LL * c;
+    const bool edge = k == 0 || k == nk - 1;
+    re_s[i] = ch < c ? (edge ? 1.f : 2.f) * __ldg(src + ch) : 0.f;
+    im_s[i] = ch < c && !edge ? 2.f * __ldg(src + c + ch) : 0.f;
+  }
+  __syncthreads();
+  const float scale = rsqrtf((float)t_len);
+  const int ch = c0 + lane;
+  for (int tb = warp; tb < t_len; tb += 32) {
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    int idx[4] = {0, 0, 0, 0}, tt[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) tt[q] = tb + 8 * q < t_len ? tb + 8 * q : 0;
+    for (int k = 0; k < nk; ++k) {
+      const float a = re_s[k * 32 + lane], bq = im_s[k * 32 + lane];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 w = tab[idx[q]];
+        acc[q] = fmaf(a, w.x, acc[q]);
+        acc[q] = fmaf(-bq, w.y, acc[q]);
+        idx[q] += tt[q];
+        if (idx[q] >= t_len) idx[q] -= t_len;
+      }
+    }
+    if (ch < c) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int t = tb + 8 * q;
+        if (t < t_len) x[(r * t_len + t) * (long long)c + ch] = acc[q] * scale;
+      }
+    }
+  }
+}
+
+// Bidirectional LSTM recurrence (torch.nn.LSTM, gates i, f, g, o):
+//   g = xp[seq, step] + W_hh h_prev;  c = s(f) c + s(i) tanh(g_g);  h = s(o) tanh(c)
+// Grid (ceil(n_seq / (P * G)), 2 directions), 256 threads. P = 256 / min(H, 256) parts
+// of the block each run G sequences; a thread owns U = max(1, H / 256) hidden units of
+// its part. xp rows hold [forward 4H | reverse 4H] gate pre-activations (input
+// projection and both biases); whh_t[dir] is W_hh transposed, [H][4H]; h_out rows
+// receive [forward H | reverse H]. Row of (seq, step): (seq / inner) * outer_stride +
+// (seq % inner) * inner_stride + step * step_stride.
+template <int G, int U>
+__global__ void __launch_bounds__(256) lstm_recurrence_kernel(const float* __restrict__ xp,
+                                                              const float* __restrict__ whh_t,
+                                                              float* __restrict__ h_out, int n_seq, int steps, int hid,
+                                                              int inner, long long outer_stride,
+                                                              long long inner_stride, long long step_stride) {
+  extern __shared__ __align__(16) float hbuf[];  // [2][P][H][G]
+  const int dir = blockIdx.y;
+  const int tpp = hid < 256 ? hid : 256;  // threads per part
+  const int parts = 256 / tpp;
+  const int part = threadIdx.x / tpp, tl = threadIdx.x - part * tpp;
+  const int seq0 = (blockIdx.x * parts + part) * G;
+  const float* w = whh_t + (long long)dir * hid * 4 * hid;
+  long long rowb[G];
+  bool live[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const int s = seq0 + g;
+    live[g] = s < n_seq;
+    const int sq = live[g] ? s : 0;
+    rowb[g] = (long long)(sq / inner) * outer_stride + (long long)(sq % inner) * inner_stride;
+  }
+  float cst[U][G];
+#pragma unroll
+  for (int m = 0; m < U; ++m)
+#pragma unroll
+    for (int g = 0; g < G; ++g) cst[m][g] = 0.f;
+  float* hpart[2] = {hbuf + (long long)part * hid * G, hbuf + ((long long)parts + part) * hid * G};
+  for (int i = tl; i < hid * G; i += tpp) hpart[0][i] = 0.f;
+  __syncthreads();
+  const long long xs = 8LL * hid, hs = 2LL * hid;
+  for (int it = 0; it < steps; ++it) {
+    const int step = dir == 0 ? it : steps - 1 - it;
+    const float* hcur = hpart[it & 1];
+    float* hnext = hpart[(it + 1) & 1];
+    float acc[U][4][G];
+#pragma unroll
+    for (int m = 0; m < U; ++m) {
+      const int u = tl + m * tpp;
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+          acc[m][q][g] = live[g] ? __ldg(xp + (rowb[g] + step * step_stride) * xs + dir * 4LL * hid + q * hid + u)
+                                 : 0.f;
+    }
+#pragma unroll 2
+    for (int k = 0; k < hid; ++k) {
+      float hv[G];
+#pragma unroll
+      for (int g4 = 0; g4 < G; g4 += 4) {
+        const float4 v = *reinterpret_cast<const float4*>(hcur + k * G + g4);
+        hv[g4] = v.x;
+        hv[g4 + 1] = v.y;
+        hv[g4 + 2] = v.z;
+        hv[g4 + 3] = v.w;
+      }
+      const float* wk = w + (long long)k * 4 * hid;
+#pragma unroll
+      for (int m = 0; m < U; ++m) {
+        const int u = tl + m * tpp;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float wv = __ldg(wk + q * hid + u);
+#pragma unroll
+          for (int g = 0; g < G; ++g) acc[m][q][g] = fmaf(wv, hv[g], acc[m][q][g]);
+        }
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < U; ++m) {
+      const int u = tl + m * tpp;
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float ig = 1.0f / (1.0f + expf(-acc[m][0][g]));
+        const float fg = 1.0f / (1.0f + expf(-acc[m][1][g]));
+        const float gg = tanhf(acc[m][2][g]);
+        const float og = 1.0f / (1.0f + expf(-acc[m][3][g]));
+        cst[m][g] = fg * cst[m][g] + ig * gg;
+        const float h = og * tanhf(cst[m][g]);
+        hnext[u * G + g] = h;
+        if (live[g]) h_out[(rowb[g] + step * step_stride) * hs + dir * (long long)hid + u] = h;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+}  // namespace
+
+extern "C" int unblend_pad_tail(const float* x, float* y, int rows, long long n_in, long long n_out, void* stream) {
+  UB_REQUIRE(x && y && rows > 0 && n_in > 0 && n_out >= n_in);
+  pad_tail_kernel<<<ub::grid_1d((long long)rows * n_out, 256), 256, 0, ub::as_stream(stream)>>>(x, y, rows, n_in,
+                                                                                               n_out);
+  UB_CHECK_LAUNCH();
+  return 0;
+}
+
+extern "C" int unblend_swap_axes(const float* x, float* y, const float* add, int batch, int n1, int n2, int groups,
+                                 void* stream) {
+  UB_REQUIRE(x && y && batch > 0 && n1 > 0 && n2 > 0 && groups > 0 && x != y);
+  UB_REQUIRE((reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0);
+  UB_REQUIRE(!add || groups == 1);
+  UB_REQUIRE((long long)batch * groups < 65536);
+  dim3 grid((n2 + 31) / 32, (n1 + 31) / 32, batch * groups);
+  swap_axes_kernel<<<grid, dim3(32, 8), 0, ub::as_stream(stream)>>>(reinterpret_cast<const float4*>(x),
+                                                                    reinterpret_cast<float4*>(y), add, batch, n1, n2,
+                                                                    groups);
+  UB_CHECK_LAUNCH();
+  return 0;
+}
+
+extern "C" int unblend_depthwise3(const float* z, const float* w, const float* bias, float* u, double* stats, int rows,
+                                  int t_len, int c, void* stream) {
+  UB_REQUIRE(z && w && bias && u && stats && rows > 0 && t_len > 0 && c > 0 && z != u);
+  UB_REQUIRE(rows < (1 << 30) && (long long)t_len * c < (1LL << 31));
+  depthwise3_kernel<<<rows, 256, 0, ub::as_stream(stream)>>>(z, w, bias, u, stats, t_len, c);
+  UB_CHECK_LAUNCH();
+  return 0;
+}
+
+extern "C" int unblend_act_copy(const float* x, long long x_stride, float* y, long long y_stride, int count,
+                                long long n, int act, void* stream) {
+  UB_REQUIRE(x && y && count > 0 && n > 0 && x_stride >= 0 && y_stride >= 0);
+  UB_REQUIRE(act == UNBLEND_ACT_NONE || act == UNBLEND_ACT_GELU || act == UNBLEND_ACT_TANH ||
+             act == UNBLEND_ACT_SWISH);
+  UB_REQUIRE(x != y || x_stride == y_stride);
+  act_copy_kernel<<<ub::grid_1d((long long)count * n, 256), 256, 0, ub::as_stream(stream)>>>(x, x_stride, y,
+                                                                                           y_stride, count, n, act);
+  UB_CHECK_LAUNCH();
+  return 0;
+}
+
+extern "C" int unblend_rfft_time(const float* x, float* y, int rows, int t_len, int c, void* stream) {
+  UB_REQUIRE(x && y && x != y && rows > 0 && t_len >= 2 && t_len % 2 == 0 && c > 0 && rows < (1 << 30));
+  const size_t smem = sizeof(float) * (2 * (size_t)t_len + 32 * (size_t)t_len);
+  UB_REQUIRE(smem <= 220 * 1024);
+  cudaFuncSetAttribute(rfft_time_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  rfft_time_kernel<<<dim3(rows, (c + 31) / 32), 256, smem, ub::as_stream(stream)>>>(x, y, t_len, c);
+  UB_CHECK_LAUNCH();
+  return 0;
+}
+
+extern "C" int unblend_irfft_time(const float* y, float* x, int rows, int n_bins, int c, void* stream) {
+  UB_REQUIRE(x && y && x != y && rows > 0 && n_bins >= 2 && c > 0 && rows < (1 << 30));
+  const int t_len = 2 * (n_bins - 1);
+  const size_t smem = sizeof(float) * (2 * (size_t)t_len + 64 * (size_t)n_bins);
+  UB_REQUIRE(smem <= 220 * 1024);
+  cudaFuncSetAttribute(irfft_time_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  irfft_time_kernel<<<dim3(rows, (c + 31) / 32), 256, smem, ub::as_stream(stream)>>>(y, x, n_bins, c);
+  UB_CHECK_LAUNCH();
+  return 0;
+}
+
+extern "C" int unblend_lstm_recurrence(const float* xp, const float* whh_t, float* h_out, int n_seq, int steps,
+                                       int hid, int inner, long long outer_stride, long long inner_stride,
+                                       long long step_stride, void* stream) {
+  UB_REQUIRE(xp && whh_t && h_out && n_seq > 0 && steps > 0 && inner > 0);
+  UB_REQUIRE(hid == 32 || hid == 64 || hid == 128 || hid == 256 || hid == 512);
+  constexpr int G = 8;
+  const int tpp = hid < 256 ? hid : 256;
+  const int parts = 256 / tpp;
+  const int per_block = parts * G;
+  const unsigned blocks = (unsigned)((n_seq + per_block - 1) / per_block);
+  const size_t smem = sizeof(float) * 2 * (size_t)parts * hid * G;
+  cudaStream_t st = ub::as_stream(stream);
+  if (hid <= 256) {
+    cudaFuncSetAttribute(lstm_recurrence_kernel<G, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    lstm_recurrence_kernel<G, 1><<<dim3(blocks, 2), 256, smem, st>>>(xp, whh_t, h_out, n_seq, steps, hid, inner,
+                                                                     outer_stride, inner_stride, step_stride);
+  } else {
+    cudaFuncSetAttribute(lstm_recurrence_kernel<G, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    lstm_recurrence_kernel<G, 2><<<dim3(blocks, 2), 256, smem, st>>>(xp, whh_t, h_out, n_seq, steps, hid, inner,
+                                                                     outer_stride, inner_stride, step_stride);
+  }
+  UB_CHECK_LAUNCH();
+  return 0;
+}

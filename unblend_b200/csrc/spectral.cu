@@ -414,10 +414,11 @@ __global__ void __launch_bounds__(NT) istft_mask_frames_kernel(const float* __re
   load_quarter_twiddles(tq, tw);
   const int t = blockIdx.x, s = blockIdx.y, b = blockIdx.z;
   const int bins = n / 2 + 1;
-  const float* sp = stft + ((long long)b * frames + t) * bins * 4;
+  const float* sp = stft ? stft + ((long long)b * frames + t) * bins * 4 : nullptr;
   const float* mp = mask + (long long)s * mask_ss + ((long long)b * frames + t) * bins * 4;
   for (int k = threadIdx.x; k < bins; k += blockDim.x) {
-    const float4 a = *reinterpret_cast<const float4*>(sp + (long long)k * 4);
+    // Without a spectrum the mask itself is inverted (a unit complex factor).
+    const float4 a = sp ? *reinterpret_cast<const float4*>(sp + (long long)k * 4) : make_float4(1.f, 0.f, 1.f, 0.f);
     const float4 m = *reinterpret_cast<const float4*>(mp + (long long)k * 4);
     float2 x0 = make_float2(a.x * m.x - a.y * m.y, a.x * m.y + a.y * m.x);
     float2 x1 = make_float2(a.z * m.z - a.w * m.w, a.z * m.w + a.w * m.z);
@@ -499,7 +500,7 @@ extern "C" int unblend_stft_frames(const float* mix, float* out, const float* wi
 extern "C" int unblend_istft_masked(const float* stft, const float* mask, long long mask_ss, const float* window,
                                     const float* mix, float* frames_buf, float* out, int batch, int stems,
                                     int complement, int length, int nfft, int hop, int zero_dc, void* stream) {
-  UB_REQUIRE(stft && mask && window && frames_buf && out && batch > 0 && stems > 0 && length > 0 && hop > 0);
+  UB_REQUIRE(mask && window && frames_buf && out && batch > 0 && stems > 0 && length > 0 && hop > 0);
   UB_REQUIRE((nfft == 2048 || nfft == 4096) && batch < 65536 && stems < 65536);
   UB_REQUIRE(!complement || (stems == 1 && mix));
   const float2* tw = current_twiddles();

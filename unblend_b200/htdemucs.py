@@ -20,98 +20,21 @@ ordered (f, t); the 2-D positional table is laid out to match.
 from __future__ import annotations
 
 import math
-from dataclasses import dataclass
 
 import torch
 from torch import nn
 
 from . import _lib
+from ._lib import ACT_GELU, ACT_GLU, ACT_NONE, PRO_ADD, PRO_GN_GELU, PRO_NONE, AttnParams
 from .apply import ValidationError
-from ._lib import ACT_GELU, ACT_GLU, ACT_NONE, PRO_ADD, PRO_GN_GELU, PRO_NONE, AttnParams, ConvParams
+from .convnet import (PRECISIONS, Act, ConvNet, StatsArena, _block_n, _conv_w, _interleave_rows, _key,  # noqa: F401
+                      ctypes_byref, split_tf32)
 from .synth import HTDEMUCS_CONFIGS
-
-
-def _key(name: str) -> str:
-    return name.replace(".", "__")
 
 
 def _moment_width(hid: int) -> int:
     """Hidden width the fused DConv kernels compute with: the true width when even, else rounded up to 4."""
     return hid if hid % 2 == 0 else -(-hid // 4) * 4
-
-
-@dataclass
-class Act:
-    """A channels-last activation view: ``t`` holds [B, H, W, C] with strides sb/sh/sw."""
-
-    t: torch.Tensor
-    B: int
-    H: int
-    W: int
-    C: int
-    sb: int
-    sh: int
-    sw: int
-
-    @staticmethod
-    def freq(B: int, F: int, T: int, C: int, device) -> "Act":
-        t = torch.empty(B * F * T * C, device=device, dtype=torch.float32)
-        return Act(t, B, F, T, C, F * T * C, T * C, C)
-
-    @staticmethod
-    def time(B: int, rows: int, cap: int, C: int, device) -> "Act":
-        t = torch.empty(B * cap * C, device=device, dtype=torch.float32)
-        return Act(t, B, 1, rows, C, cap * C, cap * C, C)
-
-    def like(self) -> "Act":
-        return Act(torch.empty_like(self.t), self.B, self.H, self.W, self.C, self.sb, self.sh, self.sw)
-
-
-class StatsArena:
-    """The float64 GroupNorm / DConv statistics sums of one forward, zeroed by one launch.
-
-    Every statistics buffer of a forward is a slice of one device buffer per
-    (device, batch) key, zeroed by a single ``unblend_zero_f64`` at the start of
-    the forward instead of one fill per buffer. The first forward of a key
-    learns the size it needs (its slices are separate zeroed buffers); later
-    forwards of that key take slices of the arena. Arenas are never freed while
-    the model lives, so captured CUDA graphs can keep referring to them.
-    """
-
-    def __init__(self) -> None:
-        self.bufs: dict = {}
-        self.retired: list = []
-        self.key = None
-        self.cur: torch.Tensor | None = None
-        self.pos = 0
-
-    def begin(self, device: torch.device, batch: int) -> None:
-        self.key = (str(device), batch)
-        self.cur = self.bufs.get(self.key)
-        self.pos = 0
-        if self.cur is not None:
-            _lib.call("unblend_zero_f64", self.cur.data_ptr(), self.cur.numel())
-
-    def take(self, n: int, device: torch.device) -> torch.Tensor:
-        """``n`` zeroed doubles on ``device`` (16-byte aligned slices of the arena inside a forward)."""
-        size = n + (n & 1)
-        if self.cur is not None and self.cur.device == device and self.pos + size <= self.cur.numel():
-            t = self.cur[self.pos:self.pos + n]
-        else:
-            t = torch.empty(size, device=device, dtype=torch.float64)
-            _lib.call("unblend_zero_f64", t.data_ptr(), size)
-            t = t[:n]
-        if self.key is not None:
-            self.pos += size
-        return t
-
-    def end(self, device: torch.device) -> None:
-        if self.cur is None or self.cur.numel() < self.pos:
-            if self.cur is not None:
-                self.retired.append(self.cur)
-            self.bufs[self.key] = torch.empty(max(self.pos, 2), device=device, dtype=torch.float64)
-        self.cur = None
-        self.key = None
 
 
 def sin_embedding(length: int, dim: int, max_period: float = 10000.0) -> torch.Tensor:
@@ -137,20 +60,6 @@ def sin_embedding_2d(d_model: int, height: int, width: int, max_period: float = 
     return pe
 
 
-def _interleave_rows(t: torch.Tensor) -> torch.Tensor:
-    """Reorder the 2C output rows (value half, gate half) to (v0, g0, v1, g1, ...)."""
-    c = t.shape[0] // 2
-    idx = torch.stack([torch.arange(c), torch.arange(c) + c], dim=1).reshape(-1)
-    return t[idx].contiguous()
-
-
-def _conv_w(w: torch.Tensor) -> torch.Tensor:
-    """Conv weight to [Cout, KH, KW, Cin] (Conv1d kernels become KH=1)."""
-    if w.dim() == 3:
-        return w.permute(0, 2, 1).unsqueeze(1).contiguous()
-    return w.permute(0, 2, 3, 1).contiguous()
-
-
 def _convtr_taps3(w: torch.Tensor) -> torch.Tensor:
     """A stride-4, kernel-8 transposed conv as one 3-tap conv with 4 output phases.
 
@@ -169,34 +78,7 @@ def _convtr_taps3(w: torch.Tensor) -> torch.Tensor:
     return torch.stack([torch.stack(t, 1) for t in phases], 0).reshape(-1, 3, w.shape[0]).contiguous()
 
 
-def split_tf32(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-    """Split fp32 ``w`` into ``hi`` (rounded to TF32, low 13 mantissa bits clear) and ``lo = w - hi``."""
-    w = w.float().contiguous()
-    hi = ((w.view(torch.int32) + 0x1000) & ~0x1FFF).view(torch.float32)
-    return hi.contiguous(), (w - hi).contiguous()
-
-
-PRECISIONS = ("fp32", "bf16", "fp32-simt")
-
-
-def _block_n(n_out: int, bn256_min: int) -> int:
-    """Output-channel tile of the tensor-core convolution: the fewest wasted MMA columns.
-
-    Candidates 64, 96, 128, 192 (and 256 from ``bn256_min`` channels on): the one
-    whose tiles cover ``n_out`` with the least padding, preferring the wider tile
-    on ties (fewer re-reads of the input rows).
-    """
-    cands = [64, 96, 128, 192] + ([256] if n_out >= bn256_min else [])
-    best = None
-    for bn in cands:
-        waste = -(-n_out // bn) * bn - n_out
-        key = (waste, -bn)
-        if best is None or key < best[0]:
-            best = (key, bn)
-    return best[1]
-
-
-class HTDemucsCuda(nn.Module):
+class HTDemucsCuda(ConvNet):
     """HTDemucs separation forward as sm_100a CUDA kernels.
 
     :param config: HTDemucs constructor config (registry ``config`` fields).
@@ -212,13 +94,7 @@ class HTDemucsCuda(nn.Module):
     external_normalization = True
 
     def __init__(self, config: dict, state_dict: dict, precision: str = "fp32") -> None:
-        super().__init__()
-        if precision not in PRECISIONS:
-            raise ValueError(f"precision must be one of {PRECISIONS}")
-        self.precision = precision
-        self._tc_cache: dict = {}
-        # Output widths from which the 256-column tile is used (per tensor-core mode).
-        self._bn256_min = {_lib.TC_TF32X3: 512, _lib.TC_BF16: 512}
+        super().__init__(precision)
         cfg = dict(HTDEMUCS_CONFIGS["htdemucs"])
         cfg.update(config)
         if cfg.get("multi_freqs") or not cfg["cac"] or cfg["norm_starts"] < cfg["depth"]:
@@ -233,8 +109,6 @@ class HTDemucsCuda(nn.Module):
         self.segment_length = int(round(cfg["segment"] * cfg["samplerate"]))
         self._fixed_batch_shape = False
         self.depth = cfg["depth"]
-        self.weights = nn.ParameterDict()
-        self._arena = StatsArena()
         self._pack(state_dict)
 
     @classmethod
@@ -247,12 +121,6 @@ class HTDemucsCuda(nn.Module):
         return cls(cfg, module.state_dict(), precision=precision)
 
     # ------------------------------------------------------------------ weights
-    def _put(self, name: str, t: torch.Tensor) -> None:
-        self.weights[_key(name)] = nn.Parameter(t.detach().float().contiguous().clone(), requires_grad=False)
-
-    def w(self, name: str) -> torch.Tensor:
-        return self.weights[_key(name)]
-
     def _pack(self, sd: dict) -> None:
         sd = {k: v.detach().float().cpu() for k, v in sd.items()}
         cfg = self.config
@@ -367,97 +235,6 @@ class HTDemucsCuda(nn.Module):
                 assert v.is_contiguous()
             cache[key] = tabs
         return cache[key]
-
-    # ------------------------------------------------------------------ launch helpers
-    def _conv(self, x: Act, w: torch.Tensor, b: torch.Tensor | None, out: Act, *, h_out: int, w_out: int,
-              n_out: int, kh: int = 1, kw: int = 1, sh: int = 1, sw: int = 1, dh: int = 1, dw: int = 1,
-              ph: int = 0, pw: int = 0, act: int = ACT_NONE, prologue: int = PRO_NONE,
-              pro_stats: torch.Tensor | None = None, pro_gamma=None, pro_beta=None, pro_per_h: int = 0,
-              pro_x2: Act | None = None, res: torch.Tensor | None = None, res_scale=None,
-              stats: torch.Tensor | None = None, stats_per_h: int = 0, n_group: int | None = None,
-              out_sg: int = 0, out_offset: int = 0, out_sh: int | None = None, out_sw: int | None = None,
-              useful: float = 1.0, post: torch.Tensor | None = None, y_bf16: bool = False) -> None:
-        p = ConvParams()
-        p.batch, p.h_in, p.w_in, p.c_in = x.B, x.H, x.W, x.C
-        p.in_sb, p.in_sh, p.in_sw = x.sb, x.sh, x.sw
-        p.h_out, p.w_out, p.n_out = h_out, w_out, n_out
-        p.kh, p.kw, p.sh, p.sw, p.dh, p.dw, p.ph, p.pw = kh, kw, sh, sw, dh, dw, ph, pw
-        p.out_sb = out.sb
-        p.out_sh = out.sh if out_sh is None else out_sh
-        p.out_sw = out.sw if out_sw is None else out_sw
-        p.out_sg = out_sg
-        n_final = n_out // 2 if act == ACT_GLU else n_out
-        p.n_group = n_group if n_group is not None else n_final
-        p.act, p.prologue = act, prologue
-        p.pro_stats, p.pro_gamma, p.pro_beta = _lib.ptr(pro_stats), _lib.ptr(pro_gamma), _lib.ptr(pro_beta)
-        p.pro_group_per_h = pro_per_h
-        if pro_x2 is not None:
-            assert (pro_x2.sb, pro_x2.sh, pro_x2.sw) == (x.sb, x.sh, x.sw)
-            p.pro_x2 = pro_x2.t.data_ptr()
-        p.res = _lib.ptr(res)
-        p.res_scale = _lib.ptr(res_scale)
-        p.stats = _lib.ptr(stats)
-        p.stats_per_h = stats_per_h
-        y = out.t.data_ptr() + 4 * out_offset
-        # Algorithmic FLOPs (``useful``: the fraction of the kernel's taps that are not structural zeros).
-        flops = 2.0 * x.B * h_out * w_out * n_out * kh * kw * x.C * useful
-        if self._tc_eligible(x, p, prologue, out_offset):
-            if prologue == PRO_ADD:
-                # Fold the decoder skip connection into its input (consumed only here).
-                _lib.call("unblend_add", x.t.data_ptr(), pro_x2.t.data_ptr(), x.t.data_ptr(), x.t.numel(),
-                          x.t.numel(), 1.0)
-                p.prologue, p.pro_x2 = PRO_NONE, None
-            mode = _lib.TC_TF32X3 if self.precision == "fp32" else _lib.TC_BF16
-            if post is not None:
-                # post [h_out, n_final]: added per (output row, channel) after the activation.
-                p.post, p.post_sh = post.data_ptr(), post.shape[1]
-            p.y_bf16 = 1 if y_bf16 else 0
-            whi, wlo = self._tc_weight(w, mode)
-            bn256 = self._bn256_min[mode]
-            if mode == _lib.TC_BF16 and kw == 3 and sw == 1 and dw * 2 <= 8:
-                # 3-wide kernel rows: tiles of <= 192 columns share one A load across the three taps.
-                bn256 = 1 << 30
-            block_n = _block_n(n_out, bn256)
-            _lib.call("unblend_conv2d_tc", x.t.data_ptr(), whi.data_ptr(), _lib.ptr(wlo), _lib.ptr(b), y,
-                      ctypes_byref(p), mode, block_n, work=flops)
-            return
-        assert not y_bf16, "bf16 output needs the tensor-core path"
-        _lib.call("unblend_conv2d_f32", x.t.data_ptr(), w.data_ptr(), _lib.ptr(b), y, ctypes_byref(p), work=flops)
-        if post is not None:
-            # CUDA-core path: the same add as a separate pass over the dense output.
-            assert out_offset == 0 and out.sb == h_out * w_out * n_final and out.sw == n_final
-            table = post[:, None, :].expand(h_out, w_out, n_final).contiguous()
-            _lib.call("unblend_add", y, table.data_ptr(), y, out.B * table.numel(), table.numel(), 1.0)
-
-    def _tc_eligible(self, x: Act, p: ConvParams, prologue: int, out_offset: int) -> bool:
-        """Whether this convolution meets the tensor-core kernel's layout requirements."""
-        if self.precision == "fp32-simt" or prologue not in (PRO_NONE, PRO_ADD):
-            return False
-        if x.C % 8 or x.C < 16 or x.sw != x.C or x.sh % 4 or x.sb % 4:
-            return False
-        if p.sw != 1:
-            cap = x.sb // x.C
-            if not (p.sw == 4 and p.kw == 8 and p.pw == 2 and p.kh == 1 and x.H == 1 and x.sb % (4 * x.C) == 0
-                    and cap >= 4 * -(-x.W // 4) and (2 * x.C) % 32 == 0):
-                return False
-        if p.act == ACT_GLU and p.n_out % 4:
-            return False
-        return all(v % 4 == 0 for v in (p.n_group, p.out_sb, p.out_sh, p.out_sw, p.out_sg, out_offset))
-
-    def _tc_weight(self, w: torch.Tensor, mode: int) -> tuple[torch.Tensor, torch.Tensor | None]:
-        """Tensor-core copy of a packed weight: (hi, lo) TF32 split or (bf16, None), cached."""
-        key = (w.data_ptr(), tuple(w.shape), mode)
-        hit = self._tc_cache.get(key)
-        if hit is None:
-            flat = w.reshape(w.shape[0], -1)
-            hit = split_tf32(flat) if mode == _lib.TC_TF32X3 else (flat.to(torch.bfloat16).contiguous(), None)
-            self._tc_cache[key] = hit
-        return hit
-
-    def _stats(self, stats: torch.Tensor, groups: int, count: float) -> torch.Tensor:
-        out = torch.empty(2 * groups, device=stats.device, dtype=torch.float32)
-        _lib.call("unblend_stats_finalize", stats.data_ptr(), out.data_ptr(), groups, float(count), 1e-5, 0, 0)
-        return out
 
     def _dconv(self, x: Act, pre: str) -> None:
         """DConv residual branch in place (unblend/blocks.py:238-317)."""
@@ -935,9 +712,3 @@ class HTDemucsCuda(nn.Module):
                   tstats.data_ptr(), tabs["window"].data_ptr(), frames_buf.data_ptr(), out.data_ptr(), B, S, T,
                   nfft)
         return out
-
-
-def ctypes_byref(p: ConvParams):
-    import ctypes
-
-    return ctypes.byref(p)
