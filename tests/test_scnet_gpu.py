@@ -83,12 +83,13 @@ def test_real_dft_along_frames(T, c):
     y = torch.empty(5, K, 2 * c, device="cuda")
     _lib.call("unblend_rfft_time", x.data_ptr(), y.data_ptr(), 5, T, c)
     spec = torch.fft.rfft(x.double(), dim=1, norm="ortho")
-    assert rel_err(y, torch.cat([spec.real, spec.imag], dim=2)) < 2e-6
+    # Direct fp32 summation over T terms: a few 1e-6 of the RMS.
+    assert rel_err(y, torch.cat([spec.real, spec.imag], dim=2)) < 1e-5
     z = torch.empty(5, T, c, device="cuda")
     _lib.call("unblend_irfft_time", y.data_ptr(), z.data_ptr(), 5, K, c)
-    ref = torch.fft.irfft(torch.complex(y[..., :c], y[..., c:]).double(), dim=1, norm="ortho")
-    assert rel_err(z, ref) < 2e-6
-    assert rel_err(z, x) < 5e-6
+    ref = torch.fft.irfft(torch.complex(y[..., :c].double(), y[..., c:].double()), dim=1, norm="ortho")
+    assert rel_err(z, ref) < 1e-5
+    assert rel_err(z, x) < 1e-5
 
 
 @pytest.mark.parametrize("hid,d,steps,n_seq,freq_axis", [(32, 32, 9, 21, True), (128, 128, 57, 40, False),

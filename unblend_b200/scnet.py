@@ -64,9 +64,13 @@ class SCNetCuda(ConvNet):
         ``samplerate``, ``segment_samples`` and the constructor config of the
         registry entry (``unblend_b200.synth.scnet_config``).
     :param state_dict: Reference-layout weights (strict key set).
-    :param precision: ``"fp32"`` (3-pass TF32 tensor-core convolutions), ``"bf16"``
-        (bf16 tensor-core operands) or ``"fp32-simt"``. The LSTM recurrences, DFTs
-        and norms run in fp32 in every mode.
+    :param precision: ``"fp32"`` (every convolution on the fp32 CUDA-core kernel),
+        ``"bf16"`` (bf16 tensor-core operands, fp32 accumulation and activations) or
+        ``"fp32-simt"`` (same as ``"fp32"``). The LSTM recurrences, DFTs and norms
+        run in fp32 in every mode. SCNet has no LayerScale damping its residual
+        branches, so the few 1e-5 of output RMS that each 3-pass TF32 tensor-core
+        convolution leaves add up over its convolution stages (1.5e-4 of output
+        RMS on the xl configuration); fp32 therefore stays on CUDA cores.
     """
 
     def __init__(self, config: dict, state_dict: dict, precision: str = "fp32") -> None:
@@ -92,6 +96,10 @@ class SCNetCuda(ConvNet):
         self.dims = list(cfg["dims"])
         self._pack({k: v.detach().float().cpu() for k, v in state_dict.items()})
         self.__dict__["_win_cache"] = {}
+
+    def _tc_eligible(self, x: Act, p, prologue: int, out_offset: int) -> bool:
+        """Tensor cores for bf16 precision only (fp32 convolutions run on CUDA cores)."""
+        return self.precision == "bf16" and super()._tc_eligible(x, p, prologue, out_offset)
 
     # ------------------------------------------------------------------ contract
     def configure_inference(self, *, sources: list[str], samplerate: int, segment_samples: int) -> None:
@@ -272,7 +280,9 @@ class SCNetCuda(ConvNet):
         for i in range(self.config["num_dplayer"]):
             q = f"separation_net.dp_modules.{i}"
             self._lstm_path(x, q, 0, True)
+            self._trace(f"dp{i}_freq", x)
             self._lstm_path(x, q, 1, False)
+            self._trace(f"dp{i}_time", x)
             B, F, T, d = x.B, x.H, x.W, x.C
             if i % 2 == 0:
                 y = Act.freq(B, F, T // 2 + 1, 2 * d, dev)
@@ -284,6 +294,7 @@ class SCNetCuda(ConvNet):
                 _lib.call("unblend_irfft_time", x.t.data_ptr(), y.t.data_ptr(), B * F, T, c,
                           work=4.0 * B * F * c * T * 2 * (T - 1))
             x = y
+            self._trace(f"fc{i}", x)
         return x
 
     def _decode(self, x: Act, skip: Act, j: int, lengths: list[int], orig: list[int]) -> Act:
@@ -296,6 +307,7 @@ class SCNetCuda(ConvNet):
         y = x.like()
         self._conv(x, self.w(f"{q}.fuse.w"), self.w(f"{q}.fuse.b"), y, h_out=F, w_out=T, n_out=2 * C, kh=3, kw=3,
                    ph=1, pw=1, act=ACT_GLU)
+        self._trace(f"fuse{j}", y)
         cout = self.w(f"{q}.up0.b").shape[0]
         out = Act.freq(B, sum(orig), T, cout, dev)
         start = off = 0
@@ -319,6 +331,14 @@ class SCNetCuda(ConvNet):
         return out
 
     # ------------------------------------------------------------------ forward
+    #: When set to a dict, ``forward`` stores a CPU copy of every stage output in
+    #: the reference's [B, C, F, T] layout (debugging aid, slow).
+    trace: dict | None = None
+
+    def _trace(self, name: str, a: Act) -> None:
+        if self.trace is not None:
+            self.trace[name] = a.t.view(a.B, a.H, a.W, a.C).permute(0, 3, 1, 2).detach().cpu().clone()
+
     def forward(self, mix: torch.Tensor) -> torch.Tensor:
         """Separate ``mix`` [B, 2, L] into ``[B, S, 2, L]`` (unblend/scnet.py:746-800, 837-895)."""
         if mix.device.type != "cuda":
@@ -360,15 +380,20 @@ class SCNetCuda(ConvNet):
         x = Act.freq(B, Fq, T, 4, dev)
         pos = self.w("pos") if self.masked else None
         _lib.call("unblend_swap_axes", frames.data_ptr(), x.t.data_ptr(), _lib.ptr(pos), B, T, Fq, 1)
+        self._trace("spec", x)
         skips, lens, origs = [], [], []
         for i in range(len(self.dims) - 1):
             x, skip, lengths, orig = self._encode(x, i)
+            self._trace(f"enc{i}", x)
+            self._trace(f"skip{i}", skip)
             skips.append(skip)
             lens.append(lengths)
             origs.append(orig)
         x = self._trunk(x)
+        self._trace("trunk", x)
         for j in range(len(self.dims) - 1):
             x = self._decode(x, skips.pop(), j, lens.pop(), origs.pop())
+            self._trace(f"dec{j}", x)
         if self.masked:
             h = Act.freq(B, Fq, T, 64, dev)
             self._conv(x, self.w("mask0.w"), self.w("mask0.b"), h, h_out=Fq, w_out=T, n_out=64, kh=3, kw=3, ph=1,
@@ -379,10 +404,14 @@ class SCNetCuda(ConvNet):
             x = m
         per_stem = torch.empty(S, B, T, Fq, 4, device=dev, dtype=torch.float32)
         _lib.call("unblend_swap_axes", x.t.data_ptr(), per_stem.data_ptr(), None, B, Fq, T, S)
-        out = torch.empty(B, S, 2, L, device=dev, dtype=torch.float32)
+        # The inverse transform runs over the padded length (its frame count follows from the
+        # length), then the trailing padding is dropped (unblend/scnet.py:783-784).
+        full = torch.empty(B, S, 2, Lp, device=dev, dtype=torch.float32)
         fbuf = torch.empty(B * S * 2 * T * nfft, device=dev, dtype=torch.float32)
         _lib.call("unblend_istft_masked", frames.data_ptr() if self.masked else None, per_stem.data_ptr(),
-                  B * T * Fq * 4, win.data_ptr(), None, fbuf.data_ptr(), out.data_ptr(), B, S, 0, L, nfft, hop, 0)
+                  B * T * Fq * 4, win.data_ptr(), None, fbuf.data_ptr(), full.data_ptr(), B, S, 0, Lp, nfft, hop, 0)
+        out = torch.empty(B, S, 2, L, device=dev, dtype=torch.float32)
+        _lib.call("unblend_act_copy", full.data_ptr(), Lp, out.data_ptr(), L, B * S * 2, L, ACT_NONE)
         return out
 
     # ------------------------------------------------------------------ optional hooks (unblend/backends.py:62-111)
