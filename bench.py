@@ -56,6 +56,9 @@ CPU_SAMPLE_SECONDS = 30.0
 ROFORMER_TRACK_SECONDS = 300.0
 ROFORMER_BATCH = 16
 ROFORMER_SEGMENT = 352800  # 8 s at 44.1 kHz
+SCNET_BATCH = 8
+SIMT_KERNELS = ("unblend_lstm_recurrence", "unblend_conv2d_f32", "unblend_rfft_time", "unblend_irfft_time")
+FP32_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
 METRIC = "audio-sec separated/sec (×realtime), HTDemucs 44.1kHz stereo, 1/2/4/8 B200"
 
 
@@ -66,10 +69,12 @@ def _args():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--model", default="htdemucs", choices=["htdemucs", "htdemucs_6s", "bsroformer", "melband"],
+    ap.add_argument("--model", default="htdemucs",
+                    choices=["htdemucs", "htdemucs_6s", "bsroformer", "melband", "scnet", "scnet_xl"],
                     help="htdemucs: the headline workload; htdemucs_6s: 6-source HTDemucs (seed 2), bf16, "
                          "shifts=1, 240 s track; bsroformer: BS-RoFormer dim 512 depth 12, 8 s segments, batch 16, "
-                         "bf16, 300 s track")
+                         "bf16, 300 s track; scnet / scnet_xl: the registry scnet_small (masked, seed 9) / "
+                         "scnet_xl_wide_v5 (seed 10), 11 s segments, batch 8, 180 s track")
     ap.add_argument("--shifts", type=int, default=None, help="random-shift rounds per track")
     ap.add_argument("--stems", default=None,
                     help="comma-separated HTDemucs stems to materialise (default: vocals for htdemucs_6s, "
@@ -88,6 +93,11 @@ def _args():
     args = ap.parse_args()
     rof = args.model in ("bsroformer", "melband")
     six = args.model == "htdemucs_6s"
+    if args.model.startswith("scnet"):
+        if args.precision is None:
+            args.precision = "fp32"
+        if args.batch is None:
+            args.batch = SCNET_BATCH
     if args.precision is None:
         args.precision = "bf16" if rof or six else "fp32"
     if args.shifts is None:
@@ -234,6 +244,27 @@ def cpu_baseline_roformer(seconds: float = 8.0, mel: bool = False) -> dict:
             "sample": f"{name} oracle over a {seconds:.0f} s synthetic track (one 8 s segment), fp32"}
 
 
+def cpu_baseline_scnet(xl: bool = False) -> dict:
+    """The SCNet oracle (fp32 CPU restatement of the reference forward) over one 11 s segment."""
+    import torch
+
+    from oracle.scnet_oracle import scnet_forward
+    from unblend_b200.synth import scnet_config, scnet_state_dict, synth_track
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    cfg = scnet_config("scnet_xl_wide_v5" if xl else "scnet_small")
+    sd = scnet_state_dict(cfg, 10 if xl else 9)
+    seconds = cfg["segment_samples"] / cfg["samplerate"]
+    mix = synth_track(seconds, 1)[None]
+    t0 = time.perf_counter()
+    scnet_forward(sd, mix, cfg)
+    dt = time.perf_counter() - t0
+    name = "scnet_xl_wide_v5" if xl else "scnet_small"
+    return {"value": seconds / dt, "unit": "audio-s/s", "cores": cores, "kind": "port",
+            "sample": f"SCNet oracle ({name}) over one {seconds:g} s segment, fp32"}
+
+
 def run_reference(args) -> None:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -241,15 +272,23 @@ def run_reference(args) -> None:
         return
     rof = args.model in ("bsroformer", "melband")
     mel = args.model == "melband"
+    sc = args.model.startswith("scnet")
     vals = []
     # Each step is one bounded sample, the same one cpu_baseline times in the B200 arm.
     for _ in range(max(1, args.steps)):
-        vals.append(cpu_baseline_roformer(mel=mel) if rof else cpu_baseline(CPU_SAMPLE_SECONDS))
+        if sc:
+            vals.append(cpu_baseline_scnet(xl=args.model == "scnet_xl"))
+        else:
+            vals.append(cpu_baseline_roformer(mel=mel) if rof else cpu_baseline(CPU_SAMPLE_SECONDS))
     v = statistics.median(x["value"] for x in vals)
     base = dict(vals[0])
     base["value"] = v
-    work = (("Mel-Band RoFormer dim 384 depth 6 fp32 forward" if mel else "BS-RoFormer dim 512 depth 12 fp32 forward")
-            if rof else "HTDemucs 4-stem fp32 apply_model") + " on host cores (bounded sample)"
+    if sc:
+        work = f"SCNet ({args.model}) fp32 forward"
+    else:
+        work = (("Mel-Band RoFormer dim 384 depth 6 fp32 forward" if mel else "BS-RoFormer dim 512 depth 12 fp32 "
+                 "forward") if rof else "HTDemucs 4-stem fp32 apply_model")
+    work += " on host cores (bounded sample)"
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "audio-s/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
             "dtype": "f32", "data": "synthetic", "vs_baseline": None,
@@ -275,7 +314,16 @@ def main() -> None:
     world, rank, local = _dist()
     dev = torch.device("cuda", torch.cuda.current_device())
     rof = args.model in ("bsroformer", "melband")
-    if args.model == "melband":
+    sc = args.model.startswith("scnet")
+    if sc:
+        from unblend_b200.scnet import SCNetCuda
+        from unblend_b200.synth import scnet_config, scnet_state_dict
+
+        xl = args.model == "scnet_xl"
+        scfg = scnet_config("scnet_xl_wide_v5" if xl else "scnet_small")
+        model = SCNetCuda(scfg, scnet_state_dict(scfg, 10 if xl else 9), precision=args.precision).to(dev)
+        seg_len = scfg["segment_samples"]
+    elif args.model == "melband":
         from unblend_b200.roformer import MelBandRoformerCuda
         from unblend_b200.synth import melband_config, melband_state_dict
 
@@ -404,16 +452,26 @@ def main() -> None:
     peaks = _peaks()
     a = agg[top]
     tflops = a["work"] / (a["ms"] * 1e-3) / 1e12 if a["ms"] > 0 else 0.0
-    roofline = {"kernel": top, "bound": "tensor", "achieved": round(tflops, 3), "peak": peaks["bf16"],
-                "unit": "TFLOP/s", "frac": round(tflops / peaks["bf16"], 5),
-                "traffic": _traffic(f"{args.model}:{args.precision}:batch{batch}", top),
-                "traffic_unit": "bytes per launch (ncu capture, see profiles/traffic_per_launch.txt)",
-                "peak_source": f"{peaks['src']} bf16 dense ({peaks['kind']}: the kernel is timed inside a "
-                               "seconds-long run)",
-                "frac_of_burst_peak": round(tflops / peaks["bf16_burst"], 5),
-                "share_of_step": round(a["ms"] / sum(v["ms"] for v in agg.values()), 3),
-                "launches_per_step": a["n"]}
-    if args.precision == "fp32":
+    if top in SIMT_KERNELS:
+        # A CUDA-core fp32 kernel: against the nominal FMA rate (148 SMs x 128 FMA x 2 x 1.965 GHz).
+        roofline = {"kernel": top, "bound": "fp32-fma", "achieved": round(tflops, 3), "peak": FP32_NOMINAL_TFLOPS,
+                    "unit": "TFLOP/s", "frac": round(tflops / FP32_NOMINAL_TFLOPS, 5), "traffic": None,
+                    "peak_source": "nominal CUDA-core fp32 FMA rate (no measured figure for it)",
+                    "share_of_step": round(a["ms"] / sum(v["ms"] for v in agg.values()), 3),
+                    "launches_per_step": a["n"]}
+    else:
+        roofline = None
+    if roofline is None:
+        roofline = {"kernel": top, "bound": "tensor", "achieved": round(tflops, 3), "peak": peaks["bf16"],
+                    "unit": "TFLOP/s", "frac": round(tflops / peaks["bf16"], 5),
+                    "traffic": _traffic(f"{args.model}:{args.precision}:batch{batch}", top),
+                    "traffic_unit": "bytes per launch (ncu capture, see profiles/traffic_per_launch.txt)",
+                    "peak_source": f"{peaks['src']} bf16 dense ({peaks['kind']}: the kernel is timed inside a "
+                                   "seconds-long run)",
+                    "frac_of_burst_peak": round(tflops / peaks["bf16_burst"], 5),
+                    "share_of_step": round(a["ms"] / sum(v["ms"] for v in agg.values()), 3),
+                    "launches_per_step": a["n"]}
+    if args.precision == "fp32" and roofline["bound"] == "tensor":
         # fp32 accuracy costs three kind::tf32 MMAs per product, each at half the bf16 rate.
         roofline["peak_fp32_3xtf32"] = round(peaks["bf16"] / 6, 1)
         roofline["frac_of_fp32_3xtf32_peak"] = round(tflops / (peaks["bf16"] / 6), 4)
@@ -424,7 +482,11 @@ def main() -> None:
     L = track.shape[-1]
     n_seg = len(range(0, L, int(0.75 * seg_len)))
     dtype = {"fp32": "f32", "bf16": "bf16", "fp32-simt": "f32"}[args.precision]
-    if rof:
+    if sc:
+        work = (f"SCNet {'scnet_xl_wide_v5 (seed 10)' if args.model == 'scnet_xl' else 'scnet_small, masked (seed 9)'}, "
+                f"{seconds:g} s stereo track, {n_seg} segments of 11 s, overlap 0.25, {batch} segments per launch, "
+                f"precision {args.precision}")
+    elif rof:
         name = ("Mel-Band RoFormer dim 384 depth 6, 60 mel bands (kim config, seed 6)" if args.model == "melband"
                 else "BS-RoFormer dim 512 depth 12 (seed 3)")
         work = (f"{name}, {seconds:g} s stereo track, {n_seg} segments of 8 s, "
@@ -453,7 +515,10 @@ def main() -> None:
             "gpu_launches": launches, "roofline": roofline, "clocks": clk, "split": phases,
             "kernels": {k: {"ms": round(v["ms"], 3), "n": v["n"]} for k, v in sorted(agg.items(), key=lambda kv: -kv[1]["ms"])}}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline_roformer(mel=args.model == "melband") if rof else cpu_baseline()
+        if sc:
+            line["cpu_baseline"] = cpu_baseline_scnet(xl=args.model == "scnet_xl")
+        else:
+            line["cpu_baseline"] = cpu_baseline_roformer(mel=args.model == "melband") if rof else cpu_baseline()
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
