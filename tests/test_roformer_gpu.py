@@ -365,10 +365,15 @@ def test_batch_rows_are_independent():
 
 @pytest.mark.parametrize("axis", [0, 1])
 @pytest.mark.parametrize("out_bf16", [1, 0])
-def test_attention_bf16_axial_gate(axis, out_bf16):
-    """Persistent bf16 attention (no rotary: Q and K arrive rotated) against a float64 reference."""
+@pytest.mark.parametrize("hd", [64, 48])
+def test_attention_bf16_axial_gate(axis, out_bf16, hd):
+    """Persistent bf16 attention (no rotary: Q and K arrive rotated) against a float64 reference.
+
+    48-dim heads (HTDemucs-6s, dim 384 over 8 heads) load 64-dim boxes that
+    overlap the next head (zero fill past the last); only the head's own dims
+    enter the products."""
     torch.manual_seed(8)
-    B, T, nb, H, hd = 2, 300, 13, 4, 64
+    B, T, nb, H = 2, 300, 13, 4
     inner = H * hd
     qkv = torch.randn(B, T, nb, 3 * inner, device="cuda").to(torch.bfloat16)
     gates = torch.rand(B, T, nb, H, device="cuda")

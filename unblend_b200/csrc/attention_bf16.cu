@@ -1,10 +1,14 @@
-// Persistent bf16 flash attention on the tcgen05 tensor cores (head dim 64).
+// Persistent bf16 flash attention on the tcgen05 tensor cores (head dim 48 or 64).
 //
 // softmax(Q K^T * scale) V per (sequence, head) for BS-RoFormer's axial
 // attention (unblend/roformer.py:478-511, 1135-1159) on the bf16 path. Q, K and
 // V are bf16 in HBM (the QKV projection writes them, with the rotary rotation
 // already applied), addressed like unblend_attention_tc2 through 5-D tensor
-// maps (dim, head, row, inner batch, outer batch).
+// maps (head span, row, inner batch, outer batch): every Q / K / V load is a box
+// of 64 dims (one 128-byte swizzled row per key or query) starting at the
+// head's first dim, so a 48-dim head's box also holds 16 dims of the next head
+// (or zero fill past the last one), which no MMA reads: S = Q K^T runs
+// HD / 16 K-steps and O = P V has N = HD.
 //
 // Work is a flat stream of (unit, key tile) pairs, a unit being 128 queries of
 // one head of one sequence; each CTA walks its units in a grid-stride loop,
@@ -35,7 +39,7 @@ using namespace ub::tc;
 
 constexpr int BQ = 128;
 constexpr int BK = 64;
-constexpr int HD = 64;
+constexpr int BOX = 64;  // dims per load (128-byte rows)
 constexpr int NT = 320;
 constexpr int STAGES = 3;
 constexpr int Q_BYTES = BQ * 128;  // 128 rows x 64 bf16
@@ -112,6 +116,7 @@ __device__ __forceinline__ void transpose_v(uint32_t v, uint32_t vt, int w, int 
   }
 }
 
+template <int HD>
 __global__ void __launch_bounds__(NT, 2)
     attention_bf16_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapK,
                           const __grid_constant__ CUtensorMap mapV, const __grid_constant__ Args a) {
@@ -172,7 +177,7 @@ __global__ void __launch_bounds__(NT, 2)
             break;
           }
           mbar_expect_tx(&q_full[qb], Q_BYTES);
-          tma_load_5d(sQ + qb * Q_BYTES, &mapQ, &q_full[qb], 0, un.h, un.qt * BQ, un.bi, un.bo);
+          tma_load_4d(sQ + qb * Q_BYTES, &mapQ, &q_full[qb], un.h * HD, un.qt * BQ, un.bi, un.bo);
         }
         const int s = gt % STAGES, r = gt / STAGES;
         if (r > 0 && !mbar_wait(&kv_free[s], (r - 1) & 1)) {
@@ -181,14 +186,15 @@ __global__ void __launch_bounds__(NT, 2)
         }
         uint8_t* st = sKV + s * STAGE;
         mbar_expect_tx(&kv_full[s], 2 * T_BYTES);
-        tma_load_5d(st + K_OFF, &mapK, &kv_full[s], 0, un.h, j * BK, un.bi, un.bo);
-        tma_load_5d(st + V_OFF, &mapV, &kv_full[s], 0, un.h, j * BK, un.bi, un.bo);
+        tma_load_4d(st + K_OFF, &mapK, &kv_full[s], un.h * HD, j * BK, un.bi, un.bo);
+        tma_load_4d(st + V_OFF, &mapV, &kv_full[s], un.h * HD, j * BK, un.bi, un.bo);
       }
       if (!ok) atomicExch(&g_error_flag, 5);
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = instr_desc(1u, 64u);  // bf16 x bf16 -> fp32, M = 128, N = 64
+      constexpr uint32_t idesc = instr_desc(1u, 64u);        // S = Q K^T: M = 128, N = 64 keys
+      constexpr uint32_t idesc_pv = instr_desc(1u, (uint32_t)HD);  // O = P V: N = HD dims
       bool ok = true;
       auto issue_s = [&](int gt) -> bool {
         const int i = gt / nkv, j = gt - (gt / nkv) * nkv;
@@ -200,7 +206,7 @@ __global__ void __launch_bounds__(NT, 2)
         const uint32_t k = smem_u32(sKV + s * STAGE + K_OFF);
         const uint32_t d = tmem + S_COL + (gt & 1) * 64;
 #pragma unroll
-        for (int ks = 0; ks < 4; ++ks)
+        for (int ks = 0; ks < HD / 16; ++ks)  // 16 head dims per MMA
           umma_bf16(d, smem_desc(q + 32 * ks, 128), smem_desc(k + 32 * ks, 128), idesc, ks > 0 ? 1u : 0u);
         umma_commit(&s_full[gt & 1]);
         if (j == nkv - 1) umma_commit(&q_free[i & 1]);
@@ -229,7 +235,7 @@ __global__ void __launch_bounds__(NT, 2)
         const uint32_t o = tmem + O_COL + ob * 64;
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks)  // 16 keys per MMA: 8 TMEM columns of bf16 pairs
-          umma_bf16_ts(o, p + 8 * ks, smem_desc(vt + 32 * ks, 128), idesc, (j > 0 || ks > 0) ? 1u : 0u);
+          umma_bf16_ts(o, p + 8 * ks, smem_desc(vt + 32 * ks, 128), idesc_pv, (j > 0 || ks > 0) ? 1u : 0u);
         umma_commit(&kv_free[s]);
         umma_commit(o_done);
       }
@@ -354,7 +360,7 @@ __global__ void __launch_bounds__(NT, 2)
           if (a.o_bf16) {
             uint4* out = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.o) + off);
 #pragma unroll
-            for (int d8 = 0; d8 < 8; ++d8) {
+            for (int d8 = 0; d8 < HD / 8; ++d8) {
               uint32_t w4[4];
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
@@ -369,7 +375,7 @@ __global__ void __launch_bounds__(NT, 2)
           } else {
             float4* out = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.o) + off);
 #pragma unroll
-            for (int d4 = 0; d4 < 16; ++d4) {
+            for (int d4 = 0; d4 < HD / 4; ++d4) {
               const int d = d4 * 4;
               const uint32_t* src = d < 32 ? &o0[d] : &o1[d - 32];
               out[d4] = make_float4(__uint_as_float(src[0]) * inv, __uint_as_float(src[1]) * inv,
@@ -401,16 +407,16 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-bool head_map(CUtensorMap* m, const void* base, int heads, int rows, int inner, int outer, long long row_stride,
+// (head span, row, inner, outer) map of one of Q / K / V: `span` = heads * hd dims per row.
+bool head_map(CUtensorMap* m, const void* base, int span, int rows, int inner, int outer, long long row_stride,
               long long inner_stride, long long outer_stride, int box_rows) {
   auto fn = encode_fn();
   if (!fn) return false;
-  cuuint64_t dims[5] = {(cuuint64_t)HD, (cuuint64_t)heads, (cuuint64_t)rows, (cuuint64_t)inner, (cuuint64_t)outer};
-  cuuint64_t strides[4] = {(cuuint64_t)HD * 2, (cuuint64_t)row_stride * 2, (cuuint64_t)inner_stride * 2,
-                           (cuuint64_t)outer_stride * 2};
-  cuuint32_t box[5] = {HD, 1, (cuuint32_t)box_rows, 1, 1};
-  cuuint32_t es[5] = {1, 1, 1, 1, 1};
-  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(base), dims, strides, box, es,
+  cuuint64_t dims[4] = {(cuuint64_t)span, (cuuint64_t)rows, (cuuint64_t)inner, (cuuint64_t)outer};
+  cuuint64_t strides[3] = {(cuuint64_t)row_stride * 2, (cuuint64_t)inner_stride * 2, (cuuint64_t)outer_stride * 2};
+  cuuint32_t box[4] = {BOX, (cuuint32_t)box_rows, 1, 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, es,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -429,7 +435,7 @@ int sm_count() {
 extern "C" int unblend_attention_bf16(const void* q, const void* k, const void* v, const UnblendAttnParams* p,
                                       void* stream) {
   UB_REQUIRE(q && k && v && p && p->out);
-  UB_REQUIRE(p->outer > 0 && p->inner > 0 && p->heads > 0 && p->lq > 0 && p->lk > 0 && p->hd == HD);
+  UB_REQUIRE(p->outer > 0 && p->inner > 0 && p->heads > 0 && p->lq > 0 && p->lk > 0 && (p->hd == 48 || p->hd == 64));
   UB_REQUIRE(p->rope == nullptr);  // rotary is applied by the producer of Q and K on this path
   const long long q_so = legal_stride(p->q_so, p->outer), q_si = legal_stride(p->q_si, p->inner);
   const long long kv_so = legal_stride(p->kv_so, p->outer), kv_si = legal_stride(p->kv_si, p->inner);
@@ -439,10 +445,13 @@ extern "C" int unblend_attention_bf16(const void* q, const void* k, const void* 
   UB_REQUIRE(p->o_sr % 8 == 0 && p->o_so % 8 == 0 && p->o_si % 8 == 0);
   UB_REQUIRE((reinterpret_cast<uintptr_t>(q) & 15) == 0 && (reinterpret_cast<uintptr_t>(k) & 15) == 0 &&
              (reinterpret_cast<uintptr_t>(v) & 15) == 0 && (reinterpret_cast<uintptr_t>(p->out) & 15) == 0);
+  // Row strides must cover the head span (the tensor maps bound each row to it).
+  const int span = p->heads * p->hd;
+  UB_REQUIRE(p->q_sr >= span && p->kv_sr >= span && p->o_sr >= span);
   CUtensorMap mq, mk, mv;
-  if (!head_map(&mq, q, p->heads, p->lq, p->inner, p->outer, p->q_sr, q_si, q_so, BQ) ||
-      !head_map(&mk, k, p->heads, p->lk, p->inner, p->outer, p->kv_sr, kv_si, kv_so, BK) ||
-      !head_map(&mv, v, p->heads, p->lk, p->inner, p->outer, p->kv_sr, kv_si, kv_so, BK))
+  if (!head_map(&mq, q, span, p->lq, p->inner, p->outer, p->q_sr, q_si, q_so, BQ) ||
+      !head_map(&mk, k, span, p->lk, p->inner, p->outer, p->kv_sr, kv_si, kv_so, BK) ||
+      !head_map(&mv, v, span, p->lk, p->inner, p->outer, p->kv_sr, kv_si, kv_so, BK))
     return UNBLEND_ERR_INVALID;
   Args a{};
   a.heads = p->heads;
@@ -464,13 +473,14 @@ extern "C" int unblend_attention_bf16(const void* q, const void* k, const void* 
   a.g_si = p->g_si;
   a.g_sr = p->g_sr;
   a.c = p->scale * 1.4426950408889634f;
-  cudaFuncSetAttribute(attention_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+  auto kern = p->hd == 48 ? attention_bf16_kernel<48> : attention_bf16_kernel<64>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
   // Persistent, two CTAs per SM (96 registers x 320 threads and ~105 KB of
   // shared memory each). The occupancy query answers 1 here, but two co-resident
   // CTAs were measured 1.4x faster on the 801-frame RoFormer sequences.
   long long grid = 2LL * sm_count();
   if (grid > units) grid = units;
-  attention_bf16_kernel<<<(unsigned)grid, NT, SMEM, ub::as_stream(stream)>>>(mq, mk, mv, a);
+  kern<<<(unsigned)grid, NT, SMEM, ub::as_stream(stream)>>>(mq, mk, mv, a);
   UB_CHECK_LAUNCH();
   return 0;
 }

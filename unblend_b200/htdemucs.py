@@ -400,7 +400,7 @@ class HTDemucsCuda(ConvNet):
 
     def _attn_bf16(self, hd: int, D: int) -> bool:
         """Whether a transformer layer's projections go straight to the bf16 attention kernel."""
-        return self.precision == "bf16" and hd == 64 and D % 32 == 0
+        return self.precision == "bf16" and hd in (48, 64) and D % 32 == 0
 
     def _attention(self, qbuf: torch.Tensor, q_off: int, kvbuf: torch.Tensor, k_off: int, v_off: int, o: int,
                    B: int, heads: int, L: int, Lk: int, hd: int, q_sb: int, q_sr: int, kv_sb: int, kv_sr: int,
@@ -414,7 +414,7 @@ class HTDemucsCuda(ConvNet):
         """
         work = 4.0 * B * L * Lk * hd * heads
         scale = 1.0 / math.sqrt(hd)
-        if qbuf.dtype == torch.bfloat16 or (self.precision == "bf16" and hd == 64 and o % 16 == 0 and
+        if qbuf.dtype == torch.bfloat16 or (self.precision == "bf16" and hd in (48, 64) and o % 16 == 0 and
                                             all(v % 8 == 0 for v in (q_off, k_off, v_off, q_sb, q_sr, kv_sb,
                                                                      kv_sr, o_sb, o_sr))):
             if qbuf.dtype == torch.bfloat16:  # projections already rounded by their epilogue
