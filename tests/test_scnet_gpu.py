@@ -92,8 +92,12 @@ def test_real_dft_along_frames(T, c):
     assert rel_err(z, x) < 1e-5
 
 
+# Hidden sizes up to 256 run the cluster kernel: one cluster (17, 21, 40 sequences), several
+# with a ragged last one (300, 2400, 4700; the last two take eight sequences per thread).
 @pytest.mark.parametrize("hid,d,steps,n_seq,freq_axis", [(32, 32, 9, 21, True), (128, 128, 57, 40, False),
-                                                         (256, 256, 30, 17, True), (512, 256, 12, 9, False)])
+                                                         (256, 256, 30, 17, True), (512, 256, 12, 9, False),
+                                                         (256, 128, 5, 300, False), (128, 64, 4, 2400, True),
+                                                         (64, 32, 3, 4700, False)])
 def test_lstm_recurrence_both_directions(hid, d, steps, n_seq, freq_axis):
     torch.manual_seed(hid)
     lstm = torch.nn.LSTM(d, hid, bidirectional=True)

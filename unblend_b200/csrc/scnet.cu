@@ -13,7 +13,9 @@
 //                   band, transposed-conv trims, the mask head's tanh)
 //   rfft_time / irfft_time   FeatureConversion: orthonormal real DFT along frames
 //   lstm_recurrence the bidirectional LSTM recurrence of DualPathRNN (input
-//                   projections precomputed by a GEMM)
+//                   projections precomputed by a GEMM): a thread-block cluster per 64
+//                   sequences and direction with W_hh resident in shared memory for
+//                   hidden sizes up to 256, W_hh streamed from L2 for 512
 #include <math.h>
 
 #include "common.cuh"
@@ -317,6 +319,201 @@ __global__ void __launch_bounds__(256) lstm_recurrence_kernel(const float* __res
   }
 }
 
+// Cluster form for hid = 32 * Q <= 256: a cluster of Q CTAs runs one direction of
+// G = 8 * SG sequences. CTA r of the cluster owns hidden units [32 r, 32 r + 32): their
+// four gate columns of W_hh^T stay in shared memory for the whole launch (as float4
+// [k][unit] = gates i, f, g, o), and every CTA keeps the h of all G sequences ([k][seq],
+// double-buffered). A warp covers 8 units x 4 sequence groups of SG: per k it reads one
+// float4 of W per unit (8 distinct addresses) and SG / 4 float4 of h per group (4
+// distinct), both one shared-memory wavefront, for 4 SG FMAs per thread. After the k loop
+// a thread updates c and h of its unit for its SG sequences, stores h and pushes it into
+// the h buffer of every CTA of the cluster (distributed shared memory); one cluster
+// barrier per step publishes the new h before any CTA reads it, and no CTA writes a
+// buffer another may still read (step t + 1 writes the buffer read in step t, which
+// every CTA finished before the barrier). The next step's input projections are loaded
+// into registers before the k loop, so their latency hides behind it.
+// Shared memory: 4 (128 hid + 16 SG hid) bytes.
+__device__ __forceinline__ uint32_t cluster_rank_u32() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void st_cluster_v4(uint32_t local_addr, uint32_t rank, float4 v) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(remote), "f"(v.x), "f"(v.y), "f"(v.z),
+               "f"(v.w)
+               : "memory");
+}
+
+__device__ __forceinline__ float sigmoid_f(float v) { return 1.0f / (1.0f + expf(-v)); }
+
+// acc[q][g] += w.q * h[g] for the four gates q and SG sequences g.
+template <int SG>
+__device__ __forceinline__ void lstm_fma4(float (&acc)[4][SG], const float4 w, const float4 (&h)[SG / 4]) {
+#pragma unroll
+  for (int h4 = 0; h4 < SG / 4; ++h4) {
+    const float hv[4] = {h[h4].x, h[h4].y, h[h4].z, h[h4].w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int g = 4 * h4 + e;
+      acc[0][g] = fmaf(w.x, hv[e], acc[0][g]);
+      acc[1][g] = fmaf(w.y, hv[e], acc[1][g]);
+      acc[2][g] = fmaf(w.z, hv[e], acc[2][g]);
+      acc[3][g] = fmaf(w.w, hv[e], acc[3][g]);
+    }
+  }
+}
+
+template <int Q, int SG>
+__global__ void __launch_bounds__(256, 1) lstm_cluster_kernel(const float* __restrict__ xp,
+                                                              const float* __restrict__ whh_t,
+                                                              float* __restrict__ h_out, int n_seq, int steps,
+                                                              int inner, long long outer_stride,
+                                                              long long inner_stride, long long step_stride) {
+  static_assert(SG == 4 || SG == 8, "four or eight sequences per thread");
+  constexpr int HID = 32 * Q, G = 8 * SG, KU = SG == 4 ? 4 : 2;
+  static_assert(HID % (2 * KU) == 0, "whole chunk pairs");
+  extern __shared__ __align__(16) float sm[];
+  float4* ws = reinterpret_cast<float4*>(sm);  // [HID][32]: (i, f, g, o) of this CTA's units
+  float* hb = sm + HID * 128;                   // [2][HID][G]
+  const uint32_t rank = cluster_rank_u32();
+  const int dir = blockIdx.y;
+  const int cluster = blockIdx.x / Q;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int ul = (warp & 3) * 8 + (lane & 7);        // unit within the CTA
+  const int sbase = ((warp >> 2) * 4 + (lane >> 3)) * SG;  // first sequence within the cluster
+  const int unit = 32 * (int)rank + ul;
+  const float* w = whh_t + (long long)dir * HID * 4 * HID;
+  for (int i = threadIdx.x; i < HID * 128; i += 256) {
+    const int k = i >> 7, r = i & 127, u = r >> 2, q = r & 3;
+    sm[i] = __ldg(w + (long long)k * 4 * HID + q * HID + 32 * (int)rank + u);
+  }
+  for (int i = threadIdx.x; i < HID * G; i += 256) hb[i] = 0.f;
+  long long rowb[SG];
+  bool live[SG];
+#pragma unroll
+  for (int g = 0; g < SG; ++g) {
+    const int s = cluster * G + sbase + g;
+    live[g] = s < n_seq;
+    const int sq = live[g] ? s : 0;
+    rowb[g] = (long long)(sq / inner) * outer_stride + (long long)(sq % inner) * inner_stride;
+  }
+  float cst[SG];
+#pragma unroll
+  for (int g = 0; g < SG; ++g) cst[g] = 0.f;
+  const long long xs = 8LL * HID, hs = 2LL * HID;
+  const float* xcol = xp + dir * 4LL * HID + unit;
+  float nx[4][SG];
+  {
+    const int step0 = dir == 0 ? 0 : steps - 1;
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+#pragma unroll
+      for (int g = 0; g < SG; ++g) nx[q][g] = live[g] ? __ldg(xcol + (rowb[g] + step0 * step_stride) * xs + q * HID) : 0.f;
+  }
+  // Every CTA's buffers are zeroed (and its W slice loaded) before any CTA pushes h.
+  cluster_sync_all();
+  for (int it = 0; it < steps; ++it) {
+    const int step = dir == 0 ? it : steps - 1 - it;
+    const float* hcur = hb + (it & 1) * HID * G + sbase;
+    float* hnext = hb + ((it + 1) & 1) * HID * G;
+    float acc[4][SG];
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+#pragma unroll
+      for (int g = 0; g < SG; ++g) acc[q][g] = nx[q][g];
+    if (it + 1 < steps) {
+      const int sn = dir == 0 ? it + 1 : steps - 2 - it;
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int g = 0; g < SG; ++g)
+          nx[q][g] = live[g] ? __ldg(xcol + (rowb[g] + sn * step_stride) * xs + q * HID) : 0.f;
+    }
+    // k in chunks of KU, the shared-memory operands of the next chunk loaded into
+    // registers while the current one is multiplied (two warps per scheduler cannot hide
+    // the load latency otherwise).
+    float4 wr0[KU], wr1[KU], hr0[KU][SG / 4], hr1[KU][SG / 4];
+#pragma unroll
+    for (int j = 0; j < KU; ++j) {
+      wr0[j] = ws[j * 32 + ul];
+#pragma unroll
+      for (int h4 = 0; h4 < SG / 4; ++h4) hr0[j][h4] = *reinterpret_cast<const float4*>(hcur + j * G + 4 * h4);
+    }
+    for (int kc = 0; kc < HID; kc += 2 * KU) {
+#pragma unroll
+      for (int j = 0; j < KU; ++j) {
+        wr1[j] = ws[(kc + KU + j) * 32 + ul];
+#pragma unroll
+        for (int h4 = 0; h4 < SG / 4; ++h4)
+          hr1[j][h4] = *reinterpret_cast<const float4*>(hcur + (kc + KU + j) * G + 4 * h4);
+      }
+#pragma unroll
+      for (int j = 0; j < KU; ++j) lstm_fma4<SG>(acc, wr0[j], hr0[j]);
+      if (kc + 2 * KU < HID) {
+#pragma unroll
+        for (int j = 0; j < KU; ++j) {
+          wr0[j] = ws[(kc + 2 * KU + j) * 32 + ul];
+#pragma unroll
+          for (int h4 = 0; h4 < SG / 4; ++h4)
+            hr0[j][h4] = *reinterpret_cast<const float4*>(hcur + (kc + 2 * KU + j) * G + 4 * h4);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < KU; ++j) lstm_fma4<SG>(acc, wr1[j], hr1[j]);
+    }
+    float hn[SG];
+#pragma unroll
+    for (int g = 0; g < SG; ++g) {
+      const float ig = sigmoid_f(acc[0][g]);
+      const float fg = sigmoid_f(acc[1][g]);
+      const float gg = tanhf(acc[2][g]);
+      const float og = sigmoid_f(acc[3][g]);
+      cst[g] = fg * cst[g] + ig * gg;
+      hn[g] = og * tanhf(cst[g]);
+      if (live[g]) h_out[(rowb[g] + step * step_stride) * hs + dir * (long long)HID + unit] = hn[g];
+    }
+    const uint32_t dst = static_cast<uint32_t>(__cvta_generic_to_shared(hnext + unit * G + sbase));
+#pragma unroll
+    for (int r = 0; r < Q; ++r)
+#pragma unroll
+      for (int g4 = 0; g4 < SG; g4 += 4)
+        st_cluster_v4(dst + 4 * g4, (uint32_t)r, make_float4(hn[g4], hn[g4 + 1], hn[g4 + 2], hn[g4 + 3]));
+    cluster_sync_all();
+  }
+}
+
+template <int Q, int SG>
+cudaError_t launch_lstm_cluster(const float* xp, const float* whh_t, float* h_out, int n_seq, int steps, int inner,
+                                long long outer_stride, long long inner_stride, long long step_stride,
+                                cudaStream_t st) {
+  constexpr int HID = 32 * Q, G = 8 * SG;
+  const size_t smem = sizeof(float) * ((size_t)HID * 128 + 2 * (size_t)HID * G);
+  cudaError_t e = cudaFuncSetAttribute(lstm_cluster_kernel<Q, SG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((n_seq + G - 1) / G) * Q, 2, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = Q;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, lstm_cluster_kernel<Q, SG>, xp, whh_t, h_out, n_seq, steps, inner, outer_stride,
+                            inner_stride, step_stride);
+}
+
 }  // namespace
 
 extern "C" int unblend_pad_tail(const float* x, float* y, int rows, long long n_in, long long n_out, void* stream) {
@@ -388,13 +585,31 @@ extern "C" int unblend_lstm_recurrence(const float* xp, const float* whh_t, floa
                                        long long step_stride, void* stream) {
   UB_REQUIRE(xp && whh_t && h_out && n_seq > 0 && steps > 0 && inner > 0);
   UB_REQUIRE(hid == 32 || hid == 64 || hid == 128 || hid == 256 || hid == 512);
+  cudaStream_t st = ub::as_stream(stream);
+  if (hid <= 256) {
+    // A cluster of hid / 32 CTAs per 8 SG sequences and direction. Eight sequences per
+    // thread halve the shared-memory reads of h per FMA; four keep more SMs busy when the
+    // pass has few sequences (and are the only fit in shared memory at hid 256).
+    const int q = hid / 32;
+    const long long ctas8 = 2LL * q * ((n_seq + 63) / 64);
+    const bool sg8 = hid < 256 && ctas8 >= 2 * 148;
+    using Launch = cudaError_t (*)(const float*, const float*, float*, int, int, int, long long, long long, long long,
+                                   cudaStream_t);
+    const Launch launch = q == 1   ? (sg8 ? launch_lstm_cluster<1, 8> : launch_lstm_cluster<1, 4>)
+                          : q == 2 ? (sg8 ? launch_lstm_cluster<2, 8> : launch_lstm_cluster<2, 4>)
+                          : q == 4 ? (sg8 ? launch_lstm_cluster<4, 8> : launch_lstm_cluster<4, 4>)
+                                   : launch_lstm_cluster<8, 4>;
+    const cudaError_t e = launch(xp, whh_t, h_out, n_seq, steps, inner, outer_stride, inner_stride, step_stride, st);
+    if (e != cudaSuccess) return (int)e;
+    UB_CHECK_LAUNCH();
+    return 0;
+  }
   constexpr int G = 8;
   const int tpp = hid < 256 ? hid : 256;
   const int parts = 256 / tpp;
   const int per_block = parts * G;
   const unsigned blocks = (unsigned)((n_seq + per_block - 1) / per_block);
   const size_t smem = sizeof(float) * 2 * (size_t)parts * hid * G;
-  cudaStream_t st = ub::as_stream(stream);
   if (hid <= 256) {
     cudaFuncSetAttribute(lstm_recurrence_kernel<G, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     lstm_recurrence_kernel<G, 1><<<dim3(blocks, 2), 256, smem, st>>>(xp, whh_t, h_out, n_seq, steps, hid, inner,

@@ -36,6 +36,10 @@ __global__ void gather_chunks_kernel(const float* __restrict__ track, int channe
   }
 }
 
+// acc[r, p] += w(j) y[k, r, trim_k + j] and sum_w[p] += w(j) over the chunks k holding p, in
+// chunk order, each product rounded before its addition: the per-chunk accumulation of
+// unblend/apply.py:1214-1238 in the same order, so the result does not depend on how the
+// chunks were split into batches.
 __global__ void overlap_add_kernel(const float* __restrict__ y, int n, int rows, int seg,
                                    const long long* __restrict__ offsets, long long length, long long lo,
                                    long long span, float power, float* __restrict__ acc,
@@ -55,7 +59,7 @@ __global__ void overlap_add_kernel(const float* __restrict__ y, int n, int rows,
       if (__ldg(offsets + mid) > p - seg) k1 = mid;
       else k0 = mid + 1;
     }
-    float a = 0.f, ws = 0.f;
+    float a = acc[(long long)r * length + p], ws = r == 0 ? sum_w[p] : 0.f;
     for (int k = k0; k < n; ++k) {
       const long long o = __ldg(offsets + k);
       if (o > p) break;
@@ -64,11 +68,11 @@ __global__ void overlap_add_kernel(const float* __restrict__ y, int n, int rows,
       if (j >= len) continue;
       const int trim = (int)((seg - len) / 2);
       const float w = split_weight((int)j, seg, power);
-      a += y[((long long)k * rows + r) * seg + trim + j] * w;
-      ws += w;
+      a = __fadd_rn(a, __fmul_rn(w, y[((long long)k * rows + r) * seg + trim + j]));
+      ws = __fadd_rn(ws, w);
     }
-    acc[(long long)r * length + p] += a;
-    if (r == 0) sum_w[p] += ws;
+    acc[(long long)r * length + p] = a;
+    if (r == 0) sum_w[p] = ws;
   }
 }
 
