@@ -124,3 +124,27 @@ def test_host_split_weight_is_the_powered_triangle(power):
     w = _split_weight_host(7, power)
     tri = torch.tensor([1, 2, 3, 4, 3, 2, 1], dtype=torch.float32)
     assert torch.allclose(w, (tri / 4) ** power)
+
+
+def test_free_memory_query_is_reused_and_corrected(monkeypatch):
+    """The residency budget re-queries cudaMemGetInfo at most once a second per device and
+    corrects a cached answer by what this process reserved since."""
+    from unblend_b200 import apply as eng
+
+    state = {"queries": 0, "reserved": 1000, "now": 50.0}
+
+    def fake_info(idx):
+        state["queries"] += 1
+        return 10_000, 80_000
+
+    monkeypatch.setattr(eng.torch.cuda, "mem_get_info", fake_info)
+    monkeypatch.setattr(eng.torch.cuda, "memory_reserved", lambda idx=None: state["reserved"])
+    monkeypatch.setattr(eng.time, "monotonic", lambda: state["now"])
+    monkeypatch.setattr(eng, "_FREE_QUERY", {})
+    dev = torch.device("cuda", 3)
+    assert eng._free_device_bytes(dev) == 10_000 and state["queries"] == 1
+    state["reserved"] = 4000  # this process reserved 3000 more bytes
+    state["now"] += 0.5
+    assert eng._free_device_bytes(dev) == 7_000 and state["queries"] == 1
+    state["now"] += 0.6  # the cached answer is older than a second: query again
+    assert eng._free_device_bytes(dev) == 10_000 and state["queries"] == 2

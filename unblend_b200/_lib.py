@@ -158,7 +158,7 @@ _HOST_SIGNATURES = {
     "unblend_dconv_error_flag": [ctypes.POINTER(c_int), c_int],
 }
 
-TC_TF32X3, TC_BF16 = 0, 1
+TC_TF32X3, TC_BF16, TC_BF16X3 = 0, 1, 2
 
 _lib = None
 

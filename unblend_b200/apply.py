@@ -19,6 +19,7 @@ from __future__ import annotations
 
 import math
 import random
+import time
 from numbers import Real
 from typing import Any, Callable
 
@@ -139,10 +140,31 @@ _GPU_ACCUM_VRAM_FRACTION = 0.3
 _GPU_ACCUM_VRAM_RESERVE_BYTES = 2 * 1024**3
 
 
+# Free device memory as last queried per device: (time, free bytes, this process's
+# reserved bytes then). cudaMemGetInfo costs milliseconds per call on this driver,
+# so a query younger than _FREE_QUERY_MAX_AGE_S is reused, corrected by what this
+# process's allocator reserved or released since (other processes' changes within
+# that window are not seen).
+_FREE_QUERY: dict[int, tuple[float, int, int]] = {}
+_FREE_QUERY_MAX_AGE_S = 1.0
+
+
+def _free_device_bytes(device: torch.device) -> int:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    now = time.monotonic()
+    reserved = torch.cuda.memory_reserved(idx)
+    hit = _FREE_QUERY.get(idx)
+    if hit is not None and now - hit[0] < _FREE_QUERY_MAX_AGE_S:
+        return max(0, hit[1] - (reserved - hit[2]))
+    free, _ = torch.cuda.mem_get_info(idx)
+    _FREE_QUERY[idx] = (now, free, reserved)
+    return free
+
+
 def _gpu_accum_budget_bytes(device: torch.device, forward_reserve_bytes: int | None = None) -> int:
     """Device bytes available for resident tracks and accumulators (0 if unknown)."""
     try:
-        free, _ = torch.cuda.mem_get_info(device)
+        free = _free_device_bytes(device)
     except Exception:
         return 0
     slack = torch.cuda.memory_reserved(device) - torch.cuda.memory_allocated(device)

@@ -120,6 +120,13 @@ def split_tf32(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     return hi.contiguous(), (w - hi).contiguous()
 
 
+def split_bf16(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Split fp32 ``w`` into bf16 ``hi`` = round(w) and ``lo`` = round(w - hi) (round to nearest even)."""
+    w = w.float().contiguous()
+    hi = w.to(torch.bfloat16)
+    return hi.contiguous(), (w - hi.float()).to(torch.bfloat16).contiguous()
+
+
 PRECISIONS = ("fp32", "bf16", "fp32-simt")
 
 
@@ -143,7 +150,8 @@ def _block_n(n_out: int, bn256_min: int) -> int:
 class ConvNet(nn.Module):
     """Weights and convolution launches shared by the HTDemucs and SCNet models.
 
-    :param precision: ``"fp32"`` (3-pass TF32 tensor-core layers), ``"bf16"``
+    :param precision: ``"fp32"`` (3-pass tensor-core layers, operands split into
+        hi / lo parts), ``"bf16"``
         (bf16 tensor-core operands, fp32 accumulation and activations) or
         ``"fp32-simt"`` (CUDA-core fp32 kernels only).
     """
@@ -155,7 +163,12 @@ class ConvNet(nn.Module):
         self.precision = precision
         self._tc_cache: dict = {}
         # Output widths from which the 256-column tile is used (per tensor-core mode).
-        self._bn256_min = {_lib.TC_TF32X3: 512, _lib.TC_BF16: 512}
+        self._bn256_min = {_lib.TC_TF32X3: 512, _lib.TC_BF16: 512, _lib.TC_BF16X3: 512}
+        # Operand split of the fp32 tensor-core convolutions: "bf16x3" (hi/lo bf16
+        # parts, kind::f16: 16 K channels per MMA) or "tf32x3" (hi/lo TF32 parts,
+        # kind::tf32: 8 per MMA). Both hold the fp32 parity bound on the registry
+        # models; bf16x3 issues half the MMAs.
+        self.fp32_split = "bf16x3"
         self.weights = nn.ParameterDict()
         self._arena = StatsArena()
 
@@ -204,7 +217,10 @@ class ConvNet(nn.Module):
                 _lib.call("unblend_add", x.t.data_ptr(), pro_x2.t.data_ptr(), x.t.data_ptr(), x.t.numel(),
                           x.t.numel(), 1.0)
                 p.prologue, p.pro_x2 = PRO_NONE, None
-            mode = _lib.TC_TF32X3 if self.precision == "fp32" else _lib.TC_BF16
+            if self.precision == "fp32":
+                mode = _lib.TC_BF16X3 if self.fp32_split == "bf16x3" else _lib.TC_TF32X3
+            else:
+                mode = _lib.TC_BF16
             if post is not None:
                 # post [h_out, n_final]: added per (output row, channel) after the activation.
                 p.post, p.post_sh = post.data_ptr(), post.shape[1]
@@ -242,12 +258,17 @@ class ConvNet(nn.Module):
         return all(v % 4 == 0 for v in (p.n_group, p.out_sb, p.out_sh, p.out_sw, p.out_sg, out_offset))
 
     def _tc_weight(self, w: torch.Tensor, mode: int) -> tuple[torch.Tensor, torch.Tensor | None]:
-        """Tensor-core copy of a packed weight: (hi, lo) TF32 split or (bf16, None), cached."""
+        """Tensor-core copy of a packed weight: (hi, lo) TF32 or bf16 split, or (bf16, None), cached."""
         key = (w.data_ptr(), tuple(w.shape), mode)
         hit = self._tc_cache.get(key)
         if hit is None:
             flat = w.reshape(w.shape[0], -1)
-            hit = split_tf32(flat) if mode == _lib.TC_TF32X3 else (flat.to(torch.bfloat16).contiguous(), None)
+            if mode == _lib.TC_TF32X3:
+                hit = split_tf32(flat)
+            elif mode == _lib.TC_BF16X3:
+                hit = split_bf16(flat)
+            else:
+                hit = (flat.to(torch.bfloat16).contiguous(), None)
             self._tc_cache[key] = hit
         return hit
 

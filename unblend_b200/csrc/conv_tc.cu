@@ -18,7 +18,10 @@
 // fp32 mode: each fp32 A tile is split in place into a TF32 "hi" part and a
 // residual "lo" tile; weights come pre-split; D += Ahi*Bhi + Ahi*Blo + Alo*Bhi
 // (3 x kind::tf32) keeps fp32-level accuracy. bf16 mode: the fp32 A tile is
-// converted to bf16 and multiplied with bf16 weights (kind::f16).
+// converted to bf16 and multiplied with bf16 weights (kind::f16). 3-pass bf16
+// mode (MODE 2): the same three products with bf16 hi / lo parts (hi = x
+// rounded to bf16, lo = x - hi rounded to bf16, 16 significant bits in all) in
+// kind::f16, whose MMAs take 16 channels each instead of 8.
 // The accumulator lives in TMEM (128 lanes x BN fp32 columns); the epilogue
 // reads it with tcgen05.ld and applies bias, GELU / GLU, the LayerScale
 // residual and GroupNorm statistics, as the SIMT kernel does.
@@ -109,10 +112,12 @@ struct Layout {
   static constexpr int ROWB = KC * 4;                                 // fp32 bytes per staged row
   static constexpr int A_BYTES = A_ROWS * ROWB;                       // fp32 staging, A_ROWS x KC
   // lo (fp32) or bf16 tile in shared memory (1 KB aligned); none with A in TMEM
+  // (MODE 2: bf16 hi and lo tiles, AT_BYTES apart)
+  static constexpr int AT_BYTES = (A_ROWS * 64 + 1023) / 1024 * 1024;
   static constexpr int AC_BYTES =
-      ATmem<BN, MODE>::value ? 0 : MODE == 0 ? A_ROWS * ROWB : (A_ROWS * 64 + 1023) / 1024 * 1024;
+      ATmem<BN, MODE>::value ? 0 : MODE == 0 ? A_ROWS * ROWB : MODE == 2 ? 2 * AT_BYTES : AT_BYTES;
   static constexpr int B_BYTES = MODE == 0 ? BN * ROWB : BN * 64;     // one weight tile
-  static constexpr int B_TILES = MODE == 0 ? 2 : 1;                   // hi + lo, or bf16
+  static constexpr int B_TILES = MODE == 1 ? 1 : 2;                   // hi + lo, or bf16
   static constexpr int STAGE = A_BYTES + AC_BYTES + NSUB * B_TILES * B_BYTES;
   static constexpr int STAGES = (200 * 1024) / STAGE > 4 ? 4 : (200 * 1024) / STAGE;
   static constexpr int A_COL = 2 * BN;  // first TMEM column of the A stages (A in TMEM)
@@ -229,7 +234,7 @@ __global__ void __launch_bounds__(NT, 1)
             tma_load_4d(st, &mapA, &full[s], ca + cc, wa, ha, c.b);
             uint8_t* sb = st + L::A_BYTES + L::AC_BYTES;
             tma_load_2d(sb, &mapB, &full[s], kb + cc, c.n0);
-            if (MODE == 0) tma_load_2d(sb + L::B_BYTES, &mapB2, &full[s], kb + cc, c.n0);
+            if (MODE != 1) tma_load_2d(sb + L::B_BYTES, &mapB2, &full[s], kb + cc, c.n0);
             if (L::NSUB > 1 && ns > 1) tma_load_2d(sb + L::B_BYTES, &mapB, &full[s], a.tap_k1[tap] + cc, c.n0);
             if (L::NSUB > 2 && ns > 2) tma_load_2d(sb + 2 * L::B_BYTES, &mapB, &full[s], a.tap_k2[tap] + cc, c.n0);
           }
@@ -238,7 +243,7 @@ __global__ void __launch_bounds__(NT, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = instr_desc(MODE == 0 ? 2u : 1u, (uint32_t)BN);
+      constexpr uint32_t idesc = instr_desc(MODE == 0 ? 2u : 1u, (uint32_t)BN);  // kind::tf32 or bf16
       bool ok = true;
       int it = 0, i = 0;
       for (long long t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++i) {
@@ -293,6 +298,16 @@ __global__ void __launch_bounds__(NT, 1)
               umma_tf32(d, dah, dbh, idesc, (kc > 0 || j > 0) ? 1u : 0u);
               umma_tf32(d, dah, dbl, idesc, 1u);
               umma_tf32(d, dal, dbh, idesc, 1u);
+            }
+          } else if (MODE == 2) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              if (j > 0 && 16 * j >= valid) break;  // 16 channels per kind::f16 step
+              const uint64_t dah = smem_desc(sac + 32 * j, 64), dal = smem_desc(sac + L::AT_BYTES + 32 * j, 64);
+              const uint64_t dbh = smem_desc(sb + 32 * j, 64), dbl = smem_desc(sb + L::B_BYTES + 32 * j, 64);
+              umma_bf16(d, dah, dbh, idesc, (kc > 0 || j > 0) ? 1u : 0u);
+              umma_bf16(d, dah, dbl, idesc, 1u);
+              umma_bf16(d, dal, dbh, idesc, 1u);
             }
           } else {
             // Sub-tap u reads the bf16 A tile from row shift_u on (64-byte rows).
@@ -375,6 +390,25 @@ __global__ void __launch_bounds__(NT, 1)
             vh.w = __uint_as_float((__float_as_uint(v.w) + 0x1000u) & 0xFFFFE000u);
             hi[k] = vh;
             lo[k] = make_float4(v.x - vh.x, v.y - vh.y, v.z - vh.z, v.w - vh.w);
+          }
+        } else if (MODE == 2) {
+          // hi = bf16(v), lo = bf16(v - hi): both written as 64-byte swizzled bf16 tiles.
+          const uint8_t* src = st;
+          uint8_t* dst = st + L::A_BYTES;
+#pragma unroll
+          for (int k = ct; k < L::A_ROWS * 8; k += 128) {
+            const int row = k >> 3, c = k & 7;
+            const float4 v = *reinterpret_cast<const float4*>(src + row * 128 + ((c ^ (row & 7)) << 4));
+            const __nv_bfloat162 h0 = __floats2bfloat162_rn(v.x, v.y);
+            const __nv_bfloat162 h1 = __floats2bfloat162_rn(v.z, v.w);
+            const float2 f0 = __bfloat1622float2(h0), f1 = __bfloat1622float2(h1);
+            const __nv_bfloat162 l0 = __floats2bfloat162_rn(v.x - f0.x, v.y - f0.y);
+            const __nv_bfloat162 l1 = __floats2bfloat162_rn(v.z - f1.x, v.w - f1.y);
+            const int off = row * 64 + (((c >> 1) ^ ((row >> 1) & 3)) << 4) + (c & 1) * 8;
+            *reinterpret_cast<uint2*>(dst + off) =
+                make_uint2(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1));
+            *reinterpret_cast<uint2*>(dst + L::AT_BYTES + off) =
+                make_uint2(*reinterpret_cast<const uint32_t*>(&l0), *reinterpret_cast<const uint32_t*>(&l1));
           }
         } else {
           const uint8_t* src = st;
@@ -701,7 +735,7 @@ extern "C" int unblend_error_flag(int* out_host, int clear) {
 
 extern "C" int unblend_conv2d_tc(const float* x, const void* w_hi, const void* w_lo, const float* bias, float* y,
                                  const UnblendConvParams* p, int mode, int block_n, void* stream) {
-  UB_REQUIRE(x && w_hi && y && p && (mode == 0 || mode == 1));
+  UB_REQUIRE(x && w_hi && y && p && (mode == 0 || mode == 1 || mode == 2));
   UB_REQUIRE(mode == 1 || w_lo);
   UB_REQUIRE(block_n == 64 || block_n == 96 || block_n == 128 || block_n == 192 || block_n == 256);
   UB_REQUIRE(p->prologue == UNBLEND_PRO_NONE);
@@ -845,6 +879,8 @@ extern "C" int unblend_conv2d_tc(const float* x, const void* w_hi, const void* w
     if (!make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w_hi, wd, ws, boxB, CU_TENSOR_MAP_SWIZZLE_64B))
       return UNBLEND_ERR_INVALID;
     mb2 = mb;
+    if (mode == 2 && !make_map(&mb2, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w_lo, wd, ws, boxB, CU_TENSOR_MAP_SWIZZLE_64B))
+      return UNBLEND_ERR_INVALID;
   }
   const long long tiles = (long long)p->batch * p->h_out * a.tiles_w * a.tiles_n;
   UB_REQUIRE(tiles > 0 && tiles < (1LL << 31));
@@ -875,6 +911,13 @@ extern "C" int unblend_conv2d_tc(const float* x, const void* w_hi, const void* w
     if (block_n == 128) return launch<128, 0>(ma, mb, mb2, mo, a, tiles, st);
     if (block_n == 192) return launch<192, 0>(ma, mb, mb2, mo, a, tiles, st);
     return launch<256, 0>(ma, mb, mb2, mo, a, tiles, st);
+  }
+  if (mode == 2) {
+    if (block_n == 64) return launch<64, 2>(ma, mb, mb2, mo, a, tiles, st);
+    if (block_n == 96) return launch<96, 2>(ma, mb, mb2, mo, a, tiles, st);
+    if (block_n == 128) return launch<128, 2>(ma, mb, mb2, mo, a, tiles, st);
+    if (block_n == 192) return launch<192, 2>(ma, mb, mb2, mo, a, tiles, st);
+    return launch<256, 2>(ma, mb, mb2, mo, a, tiles, st);
   }
   if (block_n == 64) return launch<64, 1>(ma, mb, mb2, mo, a, tiles, st);
   if (block_n == 96) return launch<96, 1>(ma, mb, mb2, mo, a, tiles, st);
