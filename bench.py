@@ -472,9 +472,10 @@ def main() -> None:
                     "share_of_step": round(a["ms"] / sum(v["ms"] for v in agg.values()), 3),
                     "launches_per_step": a["n"]}
     if args.precision == "fp32" and roofline["bound"] == "tensor":
-        # fp32 accuracy costs three MMAs per product: kind::f16 at the bf16 rate (convolutions with
-        # bf16 hi / lo operands) or kind::tf32 at half of it (TF32 hi / lo operands).
-        bf16x3 = top == "unblend_conv2d_tc" and getattr(model, "fp32_split", "") == "bf16x3"
+        # fp32 accuracy costs three MMAs per product: kind::f16 at the bf16 rate (bf16 hi / lo
+        # operands) or kind::tf32 at half of it (TF32 hi / lo operands).
+        bf16x3 = ((top == "unblend_conv2d_tc" and getattr(model, "fp32_split", "") == "bf16x3") or
+                  (top == "unblend_attention_tc" and getattr(model, "attention_split", "") == "bf16x3"))
         div = 3 if bf16x3 else 6
         roofline["fp32_split"] = "bf16x3" if bf16x3 else "tf32x3"
         roofline["peak_fp32_3pass"] = round(peaks["bf16"] / div, 1)

@@ -93,7 +93,9 @@ int unblend_conv2d_f32(const float* x, const float* w, const float* bias, float*
  * TMEM accumulator). mode 0: fp32 accuracy by the 3-pass TF32 split, weights
  * given as w_hi = w with the low 13 mantissa bits cleared and w_lo = w - w_hi
  * (fp32, [n_out, K]); mode 1: bf16 operands, w_hi is bf16 [n_out, K], w_lo
- * unused. block_n: 64, 128 or 256 output channels per tile. Requirements:
+ * unused; mode 2: fp32 accuracy by the 3-pass bf16 split, w_hi = bf16(w) and
+ * w_lo = bf16(w - w_hi) (bf16, [n_out, K]). block_n: 64, 96, 128, 192 or 256
+ * output channels per tile. Requirements:
  * no prologue, c_in % 8 == 0 and >= 16, unit stride along w (or the stride-4
  * kernel-8 pad-2 time convolution, whose input rows up to a multiple of 4
  * past w_in must be zero), n_group and all output strides multiples of 4.
@@ -209,7 +211,8 @@ int unblend_attention_f32(const float* q, const float* k, const float* v, float*
 /* The same attention on the tcgen05 tensor cores (flash attention: S and O in
  * TMEM, P written back to TMEM as the A operand of the PV product, V
  * transposed in shared memory). mode 0: 3-pass TF32 split for fp32 accuracy;
- * mode 1: single-pass TF32 with round-to-nearest operands. Requires hd <= 64,
+ * mode 1: single-pass TF32 with round-to-nearest operands; mode 2: 3-pass bf16
+ * split (hi = bf16(x), lo = bf16(x - hi)) for fp32 accuracy. Requires hd <= 64,
  * hd % 4 == 0, strides that are multiples of 4 elements and 16-byte aligned
  * base pointers. */
 int unblend_attention_tc(const float* q, const float* k, const float* v, float* out, int batch,

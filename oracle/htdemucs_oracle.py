@@ -140,8 +140,9 @@ def _mha(sd: dict, p: str, q: torch.Tensor, kv: torch.Tensor, heads: int) -> tor
     Q = Q.view(B, Lq, heads, hd).transpose(1, 2)
     Kt = Kt.view(B, Lk, heads, hd).transpose(1, 2)
     V = V.view(B, Lk, heads, hd).transpose(1, 2)
-    att = torch.softmax((Q @ Kt.transpose(-1, -2)) / math.sqrt(hd), dim=-1)
-    o = (att @ V).transpose(1, 2).reshape(B, Lq, d)
+    # softmax(Q K^T / sqrt(hd)) V, through torch's fused CPU kernel for that product (the
+    # reference's own eval fast path reaches the same kernel).
+    o = F.scaled_dot_product_attention(Q, Kt, V, scale=1.0 / math.sqrt(hd)).transpose(1, 2).reshape(B, Lq, d)
     return F.linear(o, sd[f"{p}.out_proj.weight"], sd[f"{p}.out_proj.bias"])
 
 

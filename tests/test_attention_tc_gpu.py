@@ -12,8 +12,13 @@ from unblend_b200 import _lib
 
 pytestmark = pytest.mark.gpu
 
-# mode 0: 3-pass TF32 (fp32 accuracy); mode 1: single-pass TF32.
-TOL = {0: 2e-5, 1: 1e-2}
+# mode 0: 3-pass TF32 (fp32 accuracy); mode 1: single-pass TF32; mode 2: 3-pass
+# bf16 (16 significant bits per operand). On these unit-variance inputs a score's
+# error is ~2^-16 of |q| |k| and enters the exponent as is, so mode 2 reaches
+# 1.6e-4 of the RMS on the 2688-key rows (mode 0: 1e-5); in the HTDemucs forward
+# the attention output passes a 1e-4 LayerScale, and the model-level tests hold
+# the 1e-4 x RMS parity bound against the reference with this mode.
+TOL = {0: 2e-5, 1: 1e-2, 2: 3e-4}
 
 
 def _ref(q, k, v, heads, hd):
@@ -26,7 +31,7 @@ def _ref(q, k, v, heads, hd):
     return att.transpose(1, 2).reshape(B, lq, heads * hd).float()
 
 
-@pytest.mark.parametrize("mode", [0, 1])
+@pytest.mark.parametrize("mode", [0, 1, 2])
 @pytest.mark.parametrize("lq,lk,heads,hd", [(100, 70, 3, 64), (130, 64, 2, 48), (9, 200, 4, 8), (300, 257, 2, 64),
                                             (1344, 2688, 1, 64)])
 def test_attention_tc_matches_reference(mode, lq, lk, heads, hd):
@@ -42,13 +47,13 @@ def test_attention_tc_matches_reference(mode, lq, lk, heads, hd):
     assert _lib.error_flag() == 0
     ref = _ref(q, k, v, heads, hd)
     err = rel_err(o, ref)
-    if mode == 0:
-        # fp32 mode: as accurate as the fp32 SIMT kernel (long rows average
+    if mode in (0, 2):
+        # fp32 modes: as accurate as the fp32 SIMT kernel (long rows average
         # thousands of values, so fp32 accumulation alone reaches ~1e-4 of RMS).
         o32 = torch.empty_like(o)
         _lib.call("unblend_attention_f32", q.data_ptr(), k.data_ptr(), v.data_ptr(), o32.data_ptr(), B, heads, lq,
                   lk, hd, lq * D, D, lk * D, D, lq * D, D, 1.0 / math.sqrt(hd))
-        assert err < max(TOL[0], 4 * rel_err(o32, ref))
+        assert err < max(TOL[mode], 4 * rel_err(o32, ref))
     else:
         assert err < TOL[mode]
 
@@ -64,3 +69,7 @@ def test_attention_tc_interleaved_qkv_rows():
               L * 3 * D, 3 * D, L * 3 * D, 3 * D, L * D, D, 1.0 / math.sqrt(hd), 0)
     ref = _ref(qkv[..., :D].contiguous(), qkv[..., D:2 * D].contiguous(), qkv[..., 2 * D:].contiguous(), heads, hd)
     assert rel_err(o, ref) < TOL[0]
+    o2 = torch.empty_like(o)
+    _lib.call("unblend_attention_tc", base, base + 4 * D, base + 8 * D, o2.data_ptr(), B, heads, L, L, hd,
+              L * 3 * D, 3 * D, L * 3 * D, 3 * D, L * D, D, 1.0 / math.sqrt(hd), 2)
+    assert rel_err(o2, ref) < TOL[2]

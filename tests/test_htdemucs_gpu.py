@@ -61,10 +61,10 @@ def test_registry_config_matches_reference(fname, precision):
 @pytest.mark.parametrize("split", ["bf16x3", "tf32x3"])
 @pytest.mark.parametrize("fname", ["htdemucs_small.pt", "htdemucs_full.pt", "htdemucs_6s_full.pt"])
 def test_fp32_operand_splits_match_reference(fname, split):
-    """Both operand splits of the fp32 tensor-core convolutions hold the fp32 bound."""
+    """Both operand splits of the fp32 tensor-core convolutions and attention hold the fp32 bound."""
     g = golden(fname)
     m = _model(g)
-    m.fp32_split = split
+    m.fp32_split = m.attention_split = split
     out = m(g["mix"].cuda()).cpu()
     d = g.get("decimate", 1)
     assert rel_err(out[..., ::d], g["out"]) < FP32_TOL

@@ -69,17 +69,6 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// D[tmem] (+)= A[tmem] * B[smem], kind::f16 with bf16 operands.
-__device__ __forceinline__ void umma_bf16_ts(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc,
-                                             uint32_t accum) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
-      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accum)
-      : "memory");
-}
-
 struct Unit {
   int qt, h, bi, bo;
 };

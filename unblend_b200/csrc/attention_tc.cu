@@ -15,7 +15,11 @@
 //              place, and V transposed to V^T (keys contiguous) while split
 // MODE 0 (fp32 accuracy): every product is hi*hi + hi*lo + lo*hi in
 // kind::tf32 (3 MMAs). MODE 1: single-pass TF32 with round-to-nearest
-// operands (used by the bf16 precision setting).
+// operands (used by the bf16 precision setting). MODE 2 (fp32 accuracy): the
+// same three products with bf16 hi / lo parts (hi = x rounded to bf16, lo =
+// x - hi rounded to bf16) in kind::f16, 16 dims or keys per MMA instead of 8:
+// Q, K and V^T become bf16 hi / lo tiles (128-byte rows, 128-byte swizzle)
+// beside their fp32 staging, and P is packed as bf16 hi / lo pairs over its S tile.
 //
 // Sequences are indexed by a two-level batch (outer, inner) with independent
 // strides, so BS-RoFormer's axial attention reads its [batch, frames, bands,
@@ -44,23 +48,29 @@ template <int MODE>
 struct AL {
   static constexpr int Q_BYTES = 2 * BQ * 128;   // 2 boxes of 32 dims x 128 rows (fp32)
   static constexpr int KV_BYTES = 2 * BK * 128;  // 2 boxes of 32 dims x 64 keys, or V^T (64 dims x 64 keys)
-  static constexpr int Q_TOTAL = MODE == 0 ? 2 * Q_BYTES : Q_BYTES;
-  // Stage: K (hi in place) [, K lo], V staging, V^T hi [, V^T lo].
+  static constexpr int QH_BYTES = BQ * 128;      // MODE 2: bf16 Q tile (128 rows x 64 dims)
+  static constexpr int TH_BYTES = BK * 128;      // MODE 2: bf16 K tile (64 keys x 64 dims) or V^T tile
+  // Q: fp32 staging (hi in place) + lo (MODE 0), or fp32 staging + bf16 hi + bf16 lo (MODE 2).
+  static constexpr int Q_TOTAL = MODE == 0 ? 2 * Q_BYTES : MODE == 2 ? Q_BYTES + 2 * QH_BYTES : Q_BYTES;
+  // Stage: K (hi in place) [, K lo], V staging, V^T hi [, V^T lo]; MODE 2: K staging, K hi,
+  // K lo, V staging, V^T hi, V^T lo.
   static constexpr int K_OFF = 0;
-  static constexpr int KLO_OFF = KV_BYTES;
-  static constexpr int V_OFF = MODE == 0 ? 2 * KV_BYTES : KV_BYTES;
+  static constexpr int KH_OFF = MODE == 2 ? KV_BYTES : 0;
+  static constexpr int KLO_OFF = MODE == 2 ? KV_BYTES + TH_BYTES : KV_BYTES;
+  static constexpr int V_OFF = MODE == 0 ? 2 * KV_BYTES : MODE == 2 ? KV_BYTES + 2 * TH_BYTES : KV_BYTES;
   static constexpr int VT_OFF = V_OFF + KV_BYTES;
-  static constexpr int VTLO_OFF = VT_OFF + KV_BYTES;
-  static constexpr int STAGE = MODE == 0 ? VTLO_OFF + KV_BYTES : VT_OFF + KV_BYTES;
-  static constexpr int STAGES = MODE == 0 ? 2 : 3;
+  static constexpr int VTLO_OFF = VT_OFF + (MODE == 2 ? TH_BYTES : KV_BYTES);
+  static constexpr int STAGE =
+      MODE == 0 ? VTLO_OFF + KV_BYTES : MODE == 2 ? VTLO_OFF + TH_BYTES : VT_OFF + KV_BYTES;
+  static constexpr int STAGES = MODE == 1 ? 3 : 2;
   static constexpr int SMEM = Q_TOTAL + STAGES * STAGE + 1024 + 256;
-  // TMEM columns: S/P double buffer, P lo double buffer (MODE 0), the P V
-  // product of the current tile, and the running output accumulator.
+  // TMEM columns: S/P double buffer (MODE 2: P hi and lo packed over its S tile),
+  // P lo double buffer (MODE 0), and the P V product of the current tile.
   static constexpr int S_COL = 0;
   static constexpr int PLO_COL = 128;
   static constexpr int O_COL = MODE == 0 ? 256 : 128;
-  static constexpr int OACC_COL = O_COL + 64;
   static constexpr int TMEM_COLS = MODE == 0 ? 512 : 256;
+  static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
 struct AttnArgs {
@@ -144,6 +154,75 @@ __device__ __forceinline__ void transpose_v(const uint8_t* stage_v, uint8_t* vt,
   }
 }
 
+// bf16 hi = round(v), lo = round(v - hi) of four consecutive values, as two
+// 8-byte words of packed pairs.
+__device__ __forceinline__ void split_bf16x4(float4 v, uint2& hi, uint2& lo) {
+  const __nv_bfloat162 h0 = __floats2bfloat162_rn(v.x, v.y), h1 = __floats2bfloat162_rn(v.z, v.w);
+  const float2 f0 = __bfloat1622float2(h0), f1 = __bfloat1622float2(h1);
+  const __nv_bfloat162 l0 = __floats2bfloat162_rn(v.x - f0.x, v.y - f0.y);
+  const __nv_bfloat162 l1 = __floats2bfloat162_rn(v.z - f1.x, v.w - f1.y);
+  hi = make_uint2(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1));
+  lo = make_uint2(*reinterpret_cast<const uint32_t*>(&l0), *reinterpret_cast<const uint32_t*>(&l1));
+}
+
+// Byte offset of element (row r, column c < 64) of a [rows x 64] bf16 tile with
+// 128-byte rows and the 128-byte swizzle (16-byte chunk index XOR row % 8).
+__device__ __forceinline__ int sw128h(int r, int c) { return r * 128 + ((((c >> 3) ^ (r & 7))) << 4) + (c & 7) * 2; }
+
+// MODE 2 operand preparation: the fp32 staging tile (2 boxes of [box_rows x 32
+// dims], 128-byte swizzled rows) to bf16 hi / lo tiles [box_rows x 64 dims], with
+// the optional rotary rotation of each (even, odd) dim pair at position pos0 + row.
+__device__ __forceinline__ void split_tile_bf16(const uint8_t* p, uint8_t* hi, uint8_t* lo, int t, int nt,
+                                                int box_rows, int pos0, const float2* __restrict__ rope,
+                                                int rope_len, int hd) {
+  const float4* h = reinterpret_cast<const float4*>(p);
+  const int n4 = box_rows * 16;
+  for (int i = t; i < n4; i += nt) {
+    float4 v = h[i];
+    const int box = i / (box_rows * 8), within = i - box * (box_rows * 8);
+    const int row = within >> 3;
+    const int d0 = box * 32 + (((within & 7) ^ (row & 7)) << 2);
+    if (rope && d0 < hd) {
+      int pos = pos0 + row;
+      pos = pos < rope_len ? pos : rope_len - 1;
+      const float2 cs0 = __ldg(rope + (long long)pos * (hd >> 1) + (d0 >> 1));
+      const float2 cs1 = __ldg(rope + (long long)pos * (hd >> 1) + (d0 >> 1) + 1);
+      v = make_float4(v.x * cs0.x - v.y * cs0.y, v.x * cs0.y + v.y * cs0.x, v.z * cs1.x - v.w * cs1.y,
+                      v.z * cs1.y + v.w * cs1.x);
+    }
+    uint2 vh, vl;
+    split_bf16x4(v, vh, vl);
+    const int off = sw128h(row, d0);
+    *reinterpret_cast<uint2*>(hi + off) = vh;
+    *reinterpret_cast<uint2*>(lo + off) = vl;
+  }
+}
+
+// MODE 2: V staging [2 boxes of (64 keys x 32 dims)] -> V^T hi / lo bf16 tiles [64
+// dims x 64 keys] (keys contiguous). Lane = key of a 32-key half, so the 16-bit stores
+// of one dim row land in four 16-byte chunks.
+template <int NW>
+__device__ __forceinline__ void transpose_v_bf16(const uint8_t* stage_v, uint8_t* vt, uint8_t* vt_lo, int t) {
+  const int lane = t & 31, w = t >> 5;
+#pragma unroll
+  for (int u = 0; u < 32 / NW; ++u) {
+    const int unit = w * (32 / NW) + u;  // 32 units: (key half, box, chunk)
+    const int kh = unit >> 4, box = (unit >> 3) & 1, c = unit & 7;
+    const int key = kh * 32 + lane;
+    const float4 val = *reinterpret_cast<const float4*>(stage_v + box * (64 * 128) + key * 128 + ((c ^ (key & 7)) << 4));
+    const float v4[4] = {val.x, val.y, val.z, val.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int d = box * 32 + c * 4 + e;
+      const int off = sw128h(d, key);
+      const __nv_bfloat16 hb = __float2bfloat16_rn(v4[e]);
+      const __nv_bfloat16 lb = __float2bfloat16_rn(v4[e] - __bfloat162float(hb));
+      *reinterpret_cast<__nv_bfloat16*>(vt + off) = hb;
+      *reinterpret_cast<__nv_bfloat16*>(vt_lo + off) = lb;
+    }
+  }
+}
+
 __device__ __forceinline__ float ex2f(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -158,7 +237,8 @@ __global__ void __launch_bounds__(NT, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
-  uint8_t* sQlo = smem + L::Q_BYTES;
+  uint8_t* sQlo = smem + L::Q_BYTES;            // MODE 0: TF32 lo; MODE 2: bf16 hi (lo follows)
+  uint8_t* sQhlo = sQlo + L::QH_BYTES;          // MODE 2: bf16 lo
   uint8_t* sKV = smem + L::Q_TOTAL;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + L::STAGES * L::STAGE);
   // K and V travel in separate barrier rings over the same stage slots, so the
@@ -234,16 +314,26 @@ __global__ void __launch_bounds__(NT, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t id_s = instr_desc(2u, (uint32_t)BK);  // N = 64 keys
-      constexpr uint32_t id_o = instr_desc(2u, 64u);           // N = 64 dims
+      constexpr uint32_t fmt = MODE == 2 ? 1u : 2u;                // kind::f16 (bf16) or kind::tf32
+      constexpr uint32_t id_s = instr_desc(fmt, (uint32_t)BK);  // N = 64 keys
+      constexpr uint32_t id_o = instr_desc(fmt, 64u);           // N = 64 dims
       bool ok = mbar_wait(q_ready, 0);
-      const uint32_t q_hi = smem_u32(sQ), q_lo = smem_u32(sQlo);
+      const uint32_t q_hi = smem_u32(MODE == 2 ? sQlo : sQ), q_lo = smem_u32(MODE == 2 ? sQhlo : sQlo);
       auto issue_s = [&](int j) {
         const uint8_t* st = sKV + (j % L::STAGES) * L::STAGE;
-        const uint32_t k_hi = smem_u32(st + L::K_OFF), k_lo = smem_u32(st + L::KLO_OFF);
+        const uint32_t k_hi = smem_u32(st + L::KH_OFF), k_lo = smem_u32(st + L::KLO_OFF);
         const uint32_t d = tmem + L::S_COL + (j & 1) * BK;
+        if (MODE == 2) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+          for (int i = 0; i < 4; ++i) {  // 16 dims per kind::f16 step, 32 bytes along the swizzled rows
+            umma_bf16(d, smem_desc(q_hi + 32 * i, 128), smem_desc(k_hi + 32 * i, 128), id_s, i > 0 ? 1u : 0u);
+            umma_bf16(d, smem_desc(q_hi + 32 * i, 128), smem_desc(k_lo + 32 * i, 128), id_s, 1u);
+            umma_bf16(d, smem_desc(q_lo + 32 * i, 128), smem_desc(k_hi + 32 * i, 128), id_s, 1u);
+          }
+        }
+        constexpr int tf32_steps = MODE == 2 ? 0 : 8;
+#pragma unroll
+        for (int i = 0; i < tf32_steps; ++i) {
           const uint32_t qa = (i >> 2) * (BQ * 128) + (i & 3) * 32;
           const uint32_t ka = (i >> 2) * (BK * 128) + (i & 3) * 32;
           umma_tf32(d, smem_desc(q_hi + qa, 128), smem_desc(k_hi + ka, 128), id_s, i > 0 ? 1u : 0u);
@@ -280,8 +370,18 @@ __global__ void __launch_bounds__(NT, 1)
         const uint32_t p_hi = tmem + L::S_COL + (j & 1) * BK;
         const uint32_t p_lo = tmem + L::PLO_COL + (j & 1) * BK;
         const uint32_t o = tmem + L::O_COL;
+        if (MODE == 2) {
+          // P hi packed in the S tile's columns [0, 32), P lo in [32, 64): 16 keys (8 columns) per step.
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {  // 8 keys per step
+          for (int i = 0; i < 4; ++i) {
+            umma_bf16_ts(o, p_hi + 8 * i, smem_desc(vt_hi + 32 * i, 128), id_o, i > 0 ? 1u : 0u);
+            umma_bf16_ts(o, p_hi + 8 * i, smem_desc(vt_lo + 32 * i, 128), id_o, 1u);
+            umma_bf16_ts(o, p_hi + 32 + 8 * i, smem_desc(vt_hi + 32 * i, 128), id_o, 1u);
+          }
+        }
+        constexpr int tf32_steps = MODE == 2 ? 0 : 8;
+#pragma unroll
+        for (int i = 0; i < tf32_steps; ++i) {  // 8 keys per step
           const uint32_t vb = (i >> 2) * (64 * 128) + (i & 3) * 32;
           umma_tf32_ts(o, p_hi + 8 * i, smem_desc(vt_hi + vb, 128), id_o, i > 0 ? 1u : 0u);
           if (MODE == 0) {
@@ -299,7 +399,10 @@ __global__ void __launch_bounds__(NT, 1)
     const int ct = threadIdx.x - 192;
     bool ok = mbar_wait(q_full, 0);
     if (ok) {
-      split_tile<MODE>(sQ, sQlo, L::Q_BYTES / 16, ct, 128, BQ, q0, a.rope, a.rope_len, a.hd);
+      if (MODE == 2)
+        split_tile_bf16(sQ, sQlo, sQhlo, ct, 128, BQ, q0, a.rope, a.rope_len, a.hd);
+      else
+        split_tile<MODE>(sQ, sQlo, L::Q_BYTES / 16, ct, 128, BQ, q0, a.rope, a.rope_len, a.hd);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(q_ready);
@@ -312,11 +415,18 @@ __global__ void __launch_bounds__(NT, 1)
       uint8_t* st = sKV + s * L::STAGE;
       if (k_role) {
         if (!mbar_wait(&k_full[s], r & 1)) break;
-        split_tile<MODE>(st + L::K_OFF, st + L::KLO_OFF, L::KV_BYTES / 16, rt, 64, BK, j * BK, a.rope, a.rope_len,
-                         a.hd);
+        if (MODE == 2)
+          split_tile_bf16(st + L::K_OFF, st + L::KH_OFF, st + L::KLO_OFF, rt, 64, BK, j * BK, a.rope, a.rope_len,
+                          a.hd);
+        else
+          split_tile<MODE>(st + L::K_OFF, st + L::KLO_OFF, L::KV_BYTES / 16, rt, 64, BK, j * BK, a.rope,
+                           a.rope_len, a.hd);
       } else {
         if (!mbar_wait(&v_full[s], r & 1)) break;
-        transpose_v<MODE, 2>(st + L::V_OFF, st + L::VT_OFF, st + (MODE == 0 ? L::VTLO_OFF : L::VT_OFF), rt);
+        if (MODE == 2)
+          transpose_v_bf16<2>(st + L::V_OFF, st + L::VT_OFF, st + L::VTLO_OFF, rt);
+        else
+          transpose_v<MODE, 2>(st + L::V_OFF, st + L::VT_OFF, st + (MODE == 0 ? L::VTLO_OFF : L::VT_OFF), rt);
       }
       fence_proxy_async_smem();
       __syncwarp();
@@ -368,9 +478,32 @@ __global__ void __launch_bounds__(NT, 1)
       const float corr = ex2f(m - m_new);
       float sum = 0.f;
       // P = exp2(s - m_new) rounded to TF32 (hi) plus, in MODE 0, the residual
-      // (lo), written to TMEM one 32-key half at a time.
+      // (lo), written to TMEM one 32-key half at a time. MODE 2: bf16 hi / lo
+      // pairs (keys 2i, 2i + 1 in column i), hi over the S tile's first 32
+      // columns and lo over the next 32.
+      if (MODE == 2) {
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
+        for (int half = 0; half < 2; ++half) {
+          const uint32_t (&sh)[32] = half == 0 ? s0 : s1;
+          uint32_t hp[16], lp[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float p0 = ex2f(__uint_as_float(sh[2 * i]) - m_new);
+            const float p1 = ex2f(__uint_as_float(sh[2 * i + 1]) - m_new);
+            sum += p0 + p1;
+            const __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
+            const float2 f = __bfloat1622float2(h2);
+            const __nv_bfloat162 l2 = __floats2bfloat162_rn(p0 - f.x, p1 - f.y);
+            hp[i] = *reinterpret_cast<const uint32_t*>(&h2);
+            lp[i] = *reinterpret_cast<const uint32_t*>(&l2);
+          }
+          // Keys 32 half .. 32 half + 31: hi columns 16 half .., lo columns 32 + 16 half ...
+          tmem_st16(lane_base + L::S_COL + (j & 1) * BK + 16 * half, hp);
+          tmem_st16(lane_base + L::S_COL + (j & 1) * BK + 32 + 16 * half, lp);
+        }
+      }
+#pragma unroll
+      for (int half = 0; half < 2 && MODE != 2; ++half) {
         uint32_t (&sh)[32] = half == 0 ? s0 : s1;
         uint32_t lo[32];
 #pragma unroll
@@ -475,7 +608,7 @@ long long legal_stride(long long s, int extent) { return extent == 1 && s <= 0 ?
 
 int attention_launch(const float* q, const float* k, const float* v, const UnblendAttnParams* p, int mode,
                      void* stream) {
-  UB_REQUIRE(q && k && v && p && p->out && (mode == 0 || mode == 1));
+  UB_REQUIRE(q && k && v && p && p->out && (mode == 0 || mode == 1 || mode == 2));
   UB_REQUIRE(p->outer > 0 && p->inner > 0 && p->heads > 0 && p->lq > 0 && p->lk > 0);
   UB_REQUIRE(p->hd > 0 && p->hd <= 64 && p->hd % 4 == 0);
   const long long q_so = legal_stride(p->q_so, p->outer), q_si = legal_stride(p->q_si, p->inner);
@@ -517,6 +650,9 @@ int attention_launch(const float* q, const float* k, const float* v, const Unble
   if (mode == 0) {
     cudaFuncSetAttribute(attention_tc_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, AL<0>::SMEM);
     attention_tc_kernel<0><<<(unsigned)grid, NT, AL<0>::SMEM, st>>>(mq, mk, mv, a);
+  } else if (mode == 2) {
+    cudaFuncSetAttribute(attention_tc_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, AL<2>::SMEM);
+    attention_tc_kernel<2><<<(unsigned)grid, NT, AL<2>::SMEM, st>>>(mq, mk, mv, a);
   } else {
     cudaFuncSetAttribute(attention_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, AL<1>::SMEM);
     attention_tc_kernel<1><<<(unsigned)grid, NT, AL<1>::SMEM, st>>>(mq, mk, mv, a);

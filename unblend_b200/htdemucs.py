@@ -102,6 +102,9 @@ class HTDemucsCuda(ConvNet):
         if cfg["nfft"] != 4096 or cfg["kernel_size"] != 8 or cfg["stride"] != 4 or cfg["t_emb"] != "sin":
             raise ValueError("unsupported HTDemucs geometry")
         self.config = cfg
+        # Operand split of the fp32 tensor-core attention: "bf16x3" (kind::f16, 16 dims
+        # or keys per MMA) or "tf32x3" (kind::tf32, 8 per MMA).
+        self.attention_split = "bf16x3"
         self.sources = list(cfg["sources"])
         self.samplerate = cfg["samplerate"]
         self.audio_channels = cfg["audio_channels"]
@@ -437,7 +440,10 @@ class HTDemucsCuda(ConvNet):
             return
         q, k, v = qbuf.data_ptr() + 4 * q_off, kvbuf.data_ptr() + 4 * k_off, kvbuf.data_ptr() + 4 * v_off
         if self.precision != "fp32-simt" and hd % 4 == 0 and hd <= 64 and all(p % 16 == 0 for p in (q, k, v, o)):
-            mode = 0 if self.precision == "fp32" else 1
+            if self.precision == "fp32":
+                mode = 2 if self.attention_split == "bf16x3" else 0
+            else:
+                mode = 1
             _lib.call("unblend_attention_tc", q, k, v, o, B, heads, L, Lk, hd, q_sb, q_sr, kv_sb, kv_sr, o_sb, o_sr,
                       scale, mode, work=work)
             return
