@@ -130,18 +130,31 @@ def split_bf16(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
 PRECISIONS = ("fp32", "bf16", "fp32-simt")
 
 
-def _block_n(n_out: int, bn256_min: int) -> int:
-    """Output-channel tile of the tensor-core convolution: the fewest wasted MMA columns.
+def _m_tiles(batch: int, h_out: int, w_out: int) -> int:
+    """128-row output tiles of the tensor-core convolution (rows of W split into 128s, or into the
+    largest multiple of 8 in [64, 128] that divides W when 128 does not, e.g. 336 = 3 x 112)."""
+    mv = 128
+    if w_out % 128 and h_out > 1:
+        mv = next((m for m in range(128, 63, -8) if w_out % m == 0), 128)
+    return batch * h_out * -(-w_out // mv)
 
-    Candidates 64, 96, 128, 192 (and 256 from ``bn256_min`` channels on): the one
-    whose tiles cover ``n_out`` with the least padding, preferring the wider tile
-    on ties (fewer re-reads of the input rows).
+
+def _block_n(n_out: int, bn256_min: int, m_tiles: int = 1 << 20, sms: int = 148) -> int:
+    """Output-channel tile of the tensor-core convolution.
+
+    Candidates 64, 96, 128, 192 (and 256 from ``bn256_min`` channels on). The persistent
+    kernel runs ``m_tiles * ceil(n_out / bn)`` tiles over ``sms`` CTAs, so a launch costs
+    about ceil(tiles / sms) waves of (64 + bn) column-units per tile (the MMA issue time
+    of a 128-row tile: ~48 cycles per instruction at N = 64 against 128 at N = 256, and
+    the width-independent A loads and operand conversion). The cheapest candidate wins,
+    ties going to the wider tile (fewer re-reads of the input rows): with many tiles that
+    is the fewest padded columns; with few (small batches) it trades width for fuller waves.
     """
     cands = [64, 96, 128, 192] + ([256] if n_out >= bn256_min else [])
     best = None
     for bn in cands:
-        waste = -(-n_out // bn) * bn - n_out
-        key = (waste, -bn)
+        tiles = m_tiles * -(-n_out // bn)
+        key = (-(-tiles // sms) * (64 + bn), -bn)
         if best is None or key < best[0]:
             best = (key, bn)
     return best[1]
@@ -162,12 +175,13 @@ class ConvNet(nn.Module):
             raise ValueError(f"precision must be one of {PRECISIONS}")
         self.precision = precision
         self._tc_cache: dict = {}
+        self._sm_count: dict = {}
         # Output widths from which the 256-column tile is used (per tensor-core mode).
         self._bn256_min = {_lib.TC_TF32X3: 512, _lib.TC_BF16: 512, _lib.TC_BF16X3: 512}
         # Operand split of the fp32 tensor-core convolutions: "bf16x3" (hi/lo bf16
-        # parts, kind::f16: 16 K channels per MMA) or "tf32x3" (hi/lo TF32 parts,
-        # kind::tf32: 8 per MMA). Both hold the fp32 parity bound on the registry
-        # models; bf16x3 issues half the MMAs.
+        # parts, kind::f16: 16 K channels per MMA, on tiles of 192 and 256 columns)
+        # or "tf32x3" (hi/lo TF32 parts, kind::tf32: 8 per MMA, every tile). Both
+        # hold the fp32 parity bound on the registry models; bf16x3 issues half the MMAs.
         self.fp32_split = "bf16x3"
         self.weights = nn.ParameterDict()
         self._arena = StatsArena()
@@ -217,20 +231,27 @@ class ConvNet(nn.Module):
                 _lib.call("unblend_add", x.t.data_ptr(), pro_x2.t.data_ptr(), x.t.data_ptr(), x.t.numel(),
                           x.t.numel(), 1.0)
                 p.prologue, p.pro_x2 = PRO_NONE, None
-            if self.precision == "fp32":
-                mode = _lib.TC_BF16X3 if self.fp32_split == "bf16x3" else _lib.TC_TF32X3
-            else:
-                mode = _lib.TC_BF16
             if post is not None:
                 # post [h_out, n_final]: added per (output row, channel) after the activation.
                 p.post, p.post_sh = post.data_ptr(), post.shape[1]
             p.y_bf16 = 1 if y_bf16 else 0
+            if self.precision == "fp32":
+                block_n = _block_n(n_out, self._bn256_min[_lib.TC_TF32X3], _m_tiles(x.B, h_out, w_out), self._sms(x))
+                # The bf16 split halves the MMAs; layers whose many-tile width is <= 128 columns
+                # keep the TF32 split, whose A operand sits in TMEM (A-from-TMEM MMAs issue faster
+                # at those widths: decoder.3's 3x3 rewrite 851 us against 923 us with the bf16
+                # split in shared memory). The split depends on the layer only, not on the batch
+                # (the tile width does not change any output's rounding; the split does).
+                wide = _block_n(n_out, self._bn256_min[_lib.TC_TF32X3]) >= 192
+                mode = _lib.TC_BF16X3 if self.fp32_split == "bf16x3" and wide else _lib.TC_TF32X3
+            else:
+                mode = _lib.TC_BF16
+                bn256 = self._bn256_min[mode]
+                if kw == 3 and sw == 1 and dw * 2 <= 8:
+                    # 3-wide kernel rows: tiles of <= 192 columns share one A load across the three taps.
+                    bn256 = 1 << 30
+                block_n = _block_n(n_out, bn256, _m_tiles(x.B, h_out, w_out), self._sms(x))
             whi, wlo = self._tc_weight(w, mode)
-            bn256 = self._bn256_min[mode]
-            if mode == _lib.TC_BF16 and kw == 3 and sw == 1 and dw * 2 <= 8:
-                # 3-wide kernel rows: tiles of <= 192 columns share one A load across the three taps.
-                bn256 = 1 << 30
-            block_n = _block_n(n_out, bn256)
             _lib.call("unblend_conv2d_tc", x.t.data_ptr(), whi.data_ptr(), _lib.ptr(wlo), _lib.ptr(b), y,
                       ctypes_byref(p), mode, block_n, work=flops)
             return
@@ -241,6 +262,14 @@ class ConvNet(nn.Module):
             assert out_offset == 0 and out.sb == h_out * w_out * n_final and out.sw == n_final
             table = post[:, None, :].expand(h_out, w_out, n_final).contiguous()
             _lib.call("unblend_add", y, table.data_ptr(), y, out.B * table.numel(), table.numel(), 1.0)
+
+    def _sms(self, x: Act) -> int:
+        """Streaming multiprocessors of the device holding ``x`` (cached)."""
+        dev = x.t.device
+        n = self._sm_count.get(dev.index)
+        if n is None:
+            n = self._sm_count[dev.index] = torch.cuda.get_device_properties(dev).multi_processor_count
+        return n
 
     def _tc_eligible(self, x: Act, p: ConvParams, prologue: int, out_offset: int) -> bool:
         """Whether this convolution meets the tensor-core kernel's layout requirements."""
