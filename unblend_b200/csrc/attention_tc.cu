@@ -97,10 +97,11 @@ __device__ __forceinline__ int sw128(int r, int c) { return r * 128 + ((((c >> 2
 // Round `n4` float4s at p to TF32 in place; with MODE 0 also write the residuals at lo.
 // The tile is 2 boxes of [box_rows x 32 dims] (128-byte swizzled rows) whose
 // row r holds sequence position pos0 + r; with `rope`, each (even, odd) dim
-// pair is first rotated by the (cos, sin) of that position.
+// pair is first rotated by the (cos, sin) of that position; every value is then
+// multiplied by `mul` (the softmax scale times log2(e) for Q, 1 for K).
 template <int MODE>
 __device__ __forceinline__ void split_tile(uint8_t* p, uint8_t* lo, int n4, int t, int nt, int box_rows, int pos0,
-                                           const float2* __restrict__ rope, int rope_len, int hd) {
+                                           const float2* __restrict__ rope, int rope_len, int hd, float mul) {
   float4* h = reinterpret_cast<float4*>(p);
   float4* l = reinterpret_cast<float4*>(lo);
   for (int i = t; i < n4; i += nt) {
@@ -118,6 +119,7 @@ __device__ __forceinline__ void split_tile(uint8_t* p, uint8_t* lo, int n4, int 
                         v.z * cs1.y + v.w * cs1.x);
       }
     }
+    v = make_float4(v.x * mul, v.y * mul, v.z * mul, v.w * mul);
     float4 vh;
     vh.x = tf32_round(v.x);
     vh.y = tf32_round(v.y);
@@ -171,10 +173,11 @@ __device__ __forceinline__ int sw128h(int r, int c) { return r * 128 + ((((c >> 
 
 // MODE 2 operand preparation: the fp32 staging tile (2 boxes of [box_rows x 32
 // dims], 128-byte swizzled rows) to bf16 hi / lo tiles [box_rows x 64 dims], with
-// the optional rotary rotation of each (even, odd) dim pair at position pos0 + row.
+// the optional rotary rotation of each (even, odd) dim pair at position pos0 + row,
+// then the factor `mul`.
 __device__ __forceinline__ void split_tile_bf16(const uint8_t* p, uint8_t* hi, uint8_t* lo, int t, int nt,
                                                 int box_rows, int pos0, const float2* __restrict__ rope,
-                                                int rope_len, int hd) {
+                                                int rope_len, int hd, float mul) {
   const float4* h = reinterpret_cast<const float4*>(p);
   const int n4 = box_rows * 16;
   for (int i = t; i < n4; i += nt) {
@@ -190,6 +193,7 @@ __device__ __forceinline__ void split_tile_bf16(const uint8_t* p, uint8_t* hi, u
       v = make_float4(v.x * cs0.x - v.y * cs0.y, v.x * cs0.y + v.y * cs0.x, v.z * cs1.x - v.w * cs1.y,
                       v.z * cs1.y + v.w * cs1.x);
     }
+    v = make_float4(v.x * mul, v.y * mul, v.z * mul, v.w * mul);
     uint2 vh, vl;
     split_bf16x4(v, vh, vl);
     const int off = sw128h(row, d0);
@@ -400,9 +404,9 @@ __global__ void __launch_bounds__(NT, 1)
     bool ok = mbar_wait(q_full, 0);
     if (ok) {
       if (MODE == 2)
-        split_tile_bf16(sQ, sQlo, sQhlo, ct, 128, BQ, q0, a.rope, a.rope_len, a.hd);
+        split_tile_bf16(sQ, sQlo, sQhlo, ct, 128, BQ, q0, a.rope, a.rope_len, a.hd, a.c);
       else
-        split_tile<MODE>(sQ, sQlo, L::Q_BYTES / 16, ct, 128, BQ, q0, a.rope, a.rope_len, a.hd);
+        split_tile<MODE>(sQ, sQlo, L::Q_BYTES / 16, ct, 128, BQ, q0, a.rope, a.rope_len, a.hd, a.c);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(q_ready);
@@ -417,10 +421,10 @@ __global__ void __launch_bounds__(NT, 1)
         if (!mbar_wait(&k_full[s], r & 1)) break;
         if (MODE == 2)
           split_tile_bf16(st + L::K_OFF, st + L::KH_OFF, st + L::KLO_OFF, rt, 64, BK, j * BK, a.rope, a.rope_len,
-                          a.hd);
+                          a.hd, 1.0f);
         else
           split_tile<MODE>(st + L::K_OFF, st + L::KLO_OFF, L::KV_BYTES / 16, rt, 64, BK, j * BK, a.rope,
-                           a.rope_len, a.hd);
+                           a.rope_len, a.hd, 1.0f);
       } else {
         if (!mbar_wait(&v_full[s], r & 1)) break;
         if (MODE == 2)
@@ -451,7 +455,12 @@ __global__ void __launch_bounds__(NT, 1)
         uint32_t t0[32];
         tmem_ld32(lane_base + L::O_COL + 32 * half, t0);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) oacc[32 * half + i] = fmaf(oacc[32 * half + i], corr, __uint_as_float(t0[i]));
+        for (int i = 0; i < 32; i += 2) {
+          const float2 o2 = ub::fma2(make_float2(oacc[32 * half + i], oacc[32 * half + i + 1]), make_float2(corr, corr),
+                                     make_float2(__uint_as_float(t0[i]), __uint_as_float(t0[i + 1])));
+          oacc[32 * half + i] = o2.x;
+          oacc[32 * half + i + 1] = o2.y;
+        }
       }
     };
     for (int j = 0; j < nkv && ok; ++j) {
@@ -464,19 +473,27 @@ __global__ void __launch_bounds__(NT, 1)
       __syncwarp();
       tmem_ld32(lane_base + L::S_COL + (j & 1) * BK, s0);
       tmem_ld32(lane_base + L::S_COL + (j & 1) * BK + 32, s1);
+      // Scores are already in log2 units (Q carries scale * log2(e)); keys past lk
+      // (only in the last tile) are masked to -inf.
       const int kbase = j * BK;
       float mx = -INFINITY;
+      if (kbase + BK <= a.lk) {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float v0 = kbase + i < a.lk ? __uint_as_float(s0[i]) * a.c : -INFINITY;
-        const float v1 = kbase + 32 + i < a.lk ? __uint_as_float(s1[i]) * a.c : -INFINITY;
-        s0[i] = __float_as_uint(v0);
-        s1[i] = __float_as_uint(v1);
-        mx = fmaxf(mx, fmaxf(v0, v1));
+        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, fmaxf(__uint_as_float(s0[i]), __uint_as_float(s1[i])));
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float v0 = kbase + i < a.lk ? __uint_as_float(s0[i]) : -INFINITY;
+          const float v1 = kbase + 32 + i < a.lk ? __uint_as_float(s1[i]) : -INFINITY;
+          s0[i] = __float_as_uint(v0);
+          s1[i] = __float_as_uint(v1);
+          mx = fmaxf(mx, fmaxf(v0, v1));
+        }
       }
       const float m_new = fmaxf(m, mx);
       const float corr = ex2f(m - m_new);
       float sum = 0.f;
+      float2 sum2 = make_float2(0.f, 0.f);
       // P = exp2(s - m_new) rounded to TF32 (hi) plus, in MODE 0, the residual
       // (lo), written to TMEM one 32-key half at a time. MODE 2: bf16 hi / lo
       // pairs (keys 2i, 2i + 1 in column i), hi over the S tile's first 32
@@ -488,9 +505,10 @@ __global__ void __launch_bounds__(NT, 1)
           uint32_t hp[16], lp[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const float p0 = ex2f(__uint_as_float(sh[2 * i]) - m_new);
-            const float p1 = ex2f(__uint_as_float(sh[2 * i + 1]) - m_new);
-            sum += p0 + p1;
+            const float2 d = ub::fma2(make_float2(__uint_as_float(sh[2 * i]), __uint_as_float(sh[2 * i + 1])),
+                                      make_float2(1.f, 1.f), make_float2(-m_new, -m_new));
+            const float p0 = ex2f(d.x), p1 = ex2f(d.y);
+            sum2 = ub::fma2(make_float2(p0, p1), make_float2(1.f, 1.f), sum2);
             const __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
             const float2 f = __bfloat1622float2(h2);
             const __nv_bfloat162 l2 = __floats2bfloat162_rn(p0 - f.x, p1 - f.y);
@@ -528,7 +546,7 @@ __global__ void __launch_bounds__(NT, 1)
         tc_fence_after();
         fold_tile(corr_prev);
       }
-      l = l * corr + sum;
+      l = l * corr + (sum + (sum2.x + sum2.y));
       m = m_new;
       corr_prev = corr;
       tmem_st_wait();
