@@ -161,8 +161,10 @@ __device__ __forceinline__ void transpose_v(const uint8_t* stage_v, uint8_t* vt,
 __device__ __forceinline__ void split_bf16x4(float4 v, uint2& hi, uint2& lo) {
   const __nv_bfloat162 h0 = __floats2bfloat162_rn(v.x, v.y), h1 = __floats2bfloat162_rn(v.z, v.w);
   const float2 f0 = __bfloat1622float2(h0), f1 = __bfloat1622float2(h1);
-  const __nv_bfloat162 l0 = __floats2bfloat162_rn(v.x - f0.x, v.y - f0.y);
-  const __nv_bfloat162 l1 = __floats2bfloat162_rn(v.z - f1.x, v.w - f1.y);
+  const float2 r0 = ub::fma2(make_float2(f0.x, f0.y), make_float2(-1.f, -1.f), make_float2(v.x, v.y));
+  const float2 r1 = ub::fma2(make_float2(f1.x, f1.y), make_float2(-1.f, -1.f), make_float2(v.z, v.w));
+  const __nv_bfloat162 l0 = __floats2bfloat162_rn(r0.x, r0.y);
+  const __nv_bfloat162 l1 = __floats2bfloat162_rn(r1.x, r1.y);
   hi = make_uint2(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1));
   lo = make_uint2(*reinterpret_cast<const uint32_t*>(&l0), *reinterpret_cast<const uint32_t*>(&l1));
 }
@@ -203,26 +205,31 @@ __device__ __forceinline__ void split_tile_bf16(const uint8_t* p, uint8_t* hi, u
 }
 
 // MODE 2: V staging [2 boxes of (64 keys x 32 dims)] -> V^T hi / lo bf16 tiles [64
-// dims x 64 keys] (keys contiguous). Lane = key of a 32-key half, so the 16-bit stores
-// of one dim row land in four 16-byte chunks.
+// dims x 64 keys] (keys contiguous). Lane l takes keys 2l and 2l + 1 of one 4-dim chunk
+// per step, so each dim's hi and lo parts of the key pair leave as one packed 32-bit
+// store (the 32 lanes of a store fill one 128-byte dim row).
 template <int NW>
 __device__ __forceinline__ void transpose_v_bf16(const uint8_t* stage_v, uint8_t* vt, uint8_t* vt_lo, int t) {
   const int lane = t & 31, w = t >> 5;
+  const int k0 = 2 * lane;
 #pragma unroll
-  for (int u = 0; u < 32 / NW; ++u) {
-    const int unit = w * (32 / NW) + u;  // 32 units: (key half, box, chunk)
-    const int kh = unit >> 4, box = (unit >> 3) & 1, c = unit & 7;
-    const int key = kh * 32 + lane;
-    const float4 val = *reinterpret_cast<const float4*>(stage_v + box * (64 * 128) + key * 128 + ((c ^ (key & 7)) << 4));
-    const float v4[4] = {val.x, val.y, val.z, val.w};
+  for (int u = 0; u < 16 / NW; ++u) {
+    const int unit = w * (16 / NW) + u;  // 16 units: (box, chunk)
+    const int box = unit >> 3, c = unit & 7;
+    const uint8_t* src = stage_v + box * (64 * 128);
+    const float4 va = *reinterpret_cast<const float4*>(src + k0 * 128 + ((c ^ (k0 & 7)) << 4));
+    const float4 vb = *reinterpret_cast<const float4*>(src + (k0 + 1) * 128 + ((c ^ ((k0 + 1) & 7)) << 4));
+    const float a4[4] = {va.x, va.y, va.z, va.w}, b4[4] = {vb.x, vb.y, vb.z, vb.w};
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const int d = box * 32 + c * 4 + e;
-      const int off = sw128h(d, key);
-      const __nv_bfloat16 hb = __float2bfloat16_rn(v4[e]);
-      const __nv_bfloat16 lb = __float2bfloat16_rn(v4[e] - __bfloat162float(hb));
-      *reinterpret_cast<__nv_bfloat16*>(vt + off) = hb;
-      *reinterpret_cast<__nv_bfloat16*>(vt_lo + off) = lb;
+      const int off = sw128h(d, k0);
+      const __nv_bfloat162 h2 = __floats2bfloat162_rn(a4[e], b4[e]);
+      const float2 f = __bfloat1622float2(h2);
+      const float2 r = ub::fma2(f, make_float2(-1.f, -1.f), make_float2(a4[e], b4[e]));
+      const __nv_bfloat162 l2 = __floats2bfloat162_rn(r.x, r.y);
+      *reinterpret_cast<uint32_t*>(vt + off) = *reinterpret_cast<const uint32_t*>(&h2);
+      *reinterpret_cast<uint32_t*>(vt_lo + off) = *reinterpret_cast<const uint32_t*>(&l2);
     }
   }
 }
@@ -511,7 +518,8 @@ __global__ void __launch_bounds__(NT, 1)
             sum2 = ub::fma2(make_float2(p0, p1), make_float2(1.f, 1.f), sum2);
             const __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
             const float2 f = __bfloat1622float2(h2);
-            const __nv_bfloat162 l2 = __floats2bfloat162_rn(p0 - f.x, p1 - f.y);
+            const float2 r = ub::fma2(f, make_float2(-1.f, -1.f), make_float2(p0, p1));
+            const __nv_bfloat162 l2 = __floats2bfloat162_rn(r.x, r.y);
             hp[i] = *reinterpret_cast<const uint32_t*>(&h2);
             lp[i] = *reinterpret_cast<const uint32_t*>(&l2);
           }
