@@ -43,7 +43,9 @@ def test_fused_dconv_freq_rows(model_and_sd, pre, C):
     assert rel_err(a.t.view(B, F, T, C).cpu(), ref) < tol
 
 
-@pytest.mark.parametrize("pre,C,L", [("tencoder.0", 48, 1001), ("tencoder.2", 192, 333)])
+# L = 1008 leaves no capacity rows (groups back to back); 1001 and 333 keep capacity rows.
+@pytest.mark.parametrize("pre,C,L", [("tencoder.0", 48, 1001), ("tencoder.2", 192, 333), ("tencoder.0", 48, 1008),
+                                     ("tencoder.1", 96, 1008)])
 def test_fused_dconv_time_rows_with_capacity(model_and_sd, pre, C, L):
     model, sd = model_and_sd
     B, cap = 2, 4 * -(-L // 4)

@@ -181,18 +181,8 @@ __global__ void __launch_bounds__(ROWS) dconv_apply_kernel(float* __restrict__ x
 // 2*CPT dot products).
 constexpr int CPT = 2;      // output channels per thread
 constexpr int NTH2 = 256;   // threads per CTA (CG * RPP <= NTH2)
-constexpr int IROWS = 64;   // rows per work item
-constexpr int NBUF = 4;     // items in flight: loads run NBUF-1 items ahead of the compute
 
 __device__ __forceinline__ uint32_t sm_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
-
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sm_u32(bar)), "r"(bytes) : "memory");
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   sm_u32(dst)),
-               "l"(src), "r"(bytes), "r"(sm_u32(bar))
-               : "memory");
-}
 
 // Bounded wait (about 2 s of %globaltimer) for the phase `parity` of `bar`; false on timeout.
 __device__ __forceinline__ bool wait_phase(uint64_t* bar, uint32_t parity) {
@@ -706,8 +696,8 @@ extern "C" int unblend_dconv_conv1(const float* x, long long x_gs, int groups, i
   const int mh = maxh_for(hs);
   UB_REQUIRE(mh > 0);
   cudaStream_t st = ub::as_stream(stream);
-  if (hs <= 16 && c % C1_CK == 0 && x_gs % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
-      (reinterpret_cast<uintptr_t>(h) & 15) == 0) {
+  const bool aligned = (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(h) & 15) == 0;
+  if (hs <= 16 && c % C1_CK == 0 && x_gs % 4 == 0 && aligned) {
     const size_t smem1 = sizeof(float) * ((size_t)3 * c * hs + (size_t)(C1_IR + 2 * dil) * C1_XS);
     UB_REQUIRE(smem1 <= 200 * 1024);
     dim3 grid1((rows + C1_IR - 1) / C1_IR, groups);
