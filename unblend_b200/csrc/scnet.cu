@@ -353,19 +353,18 @@ __device__ __forceinline__ void st_cluster_v4(uint32_t local_addr, uint32_t rank
 
 __device__ __forceinline__ float sigmoid_f(float v) { return 1.0f / (1.0f + expf(-v)); }
 
-// acc[q][g] += w.q * h[g] for the four gates q and SG sequences g.
+// acc[q][p] += w.q * (h[2p], h[2p + 1]) for the four gates q and SG / 2 sequence pairs p,
+// as packed two-lane FMAs.
 template <int SG>
-__device__ __forceinline__ void lstm_fma4(float (&acc)[4][SG], const float4 w, const float4 (&h)[SG / 4]) {
+__device__ __forceinline__ void lstm_fma4(float2 (&acc)[4][SG / 2], const float4 w, const float4 (&h)[SG / 4]) {
 #pragma unroll
   for (int h4 = 0; h4 < SG / 4; ++h4) {
-    const float hv[4] = {h[h4].x, h[h4].y, h[h4].z, h[h4].w};
+    const float2 h01 = make_float2(h[h4].x, h[h4].y), h23 = make_float2(h[h4].z, h[h4].w);
+    const float wq[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int g = 4 * h4 + e;
-      acc[0][g] = fmaf(w.x, hv[e], acc[0][g]);
-      acc[1][g] = fmaf(w.y, hv[e], acc[1][g]);
-      acc[2][g] = fmaf(w.z, hv[e], acc[2][g]);
-      acc[3][g] = fmaf(w.w, hv[e], acc[3][g]);
+    for (int q = 0; q < 4; ++q) {
+      acc[q][2 * h4] = ub::fma2(make_float2(wq[q], wq[q]), h01, acc[q][2 * h4]);
+      acc[q][2 * h4 + 1] = ub::fma2(make_float2(wq[q], wq[q]), h23, acc[q][2 * h4 + 1]);
     }
   }
 }
@@ -423,11 +422,11 @@ __global__ void __launch_bounds__(256, 1) lstm_cluster_kernel(const float* __res
     const int step = dir == 0 ? it : steps - 1 - it;
     const float* hcur = hb + (it & 1) * HID * G + sbase;
     float* hnext = hb + ((it + 1) & 1) * HID * G;
-    float acc[4][SG];
+    float2 acc[4][SG / 2];
 #pragma unroll
     for (int q = 0; q < 4; ++q)
 #pragma unroll
-      for (int g = 0; g < SG; ++g) acc[q][g] = nx[q][g];
+      for (int p = 0; p < SG / 2; ++p) acc[q][p] = make_float2(nx[q][2 * p], nx[q][2 * p + 1]);
     if (it + 1 < steps) {
       const int sn = dir == 0 ? it + 1 : steps - 2 - it;
 #pragma unroll
@@ -471,10 +470,12 @@ __global__ void __launch_bounds__(256, 1) lstm_cluster_kernel(const float* __res
     float hn[SG];
 #pragma unroll
     for (int g = 0; g < SG; ++g) {
-      const float ig = sigmoid_f(acc[0][g]);
-      const float fg = sigmoid_f(acc[1][g]);
-      const float gg = tanhf(acc[2][g]);
-      const float og = sigmoid_f(acc[3][g]);
+      const float a0 = g & 1 ? acc[0][g >> 1].y : acc[0][g >> 1].x, a1 = g & 1 ? acc[1][g >> 1].y : acc[1][g >> 1].x;
+      const float a2 = g & 1 ? acc[2][g >> 1].y : acc[2][g >> 1].x, a3 = g & 1 ? acc[3][g >> 1].y : acc[3][g >> 1].x;
+      const float ig = sigmoid_f(a0);
+      const float fg = sigmoid_f(a1);
+      const float gg = tanhf(a2);
+      const float og = sigmoid_f(a3);
       cst[g] = fg * cst[g] + ig * gg;
       hn[g] = og * tanhf(cst[g]);
       if (live[g]) h_out[(rowb[g] + step * step_stride) * hs + dir * (long long)HID + unit] = hn[g];
