@@ -148,3 +148,23 @@ def test_free_memory_query_is_reused_and_corrected(monkeypatch):
     assert eng._free_device_bytes(dev) == 7_000 and state["queries"] == 1
     state["now"] += 0.6  # the cached answer is older than a second: query again
     assert eng._free_device_bytes(dev) == 10_000 and state["queries"] == 2
+
+
+def test_tail_padding_rule_for_graph_replayed_models():
+    """Fixed-shape models are zero-padded up to the batch, except that models whose graphs
+    leave smaller batches to eager launches (``_eager_tails``) keep tails below 7/8 of it."""
+    from types import SimpleNamespace
+
+    from unblend_b200.apply import _PooledRun
+
+    def rows(model, n, cbs=16):
+        run = _PooledRun(model, [], torch.device("cpu"), 8, 4, cbs, 1.0, None, None, True)
+        return run._rows(n)
+
+    plain = SimpleNamespace(_fixed_batch_shape=False)
+    fixed = SimpleNamespace(_fixed_batch_shape=True)
+    eager = SimpleNamespace(_fixed_batch_shape=True, _eager_tails=True)
+    assert [rows(plain, n) for n in (2, 14, 16)] == [2, 14, 16]
+    assert [rows(fixed, n) for n in (2, 14, 16)] == [16, 16, 16]
+    assert [rows(eager, n) for n in (2, 13, 14, 16)] == [2, 13, 16, 16]
+    assert rows(eager, 31, 32) == 32 and rows(eager, 27, 32) == 27

@@ -133,6 +133,9 @@ def test_compiled_core_replays_cuda_graphs():
     ma.enable_compiled_core()
     out = apply_model(ma, ga["mix"].cuda(), overlap=ga["overlap"], chunk_batch_size=ga["chunk_batch_size"])
     assert rel_err(out.cpu()[..., :: ga["decimate"]], ga["shifts0"]["out"]) < FP32_TOL
+    # 4 chunks at 3 per batch: the full batch is replayed from a graph, the 1-chunk tail
+    # (below 7/8 of a batch) runs eagerly at its own size instead of being padded.
+    assert [k[0][0] for k in ma.__dict__["_graphed"].graphs] == [ga["chunk_batch_size"]]
     assert _lib.error_flag() == 0
 
 

@@ -318,8 +318,15 @@ class _PooledRun:
         return y
 
     def _rows(self, n: int) -> int:
-        # Captured CUDA graphs replay one batch shape: tails are zero-padded up to it.
-        return self.cbs if self.fixed and n < self.cbs else n
+        # Captured CUDA graphs replay one batch shape: tails are zero-padded up to it
+        # (unblend/apply.py:1189-1196). Models whose graphs leave smaller batches to eager
+        # launches (``_eager_tails``) are padded only when the tail is within an eighth of
+        # the full batch; a smaller tail runs at its own size instead of computing padding.
+        if not self.fixed or n >= self.cbs:
+            return n
+        if getattr(self.model, "_eager_tails", False) and 8 * n < 7 * self.cbs:
+            return n
+        return self.cbs
 
     def run_batch(self, items: list[tuple[int, int]]) -> list[dict]:
         n, C, seg, S = len(items), self.C, self.segment, self.S

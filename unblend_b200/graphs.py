@@ -8,7 +8,9 @@ captured as-is into a ``torch.cuda.CUDAGraph`` per input shape: the first call
 with a shape runs the forward once eagerly (lazy kernel attributes, tables),
 then captures it; later calls copy the input into the captured buffer and
 replay the graph, so a forward costs one graph launch on the host instead of a
-few hundred kernel launches.
+few hundred kernel launches. A batch smaller than one already captured (a tail)
+runs eagerly at its own size; ``apply_model`` pads such tails up to the captured
+shape only when they are within an eighth of it (``_eager_tails``).
 """
 
 from __future__ import annotations
@@ -30,6 +32,11 @@ class GraphedForward:
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         key = (tuple(x.shape), x.dtype, x.device)
         entry = self.graphs.get(key)
+        if entry is None and any(k[0][1:] == key[0][1:] and k[0][0] > x.shape[0] and k[1:] == key[1:]
+                                 for k in self.graphs):
+            # A tail batch smaller than a captured one: eager launches at its own size
+            # (a graph per tail size would hold a private memory pool each).
+            return self.fn(x)
         if entry is None:
             static_in = x.clone()
             side = torch.cuda.Stream(device=x.device)

@@ -111,6 +111,7 @@ class HTDemucsCuda(ConvNet):
         self.max_allowed_segment = cfg["segment"]
         self.segment_length = int(round(cfg["segment"] * cfg["samplerate"]))
         self._fixed_batch_shape = False
+        self._eager_tails = False
         self.depth = cfg["depth"]
         self._pack(state_dict)
 
@@ -593,12 +594,13 @@ class HTDemucsCuda(ConvNet):
         self._tables(dev, nfft // 2 // 4**self.depth, frames, lt)
 
     def enable_compiled_core(self) -> None:
-        """Replay the forward from CUDA graphs (one per batch shape); tail batches get zero-padded."""
+        """Replay the forward from CUDA graphs; tails below 7/8 of the captured batch run eagerly, others are zero-padded."""
         from .graphs import GraphedForward
 
         self.prefill_inference_caches()
         self.__dict__["_graphed"] = GraphedForward(self._forward_arena)
         self._fixed_batch_shape = True
+        self._eager_tails = True
 
     def disable_compiled_core(self) -> None:
         """Back to eager launches; releases the captured graphs."""
@@ -606,6 +608,7 @@ class HTDemucsCuda(ConvNet):
         if graphed is not None:
             graphed.release()
         self._fixed_batch_shape = False
+        self._eager_tails = False
 
     def select_sources(self, names: list[str] | None) -> "HTDemucsCuda":
         """Materialise only the named stems (all of them when ``names`` is None).

@@ -147,6 +147,7 @@ class BSRoformerCuda(nn.Module):
         # configure_inference turns it on (unblend/roformer.py:1064, 1524).
         self.match_input_audio_length = bool(cfg.get("match_input_audio_length", False))
         self._fixed_batch_shape = False
+        self._eager_tails = False
         self._pack(state_dict)
         self._device = torch.device("cpu")
 
@@ -412,12 +413,13 @@ class BSRoformerCuda(nn.Module):
             self._tables(1 + seg // self.hop)
 
     def enable_compiled_core(self) -> None:
-        """Replay the forward from CUDA graphs (one per batch shape); tail batches get zero-padded."""
+        """Replay the forward from CUDA graphs; tails below 7/8 of the captured batch run eagerly, others are zero-padded."""
         from .graphs import GraphedForward
 
         self.prefill_inference_caches()
         self.__dict__["_graphed"] = GraphedForward(self._forward_impl)
         self._fixed_batch_shape = True
+        self._eager_tails = True
 
     def disable_compiled_core(self) -> None:
         """Back to eager launches; releases the captured graphs."""
@@ -425,6 +427,7 @@ class BSRoformerCuda(nn.Module):
         if graphed is not None:
             graphed.release()
         self._fixed_batch_shape = False
+        self._eager_tails = False
 
     def _forward_impl(self, mix: torch.Tensor) -> torch.Tensor:
         """The forward on a contiguous fp32 ``[B, 2, L]`` CUDA mixture."""

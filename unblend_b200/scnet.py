@@ -93,6 +93,7 @@ class SCNetCuda(ConvNet):
         self.audio_channels = 2
         self.max_allowed_segment = cfg.get("segment_samples", 485100) / float(self.samplerate)
         self._fixed_batch_shape = False
+        self._eager_tails = False
         self.dims = list(cfg["dims"])
         self._pack({k: v.detach().float().cpu() for k, v in state_dict.items()})
         self.__dict__["_win_cache"] = {}
@@ -416,11 +417,12 @@ class SCNetCuda(ConvNet):
 
     # ------------------------------------------------------------------ optional hooks (unblend/backends.py:62-111)
     def enable_compiled_core(self) -> None:
-        """Replay the forward from CUDA graphs (one per batch shape); tail batches get zero-padded."""
+        """Replay the forward from CUDA graphs; tails below 7/8 of the captured batch run eagerly, others are zero-padded."""
         from .graphs import GraphedForward
 
         self.__dict__["_graphed"] = GraphedForward(self._forward_arena)
         self._fixed_batch_shape = True
+        self._eager_tails = True
 
     def disable_compiled_core(self) -> None:
         """Back to eager launches; releases the captured graphs."""
@@ -428,6 +430,7 @@ class SCNetCuda(ConvNet):
         if graphed is not None:
             graphed.release()
         self._fixed_batch_shape = False
+        self._eager_tails = False
 
 
 def build_scnet(architecture: str, config: dict, *, sources: list[str], samplerate: int, segment_samples: int,
