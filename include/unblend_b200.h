@@ -82,6 +82,10 @@ typedef struct {
    * feed bf16 consumers directly: no GLU, residual or output groups, n_out a multiple
    * of 32, whole 16-row tiles (the TMA bulk-store epilogue). */
   int y_bf16;
+  /* 1: x is bf16 (tensor-core mode 3 only): activations a producing kernel wrote as
+   * bf16 for a consumer that multiplies in bf16; unit stride along w, row strides
+   * multiples of 8 elements. */
+  int x_bf16;
 } UnblendConvParams;
 
 /* Conv1d / Conv2d / Linear (unblend/blocks.py:461,467,695,297,300; torch nn.Linear in
@@ -94,13 +98,14 @@ int unblend_conv2d_f32(const float* x, const float* w, const float* bias, float*
  * given as w_hi = w with the low 13 mantissa bits cleared and w_lo = w - w_hi
  * (fp32, [n_out, K]); mode 1: bf16 operands, w_hi is bf16 [n_out, K], w_lo
  * unused; mode 2: fp32 accuracy by the 3-pass bf16 split, w_hi = bf16(w) and
- * w_lo = bf16(w - w_hi) (bf16, [n_out, K]). block_n: 64, 96, 128, 192 or 256
+ * w_lo = bf16(w - w_hi) (bf16, [n_out, K]); mode 3: as mode 1 with bf16 x
+ * (p->x_bf16 = 1; x is fp32 in the other modes). block_n: 64, 96, 128, 192 or 256
  * output channels per tile. Requirements:
  * no prologue, c_in % 8 == 0 and >= 16, unit stride along w (or the stride-4
  * kernel-8 pad-2 time convolution, whose input rows up to a multiple of 4
  * past w_in must be zero), n_group and all output strides multiples of 4.
  * Replaces the same reference operators as unblend_conv2d_f32. */
-int unblend_conv2d_tc(const float* x, const void* w_hi, const void* w_lo, const float* bias, float* y,
+int unblend_conv2d_tc(const void* x, const void* w_hi, const void* w_lo, const float* bias, float* y,
                       const UnblendConvParams* p, int mode, int block_n, void* stream);
 
 /* Read the device flag that the tensor-core kernels set when a bounded
@@ -198,6 +203,13 @@ int unblend_dconv_error_flag(int* out_host, int clear);
 int unblend_layer_norm(const float* x, float* y, const float* gamma, const float* beta,
                        const float* pos, float pos_scale, long long pos_rows, long long rows,
                        int c, void* stream);
+
+/* The same LayerNorm written as bf16 (round to nearest even), for rows that only feed
+ * bf16 tensor-core GEMMs (the transformer projections and FeedForward input in bf16
+ * precision): replaces the same torch nn.LayerNorm (unblend/transformer.py:328-359). */
+int unblend_layer_norm_bf16(const float* x, void* y, const float* gamma, const float* beta,
+                            const float* pos, float pos_scale, long long pos_rows, long long rows,
+                            int c, void* stream);
 
 /* Multi-head attention core softmax(Q K^T * scale) V for all heads
  * (torch nn.MultiheadAttention, unblend/transformer.py:290-301, 402-412).

@@ -311,6 +311,7 @@ def _conv_tc(x, w, b, y, mode, block_n, **kw):
     if kw.get("post") is not None:
         p.post, p.post_sh = kw["post"].data_ptr(), kw["post"].shape[1]
     p.y_bf16 = 1 if y.dtype == torch.bfloat16 else 0
+    p.x_bf16 = 1 if x.dtype == torch.bfloat16 else 0
     _lib.call("unblend_conv2d_tc", x.data_ptr(), whi.data_ptr(), _lib.ptr(wlo), _lib.ptr(b), y.data_ptr(),
               ctypes.byref(p), mode, block_n)
     torch.cuda.synchronize()
@@ -464,3 +465,40 @@ def test_tc_bf16_output(block_n):
              out_s=(L * N, L * N, N))
     ref = x @ w[:, 0, 0].t() + b
     assert rel_err(y.float(), ref) < TC_TOL[_lib.TC_BF16]
+
+
+@pytest.mark.parametrize("kh,kw,C,N,block_n,act", [(3, 3, 48, 96, 96, ACT_GLU), (1, 1, 512, 512, 256, ACT_GELU),
+                                                   (1, 3, 64, 192, 192, ACT_NONE)])
+def test_tc_bf16_activations_match_the_converted_path(kh, kw, C, N, block_n, act):
+    """Mode 3 (bf16 activations loaded as they are) against mode 1 on the same values in fp32:
+    mode 1 rounds its fp32 A tiles to bf16 (nearest even) before the same MMAs, so the two
+    outputs are identical, sub-tap groups of 3-wide kernel rows included."""
+    B, H, W = 2, 5, 300
+    x = _cl((B, H, W, C)).to(torch.bfloat16)
+    w, b = _cl((N, kh, kw, C)) * 0.05, _cl((N,))
+    n_final = N // 2 if act == ACT_GLU else N
+    outs = []
+    for mode, xin in ((_lib.TC_BF16, x.float()), (_lib.TC_BF16_ACT, x)):
+        y = torch.empty(B, H, W, n_final, device="cuda")
+        _conv_tc(xin, w, b, y, mode, block_n, B=B, H=H, W=W, C=C, in_s=(H * W * C, W * C, C), Ho=H, Wo=W, N=N,
+                 out_s=(H * W * n_final, W * n_final, n_final), kh=kh, kw=kw, ph=kh // 2, pw=kw // 2, act=act)
+        outs.append(y)
+    assert torch.equal(outs[0], outs[1])
+    ref = _ref_conv(x.float(), w, b, kh, kw, 1, 1, 1, 1, kh // 2, kw // 2)
+    if act == ACT_GLU:
+        ref = ref[..., 0::2] * torch.sigmoid(ref[..., 1::2])
+    elif act == ACT_GELU:
+        ref = torch.nn.functional.gelu(ref)
+    assert rel_err(outs[1], ref) < TC_TOL[_lib.TC_BF16]
+
+
+def test_layer_norm_bf16_output():
+    rows, c = 3000, 512
+    x = torch.randn(rows, c, device="cuda") * 3 + 1
+    g, bt = torch.randn(c, device="cuda"), torch.randn(c, device="cuda")
+    y = torch.empty(rows, c, device="cuda", dtype=torch.bfloat16)
+    _lib.call("unblend_layer_norm_bf16", x.data_ptr(), y.data_ptr(), g.data_ptr(), bt.data_ptr(), None, 1.0, 1,
+              rows, c)
+    ref = torch.nn.functional.layer_norm(x, (c,), g, bt, 1e-5)
+    # One bf16 rounding of an fp32-accurate value: within half an ulp of bf16 (2^-9 relative).
+    assert ((y.float() - ref).abs() <= ref.abs() * 2.0 ** -8 + 1e-6).all()

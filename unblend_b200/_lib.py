@@ -47,7 +47,7 @@ class ConvParams(ctypes.Structure):
         ("res", c_void_p), ("res_scale", c_void_p),
         ("stats", c_void_p), ("stats_per_h", c_int),
         ("post", c_void_p), ("post_sh", c_ll),
-        ("y_bf16", c_int),
+        ("y_bf16", c_int), ("x_bf16", c_int),
     ]
 
 
@@ -94,6 +94,8 @@ _SIGNATURES = {
                            c_ll, c_void_p],
     "unblend_layer_norm": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_ll, c_ll, c_int,
                            c_void_p],
+    "unblend_layer_norm_bf16": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_ll, c_ll, c_int,
+                                c_void_p],
     "unblend_attention_f32": [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
                               c_ll, c_ll, c_ll, c_ll, c_ll, c_ll, c_float, c_void_p],
     "unblend_add": [c_void_p, c_void_p, c_void_p, c_ll, c_ll, c_float, c_void_p],
@@ -158,7 +160,7 @@ _HOST_SIGNATURES = {
     "unblend_dconv_error_flag": [ctypes.POINTER(c_int), c_int],
 }
 
-TC_TF32X3, TC_BF16, TC_BF16X3 = 0, 1, 2
+TC_TF32X3, TC_BF16, TC_BF16X3, TC_BF16_ACT = 0, 1, 2, 3
 
 _lib = None
 

@@ -246,16 +246,19 @@ class ConvNet(nn.Module):
                 mode = _lib.TC_BF16X3 if self.fp32_split == "bf16x3" and wide else _lib.TC_TF32X3
             else:
                 mode = _lib.TC_BF16
-                bn256 = self._bn256_min[mode]
+                if x.t.dtype == torch.bfloat16:
+                    # Activations a producer wrote as bf16 for this layer: loaded as they are.
+                    mode, p.x_bf16 = _lib.TC_BF16_ACT, 1
+                bn256 = self._bn256_min[_lib.TC_BF16]
                 if kw == 3 and sw == 1 and dw * 2 <= 8:
                     # 3-wide kernel rows: tiles of <= 192 columns share one A load across the three taps.
                     bn256 = 1 << 30
                 block_n = _block_n(n_out, bn256, _m_tiles(x.B, h_out, w_out), self._sms(x))
-            whi, wlo = self._tc_weight(w, mode)
+            whi, wlo = self._tc_weight(w, _lib.TC_BF16 if mode == _lib.TC_BF16_ACT else mode)
             _lib.call("unblend_conv2d_tc", x.t.data_ptr(), whi.data_ptr(), _lib.ptr(wlo), _lib.ptr(b), y,
                       ctypes_byref(p), mode, block_n, work=flops)
             return
-        assert not y_bf16, "bf16 output needs the tensor-core path"
+        assert not y_bf16 and x.t.dtype == torch.float32, "bf16 activations need the tensor-core path"
         _lib.call("unblend_conv2d_f32", x.t.data_ptr(), w.data_ptr(), _lib.ptr(b), y, ctypes_byref(p), work=flops)
         if post is not None:
             # CUDA-core path: the same add as a separate pass over the dense output.
@@ -276,6 +279,8 @@ class ConvNet(nn.Module):
         if self.precision == "fp32-simt" or prologue not in (PRO_NONE, PRO_ADD):
             return False
         if x.C % 8 or x.C < 16 or x.sw != x.C or x.sh % 4 or x.sb % 4:
+            return False
+        if x.t.dtype == torch.bfloat16 and (self.precision != "bf16" or p.sw != 1 or x.sh % 8 or x.sb % 8):
             return False
         if p.sw != 1:
             cap = x.sb // x.C

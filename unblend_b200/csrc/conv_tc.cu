@@ -21,7 +21,10 @@
 // converted to bf16 and multiplied with bf16 weights (kind::f16). 3-pass bf16
 // mode (MODE 2): the same three products with bf16 hi / lo parts (hi = x
 // rounded to bf16, lo = x - hi rounded to bf16, 16 significant bits in all) in
-// kind::f16, whose MMAs take 16 channels each instead of 8.
+// kind::f16, whose MMAs take 16 channels each instead of 8. bf16-activation mode
+// (MODE 3): the input is already bf16 in memory (written by the producing kernel
+// for a consumer that multiplies in bf16), so TMA lands the A tile in its MMA
+// layout and nothing is converted; otherwise as the bf16 mode.
 // The accumulator lives in TMEM (128 lanes x BN fp32 columns); the epilogue
 // reads it with tcgen05.ld and applies bias, GELU / GLU, the LayerScale
 // residual and GroupNorm statistics, as the SIMT kernel does.
@@ -101,7 +104,7 @@ struct ChunkK {
 // from L2 once per kernel row instead of once per tap.
 template <int BN, int MODE>
 struct SubTaps {
-  static constexpr int value = (MODE == 1 && BN <= 192) ? 3 : 1;
+  static constexpr int value = ((MODE == 1 || MODE == 3) && BN <= 192) ? 3 : 1;
 };
 
 template <int BN, int MODE>
@@ -110,14 +113,14 @@ struct Layout {
   static constexpr int NSUB = SubTaps<BN, MODE>::value;
   static constexpr int A_ROWS = NSUB > 1 ? 136 : 128;                 // 128 rows + shift headroom
   static constexpr int ROWB = KC * 4;                                 // fp32 bytes per staged row
-  static constexpr int A_BYTES = A_ROWS * ROWB;                       // fp32 staging, A_ROWS x KC
+  static constexpr int A_BYTES = MODE == 3 ? 0 : A_ROWS * ROWB;       // fp32 staging, A_ROWS x KC (none: MODE 3)
   // lo (fp32) or bf16 tile in shared memory (1 KB aligned); none with A in TMEM
   // (MODE 2: bf16 hi and lo tiles, AT_BYTES apart)
   static constexpr int AT_BYTES = (A_ROWS * 64 + 1023) / 1024 * 1024;
   static constexpr int AC_BYTES =
       ATmem<BN, MODE>::value ? 0 : MODE == 0 ? A_ROWS * ROWB : MODE == 2 ? 2 * AT_BYTES : AT_BYTES;
   static constexpr int B_BYTES = MODE == 0 ? BN * ROWB : BN * 64;     // one weight tile
-  static constexpr int B_TILES = MODE == 1 ? 1 : 2;                   // hi + lo, or bf16
+  static constexpr int B_TILES = (MODE == 1 || MODE == 3) ? 1 : 2;   // hi + lo, or bf16
   static constexpr int STAGE = A_BYTES + AC_BYTES + NSUB * B_TILES * B_BYTES;
   static constexpr int STAGES = (200 * 1024) / STAGE > 4 ? 4 : (200 * 1024) / STAGE;
   static constexpr int A_COL = 2 * BN;  // first TMEM column of the A stages (A in TMEM)
@@ -141,7 +144,7 @@ __device__ __forceinline__ float tanh_approx(float x) {
 // hardware exp2 and reciprocal (relative error ~1e-7).
 template <int MODE>
 __device__ __forceinline__ float epi_gelu(float x) {
-  if (MODE == 1) {
+  if (MODE == 1 || MODE == 3) {
     const float z = 0.7978845608028654f * fmaf(0.044715f * x, x * x, x);
     return 0.5f * x * (1.0f + tanh_approx(z));
   }
@@ -150,7 +153,7 @@ __device__ __forceinline__ float epi_gelu(float x) {
 
 template <int MODE>
 __device__ __forceinline__ float epi_sigmoid(float x) {
-  if (MODE == 1) return fmaf(0.5f, tanh_approx(0.5f * x), 0.5f);
+  if (MODE == 1 || MODE == 3) return fmaf(0.5f, tanh_approx(0.5f * x), 0.5f);
   return __frcp_rn(1.0f + __expf(-x));
 }
 
@@ -213,7 +216,7 @@ __global__ void __launch_bounds__(NT, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      const uint32_t bytes_a = (uint32_t)(a.a_rows * L::ROWB);
+      const uint32_t bytes_a = (uint32_t)(a.a_rows * (MODE == 3 ? 64 : L::ROWB));
       int it = 0;
       bool ok = true;
       for (long long t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
@@ -234,7 +237,7 @@ __global__ void __launch_bounds__(NT, 1)
             tma_load_4d(st, &mapA, &full[s], ca + cc, wa, ha, c.b);
             uint8_t* sb = st + L::A_BYTES + L::AC_BYTES;
             tma_load_2d(sb, &mapB, &full[s], kb + cc, c.n0);
-            if (MODE != 1) tma_load_2d(sb + L::B_BYTES, &mapB2, &full[s], kb + cc, c.n0);
+            if (MODE == 0 || MODE == 2) tma_load_2d(sb + L::B_BYTES, &mapB2, &full[s], kb + cc, c.n0);
             if (L::NSUB > 1 && ns > 1) tma_load_2d(sb + L::B_BYTES, &mapB, &full[s], a.tap_k1[tap] + cc, c.n0);
             if (L::NSUB > 2 && ns > 2) tma_load_2d(sb + 2 * L::B_BYTES, &mapB, &full[s], a.tap_k2[tap] + cc, c.n0);
           }
@@ -391,6 +394,8 @@ __global__ void __launch_bounds__(NT, 1)
             hi[k] = vh;
             lo[k] = make_float4(v.x - vh.x, v.y - vh.y, v.z - vh.z, v.w - vh.w);
           }
+        } else if (MODE == 3) {
+          // The TMA wrote the bf16 tile in its MMA layout: nothing to convert.
         } else if (MODE == 2) {
           // hi = bf16(v), lo = bf16(v - hi): both written as 64-byte swizzled bf16 tiles.
           const uint8_t* src = st;
@@ -733,10 +738,11 @@ extern "C" int unblend_error_flag(int* out_host, int clear) {
   return 0;
 }
 
-extern "C" int unblend_conv2d_tc(const float* x, const void* w_hi, const void* w_lo, const float* bias, float* y,
+extern "C" int unblend_conv2d_tc(const void* x, const void* w_hi, const void* w_lo, const float* bias, float* y,
                                  const UnblendConvParams* p, int mode, int block_n, void* stream) {
-  UB_REQUIRE(x && w_hi && y && p && (mode == 0 || mode == 1 || mode == 2));
-  UB_REQUIRE(mode == 1 || w_lo);
+  UB_REQUIRE(x && w_hi && y && p && mode >= 0 && mode <= 3);
+  UB_REQUIRE((mode == 3) == (p->x_bf16 != 0));  // mode 3 takes bf16 activations, the others fp32
+  UB_REQUIRE(mode == 1 || mode == 3 || w_lo);  // the split modes take hi and lo weights
   UB_REQUIRE(block_n == 64 || block_n == 96 || block_n == 128 || block_n == 192 || block_n == 256);
   UB_REQUIRE(p->prologue == UNBLEND_PRO_NONE);
   UB_REQUIRE(p->c_in % 8 == 0 && p->c_in >= 16);
@@ -744,6 +750,9 @@ extern "C" int unblend_conv2d_tc(const float* x, const void* w_hi, const void* w
              p->out_sb % 4 == 0);
   UB_REQUIRE(p->act != UNBLEND_ACT_GLU || p->n_out % 2 == 0);
   UB_REQUIRE(p->in_sw == p->c_in && p->in_sh % 4 == 0 && p->in_sb % 4 == 0);
+  // bf16 rows: 16-byte aligned row starts for the tensor map, unit stride only.
+  UB_REQUIRE(mode != 3 || (p->sw == 1 && p->c_in % 8 == 0 && p->in_sh % 8 == 0 && p->in_sb % 8 == 0 &&
+                           (reinterpret_cast<uintptr_t>(x) & 15) == 0));
   UB_REQUIRE(!bias || (reinterpret_cast<uintptr_t>(bias) & 15) == 0);
   UB_REQUIRE((reinterpret_cast<uintptr_t>(y) & 15) == 0 && (!p->res || (reinterpret_cast<uintptr_t>(p->res) & 15) == 0));
   UB_REQUIRE(p->act != UNBLEND_ACT_GLU || p->n_out % 4 == 0);
@@ -783,15 +792,16 @@ extern "C" int unblend_conv2d_tc(const float* x, const void* w_hi, const void* w
     dims[1] = (cuuint64_t)p->w_in;
     dims[2] = (cuuint64_t)p->h_in;
     dims[3] = (cuuint64_t)p->batch;
-    strides[0] = (cuuint64_t)p->in_sw * 4;
-    strides[1] = (cuuint64_t)p->in_sh * 4;
-    strides[2] = (cuuint64_t)p->in_sb * 4;
+    const cuuint64_t es = mode == 3 ? 2 : 4;  // input element bytes
+    strides[0] = (cuuint64_t)p->in_sw * es;
+    strides[1] = (cuuint64_t)p->in_sh * es;
+    strides[2] = (cuuint64_t)p->in_sb * es;
     a.a_sh = p->sh;
     UB_REQUIRE(kh_taps * kw_taps <= MAXT);
     // Up to three consecutive taps of a kernel row share one A load when the
     // kernel groups sub-taps (bf16 mode, tiles up to 192 columns) and their
     // shifts stay within the 8 rows of headroom.
-    const int nsub = (mode == 1 && block_n <= 192) ? 3 : 1;
+    const int nsub = ((mode == 1 || mode == 3) && block_n <= 192) ? 3 : 1;
     for (int i = 0; i < kh_taps; ++i)
       for (int j = 0; j < kw_taps;) {
         int n = kw_taps - j < nsub ? kw_taps - j : nsub;
@@ -861,8 +871,13 @@ extern "C" int unblend_conv2d_tc(const float* x, const void* w_hi, const void* w
   a.tiles_w = (p->w_out + m_valid - 1) / m_valid;
   a.tiles_n = (p->n_out + block_n - 1) / block_n;
   cuuint32_t boxA[4] = {(cuuint32_t)kc, (cuuint32_t)a.a_rows, 1, 1};
-  if (!make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, dims, strides, boxA, kc_swizzle))
+  if (mode == 3) {
+    // bf16 rows of 32 channels (64 bytes): the MMA's 64-byte swizzled K-major layout.
+    if (!make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, x, dims, strides, boxA, CU_TENSOR_MAP_SWIZZLE_64B))
+      return UNBLEND_ERR_INVALID;
+  } else if (!make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, dims, strides, boxA, kc_swizzle)) {
     return UNBLEND_ERR_INVALID;
+  }
   // Weights [N, K] (K contiguous): fp32 hi/lo pair or bf16.
   cuuint64_t wd[2] = {(cuuint64_t)K, (cuuint64_t)p->n_out};
   if (mode == 0) {
@@ -911,6 +926,13 @@ extern "C" int unblend_conv2d_tc(const float* x, const void* w_hi, const void* w
     if (block_n == 128) return launch<128, 0>(ma, mb, mb2, mo, a, tiles, st);
     if (block_n == 192) return launch<192, 0>(ma, mb, mb2, mo, a, tiles, st);
     return launch<256, 0>(ma, mb, mb2, mo, a, tiles, st);
+  }
+  if (mode == 3) {
+    if (block_n == 64) return launch<64, 3>(ma, mb, mb2, mo, a, tiles, st);
+    if (block_n == 96) return launch<96, 3>(ma, mb, mb2, mo, a, tiles, st);
+    if (block_n == 128) return launch<128, 3>(ma, mb, mb2, mo, a, tiles, st);
+    if (block_n == 192) return launch<192, 3>(ma, mb, mb2, mo, a, tiles, st);
+    return launch<256, 3>(ma, mb, mb2, mo, a, tiles, st);
   }
   if (mode == 2) {
     if (block_n == 64) return launch<64, 2>(ma, mb, mb2, mo, a, tiles, st);

@@ -127,7 +127,9 @@ __global__ void dconv_tail_kernel(float* __restrict__ x, const float* __restrict
 }
 
 // One warp per row; c <= 1024 and c % 32 == 0 not required.
-__global__ void layer_norm_kernel(const float* __restrict__ x, float* __restrict__ y,
+// One warp per row. OutT float, or __nv_bfloat16 for a row that only feeds bf16 GEMMs.
+template <typename OutT>
+__global__ void layer_norm_kernel(const float* __restrict__ x, OutT* __restrict__ y,
                                   const float* __restrict__ gamma, const float* __restrict__ beta,
                                   const float* __restrict__ pos, float pos_scale, long long pos_rows,
                                   long long rows, int c) {
@@ -157,7 +159,7 @@ __global__ void layer_norm_kernel(const float* __restrict__ x, float* __restrict
   }
   const float var = ub::warp_sum(s2) / c;
   const float rstd = rsqrtf(var + 1e-5f);
-  float* yr = y + row * c;
+  OutT* yr = y + row * c;
   const float* pr = pos ? pos + (row % pos_rows) * c : nullptr;
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
@@ -165,7 +167,10 @@ __global__ void layer_norm_kernel(const float* __restrict__ x, float* __restrict
     if (j < nper && ch < c) {
       float v = (vals[j] - mean) * rstd * gamma[ch] + beta[ch];
       if (pr) v += pos_scale * pr[ch];
-      yr[ch] = v;
+      if constexpr (sizeof(OutT) == 2)
+        yr[ch] = __float2bfloat16_rn(v);
+      else
+        yr[ch] = v;
     }
   }
 }
@@ -355,8 +360,20 @@ extern "C" int unblend_layer_norm(const float* x, float* y, const float* gamma, 
   UB_REQUIRE(x && y && gamma && beta && rows > 0 && c > 0 && c <= 1024);
   UB_REQUIRE(!pos || pos_rows > 0);
   unsigned grid = (unsigned)((rows + 7) / 8);
-  layer_norm_kernel<<<grid, 256, 0, ub::as_stream(stream)>>>(x, y, gamma, beta, pos, pos_scale,
-                                                               pos_rows, rows, c);
+  layer_norm_kernel<float><<<grid, 256, 0, ub::as_stream(stream)>>>(x, y, gamma, beta, pos, pos_scale,
+                                                                      pos_rows, rows, c);
+  UB_CHECK_LAUNCH();
+  return 0;
+}
+
+extern "C" int unblend_layer_norm_bf16(const float* x, void* y, const float* gamma, const float* beta,
+                                       const float* pos, float pos_scale, long long pos_rows, long long rows,
+                                       int c, void* stream) {
+  UB_REQUIRE(x && y && gamma && beta && rows > 0 && c > 0 && c <= 1024);
+  UB_REQUIRE(!pos || pos_rows > 0);
+  unsigned grid = (unsigned)((rows + 7) / 8);
+  layer_norm_kernel<__nv_bfloat16><<<grid, 256, 0, ub::as_stream(stream)>>>(
+      x, reinterpret_cast<__nv_bfloat16*>(y), gamma, beta, pos, pos_scale, pos_rows, rows, c);
   UB_CHECK_LAUNCH();
   return 0;
 }

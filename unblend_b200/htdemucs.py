@@ -396,10 +396,12 @@ class HTDemucsCuda(ConvNet):
                    y_bf16=out.dtype == torch.bfloat16)
 
     def _ln(self, x: torch.Tensor, rows: int, c: int, name: str, pos: torch.Tensor | None = None,
-            pos_rows: int = 1) -> torch.Tensor:
-        y = torch.empty_like(x)
-        _lib.call("unblend_layer_norm", x.data_ptr(), y.data_ptr(), self.w(f"{name}.weight").data_ptr(),
-                  self.w(f"{name}.bias").data_ptr(), _lib.ptr(pos), 1.0, pos_rows, rows, c)
+            pos_rows: int = 1, bf16: bool = False) -> torch.Tensor:
+        """LayerNorm of ``rows`` rows; ``bf16``: written as bf16 for rows that only feed bf16 GEMMs."""
+        y = torch.empty_like(x, dtype=torch.bfloat16 if bf16 else torch.float32)
+        _lib.call("unblend_layer_norm_bf16" if bf16 else "unblend_layer_norm", x.data_ptr(), y.data_ptr(),
+                  self.w(f"{name}.weight").data_ptr(), self.w(f"{name}.bias").data_ptr(), _lib.ptr(pos), 1.0,
+                  pos_rows, rows, c)
         return y
 
     def _attn_bf16(self, hd: int, D: int) -> bool:
@@ -408,7 +410,7 @@ class HTDemucsCuda(ConvNet):
 
     def _attention(self, qbuf: torch.Tensor, q_off: int, kvbuf: torch.Tensor, k_off: int, v_off: int, o: int,
                    B: int, heads: int, L: int, Lk: int, hd: int, q_sb: int, q_sr: int, kv_sb: int, kv_sr: int,
-                   o_sb: int, o_sr: int) -> None:
+                   o_sb: int, o_sr: int, o_bf16: bool = False) -> None:
         """softmax(Q K^T / sqrt(hd)) V for all heads: tensor-core flash attention, or SIMT.
 
         Q sits at element ``q_off`` of ``qbuf``, K and V at ``k_off`` / ``v_off`` of
@@ -434,7 +436,7 @@ class HTDemucsCuda(ConvNet):
             a.outer, a.inner, a.heads, a.lq, a.lk, a.hd = B, 1, heads, L, Lk, hd
             a.q_so, a.q_si, a.q_sr = q_sb, 8, q_sr
             a.kv_so, a.kv_si, a.kv_sr = kv_sb, 8, kv_sr
-            a.out, a.o_so, a.o_si, a.o_sr, a.out_bf16 = o, o_sb, 0, o_sr, 0
+            a.out, a.o_so, a.o_si, a.o_sr, a.out_bf16 = o, o_sb, 0, o_sr, 1 if o_bf16 else 0
             a.scale = scale
             _lib.call("unblend_attention_bf16", qb.data_ptr() + 2 * q_off, kvb.data_ptr() + 2 * k_off,
                       kvb.data_ptr() + 2 * v_off, ctypes_byref(a), work=work)
@@ -458,31 +460,34 @@ class HTDemucsCuda(ConvNet):
         hd = D // heads
         dev = x.device
         attn = "cross_attn" if cross else "self_attn"
-        h = self._ln(x, B * L, D, f"{q}.norm1")
-        att = torch.empty(B * L * D, device=dev, dtype=torch.float32)
-        # bf16 precision with 64-dim heads: the projections leave the tensor cores as bf16
-        # for the bf16 attention kernel (no separate rounding pass).
+        # bf16 precision: the activations that only feed bf16 GEMMs (LayerNorm outputs, the
+        # attention output, the FeedForward hidden layer) are written as bf16 by their
+        # producers and loaded as they are; with 48/64-dim heads the projections leave the
+        # tensor cores as bf16 for the bf16 attention kernel (no separate rounding pass).
+        bf = self.precision == "bf16"
+        h = self._ln(x, B * L, D, f"{q}.norm1", bf16=bf)
         pdt = torch.bfloat16 if self._attn_bf16(hd, D) else torch.float32
+        att = torch.empty(B * L * D, device=dev, dtype=pdt)
         if not cross:
             win, bin_ = self.w(f"{q}.{attn}.in_proj_weight"), self.w(f"{q}.{attn}.in_proj_bias")
             qkv = torch.empty(B * L * 3 * D, device=dev, dtype=pdt)
             self._linear(h, B, L, D, win, bin_, qkv, 3 * D)
             self._attention(qkv, 0, qkv, D, 2 * D, att.data_ptr(), B, heads, L, L, hd, L * 3 * D,
-                            3 * D, L * 3 * D, 3 * D, L * D, D)
+                            3 * D, L * 3 * D, 3 * D, L * D, D, o_bf16=att.dtype == torch.bfloat16)
         else:
-            kvn = self._ln(kv_src, B * Lk, D, f"{q}.norm2")
+            kvn = self._ln(kv_src, B * Lk, D, f"{q}.norm2", bf16=bf)
             qp = torch.empty(B * L * D, device=dev, dtype=pdt)
             self._linear(h, B, L, D, self.w(f"{q}.in_q.w"), self.w(f"{q}.in_q.b"), qp, D)
             kv = torch.empty(B * Lk * 2 * D, device=dev, dtype=pdt)
             self._linear(kvn, B, Lk, D, self.w(f"{q}.in_kv.w"), self.w(f"{q}.in_kv.b"), kv, 2 * D)
             self._attention(qp, 0, kv, 0, D, att.data_ptr(), B, heads, L, Lk, hd, L * D, D,
-                            Lk * 2 * D, 2 * D, L * D, D)
+                            Lk * 2 * D, 2 * D, L * D, D, o_bf16=att.dtype == torch.bfloat16)
         x_new = torch.empty_like(x)
         self._linear(att, B, L, D, self.w(f"{q}.{attn}.out_proj.weight"), self.w(f"{q}.{attn}.out_proj.bias"),
                      x_new, D, res=x, res_scale=self.w(f"{q}.gamma_1.scale"))
-        h2 = self._ln(x_new, B * L, D, f"{q}.norm3" if cross else f"{q}.norm2")
+        h2 = self._ln(x_new, B * L, D, f"{q}.norm3" if cross else f"{q}.norm2", bf16=bf)
         hidden = self.w(f"{q}.linear1.bias").shape[0]
-        f = torch.empty(B * L * hidden, device=dev, dtype=torch.float32)
+        f = torch.empty(B * L * hidden, device=dev, dtype=torch.bfloat16 if bf and hidden % 32 == 0 else torch.float32)
         self._linear(h2, B, L, D, self.w(f"{q}.linear1.weight"), self.w(f"{q}.linear1.bias"), f, hidden,
                      act=ACT_GELU)
         st = self._arena.take(2 * B, dev)
