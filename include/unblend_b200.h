@@ -546,6 +546,16 @@ int unblend_lstm_recurrence(const float* xp, const float* whh_t, float* h_out, i
                             int inner, long long outer_stride, long long inner_stride, long long step_stride,
                             void* stream);
 
+/* The same recurrence for the bf16 precision setting on the tensor cores: W_hh and h
+ * rounded to bf16 for the W_hh h product (fp32 accumulation, cell state and input
+ * projections); xp 16-byte aligned; hid 128 or 256 (other sizes: unblend_lstm_recurrence). */
+int unblend_lstm_recurrence_bf16(const float* xp, const float* whh_t, float* h_out, int n_seq, int steps, int hid,
+                                 int inner, long long outer_stride, long long inner_stride, long long step_stride,
+                                 void* stream);
+
+/* Device flag set when a bounded wait of unblend_lstm_recurrence_bf16 gives up (0 = none). Synchronous. */
+int unblend_lstm_error_flag(int* out_host, int clear);
+
 #ifdef __cplusplus
 }
 #endif

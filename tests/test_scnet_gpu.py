@@ -125,6 +125,57 @@ def test_lstm_recurrence_both_directions(hid, d, steps, n_seq, freq_axis):
     assert rel_err(got, ref) < 2e-5
 
 
+def _lstm_bf16_emulated(xp_seq: torch.Tensor, whh: torch.Tensor, hid: int) -> torch.Tensor:
+    """The recurrence with W_hh and h rounded to bf16 for W_hh h (float64 otherwise):
+    xp_seq [steps, n_seq, 8 hid] (both directions), whh [2][hid][4 hid] -> [steps, n_seq, 2 hid]."""
+    steps, n_seq = xp_seq.shape[:2]
+    out = torch.zeros(steps, n_seq, 2 * hid, dtype=torch.float64)
+    for d in range(2):
+        w = whh[d].to(torch.bfloat16).double()  # [hid, 4 hid] = W_hh^T
+        h = torch.zeros(n_seq, hid, dtype=torch.float64)
+        c = torch.zeros(n_seq, hid, dtype=torch.float64)
+        order = range(steps) if d == 0 else range(steps - 1, -1, -1)
+        for t in order:
+            g = xp_seq[t, :, 4 * hid * d:4 * hid * (d + 1)].double() + h.to(torch.bfloat16).double() @ w
+            i, f, gg, o = g.split(hid, dim=1)
+            c = torch.sigmoid(f) * c + torch.sigmoid(i) * torch.tanh(gg)
+            h = torch.sigmoid(o) * torch.tanh(c)
+            out[t, :, hid * d:hid * (d + 1)] = h
+    return out
+
+
+@pytest.mark.parametrize("hid,steps,n_seq,freq_axis", [(128, 13, 100, True), (256, 21, 70, False),
+                                                       (256, 7, 130, True), (128, 40, 9, False)])
+def test_lstm_recurrence_bf16_tensor_cores(hid, steps, n_seq, freq_axis):
+    """The bf16 recurrence against the same arithmetic emulated in float64 (W_hh and h
+    rounded to bf16 for the product), and against the fp32 LSTM within bf16 accuracy."""
+    torch.manual_seed(hid + steps)
+    d = 64
+    lstm = torch.nn.LSTM(d, hid, bidirectional=True)
+    sd = {f"l.{k}": v.detach() for k, v in lstm.state_dict().items()}
+    x = torch.randn(steps, n_seq, d)
+    ref32 = lstm_bidirectional(sd, "l", x)
+    xp = torch.cat([x @ sd["l.weight_ih_l0"].t() + sd["l.bias_ih_l0"] + sd["l.bias_hh_l0"],
+                    x @ sd["l.weight_ih_l0_reverse"].t() + sd["l.bias_ih_l0_reverse"] + sd["l.bias_hh_l0_reverse"]],
+                   dim=2)
+    whh = torch.stack([sd["l.weight_hh_l0"].t(), sd["l.weight_hh_l0_reverse"].t()]).contiguous()
+    emu = _lstm_bf16_emulated(xp, whh, hid)
+    if freq_axis:
+        xp_d, T, Fq = xp.contiguous(), n_seq, steps
+        args = (n_seq, steps, hid, T, Fq * T, 1, T)
+    else:
+        xp_d, Fq, T = xp.permute(1, 0, 2).contiguous(), n_seq, steps
+        args = (n_seq, steps, hid, Fq, Fq * T, T, 1)
+    xp_d = xp_d.cuda()
+    h = torch.full((xp_d.shape[0], xp_d.shape[1], 2 * hid), float("nan"), device="cuda")
+    _lib.call("unblend_lstm_recurrence_bf16", xp_d.data_ptr(), whh.cuda().data_ptr(), h.data_ptr(), *args)
+    got = h.cpu() if freq_axis else h.cpu().permute(1, 0, 2)
+    assert torch.isfinite(got).all()
+    assert rel_err(got, emu) < 5e-3
+    assert rel_err(got, ref32) < 5e-2
+    assert _lib.error_flag() == 0
+
+
 # ---------------------------------------------------------------- model
 
 def _model(g, precision="fp32") -> SCNetCuda:

@@ -147,6 +147,9 @@ _SIGNATURES = {
     "unblend_rfft_time": [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p],
     "unblend_irfft_time": [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p],
     "unblend_lstm_recurrence": [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_ll, c_ll, c_ll, c_void_p],
+    "unblend_lstm_recurrence_bf16": [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_ll, c_ll, c_ll,
+                                     c_void_p],
+    "unblend_lstm_error_flag": [c_void_p, c_int],
     "unblend_istft_masked": [c_void_p, c_void_p, c_ll, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
                              c_int, c_int, c_int, c_int, c_void_p],
 }
@@ -210,7 +213,7 @@ def error_flag(clear: bool = True) -> int:
     """Read (and by default clear) the device flag that bounded waits set on timeout."""
     total = 0
     for name in ("unblend_error_flag", "unblend_attention_error_flag", "unblend_gemm_error_flag",
-                 "unblend_attention_bf16_error_flag", "unblend_dconv_error_flag"):
+                 "unblend_attention_bf16_error_flag", "unblend_dconv_error_flag", "unblend_lstm_error_flag"):
         v = c_int(0)
         check(name, getattr(load(), name)(ctypes.byref(v), 1 if clear else 0))
         total |= v.value

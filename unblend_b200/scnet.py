@@ -271,7 +271,10 @@ class SCNetCuda(ConvNet):
         else:           # sequences (b, f), steps t
             args = (B * F, T, hid, F, F * T, T, 1)
         n_seq, steps = args[0], args[1]
-        _lib.call("unblend_lstm_recurrence", xp.t.data_ptr(), self.w(f"{q}.hh{j}").data_ptr(), h.t.data_ptr(), *args,
+        # bf16 precision: W_hh h on the tensor cores with bf16 operands (hidden 128 / 256).
+        rec = "unblend_lstm_recurrence_bf16" if self.precision == "bf16" and hid in (128, 256) else \
+            "unblend_lstm_recurrence"
+        _lib.call(rec, xp.t.data_ptr(), self.w(f"{q}.hh{j}").data_ptr(), h.t.data_ptr(), *args,
                   work=2.0 * 2 * n_seq * steps * 4 * hid * hid)
         self._conv(h, self.w(f"{q}.lin{j}.w"), self.w(f"{q}.lin{j}.b"), x, h_out=F, w_out=T, n_out=d, res=x.t)
 
