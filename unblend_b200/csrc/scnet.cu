@@ -11,7 +11,8 @@
 //                   GroupNorm(1) sums of each (batch, frequency) row
 //   act_copy        strided copy with GELU / tanh / Swish (band outputs into the full
 //                   band, transposed-conv trims, the mask head's tanh)
-//   rfft_time / irfft_time   FeatureConversion: orthonormal real DFT along frames
+//   rfft_time / irfft_time   FeatureConversion: orthonormal real DFT along frames (mixed-radix
+//                            FFTs when the frame count factors into radices up to 17, else direct sums)
 //   lstm_recurrence the bidirectional LSTM recurrence of DualPathRNN (input
 //                   projections precomputed by a GEMM): a thread-block cluster per 64
 //                   sequences and direction with W_hh resident in shared memory for
@@ -319,6 +320,181 @@ __global__ void __launch_bounds__(256) lstm_recurrence_kernel(const float* __res
   }
 }
 
+// ---------------------------------------------------------------------------
+// Real DFTs along frames as mixed-radix FFTs (radices 2, 3, 4, 5, 7, 11, 13, 17; 476
+// frames = 4 x 7 x 17). A block takes FFT_PAIRS channel pairs of one row; channels
+// (2p, 2p + 1) travel as the real and imaginary parts of one complex sequence, so one
+// complex FFT serves two real transforms. Each stage is one pass of the Stockham
+// autosort formulation (Govindaraju et al., "High performance discrete Fourier
+// transforms on graphics processors", SC 2008): butterfly j of a radix-R stage with Ns
+// already combined points reads in[j + r T / R] (r < R), rotates element r by the
+// twiddle of (j mod Ns) r / (Ns R) turns, takes an R-point DFT and writes
+// out[(j / Ns) Ns R + (j mod Ns) + r Ns]; the output is in natural order. Twiddles come
+// from a table of cos / sin (2 pi i / T) evaluated in double precision.
+constexpr int FFT_PAIRS = 8;     // channel pairs per block (16 channels)
+constexpr int FFT_THREADS = 256; // FFT_PAIRS pairs x 32 butterfly workers
+constexpr int FFT_MAXR = 8;      // radices per factorisation
+
+struct FftPlan {
+  int n;
+  int radix[FFT_MAXR];
+};
+
+// e^{sign 2 pi i idx / T} from the table (tab[i] = (cos, sin) of 2 pi i / T).
+__device__ __forceinline__ float2 tw(const float2* tab, int idx, float sign) {
+  const float2 w = tab[idx];
+  return make_float2(w.x, sign * w.y);
+}
+
+__device__ __forceinline__ float2 cmul(float2 a, float2 b) {
+  return make_float2(a.x * b.x - a.y * b.y, a.x * b.y + a.y * b.x);
+}
+
+template <int R>
+__device__ __forceinline__ void fft_stage(const float2* __restrict__ in, float2* __restrict__ out, int T, int ns,
+                                          const float2* __restrict__ tab, float sign, int pair, int worker) {
+  const int m = T / R, step_r = T / R;  // butterflies per pair; table stride of 1 / R turn
+  for (int j = worker; j < m; j += FFT_THREADS / FFT_PAIRS) {
+    const int k = j % ns;
+    float2 v[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) v[r] = in[(j + r * m) * FFT_PAIRS + pair];
+    if (ns > 1) {
+      const int unit = T / (ns * R);  // table stride of 1 / (ns R) turn
+#pragma unroll
+      for (int r = 1; r < R; ++r) v[r] = cmul(v[r], tw(tab, k * r * unit, sign));
+    }
+    float2 o[R];
+#pragma unroll
+    for (int q = 0; q < R; ++q) {
+      float2 acc = v[0];
+#pragma unroll
+      for (int r = 1; r < R; ++r) {
+        const float2 w = tw(tab, ((r * q) % R) * step_r, sign);
+        acc.x = fmaf(v[r].x, w.x, fmaf(-v[r].y, w.y, acc.x));
+        acc.y = fmaf(v[r].x, w.y, fmaf(v[r].y, w.x, acc.y));
+      }
+      o[q] = acc;
+    }
+    const int base = (j / ns) * ns * R + k;
+#pragma unroll
+    for (int q = 0; q < R; ++q) out[(base + q * ns) * FFT_PAIRS + pair] = o[q];
+  }
+}
+
+// In-place over the two buffers: the result ends in buf[0] or buf[1] (returned).
+__device__ float2* fft_run(float2* a, float2* b, const FftPlan& plan, const float2* tab, float sign, int pair,
+                           int worker) {
+  int ns = 1;
+  for (int s = 0; s < FFT_MAXR && plan.radix[s] > 1; ++s) {
+    const int R = plan.radix[s];
+    switch (R) {
+      case 2: fft_stage<2>(a, b, plan.n, ns, tab, sign, pair, worker); break;
+      case 3: fft_stage<3>(a, b, plan.n, ns, tab, sign, pair, worker); break;
+      case 4: fft_stage<4>(a, b, plan.n, ns, tab, sign, pair, worker); break;
+      case 5: fft_stage<5>(a, b, plan.n, ns, tab, sign, pair, worker); break;
+      case 7: fft_stage<7>(a, b, plan.n, ns, tab, sign, pair, worker); break;
+      case 11: fft_stage<11>(a, b, plan.n, ns, tab, sign, pair, worker); break;
+      case 13: fft_stage<13>(a, b, plan.n, ns, tab, sign, pair, worker); break;
+      default: fft_stage<17>(a, b, plan.n, ns, tab, sign, pair, worker); break;
+    }
+    __syncthreads();
+    ns *= R;
+    float2* t = a;
+    a = b;
+    b = t;
+  }
+  return a;
+}
+
+// Grid (rows, ceil(C / 16)). x [rows, T, C] -> y [rows, K, 2C] (K = T/2 + 1), orthonormal:
+// y[., k, c] = Re X_c[k] / sqrt(T), y[., k, C + c] = Im X_c[k] / sqrt(T), X = sum_t x e^{-2 pi i k t / T}.
+__global__ void __launch_bounds__(FFT_THREADS) rfft_fft_kernel(const float* __restrict__ x, float* __restrict__ y,
+                                                              int C, const FftPlan plan) {
+  extern __shared__ __align__(16) float2 fsm[];
+  const int T = plan.n, K = T / 2 + 1;
+  float2* tab = fsm;
+  float2* a = fsm + T;
+  float2* b = a + T * FFT_PAIRS;
+  const long long row = blockIdx.x;
+  const int pair = threadIdx.x % FFT_PAIRS, worker = threadIdx.x / FFT_PAIRS;
+  const int ch0 = blockIdx.y * 2 * FFT_PAIRS + 2 * pair, ch1 = ch0 + 1;
+  twiddle_table(tab, T);
+  for (int t = worker; t < T; t += FFT_THREADS / FFT_PAIRS) {
+    const float* xr = x + (row * T + t) * C;
+    a[t * FFT_PAIRS + pair] = make_float2(ch0 < C ? __ldg(xr + ch0) : 0.f, ch1 < C ? __ldg(xr + ch1) : 0.f);
+  }
+  __syncthreads();
+  const float2* z = fft_run(a, b, plan, tab, -1.f, pair, worker);
+  const float s = rsqrtf((float)T);
+  for (int k = worker; k < K; k += FFT_THREADS / FFT_PAIRS) {
+    const float2 p = z[k * FFT_PAIRS + pair], q = z[((T - k) % T) * FFT_PAIRS + pair];
+    // Channel ch0 = (Z[k] + conj Z[T-k]) / 2, ch1 = (Z[k] - conj Z[T-k]) / 2i.
+    float* yr = y + (row * K + k) * 2LL * C;
+    if (ch0 < C) {
+      yr[ch0] = 0.5f * (p.x + q.x) * s;
+      yr[C + ch0] = 0.5f * (p.y - q.y) * s;
+    }
+    if (ch1 < C) {
+      yr[ch1] = 0.5f * (p.y + q.y) * s;
+      yr[C + ch1] = -0.5f * (p.x - q.x) * s;
+    }
+  }
+}
+
+// Grid (rows, ceil(C / 16)). y [rows, K, 2C] -> x [rows, T, C], T = 2 (K - 1): the inverse of the
+// Hermitian spectrum (imaginary parts of bins 0 and K - 1 dropped), orthonormal.
+__global__ void __launch_bounds__(FFT_THREADS) irfft_fft_kernel(const float* __restrict__ y, float* __restrict__ x,
+                                                               int C, const FftPlan plan) {
+  extern __shared__ __align__(16) float2 fsm[];
+  const int T = plan.n, K = T / 2 + 1;
+  float2* tab = fsm;
+  float2* a = fsm + T;
+  float2* b = a + T * FFT_PAIRS;
+  const long long row = blockIdx.x;
+  const int pair = threadIdx.x % FFT_PAIRS, worker = threadIdx.x / FFT_PAIRS;
+  const int ch0 = blockIdx.y * 2 * FFT_PAIRS + 2 * pair, ch1 = ch0 + 1;
+  twiddle_table(tab, T);
+  for (int k = worker; k < T; k += FFT_THREADS / FFT_PAIRS) {
+    const int kk = k < K ? k : T - k;  // bins past K - 1 are conjugates of T - k
+    const float* yr = y + (row * K + kk) * 2LL * C;
+    const bool keep_im = kk != 0 && kk != K - 1;
+    float2 sa = make_float2(ch0 < C ? __ldg(yr + ch0) : 0.f, ch0 < C && keep_im ? __ldg(yr + C + ch0) : 0.f);
+    float2 sb = make_float2(ch1 < C ? __ldg(yr + ch1) : 0.f, ch1 < C && keep_im ? __ldg(yr + C + ch1) : 0.f);
+    if (k >= K) {
+      sa.y = -sa.y;
+      sb.y = -sb.y;
+    }
+    a[k * FFT_PAIRS + pair] = make_float2(sa.x - sb.y, sa.y + sb.x);  // S_a + i S_b
+  }
+  __syncthreads();
+  const float2* z = fft_run(a, b, plan, tab, 1.f, pair, worker);
+  const float s = rsqrtf((float)T);
+  for (int t = worker; t < T; t += FFT_THREADS / FFT_PAIRS) {
+    const float2 v = z[t * FFT_PAIRS + pair];
+    float* xr = x + (row * T + t) * C;
+    if (ch0 < C) xr[ch0] = v.x * s;
+    if (ch1 < C) xr[ch1] = v.y * s;
+  }
+}
+
+// Radices for an FFT of n points (fours first), or false when a prime factor exceeds 17
+// or more than FFT_MAXR stages would be needed.
+bool fft_plan(int n, FftPlan* p) {
+  p->n = n;
+  for (int i = 0; i < FFT_MAXR; ++i) p->radix[i] = 1;
+  int s = 0;
+  const int primes[] = {4, 2, 3, 5, 7, 11, 13, 17};
+  for (int r : primes) {
+    while (n % r == 0) {
+      if (s == FFT_MAXR) return false;
+      p->radix[s++] = r;
+      n /= r;
+    }
+  }
+  return n == 1;
+}
+
 // Cluster form for hid = 32 * Q <= 256: a cluster of Q CTAs runs one direction of
 // G = 8 * SG sequences. CTA r of the cluster owns hidden units [32 r, 32 r + 32): their
 // four gate columns of W_hh^T stay in shared memory for the whole launch (as float4
@@ -562,6 +738,17 @@ extern "C" int unblend_act_copy(const float* x, long long x_stride, float* y, lo
 
 extern "C" int unblend_rfft_time(const float* x, float* y, int rows, int t_len, int c, void* stream) {
   UB_REQUIRE(x && y && x != y && rows > 0 && t_len >= 2 && t_len % 2 == 0 && c > 0 && rows < (1 << 30));
+  FftPlan plan;
+  if (fft_plan(t_len, &plan)) {
+    const size_t smem = sizeof(float2) * (size_t)t_len * (1 + 2 * FFT_PAIRS);
+    UB_REQUIRE(smem <= 200 * 1024);
+    cudaFuncSetAttribute(rfft_fft_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    rfft_fft_kernel<<<dim3(rows, (c + 2 * FFT_PAIRS - 1) / (2 * FFT_PAIRS)), FFT_THREADS, smem,
+                      ub::as_stream(stream)>>>(x, y, c, plan);
+    UB_CHECK_LAUNCH();
+    return 0;
+  }
+  // Frame counts with a prime factor above 17: the direct sums.
   const size_t smem = sizeof(float) * (2 * (size_t)t_len + 32 * (size_t)t_len);
   UB_REQUIRE(smem <= 220 * 1024);
   cudaFuncSetAttribute(rfft_time_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -573,6 +760,16 @@ extern "C" int unblend_rfft_time(const float* x, float* y, int rows, int t_len, 
 extern "C" int unblend_irfft_time(const float* y, float* x, int rows, int n_bins, int c, void* stream) {
   UB_REQUIRE(x && y && x != y && rows > 0 && n_bins >= 2 && c > 0 && rows < (1 << 30));
   const int t_len = 2 * (n_bins - 1);
+  FftPlan plan;
+  if (fft_plan(t_len, &plan)) {
+    const size_t smem_f = sizeof(float2) * (size_t)t_len * (1 + 2 * FFT_PAIRS);
+    UB_REQUIRE(smem_f <= 200 * 1024);
+    cudaFuncSetAttribute(irfft_fft_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_f);
+    irfft_fft_kernel<<<dim3(rows, (c + 2 * FFT_PAIRS - 1) / (2 * FFT_PAIRS)), FFT_THREADS, smem_f,
+                       ub::as_stream(stream)>>>(y, x, c, plan);
+    UB_CHECK_LAUNCH();
+    return 0;
+  }
   const size_t smem = sizeof(float) * (2 * (size_t)t_len + 64 * (size_t)n_bins);
   UB_REQUIRE(smem <= 220 * 1024);
   cudaFuncSetAttribute(irfft_time_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
