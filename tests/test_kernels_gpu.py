@@ -502,3 +502,38 @@ def test_layer_norm_bf16_output():
     ref = torch.nn.functional.layer_norm(x, (c,), g, bt, 1e-5)
     # One bf16 rounding of an fp32-accurate value: within half an ulp of bf16 (2^-9 relative).
     assert ((y.float() - ref).abs() <= ref.abs() * 2.0 ** -8 + 1e-6).all()
+
+
+@pytest.mark.parametrize("C,N,kh,kw,dw,act,res", [(48, 96, 3, 3, 1, ACT_GLU, False), (64, 130, 1, 1, 1, ACT_NONE, True),
+                                                  (32, 64, 1, 3, 2, ACT_GELU, False)])
+def test_conv_simt_wide_tiles_match_the_generic_kernel(C, N, kh, kw, dw, act, res):
+    """Channels a multiple of 16 and >= 64 outputs take the 128 x 128 tile kernel; the same
+    problem with a padded channel stride takes the generic one. Both sum every output over K
+    in the same order (bit-identical), and match torch's fp32 convolution."""
+    B, H, W = 2, 5, 301
+    x = _cl((B, H, W, C))
+    w, b = _cl((N, kh, kw, C)) * 0.1, _cl((N,))
+    xp = torch.zeros(B, H, W, C + 4, device="cuda")
+    xp[..., :C] = x
+    n_final = N // 2 if act == ACT_GLU else N
+    r = _cl((B, H, W, n_final)) if res else None
+    sc = _cl((n_final,)) if res else None
+    outs = []
+    for xin, cs in ((x, C), (xp, C + 4)):
+        y = torch.empty(B, H, W, n_final, device="cuda")
+        st = torch.zeros(2 * B * H, device="cuda", dtype=torch.float64)
+        _conv(xin, w, b, y, B=B, H=H, W=W, C=C, in_s=(H * W * cs, W * cs, cs), Ho=H, Wo=W, N=N,
+              out_s=(H * W * n_final, W * n_final, n_final), kh=kh, kw=kw, dw=dw, ph=kh // 2, pw=dw * (kw // 2),
+              act=act, res=r, res_scale=sc, stats=st, stats_per_h=1)
+        outs.append((y, st))
+    assert torch.equal(outs[0][0], outs[1][0])
+    # Statistics: fp32 partial sums of 8 (wide) or 4 (generic) values per thread, then double.
+    assert torch.allclose(outs[0][1], outs[1][1], rtol=1e-6, atol=1e-4)
+    z = _ref_conv(x, w, b, kh, kw, 1, 1, 1, dw, kh // 2, dw * (kw // 2))
+    if act == ACT_GLU:
+        z = z[..., 0::2] * torch.sigmoid(z[..., 1::2])
+    elif act == ACT_GELU:
+        z = F.gelu(z)
+    if res:
+        z = r + sc * z
+    assert rel_err(outs[0][0], z) < TOL

@@ -188,6 +188,146 @@ __global__ void __launch_bounds__(NT) conv_simt_kernel(ConvArgs a) {
   }
 }
 
+// Wide-tile form for channels-last inputs whose channel count is a multiple of 16 (no
+// prologue): a 128 x 128 output tile per block, 8 x 8 per thread (one float4 pair of A and
+// of B per k feeds 64 FMAs), and since a 16-wide K tile then lies inside one tap, each
+// thread computes its input row's offset once per K tile and loads 2 float4 of channels.
+// The K order of every output's sum is the generic kernel's (bit-identical results).
+constexpr int WBM = 128, WBN = 128, WBK = 16, WNT = 256;
+
+__global__ void __launch_bounds__(WNT, 2) conv_simt_wide_kernel(ConvArgs a) {
+  const UnblendConvParams& p = a.p;
+  __shared__ __align__(16) float As[2][WBK][WBM + 4];
+  __shared__ __align__(16) float Bs[2][WBK][WBN + 4];
+  const int tid = threadIdx.x;
+  const long long m0 = (long long)blockIdx.x * WBM;
+  const int n0 = blockIdx.y * WBN;
+  // Load role: row / channel tid >> 1, K half (tid & 1) * 8.
+  const int lr = tid >> 1, lk = (tid & 1) * 8;
+  const long long m = m0 + lr;
+  const bool mvalid = m < a.M;
+  int wo = 0, ho = 0, b = 0;
+  if (mvalid) {
+    wo = (int)(m % p.w_out);
+    const long long t = m / p.w_out;
+    ho = (int)(t % p.h_out);
+    b = (int)(t / p.h_out);
+  }
+  const int hbase = ho * p.sh - p.ph, wbase = wo * p.sw - p.pw;
+  const float* xb = a.x + (long long)b * p.in_sb;
+  const int nrow = n0 + lr;
+  const float* wrow = a.w + (long long)nrow * a.K + lk;
+  float4 ra0, ra1, rb0, rb1;
+  auto load_tiles = [&](int k0) {
+    const int tap = k0 / p.c_in, ci = k0 - tap * p.c_in + lk;
+    const int kh = tap / p.kw, kw = tap - kh * p.kw;
+    const int hi = hbase + kh * p.dh, wi = wbase + kw * p.dw;
+    ra0 = ra1 = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (mvalid && hi >= 0 && hi < p.h_in && wi >= 0 && wi < p.w_in) {
+      const float4* src = reinterpret_cast<const float4*>(xb + (long long)hi * p.in_sh + (long long)wi * p.in_sw + ci);
+      ra0 = __ldg(src);
+      ra1 = __ldg(src + 1);
+    }
+    rb0 = rb1 = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (nrow < p.n_out) {
+      const float4* src = reinterpret_cast<const float4*>(wrow + k0);
+      rb0 = __ldg(src);
+      rb1 = __ldg(src + 1);
+    }
+  };
+  auto store_tiles = [&](int buf) {
+    const float av[8] = {ra0.x, ra0.y, ra0.z, ra0.w, ra1.x, ra1.y, ra1.z, ra1.w};
+    const float bv[8] = {rb0.x, rb0.y, rb0.z, rb0.w, rb1.x, rb1.y, rb1.z, rb1.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      As[buf][lk + i][lr] = av[i];
+      Bs[buf][lk + i][lr] = bv[i];
+    }
+  };
+  const int tx = tid & 15;  // N: 8 columns each
+  const int ty = tid >> 4;  // M: 8 rows each
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+  const int ktiles = a.K / WBK;
+  load_tiles(0);
+  store_tiles(0);
+  __syncthreads();
+  for (int kt = 0; kt < ktiles; ++kt) {
+    const int buf = kt & 1;
+    if (kt + 1 < ktiles) load_tiles((kt + 1) * WBK);
+#pragma unroll
+    for (int kk = 0; kk < WBK; ++kk) {
+      const float4 a0 = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 8]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 8 + 4]);
+      const float4 b0 = *reinterpret_cast<const float4*>(&Bs[buf][kk][tx * 8]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&Bs[buf][kk][tx * 8 + 4]);
+      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    if (kt + 1 < ktiles) store_tiles(buf ^ 1);
+    __syncthreads();
+  }
+  // Epilogue: as the generic kernel, eight columns per thread.
+  const bool glu = p.act == UNBLEND_ACT_GLU;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const long long mm = m0 + ty * 8 + i;
+    const bool rv = mm < a.M;
+    int owo = 0, oho = 0, ob = 0;
+    if (rv) {
+      owo = (int)(mm % p.w_out);
+      const long long t = mm / p.w_out;
+      oho = (int)(t % p.h_out);
+      ob = (int)(t / p.h_out);
+    }
+    const long long rowoff = (long long)ob * p.out_sb + (long long)oho * p.out_sh + (long long)owo * p.out_sw;
+    float s1 = 0.f, s2 = 0.f;
+    float vals[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int n = n0 + tx * 8 + j;
+      float v = acc[i][j];
+      if (n < p.n_out && a.bias) v += __ldg(a.bias + n);
+      if (p.act == UNBLEND_ACT_GELU) v = ub::gelu_erf(v);
+      vals[j] = v;
+    }
+    const int nouts = glu ? 4 : 8;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (j >= nouts) break;
+      const int n = glu ? (n0 + tx * 8) / 2 + j : n0 + tx * 8 + j;
+      const int ncount = glu ? p.n_out / 2 : p.n_out;
+      float v = glu ? vals[2 * j] * ub::sigmoidf_(vals[2 * j + 1]) : vals[j];
+      if (rv && n < ncount) {
+        const long long off = rowoff + (long long)(n / p.n_group) * p.out_sg + (n % p.n_group);
+        if (p.res) v = p.res[off] + (p.res_scale ? __ldg(p.res_scale + n) : 1.f) * v;
+        a.y[off] = v;
+        s1 += v;
+        s2 += v * v;
+      }
+    }
+    if (p.stats) {
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) {
+        s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+        s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+      }
+      if (tx == 0 && rv) {
+        const int g = p.stats_per_h ? ob * p.h_out + oho : ob;
+        atomicAdd(p.stats + 2 * g, (double)s1);
+        atomicAdd(p.stats + 2 * g + 1, (double)s2);
+      }
+    }
+  }
+}
+
 // First-layer convolutions (c_in <= 4 input channels, up to 8 taps along one
 // axis, n_out a multiple of 16 up to 64, bias + optional GELU, nothing else):
 // K = taps * c_in <= 32 is too short for the tiled kernel above, whose tile
@@ -308,6 +448,16 @@ extern "C" int unblend_conv2d_f32(const float* x, const float* w, const float* b
     if (p->c_in == 4) conv_thin_kernel<4, 8><<<(unsigned)blocks, TH_NT, 0, ub::as_stream(stream)>>>(a);
     else if (p->c_in == 2) conv_thin_kernel<2, 8><<<(unsigned)blocks, TH_NT, 0, ub::as_stream(stream)>>>(a);
     else conv_thin_kernel<1, 8><<<(unsigned)blocks, TH_NT, 0, ub::as_stream(stream)>>>(a);
+    UB_CHECK_LAUNCH();
+    return 0;
+  }
+  const bool wide = p->prologue == UNBLEND_PRO_NONE && p->c_in % WBK == 0 && p->in_sw == p->c_in &&
+                    p->in_sh % 4 == 0 && p->in_sb % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+                    (reinterpret_cast<uintptr_t>(w) & 15) == 0 && p->n_out >= 64;
+  if (wide) {
+    dim3 gw((unsigned)((a.M + WBM - 1) / WBM), (unsigned)((p->n_out + WBN - 1) / WBN));
+    UB_REQUIRE(gw.y < 65536 && gw.x < (1u << 31));
+    conv_simt_wide_kernel<<<gw, WNT, 0, ub::as_stream(stream)>>>(a);
     UB_CHECK_LAUNCH();
     return 0;
   }
