@@ -99,8 +99,10 @@ int unblend_conv2d_f32(const float* x, const float* w, const float* bias, float*
  * (fp32, [n_out, K]); mode 1: bf16 operands, w_hi is bf16 [n_out, K], w_lo
  * unused; mode 2: fp32 accuracy by the 3-pass bf16 split, w_hi = bf16(w) and
  * w_lo = bf16(w - w_hi) (bf16, [n_out, K]); mode 3: as mode 1 with bf16 x
- * (p->x_bf16 = 1; x is fp32 in the other modes). block_n: 64, 96, 128, 192 or 256
- * output channels per tile. Requirements:
+ * (p->x_bf16 = 1; x is fp32 in the other modes); mode 4: as mode 2, with the
+ * taps of each kernel row (up to three, shifts within 8 positions) sharing one
+ * input load and split, block_n <= 128 (K summed in another order than mode 2).
+ * block_n: 64, 96, 128, 192 or 256 output channels per tile. Requirements:
  * no prologue, c_in % 8 == 0 and >= 16, unit stride along w (or the stride-4
  * kernel-8 pad-2 time convolution, whose input rows up to a multiple of 4
  * past w_in must be zero), n_group and all output strides multiples of 4.

@@ -62,14 +62,22 @@ def test_attention_tc_interleaved_qkv_rows():
     """Self-attention reads Q, K and V out of one [L, 3D] projection."""
     B, L, heads, hd = 2, 200, 8, 64
     D = heads * hd
-    qkv = torch.randn(B, L, 3 * D, device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(11)
+    qkv = torch.randn(B, L, 3 * D, device="cuda", generator=g)
     o = torch.empty(B, L, D, device="cuda")
     base = qkv.data_ptr()
     _lib.call("unblend_attention_tc", base, base + 4 * D, base + 8 * D, o.data_ptr(), B, heads, L, L, hd,
               L * 3 * D, 3 * D, L * 3 * D, 3 * D, L * D, D, 1.0 / math.sqrt(hd), 0)
-    ref = _ref(qkv[..., :D].contiguous(), qkv[..., D:2 * D].contiguous(), qkv[..., 2 * D:].contiguous(), heads, hd)
-    assert rel_err(o, ref) < TOL[0]
+    q, k, v = (qkv[..., i * D:(i + 1) * D].contiguous() for i in range(3))
+    ref = _ref(q, k, v, heads, hd)
+    # The fp32 SIMT kernel on the same rows sets the accuracy floor (as in the test above).
+    o32 = torch.empty_like(o)
+    _lib.call("unblend_attention_f32", q.data_ptr(), k.data_ptr(), v.data_ptr(), o32.data_ptr(), B, heads, L, L, hd,
+              L * D, D, L * D, D, L * D, D, 1.0 / math.sqrt(hd))
+    floor = 4 * rel_err(o32, ref)
+    assert rel_err(o, ref) < max(TOL[0], floor)
     o2 = torch.empty_like(o)
     _lib.call("unblend_attention_tc", base, base + 4 * D, base + 8 * D, o2.data_ptr(), B, heads, L, L, hd,
               L * 3 * D, 3 * D, L * 3 * D, 3 * D, L * D, D, 1.0 / math.sqrt(hd), 2)
-    assert rel_err(o2, ref) < TOL[2]
+    assert rel_err(o2, ref) < max(TOL[2], floor)
+    assert _lib.error_flag() == 0

@@ -288,7 +288,7 @@ def _conv_tc(x, w, b, y, mode, block_n, **kw):
     wf = w.reshape(w.shape[0], -1).contiguous()
     if mode == _lib.TC_TF32X3:
         whi, wlo = _split_tf32(wf)
-    elif mode == _lib.TC_BF16X3:
+    elif mode in (_lib.TC_BF16X3, _lib.TC_BF16X3_TAPS):
         from unblend_b200.convnet import split_bf16
 
         whi, wlo = split_bf16(wf)
@@ -379,7 +379,51 @@ def test_tc_3x3_glu_and_dilated(mode, block_n):
     assert torch.allclose(st[0::2], o2.sum(1), rtol=1e-6, atol=1e-4)
 
 
-@pytest.mark.parametrize("mode", MODES, ids=["tf32x3", "bf16", "bf16x3"])
+@pytest.mark.parametrize("block_n", [64, 96, 128])
+def test_tc_3pass_shared_tap_loads(block_n):
+    """Mode 4: the three taps of each 3-wide kernel row share one input load and hi / lo split; the
+    fp32 bound holds on 3x3 GLU, dilated k=3 (shifts 2 and 4) and the time branch's 1x3 rewrite, and the
+    result stays within fp32 summation-order noise of mode 2."""
+    B, H, W, C, N = 1, 8, 336, 96, 192
+    x, w, b = _cl((B, H, W, C)), _cl((N, 3, 3, C)) * 0.03, _cl((N,))
+    kw = dict(B=B, H=H, W=W, C=C, in_s=(H * W * C, W * C, C), Ho=H, Wo=W, N=N,
+              out_s=(H * W * N // 2, W * N // 2, N // 2), kh=3, kw=3, ph=1, pw=1, act=ACT_GLU)
+    y = torch.empty(B, H, W, N // 2, device="cuda")
+    _conv_tc(x, w, b, y, _lib.TC_BF16X3_TAPS, block_n, **kw)
+    z = _ref_conv(x, w, b, 3, 3, 1, 1, 1, 1, 1, 1)
+    assert rel_err(y, z[..., 0::2] * torch.sigmoid(z[..., 1::2])) < TC_TOL[_lib.TC_BF16X3]
+    y2 = torch.empty_like(y)
+    _conv_tc(x, w, b, y2, _lib.TC_BF16X3, block_n, **kw)
+    assert rel_err(y, y2) < 1e-5
+    for dw in (1, 2, 4):
+        w2, b2 = _cl((64, 1, 3, C)) * 0.05, _cl((64,))
+        y3 = torch.empty(B, H, W, 64, device="cuda")
+        st = torch.zeros(2 * B * H, device="cuda", dtype=torch.float64)
+        _conv_tc(x, w2, b2, y3, _lib.TC_BF16X3_TAPS, min(block_n, 64), B=B, H=H, W=W, C=C,
+                 in_s=(H * W * C, W * C, C), Ho=H, Wo=W, N=64, out_s=(H * W * 64, W * 64, 64), kw=3, dw=dw,
+                 pw=dw, stats=st, stats_per_h=1)
+        assert rel_err(y3, _ref_conv(x, w2, b2, 1, 3, 1, 1, 1, dw, 0, dw)) < TC_TOL[_lib.TC_BF16X3], dw
+        o3 = y3.double().reshape(B * H, -1)
+        assert torch.allclose(st[0::2], o3.sum(1), rtol=1e-6, atol=1e-4)
+    # time branch: 1 x 3 over 2 x 1000 positions (tiles past the end of the rows are masked)
+    L, Ct = 1000, 48
+    xt, wt, bt = _cl((2, 1, L, Ct)), _cl((96, 1, 3, Ct)) * 0.05, _cl((96,))
+    yt = torch.empty(2, 1, L, 48, device="cuda")
+    _conv_tc(xt, wt, bt, yt, _lib.TC_BF16X3_TAPS, block_n, B=2, H=1, W=L, C=Ct, in_s=(L * Ct, L * Ct, Ct), Ho=1,
+             Wo=L, N=96, out_s=(L * 48, L * 48, 48), kw=3, pw=1, act=ACT_GLU)
+    zt = _ref_conv(xt, wt, bt, 1, 3, 1, 1, 1, 1, 0, 1)
+    assert rel_err(yt, zt[..., 0::2] * torch.sigmoid(zt[..., 1::2])) < TC_TOL[_lib.TC_BF16X3]
+
+
+def test_tc_3pass_shared_tap_loads_rejects_wide_tiles():
+    x, w, b = _cl((1, 4, 64, 32)), _cl((64, 3, 3, 32)), _cl((64,))
+    y = torch.empty(1, 4, 64, 64, device="cuda")
+    with pytest.raises(RuntimeError):
+        _conv_tc(x, w, b, y, _lib.TC_BF16X3_TAPS, 192, B=1, H=4, W=64, C=32, in_s=(4 * 64 * 32, 64 * 32, 32), Ho=4,
+                 Wo=64, N=64, out_s=(4 * 64 * 64, 64 * 64, 64), kh=3, kw=3, ph=1, pw=1)
+
+
+@pytest.mark.parametrize("mode", MODES + [_lib.TC_BF16X3_TAPS], ids=["tf32x3", "bf16", "bf16x3", "bf16x3-taps"])
 @pytest.mark.parametrize("B", [8, 32])
 def test_tc_decoder3_rewrite_headline_shape(mode, B):
     """The largest 3x3 rewrite of the headline forward: HTDemucs decoder.3 (512 frequency rows x 336
@@ -397,7 +441,7 @@ def test_tc_decoder3_rewrite_headline_shape(mode, B):
     for i in range(0, B, 4):  # the fp32 reference in slices of 4 segments (bounded memory)
         z = _ref_conv(x[i:i + 4], w, b, 3, 3, 1, 1, 1, 1, 1, 1)
         err = max(err, rel_err(y[i:i + 4], z[..., 0::2] * torch.sigmoid(z[..., 1::2])))
-    assert err < TC_TOL[mode]
+    assert err < TC_TOL[_lib.TC_BF16X3 if mode == _lib.TC_BF16X3_TAPS else mode]
 
 
 @pytest.mark.parametrize("mode", MODES)

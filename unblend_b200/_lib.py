@@ -163,7 +163,9 @@ _HOST_SIGNATURES = {
     "unblend_dconv_error_flag": [ctypes.POINTER(c_int), c_int],
 }
 
-TC_TF32X3, TC_BF16, TC_BF16X3, TC_BF16_ACT = 0, 1, 2, 3
+# Tensor-core convolution modes (unblend_conv2d_tc): 3-pass TF32, bf16, 3-pass bf16,
+# bf16 activations, 3-pass bf16 with the taps of a kernel row sharing one input load.
+TC_TF32X3, TC_BF16, TC_BF16X3, TC_BF16_ACT, TC_BF16X3_TAPS = 0, 1, 2, 3, 4
 
 _lib = None
 

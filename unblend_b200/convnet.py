@@ -139,7 +139,7 @@ def _m_tiles(batch: int, h_out: int, w_out: int) -> int:
     return batch * h_out * -(-w_out // mv)
 
 
-def _block_n(n_out: int, bn256_min: int, m_tiles: int = 1 << 20, sms: int = 148) -> int:
+def _block_n(n_out: int, bn256_min: int, m_tiles: int = 1 << 20, sms: int = 148, max_bn: int = 256) -> int:
     """Output-channel tile of the tensor-core convolution.
 
     Candidates 64, 96, 128, 192 (and 256 from ``bn256_min`` channels on). The persistent
@@ -150,7 +150,7 @@ def _block_n(n_out: int, bn256_min: int, m_tiles: int = 1 << 20, sms: int = 148)
     ties going to the wider tile (fewer re-reads of the input rows): with many tiles that
     is the fewest padded columns; with few (small batches) it trades width for fuller waves.
     """
-    cands = [64, 96, 128, 192] + ([256] if n_out >= bn256_min else [])
+    cands = [bn for bn in [64, 96, 128, 192] + ([256] if n_out >= bn256_min else []) if bn <= max_bn]
     best = None
     for bn in cands:
         tiles = m_tiles * -(-n_out // bn)
@@ -158,6 +158,19 @@ def _block_n(n_out: int, bn256_min: int, m_tiles: int = 1 << 20, sms: int = 148)
         if best is None or key < best[0]:
             best = (key, bn)
     return best[1]
+
+
+def _subtaps_pay(n_out: int, bn256_min: int) -> bool:
+    """Whether a 3-wide kernel row of the 3-pass bf16 split runs faster with its three taps sharing one
+    A load and operand split (tiles of <= 128 columns) than on the widest tiles without sharing.
+
+    Worth it up to 1.5x the tiles of the widest choice (HTDemucs decoder 3x3 rewrites at 32 segments:
+    48 -> 96 channels 3.37 -> 2.33 ms, 192 -> 384 1.59 -> 1.36 ms; not 96 -> 192 on 96-column tiles,
+    1.63 -> 1.73 ms, nor 384 -> 768 on 128-column tiles, 1.22 -> 1.37 ms). Depends on the layer only.
+    """
+    full = -(-n_out // _block_n(n_out, bn256_min))
+    shared = -(-n_out // _block_n(n_out, bn256_min, max_bn=128))
+    return 2 * shared <= 3 * full
 
 
 class ConvNet(nn.Module):
@@ -183,6 +196,9 @@ class ConvNet(nn.Module):
         # or "tf32x3" (hi/lo TF32 parts, kind::tf32: 8 per MMA, every tile). Both
         # hold the fp32 parity bound on the registry models; bf16x3 issues half the MMAs.
         self.fp32_split = "bf16x3"
+        # With the bf16x3 split, 3-wide kernel rows (stride 1) run on tiles of <= 128
+        # columns whose three taps share one A load and one operand split, where that pays.
+        self.fp32_subtaps = True
         self.weights = nn.ParameterDict()
         self._arena = StatsArena()
 
@@ -236,14 +252,23 @@ class ConvNet(nn.Module):
                 p.post, p.post_sh = post.data_ptr(), post.shape[1]
             p.y_bf16 = 1 if y_bf16 else 0
             if self.precision == "fp32":
-                block_n = _block_n(n_out, self._bn256_min[_lib.TC_TF32X3], _m_tiles(x.B, h_out, w_out), self._sms(x))
                 # The bf16 split halves the MMAs; layers whose many-tile width is <= 128 columns
                 # keep the TF32 split, whose A operand sits in TMEM (A-from-TMEM MMAs issue faster
                 # at those widths: decoder.3's 3x3 rewrite 851 us against 923 us with the bf16
-                # split in shared memory). The split depends on the layer only, not on the batch
-                # (the tile width does not change any output's rounding; the split does).
-                wide = _block_n(n_out, self._bn256_min[_lib.TC_TF32X3]) >= 192
-                mode = _lib.TC_BF16X3 if self.fp32_split == "bf16x3" and wide else _lib.TC_TF32X3
+                # split in shared memory), unless their three taps along w share one A load and
+                # operand split (bf16 split, tiles of <= 128 columns; 3.37 -> 2.33 ms for that
+                # layer at 32 segments). The split and the tap grouping depend on the layer only,
+                # not on the batch (the tile width does not change any output's rounding; the
+                # split and the K order do).
+                bn256 = self._bn256_min[_lib.TC_TF32X3]
+                subtap = self.fp32_subtaps and kw == 3 and sw == 1 and dw * 2 <= 8 and _subtaps_pay(n_out, bn256)
+                wide = _block_n(n_out, bn256) >= 192
+                if self.fp32_split == "bf16x3" and subtap:
+                    mode = _lib.TC_BF16X3_TAPS
+                else:
+                    mode = _lib.TC_BF16X3 if self.fp32_split == "bf16x3" and wide else _lib.TC_TF32X3
+                block_n = _block_n(n_out, bn256, _m_tiles(x.B, h_out, w_out), self._sms(x),
+                                   max_bn=128 if mode == _lib.TC_BF16X3_TAPS else 256)
             else:
                 mode = _lib.TC_BF16
                 if x.t.dtype == torch.bfloat16:
@@ -254,7 +279,8 @@ class ConvNet(nn.Module):
                     # 3-wide kernel rows: tiles of <= 192 columns share one A load across the three taps.
                     bn256 = 1 << 30
                 block_n = _block_n(n_out, bn256, _m_tiles(x.B, h_out, w_out), self._sms(x))
-            whi, wlo = self._tc_weight(w, _lib.TC_BF16 if mode == _lib.TC_BF16_ACT else mode)
+            wmode = {_lib.TC_BF16_ACT: _lib.TC_BF16, _lib.TC_BF16X3_TAPS: _lib.TC_BF16X3}.get(mode, mode)
+            whi, wlo = self._tc_weight(w, wmode)
             _lib.call("unblend_conv2d_tc", x.t.data_ptr(), whi.data_ptr(), _lib.ptr(wlo), _lib.ptr(b), y,
                       ctypes_byref(p), mode, block_n, work=flops)
             return

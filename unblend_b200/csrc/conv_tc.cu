@@ -21,7 +21,9 @@
 // converted to bf16 and multiplied with bf16 weights (kind::f16). 3-pass bf16
 // mode (MODE 2): the same three products with bf16 hi / lo parts (hi = x
 // rounded to bf16, lo = x - hi rounded to bf16, 16 significant bits in all) in
-// kind::f16, whose MMAs take 16 channels each instead of 8. bf16-activation mode
+// kind::f16, whose MMAs take 16 channels each instead of 8; MODE 4 is MODE 2 with
+// the three taps of a 3-wide kernel row sharing one A load and split (tiles of up
+// to 128 columns; a different K order, so not bit-identical). bf16-activation mode
 // (MODE 3): the input is already bf16 in memory (written by the producing kernel
 // for a consumer that multiplies in bf16), so TMA lands the A tile in its MMA
 // layout and nothing is converted; otherwise as the bf16 mode.
@@ -98,13 +100,19 @@ struct ChunkK {
   static constexpr int value = (MODE == 0 && BN == 256) ? 16 : 32;
 };
 
-// Sub-taps per A load: the bf16 mode with tiles of up to 192 columns groups up
-// to three taps along w (a 3-wide kernel row) onto one A load of 128 + 8 rows,
-// each sub-tap's MMAs starting at its shifted row; the input tile then crosses
-// from L2 once per kernel row instead of once per tap.
+// MODE 2 and MODE 4 are the 3-pass bf16 split; MODE 4 groups the taps of a
+// 3-wide kernel row (below) on tiles of up to 128 columns.
+__host__ __device__ constexpr bool bf16x3(int mode) { return mode == 2 || mode == 4; }
+
+// Sub-taps per A load: the bf16 modes with tiles of up to 192 columns, and MODE 4
+// (tiles of up to 128 columns: wider 3-pass tiles would leave room for one
+// pipeline stage), group up to three taps along w (a 3-wide kernel row) onto one
+// A load of 128 + 8 rows, each sub-tap's MMAs starting at its shifted row; the
+// input tile then crosses from L2, and is converted, once per kernel row instead
+// of once per tap.
 template <int BN, int MODE>
 struct SubTaps {
-  static constexpr int value = ((MODE == 1 || MODE == 3) && BN <= 192) ? 3 : 1;
+  static constexpr int value = (((MODE == 1 || MODE == 3) && BN <= 192) || (MODE == 4 && BN <= 128)) ? 3 : 1;
 };
 
 template <int BN, int MODE>
@@ -118,7 +126,7 @@ struct Layout {
   // (MODE 2: bf16 hi and lo tiles, AT_BYTES apart)
   static constexpr int AT_BYTES = (A_ROWS * 64 + 1023) / 1024 * 1024;
   static constexpr int AC_BYTES =
-      ATmem<BN, MODE>::value ? 0 : MODE == 0 ? A_ROWS * ROWB : MODE == 2 ? 2 * AT_BYTES : AT_BYTES;
+      ATmem<BN, MODE>::value ? 0 : MODE == 0 ? A_ROWS * ROWB : bf16x3(MODE) ? 2 * AT_BYTES : AT_BYTES;
   static constexpr int B_BYTES = MODE == 0 ? BN * ROWB : BN * 64;     // one weight tile
   static constexpr int B_TILES = (MODE == 1 || MODE == 3) ? 1 : 2;   // hi + lo, or bf16
   static constexpr int STAGE = A_BYTES + AC_BYTES + NSUB * B_TILES * B_BYTES;
@@ -236,10 +244,17 @@ __global__ void __launch_bounds__(NT, 1)
             mbar_expect_tx(&full[s], bytes);
             tma_load_4d(st, &mapA, &full[s], ca + cc, wa, ha, c.b);
             uint8_t* sb = st + L::A_BYTES + L::AC_BYTES;
+            // Sub-tap u's weight tile(s) at sb + u * B_TILES * B_BYTES (hi, then lo for the split modes).
             tma_load_2d(sb, &mapB, &full[s], kb + cc, c.n0);
-            if (MODE == 0 || MODE == 2) tma_load_2d(sb + L::B_BYTES, &mapB2, &full[s], kb + cc, c.n0);
-            if (L::NSUB > 1 && ns > 1) tma_load_2d(sb + L::B_BYTES, &mapB, &full[s], a.tap_k1[tap] + cc, c.n0);
-            if (L::NSUB > 2 && ns > 2) tma_load_2d(sb + 2 * L::B_BYTES, &mapB, &full[s], a.tap_k2[tap] + cc, c.n0);
+            if (MODE == 0 || bf16x3(MODE)) tma_load_2d(sb + L::B_BYTES, &mapB2, &full[s], kb + cc, c.n0);
+#pragma unroll
+            for (int u = 1; u < L::NSUB; ++u) {
+              if (u >= ns) break;
+              const int ku = (u == 1 ? a.tap_k1[tap] : a.tap_k2[tap]) + cc;
+              uint8_t* su = sb + u * L::B_TILES * L::B_BYTES;
+              tma_load_2d(su, &mapB, &full[s], ku, c.n0);
+              if (L::B_TILES == 2) tma_load_2d(su + L::B_BYTES, &mapB2, &full[s], ku, c.n0);
+            }
           }
         }
       }
@@ -302,15 +317,23 @@ __global__ void __launch_bounds__(NT, 1)
               umma_tf32(d, dah, dbl, idesc, 1u);
               umma_tf32(d, dal, dbh, idesc, 1u);
             }
-          } else if (MODE == 2) {
+          } else if (bf16x3(MODE)) {
+            // Sub-tap u reads the hi / lo tiles from row shift_u on (64-byte rows).
+            const int ns = L::NSUB > 1 ? a.tap_n[ctap] : 1;
 #pragma unroll
-            for (int j = 0; j < 2; ++j) {
-              if (j > 0 && 16 * j >= valid) break;  // 16 channels per kind::f16 step
-              const uint64_t dah = smem_desc(sac + 32 * j, 64), dal = smem_desc(sac + L::AT_BYTES + 32 * j, 64);
-              const uint64_t dbh = smem_desc(sb + 32 * j, 64), dbl = smem_desc(sb + L::B_BYTES + 32 * j, 64);
-              umma_bf16(d, dah, dbh, idesc, (kc > 0 || j > 0) ? 1u : 0u);
-              umma_bf16(d, dah, dbl, idesc, 1u);
-              umma_bf16(d, dal, dbh, idesc, 1u);
+            for (int u = 0; u < L::NSUB; ++u) {
+              if (u >= ns) break;
+              const int shift = u == 0 ? 0 : u == 1 ? a.tap_s1[ctap] : a.tap_s2[ctap];
+              const uint32_t au = sac + (uint32_t)(64 * shift), bu = sb + (uint32_t)(u * 2 * L::B_BYTES);
+#pragma unroll
+              for (int j = 0; j < 2; ++j) {
+                if (j > 0 && 16 * j >= valid) break;  // 16 channels per kind::f16 step
+                const uint64_t dah = smem_desc(au + 32 * j, 64), dal = smem_desc(au + L::AT_BYTES + 32 * j, 64);
+                const uint64_t dbh = smem_desc(bu + 32 * j, 64), dbl = smem_desc(bu + L::B_BYTES + 32 * j, 64);
+                umma_bf16(d, dah, dbh, idesc, (kc > 0 || j > 0 || u > 0) ? 1u : 0u);
+                umma_bf16(d, dah, dbl, idesc, 1u);
+                umma_bf16(d, dal, dbh, idesc, 1u);
+              }
             }
           } else {
             // Sub-tap u reads the bf16 A tile from row shift_u on (64-byte rows).
@@ -396,7 +419,7 @@ __global__ void __launch_bounds__(NT, 1)
           }
         } else if (MODE == 3) {
           // The TMA wrote the bf16 tile in its MMA layout: nothing to convert.
-        } else if (MODE == 2) {
+        } else if (bf16x3(MODE)) {
           // hi = bf16(v), lo = bf16(v - hi): both written as 64-byte swizzled bf16 tiles.
           const uint8_t* src = st;
           uint8_t* dst = st + L::A_BYTES;
@@ -740,7 +763,8 @@ extern "C" int unblend_error_flag(int* out_host, int clear) {
 
 extern "C" int unblend_conv2d_tc(const void* x, const void* w_hi, const void* w_lo, const float* bias, float* y,
                                  const UnblendConvParams* p, int mode, int block_n, void* stream) {
-  UB_REQUIRE(x && w_hi && y && p && mode >= 0 && mode <= 3);
+  UB_REQUIRE(x && w_hi && y && p && mode >= 0 && mode <= 4);
+  UB_REQUIRE(mode != 4 || block_n <= 128);  // shared tap loads: tiles of up to 128 columns
   UB_REQUIRE((mode == 3) == (p->x_bf16 != 0));  // mode 3 takes bf16 activations, the others fp32
   UB_REQUIRE(mode == 1 || mode == 3 || w_lo);  // the split modes take hi and lo weights
   UB_REQUIRE(block_n == 64 || block_n == 96 || block_n == 128 || block_n == 192 || block_n == 256);
@@ -799,9 +823,9 @@ extern "C" int unblend_conv2d_tc(const void* x, const void* w_hi, const void* w_
     a.a_sh = p->sh;
     UB_REQUIRE(kh_taps * kw_taps <= MAXT);
     // Up to three consecutive taps of a kernel row share one A load when the
-    // kernel groups sub-taps (bf16 mode, tiles up to 192 columns) and their
-    // shifts stay within the 8 rows of headroom.
-    const int nsub = ((mode == 1 || mode == 3) && block_n <= 192) ? 3 : 1;
+    // kernel groups sub-taps (bf16 modes, tiles up to 192 columns; mode 4, tiles
+    // up to 128 columns) and their shifts stay within the 8 rows of headroom.
+    const int nsub = (((mode == 1 || mode == 3) && block_n <= 192) || mode == 4) ? 3 : 1;
     for (int i = 0; i < kh_taps; ++i)
       for (int j = 0; j < kw_taps;) {
         int n = kw_taps - j < nsub ? kw_taps - j : nsub;
@@ -894,7 +918,7 @@ extern "C" int unblend_conv2d_tc(const void* x, const void* w_hi, const void* w_
     if (!make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w_hi, wd, ws, boxB, CU_TENSOR_MAP_SWIZZLE_64B))
       return UNBLEND_ERR_INVALID;
     mb2 = mb;
-    if (mode == 2 && !make_map(&mb2, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w_lo, wd, ws, boxB, CU_TENSOR_MAP_SWIZZLE_64B))
+    if (bf16x3(mode) && !make_map(&mb2, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w_lo, wd, ws, boxB, CU_TENSOR_MAP_SWIZZLE_64B))
       return UNBLEND_ERR_INVALID;
   }
   const long long tiles = (long long)p->batch * p->h_out * a.tiles_w * a.tiles_n;
@@ -933,6 +957,11 @@ extern "C" int unblend_conv2d_tc(const void* x, const void* w_hi, const void* w_
     if (block_n == 128) return launch<128, 3>(ma, mb, mb2, mo, a, tiles, st);
     if (block_n == 192) return launch<192, 3>(ma, mb, mb2, mo, a, tiles, st);
     return launch<256, 3>(ma, mb, mb2, mo, a, tiles, st);
+  }
+  if (mode == 4) {
+    if (block_n == 64) return launch<64, 4>(ma, mb, mb2, mo, a, tiles, st);
+    if (block_n == 96) return launch<96, 4>(ma, mb, mb2, mo, a, tiles, st);
+    return launch<128, 4>(ma, mb, mb2, mo, a, tiles, st);
   }
   if (mode == 2) {
     if (block_n == 64) return launch<64, 2>(ma, mb, mb2, mo, a, tiles, st);
