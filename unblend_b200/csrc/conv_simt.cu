@@ -163,7 +163,7 @@ __global__ void __launch_bounds__(NT) conv_simt_kernel(ConvArgs a) {
       if (j >= nouts) break;
       int n = glu ? (n0 + tx * 4) / 2 + j : n0 + tx * 4 + j;
       int ncount = glu ? p.n_out / 2 : p.n_out;
-      float v = glu ? vals[2 * j] * ub::sigmoidf_(vals[2 * j + 1]) : vals[j];
+      float v = glu ? vals[2 * j] * ub::sigmoid_approx(vals[2 * j + 1]) : vals[j];
       if (rv && n < ncount) {
         long long off = rowoff + (long long)(n / p.n_group) * p.out_sg + (n % p.n_group);
         if (p.res) v = p.res[off] + (p.res_scale ? __ldg(p.res_scale + n) : 1.f) * v;
@@ -304,7 +304,7 @@ __global__ void __launch_bounds__(WNT, 2) conv_simt_wide_kernel(ConvArgs a) {
       if (j >= nouts) break;
       const int n = glu ? (n0 + tx * 8) / 2 + j : n0 + tx * 8 + j;
       const int ncount = glu ? p.n_out / 2 : p.n_out;
-      float v = glu ? vals[2 * j] * ub::sigmoidf_(vals[2 * j + 1]) : vals[j];
+      float v = glu ? vals[2 * j] * ub::sigmoid_approx(vals[2 * j + 1]) : vals[j];
       if (rv && n < ncount) {
         const long long off = rowoff + (long long)(n / p.n_group) * p.out_sg + (n % p.n_group);
         if (p.res) v = p.res[off] + (p.res_scale ? __ldg(p.res_scale + n) : 1.f) * v;

@@ -159,7 +159,7 @@ __global__ void __launch_bounds__(ROWS) dconv_apply_kernel(float* __restrict__ x
       const float zg = dot_row<MAXH>(ws + (n + 1) * H, a, H, bs[n + 1]);
       const float v = (zv - mean2) * rstd2 * gw[n] + gb[n];
       const float gt = (zg - mean2) * rstd2 * gw[n + 1] + gb[n + 1];
-      o[e] = sc[c + e] * (v * ub::sigmoidf_(gt));
+      o[e] = sc[c + e] * (v * ub::sigmoid_approx(gt));
     }
     xv.x += o[0];
     xv.y += o[1];

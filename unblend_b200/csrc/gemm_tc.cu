@@ -128,7 +128,7 @@ __device__ __forceinline__ float act_fn(float x) {
 template <bool FAST>
 __device__ __forceinline__ float sigmoid_fn(float x) {
   if (FAST) return 0.5f * tanh_approx(0.5f * x) + 0.5f;
-  return ub::sigmoidf_(x);
+  return ub::sigmoid_approx(x);
 }
 
 // Store NV (4, or 2 after GLU) consecutive values of one row at element

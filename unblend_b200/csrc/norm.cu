@@ -122,7 +122,7 @@ __global__ void dconv_tail_kernel(float* __restrict__ x, const float* __restrict
     const float va = (zz.x - mean) * rstd * gamma[2 * ch] + beta[2 * ch];
     const float vg = (zz.y - mean) * rstd * gamma[2 * ch + 1] + beta[2 * ch + 1];
     float* xp = x + g * x_gs + rr * c + ch;
-    *xp = *xp + scale[ch] * (va * ub::sigmoidf_(vg));
+    *xp = *xp + scale[ch] * (va * ub::sigmoid_approx(vg));
   }
 }
 
@@ -264,7 +264,7 @@ __global__ void dconv_tail4_kernel(float* __restrict__ x, const float4* __restri
     for (int k = 0; k < 4; ++k) {
       const float va = (zv[2 * k] - mean) * rstd * gv[2 * k] + bv[2 * k];
       const float vg = (zv[2 * k + 1] - mean) * rstd * gv[2 * k + 1] + bv[2 * k + 1];
-      o[k] = o[k] + sv[k] * (va * ub::sigmoidf_(vg));
+      o[k] = o[k] + sv[k] * (va * ub::sigmoid_approx(vg));
     }
     *xp = make_float4(o[0], o[1], o[2], o[3]);
   }
