@@ -10,11 +10,11 @@
 // Persistent: one CTA per SM walks the 128 x BN output tiles in a grid-stride
 // loop, with the accumulator double-buffered in TMEM (2 x BN columns) so the
 // epilogue of one tile overlaps the main loop of the next.
-// Warp roles (320 threads):
+// Warp roles (448 threads):
 //   warp 0    TMA producer (one elected lane)
 //   warp 1    TMEM allocation + MMA issue (one elected lane)
 //   warps 2-5 operand conversion in shared memory
-//   warps 6-9 epilogue
+//   warps 6-13 epilogue (two per TMEM lane quarter, alternate 32-column chunks)
 // fp32 mode: each fp32 A tile is split in place into a TF32 "hi" part and a
 // residual "lo" tile; weights come pre-split; D += Ahi*Bhi + Ahi*Blo + Alo*Bhi
 // (3 x kind::tf32) keeps fp32-level accuracy. bf16 mode: the fp32 A tile is
@@ -42,7 +42,8 @@ namespace {
 using namespace ub::tc;
 
 constexpr int MAXT = 16;
-constexpr int NT = 320;
+constexpr int NT = 448;
+constexpr int EPI_WARPS = 8;
 
 struct TcArgs {
   long long tiles;
@@ -130,11 +131,14 @@ struct Layout {
   static constexpr int B_BYTES = MODE == 0 ? BN * ROWB : BN * 64;     // one weight tile
   static constexpr int B_TILES = (MODE == 1 || MODE == 3) ? 1 : 2;   // hi + lo, or bf16
   static constexpr int STAGE = A_BYTES + AC_BYTES + NSUB * B_TILES * B_BYTES;
-  static constexpr int STAGES = (200 * 1024) / STAGE > 4 ? 4 : (200 * 1024) / STAGE;
+  static constexpr int EPI_BYTES = EPI_WARPS * 32 * 32 * 4;  // one 32 x 32 fp32 transpose tile per epilogue warp
+  static constexpr int STAGE_BUDGET = 232448 - EPI_BYTES - 1024 - 256;  // 227 KB per CTA
+  static constexpr int STAGES = STAGE_BUDGET / STAGE > 4 ? 4 : STAGE_BUDGET / STAGE;
   static constexpr int A_COL = 2 * BN;  // first TMEM column of the A stages (A in TMEM)
   static_assert(!ATmem<BN, MODE>::value || STAGES == 4, "four A stages in TMEM");
-  static constexpr int EPI_BYTES = 4 * 32 * 32 * 4;  // one 32 x 32 fp32 transpose tile per epilogue warp
+  static_assert(STAGES >= 2, "at least two pipeline stages");
   static constexpr int SMEM = STAGES * STAGE + EPI_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static_assert(SMEM <= 232448, "shared memory per CTA");
 };
 
 __device__ __forceinline__ float gelu(float x) { return ub::gelu_erf(x); }
@@ -213,7 +217,7 @@ __global__ void __launch_bounds__(NT, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 4);
+      mbar_init(&acc_empty[i], EPI_WARPS);
     }
     fence_mbar_init();
   }
@@ -461,12 +465,13 @@ __global__ void __launch_bounds__(NT, 1)
       }
     }
   } else {
-    // Epilogue warps 6-9: TMEM -> registers -> shared-memory transpose -> fused
+    // Epilogue warps 6-13: TMEM -> registers -> shared-memory transpose -> fused
     // ops -> global. After the transpose each lane owns 4 consecutive output
     // channels of 8 rows, so bias / scale loads are one float4 per lane and
     // each store instruction of the warp writes 4 whole row segments.
     const int q = warp & 3;  // TMEM lane quarter this warp may read
     float4* stage = reinterpret_cast<float4*>(epi_smem + (warp - 6) * 4096);
+    const int c_first = 32 * ((warp - 6) >> 2);  // this warp's first chunk; the pair alternates chunks
     const int ch = lane & 7;
     const bool glu = a.act == UNBLEND_ACT_GLU;
     int i = 0;
@@ -479,7 +484,7 @@ __global__ void __launch_bounds__(NT, 1)
       const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
       double s1 = 0.0, s2 = 0.0;  // per-lane statistics: fp32 partials of 4 values, summed in double
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
+      for (int c0 = c_first; c0 < BN; c0 += 64) {
         if (n0 + c0 >= a.n_out) break;  // uniform across the warp
         uint32_t acc[32];
         __syncwarp();
